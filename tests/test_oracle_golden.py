@@ -1,0 +1,331 @@
+"""The CPU oracle against the reference's golden vectors and known-answer tests (no GPU)."""
+
+from __future__ import annotations
+
+import json
+import struct
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+from oracle import acceptance, core, drafter, optim
+
+
+def load(name):
+    return np.load(GOLDEN / name)
+
+
+# ------------------------------------------------------------------ signs / packing
+
+
+def test_sign_kat_and_ste():
+    # tests/numerical/test_model.py:451-457 of the reference
+    src = np.array([-2.0, -1.0, -0.0, 0.0, 1.0, 2.0], dtype=np.float32)
+    assert core.hard_sign(src).tolist() == [-1, -1, 1, 1, 1, 1]
+    assert core.sign_backward(np.ones(6, np.float32), src).tolist() == [0, 1, 1, 1, 1, 0]
+    with pytest.raises(ValueError, match="F32"):
+        core.hard_sign(src.astype(np.float64))
+
+
+def test_sign_matches_reference_values_and_gradients():
+    f = load("signs.npz")
+    assert np.array_equal(core.hard_sign(f["value"]), f["sign"])
+    assert np.array_equal(core.sign_backward(f["upstream"], f["value"]), f["grad"])
+
+
+def test_packing_kat_and_widths():
+    f = load("packing.npz")
+    words = core.packed_signs(f["kat_value"])
+    assert words.tobytes() == struct.pack("<II", 0x80000001, 1)
+    assert np.array_equal(words, f["kat_words"])
+    for columns in (1, 7, 8, 31, 32, 33, 65, 300):
+        assert np.array_equal(core.packed_signs(f[f"value_{columns}"]), f[f"words_{columns}"]), columns
+    with pytest.raises(ValueError, match="finite"):
+        core.packed_signs(np.array([[np.nan]], dtype=np.float32))
+    with pytest.raises(ValueError, match="finite"):
+        core.packed_signs(np.zeros(3, dtype=np.float32))
+
+
+@pytest.mark.parametrize("shape", [(1, 1), (16, 256), (17, 257), (37, 300), (48, 700)])
+def test_t16_roundtrip(shape):
+    rng = np.random.default_rng(sum(shape))
+    latent = rng.standard_normal(shape).astype(np.float32)
+    latent[0, 0] = -0.0
+    words = core.tile_signs_t16(latent)
+    nrb, ncp = core.t16_shape(*shape)
+    assert words.shape == (nrb * ncp * 128,)
+    assert np.array_equal(core.untile_signs_t16(words, *shape), latent >= 0)
+
+
+# ------------------------------------------------------------------ projections
+
+
+def projection_cases():
+    f = load("projection.npz")
+    for i in range(int(f["count"])):
+        yield {k.split("_", 1)[1]: f[k] for k in f.files if k.startswith(f"{i}_")}
+
+
+def test_projection_forward_bit_exact_against_reference():
+    for c in projection_cases():
+        out = core.projection_forward(c["value"], c["latent"], c["scale"], c["midpoint"], c["gain"], c["bound"], int(c["bits"]))
+        assert np.array_equal(out, c["output"]), int(c["bits"])
+
+
+def test_projection_backward_against_reference():
+    for c in projection_cases():
+        grads = optim.projection_backward(c["upstream"], c["value"], c["latent"], c["scale"], c["midpoint"],
+                                          c["log_gain"], c["log_clip"], int(c["bits"]))
+        np.testing.assert_allclose(grads["input"], c["grad_input"], rtol=1e-5, atol=1e-6)
+        for name in ("latent_sign", "scale", "midpoint", "log_gain", "log_clip"):
+            np.testing.assert_allclose(grads[name], c["grad_" + name], rtol=1e-4, atol=1e-5, err_msg=name)
+
+
+def test_projection_scalar_oracle():
+    # tests/numerical/test_model.py:437-449 of the reference
+    out = core.projection_forward(np.array([[0.1, 0.7]], np.float32), np.array([[0.2, -0.4]], np.float32),
+                                  np.array([0.3], np.float32), np.zeros(1, np.float32), np.ones(2, np.float32),
+                                  np.float32(1.0), 4)
+    assert abs(float(out[0, 0]) - (1 - 5) * 0.3 / 7) < 1e-6
+    grads = optim.projection_backward(np.ones((1, 1), np.float32), np.array([[0.1, 0.7]], np.float32),
+                                      np.array([[0.2, -0.4]], np.float32), np.array([0.3], np.float32),
+                                      np.zeros(1, np.float32), np.zeros(2, np.float32), np.float32(0.0), 4)
+    np.testing.assert_allclose(grads["midpoint"], [6 / 7], rtol=1e-6)
+    np.testing.assert_allclose(grads["latent_sign"], [[0.3 / 7, 1.5 / 7]], rtol=1e-6)
+
+
+def test_historical_arithmetic():
+    # evidence/arithmetic-reference.json of the reference
+    g = json.loads((GOLDEN / "arithmetic.json").read_text())
+    w = np.array(g["weights"], np.float32)
+    w[1, 2] = -0.0
+    x = np.array(g["inputs"], np.float32)
+    log_gain = np.array(g["gain"], np.float32)
+    log_clip = np.float32(np.log(np.float32(g["clip"])))
+    scale = np.abs(w).mean(-1, dtype=np.float32)
+    mid = np.array(g["midpoint"], np.float32)
+    gain = np.exp(log_gain).astype(np.float32)
+    bound = np.exp(log_clip).astype(np.float32)
+    out = core.projection_forward(x, w, scale, mid, gain, bound, 4)
+    np.testing.assert_allclose(out, np.array(g["output"], np.float32), atol=1e-7, rtol=1e-6)
+    grads = optim.projection_backward(np.ones_like(out), x, w, scale, mid, log_gain, log_clip, 4)
+    np.testing.assert_allclose(grads["input"], np.array(g["input_grad"], np.float32), atol=1e-7, rtol=1e-6)
+    for name, value in g["gradients"].items():
+        np.testing.assert_allclose(grads[name], np.array(value, np.float32), atol=1e-7, rtol=1e-6, err_msg=name)
+    params = {"latent_sign": w, "scale": scale, "midpoint": mid, "log_gain": log_gain, "log_clip": log_clip}
+    for name, value in g["updated"].items():
+        p, _, _ = optim.adamw_step(params[name], grads[name], np.zeros_like(params[name]),
+                                   np.zeros_like(params[name]), 1, 1e-4)
+        np.testing.assert_allclose(p, np.array(value, np.float32), atol=1e-7, rtol=1e-6, err_msg=name)
+
+
+def test_he4_ffn_against_reference():
+    f = load("he4_ffn.npz")
+    norm = core.rms(f["residual"], f["ffn_norm"], float(f["epsilon"]))
+    np.testing.assert_allclose(norm, f["norm"], rtol=1e-6, atol=1e-7)
+
+    def params(name):
+        return {k: f[f"{name}_{k}"] for k in ("latent", "scale", "midpoint", "gain", "bound")}
+
+    gate, up, down = params("gate"), params("up"), params("down")
+    # projections bit-exact given identical inputs
+    assert np.array_equal(core.projection_forward(f["norm"], gate["latent"], gate["scale"], gate["midpoint"],
+                                                  gate["gain"], gate["bound"], 4), f["gate_out"])
+    assert np.array_equal(core.projection_forward(f["hidden"], down["latent"], down["scale"], down["midpoint"],
+                                                  down["gain"], down["bound"], 8), f["down_out"])
+    out = core.he4_ffn(f["norm"], f["residual"], gate, up, down)
+    np.testing.assert_allclose(out, f["output"], rtol=1e-5, atol=1e-6)
+
+
+def test_w1_ffn_against_reference_parts():
+    f = load("w1_ffn.npz")
+    y = core.w1_ffn(f["x"], f["w_gate"], f["w_up"], f["w_down"])
+    np.testing.assert_allclose(y, f["y"], rtol=1e-5, atol=1e-6)
+
+
+def test_w1a1_popcount_equals_pm_dot():
+    rng = np.random.default_rng(3)
+    for t, k, o in ((1, 1, 1), (5, 33, 7), (16, 2560, 40), (3, 97, 65)):
+        x = rng.standard_normal((t, k)).astype(np.float32)
+        w = rng.standard_normal((o, k)).astype(np.float32)
+        x[0, 0] = -0.0
+        _, dot, s = core.w1a1_projection(x, w, np.ones(o, np.float32))
+        pop = core.popcount_dot(core.pack_bits_rows(x), core.pack_bits_rows(w), k)
+        assert np.array_equal(dot, pop)
+        np.testing.assert_allclose(s, np.abs(x).mean(-1), rtol=1e-5)
+
+
+# ------------------------------------------------------------------ drafter forward
+
+
+def tiny_tensors(f, window):
+    tensors = {k[2:]: f[k] for k in f.files if k.startswith("t_")}
+    tag = f"w{window}_q_"
+    tensors.update({k[len(tag):]: f[k] for k in f.files if k.startswith(tag)})
+    return tensors
+
+
+@pytest.mark.parametrize("window", [4096, 5])
+def test_tiny_he4_forward_against_reference(window):
+    f = load("tiny_he4.npz")
+    cfg = drafter.Geometry(hidden=4, intermediate=8, heads=2, kv_heads=1, head_dim=2, window=window)
+    tensors = tiny_tensors(f, window)
+    tokens = tuple(range(20))
+    for anchor in (2, 7, 19):
+        logits = drafter.he4_forward(tensors, f["vocabulary"], 19, f["features"], tokens, anchor, cfg)
+        np.testing.assert_allclose(logits, f[f"w{window}_logits_{anchor}"], rtol=1e-4, atol=1e-5)
+    logits = drafter.he4_forward(tensors, f["vocabulary"], 19, f["features"], tokens, 7, cfg, slots=3)
+    np.testing.assert_allclose(logits, f[f"w{window}_logits_7_s3"], rtol=1e-4, atol=1e-5)
+
+
+def test_cache_layer_golden():
+    f = load("layer.npz")
+    tensors = {k[2:]: f[k] for k in f.files if k.startswith("t_")}
+    ones4 = np.ones(4, np.float32)
+    tensors.update({
+        "blk.0.ffn_gate.scale": np.abs(tensors["blk.0.ffn_gate.weight"]).mean(-1, dtype=np.float32),
+        "blk.0.ffn_up.scale": np.abs(tensors["blk.0.ffn_up.weight"]).mean(-1, dtype=np.float32),
+        "blk.0.ffn_down.scale": np.abs(tensors["blk.0.ffn_down.weight"]).mean(-1, dtype=np.float32),
+        "blk.0.ffn_gate.midpoint": np.zeros(8, np.float32), "blk.0.ffn_up.midpoint": np.zeros(8, np.float32),
+        "blk.0.ffn_down.midpoint": np.zeros(4, np.float32),
+        "blk.0.ffn_gate_up.gain": ones4, "blk.0.ffn_gate_up.bound": np.float32(1.0),
+        "blk.0.ffn_down.gain": np.ones(8, np.float32), "blk.0.ffn_down.bound": np.float32(1.0),
+    })
+    cfg = drafter.Geometry(hidden=4, intermediate=8, heads=2, kv_heads=1, head_dim=2)
+    context = drafter.layer_context(tensors, 0, f["encoded"], np.arange(3), cfg)
+    out = drafter.layer_forward(tensors, 0, f["state"], context, np.arange(3, 19), np.ones((16, 19), bool), cfg)
+    np.testing.assert_allclose(out, f["output"], atol=1e-6, rtol=1e-5)
+
+
+def test_rope_identity_and_rms():
+    value = np.array([[[3.0, 4.0]]], np.float32)
+    assert np.array_equal(drafter.rope(value, np.array([0]), 1e7), value)
+    np.testing.assert_allclose(core.rms(value, np.ones(2, np.float32), 1e-6), value / np.sqrt(12.5 + 1e-6), rtol=1e-6)
+
+
+def test_cache_storage_rounding_and_overflow():
+    v = np.array([0.1234567, -1.234567], np.float32)
+    assert np.array_equal(drafter.cache_storage(v), v.astype(np.float16).astype(np.float32))
+    with pytest.raises(ValueError, match="overflow"):
+        drafter.cache_storage(np.array([70000.0], np.float32))
+
+
+# ------------------------------------------------------------------ acceptance
+
+
+def test_greedy_rounds_validated_by_reference_oracle():
+    g = json.loads((GOLDEN / "greedy.json").read_text())
+    for case in g["rounds"]:
+        acc, nxt = acceptance.greedy_prefix(case["targets"], case["drafts"], case["eog"])
+        assert (acc, nxt) == (case["accepted"], case["next"]), case
+    for case in g["ties"]:
+        assert int(acceptance.argmax_rows(np.array(case["row"], np.float32))) == case["argmax"]
+
+
+def test_greedy_reference_unit_cases():
+    # tests/test_verifier.py:28-43 of the reference, as logits
+    eog = [99]
+
+    def logits_for(targets, vocab=128):
+        rows = np.full((1, len(targets), vocab), -5.0, np.float32)
+        for i, t in enumerate(targets):
+            rows[0, i, t] = 3.0
+        return rows
+
+    acc, nxt, _ = acceptance.accept_greedy(logits_for([5, 9, 10]), np.array([[5, 6]]), eog)
+    assert (acc[0], nxt[0]) == (1, 9)
+    acc, nxt, _ = acceptance.accept_greedy(logits_for([5, 9, 1]), np.array([[5, 9]]), eog)
+    assert (acc[0], nxt[0]) == (2, 1)
+    acc, nxt, _ = acceptance.accept_greedy(logits_for([99, 7, 1]), np.array([[99, 7]]), eog)
+    assert (acc[0], nxt[0]) == (0, 99)
+    bad = logits_for([1, 2])
+    bad[0, 1, 3] = np.inf
+    with pytest.raises(ValueError, match="nonfinite"):
+        acceptance.accept_greedy(bad, np.array([[1]]), eog)
+
+
+def test_philox_known_answers():
+    # Random123 known-answer vectors for Philox4x32-10
+    kat = [
+        ((0, 0, 0, 0), (0, 0), (0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8)),
+        ((0xFFFFFFFF,) * 4, (0xFFFFFFFF,) * 2, (0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD)),
+        ((0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344), (0xA4093822, 0x299F31D0),
+         (0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1)),
+    ]
+    for ctr, key, expected in kat:
+        out = acceptance.philox4x32_10(np.array([ctr], dtype=np.uint64), key)
+        assert tuple(int(v) for v in out[0]) == expected
+
+
+def test_exp_fixed_accuracy():
+    x = -np.linspace(0, 87, 200001, dtype=np.float32)
+    got = acceptance.exp_fixed(x).astype(np.float64)
+    want = np.exp(x.astype(np.float64))
+    rel = np.abs(got - want) / want
+    assert rel.max() < 4e-7
+    assert acceptance.exp_fixed(np.array([-200.0], np.float32))[0] == 0.0
+
+
+def test_sample_index_edges():
+    w = np.zeros(10000, np.float32)
+    w[4097] = 1.0
+    for u in (0.0, 0.5, np.float32(1 - 2**-24)):
+        assert acceptance.sample_index(w, np.float32(u)) == 4097
+    w = np.ones(9000, np.float32)
+    assert acceptance.sample_index(w, np.float32(0.0)) == 0
+    assert acceptance.sample_index(w, np.float32(1 - 2**-24)) == 8999
+
+
+def test_rejection_statistics_match_reference_sampler_check():
+    # native/verifier-test.cpp:43-80 of the reference: marginals within 0.035 of p,
+    # acceptance within 0.035 of sum(min(p, q)).
+    cases = [((0.55, 0.35, 0.10), (0.10, 0.70, 0.20)), ((0.55, 0.35, 0.10), (1.00, 0.00, 0.00)),
+             ((0.55, 0.35, 0.10), (0.55, 0.35, 0.10)), ((0.00, 0.60, 0.40), (0.50, 0.50, 0.00))]
+    rng = np.random.default_rng(9101)
+    trials = 4000
+    for p, q in cases:
+        p, q = np.array(p), np.array(q)
+        lp = np.where(p > 0, np.log(np.maximum(p, 1e-30)), -60.0).astype(np.float32)
+        lq = np.where(q > 0, np.log(np.maximum(q, 1e-30)), -60.0).astype(np.float32)
+        drafts = rng.choice(3, size=(trials, 1), p=q)
+        target = np.broadcast_to(lp, (trials, 2, 3))
+        draft = np.broadcast_to(lq, (trials, 1, 3))
+        acc, nxt = acceptance.accept_rejection(target, draft, drafts, seed=8101)
+        first = np.where(acc == 1, drafts[:, 0], nxt)
+        observed = np.bincount(first, minlength=3) / trials
+        assert np.abs(observed - p).max() <= 0.035, (p, q, observed)
+        assert abs(acc.mean() - np.minimum(p, q).sum()) <= 0.035
+
+
+def test_rejection_eog_stop():
+    # native/verifier-test.cpp:84-97: drafts [eos, eos] under a point mass stop after one token
+    lp = np.full((1, 3, 8), -60.0, np.float32)
+    lp[..., 2] = 0.0
+    lq = lp[:, :2]
+    acc, nxt = acceptance.accept_rejection(lp, lq, np.array([[2, 2]]), seed=1, eog=[2])
+    assert (int(acc[0]), int(nxt[0])) == (0, 2)
+
+
+# ------------------------------------------------------------------ optimizer
+
+
+def test_adamw_against_reference():
+    f = load("adamw.npz")
+    p, m, v = f["param0"], np.zeros_like(f["param0"]), np.zeros_like(f["param0"])
+    for step in range(3):
+        p, m, v = optim.adamw_step(p, f[f"grad{step}"], m, v, step + 1, 1e-3)
+        np.testing.assert_allclose(m, f[f"exp_avg{step + 1}"], rtol=1e-6, atol=1e-8)
+        np.testing.assert_allclose(v, f[f"exp_avg_sq{step + 1}"], rtol=1e-6, atol=1e-10)
+        np.testing.assert_allclose(p, f[f"param{step + 1}"], rtol=1e-6, atol=1e-7)
+
+
+def test_bound_latents_against_reference():
+    f = load("bound.npz")
+    # the row mean is a float reduction whose order differs from torch's by an ulp
+    bounded = optim.bound_latents(f["value"], 3.0)
+    np.testing.assert_allclose(bounded, f["bounded"], rtol=4e-7, atol=0)
+    assert np.array_equal(bounded >= 0, f["bounded"] >= 0)
+    kat = optim.bound_latents(np.array([[0.0, -0.0, 2.0, -14.0], [0.0] * 4], np.float32), 2.0)
+    assert np.array_equal(kat, f["kat"])
+    assert kat.tolist() == [[0.0, -0.0, 0.25, -1.0], [0.0] * 4]
