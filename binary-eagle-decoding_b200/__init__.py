@@ -1,0 +1,10 @@
+"""bitdraft-b200: B200 (sm_100a) kernels for the one-bit HE4 drafter hot path.
+
+The model/config API mirrors ``w1a1_eagle.model`` of the reference
+(philippesic/binary-eagle-decoding): ``Geometry``, ``Projection``, ``Layer``,
+``HE4``, ``hard_sign``, ``bound_latents``, ``clamp_latents``, ``cache_storage``,
+``rms``, ``rope``.  All computation on the hot path runs in ``libbitdraft.so``
+(C ABI in ``include/bitdraft.h``); there is no CPU fallback.
+"""
+
+from . import _lib, ops  # noqa: F401

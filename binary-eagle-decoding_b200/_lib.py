@@ -1,0 +1,120 @@
+"""ctypes binding of ``libbitdraft.so`` (the C ABI declared in ``include/bitdraft.h``).
+
+The library is the product: there is no CPU fallback.  If it is missing the
+first call raises ``RuntimeError`` naming the build step.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+LIBRARY = HERE / "libbitdraft.so"
+HEADER = HERE.parent / "include" / "bitdraft.h"
+
+c_int, c_int64, c_size_t, c_void_p = ctypes.c_int, ctypes.c_int64, ctypes.c_size_t, ctypes.c_void_p
+P = c_void_p  # every device pointer travels as a plain address
+
+BD_OK = 0
+FLAG_NONFINITE_LATENT = 1
+FLAG_NONFINITE_INPUT = 2
+FLAG_BAD_BOUND = 4
+FLAG_NONFINITE_LOGITS = 8
+FLAG_BAD_TOKEN = 16
+FLAG_NONFINITE_STATE = 32
+FLAG_CACHE_OVERFLOW = 64
+
+# Messages of the reference's ValueErrors for the same conditions.
+FLAG_MESSAGES = (
+    (FLAG_NONFINITE_LATENT, "finite F32 sign matrix required"),
+    (FLAG_NONFINITE_INPUT, "nonfinite quantizer input"),
+    (FLAG_BAD_BOUND, "invalid learned clipping bound"),
+    (FLAG_NONFINITE_LOGITS, "nonfinite verifier logits"),
+    (FLAG_BAD_TOKEN, "draft token outside the vocabulary"),
+    (FLAG_NONFINITE_STATE, "nonfinite drafter state"),
+    (FLAG_CACHE_OVERFLOW, "F16 cache storage overflow"),
+)
+
+
+class FfnHe4Args(ctypes.Structure):
+    _fields_ = [
+        ("x", P), ("residual", P), ("y", P), ("tokens", c_int), ("hidden", c_int64), ("inter", c_int64),
+        ("signs_gate_up", P), ("scale_gate", P), ("midpoint_gate", P), ("scale_up", P), ("midpoint_up", P),
+        ("gain_gate_up", P), ("bound_gate_up", P), ("signs_down", P), ("scale_down", P), ("midpoint_down", P),
+        ("gain_down", P), ("bound_down", P), ("hidden_out", P), ("workspace", P), ("workspace_bytes", c_size_t),
+        ("flags", P),
+    ]
+
+
+class FfnW1Args(ctypes.Structure):
+    _fields_ = [
+        ("x", P), ("y", P), ("tokens", c_int), ("hidden", c_int64), ("inter", c_int64),
+        ("signs_gate_up", P), ("scale_gate", P), ("scale_up", P), ("signs_down", P), ("scale_down", P),
+        ("hidden_out", P), ("workspace", P), ("workspace_bytes", c_size_t), ("flags", P),
+    ]
+
+
+SIGNATURES = {
+    "bd_abi_version": (c_int, []),
+    "bd_status_string": (ctypes.c_char_p, [c_int]),
+    "bd_device_info": (c_int, [P, P, P]),
+    "bd_pack_signs": (c_int, [P, c_int64, c_int64, P, P, P]),
+    "bd_t16_words": (c_int64, [c_int64, c_int64]),
+    "bd_tile_signs_t16": (c_int, [P, c_int64, c_int64, P, c_int, c_int, P, P]),
+    "bd_tile_gguf_t16": (c_int, [P, c_int64, c_int64, P, c_int, c_int, P]),
+    "bd_quantize_codes": (c_int, [P, c_int64, c_int64, c_int64, P, P, c_int, P, P, P, P]),
+    "bd_codes_ld": (c_int64, [c_int64]),
+    "bd_projection_workspace_bytes": (c_size_t, [c_int, c_int64]),
+    "bd_projection_he4": (c_int, [P, P, c_int, c_int64, c_int64, P, P, P, P, c_int, P, P, P, P, c_size_t, P]),
+    "bd_ffn_workspace_bytes": (c_size_t, [c_int, c_int64, c_int64]),
+    "bd_ffn_he4": (c_int, [ctypes.POINTER(FfnHe4Args), P]),
+    "bd_ffn_w1": (c_int, [ctypes.POINTER(FfnW1Args), P]),
+    "bd_accept_workspace_bytes": (c_size_t, [c_int, c_int]),
+    "bd_accept_greedy": (c_int, [P, c_int, c_int, c_int64, P, P, c_int, P, P, P, P, c_size_t, P, P]),
+    "bd_argmax_rows_bf16": (c_int, [P, c_int64, c_int64, P, P, P]),
+}
+
+_lib = None
+
+
+def header_symbols() -> list[str]:
+    """Names of the functions declared in ``include/bitdraft.h``."""
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"\b(bd_[a-z0-9_]+)\s*\(", text)))
+
+
+def load() -> ctypes.CDLL:
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIBRARY.exists():
+        raise RuntimeError(
+            f"{LIBRARY.name} is not built: run `python __graft_entry__.py build` "
+            "(nvcc for sm_100a); there is no CPU fallback"
+        )
+    lib = ctypes.CDLL(str(LIBRARY))
+    for name, (restype, argtypes) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = restype
+        fn.argtypes = argtypes
+    _lib = lib
+    return lib
+
+
+def call(name: str, *args) -> None:
+    """Call an int-status entry point; raise on a non-zero status."""
+    status = getattr(load(), name)(*args)
+    if status != BD_OK:
+        message = load().bd_status_string(status).decode()
+        if status == 1:
+            raise ValueError(f"{name}: {message}")
+        raise RuntimeError(f"{name}: {message} (status {status})")
+
+
+def raise_flags(value: int) -> None:
+    """Turn device-reported flag bits into the reference's ValueError."""
+    for bit, message in FLAG_MESSAGES:
+        if value & bit:
+            raise ValueError(message)

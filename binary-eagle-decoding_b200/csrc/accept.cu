@@ -1,0 +1,186 @@
+// Block-draft acceptance over vocabulary-sized bf16 logit rows.
+//
+// Greedy: one CTA per logit row computes the row argmax (strict '>' so the
+// lowest index wins ties, -0.0 == +0.0, non-finite logits flagged), and the last
+// CTA of each request walks the drafts (benchmarks/verifier.py:107-113).
+#include "common.cuh"
+
+namespace bd {
+
+constexpr int kArgmaxThreads = 512;
+
+// Orderable 64-bit key: larger value first, then smaller index.
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
+    uint32_t b = __float_as_uint(v == 0.0f ? 0.0f : v);
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return (static_cast<unsigned long long>(b) << 32) | static_cast<unsigned long long>(~idx);
+}
+
+__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long k) {
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) {
+        const unsigned long long o = __shfl_xor_sync(0xffffffffu, k, d);
+        k = o > k ? o : k;
+    }
+    return k;
+}
+
+struct GreedyArgs {
+    const uint16_t *logits;
+    int64_t rows, vocab;
+    int32_t *targets;
+    int32_t *flags;
+    int positions;             // drafts + 1 rows per request (0: plain argmax)
+    const int32_t *drafts;     // [requests][positions - 1]
+    const int32_t *eog;
+    int n_eog;
+    int32_t *accepted, *next_token;
+    int32_t *counters;         // [requests], zero on entry, left zero
+};
+
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_greedy_kernel(const GreedyArgs a) {
+    __shared__ unsigned long long part[kArgmaxThreads / 32];
+    __shared__ int last;
+    const int64_t row = blockIdx.x;
+    const uint16_t *src = a.logits + row * a.vocab;
+    unsigned long long best = 0;
+    bool bad = false;
+    const bool vec = (a.vocab % 8) == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0;
+    if (vec) {
+        const int64_t nvec = a.vocab / 8;
+        const uint4 *p = reinterpret_cast<const uint4 *>(src);
+        int64_t i = threadIdx.x;
+        for (; i + 3 * kArgmaxThreads < nvec; i += 4 * kArgmaxThreads) {
+            uint4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] = ld_stream_u4(p + i + u * kArgmaxThreads);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+                const uint32_t base = static_cast<uint32_t>((i + u * kArgmaxThreads) * 8);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const float f = __uint_as_float((e & 1) ? (w[e >> 1] & 0xffff0000u) : (w[e >> 1] << 16));
+                    bad |= !isfinite(f);
+                    const unsigned long long k = argmax_key(f, base + e);
+                    best = (isfinite(f) && k > best) ? k : best;
+                }
+            }
+        }
+        for (; i < nvec; i += kArgmaxThreads) {
+            const uint4 v = ld_stream_u4(p + i);
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float f = __uint_as_float((e & 1) ? (w[e >> 1] & 0xffff0000u) : (w[e >> 1] << 16));
+                bad |= !isfinite(f);
+                const unsigned long long k = argmax_key(f, static_cast<uint32_t>(i * 8 + e));
+                best = (isfinite(f) && k > best) ? k : best;
+            }
+        }
+    } else {
+        for (int64_t i = threadIdx.x; i < a.vocab; i += kArgmaxThreads) {
+            const float f = bf16_bits_to_f32(src[i]);
+            bad |= !isfinite(f);
+            const unsigned long long k = argmax_key(f, static_cast<uint32_t>(i));
+            best = (isfinite(f) && k > best) ? k : best;
+        }
+    }
+    best = warp_max_u64(best);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = best;
+    if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) set_flag(a.flags, BD_FLAG_NONFINITE_LOGITS);
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        unsigned long long k = threadIdx.x < kArgmaxThreads / 32 ? part[threadIdx.x] : 0ull;
+        k = warp_max_u64(k);
+        if (threadIdx.x == 0) {
+            const int32_t idx = static_cast<int32_t>(~static_cast<uint32_t>(k & 0xffffffffull));
+            a.targets[row] = idx;
+            last = 0;
+            if (a.positions > 0) {
+                __threadfence();
+                const int64_t request = row / a.positions;
+                const int old = atomicAdd(a.counters + request, 1);
+                last = old == a.positions - 1;
+            }
+        }
+    }
+    __syncthreads();
+    if (!last || threadIdx.x != 0) return;
+    // the last row of this request: walk the drafts
+    __threadfence();
+    const int64_t request = row / a.positions;
+    const int n = a.positions - 1;
+    const int32_t *tg = a.targets + request * a.positions;
+    const int32_t *dr = a.drafts + request * n;
+    int acc = n;
+    int nxt = __ldcg(tg + n);
+    for (int i = 0; i < n; ++i) {
+        const int t = __ldcg(tg + i);
+        bool is_eog = false;
+        for (int e = 0; e < a.n_eog; ++e) is_eog |= a.eog[e] == t;
+        if (t != dr[i] || (is_eog && i + 1 < n)) {
+            acc = i;
+            nxt = t;
+            break;
+        }
+    }
+    a.accepted[request] = acc;
+    a.next_token[request] = nxt;
+    atomicExch(a.counters + request, 0);
+}
+
+}  // namespace bd
+
+using namespace bd;
+
+extern "C" size_t bd_accept_workspace_bytes(int requests, int drafts) {
+    const size_t rows = static_cast<size_t>(requests) * (drafts + 1);
+    return ((rows * sizeof(int32_t) + 255) & ~static_cast<size_t>(255)) + static_cast<size_t>(requests) * 4 + 256;
+}
+
+extern "C" int bd_accept_greedy(const uint16_t *logits, int requests, int drafts, int64_t vocab,
+                                const int32_t *draft_tokens, const int32_t *eog, int n_eog, int32_t *accepted,
+                                int32_t *next_token, int32_t *targets, void *workspace, size_t workspace_bytes,
+                                int32_t *flags, bd_stream_t stream) {
+    if (requests < 0 || drafts < 0 || vocab < 1 || vocab > 0x7fffffff || n_eog < 0) return BD_ERR_INVALID;
+    if (requests == 0) return BD_OK;
+    if (!logits || (drafts > 0 && !draft_tokens) || (n_eog > 0 && !eog) || !accepted || !next_token)
+        return BD_ERR_INVALID;
+    if (!workspace || workspace_bytes < bd_accept_workspace_bytes(requests, drafts)) return BD_ERR_WORKSPACE;
+    const size_t rows = static_cast<size_t>(requests) * (drafts + 1);
+    char *ws = static_cast<char *>(workspace);
+    int32_t *counters = reinterpret_cast<int32_t *>(ws + ((rows * sizeof(int32_t) + 255) & ~static_cast<size_t>(255)));
+    GreedyArgs a{};
+    a.logits = logits;
+    a.rows = static_cast<int64_t>(rows);
+    a.vocab = vocab;
+    a.targets = targets ? targets : reinterpret_cast<int32_t *>(ws);
+    a.flags = flags;
+    a.positions = drafts + 1;
+    a.drafts = draft_tokens;
+    a.eog = eog;
+    a.n_eog = n_eog;
+    a.accepted = accepted;
+    a.next_token = next_token;
+    a.counters = counters;
+    argmax_greedy_kernel<<<static_cast<unsigned>(rows), kArgmaxThreads, 0, stream>>>(a);
+    BD_CHECK_LAUNCH();
+    return BD_OK;
+}
+
+extern "C" int bd_argmax_rows_bf16(const uint16_t *logits, int64_t rows, int64_t vocab, int32_t *out,
+                                   int32_t *flags, bd_stream_t stream) {
+    if (rows < 0 || vocab < 1 || vocab > 0x7fffffff) return BD_ERR_INVALID;
+    if (rows == 0) return BD_OK;
+    if (!logits || !out) return BD_ERR_INVALID;
+    GreedyArgs a{};
+    a.logits = logits;
+    a.rows = rows;
+    a.vocab = vocab;
+    a.targets = out;
+    a.flags = flags;
+    argmax_greedy_kernel<<<static_cast<unsigned>(rows), kArgmaxThreads, 0, stream>>>(a);
+    BD_CHECK_LAUNCH();
+    return BD_OK;
+}

@@ -1,0 +1,87 @@
+// Shared device helpers of the bitdraft sm_100a library.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "bitdraft.h"
+
+#define BD_CHECK_LAUNCH()                                   \
+    do {                                                    \
+        cudaError_t e_ = cudaGetLastError();                \
+        if (e_ != cudaSuccess) return BD_ERR_LAUNCH;        \
+    } while (0)
+
+namespace bd {
+
+__device__ __forceinline__ void set_flag(int32_t *flags, uint32_t bit) {
+    if (flags) atomicOr(reinterpret_cast<unsigned int *>(flags), bit);
+}
+
+__device__ __forceinline__ bool finite(float v) { return isfinite(v); }
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) {
+    return __uint_as_float(static_cast<uint32_t>(b) << 16);
+}
+
+// Integer MMA m16n8k32: D(int32) += A(16x32 s8, row) * B(32x8 s8, col).
+__device__ __forceinline__ void mma_s8_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// bf16 MMA m16n8k16: D(f32) += A(16x16 bf16, row) * B(16x8 bf16, col).
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Streaming 16-byte global load that does not allocate in L1 (weights are read once).
+__device__ __forceinline__ uint4 ld_stream_u4(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// The quantizer of Projection.forward for one element (see bd_quantize_codes).
+struct Quant {
+    float bound, ratio, step, maximum;
+    __device__ __forceinline__ void init(float b, int bits) {
+        maximum = static_cast<float>((1 << (bits - 1)) - 1);
+        bound = b;
+        ratio = __fmul_rn(__frcp_rn(b), maximum);
+        step = __fdiv_rn(b, maximum);
+    }
+    __device__ __forceinline__ int code(float gained) const {
+        float clipped = fmaxf(fminf(gained, bound), -bound);
+        float normalized = __fmul_rn(clipped, ratio);
+        float r = rintf(normalized);
+        r = fminf(fmaxf(r, -maximum), maximum);
+        return static_cast<int>(r);
+    }
+};
+
+__device__ __forceinline__ bool bad_bound(float b) { return !(isfinite(b) && b > 0.0f); }
+
+// HE4 projection epilogue: (D * max(scale,0)) * step + (sum * step) * midpoint, op by op.
+__device__ __forceinline__ float he4_value(int dot, float scale, float step, int code_sum, float midpoint) {
+    float s = scale < 0.0f ? 0.0f : scale;  // clamp_min(scale, 0), NaN propagates
+    float a = __fmul_rn(__fmul_rn(static_cast<float>(dot), s), step);
+    float b = __fmul_rn(__fmul_rn(static_cast<float>(code_sum), step), midpoint);
+    return __fadd_rn(a, b);
+}
+
+__device__ __forceinline__ float silu(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
+
+}  // namespace bd

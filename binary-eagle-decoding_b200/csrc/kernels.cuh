@@ -1,0 +1,59 @@
+// Internal launch helpers shared between the library's translation units.
+#pragma once
+
+#include "common.cuh"
+
+namespace bd {
+
+int launch_quantize_codes(const float *x, int64_t rows, int64_t cols, int64_t ld, const float *gain,
+                          const float *bound, int bits, int8_t *codes, int32_t *sums, int32_t *flags,
+                          int32_t *zero_sums, int zero_count, cudaStream_t stream);
+int launch_quantize_planes(const float *x, int64_t rows, int64_t cols, int64_t ld, int8_t *hi, int8_t *lo,
+                           int32_t *sums_hi, int32_t *sums_lo, float *row_scale, int32_t *flags,
+                           cudaStream_t stream);
+int launch_binarize(const float *x, int64_t rows, int64_t cols, int64_t ld, int8_t *codes, int32_t *sums,
+                    float *mean_abs, uint32_t *words, int64_t words_ld, int32_t *flags, cudaStream_t stream);
+
+// Epilogue selectors of the T16 integer-MMA projection kernels.
+enum Epilogue : int {
+    EPI_HE4 = 0,   // HE4 projection value (+ residual)
+    EPI_W1 = 1,    // (D * row_scale[t]) * scale[o]   (two int8 planes)
+    EPI_W1A1 = 2,  // (D * scale[o]) * mean_abs[t]
+};
+
+// Arguments of one T16 projection (single matrix or gate/up pair).
+struct ProjArgs {
+    const uint32_t *bits;     // T16 words (rb-major units; pairs: virtual rb 2p+m)
+    int64_t rows;             // output features (per matrix)
+    int64_t cols;             // input features
+    int64_t ncp;              // column pairs
+    const int8_t *codes0;     // [tokens][ld] plane 0
+    const int8_t *codes1;     // plane 1 (W1) or null
+    const int32_t *csum0;     // [tokens]
+    const int32_t *csum1;
+    int64_t ld;               // codes row stride (multiple of 256)
+    int tokens;
+    int kgroups;              // CTAs along K (single-matrix kernel)
+    // epilogue operands (matrix 0 = gate or the single matrix, 1 = up)
+    const float *scale0, *mid0, *scale1, *mid1;
+    const float *bound;       // HE4 bound of this projection's codes
+    int code_bits;            // HE4 code bits of this projection's input
+    const float *row_scale;   // W1 per-token scale, W1A1 per-token mean|x|
+    const float *residual;    // [tokens][rows] or null
+    float *out;               // [tokens][rows] (single matrix) or hidden [tokens][rows] (pair)
+    int32_t *raw_dot;         // optional [tokens][rows] exact +-1 dot (single matrix)
+    // gate/up -> down hand-off (HE4): next projection's codes
+    const float *next_gain, *next_bound;
+    int8_t *next_codes;       // [tokens][next_ld]
+    int32_t *next_csum;       // [tokens] (accumulated with atomics; zeroed by the caller)
+    int64_t next_ld;
+    // split-K accumulators (single matrix, kgroups > 1)
+    int32_t *acc;             // [planes][rows_pad][tpad] zero on entry, left zero
+    int32_t *counters;        // [nrb] zero on entry, left zero
+    int32_t *flags;
+};
+
+int launch_gateup(const ProjArgs &a, int epi, cudaStream_t stream);
+int launch_proj(const ProjArgs &a, int epi, cudaStream_t stream);
+
+}  // namespace bd

@@ -1,0 +1,195 @@
+// Activation quantizers feeding the integer-MMA projections.
+//   * HE4 learned-gain/clip codes (Projection.forward, w1a1_eagle/model.py:128-140)
+//   * per-token 16-bit fixed point as two int8 planes (pure one-bit-weight blocks)
+//   * W1A1 sign binarisation with the fixed-order per-token mean|x|
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace bd {
+
+template <typename T>
+__device__ __forceinline__ T block_sum_256(T v, T *scratch) {
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    T total = scratch[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) total += scratch[w];
+    __syncthreads();
+    return total;
+}
+
+// One 256-thread CTA per row; thread handles 4 consecutive columns per step.
+__global__ void __launch_bounds__(256) quantize_codes_kernel(const float *__restrict__ x, int64_t cols, int64_t ld,
+                                                             const float *__restrict__ gain,
+                                                             const float *__restrict__ bound_ptr, int bits,
+                                                             int8_t *__restrict__ codes, int32_t *__restrict__ sums,
+                                                             int32_t *flags, int32_t *zero_sums, int zero_count) {
+    __shared__ int scratch[8];
+    const int64_t row = blockIdx.x;
+    if (row == 0 && zero_sums)
+        for (int i = threadIdx.x; i < zero_count; i += blockDim.x) zero_sums[i] = 0;
+    const float b = *bound_ptr;
+    if (bad_bound(b)) {
+        if (threadIdx.x == 0) set_flag(flags, BD_FLAG_BAD_BOUND);
+    }
+    Quant q;
+    q.init(b, bits);
+    int sum = 0;
+    bool bad = false;
+    for (int64_t k0 = 4 * threadIdx.x; k0 < ld; k0 += 4 * blockDim.x) {
+        int c[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int64_t k = k0 + j;
+            c[j] = 0;
+            if (k < cols) {
+                const float g = __fmul_rn(x[row * cols + k], gain[k]);
+                bad |= !isfinite(g);
+                c[j] = q.code(g);
+            }
+            sum += c[j];
+        }
+        char4 v = make_char4(static_cast<signed char>(c[0]), static_cast<signed char>(c[1]),
+                             static_cast<signed char>(c[2]), static_cast<signed char>(c[3]));
+        *reinterpret_cast<char4 *>(codes + row * ld + k0) = v;
+    }
+    if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) set_flag(flags, BD_FLAG_NONFINITE_INPUT);
+    const int total = block_sum_256(sum, scratch);
+    if (threadIdx.x == 0) sums[row] = total;
+}
+
+// Per-token 16-bit fixed point: q = rint(x * 32639 / max|x|), q = 256 hi + lo.
+__global__ void __launch_bounds__(256) quantize_planes_kernel(const float *__restrict__ x, int64_t cols, int64_t ld,
+                                                              int8_t *__restrict__ hi, int8_t *__restrict__ lo,
+                                                              int32_t *__restrict__ sums_hi,
+                                                              int32_t *__restrict__ sums_lo,
+                                                              float *__restrict__ row_scale, int32_t *flags) {
+    __shared__ float fscratch[8];
+    __shared__ int iscratch[8];
+    const int64_t row = blockIdx.x;
+    float m = 0.0f;
+    bool bad = false;
+    for (int64_t k = threadIdx.x; k < cols; k += blockDim.x) {
+        const float v = x[row * cols + k];
+        bad |= !isfinite(v);
+        m = fmaxf(m, fabsf(v));
+    }
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, d));
+    if ((threadIdx.x & 31) == 0) fscratch[threadIdx.x >> 5] = m;
+    __syncthreads();
+    m = fscratch[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) m = fmaxf(m, fscratch[w]);
+    if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) set_flag(flags, BD_FLAG_NONFINITE_INPUT);
+    const float inv = m > 0.0f ? __fdiv_rn(32639.0f, m) : 0.0f;
+    int shi = 0, slo = 0;
+    for (int64_t k = threadIdx.x; k < ld; k += blockDim.x) {
+        int h = 0, l = 0;
+        if (k < cols) {
+            float r = rintf(__fmul_rn(x[row * cols + k], inv));
+            r = fminf(fmaxf(r, -32639.0f), 32639.0f);
+            const int qv = static_cast<int>(r);
+            h = (qv + 128) >> 8;
+            l = qv - 256 * h;
+        }
+        hi[row * ld + k] = static_cast<int8_t>(h);
+        lo[row * ld + k] = static_cast<int8_t>(l);
+        shi += h;
+        slo += l;
+    }
+    __syncthreads();
+    shi = block_sum_256(shi, iscratch);
+    slo = block_sum_256(slo, iscratch);
+    if (threadIdx.x == 0) {
+        sums_hi[row] = shi;
+        sums_lo[row] = slo;
+        row_scale[row] = __fdiv_rn(m, 32639.0f);
+    }
+}
+
+// W1A1: codes = x >= 0 ? +1 : -1; mean|x| in the fixed order of oracle.core.fixed_mean_abs
+// (lane l of 256 adds |x[l + 256 i]| sequentially, then a balanced tree of adjacent pairs).
+__global__ void __launch_bounds__(256) binarize_kernel(const float *__restrict__ x, int64_t cols, int64_t ld,
+                                                       int8_t *__restrict__ codes, int32_t *__restrict__ sums,
+                                                       float *__restrict__ mean_abs, uint32_t *__restrict__ words,
+                                                       int64_t words_ld, int32_t *flags) {
+    __shared__ float fscratch[8];
+    __shared__ int iscratch[8];
+    const int64_t row = blockIdx.x;
+    float acc = 0.0f;
+    int s = 0;
+    bool bad = false;
+    for (int64_t k = threadIdx.x; k < ld; k += blockDim.x) {
+        int c = 0;
+        if (k < cols) {
+            const float v = x[row * cols + k];
+            bad |= !isfinite(v);
+            acc = __fadd_rn(acc, fabsf(v));
+            c = v >= 0.0f ? 1 : -1;
+        }
+        codes[row * ld + k] = static_cast<int8_t>(c);
+        s += c;
+        if (words) {
+            const unsigned word = __ballot_sync(0xffffffffu, c > 0);
+            if ((threadIdx.x & 31) == 0 && (k >> 5) < words_ld) words[row * words_ld + (k >> 5)] = word;
+        }
+    }
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, d));
+    if ((threadIdx.x & 31) == 0) fscratch[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const float a = __fadd_rn(__fadd_rn(fscratch[0], fscratch[1]), __fadd_rn(fscratch[2], fscratch[3]));
+        const float b = __fadd_rn(__fadd_rn(fscratch[4], fscratch[5]), __fadd_rn(fscratch[6], fscratch[7]));
+        mean_abs[row] = __fdiv_rn(__fadd_rn(a, b), static_cast<float>(cols));
+    }
+    if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) set_flag(flags, BD_FLAG_NONFINITE_INPUT);
+    s = block_sum_256(s, iscratch);
+    if (threadIdx.x == 0) sums[row] = s;
+}
+
+int launch_quantize_codes(const float *x, int64_t rows, int64_t cols, int64_t ld, const float *gain,
+                          const float *bound, int bits, int8_t *codes, int32_t *sums, int32_t *flags,
+                          int32_t *zero_sums, int zero_count, cudaStream_t stream) {
+    if (rows == 0) return BD_OK;
+    quantize_codes_kernel<<<static_cast<unsigned>(rows), 256, 0, stream>>>(x, cols, ld, gain, bound, bits, codes,
+                                                                           sums, flags, zero_sums, zero_count);
+    BD_CHECK_LAUNCH();
+    return BD_OK;
+}
+
+int launch_quantize_planes(const float *x, int64_t rows, int64_t cols, int64_t ld, int8_t *hi, int8_t *lo,
+                           int32_t *sums_hi, int32_t *sums_lo, float *row_scale, int32_t *flags,
+                           cudaStream_t stream) {
+    if (rows == 0) return BD_OK;
+    quantize_planes_kernel<<<static_cast<unsigned>(rows), 256, 0, stream>>>(x, cols, ld, hi, lo, sums_hi, sums_lo,
+                                                                            row_scale, flags);
+    BD_CHECK_LAUNCH();
+    return BD_OK;
+}
+
+int launch_binarize(const float *x, int64_t rows, int64_t cols, int64_t ld, int8_t *codes, int32_t *sums,
+                    float *mean_abs, uint32_t *words, int64_t words_ld, int32_t *flags, cudaStream_t stream) {
+    if (rows == 0) return BD_OK;
+    binarize_kernel<<<static_cast<unsigned>(rows), 256, 0, stream>>>(x, cols, ld, codes, sums, mean_abs, words,
+                                                                     words_ld, flags);
+    BD_CHECK_LAUNCH();
+    return BD_OK;
+}
+
+}  // namespace bd
+
+extern "C" int64_t bd_codes_ld(int64_t cols) { return cols <= 0 ? 0 : (cols + 255) / 256 * 256; }
+
+extern "C" int bd_quantize_codes(const float *x, int64_t rows, int64_t cols, int64_t ld, const float *gain,
+                                 const float *bound, int bits, int8_t *codes, int32_t *code_sums, int32_t *flags,
+                                 bd_stream_t stream) {
+    if (rows < 0 || cols < 0 || ld < cols || (ld & 3) || (bits != 4 && bits != 8)) return BD_ERR_INVALID;
+    if (rows > 0 && (!x || !gain || !bound || !codes || !code_sums)) return BD_ERR_INVALID;
+    return bd::launch_quantize_codes(x, rows, cols, ld, gain, bound, bits, codes, code_sums, flags, nullptr, 0,
+                                     stream);
+}

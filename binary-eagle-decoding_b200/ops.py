@@ -1,0 +1,304 @@
+"""Torch-facing wrappers of the C ABI: device memory, streams and error flags.
+
+PyTorch supplies device buffers and the current stream; every computation is a
+``libbitdraft.so`` kernel.  Data-dependent errors come back as device flags and
+are raised as the reference's ``ValueError`` messages when the wrapper (or the
+caller, for deferred checks) reads them.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+from torch import Tensor
+
+from . import _lib
+
+MAX_DECODE_TOKENS = 32
+
+
+def _p(t: Tensor | None):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(*tensors: Tensor) -> torch.device:
+    device = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError("bitdraft kernels take CUDA tensors")
+        if not t.is_contiguous():
+            raise ValueError("bitdraft kernels take contiguous tensors")
+        device = t.device if device is None else device
+        if t.device != device:
+            raise ValueError("all tensors must be on one device")
+    if device is None:
+        raise ValueError("no device tensor given")
+    return device
+
+
+class Flags:
+    """A device int32 word the kernels OR error bits into."""
+
+    def __init__(self, device: torch.device):
+        self.tensor = torch.zeros(1, dtype=torch.int32, device=device)
+
+    @property
+    def ptr(self) -> int:
+        return self.tensor.data_ptr()
+
+    def check(self) -> None:
+        value = int(self.tensor.item())
+        if value:
+            self.tensor.zero_()
+            _lib.raise_flags(value)
+
+
+_workspaces: dict[tuple, Tensor] = {}
+
+
+def workspace(device: torch.device, kind: str, nbytes: int) -> Tensor:
+    """A zeroed, cached byte buffer; the kernels leave their workspaces zeroed."""
+    key = (device.index if device.index is not None else torch.cuda.current_device(), kind)
+    buf = _workspaces.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
+        _workspaces[key] = buf
+    return buf
+
+
+# --------------------------------------------------------------------------- signs
+
+
+def pack_signs(latent: Tensor) -> Tensor:
+    """GGUF sign words ``int32 [rows, ceil(cols/32)]`` (export.packed_signs, export.py:79-86)."""
+    if latent.dtype != torch.float32 or latent.ndim != 2:
+        raise ValueError("finite F32 sign matrix required")
+    device = _require_cuda(latent)
+    rows, cols = latent.shape
+    words = torch.empty((rows, (cols + 31) // 32), dtype=torch.int32, device=device)
+    flags = Flags(device)
+    _lib.call("bd_pack_signs", _p(latent), rows, cols, _p(words), flags.ptr, _stream(device))
+    flags.check()
+    return words
+
+
+def t16_words(rows: int, cols: int) -> int:
+    return int(_lib.load().bd_t16_words(rows, cols))
+
+
+def tile_t16(latent: Tensor, block_stride: int = 1, block_offset: int = 0, out: Tensor | None = None,
+             flags: Flags | None = None) -> Tensor:
+    """T16 decode-layout sign words of an F32 latent matrix (int32 storage)."""
+    if latent.dtype != torch.float32 or latent.ndim != 2:
+        raise ValueError("finite F32 sign matrix required")
+    device = _require_cuda(latent)
+    rows, cols = latent.shape
+    if out is None:
+        out = torch.zeros(t16_words(rows, cols) * block_stride, dtype=torch.int32, device=device)
+    own = flags is None
+    flags = flags or Flags(device)
+    _lib.call("bd_tile_signs_t16", _p(latent), rows, cols, _p(out), block_stride, block_offset, flags.ptr,
+              _stream(device))
+    if own:
+        flags.check()
+    return out
+
+
+def tile_gguf_t16(words: Tensor, rows: int, cols: int, block_stride: int = 1, block_offset: int = 0,
+                  out: Tensor | None = None) -> Tensor:
+    device = _require_cuda(words)
+    if out is None:
+        out = torch.zeros(t16_words(rows, cols) * block_stride, dtype=torch.int32, device=device)
+    _lib.call("bd_tile_gguf_t16", _p(words), rows, cols, _p(out), block_stride, block_offset, _stream(device))
+    return out
+
+
+def tile_gate_up(gate: Tensor, up: Tensor, flags: Flags | None = None) -> Tensor:
+    """Gate and up signs with their 16-row blocks interleaved (gate, up, gate, up, ...)."""
+    if gate.shape != up.shape:
+        raise ValueError("gate and up must have one shape")
+    out = torch.zeros(t16_words(*gate.shape) * 2, dtype=torch.int32, device=gate.device)
+    tile_t16(gate, 2, 0, out, flags)
+    tile_t16(up, 2, 1, out, flags)
+    return out
+
+
+# --------------------------------------------------------------------------- projections
+
+
+def codes_ld(cols: int) -> int:
+    return int(_lib.load().bd_codes_ld(cols))
+
+
+def quantize_codes(x: Tensor, gain: Tensor, bound: Tensor, bits: int, flags: Flags | None = None):
+    """HE4 activation codes ``int8 [tokens, ld]`` and exact row sums (model.py:128-140)."""
+    device = _require_cuda(x, gain, bound)
+    rows, cols = x.shape
+    ld = codes_ld(cols)
+    codes = torch.empty((rows, ld), dtype=torch.int8, device=device)
+    sums = torch.empty(rows, dtype=torch.int32, device=device)
+    own = flags is None
+    flags = flags or Flags(device)
+    _lib.call("bd_quantize_codes", _p(x), rows, cols, ld, _p(gain), _p(bound), bits, _p(codes), _p(sums),
+              flags.ptr, _stream(device))
+    if own:
+        flags.check()
+    return codes, sums
+
+
+def projection_he4(codes: Tensor, sums: Tensor, signs_t16: Tensor, in_features: int, scale: Tensor,
+                   midpoint: Tensor, bound: Tensor, bits: int, residual: Tensor | None = None,
+                   raw_dot: bool = False):
+    """HE4 projection forward value from codes (model.py:141-150); optional exact dots."""
+    device = _require_cuda(codes, sums, signs_t16, scale, midpoint, bound, residual)
+    tokens = codes.shape[0]
+    out_features = scale.shape[0]
+    y = torch.empty((tokens, out_features), dtype=torch.float32, device=device)
+    raw = torch.empty((tokens, out_features), dtype=torch.int32, device=device) if raw_dot else None
+    nbytes = int(_lib.load().bd_projection_workspace_bytes(tokens, out_features))
+    ws = workspace(device, "projection", nbytes)
+    _lib.call("bd_projection_he4", _p(codes), _p(sums), tokens, in_features, out_features, _p(signs_t16),
+              _p(scale), _p(midpoint), _p(bound), bits, _p(residual), _p(y), _p(raw), _p(ws), ws.numel(),
+              _stream(device))
+    return (y, raw) if raw_dot else y
+
+
+@dataclass
+class PackedProjection:
+    scale: Tensor
+    midpoint: Tensor
+
+
+@dataclass
+class PackedFFN:
+    """Device-resident sign tiles and epilogue operands of one SwiGLU block."""
+
+    hidden: int
+    inter: int
+    signs_gate_up: Tensor
+    signs_down: Tensor
+    scale_gate: Tensor
+    scale_up: Tensor
+    scale_down: Tensor
+    midpoint_gate: Tensor | None = None
+    midpoint_up: Tensor | None = None
+    midpoint_down: Tensor | None = None
+    gain_gate_up: Tensor | None = None
+    bound_gate_up: Tensor | None = None
+    gain_down: Tensor | None = None
+    bound_down: Tensor | None = None
+
+
+def pack_ffn(gate: Tensor, up: Tensor, down: Tensor, scale_gate: Tensor | None = None,
+             scale_up: Tensor | None = None, scale_down: Tensor | None = None) -> PackedFFN:
+    """Pack latent F32 matrices; row scales default to ``mean|W|`` (model.py:123)."""
+    flags = Flags(gate.device)
+    signs_gate_up = tile_gate_up(gate.contiguous(), up.contiguous(), flags)
+    signs_down = tile_t16(down.contiguous(), flags=flags)
+    flags.check()
+    return PackedFFN(
+        hidden=gate.shape[1], inter=gate.shape[0], signs_gate_up=signs_gate_up, signs_down=signs_down,
+        scale_gate=(gate.abs().mean(-1) if scale_gate is None else scale_gate).contiguous(),
+        scale_up=(up.abs().mean(-1) if scale_up is None else scale_up).contiguous(),
+        scale_down=(down.abs().mean(-1) if scale_down is None else scale_down).contiguous(),
+    )
+
+
+def ffn_he4(x: Tensor, ffn: PackedFFN, residual: Tensor | None = None, hidden_out: bool = False,
+            flags: Flags | None = None):
+    """HE4 SwiGLU block ``residual + down(silu(gate(x)) * up(x))`` (model.py:220-223)."""
+    device = _require_cuda(x, residual)
+    tokens = x.shape[0]
+    if not 1 <= tokens <= MAX_DECODE_TOKENS:
+        raise ValueError("decode feed-forward takes 1 to 32 tokens")
+    y = torch.empty((tokens, ffn.hidden), dtype=torch.float32, device=device)
+    h = torch.empty((tokens, ffn.inter), dtype=torch.float32, device=device) if hidden_out else None
+    nbytes = int(_lib.load().bd_ffn_workspace_bytes(tokens, ffn.hidden, ffn.inter))
+    ws = workspace(device, "ffn", nbytes)
+    own = flags is None
+    flags = flags or Flags(device)
+    args = _lib.FfnHe4Args(
+        _p(x), _p(residual), _p(y), tokens, ffn.hidden, ffn.inter, _p(ffn.signs_gate_up), _p(ffn.scale_gate),
+        _p(ffn.midpoint_gate), _p(ffn.scale_up), _p(ffn.midpoint_up), _p(ffn.gain_gate_up), _p(ffn.bound_gate_up),
+        _p(ffn.signs_down), _p(ffn.scale_down), _p(ffn.midpoint_down), _p(ffn.gain_down), _p(ffn.bound_down),
+        _p(h), _p(ws), ws.numel(), flags.ptr,
+    )
+    _lib.call("bd_ffn_he4", _lib.ctypes.byref(args), _stream(device))
+    if own:
+        flags.check()
+    return (y, h) if hidden_out else y
+
+
+def ffn_w1(x: Tensor, ffn: PackedFFN, hidden_out: bool = False, flags: Flags | None = None):
+    """Pure one-bit-weight SwiGLU with fp32 activations (16-bit fixed point inside)."""
+    device = _require_cuda(x)
+    tokens = x.shape[0]
+    if not 1 <= tokens <= MAX_DECODE_TOKENS:
+        raise ValueError("decode feed-forward takes 1 to 32 tokens")
+    y = torch.empty((tokens, ffn.hidden), dtype=torch.float32, device=device)
+    h = torch.empty((tokens, ffn.inter), dtype=torch.float32, device=device) if hidden_out else None
+    nbytes = int(_lib.load().bd_ffn_workspace_bytes(tokens, ffn.hidden, ffn.inter))
+    ws = workspace(device, "ffn", nbytes)
+    own = flags is None
+    flags = flags or Flags(device)
+    args = _lib.FfnW1Args(
+        _p(x), _p(y), tokens, ffn.hidden, ffn.inter, _p(ffn.signs_gate_up), _p(ffn.scale_gate), _p(ffn.scale_up),
+        _p(ffn.signs_down), _p(ffn.scale_down), _p(h), _p(ws), ws.numel(), flags.ptr,
+    )
+    _lib.call("bd_ffn_w1", _lib.ctypes.byref(args), _stream(device))
+    if own:
+        flags.check()
+    return (y, h) if hidden_out else y
+
+
+# --------------------------------------------------------------------------- acceptance
+
+
+def accept_greedy(logits: Tensor, drafts: Tensor, eog: Tensor | None = None, targets: bool = False,
+                  flags: Flags | None = None):
+    """Greedy block acceptance (benchmarks/verifier.py:107-113).
+
+    ``logits`` bf16 ``[B, n+1, V]``, ``drafts`` int32 ``[B, n]``, ``eog`` int32.
+    Returns ``(accepted [B], next_token [B])`` (+ ``targets [B, n+1]``).
+    """
+    if logits.dtype != torch.bfloat16 or logits.ndim != 3:
+        raise ValueError("logits must be bf16 [requests, drafts + 1, vocab]")
+    if drafts.dtype != torch.int32 or drafts.ndim != 2 or logits.shape[:2] != (drafts.shape[0], drafts.shape[1] + 1):
+        raise ValueError("drafts must be int32 [requests, drafts]")
+    device = _require_cuda(logits, drafts, eog)
+    requests, n = drafts.shape
+    accepted = torch.empty(requests, dtype=torch.int32, device=device)
+    nxt = torch.empty(requests, dtype=torch.int32, device=device)
+    tg = torch.empty((requests, n + 1), dtype=torch.int32, device=device) if targets else None
+    nbytes = int(_lib.load().bd_accept_workspace_bytes(requests, n))
+    ws = workspace(device, "accept", nbytes)
+    own = flags is None
+    flags = flags or Flags(device)
+    n_eog = 0 if eog is None else eog.numel()
+    _lib.call("bd_accept_greedy", _p(logits), requests, n, logits.shape[2], _p(drafts), _p(eog), n_eog,
+              _p(accepted), _p(nxt), _p(tg), _p(ws), ws.numel(), flags.ptr, _stream(device))
+    if own:
+        flags.check()
+    return (accepted, nxt, tg) if targets else (accepted, nxt)
+
+
+def argmax_rows(logits: Tensor, flags: Flags | None = None) -> Tensor:
+    """Row argmax of bf16 rows, lowest index on ties (contracts.py:130-137)."""
+    if logits.dtype != torch.bfloat16:
+        raise ValueError("logits must be bf16")
+    device = _require_cuda(logits)
+    rows = logits.numel() // logits.shape[-1]
+    out = torch.empty(logits.shape[:-1], dtype=torch.int32, device=device)
+    own = flags is None
+    flags = flags or Flags(device)
+    _lib.call("bd_argmax_rows_bf16", _p(logits), rows, logits.shape[-1], _p(out), flags.ptr, _stream(device))
+    if own:
+        flags.check()
+    return out

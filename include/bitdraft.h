@@ -1,0 +1,162 @@
+/*
+ * bitdraft.h -- C ABI of the B200 (sm_100a) binary-drafter hot path.
+ *
+ * Plain pointers and sizes only; every pointer argument is DEVICE memory unless
+ * its comment says host.  Every entry point is stream-ordered on the given
+ * cudaStream_t (pass 0 for the legacy default stream), returns an int status
+ * (BD_OK = 0) for host-side validation and launch errors, and reports
+ * data-dependent errors (non-finite inputs, invalid learned bounds) by OR-ing
+ * BD_FLAG_* bits into a device int32 `flags` word that the caller reads after
+ * the stream has reached the call.  The reference raises ValueError for the
+ * same conditions at the same points; the Python host layer turns flags into
+ * ValueError with the reference's messages.
+ *
+ * Each entry point cites the reference (philippesic/binary-eagle-decoding)
+ * interface it replaces.
+ */
+#ifndef BITDRAFT_H
+#define BITDRAFT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *bd_stream_t; /* == cudaStream_t */
+
+/* ---- status codes (host return values) ---- */
+#define BD_OK 0
+#define BD_ERR_INVALID 1   /* bad shape, null pointer or unsupported size */
+#define BD_ERR_ALIGNMENT 2 /* pointer not aligned as documented */
+#define BD_ERR_LAUNCH 3    /* CUDA launch or runtime error */
+#define BD_ERR_WORKSPACE 4 /* workspace too small */
+#define BD_ERR_DEVICE 5    /* no usable sm_100 device */
+
+/* ---- device-reported flags (OR-ed into *flags) ---- */
+#define BD_FLAG_NONFINITE_LATENT 1u   /* export.py:80-81 "finite F32 sign matrix required" */
+#define BD_FLAG_NONFINITE_INPUT 2u    /* model.py:130-131 "nonfinite quantizer input" */
+#define BD_FLAG_BAD_BOUND 4u          /* model.py:133-134 "invalid learned clipping bound" */
+#define BD_FLAG_NONFINITE_LOGITS 8u   /* verifier-trace.hpp:30 "nonfinite verifier logits" */
+#define BD_FLAG_BAD_TOKEN 16u         /* a draft token outside [0, vocab) */
+#define BD_FLAG_NONFINITE_STATE 32u   /* non-finite values in a forward / update */
+#define BD_FLAG_CACHE_OVERFLOW 64u    /* model.py:100-101 "F16 cache storage overflow" */
+
+int bd_abi_version(void);
+const char *bd_status_string(int status);
+/* Number of SMs of the current device and whether it is sm_100 (host query). */
+int bd_device_info(int *sm_count, int *major, int *minor);
+
+/* ====================================================================== signs
+ * bd_pack_signs replaces export.packed_signs (w1a1_eagle/numerical/export.py:79-86):
+ * words[r * ceil(cols/32) + w] bit j = latent[r, 32 w + j] >= 0 (padding bits 0).
+ * Sets BD_FLAG_NONFINITE_LATENT if any latent is not finite (words still written).
+ */
+int bd_pack_signs(const float *latent, int64_t rows, int64_t cols, int32_t *words,
+                  int32_t *flags, bd_stream_t stream);
+
+/* T16 tiled sign layout used by the decode kernels (see DESIGN: "T16").  Words:
+ * bd_t16_words(rows, cols) uint32.  `block_stride`/`block_offset` interleave
+ * several matrices' 16-row blocks into one buffer (stride 2, offset 0/1 puts
+ * gate and up row blocks side by side); pass 1/0 for a plain matrix.  Replaces
+ * the sign materialisation of hard_sign (w1a1_eagle/model.py:92-95) for the
+ * forward: the packed bits ARE the signs. */
+int64_t bd_t16_words(int64_t rows, int64_t cols);
+int bd_tile_signs_t16(const float *latent, int64_t rows, int64_t cols, uint32_t *tiled,
+                      int block_stride, int block_offset, int32_t *flags, bd_stream_t stream);
+/* Same tiling from GGUF words (as written by bd_pack_signs / export_he4). */
+int bd_tile_gguf_t16(const int32_t *words, int64_t rows, int64_t cols, uint32_t *tiled,
+                     int block_stride, int block_offset, bd_stream_t stream);
+
+/* =================================================================== quantizer
+ * bd_quantize_codes replaces the activation quantizer of Projection.forward
+ * (w1a1_eagle/model.py:128-140): codes[t * ld + k] = clamp(rint(clip(x*gain,
+ * +-bound) * (1/bound * max)), +-max) as int8, max = 2^(bits-1) - 1; columns
+ * cols..ld-1 are written 0; code_sums[t] = exact sum of the row's codes.
+ * gain [cols] and bound [1] are the exponentiated parameters (device). */
+int bd_quantize_codes(const float *x, int64_t rows, int64_t cols, int64_t ld, const float *gain,
+                      const float *bound, int bits, int8_t *codes, int32_t *code_sums,
+                      int32_t *flags, bd_stream_t stream);
+
+/* ================================================================ projections
+ * One HE4 projection (w1a1_eagle/model.py:141-150, forward value):
+ * y[t, o] = (D[t,o] * max(scale[o],0)) * step + (code_sums[t] * step) * midpoint[o]
+ *           (+ residual[t, o] if residual != NULL), D = exact codes . signs.
+ * signs: T16 [out, in]; codes from bd_quantize_codes with ld = bd_codes_ld(in).
+ * tokens <= 32.  raw_dot (optional) receives the exact integer D.  The
+ * workspace (bd_projection_workspace_bytes) holds split-K accumulators; zero it
+ * once before first use (the kernels leave it zeroed). */
+int64_t bd_codes_ld(int64_t cols);
+size_t bd_projection_workspace_bytes(int tokens, int64_t out_features);
+int bd_projection_he4(const int8_t *codes, const int32_t *code_sums, int tokens, int64_t in_features,
+                      int64_t out_features, const uint32_t *signs_t16, const float *scale,
+                      const float *midpoint, const float *bound, int bits, const float *residual,
+                      float *y, int32_t *raw_dot, void *workspace, size_t workspace_bytes,
+                      bd_stream_t stream);
+
+/* ============================================================ feed-forward blocks
+ * HE4 SwiGLU block, the FFN of Layer.forward / Layer.group
+ * (w1a1_eagle/model.py:220-223, 271-274):
+ *   y = residual + down(silu(gate(n)) * up(n)),
+ * gate/up: 4-bit codes with the shared gain/bound (model.py:184-187),
+ * down: 8-bit codes with its own gain/bound (model.py:188-193).
+ * signs_gate_up: T16 of gate and up interleaved (block_stride 2, offsets 0/1);
+ * signs_down: T16 [hidden, inter].  tokens <= 32.  Workspace: see
+ * bd_ffn_workspace_bytes; zero it once before first use (kernels leave it zeroed). */
+typedef struct {
+    const float *x;          /* [tokens, hidden] normalised input n            */
+    const float *residual;   /* [tokens, hidden] or NULL                        */
+    float *y;                /* [tokens, hidden]                                */
+    int tokens;
+    int64_t hidden, inter;
+    const uint32_t *signs_gate_up;
+    const float *scale_gate, *midpoint_gate, *scale_up, *midpoint_up;
+    const float *gain_gate_up; /* [hidden] */
+    const float *bound_gate_up; /* [1] */
+    const uint32_t *signs_down;
+    const float *scale_down, *midpoint_down;
+    const float *gain_down;  /* [inter] */
+    const float *bound_down; /* [1] */
+    float *hidden_out;       /* optional [tokens, inter] silu(gate)*up, or NULL */
+    void *workspace;
+    size_t workspace_bytes;
+    int32_t *flags;
+} bd_ffn_he4_args;
+size_t bd_ffn_workspace_bytes(int tokens, int64_t hidden, int64_t inter);
+int bd_ffn_he4(const bd_ffn_he4_args *args, bd_stream_t stream);
+
+/* Pure one-bit-weight SwiGLU (fp32 activations; no reference module -- built
+ * from hard_sign (model.py:92-95) and the mean|W| row scale (model.py:123)):
+ *   y = sd * sign(Wd) . (silu(sg * sign(Wg) x) * (su * sign(Wu) x)).
+ * Activations are carried as per-token 16-bit fixed point (two int8 planes,
+ * exact integer accumulation).  tokens <= 32. */
+typedef struct {
+    const float *x; float *y; int tokens; int64_t hidden, inter;
+    const uint32_t *signs_gate_up; const float *scale_gate, *scale_up;
+    const uint32_t *signs_down; const float *scale_down;
+    float *hidden_out; void *workspace; size_t workspace_bytes; int32_t *flags;
+} bd_ffn_w1_args;
+int bd_ffn_w1(const bd_ffn_w1_args *args, bd_stream_t stream);
+
+/* ================================================================== acceptance
+ * Greedy block acceptance (benchmarks/verifier.py:92-137 core loop 107-113,
+ * argmax rule w1a1_eagle/contracts.py:130-137 and native/verifier-trace.hpp:28-34):
+ * logits bf16 [requests, drafts+1, vocab] (row-major, raw uint16 bits),
+ * drafts int32 [requests, drafts]; eog int32 [n_eog] (sorted or not).
+ * Outputs accepted[requests], next_token[requests], targets[requests*(drafts+1)]
+ * (targets may be NULL).  emitted = drafts[:accepted] + [next_token]. */
+size_t bd_accept_workspace_bytes(int requests, int drafts);
+int bd_accept_greedy(const uint16_t *logits, int requests, int drafts, int64_t vocab,
+                     const int32_t *draft_tokens, const int32_t *eog, int n_eog,
+                     int32_t *accepted, int32_t *next_token, int32_t *targets,
+                     void *workspace, size_t workspace_bytes, int32_t *flags, bd_stream_t stream);
+
+/* Row argmax of bf16 or fp32 rows (lowest index on ties), used for drafting. */
+int bd_argmax_rows_bf16(const uint16_t *logits, int64_t rows, int64_t vocab, int32_t *out,
+                        int32_t *flags, bd_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BITDRAFT_H */

@@ -160,8 +160,12 @@ def quantize_codes(value: np.ndarray, gain: np.ndarray, bound, bits: int):
 
 
 def integer_dot(codes: np.ndarray, bits_pm: np.ndarray) -> np.ndarray:
-    """Exact ``codes @ signs.T`` for integer codes and +-1 signs (int64)."""
-    return codes.astype(np.int64) @ bits_pm.astype(np.int64).T
+    """Exact ``codes @ signs.T`` for integer codes and +-1 signs (int64).
+
+    Evaluated in float64 BLAS: every product and partial sum is an integer of
+    magnitude below 2^53, so the result is exact.
+    """
+    return np.rint(codes.astype(np.float64) @ bits_pm.astype(np.float64).T).astype(np.int64)
 
 
 def projection_forward(value, latent, scale, midpoint, gain, bound, bits: int) -> np.ndarray:

@@ -1,0 +1,49 @@
+"""The C-ABI library loads and exports every declared symbol (no GPU needed)."""
+
+from __future__ import annotations
+
+import ctypes
+import subprocess
+
+import pytest
+
+from conftest import submodule
+
+
+def test_library_exports_every_header_symbol():
+    lib = submodule("_lib")
+    names = lib.header_symbols()
+    assert len(names) >= 15
+    handle = lib.load()
+    missing = [n for n in names if not hasattr(handle, n)]
+    assert not missing, missing
+    # every declared symbol has a Python signature and vice versa
+    assert set(names) == set(lib.SIGNATURES), set(names) ^ set(lib.SIGNATURES)
+
+
+def test_library_is_sm100a_and_pure_c_abi():
+    lib = submodule("_lib")
+    out = subprocess.run(["nm", "-D", "--defined-only", str(lib.LIBRARY)], capture_output=True, text=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    assert {n for n in exported if n.startswith("bd_")} == set(lib.header_symbols())
+
+
+def test_host_only_entry_points():
+    lib = submodule("_lib").load()
+    assert lib.bd_abi_version() == 1
+    assert lib.bd_status_string(0) == b"ok"
+    assert lib.bd_t16_words(9728, 2560) == 608 * 10 * 128
+    assert lib.bd_t16_words(1, 1) == 128
+    assert lib.bd_codes_ld(2560) == 2560 and lib.bd_codes_ld(1) == 256
+    assert lib.bd_ffn_workspace_bytes(16, 2560, 9728) > 0
+    # host-side validation happens before any device work
+    assert lib.bd_pack_signs(None, -1, 4, None, None, None) == 1
+    assert lib.bd_quantize_codes(None, 1, 8, 8, None, None, 5, None, None, None, None) == 1
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    lib = submodule("_lib")
+    monkeypatch.setattr(lib, "_lib", None)
+    monkeypatch.setattr(lib, "LIBRARY", tmp_path / "libbitdraft.so")
+    with pytest.raises(RuntimeError, match="not built"):
+        lib.load()

@@ -1,0 +1,288 @@
+"""CUDA kernels against the oracle and the reference fixtures (needs a B200)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN, package
+from oracle import acceptance, core
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda:0")
+
+
+@pytest.fixture(scope="module")
+def ops():
+    return package().ops
+
+
+def dev(a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+    return t if dtype is None else t.to(dtype)
+
+
+def rel(a, b):
+    return float(np.linalg.norm(np.asarray(a, np.float64) - b) / max(np.linalg.norm(np.asarray(b, np.float64)), 1e-30))
+
+
+# ------------------------------------------------------------------ signs
+
+
+def test_pack_signs_reference_fixture(ops):
+    f = np.load(GOLDEN / "packing.npz")
+    assert np.array_equal(ops.pack_signs(dev(f["kat_value"])).cpu().numpy(), f["kat_words"])
+    for columns in (1, 7, 8, 31, 32, 33, 65, 300):
+        got = ops.pack_signs(dev(f[f"value_{columns}"])).cpu().numpy()
+        assert np.array_equal(got, f[f"words_{columns}"]), columns
+
+
+def test_pack_signs_random_and_nonfinite(ops):
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((1031, 2561)).astype(np.float32)
+    x[3, 5] = -0.0
+    assert np.array_equal(ops.pack_signs(dev(x)).cpu().numpy(), core.packed_signs(x))
+    x[7, 9] = np.nan
+    with pytest.raises(ValueError, match="finite F32 sign matrix required"):
+        ops.pack_signs(dev(x))
+    with pytest.raises(ValueError):
+        ops.pack_signs(dev(x.astype(np.float64)))
+
+
+@pytest.mark.parametrize("shape", [(1, 1), (16, 256), (17, 257), (48, 700), (100, 2560)])
+def test_tile_t16_matches_oracle(ops, shape):
+    rng = np.random.default_rng(shape[0] * 7 + shape[1])
+    x = rng.standard_normal(shape).astype(np.float32)
+    x[0, 0] = -0.0
+    got = ops.tile_t16(dev(x)).cpu().numpy().view(np.uint32)
+    assert np.array_equal(got, core.tile_signs_t16(x))
+
+
+def test_tile_from_gguf_equals_direct_full_size(ops):
+    # size-independent property at the full gate shape: GGUF words -> T16 == latent -> T16
+    g = torch.Generator(device=DEV).manual_seed(2)
+    x = torch.randn((9728, 2560), generator=g, device=DEV) * 0.02
+    words = ops.pack_signs(x)
+    assert torch.equal(ops.tile_gguf_t16(words, 9728, 2560), ops.tile_t16(x))
+    y = torch.randn((2560, 9728), generator=g, device=DEV)
+    assert torch.equal(ops.tile_gguf_t16(ops.pack_signs(y), 2560, 9728), ops.tile_t16(y))
+
+
+# ------------------------------------------------------------------ quantizer + projections
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_quantize_codes_bit_exact(ops, bits):
+    rng = np.random.default_rng(bits)
+    x = (rng.standard_normal((13, 777)) * 2).astype(np.float32)
+    gain = np.exp(rng.standard_normal(777).astype(np.float32) * 0.3).astype(np.float32)
+    bound = np.float32(0.83)
+    codes, sums = ops.quantize_codes(dev(x), dev(gain), dev(np.array([bound])), bits)
+    want, _ = core.quantize_codes(x, gain, bound, bits)
+    got = codes.cpu().numpy()
+    assert np.array_equal(got[:, :777], want.astype(np.int8))
+    assert not got[:, 777:].any()
+    assert np.array_equal(sums.cpu().numpy(), want.sum(-1).astype(np.int32))
+    with pytest.raises(ValueError, match="invalid learned clipping bound"):
+        ops.quantize_codes(dev(x), dev(gain), dev(np.array([np.float32(-1.0)])), bits)
+    x[2, 3] = np.inf
+    with pytest.raises(ValueError, match="nonfinite quantizer input"):
+        ops.quantize_codes(dev(x), dev(gain), dev(np.array([bound])), bits)
+
+
+def projection_cases():
+    f = np.load(GOLDEN / "projection.npz")
+    for i in range(int(f["count"])):
+        yield {k.split("_", 1)[1]: f[k] for k in f.files if k.startswith(f"{i}_")}
+
+
+def run_projection(ops, x, latent, scale, midpoint, gain, bound, bits, residual=None):
+    codes, sums = ops.quantize_codes(dev(x), dev(gain), dev(np.array([bound], np.float32)), bits)
+    signs = ops.tile_t16(dev(latent))
+    return ops.projection_he4(codes, sums, signs, latent.shape[1], dev(scale), dev(midpoint),
+                              dev(np.array([bound], np.float32)), bits,
+                              residual=None if residual is None else dev(residual), raw_dot=True)
+
+
+def test_projection_he4_bit_exact_against_reference_fixture(ops):
+    for c in projection_cases():
+        y, _ = run_projection(ops, c["value"], c["latent"], c["scale"], c["midpoint"], c["gain"], c["bound"],
+                              int(c["bits"]))
+        assert np.array_equal(y.cpu().numpy(), c["output"]), int(c["bits"])
+
+
+@pytest.mark.parametrize("tokens,inner,outer,bits", [(16, 2560, 9728, 4), (16, 9728, 2560, 8), (1, 2560, 9728, 4),
+                                                     (32, 300, 70, 8), (9, 9728, 2560, 4), (24, 513, 1000, 8)])
+def test_projection_he4_bit_exact_full_sizes(ops, tokens, inner, outer, bits):
+    rng = np.random.default_rng(tokens * 1000 + outer)
+    x = rng.standard_normal((tokens, inner)).astype(np.float32)
+    w = (rng.standard_normal((outer, inner)) * 0.02).astype(np.float32)
+    scale = np.abs(w).mean(-1, dtype=np.float32)
+    mid = (rng.standard_normal(outer) * 0.01).astype(np.float32)
+    gain = np.exp(rng.standard_normal(inner).astype(np.float32) * 0.2).astype(np.float32)
+    bound = np.float32(1.3)
+    res = rng.standard_normal((tokens, outer)).astype(np.float32)
+    y, raw = run_projection(ops, x, w, scale, mid, gain, bound, bits, residual=res)
+    codes, _ = core.quantize_codes(x, gain, bound, bits)
+    want_dot = core.integer_dot(codes, core.hard_sign(w))
+    assert np.array_equal(raw.cpu().numpy(), want_dot.astype(np.int32))
+    want = (res + core.projection_forward(x, w, scale, mid, gain, bound, bits)).astype(np.float32)
+    assert np.array_equal(y.cpu().numpy(), want)
+    # the split-K workspace is left zeroed: a second call gives identical results
+    y2, raw2 = run_projection(ops, x, w, scale, mid, gain, bound, bits, residual=res)
+    assert torch.equal(y, y2) and torch.equal(raw, raw2)
+
+
+# ------------------------------------------------------------------ feed-forward blocks
+
+
+def he4_params(f, name):
+    return {k: f[f"{name}_{k}"] for k in ("latent", "scale", "midpoint", "gain", "bound")}
+
+
+def pack_he4(ops, gate, up, down):
+    ffn = ops.pack_ffn(dev(gate["latent"]), dev(up["latent"]), dev(down["latent"]), dev(gate["scale"]),
+                       dev(up["scale"]), dev(down["scale"]))
+    ffn.midpoint_gate, ffn.midpoint_up, ffn.midpoint_down = dev(gate["midpoint"]), dev(up["midpoint"]), dev(down["midpoint"])
+    ffn.gain_gate_up, ffn.bound_gate_up = dev(gate["gain"]), dev(np.atleast_1d(np.float32(gate["bound"])))
+    ffn.gain_down, ffn.bound_down = dev(down["gain"]), dev(np.atleast_1d(np.float32(down["bound"])))
+    return ffn
+
+
+def test_ffn_he4_against_reference_fixture(ops):
+    f = np.load(GOLDEN / "he4_ffn.npz")
+    gate, up, down = he4_params(f, "gate"), he4_params(f, "up"), he4_params(f, "down")
+    ffn = pack_he4(ops, gate, up, down)
+    y, h = ops.ffn_he4(dev(f["norm"]), ffn, dev(f["residual"]), hidden_out=True)
+    np.testing.assert_allclose(h.cpu().numpy(), f["hidden"], rtol=1e-6, atol=1e-7)
+    np.testing.assert_allclose(y.cpu().numpy(), f["output"], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("tokens", [16, 1, 7, 32])
+def test_ffn_he4_config1_shape(ops, tokens):
+    rng = np.random.default_rng(100 + tokens)
+    H, F = 2560, 9728
+    mats = {"gate": (F, H), "up": (F, H), "down": (H, F)}
+    params = {}
+    for name, shape in mats.items():
+        w = (rng.standard_normal(shape) * 0.02).astype(np.float32)
+        params[name] = {"latent": w, "scale": np.abs(w).mean(-1, dtype=np.float32),
+                        "midpoint": (rng.standard_normal(shape[0]) * 1e-3).astype(np.float32),
+                        "gain": np.exp(rng.standard_normal(shape[1]).astype(np.float32) * 0.1).astype(np.float32),
+                        "bound": np.float32(2.0 if name != "down" else 0.05)}
+    params["up"]["gain"], params["up"]["bound"] = params["gate"]["gain"], params["gate"]["bound"]
+    x = rng.standard_normal((tokens, H)).astype(np.float32)
+    res = rng.standard_normal((tokens, H)).astype(np.float32)
+    ffn = pack_he4(ops, params["gate"], params["up"], params["down"])
+    y, h = ops.ffn_he4(dev(x), ffn, dev(res), hidden_out=True)
+    g = core.projection_forward(x, **{k: params["gate"][k] for k in ("latent", "scale", "midpoint", "gain", "bound")}, bits=4)
+    u = core.projection_forward(x, **{k: params["up"][k] for k in ("latent", "scale", "midpoint", "gain", "bound")}, bits=4)
+    want_h = (core.silu(g) * u).astype(np.float32)
+    assert rel(h.cpu().numpy(), want_h) < 1e-6
+    want = core.he4_ffn(x, res, params["gate"], params["up"], params["down"])
+    assert rel(y.cpu().numpy() - res, want - res) < 1e-3
+    # the down projection given the device's own hidden state is bit-exact
+    down_given_h = core.projection_forward(h.cpu().numpy(), **{k: params["down"][k] for k in
+                                                               ("latent", "scale", "midpoint", "gain", "bound")}, bits=8)
+    assert np.array_equal(y.cpu().numpy(), (res + down_given_h).astype(np.float32))
+
+
+def test_ffn_w1_reference_parts_fixture(ops):
+    f = np.load(GOLDEN / "w1_ffn.npz")
+    ffn = ops.pack_ffn(dev(f["w_gate"]), dev(f["w_up"]), dev(f["w_down"]))
+    y = ops.ffn_w1(dev(f["x"]), ffn)
+    assert rel(y.cpu().numpy(), f["y"]) < 1e-3
+
+
+@pytest.mark.parametrize("tokens", [16, 3, 32])
+def test_ffn_w1_config1(ops, tokens):
+    # config 1: x N(0,1) [16, 2560]; W N(0, 0.02) seeds 1/2/3; tolerance 1e-2 relative (bf16-class)
+    H, F = 2560, 9728
+    x = torch.randn((tokens, H), generator=torch.Generator().manual_seed(0)).numpy()
+    wg = (torch.randn((F, H), generator=torch.Generator().manual_seed(1)) * 0.02).numpy()
+    wu = (torch.randn((F, H), generator=torch.Generator().manual_seed(2)) * 0.02).numpy()
+    wd = (torch.randn((H, F), generator=torch.Generator().manual_seed(3)) * 0.02).numpy()
+    ffn = ops.pack_ffn(dev(wg), dev(wu), dev(wd))
+    y = ops.ffn_w1(dev(x), ffn).cpu().numpy()
+    want = core.w1_ffn(x, wg, wu, wd)
+    err = rel(y, want)
+    assert err < 1e-2, err
+    np.testing.assert_allclose(y, want, rtol=1e-2, atol=1e-2 * np.abs(want).max())
+
+
+# ------------------------------------------------------------------ greedy acceptance
+
+
+def planted(logits, seed):
+    """Drafts equal to the target argmax for a random prefix, then a mismatch."""
+    rng = np.random.default_rng(seed)
+    B, P, V = logits.shape
+    targets = logits.float().argmax(-1).numpy()
+    drafts = rng.integers(0, V, size=(B, P - 1)).astype(np.int32)
+    for b in range(B):
+        cut = int(rng.integers(0, P))
+        drafts[b, :cut] = targets[b, :cut]
+    return drafts
+
+
+def test_greedy_config4_full_size(ops):
+    B, P, V = 32, 17, 151936
+    logits = (torch.randn((B, P, V), generator=torch.Generator().manual_seed(5)) * 3).to(torch.bfloat16)
+    drafts = planted(logits, 6)
+    uniform = torch.randint(0, V, (B, P - 1), generator=torch.Generator().manual_seed(6)).to(torch.int32).numpy()
+    eog = np.array([int(drafts[3, 0]), 151643], dtype=np.int32)
+    for d in (drafts, uniform):
+        acc, nxt, tg = ops.accept_greedy(logits.to(DEV), dev(d), dev(eog), targets=True)
+        w_acc, w_nxt, w_tg = acceptance.accept_greedy(logits.float().numpy(), d, eog.tolist())
+        assert np.array_equal(tg.cpu().numpy(), w_tg)
+        assert np.array_equal(acc.cpu().numpy(), w_acc)
+        assert np.array_equal(nxt.cpu().numpy(), w_nxt)
+    assert acc.cpu().numpy().max() <= 16
+
+
+def test_greedy_ties_signed_zero_and_odd_vocab(ops):
+    for V in (1, 7, 8, 1001, 4099):
+        rows = np.zeros((3, 4, V), np.float32)
+        rows[0, :, V // 2:] = 1.0  # ties -> lowest index V//2
+        rows[1] = -1.0
+        rows[1, :, 0] = -0.0       # -0.0 == +0.0 -> the first of them wins
+        rows[1, :, V - 1] = 0.0
+        rows[2] = np.random.default_rng(V).integers(-2, 2, size=(4, V))
+        logits = torch.from_numpy(rows).to(torch.bfloat16)
+        drafts = np.full((3, 3), 0, np.int32)
+        acc, nxt, tg = ops.accept_greedy(logits.to(DEV), dev(drafts), None, targets=True)
+        w_acc, w_nxt, w_tg = acceptance.accept_greedy(logits.float().numpy(), drafts)
+        assert np.array_equal(tg.cpu().numpy(), w_tg), V
+        assert np.array_equal(acc.cpu().numpy(), w_acc) and np.array_equal(nxt.cpu().numpy(), w_nxt)
+
+
+def test_greedy_eog_and_zero_drafts_and_nonfinite(ops):
+    V = 128
+
+    def logits_for(targets):
+        rows = np.full((1, len(targets), V), -5.0, np.float32)
+        for i, t in enumerate(targets):
+            rows[0, i, t] = 3.0
+        return torch.from_numpy(rows).to(torch.bfloat16).to(DEV)
+
+    eog = dev(np.array([99], np.int32))
+    acc, nxt = ops.accept_greedy(logits_for([5, 9, 10]), dev(np.array([[5, 6]], np.int32)), eog)
+    assert (int(acc), int(nxt)) == (1, 9)
+    acc, nxt = ops.accept_greedy(logits_for([99, 7, 1]), dev(np.array([[99, 7]], np.int32)), eog)
+    assert (int(acc), int(nxt)) == (0, 99)
+    acc, nxt = ops.accept_greedy(logits_for([5, 99]), dev(np.array([[5]], np.int32)), eog)
+    assert (int(acc), int(nxt)) == (1, 99)  # an accepted EOG as the last draft still gets the bonus
+    acc, nxt = ops.accept_greedy(logits_for([42]), dev(np.zeros((1, 0), np.int32)), eog)
+    assert (int(acc), int(nxt)) == (0, 42)
+    bad = logits_for([1, 2])
+    bad[0, 1, 3] = float("inf")
+    with pytest.raises(ValueError, match="nonfinite verifier logits"):
+        ops.accept_greedy(bad, dev(np.array([[1]], np.int32)), eog)
+
+
+def test_argmax_rows(ops):
+    x = (torch.randn((16, 151936), generator=torch.Generator().manual_seed(9)) * 3).to(torch.bfloat16)
+    got = ops.argmax_rows(x.to(DEV)).cpu().numpy()
+    assert np.array_equal(got, acceptance.argmax_rows(x.float().numpy()))
