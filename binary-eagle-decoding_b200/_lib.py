@@ -66,6 +66,7 @@ SIGNATURES = {
     "bd_tile_gguf_t16": (c_int, [P, c_int64, c_int64, P, c_int, c_int, P]),
     "bd_quantize_codes": (c_int, [P, c_int64, c_int64, c_int64, P, P, c_int, P, P, P, P]),
     "bd_codes_ld": (c_int64, [c_int64]),
+    "bd_codes_bytes": (c_int64, [c_int64, c_int64]),
     "bd_projection_workspace_bytes": (c_size_t, [c_int, c_int64]),
     "bd_projection_he4": (c_int, [P, P, c_int, c_int64, c_int64, P, P, P, P, c_int, P, P, P, P, c_size_t, P]),
     "bd_ffn_workspace_bytes": (c_size_t, [c_int, c_int64, c_int64]),

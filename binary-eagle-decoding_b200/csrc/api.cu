@@ -47,7 +47,7 @@ static FfnPieces carve_ffn(void *ws, int64_t hidden, int64_t inter, bool planes,
     FfnPieces p{};
     p.codes_in = c.take<int8_t>(kMaxTokens * ld_h);
     p.codes_mid = c.take<int8_t>(kMaxTokens * ld_f);
-    p.sum_in = c.take<int32_t>(kMaxTokens);
+    p.sum_in = c.take<int32_t>(kMaxTokens * quant_parts(hidden));
     p.sum_mid = c.take<int32_t>(kMaxTokens);
     if (planes) {
         p.codes_in_lo = c.take<int8_t>(kMaxTokens * ld_h);
@@ -115,6 +115,7 @@ extern "C" int bd_projection_he4(const int8_t *codes, const int32_t *code_sums, 
     a.ncp = (in_features + 255) / 256;
     a.codes0 = codes;
     a.csum0 = code_sums;
+    a.nparts = 1;
     a.ld = a.ncp * 256;
     a.tokens = tokens;
     a.kgroups = choose_kgroups(out_features, a.ncp, sm_count_cached());
@@ -155,8 +156,10 @@ extern "C" int bd_ffn_he4(const bd_ffn_he4_args *p, bd_stream_t stream) {
     FfnPieces w = carve_ffn(p->workspace, p->hidden, p->inter, false, &need);
     if (!p->workspace || need > p->workspace_bytes) return BD_ERR_WORKSPACE;
     const int64_t ld_h = (p->hidden + 255) / 256 * 256, ld_f = (p->inter + 255) / 256 * 256;
+    // The quantizer writes per-slice partial code sums of the gate/up input and
+    // zeroes the down projection's code sums, which gate/up accumulate.
     int st = launch_quantize_codes(p->x, p->tokens, p->hidden, ld_h, p->gain_gate_up, p->bound_gate_up, 4,
-                                   w.codes_in, w.sum_in, p->flags, w.sum_mid, kMaxTokens, stream);
+                                   w.codes_in, w.sum_in, true, p->flags, w.sum_mid, kMaxTokens, stream);
     if (st) return st;
 
     ProjArgs gu{};
@@ -166,6 +169,7 @@ extern "C" int bd_ffn_he4(const bd_ffn_he4_args *p, bd_stream_t stream) {
     gu.ncp = ld_h / 256;
     gu.codes0 = w.codes_in;
     gu.csum0 = w.sum_in;
+    gu.nparts = quant_parts(p->hidden);
     gu.ld = ld_h;
     gu.tokens = p->tokens;
     gu.kgroups = 1;
@@ -192,6 +196,7 @@ extern "C" int bd_ffn_he4(const bd_ffn_he4_args *p, bd_stream_t stream) {
     dn.ncp = ld_f / 256;
     dn.codes0 = w.codes_mid;
     dn.csum0 = w.sum_mid;
+    dn.nparts = 1;
     dn.ld = ld_f;
     dn.tokens = p->tokens;
     dn.kgroups = choose_kgroups(p->hidden, dn.ncp, sm_count_cached());
@@ -230,6 +235,7 @@ extern "C" int bd_ffn_w1(const bd_ffn_w1_args *p, bd_stream_t stream) {
     gu.codes1 = w.codes_in_lo;
     gu.csum0 = w.sum_in;
     gu.csum1 = w.sum_in_lo;
+    gu.nparts = 1;
     gu.ld = ld_h;
     gu.tokens = p->tokens;
     gu.kgroups = 1;
@@ -253,6 +259,7 @@ extern "C" int bd_ffn_w1(const bd_ffn_w1_args *p, bd_stream_t stream) {
     dn.codes1 = w.codes_mid_lo;
     dn.csum0 = w.sum_mid;
     dn.csum1 = w.sum_mid_lo;
+    dn.nparts = 1;
     dn.ld = ld_f;
     dn.tokens = p->tokens;
     dn.kgroups = choose_kgroups(p->hidden, dn.ncp, sm_count_cached());

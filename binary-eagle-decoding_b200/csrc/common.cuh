@@ -54,6 +54,35 @@ __device__ __forceinline__ uint4 ld_stream_u4(const void *p) {
     return v;
 }
 
+// 16-byte asynchronous global->shared copy; src_bytes 0 writes zeros.
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem, int src_bytes) {
+    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(src_bytes));
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
+}
+
+// Programmatic dependent launch: a kernel launched with the PDL attribute may
+// start while its predecessor finishes; before grid_wait() it may only read
+// data no earlier kernel writes (weights), and it must not write anything.
+__device__ __forceinline__ void grid_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n"); }
+
+// B-fragment layout of int8 activation codes ("F8"): blocks of 8 tokens by 64
+// columns (a pair of 32-column k-steps), 512 bytes each, nt-major; inside a
+// block, lane l = 4 g + t (token 8 nt + g) holds 16 bytes: for k-step s of the
+// pair, bytes 8 (s & 1) + 4 h + j are the codes of column 32 s + 16 h + 4 t + j.
+// nsp = row stride in column pairs (ld / 64).
+__device__ __forceinline__ int64_t frag_offset(int token, int64_t k, int64_t nsp) {
+    const int64_t nt = token >> 3;
+    const int g = token & 7;
+    const int64_t s = k >> 5;
+    const int kk = static_cast<int>(k & 31);
+    const int half = kk >> 4, t = (kk & 15) >> 2, j = kk & 3;
+    return (((nt * nsp + (s >> 1)) * 32 + g * 4 + t) << 4) + ((s & 1) << 3) + (half << 2) + j;
+}
+
 // The quantizer of Projection.forward for one element (see bd_quantize_codes).
 struct Quant {
     float bound, ratio, step, maximum;

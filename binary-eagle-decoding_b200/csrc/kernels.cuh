@@ -1,12 +1,34 @@
 // Internal launch helpers shared between the library's translation units.
 #pragma once
 
+#include <utility>
+
 #include "common.cuh"
 
 namespace bd {
 
+// Launch with programmatic stream serialization (the kernel calls grid_wait()
+// before touching anything an earlier kernel writes).
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...) == cudaSuccess ? BD_OK : BD_ERR_LAUNCH;
+}
+
+// Column slices (of 1024) of the HE4 quantizer grid = partial code sums per row.
+inline int quant_parts(int64_t cols) { return static_cast<int>((cols + 1023) / 1024); }
+
 int launch_quantize_codes(const float *x, int64_t rows, int64_t cols, int64_t ld, const float *gain,
-                          const float *bound, int bits, int8_t *codes, int32_t *sums, int32_t *flags,
+                          const float *bound, int bits, int8_t *codes, int32_t *sums, bool partial, int32_t *flags,
                           int32_t *zero_sums, int zero_count, cudaStream_t stream);
 int launch_quantize_planes(const float *x, int64_t rows, int64_t cols, int64_t ld, int8_t *hi, int8_t *lo,
                            int32_t *sums_hi, int32_t *sums_lo, float *row_scale, int32_t *flags,
@@ -27,10 +49,11 @@ struct ProjArgs {
     int64_t rows;             // output features (per matrix)
     int64_t cols;             // input features
     int64_t ncp;              // column pairs
-    const int8_t *codes0;     // [tokens][ld] plane 0
+    const int8_t *codes0;     // F8 fragment layout (frag_offset), plane 0
     const int8_t *codes1;     // plane 1 (W1) or null
-    const int32_t *csum0;     // [tokens]
+    const int32_t *csum0;     // [tokens][nparts] partial code sums
     const int32_t *csum1;
+    int nparts;               // partial sums per token (1: full sums)
     int64_t ld;               // codes row stride (multiple of 256)
     int tokens;
     int kgroups;              // CTAs along K (single-matrix kernel)

@@ -1,4 +1,5 @@
-// Activation quantizers feeding the integer-MMA projections.
+// Activation quantizers feeding the integer-MMA projections.  All of them write
+// int8 codes in the F8 B-fragment layout (frag_offset in common.cuh).
 //   * HE4 learned-gain/clip codes (Projection.forward, w1a1_eagle/model.py:128-140)
 //   * per-token 16-bit fixed point as two int8 planes (pure one-bit-weight blocks)
 //   * W1A1 sign binarisation with the fixed-order per-token mean|x|
@@ -21,47 +22,66 @@ __device__ __forceinline__ T block_sum_256(T v, T *scratch) {
     return total;
 }
 
-// One 256-thread CTA per row; thread handles 4 consecutive columns per step.
+// Grid (rows, ceil(cols / 1024)): each thread quantizes 4 consecutive columns
+// with all loads in flight at once.  Code sums go either to partial[row][y]
+// (partial = true, no zeroing needed) or, with integer atomics, to a zeroed
+// full[row].
 __global__ void __launch_bounds__(256) quantize_codes_kernel(const float *__restrict__ x, int64_t cols, int64_t ld,
                                                              const float *__restrict__ gain,
                                                              const float *__restrict__ bound_ptr, int bits,
                                                              int8_t *__restrict__ codes, int32_t *__restrict__ sums,
-                                                             int32_t *flags, int32_t *zero_sums, int zero_count) {
+                                                             bool partial, int32_t *flags, int32_t *zero_sums,
+                                                             int zero_count) {
     __shared__ int scratch[8];
-    const int64_t row = blockIdx.x;
-    if (row == 0 && zero_sums)
+    grid_wait();
+    grid_launch_dependents();
+    const int row = blockIdx.x;
+    if (row == 0 && blockIdx.y == 0 && zero_sums)
         for (int i = threadIdx.x; i < zero_count; i += blockDim.x) zero_sums[i] = 0;
     const float b = *bound_ptr;
-    if (bad_bound(b)) {
-        if (threadIdx.x == 0) set_flag(flags, BD_FLAG_BAD_BOUND);
-    }
+    if (bad_bound(b) && threadIdx.x == 0 && blockIdx.y == 0) set_flag(flags, BD_FLAG_BAD_BOUND);
     Quant q;
     q.init(b, bits);
+    const int64_t k0 = static_cast<int64_t>(blockIdx.y) * 1024 + 4 * threadIdx.x;
     int sum = 0;
     bool bad = false;
-    for (int64_t k0 = 4 * threadIdx.x; k0 < ld; k0 += 4 * blockDim.x) {
+    if (k0 < cols) {
+        float xv[4], gv[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const bool live = k0 + j < cols;
+            xv[j] = live ? x[row * cols + k0 + j] : 0.0f;
+            gv[j] = live ? gain[k0 + j] : 0.0f;
+        }
         int c[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            const int64_t k = k0 + j;
             c[j] = 0;
-            if (k < cols) {
-                const float g = __fmul_rn(x[row * cols + k], gain[k]);
+            if (k0 + j < cols) {
+                const float g = __fmul_rn(xv[j], gv[j]);
                 bad |= !isfinite(g);
                 c[j] = q.code(g);
             }
             sum += c[j];
         }
-        char4 v = make_char4(static_cast<signed char>(c[0]), static_cast<signed char>(c[1]),
-                             static_cast<signed char>(c[2]), static_cast<signed char>(c[3]));
-        *reinterpret_cast<char4 *>(codes + row * ld + k0) = v;
+        *reinterpret_cast<char4 *>(codes + frag_offset(row, k0, ld / 64)) =
+            make_char4(static_cast<signed char>(c[0]), static_cast<signed char>(c[1]),
+                       static_cast<signed char>(c[2]), static_cast<signed char>(c[3]));
     }
     if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) set_flag(flags, BD_FLAG_NONFINITE_INPUT);
-    const int total = block_sum_256(sum, scratch);
-    if (threadIdx.x == 0) sums[row] = total;
+    if (sums) {
+        const int total = block_sum_256(sum, scratch);
+        if (threadIdx.x == 0) {
+            if (partial)
+                sums[row * gridDim.y + blockIdx.y] = total;
+            else if (total)
+                atomicAdd(sums + row, total);
+        }
+    }
 }
 
 // Per-token 16-bit fixed point: q = rint(x * 32639 / max|x|), q = 256 hi + lo.
+// One CTA per row: the row maximum needs the whole row.
 __global__ void __launch_bounds__(256) quantize_planes_kernel(const float *__restrict__ x, int64_t cols, int64_t ld,
                                                               int8_t *__restrict__ hi, int8_t *__restrict__ lo,
                                                               int32_t *__restrict__ sums_hi,
@@ -69,13 +89,21 @@ __global__ void __launch_bounds__(256) quantize_planes_kernel(const float *__res
                                                               float *__restrict__ row_scale, int32_t *flags) {
     __shared__ float fscratch[8];
     __shared__ int iscratch[8];
-    const int64_t row = blockIdx.x;
+    grid_wait();
+    grid_launch_dependents();
+    const int row = blockIdx.x;
+    const int64_t nsp = ld / 64;
     float m = 0.0f;
     bool bad = false;
-    for (int64_t k = threadIdx.x; k < cols; k += blockDim.x) {
-        const float v = x[row * cols + k];
-        bad |= !isfinite(v);
-        m = fmaxf(m, fabsf(v));
+    for (int64_t k0 = 4 * threadIdx.x; k0 < cols; k0 += 4 * blockDim.x) {
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = k0 + j < cols ? x[row * cols + k0 + j] : 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            bad |= !isfinite(v[j]);
+            m = fmaxf(m, fabsf(v[j]));
+        }
     }
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, d));
@@ -87,21 +115,25 @@ __global__ void __launch_bounds__(256) quantize_planes_kernel(const float *__res
     if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) set_flag(flags, BD_FLAG_NONFINITE_INPUT);
     const float inv = m > 0.0f ? __fdiv_rn(32639.0f, m) : 0.0f;
     int shi = 0, slo = 0;
-    for (int64_t k = threadIdx.x; k < ld; k += blockDim.x) {
-        int h = 0, l = 0;
-        if (k < cols) {
-            float r = rintf(__fmul_rn(x[row * cols + k], inv));
-            r = fminf(fmaxf(r, -32639.0f), 32639.0f);
-            const int qv = static_cast<int>(r);
-            h = (qv + 128) >> 8;
-            l = qv - 256 * h;
+    for (int64_t k0 = 4 * threadIdx.x; k0 < cols; k0 += 4 * blockDim.x) {
+        int h[4], l[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            h[j] = l[j] = 0;
+            if (k0 + j < cols) {
+                float r = rintf(__fmul_rn(x[row * cols + k0 + j], inv));
+                r = fminf(fmaxf(r, -32639.0f), 32639.0f);
+                const int qv = static_cast<int>(r);
+                h[j] = (qv + 128) >> 8;
+                l[j] = qv - 256 * h[j];
+            }
+            shi += h[j];
+            slo += l[j];
         }
-        hi[row * ld + k] = static_cast<int8_t>(h);
-        lo[row * ld + k] = static_cast<int8_t>(l);
-        shi += h;
-        slo += l;
+        const int64_t off = frag_offset(row, k0, nsp);
+        *reinterpret_cast<char4 *>(hi + off) = make_char4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<char4 *>(lo + off) = make_char4(l[0], l[1], l[2], l[3]);
     }
-    __syncthreads();
     shi = block_sum_256(shi, iscratch);
     slo = block_sum_256(slo, iscratch);
     if (threadIdx.x == 0) {
@@ -119,7 +151,10 @@ __global__ void __launch_bounds__(256) binarize_kernel(const float *__restrict__
                                                        int64_t words_ld, int32_t *flags) {
     __shared__ float fscratch[8];
     __shared__ int iscratch[8];
-    const int64_t row = blockIdx.x;
+    grid_wait();
+    grid_launch_dependents();
+    const int row = blockIdx.x;
+    const int64_t nsp = ld / 64;
     float acc = 0.0f;
     int s = 0;
     bool bad = false;
@@ -131,7 +166,7 @@ __global__ void __launch_bounds__(256) binarize_kernel(const float *__restrict__
             acc = __fadd_rn(acc, fabsf(v));
             c = v >= 0.0f ? 1 : -1;
         }
-        codes[row * ld + k] = static_cast<int8_t>(c);
+        if (codes) codes[frag_offset(row, k, nsp)] = static_cast<int8_t>(c);
         s += c;
         if (words) {
             const unsigned word = __ballot_sync(0xffffffffu, c > 0);
@@ -149,47 +184,50 @@ __global__ void __launch_bounds__(256) binarize_kernel(const float *__restrict__
     }
     if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) set_flag(flags, BD_FLAG_NONFINITE_INPUT);
     s = block_sum_256(s, iscratch);
-    if (threadIdx.x == 0) sums[row] = s;
+    if (threadIdx.x == 0 && sums) sums[row] = s;
 }
 
 int launch_quantize_codes(const float *x, int64_t rows, int64_t cols, int64_t ld, const float *gain,
-                          const float *bound, int bits, int8_t *codes, int32_t *sums, int32_t *flags,
+                          const float *bound, int bits, int8_t *codes, int32_t *sums, bool partial, int32_t *flags,
                           int32_t *zero_sums, int zero_count, cudaStream_t stream) {
     if (rows == 0) return BD_OK;
-    quantize_codes_kernel<<<static_cast<unsigned>(rows), 256, 0, stream>>>(x, cols, ld, gain, bound, bits, codes,
-                                                                           sums, flags, zero_sums, zero_count);
-    BD_CHECK_LAUNCH();
-    return BD_OK;
+    if (sums && !partial && cudaMemsetAsync(sums, 0, rows * sizeof(int32_t), stream) != cudaSuccess)
+        return BD_ERR_LAUNCH;
+    const dim3 grid(static_cast<unsigned>(rows), static_cast<unsigned>(quant_parts(cols)));
+    return launch_pdl(quantize_codes_kernel, grid, dim3(256), 0, stream, x, cols, ld, gain, bound, bits, codes, sums,
+                      partial, flags, zero_sums, zero_count);
 }
 
 int launch_quantize_planes(const float *x, int64_t rows, int64_t cols, int64_t ld, int8_t *hi, int8_t *lo,
                            int32_t *sums_hi, int32_t *sums_lo, float *row_scale, int32_t *flags,
                            cudaStream_t stream) {
     if (rows == 0) return BD_OK;
-    quantize_planes_kernel<<<static_cast<unsigned>(rows), 256, 0, stream>>>(x, cols, ld, hi, lo, sums_hi, sums_lo,
-                                                                            row_scale, flags);
-    BD_CHECK_LAUNCH();
-    return BD_OK;
+    return launch_pdl(quantize_planes_kernel, dim3(static_cast<unsigned>(rows)), dim3(256), 0, stream, x, cols, ld,
+                      hi, lo, sums_hi, sums_lo, row_scale, flags);
 }
 
 int launch_binarize(const float *x, int64_t rows, int64_t cols, int64_t ld, int8_t *codes, int32_t *sums,
                     float *mean_abs, uint32_t *words, int64_t words_ld, int32_t *flags, cudaStream_t stream) {
     if (rows == 0) return BD_OK;
-    binarize_kernel<<<static_cast<unsigned>(rows), 256, 0, stream>>>(x, cols, ld, codes, sums, mean_abs, words,
-                                                                     words_ld, flags);
-    BD_CHECK_LAUNCH();
-    return BD_OK;
+    return launch_pdl(binarize_kernel, dim3(static_cast<unsigned>(rows)), dim3(256), 0, stream, x, cols, ld, codes,
+                      sums, mean_abs, words, words_ld, flags);
 }
 
 }  // namespace bd
 
 extern "C" int64_t bd_codes_ld(int64_t cols) { return cols <= 0 ? 0 : (cols + 255) / 256 * 256; }
 
+extern "C" int64_t bd_codes_bytes(int64_t rows, int64_t cols) {
+    if (rows < 0 || cols < 0) return -1;
+    return (rows + 7) / 8 * 8 * bd_codes_ld(cols);
+}
+
 extern "C" int bd_quantize_codes(const float *x, int64_t rows, int64_t cols, int64_t ld, const float *gain,
                                  const float *bound, int bits, int8_t *codes, int32_t *code_sums, int32_t *flags,
                                  bd_stream_t stream) {
-    if (rows < 0 || cols < 0 || ld < cols || (ld & 3) || (bits != 4 && bits != 8)) return BD_ERR_INVALID;
+    if (rows < 0 || rows > 0x7fffffff || cols < 0 || ld < cols || (ld & 255) || (bits != 4 && bits != 8))
+        return BD_ERR_INVALID;
     if (rows > 0 && (!x || !gain || !bound || !codes || !code_sums)) return BD_ERR_INVALID;
-    return bd::launch_quantize_codes(x, rows, cols, ld, gain, bound, bits, codes, code_sums, flags, nullptr, 0,
-                                     stream);
+    return bd::launch_quantize_codes(x, rows, cols, ld, gain, bound, bits, codes, code_sums, false, flags, nullptr,
+                                     0, stream);
 }

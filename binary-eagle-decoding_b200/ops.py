@@ -138,11 +138,11 @@ def codes_ld(cols: int) -> int:
 
 
 def quantize_codes(x: Tensor, gain: Tensor, bound: Tensor, bits: int, flags: Flags | None = None):
-    """HE4 activation codes ``int8 [tokens, ld]`` and exact row sums (model.py:128-140)."""
+    """HE4 activation codes (int8, F8 fragment layout) and exact row sums (model.py:128-140)."""
     device = _require_cuda(x, gain, bound)
     rows, cols = x.shape
     ld = codes_ld(cols)
-    codes = torch.empty((rows, ld), dtype=torch.int8, device=device)
+    codes = torch.zeros(int(_lib.load().bd_codes_bytes(rows, cols)), dtype=torch.int8, device=device)
     sums = torch.empty(rows, dtype=torch.int32, device=device)
     own = flags is None
     flags = flags or Flags(device)
@@ -158,7 +158,7 @@ def projection_he4(codes: Tensor, sums: Tensor, signs_t16: Tensor, in_features: 
                    raw_dot: bool = False):
     """HE4 projection forward value from codes (model.py:141-150); optional exact dots."""
     device = _require_cuda(codes, sums, signs_t16, scale, midpoint, bound, residual)
-    tokens = codes.shape[0]
+    tokens = sums.shape[0]
     out_features = scale.shape[0]
     y = torch.empty((tokens, out_features), dtype=torch.float32, device=device)
     raw = torch.empty((tokens, out_features), dtype=torch.int32, device=device) if raw_dot else None

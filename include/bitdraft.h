@@ -71,10 +71,16 @@ int bd_tile_gguf_t16(const int32_t *words, int64_t rows, int64_t cols, uint32_t 
 
 /* =================================================================== quantizer
  * bd_quantize_codes replaces the activation quantizer of Projection.forward
- * (w1a1_eagle/model.py:128-140): codes[t * ld + k] = clamp(rint(clip(x*gain,
- * +-bound) * (1/bound * max)), +-max) as int8, max = 2^(bits-1) - 1; columns
- * cols..ld-1 are written 0; code_sums[t] = exact sum of the row's codes.
- * gain [cols] and bound [1] are the exponentiated parameters (device). */
+ * (w1a1_eagle/model.py:128-140): code(t, k) = clamp(rint(clip(x*gain, +-bound)
+ * * (1/bound * max)), +-max) as int8, max = 2^(bits-1) - 1, stored in the F8
+ * B-fragment layout: blocks of 8 rows by 64 columns, 512 bytes each, row-block
+ * major; inside a block the 16 bytes of lane l = 4 (t % 8) + q hold, for the
+ * two 32-column k-steps s of the block, the codes of columns 32 s + 16 h + 4 q
+ * + j at byte 8 (s & 1) + 4 h + j.  ld = bd_codes_ld(cols) (a multiple of 256),
+ * buffer size bd_codes_bytes(rows, cols); columns >= cols are not written.
+ * code_sums[t] = exact sum of row t's codes.  gain [cols] and bound [1] are the
+ * exponentiated parameters (device). */
+int64_t bd_codes_bytes(int64_t rows, int64_t cols);
 int bd_quantize_codes(const float *x, int64_t rows, int64_t cols, int64_t ld, const float *gain,
                       const float *bound, int bits, int8_t *codes, int32_t *code_sums,
                       int32_t *flags, bd_stream_t stream);

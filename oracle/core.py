@@ -126,6 +126,49 @@ def untile_signs_t16(words: np.ndarray, rows: int, cols: int) -> np.ndarray:
     return full[:rows, :cols]
 
 
+# --------------------------------------------------------------------------- F8 code layout
+#
+# Activation codes feed the integer MMAs as B fragments.  The F8 layout stores
+# them so that each lane of a warp fetches the fragments of two 32-column
+# k-steps with one 16-byte load: blocks of 8 rows by 64 columns (512 bytes),
+# row-block major; inside a block, lane ``4 g + q`` (row ``8 nt + g``) holds, for
+# k-step ``s`` of the block, the codes of columns ``32 s + 16 h + 4 q + j`` at
+# byte ``8 (s & 1) + 4 h + j``.  The row stride ``ld`` is the column count
+# rounded up to 256.
+
+
+def codes_ld(cols: int) -> int:
+    return (cols + 255) // 256 * 256
+
+
+def f8_offsets(rows: int, cols: int) -> np.ndarray:
+    """Byte offset of every (row, column) code in the F8 layout, ``[rows, cols]``."""
+    ld = codes_ld(cols)
+    nsp = ld // 64
+    t = np.arange(rows)[:, None]
+    k = np.arange(cols)[None, :]
+    nt, g = t >> 3, t & 7
+    s, kk = k >> 5, k & 31
+    half, q, j = kk >> 4, (kk & 15) >> 2, kk & 3
+    return (((nt * nsp + (s >> 1)) * 32 + g * 4 + q) << 4) + ((s & 1) << 3) + (half << 2) + j
+
+
+def f8_bytes(rows: int, cols: int) -> int:
+    return (rows + 7) // 8 * 8 * codes_ld(cols)
+
+
+def tile_codes_f8(codes: np.ndarray) -> np.ndarray:
+    """int8 F8 buffer of integer codes ``[rows, cols]`` (padding left zero)."""
+    rows, cols = codes.shape
+    out = np.zeros(f8_bytes(rows, cols), dtype=np.int8)
+    out[f8_offsets(rows, cols)] = codes.astype(np.int8)
+    return out
+
+
+def untile_codes_f8(buffer: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    return np.asarray(buffer, dtype=np.int8)[f8_offsets(rows, cols)]
+
+
 # --------------------------------------------------------------------------- quantizer
 
 

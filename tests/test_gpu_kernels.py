@@ -82,8 +82,8 @@ def test_quantize_codes_bit_exact(ops, bits):
     codes, sums = ops.quantize_codes(dev(x), dev(gain), dev(np.array([bound])), bits)
     want, _ = core.quantize_codes(x, gain, bound, bits)
     got = codes.cpu().numpy()
-    assert np.array_equal(got[:, :777], want.astype(np.int8))
-    assert not got[:, 777:].any()
+    assert np.array_equal(got, core.tile_codes_f8(want))  # padding stays zero
+    assert np.array_equal(core.untile_codes_f8(got, 13, 777), want.astype(np.int8))
     assert np.array_equal(sums.cpu().numpy(), want.sum(-1).astype(np.int32))
     with pytest.raises(ValueError, match="invalid learned clipping bound"):
         ops.quantize_codes(dev(x), dev(gain), dev(np.array([np.float32(-1.0)])), bits)

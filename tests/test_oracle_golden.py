@@ -329,3 +329,12 @@ def test_bound_latents_against_reference():
     kat = optim.bound_latents(np.array([[0.0, -0.0, 2.0, -14.0], [0.0] * 4], np.float32), 2.0)
     assert np.array_equal(kat, f["kat"])
     assert kat.tolist() == [[0.0, -0.0, 0.25, -1.0], [0.0] * 4]
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 1), (8, 256), (13, 777), (32, 2560)])
+def test_f8_layout_is_a_permutation(rows, cols):
+    off = core.f8_offsets(rows, cols)
+    assert off.min() >= 0 and off.max() < core.f8_bytes(rows, cols)
+    assert np.unique(off).size == rows * cols
+    codes = np.random.default_rng(rows).integers(-127, 128, size=(rows, cols))
+    assert np.array_equal(core.untile_codes_f8(core.tile_codes_f8(codes), rows, cols), codes.astype(np.int8))
