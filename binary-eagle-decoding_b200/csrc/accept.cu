@@ -38,13 +38,35 @@ struct GreedyArgs {
     int32_t *counters;         // [requests], zero on entry, left zero
 };
 
+// Running maximum of one thread: indices arrive in increasing order, so a
+// strict '>' keeps the lowest index of the maximum.  Non-finite values are
+// found separately (packed NaN-propagating min/max) and never win.
+struct RunMax {
+    float v = -INFINITY;
+    uint32_t i = 0xffffffffu;
+    __device__ __forceinline__ void push(float f, uint32_t idx) {
+        const bool up = f > v && f != INFINITY;
+        v = up ? f : v;
+        i = up ? idx : i;
+    }
+};
+
+__device__ __forceinline__ void push_word(RunMax &m, __nv_bfloat162 &lo, __nv_bfloat162 &hi, uint32_t w,
+                                          uint32_t idx) {
+    m.push(__uint_as_float(w << 16), idx);
+    m.push(__uint_as_float(w & 0xffff0000u), idx + 1);
+    const __nv_bfloat162 pair = *reinterpret_cast<const __nv_bfloat162 *>(&w);
+    hi = __hmax2_nan(hi, pair);
+    lo = __hmin2_nan(lo, pair);
+}
+
 __global__ void __launch_bounds__(kArgmaxThreads) argmax_greedy_kernel(const GreedyArgs a) {
     __shared__ unsigned long long part[kArgmaxThreads / 32];
     __shared__ int last;
     const int64_t row = blockIdx.x;
     const uint16_t *src = a.logits + row * a.vocab;
-    unsigned long long best = 0;
-    bool bad = false;
+    RunMax m;
+    __nv_bfloat162 hi = __float2bfloat162_rn(-1.0f), lo = __float2bfloat162_rn(1.0f);
     const bool vec = (a.vocab % 8) == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0;
     if (vec) {
         const int64_t nvec = a.vocab / 8;
@@ -56,36 +78,33 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_greedy_kernel(const Gre
             for (int u = 0; u < 4; ++u) v[u] = ld_stream_u4(p + i + u * kArgmaxThreads);
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
-                const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
                 const uint32_t base = static_cast<uint32_t>((i + u * kArgmaxThreads) * 8);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const float f = __uint_as_float((e & 1) ? (w[e >> 1] & 0xffff0000u) : (w[e >> 1] << 16));
-                    bad |= !isfinite(f);
-                    const unsigned long long k = argmax_key(f, base + e);
-                    best = (isfinite(f) && k > best) ? k : best;
-                }
+                push_word(m, lo, hi, v[u].x, base);
+                push_word(m, lo, hi, v[u].y, base + 2);
+                push_word(m, lo, hi, v[u].z, base + 4);
+                push_word(m, lo, hi, v[u].w, base + 6);
             }
         }
         for (; i < nvec; i += kArgmaxThreads) {
             const uint4 v = ld_stream_u4(p + i);
-            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const float f = __uint_as_float((e & 1) ? (w[e >> 1] & 0xffff0000u) : (w[e >> 1] << 16));
-                bad |= !isfinite(f);
-                const unsigned long long k = argmax_key(f, static_cast<uint32_t>(i * 8 + e));
-                best = (isfinite(f) && k > best) ? k : best;
-            }
+            const uint32_t base = static_cast<uint32_t>(i * 8);
+            push_word(m, lo, hi, v.x, base);
+            push_word(m, lo, hi, v.y, base + 2);
+            push_word(m, lo, hi, v.z, base + 4);
+            push_word(m, lo, hi, v.w, base + 6);
         }
     } else {
         for (int64_t i = threadIdx.x; i < a.vocab; i += kArgmaxThreads) {
-            const float f = bf16_bits_to_f32(src[i]);
-            bad |= !isfinite(f);
-            const unsigned long long k = argmax_key(f, static_cast<uint32_t>(i));
-            best = (isfinite(f) && k > best) ? k : best;
+            const uint32_t w = src[i];
+            m.push(__uint_as_float(w << 16), static_cast<uint32_t>(i));
+            const __nv_bfloat162 pair = *reinterpret_cast<const __nv_bfloat162 *>(&w);
+            hi = __hmax2_nan(hi, pair);
+            lo = __hmin2_nan(lo, pair);
         }
     }
+    const float2 hf = __bfloat1622float2(hi), lf = __bfloat1622float2(lo);
+    const bool bad = !isfinite(hf.x) || !isfinite(hf.y) || !isfinite(lf.x) || !isfinite(lf.y);
+    unsigned long long best = m.i == 0xffffffffu ? 0ull : argmax_key(m.v, m.i);
     best = warp_max_u64(best);
     if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = best;
     if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) set_flag(a.flags, BD_FLAG_NONFINITE_LOGITS);

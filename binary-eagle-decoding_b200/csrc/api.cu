@@ -4,7 +4,6 @@
 #include "kernels.cuh"
 
 namespace bd {
-int choose_kgroups(int64_t rows, int64_t ncp, int sms);
 
 constexpr int kMaxTokens = 32;
 
@@ -118,7 +117,7 @@ extern "C" int bd_projection_he4(const int8_t *codes, const int32_t *code_sums, 
     a.nparts = 1;
     a.ld = a.ncp * 256;
     a.tokens = tokens;
-    a.kgroups = choose_kgroups(out_features, a.ncp, sm_count_cached());
+    plan_proj(a, 1);
     a.scale0 = scale;
     a.mid0 = midpoint;
     a.bound = bound;
@@ -126,11 +125,11 @@ extern "C" int bd_projection_he4(const int8_t *codes, const int32_t *code_sums, 
     a.residual = residual;
     a.out = y;
     a.raw_dot = raw_dot;
-    if (a.kgroups > 1) {
+    if (workspace) {  // split-K accumulators; without them the launcher does not split K
         Carver c{static_cast<char *>(workspace)};
         a.acc = c.take<int32_t>(2 * ((out_features + 15) / 16 * 16) * kMaxTokens);
         a.counters = c.take<int32_t>((out_features + 15) / 16);
-        if (!workspace || c.off > workspace_bytes) return BD_ERR_WORKSPACE;
+        if (c.off > workspace_bytes) return BD_ERR_WORKSPACE;
     }
     return launch_proj(a, EPI_HE4, stream);
 }
@@ -199,7 +198,7 @@ extern "C" int bd_ffn_he4(const bd_ffn_he4_args *p, bd_stream_t stream) {
     dn.nparts = 1;
     dn.ld = ld_f;
     dn.tokens = p->tokens;
-    dn.kgroups = choose_kgroups(p->hidden, dn.ncp, sm_count_cached());
+    plan_proj(dn, 1);
     dn.scale0 = p->scale_down;
     dn.mid0 = p->midpoint_down;
     dn.bound = p->bound_down;
@@ -262,7 +261,7 @@ extern "C" int bd_ffn_w1(const bd_ffn_w1_args *p, bd_stream_t stream) {
     dn.nparts = 1;
     dn.ld = ld_f;
     dn.tokens = p->tokens;
-    dn.kgroups = choose_kgroups(p->hidden, dn.ncp, sm_count_cached());
+    plan_proj(dn, 2);
     dn.scale0 = p->scale_down;
     dn.row_scale = w.scale_mid;
     dn.out = p->y;

@@ -1,31 +1,36 @@
 // Decode-size (tokens <= 32) packed-sign projections on the integer tensor pipe.
 //
-// Weights arrive as T16 sign words (see pack.cu); each lane expands its 16-byte
-// slice of a 512-byte unit directly into the 0/1 int8 A fragments of
-// m16n8k32 MMAs (two instructions per register, no shared memory for weights).
-// Activation codes are kept in the B-fragment layout (see frag_offset): each
-// lane fetches the B fragments of two k-steps with one 16-byte L1-cached load,
-// shared by the gate and up matrices.  With b in {0,1} (b = 1 for latent >= 0)
-// the +-1 dot is D = 2 * D01 - sum(codes), exact in int32, so every epilogue
-// starts from the exact integer dot.  Kernels use programmatic dependent
-// launch: the weight bits (read-only) are requested before grid_wait(), so
-// their HBM latency overlaps the previous kernel.
+// A CTA owns a rectangle of 512-byte sign units (row blocks x column pairs).
+// Before waiting on the previous kernel (programmatic dependent launch) it
+// streams its sign tiles -- read-only weights -- into shared memory with
+// cp.async, together with the epilogue operands; after the wait it stages the
+// activation codes (F8 B-fragment layout, frag_offset) for its column range.
+// Warps then walk (row block, column pair) items: each lane expands its 16
+// bytes of a unit into the 0/1 int8 A fragments of m16n8k32 MMAs (two
+// instructions per register) and reads its B fragments with 16-byte shared
+// loads.  With b in {0,1} (b = 1 for latent >= 0) the +-1 dot is
+// D = 2 * D01 - sum(codes), exact in int32; partial sums meet in shared int32
+// accumulators (order-free, exact), and the epilogue runs on all threads.
+// Grids are sized on the host to a single wave of CTAs.
+//
+// Early-start invariant: before grid_wait() a kernel reads only weights and
+// parameters; kernels call grid_launch_dependents() only after their own
+// grid_wait(), so the kernel that started early can rely on every kernel
+// before its predecessor having completed.  A kernel that writes sign tiles
+// (the optimizer's re-pack) never triggers early starts.
 #include "kernels.cuh"
 
 namespace bd {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kSplit = 4;                 // warps sharing one row block (pair) along K
-constexpr int kBlocksPerCta = kWarps / kSplit;
-constexpr int kBatch = 4;                 // column pairs of weight bits in flight per warp
+constexpr size_t kSmemLimit = 220 * 1024;
 
-// Load the B fragments (NT n-tiles) of k-step pair sp for this lane.
-template <int NT>
-__device__ __forceinline__ void load_b(uint4 (&b)[NT], const int8_t *codes, int64_t nsp, int64_t sp, int lane) {
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-        b[nt] = __ldg(reinterpret_cast<const uint4 *>(codes + (((nt * nsp + sp) * 32 + lane) << 4)));
+// Stage `bytes` (multiple of 16) from global to shared with 16-byte cp.async.
+__device__ __forceinline__ void stage(void *dst, const void *src, int64_t bytes) {
+    char *d = static_cast<char *>(dst);
+    const char *s = static_cast<const char *>(src);
+    for (int64_t i = threadIdx.x * 16; i < bytes; i += kThreads * 16) cp_async16(d + i, s + i, 16);
 }
 
 // A fragments (0/1 bytes) of k-step q of chunk words (wa: row g, wb: row g + 8).
@@ -39,18 +44,58 @@ struct AFrag {
     }
 };
 
-// One 256-column unit of up to two matrices (M matrices) against PLANES code planes.
+// Shape of one CTA's work, shared by both kernels.
+struct Tile {
+    int blocks;     // row blocks (pairs for gate/up) owned by this CTA
+    int64_t block0; // first row block (pair)
+    int cp0, ncpc;  // column-pair range [cp0, cp0 + ncpc)
+};
+
+// Shared-memory plan (byte offsets) of a CTA.
+struct Plan {
+    int M;          // matrices per block (2 for gate/up)
+    int TP;         // padded tokens (8 NT)
+    int planes;
+    int64_t bits, codes, acc, params, sums, total;
+    __host__ __device__ Plan(int m, int tp, int p, int blocks, int ncpc) : M(m), TP(tp), planes(p) {
+        int64_t off = 0;
+        bits = off;
+        off += static_cast<int64_t>(blocks) * m * ncpc * 512;
+        codes = off;
+        off += static_cast<int64_t>(planes) * (tp / 8) * ncpc * 4 * 512;
+        acc = off;
+        off += static_cast<int64_t>(blocks) * m * 16 * tp * planes * 4;
+        params = off;
+        off += static_cast<int64_t>(blocks) * 16 * 5 * 4;
+        sums = off;
+        off += 2 * 32 * 4;
+        total = off;
+    }
+};
+
+// Per-item MMA: M matrices of row block `blk` at column pair `cp` (relative to
+// the staged slice) against PLANES staged code planes.
 template <int NT, int PLANES, int M>
-__device__ __forceinline__ void unit_mma(int (&acc)[M][PLANES][NT][4], const uint4 (&w)[M], const int8_t *codes0,
-                                         const int8_t *codes1, int64_t nsp, int64_t cp, int lane) {
+__device__ __forceinline__ void item_mma(int (&acc)[M][PLANES][NT][4], const char *sm, const Plan &pl, int blk,
+                                         int cpr, int ncpc, int lane) {
+    uint4 w[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+        w[m] = *reinterpret_cast<const uint4 *>(sm + pl.bits + ((blk * M + m) * ncpc + cpr) * 512 + lane * 16);
+    const char *codes = sm + pl.codes;
+    const int64_t plane_bytes = static_cast<int64_t>(NT) * ncpc * 4 * 512;
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
 #pragma unroll
         for (int qp = 0; qp < 2; ++qp) {
-            const int64_t sp = cp * 4 + c * 2 + qp;
-            uint4 b0[NT], b1[NT];
-            load_b<NT>(b0, codes0, nsp, sp, lane);
-            if (PLANES == 2) load_b<NT>(b1, codes1, nsp, sp, lane);
+            const int sp = cpr * 4 + c * 2 + qp;
+            uint4 b[PLANES][NT];
+#pragma unroll
+            for (int p = 0; p < PLANES; ++p)
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+                    b[p][nt] = *reinterpret_cast<const uint4 *>(codes + p * plane_bytes +
+                                                                ((nt * ncpc * 4 + sp) * 32 + lane) * 16);
 #pragma unroll
             for (int qq = 0; qq < 2; ++qq) {
                 const int q = 2 * qp + qq;
@@ -58,28 +103,44 @@ __device__ __forceinline__ void unit_mma(int (&acc)[M][PLANES][NT][4], const uin
                 for (int m = 0; m < M; ++m) {
                     const AFrag a(c ? w[m].z : w[m].x, c ? w[m].w : w[m].y, q);
 #pragma unroll
-                    for (int nt = 0; nt < NT; ++nt) {
-                        mma_s8_16832(acc[m][0][nt], a.r[0], a.r[1], a.r[2], a.r[3], qq ? b0[nt].z : b0[nt].x,
-                                     qq ? b0[nt].w : b0[nt].y);
-                        if (PLANES == 2)
-                            mma_s8_16832(acc[m][PLANES - 1][nt], a.r[0], a.r[1], a.r[2], a.r[3],
-                                         qq ? b1[nt].z : b1[nt].x, qq ? b1[nt].w : b1[nt].y);
-                    }
+                    for (int p = 0; p < PLANES; ++p)
+#pragma unroll
+                        for (int nt = 0; nt < NT; ++nt)
+                            mma_s8_16832(acc[m][p][nt], a.r[0], a.r[1], a.r[2], a.r[3], qq ? b[p][nt].z : b[p][nt].x,
+                                         qq ? b[p][nt].w : b[p][nt].y);
                 }
             }
         }
     }
 }
 
-// Exact +-1 dot from the 0/1 partial sums of all planes.
-template <int PLANES>
-__device__ __forceinline__ int pm_dot(const int (&d01)[PLANES], int cs0, int cs1) {
-    if (PLANES == 2) return 256 * (2 * d01[0] - cs0) + (2 * d01[PLANES - 1] - cs1);
-    return 2 * d01[0] - cs0;
+// Add a warp's register accumulators of block `blk` into the shared totals.
+template <int NT, int PLANES, int M>
+__device__ __forceinline__ void flush(int (&acc)[M][PLANES][NT][4], int *sacc, int blk, int lane) {
+    const int g = lane >> 2, t = lane & 3;
+    constexpr int TP = NT * 8;
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+#pragma unroll
+        for (int p = 0; p < PLANES; ++p)
+#pragma unroll
+            for (int n = 0; n < NT; ++n)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int row = g + 8 * (i >> 1), token = n * 8 + 2 * t + (i & 1);
+                    const int v = acc[m][p][n][i];
+                    if (v) atomicAdd(sacc + (((blk * M + m) * PLANES + p) * 16 + row) * TP + token, v);
+                    acc[m][p][n][i] = 0;
+                }
 }
 
-template <int M, int PLANES, int NT>
-__device__ __forceinline__ void zero_acc(int (&acc)[M][PLANES][NT][4]) {
+// Walk this CTA's (block, column pair) items: warp w takes a contiguous share.
+template <int NT, int PLANES, int M>
+__device__ __forceinline__ void walk_items(const char *sm, int *sacc, const Plan &pl, const Tile &tile) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int items = tile.blocks * tile.ncpc;
+    const int i0 = warp * items / kWarps, i1 = (warp + 1) * items / kWarps;
+    int acc[M][PLANES][NT][4];
 #pragma unroll
     for (int m = 0; m < M; ++m)
 #pragma unroll
@@ -88,44 +149,46 @@ __device__ __forceinline__ void zero_acc(int (&acc)[M][PLANES][NT][4]) {
             for (int n = 0; n < NT; ++n)
 #pragma unroll
                 for (int i = 0; i < 4; ++i) acc[m][p][n][i] = 0;
+    int blk = i0 < i1 ? i0 / tile.ncpc : 0;
+    for (int it = i0; it < i1; ++it) {
+        const int b = it / tile.ncpc, cpr = it - b * tile.ncpc;
+        if (b != blk) {
+            flush<NT, PLANES, M>(acc, sacc, blk, lane);
+            blk = b;
+        }
+        item_mma<NT, PLANES, M>(acc, sm, pl, b, cpr, tile.ncpc, lane);
+    }
+    if (i0 < i1) flush<NT, PLANES, M>(acc, sacc, blk, lane);
 }
 
-// Sum the kSplit K-slices of each row block through shared memory; the slice-0
-// warp ends with the totals.  All warps of the CTA must call this.
-template <int M, int PLANES, int NT>
-__device__ __forceinline__ void reduce_split(int (&acc)[M][PLANES][NT][4], int *red, int slot, int ks, int lane) {
-    constexpr int VALS = M * PLANES * NT * 4;
-    int *buf = red + slot * 32 * VALS + lane;
-#pragma unroll
-    for (int r = 1; r < kSplit; ++r) {
-        if (ks == r) {
-            int v = 0;
-#pragma unroll
-            for (int m = 0; m < M; ++m)
-#pragma unroll
-                for (int p = 0; p < PLANES; ++p)
-#pragma unroll
-                    for (int n = 0; n < NT; ++n)
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) buf[(v++) * 32] = acc[m][p][n][i];
+// Stage this CTA's sign tiles: for each owned block and matrix, ncpc contiguous units.
+__device__ __forceinline__ void stage_bits(char *sm, const Plan &pl, const ProjArgs &a, const Tile &tile) {
+    for (int b = 0; b < tile.blocks; ++b)
+        for (int m = 0; m < pl.M; ++m) {
+            const int64_t vrb = (tile.block0 + b) * pl.M + m;
+            stage(sm + pl.bits + static_cast<int64_t>(b * pl.M + m) * tile.ncpc * 512,
+                  a.bits + (vrb * a.ncp + tile.cp0) * 128, static_cast<int64_t>(tile.ncpc) * 512);
         }
-        __syncthreads();
-        if (ks == 0) {
-            int v = 0;
-#pragma unroll
-            for (int m = 0; m < M; ++m)
-#pragma unroll
-                for (int p = 0; p < PLANES; ++p)
-#pragma unroll
-                    for (int n = 0; n < NT; ++n)
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) acc[m][p][n][i] += buf[(v++) * 32];
-        }
-        __syncthreads();
+}
+
+// Stage the codes of columns [cp0, cp0 + ncpc) pairs for every n-tile and plane.
+__device__ __forceinline__ void stage_codes(char *sm, const Plan &pl, const ProjArgs &a, const Tile &tile, int nt_count) {
+    const int64_t nsp = a.ld / 64;
+    for (int p = 0; p < pl.planes; ++p) {
+        const int8_t *src = p ? a.codes1 : a.codes0;
+        for (int nt = 0; nt < nt_count; ++nt)
+            stage(sm + pl.codes + (static_cast<int64_t>(p) * nt_count + nt) * tile.ncpc * 4 * 512,
+                  src + (nt * nsp + static_cast<int64_t>(tile.cp0) * 4) * 512, static_cast<int64_t>(tile.ncpc) * 4 * 512);
     }
 }
 
-// Row sums of the codes: either full sums ([tokens]) or nparts partial sums per token.
+// Exact +-1 dot from the 0/1 partial sums of all planes.
+template <int PLANES>
+__device__ __forceinline__ int pm_dot(int d0, int d1, int cs0, int cs1) {
+    if (PLANES == 2) return 256 * (2 * d0 - cs0) + (2 * d1 - cs1);
+    return 2 * d0 - cs0;
+}
+
 __device__ __forceinline__ int code_sum(const int32_t *sums, int nparts, int token) {
     int s = 0;
     for (int i = 0; i < nparts; ++i) s += sums[token * nparts + i];
@@ -134,246 +197,287 @@ __device__ __forceinline__ int code_sum(const int32_t *sums, int nparts, int tok
 
 // --------------------------------------------------------------------------- gate/up pair kernel
 template <int NT, int PLANES, int EPI>
-__global__ void __launch_bounds__(kThreads) gateup_kernel(const ProjArgs a) {
-    __shared__ int red[kBlocksPerCta * 32 * 2 * PLANES * NT * 4];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int g = lane >> 2, t = lane & 3;
-    const int slot = warp / kSplit, ks = warp % kSplit;
+__global__ void __launch_bounds__(kThreads) gateup_kernel(const ProjArgs a, int pairs_per_cta) {
+    extern __shared__ __align__(16) char sm[];
+    constexpr int TP = NT * 8;
     const int64_t npairs = (a.rows + 15) / 16;
-    const int64_t pair = static_cast<int64_t>(blockIdx.x) * kBlocksPerCta + slot;
-    const int ncp = static_cast<int>(a.ncp);
-    const int cp0 = ks * ncp / kSplit, cp1 = (ks + 1) * ncp / kSplit;
-    const bool active = pair < npairs && cp0 < cp1;
-    const int64_t nsp = a.ld / 64;
+    Tile tile;
+    tile.block0 = static_cast<int64_t>(blockIdx.x) * pairs_per_cta;
+    tile.blocks = static_cast<int>(min(static_cast<int64_t>(pairs_per_cta), npairs - tile.block0));
+    tile.cp0 = 0;
+    tile.ncpc = static_cast<int>(a.ncp);
+    const Plan pl(2, TP, PLANES, pairs_per_cta, tile.ncpc);
+    int *sacc = reinterpret_cast<int *>(sm + pl.acc);
+    float *prm = reinterpret_cast<float *>(sm + pl.params);  // [5][pairs*16]: scale0 mid0 scale1 mid1 next_gain
+    int *ssum = reinterpret_cast<int *>(sm + pl.sums);       // [2][32]: input code sums, next code sums
 
-    const uint32_t *bits0 = a.bits + (2 * pair) * a.ncp * 128 + lane * 4;
-    const uint32_t *bits1 = a.bits + (2 * pair + 1) * a.ncp * 128 + lane * 4;
-    uint4 wg[kBatch], wu[kBatch];
-    if (active) {
-#pragma unroll
-        for (int i = 0; i < kBatch; ++i)
-            if (cp0 + i < cp1) {
-                wg[i] = ld_stream_u4(bits0 + (cp0 + i) * 128);
-                wu[i] = ld_stream_u4(bits1 + (cp0 + i) * 128);
-            }
+    // read-only operands first (weights and parameters)
+    stage_bits(sm, pl, a, tile);
+    const int rows_c = tile.blocks * 16;
+    for (int i = threadIdx.x; i < rows_c; i += kThreads) {
+        const int64_t o = tile.block0 * 16 + i;
+        const bool live = o < a.rows;
+        prm[0 * rows_c + i] = live ? __ldg(a.scale0 + o) : 0.0f;
+        prm[1 * rows_c + i] = (live && a.mid0) ? __ldg(a.mid0 + o) : 0.0f;
+        prm[2 * rows_c + i] = live ? __ldg(a.scale1 + o) : 0.0f;
+        prm[3 * rows_c + i] = (live && a.mid1) ? __ldg(a.mid1 + o) : 0.0f;
+        prm[4 * rows_c + i] = (live && a.next_gain) ? __ldg(a.next_gain + o) : 0.0f;
     }
+    for (int i = threadIdx.x; i < tile.blocks * 2 * 16 * TP * PLANES; i += kThreads) sacc[i] = 0;
     grid_wait();
     grid_launch_dependents();
-
-    int acc[2][PLANES][NT][4];
-    zero_acc(acc);
-    if (active) {
-        for (int base = cp0; base < cp1; base += kBatch) {
-            if (base != cp0) {
-#pragma unroll
-                for (int i = 0; i < kBatch; ++i)
-                    if (base + i < cp1) {
-                        wg[i] = ld_stream_u4(bits0 + (base + i) * 128);
-                        wu[i] = ld_stream_u4(bits1 + (base + i) * 128);
-                    }
-            }
-#pragma unroll
-            for (int i = 0; i < kBatch; ++i)
-                if (base + i < cp1) {
-                    const uint4 w[2] = {wg[i], wu[i]};
-                    unit_mma<NT, PLANES, 2>(acc, w, a.codes0, a.codes1, nsp, base + i, lane);
-                }
-        }
+    stage_codes(sm, pl, a, tile, NT);
+    if (threadIdx.x < 64) ssum[threadIdx.x] = 0;
+    cp_async_wait_all();
+    __syncthreads();
+    if (threadIdx.x < TP) {
+        ssum[threadIdx.x] = threadIdx.x < a.tokens ? code_sum(a.csum0, a.nparts, threadIdx.x) : 0;
+        if (PLANES == 2) ssum[32 + threadIdx.x] = threadIdx.x < a.tokens ? code_sum(a.csum1, a.nparts, threadIdx.x) : 0;
     }
-    reduce_split(acc, red, slot, ks, lane);
-    if (ks != 0 || pair >= npairs) return;
-
+    walk_items<NT, PLANES, 2>(sm, sacc, pl, tile);
+    __syncthreads();
+    int lo_sum = 0, lo_token = -1;  // running per-token sum of the next projection's codes
     Quant qin, qnext;
     if (EPI == EPI_HE4) {
-        qin.init(*a.bound, a.code_bits);
-        qnext.init(*a.next_bound, 8);
+        qin.init(__ldg(a.bound), a.code_bits);
+        qnext.init(__ldg(a.next_bound), 8);
     }
-    const int64_t next_nsp = a.next_ld / 64;
+    // every thread owns (pair, token, row) elements, rows fastest
+    const int elems = tile.blocks * TP * 16;  // (pair, token, row), rows fastest; TP is a constant
     bool bad = false;
-#pragma unroll
-    for (int n = 0; n < NT; ++n) {
-        int next_sum[2] = {0, 0};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int row = g + 8 * (i >> 1);
-            const int token = n * 8 + 2 * t + (i & 1);
-            const int64_t o = pair * 16 + row;
-            if (token >= a.tokens || o >= a.rows) continue;
-            int dg[PLANES], du[PLANES];
-#pragma unroll
-            for (int p = 0; p < PLANES; ++p) {
-                dg[p] = acc[0][p][n][i];
-                du[p] = acc[1][p][n][i];
-            }
-            const int cs0 = code_sum(a.csum0, a.nparts, token);
-            const int cs1 = PLANES == 2 ? code_sum(a.csum1, a.nparts, token) : 0;
-            const int Dg = pm_dot<PLANES>(dg, cs0, cs1);
-            const int Du = pm_dot<PLANES>(du, cs0, cs1);
-            float gv, uv;
-            if (EPI == EPI_HE4) {
-                gv = he4_value(Dg, a.scale0[o], qin.step, cs0, a.mid0[o]);
-                uv = he4_value(Du, a.scale1[o], qin.step, cs0, a.mid1[o]);
-            } else if (EPI == EPI_W1) {
-                const float rs = a.row_scale[token];
-                gv = __fmul_rn(__fmul_rn(static_cast<float>(Dg), rs), a.scale0[o]);
-                uv = __fmul_rn(__fmul_rn(static_cast<float>(Du), rs), a.scale1[o]);
-            } else {
-                const float rs = a.row_scale[token];
-                gv = __fmul_rn(__fmul_rn(static_cast<float>(Dg), a.scale0[o]), rs);
-                uv = __fmul_rn(__fmul_rn(static_cast<float>(Du), a.scale1[o]), rs);
-            }
-            const float h = __fmul_rn(silu(gv), uv);
-            if (a.out) a.out[token * a.rows + o] = h;
-            if (EPI == EPI_HE4) {
-                const float gained = __fmul_rn(h, a.next_gain[o]);
-                bad |= !isfinite(gained);
-                const int code = qnext.code(gained);
-                a.next_codes[frag_offset(token, o, next_nsp)] = static_cast<int8_t>(code);
-                next_sum[i & 1] += code;
-            }
-        }
+    int *nsum = ssum + 32;  // next-code sums (HE4 only, where the second plane is unused)
+    if (EPI == EPI_HE4 && threadIdx.x < 32) nsum[threadIdx.x] = 0;
+    __syncthreads();
+    for (int e = threadIdx.x; e < elems; e += kThreads) {
+        const int row = e & 15;
+        const int rest = e >> 4;
+        const int token = rest % TP;
+        const int b = rest / TP;
+        const int64_t o = (tile.block0 + b) * 16 + row;
+        if (o >= a.rows || token >= a.tokens) continue;
+        const int r = b * 16 + row;
+        const int cs0 = ssum[token];
+        const int cs1 = PLANES == 2 ? ssum[32 + token] : 0;
+        const int *g0 = sacc + (((b * 2 + 0) * PLANES + 0) * 16 + row) * TP + token;
+        const int *u0 = sacc + (((b * 2 + 1) * PLANES + 0) * 16 + row) * TP + token;
+        const int Dg = pm_dot<PLANES>(g0[0], PLANES == 2 ? g0[16 * TP] : 0, cs0, cs1);
+        const int Du = pm_dot<PLANES>(u0[0], PLANES == 2 ? u0[16 * TP] : 0, cs0, cs1);
+        float gv, uv;
         if (EPI == EPI_HE4) {
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                int s = next_sum[j];
-                s += __shfl_xor_sync(0xffffffffu, s, 4);
-                s += __shfl_xor_sync(0xffffffffu, s, 8);
-                s += __shfl_xor_sync(0xffffffffu, s, 16);
-                const int token = n * 8 + 2 * t + j;
-                if (g == 0 && token < a.tokens && s != 0) atomicAdd(a.next_csum + token, s);
+            gv = he4_value(Dg, prm[r], qin.step, cs0, prm[rows_c + r]);
+            uv = he4_value(Du, prm[2 * rows_c + r], qin.step, cs0, prm[3 * rows_c + r]);
+        } else if (EPI == EPI_W1) {
+            const float rs = __ldg(a.row_scale + token);
+            gv = __fmul_rn(__fmul_rn(static_cast<float>(Dg), rs), prm[r]);
+            uv = __fmul_rn(__fmul_rn(static_cast<float>(Du), rs), prm[2 * rows_c + r]);
+        } else {
+            const float rs = __ldg(a.row_scale + token);
+            gv = __fmul_rn(__fmul_rn(static_cast<float>(Dg), prm[r]), rs);
+            uv = __fmul_rn(__fmul_rn(static_cast<float>(Du), prm[2 * rows_c + r]), rs);
+        }
+        const float h = __fmul_rn(silu(gv), uv);
+        if (a.out) a.out[token * a.rows + o] = h;
+        if (EPI == EPI_HE4) {
+            const float gained = __fmul_rn(h, prm[4 * rows_c + r]);
+            bad |= !isfinite(gained);
+            const int code = qnext.code(gained);
+            a.next_codes[frag_offset(token, o, a.next_ld / 64)] = static_cast<int8_t>(code);
+            if (token != lo_token) {
+                if (lo_token >= 0 && lo_sum) atomicAdd(nsum + lo_token, lo_sum);
+                lo_token = token;
+                lo_sum = 0;
             }
+            lo_sum += code;
         }
     }
-    if (EPI == EPI_HE4 && __any_sync(0xffffffffu, bad) && lane == 0) set_flag(a.flags, BD_FLAG_NONFINITE_INPUT);
+    if (EPI == EPI_HE4) {
+        if (lo_token >= 0 && lo_sum) atomicAdd(nsum + lo_token, lo_sum);
+        if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) set_flag(a.flags, BD_FLAG_NONFINITE_INPUT);
+        __syncthreads();
+        if (threadIdx.x < a.tokens && nsum[threadIdx.x]) atomicAdd(a.next_csum + threadIdx.x, nsum[threadIdx.x]);
+    }
 }
 
 // --------------------------------------------------------------------------- single-matrix kernel
 template <int NT, int PLANES, int EPI>
-__global__ void __launch_bounds__(kThreads) proj_kernel(const ProjArgs a) {
-    __shared__ int red[kBlocksPerCta * 32 * PLANES * NT * 4];
+__global__ void __launch_bounds__(kThreads) proj_kernel(const ProjArgs a, int blocks_per_cta) {
+    extern __shared__ __align__(16) char sm[];
+    __shared__ int last;
     constexpr int TP = NT * 8;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int g = lane >> 2, t = lane & 3;
-    const int slot = warp / kSplit, ks = warp % kSplit;
     const int64_t nrb = (a.rows + 15) / 16;
-    const int64_t rb = static_cast<int64_t>(blockIdx.x) * kBlocksPerCta + slot;
     const int ncp = static_cast<int>(a.ncp);
-    const int kc0 = static_cast<int>(blockIdx.y) * ncp / a.kgroups;
-    const int kc1 = static_cast<int>(blockIdx.y + 1) * ncp / a.kgroups;
-    const int cp0 = kc0 + ks * (kc1 - kc0) / kSplit;
-    const int cp1 = kc0 + (ks + 1) * (kc1 - kc0) / kSplit;
-    const bool active = rb < nrb && cp0 < cp1;
-    const int64_t nsp = a.ld / 64;
+    Tile tile;
+    tile.block0 = static_cast<int64_t>(blockIdx.x) * blocks_per_cta;
+    tile.blocks = static_cast<int>(min(static_cast<int64_t>(blocks_per_cta), nrb - tile.block0));
+    tile.cp0 = static_cast<int>(blockIdx.y) * ncp / a.kgroups;
+    tile.ncpc = static_cast<int>(blockIdx.y + 1) * ncp / a.kgroups - tile.cp0;
+    const int ncpc_max = (ncp + a.kgroups - 1) / a.kgroups;
+    const Plan pl(1, TP, PLANES, blocks_per_cta, ncpc_max);
+    int *sacc = reinterpret_cast<int *>(sm + pl.acc);
+    float *prm = reinterpret_cast<float *>(sm + pl.params);  // [2][blocks*16]: scale0, mid0
 
-    const uint32_t *bits = a.bits + rb * a.ncp * 128 + lane * 4;
-    uint4 wr[kBatch];
-    if (active) {
-#pragma unroll
-        for (int i = 0; i < kBatch; ++i)
-            if (cp0 + i < cp1) wr[i] = ld_stream_u4(bits + (cp0 + i) * 128);
+    if (tile.ncpc > 0) stage_bits(sm, pl, a, tile);
+    const int rows_c = tile.blocks * 16;
+    for (int i = threadIdx.x; i < rows_c; i += kThreads) {
+        const int64_t o = tile.block0 * 16 + i;
+        const bool live = o < a.rows;
+        prm[i] = live ? __ldg(a.scale0 + o) : 0.0f;
+        prm[rows_c + i] = (live && a.mid0) ? __ldg(a.mid0 + o) : 0.0f;
     }
+    for (int i = threadIdx.x; i < tile.blocks * 16 * TP * PLANES; i += kThreads) sacc[i] = 0;
     grid_wait();
     grid_launch_dependents();
-
-    int acc[1][PLANES][NT][4];
-    zero_acc(acc);
-    if (active) {
-        for (int base = cp0; base < cp1; base += kBatch) {
-            if (base != cp0) {
-#pragma unroll
-                for (int i = 0; i < kBatch; ++i)
-                    if (base + i < cp1) wr[i] = ld_stream_u4(bits + (base + i) * 128);
-            }
-#pragma unroll
-            for (int i = 0; i < kBatch; ++i)
-                if (base + i < cp1) {
-                    const uint4 w[1] = {wr[i]};
-                    unit_mma<NT, PLANES, 1>(acc, w, a.codes0, a.codes1, nsp, base + i, lane);
-                }
-        }
-    }
-    reduce_split(acc, red, slot, ks, lane);
-    if (ks != 0 || rb >= nrb) return;
-
+    // The plan's regions are sized for ncpc_max; this CTA's slice (tile.ncpc,
+    // possibly one pair shorter) is staged and walked with its own stride.
+    if (tile.ncpc > 0) stage_codes(sm, pl, a, tile, NT);
+    cp_async_wait_all();
+    __syncthreads();
+    if (tile.ncpc > 0) walk_items<NT, PLANES, 1>(sm, sacc, pl, tile);
+    __syncthreads();
+    const int elems = tile.blocks * 16 * TP * PLANES;  // accumulator cells of this CTA
     if (a.kgroups > 1) {
-        // split-K across CTAs: integer partial sums meet in global accumulators;
-        // the last arriving CTA of this row block reads them back (and leaves zeros).
         const int64_t rows_pad = nrb * 16;
-#pragma unroll
-        for (int p = 0; p < PLANES; ++p)
-#pragma unroll
-            for (int n = 0; n < NT; ++n)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int row = g + 8 * (i >> 1);
-                    const int token = n * 8 + 2 * t + (i & 1);
-                    const int v = acc[0][p][n][i];
-                    if (v) atomicAdd(a.acc + (p * rows_pad + rb * 16 + row) * TP + token, v);
-                }
-        __threadfence();
-        __syncwarp();
-        int old = 0;
-        if (lane == 0) old = atomicAdd(a.counters + rb, 1);
-        old = __shfl_sync(0xffffffffu, old, 0);
-        if (old != a.kgroups - 1) return;
-        __threadfence();
-#pragma unroll
-        for (int p = 0; p < PLANES; ++p)
-#pragma unroll
-            for (int n = 0; n < NT; ++n)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int row = g + 8 * (i >> 1);
-                    const int token = n * 8 + 2 * t + (i & 1);
-                    acc[0][p][n][i] = atomicExch(a.acc + (p * rows_pad + rb * 16 + row) * TP + token, 0);
-                }
-        if (lane == 0) atomicExch(a.counters + rb, 0);
-    }
-
-    Quant qin;
-    if (EPI == EPI_HE4) qin.init(*a.bound, a.code_bits);
-#pragma unroll
-    for (int n = 0; n < NT; ++n)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int row = g + 8 * (i >> 1);
-            const int token = n * 8 + 2 * t + (i & 1);
-            const int64_t o = rb * 16 + row;
-            if (token >= a.tokens || o >= a.rows) continue;
-            int d[PLANES];
-#pragma unroll
-            for (int p = 0; p < PLANES; ++p) d[p] = acc[0][p][n][i];
-            const int cs0 = code_sum(a.csum0, a.nparts, token);
-            const int cs1 = PLANES == 2 ? code_sum(a.csum1, a.nparts, token) : 0;
-            const int D = pm_dot<PLANES>(d, cs0, cs1);
-            float y;
-            if (EPI == EPI_HE4) {
-                y = he4_value(D, a.scale0[o], qin.step, cs0, a.mid0[o]);
-            } else if (EPI == EPI_W1) {
-                y = __fmul_rn(__fmul_rn(static_cast<float>(D), a.row_scale[token]), a.scale0[o]);
-            } else {
-                y = __fmul_rn(__fmul_rn(static_cast<float>(D), a.scale0[o]), a.row_scale[token]);
-            }
-            if (a.residual) y = __fadd_rn(a.residual[token * a.rows + o], y);
-            a.out[token * a.rows + o] = y;
-            if (a.raw_dot) a.raw_dot[token * a.rows + o] = D;
+        for (int e = threadIdx.x; e < elems; e += kThreads) {
+            const int token = e % TP;
+            const int rest = e / TP;
+            const int row = rest % 16;
+            const int rest2 = rest / 16;
+            const int p = rest2 % PLANES;
+            const int b = rest2 / PLANES;
+            const int v = sacc[e];
+            if (v) atomicAdd(a.acc + (p * rows_pad + (tile.block0 + b) * 16 + row) * TP + token, v);
         }
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) last = atomicAdd(a.counters + blockIdx.x, 1) == a.kgroups - 1;
+        __syncthreads();
+        if (!last) return;
+        __threadfence();
+        for (int e = threadIdx.x; e < elems; e += kThreads) {
+            const int token = e % TP;
+            const int rest = e / TP;
+            const int row = rest % 16;
+            const int rest2 = rest / 16;
+            const int p = rest2 % PLANES;
+            const int b = rest2 / PLANES;
+            sacc[e] = atomicExch(a.acc + (p * rows_pad + (tile.block0 + b) * 16 + row) * TP + token, 0);
+        }
+        if (threadIdx.x == 0) atomicExch(a.counters + blockIdx.x, 0);
+        __syncthreads();
+    }
+    Quant qin;
+    if (EPI == EPI_HE4) qin.init(__ldg(a.bound), a.code_bits);
+    const int outs = tile.blocks * TP * 16;
+    for (int e = threadIdx.x; e < outs; e += kThreads) {
+        const int row = e & 15;
+        const int rest = e >> 4;
+        const int token = rest % TP;
+        const int b = rest / TP;
+        const int64_t o = (tile.block0 + b) * 16 + row;
+        if (o >= a.rows || token >= a.tokens) continue;
+        const int r = b * 16 + row;
+        const int cs0 = code_sum(a.csum0, a.nparts, token);
+        const int cs1 = PLANES == 2 ? code_sum(a.csum1, a.nparts, token) : 0;
+        const int *c0 = sacc + ((b * PLANES + 0) * 16 + row) * TP + token;
+        const int D = pm_dot<PLANES>(c0[0], PLANES == 2 ? c0[16 * TP] : 0, cs0, cs1);
+        float y;
+        if (EPI == EPI_HE4) {
+            y = he4_value(D, prm[r], qin.step, cs0, prm[rows_c + r]);
+        } else if (EPI == EPI_W1) {
+            y = __fmul_rn(__fmul_rn(static_cast<float>(D), __ldg(a.row_scale + token)), prm[r]);
+        } else {
+            y = __fmul_rn(__fmul_rn(static_cast<float>(D), prm[r]), __ldg(a.row_scale + token));
+        }
+        if (a.residual) y = __fadd_rn(a.residual[token * a.rows + o], y);
+        a.out[token * a.rows + o] = y;
+        if (a.raw_dot) a.raw_dot[token * a.rows + o] = D;
+    }
 }
 
 // --------------------------------------------------------------------------- launchers
 
-template <int NT, int PLANES, int EPI>
-static int launch_gateup_t(const ProjArgs &a, cudaStream_t stream) {
-    const int64_t npairs = (a.rows + 15) / 16;
-    const unsigned grid = static_cast<unsigned>((npairs + kBlocksPerCta - 1) / kBlocksPerCta);
-    return launch_pdl(gateup_kernel<NT, PLANES, EPI>, dim3(grid), dim3(kThreads), 0, stream, a);
+static int sms_cached() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0, v = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess &&
+            cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0)
+            n = v;
+        else
+            n = 148;
+    }
+    return n;
+}
+
+// Resident CTAs per SM of `kern` with `smem` dynamic bytes (registers, threads
+// and shared memory all counted by the occupancy calculator).
+template <typename Kern>
+static int ctas_per_sm(Kern kern, int64_t smem) {
+    int n = 0;
+    if (smem > static_cast<int64_t>(kSmemLimit)) return 0;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemLimit)) !=
+            cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kThreads, static_cast<size_t>(smem)) != cudaSuccess)
+        return 0;
+    return n;
 }
 
 template <int NT, int PLANES, int EPI>
-static int launch_proj_t(const ProjArgs &a, cudaStream_t stream) {
+static int launch_gateup_t(const ProjArgs &a, cudaStream_t stream) {
+    const int64_t npairs = (a.rows + 15) / 16;
+    const int sms = sms_cached();
+    auto kern = gateup_kernel<NT, PLANES, EPI>;
+    // fewest pairs per CTA such that all CTAs are resident at once
+    int per = 0;
+    for (int p = 1; p <= 64; ++p) {
+        const Plan pl(2, NT * 8, PLANES, p, static_cast<int>(a.ncp));
+        const int occ = ctas_per_sm(kern, pl.total);
+        if (occ == 0) break;
+        per = p;
+        if (static_cast<int64_t>(p) * occ * sms >= npairs) break;
+    }
+    if (per == 0) return BD_ERR_INVALID;
+    const Plan pl(2, NT * 8, PLANES, per, static_cast<int>(a.ncp));
+    const unsigned grid = static_cast<unsigned>((npairs + per - 1) / per);
+    return launch_pdl(kern, dim3(grid), dim3(kThreads), static_cast<size_t>(pl.total), stream, a, per);
+}
+
+// Row blocks per CTA and K groups of a single-matrix projection: one resident
+// wave, small CTAs, and a K split only where it buys parallelism (its global
+// atomics and last-arriver epilogue cost time).
+template <int NT, int PLANES, int EPI>
+static int launch_proj_t(const ProjArgs &a0, cudaStream_t stream) {
+    ProjArgs a = a0;
     const int64_t nrb = (a.rows + 15) / 16;
-    dim3 grid(static_cast<unsigned>((nrb + kBlocksPerCta - 1) / kBlocksPerCta), static_cast<unsigned>(a.kgroups));
-    return launch_pdl(proj_kernel<NT, PLANES, EPI>, grid, dim3(kThreads), 0, stream, a);
+    const int sms = sms_cached();
+    auto kern = proj_kernel<NT, PLANES, EPI>;
+    int best_per = 0, best_kg = 1;
+    double best_cost = 1e30;
+    const int max_kg = a.acc && a.counters ? static_cast<int>(a.ncp) : 1;
+    for (int per = 1; per <= 16; ++per) {
+        for (int kg = 1; kg <= max_kg; ++kg) {
+            const int ncpc = static_cast<int>((a.ncp + kg - 1) / kg);
+            const Plan pl(1, NT * 8, PLANES, per, ncpc);
+            const int occ = ctas_per_sm(kern, pl.total);
+            if (occ == 0) continue;
+            const int64_t ctas = (nrb + per - 1) / per * kg;
+            const int64_t slots = static_cast<int64_t>(occ) * sms;
+            const int64_t waves = (ctas + slots - 1) / slots;
+            const double cost = waves * (per * ncpc + 6.0) + (kg > 1 ? 4.0 + 0.3 * per * kg : 0.0);
+            if (cost < best_cost) {
+                best_cost = cost;
+                best_per = per;
+                best_kg = kg;
+            }
+        }
+    }
+    if (best_per == 0) return BD_ERR_INVALID;
+    a.blocks_per_cta = best_per;
+    a.kgroups = best_kg;
+    const int ncpc_max = static_cast<int>((a.ncp + a.kgroups - 1) / a.kgroups);
+    const Plan pl(1, NT * 8, PLANES, best_per, ncpc_max);
+    dim3 grid(static_cast<unsigned>((nrb + best_per - 1) / best_per), static_cast<unsigned>(a.kgroups));
+    return launch_pdl(kern, grid, dim3(kThreads), static_cast<size_t>(pl.total), stream, a, best_per);
 }
 
 #define BD_DISPATCH_NT(fn, planes, epi)                                  \
@@ -392,20 +496,16 @@ int launch_gateup(const ProjArgs &a, int epi, cudaStream_t stream) {
 }
 
 int launch_proj(const ProjArgs &a, int epi, cudaStream_t stream) {
-    if (a.tokens < 1 || a.tokens > 32 || a.kgroups < 1 || a.nparts < 1) return BD_ERR_INVALID;
+    if (a.tokens < 1 || a.tokens > 32 || a.nparts < 1) return BD_ERR_INVALID;
     if (epi == EPI_HE4) BD_DISPATCH_NT(launch_proj_t, 1, EPI_HE4);
     if (epi == EPI_W1) BD_DISPATCH_NT(launch_proj_t, 2, EPI_W1);
     BD_DISPATCH_NT(launch_proj_t, 1, EPI_W1A1);
 }
 
-// K groups (CTAs along K) for the single-matrix kernel: about two waves of
-// CTAs, at least kSplit column pairs per group.
-int choose_kgroups(int64_t rows, int64_t ncp, int sms) {
-    const int64_t ctas = ((rows + 15) / 16 + kBlocksPerCta - 1) / kBlocksPerCta;
-    int64_t kg = (2 * sms + ctas - 1) / ctas;
-    if (kg > ncp / kSplit) kg = ncp / kSplit;
-    if (kg < 1) kg = 1;
-    return static_cast<int>(kg);
+// Kept for the callers' sake: the launcher plans the grid itself.
+void plan_proj(ProjArgs &a, int) {
+    a.kgroups = 1;
+    a.blocks_per_cta = 1;
 }
 
 }  // namespace bd

@@ -57,6 +57,7 @@ struct ProjArgs {
     int64_t ld;               // codes row stride (multiple of 256)
     int tokens;
     int kgroups;              // CTAs along K (single-matrix kernel)
+    int blocks_per_cta;       // row blocks per CTA (single-matrix kernel)
     // epilogue operands (matrix 0 = gate or the single matrix, 1 = up)
     const float *scale0, *mid0, *scale1, *mid1;
     const float *bound;       // HE4 bound of this projection's codes
@@ -78,5 +79,7 @@ struct ProjArgs {
 
 int launch_gateup(const ProjArgs &a, int epi, cudaStream_t stream);
 int launch_proj(const ProjArgs &a, int epi, cudaStream_t stream);
+// Choose kgroups / blocks_per_cta of a single-matrix projection (one CTA wave).
+void plan_proj(ProjArgs &a, int planes);
 
 }  // namespace bd
