@@ -75,6 +75,16 @@ SIGNATURES = {
     "bd_accept_workspace_bytes": (c_size_t, [c_int, c_int]),
     "bd_accept_greedy": (c_int, [P, c_int, c_int, c_int64, P, P, c_int, P, P, P, P, c_size_t, P, P]),
     "bd_argmax_rows_bf16": (c_int, [P, c_int64, c_int64, P, P, P]),
+    "bd_w16_bytes": (c_int64, [c_int64, c_int64]),
+    "bd_tile_w16": (c_int, [P, c_int, c_int64, c_int64, P, P]),
+    "bd_x16_bytes": (c_int64, [c_int, c_int64]),
+    "bd_pack_x16": (c_int, [P, c_int, c_int64, c_int64, P, ctypes.c_float, P, P, c_int64, P, P]),
+    "bd_gemv_bf16": (c_int, [P, c_int64, c_int64, P, c_int, P, c_int64, P, P, P, P]),
+    "bd_argmax_finish": (c_int, [P, c_int, P, P]),
+    "bd_embed_rows": (c_int, [P, c_int64, c_int64, P, c_int, P, P, P]),
+    "bd_rms_rows": (c_int, [P, c_int, c_int64, c_int64, P, ctypes.c_float, P, c_int64, P]),
+    "bd_heads_post": (c_int, [P, c_int, c_int64, c_int64, c_int, c_int, P, ctypes.c_float, c_int,
+                              ctypes.c_float, c_int64, P, c_int64, P, P]),
 }
 
 _lib = None
@@ -104,8 +114,15 @@ def load() -> ctypes.CDLL:
     return lib
 
 
+# Kernel launches issued by each entry point (for launch accounting).
+KERNELS_PER_CALL = {"bd_ffn_he4": 3, "bd_ffn_w1": 4}
+launches = 0
+
+
 def call(name: str, *args) -> None:
     """Call an int-status entry point; raise on a non-zero status."""
+    global launches
+    launches += KERNELS_PER_CALL.get(name, 1)
     status = getattr(load(), name)(*args)
     if status != BD_OK:
         message = load().bd_status_string(status).decode()

@@ -1,0 +1,118 @@
+// Small per-row kernels of the block-drafter forward (w1a1_eagle/model.py):
+// embedding gather, rms rows, and the per-head q/k/v post-processing
+// (rms over the head with its norm weight, rotary embedding, fp16 storage with
+// the cache_storage overflow check).
+#include "kernels.cuh"
+
+#include <cuda_fp16.h>
+
+namespace bd {
+
+// state[t] = vocabulary[ids[t]] (bf16 table -> fp32), HE4.forward's embedding (model.py:380-381).
+__global__ void embed_kernel(const uint16_t *__restrict__ table, int64_t vocab, int64_t hidden,
+                             const int32_t *__restrict__ ids, float *__restrict__ out, int32_t *flags) {
+    grid_wait();
+    grid_launch_dependents();
+    const int t = blockIdx.x;
+    int id = ids[t];
+    if (id < 0 || id >= vocab) {
+        if (threadIdx.x == 0) set_flag(flags, BD_FLAG_BAD_TOKEN);
+        id = 0;
+    }
+    const uint16_t *row = table + id * hidden;
+    for (int64_t k = threadIdx.x; k < hidden; k += blockDim.x)
+        out[t * hidden + k] = __uint_as_float(static_cast<uint32_t>(row[k]) << 16);
+}
+
+__device__ __forceinline__ float block_sum(float v, float *part) {
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
+    const int warps = blockDim.x >> 5;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float total = 0.0f;
+    for (int w = 0; w < warps; ++w) total += part[w];
+    return total;
+}
+
+// out = x * rsqrt(mean(x^2) + eps) * w (model.py:50-51), one CTA per row.
+__global__ void rms_rows_kernel(const float *__restrict__ x, int64_t cols, int64_t ldx, const float *__restrict__ w,
+                                float eps, float *__restrict__ out, int64_t ldo) {
+    __shared__ float part[32];
+    grid_wait();
+    grid_launch_dependents();
+    const float *row = x + blockIdx.x * ldx;
+    float ss = 0.0f;
+    for (int64_t k = threadIdx.x; k < cols; k += blockDim.x) ss = fmaf(row[k], row[k], ss);
+    const float scale = rsqrtf(block_sum(ss, part) / static_cast<float>(cols) + eps);
+    for (int64_t k = threadIdx.x; k < cols; k += blockDim.x) out[blockIdx.x * ldo + k] = row[k] * scale * w[k];
+}
+
+// Heads of row r of src (columns col0 + h * d ...): optional rms over the head
+// with weight nw, optional rotary embedding at position pos0 + r
+// (model.py:54-63: out_j = v_j cos(a_j) - v_{j+d/2} sin(a_j), out_{j+d/2} =
+// v_{j+d/2} cos(a_j) + v_j sin(a_j), a_j = pos * theta^(-2j/d)), stored as fp16
+// at dst[(r * heads + h) * d + j] of a row stride dst_ld (elements).
+// Grid (rows, heads), d/2 threads.
+__global__ void heads_post_kernel(const float *__restrict__ src, int64_t ld_src, int64_t col0, int heads, int d,
+                                  const float *__restrict__ nw, float eps, int rope, float theta, int64_t pos0,
+                                  __half *__restrict__ dst, int64_t dst_ld, int32_t *flags) {
+    __shared__ float part[32];
+    grid_wait();
+    grid_launch_dependents();
+    const int r = blockIdx.x, h = blockIdx.y, j = threadIdx.x, half = d >> 1;
+    const bool live = j < half;  // the block is padded to whole warps
+    const float *v = src + r * ld_src + col0 + h * d;
+    float a = live ? v[j] : 0.0f, b = live ? v[j + half] : 0.0f;
+    if (nw) {
+        const float scale = rsqrtf(block_sum(fmaf(a, a, b * b), part) / static_cast<float>(d) + eps);
+        if (live) {
+            a = a * scale * nw[j];
+            b = b * scale * nw[j + half];
+        }
+    }
+    if (!live) return;
+    if (rope) {
+        const float freq = powf(theta, -static_cast<float>(2 * j) / static_cast<float>(d));
+        const float angle = static_cast<float>(pos0 + r) * freq;
+        float s, c;
+        sincosf(angle, &s, &c);
+        const float na = a * c + (-b) * s;
+        const float nb = b * c + a * s;
+        a = na;
+        b = nb;
+    }
+    const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+    if (!isfinite(__half2float(ha)) || !isfinite(__half2float(hb))) set_flag(flags, BD_FLAG_CACHE_OVERFLOW);
+    __half *out = dst + r * dst_ld + h * d;
+    out[j] = ha;
+    out[j + half] = hb;
+}
+
+}  // namespace bd
+
+using namespace bd;
+
+extern "C" int bd_embed_rows(const uint16_t *table, int64_t vocab, int64_t hidden, const int32_t *ids, int n,
+                             float *out, int32_t *flags, bd_stream_t stream) {
+    if (vocab < 1 || hidden < 1 || n < 1 || !table || !ids || !out) return BD_ERR_INVALID;
+    return launch_pdl(embed_kernel, dim3(n), dim3(256), 0, stream, table, vocab, hidden, ids, out, flags);
+}
+
+extern "C" int bd_rms_rows(const float *x, int n, int64_t cols, int64_t ldx, const float *weight, float epsilon,
+                           float *out, int64_t ldo, bd_stream_t stream) {
+    if (n < 1 || cols < 1 || ldx < cols || ldo < cols || !x || !weight || !out) return BD_ERR_INVALID;
+    return launch_pdl(rms_rows_kernel, dim3(n), dim3(256), 0, stream, x, cols, ldx, weight, epsilon, out, ldo);
+}
+
+extern "C" int bd_heads_post(const float *src, int n, int64_t ld_src, int64_t col0, int heads, int head_dim,
+                             const float *norm_weight, float epsilon, int rope, float theta, int64_t pos0,
+                             uint16_t *dst_f16, int64_t dst_ld, int32_t *flags, bd_stream_t stream) {
+    if (n < 1 || heads < 1 || head_dim < 2 || (head_dim & 1) || head_dim > 2048 || !src || !dst_f16)
+        return BD_ERR_INVALID;
+    const unsigned threads = static_cast<unsigned>((head_dim / 2 + 31) / 32 * 32);
+    return launch_pdl(heads_post_kernel, dim3(n, heads), dim3(threads), 0, stream, src, ld_src, col0, heads,
+                      head_dim, norm_weight, epsilon, rope, theta, pos0, reinterpret_cast<__half *>(dst_f16), dst_ld,
+                      flags);
+}

@@ -1,0 +1,324 @@
+// bf16 matrix x small activation block (tokens <= 32): the attention projections,
+// context fusion and the tied LM head of the drafter.  HBM-bound: every weight
+// byte is read once, straight into registers, in a tile order where each lane's
+// 16-byte load is exactly its m16n8k16 A fragment (W16 layout).  Activations
+// are split into bf16 hi + lo planes (x ~= hi + lo to ~16 bits) laid out as B
+// fragments (X16 layout), so the fp32 accumulation sees ~fp32-quality inputs
+// for the cost of a second MMA the HBM stream hides.  Each CTA owns RB row
+// blocks; its 8 warps split K and their partial sums are added in a fixed order
+// through shared memory (deterministic).  Epilogues: store (+ residual) and a
+// running per-token argmax (largest value, lowest row on ties) kept as 64-bit
+// keys updated with atomicMax.
+#include <algorithm>
+
+#include "kernels.cuh"
+
+namespace bd {
+
+constexpr int kGemvThreads = 256;
+constexpr int kGemvWarps = kGemvThreads / 32;
+constexpr int kGemvUnroll = 4;
+
+struct GemvArgs {
+    const uint4 *w;              // W16 tiles
+    int64_t rows, cols, nkt;     // O, K (unpadded), K tiles of 16
+    const uint2 *x;              // X16 fragments: [plane][ntb][nkt][32]
+    int64_t ntb;                 // token blocks of 8 in the X16 buffer
+    int tokens;
+    float *out;                  // [tokens][ld_out] or null
+    int64_t ld_out;
+    const float *residual;       // [tokens][ld_out] or null
+    unsigned long long *argmax;  // [tokens] running keys or null
+    int32_t *flags;
+};
+
+__device__ __forceinline__ unsigned long long order_key(float v, uint32_t idx) {
+    uint32_t b = __float_as_uint(v == 0.0f ? 0.0f : v);
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return (static_cast<unsigned long long>(b) << 32) | static_cast<unsigned long long>(~idx);
+}
+
+template <int NT, int RB>
+__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
+    __shared__ float red[kGemvWarps][RB * NT * 4][32];
+    __shared__ unsigned long long best[32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t nrb = (a.rows + 15) / 16;
+    const int64_t rb0 = static_cast<int64_t>(blockIdx.x) * RB;
+    const int64_t kt0 = warp * a.nkt / kGemvWarps, kt1 = (warp + 1) * a.nkt / kGemvWarps;
+    float acc[RB][NT][4];
+#pragma unroll
+    for (int r = 0; r < RB; ++r)
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[r][n][i] = 0.0f;
+
+    const uint4 *wrow[RB];
+#pragma unroll
+    for (int r = 0; r < RB; ++r) wrow[r] = a.w + (rb0 + r < nrb ? rb0 + r : nrb - 1) * a.nkt * 32 + lane;
+    const int64_t plane = a.ntb * a.nkt * 32;
+
+    uint4 wa[kGemvUnroll][RB];
+    // first batch of weights before the dependency wait (weights are read-only)
+#pragma unroll
+    for (int u = 0; u < kGemvUnroll; ++u)
+#pragma unroll
+        for (int r = 0; r < RB; ++r)
+            if (kt0 + u < kt1) wa[u][r] = ld_stream_u4(wrow[r] + (kt0 + u) * 32);
+    grid_wait();
+    grid_launch_dependents();
+    if (threadIdx.x < 32) best[threadIdx.x] = 0ull;
+
+    for (int64_t kt = kt0; kt < kt1; kt += kGemvUnroll) {
+        uint2 xb[kGemvUnroll][2][NT];
+#pragma unroll
+        for (int u = 0; u < kGemvUnroll; ++u)
+            if (kt + u < kt1)
+#pragma unroll
+                for (int p = 0; p < 2; ++p)
+#pragma unroll
+                    for (int n = 0; n < NT; ++n) xb[u][p][n] = __ldg(a.x + p * plane + (n * a.nkt + kt + u) * 32 + lane);
+#pragma unroll
+        for (int u = 0; u < kGemvUnroll; ++u) {
+            if (kt + u < kt1) {
+#pragma unroll
+                for (int r = 0; r < RB; ++r)
+#pragma unroll
+                    for (int p = 0; p < 2; ++p)
+#pragma unroll
+                        for (int n = 0; n < NT; ++n)
+                            mma_bf16_16816(acc[r][n], wa[u][r].x, wa[u][r].y, wa[u][r].z, wa[u][r].w, xb[u][p][n].x,
+                                           xb[u][p][n].y);
+            }
+        }
+        // next batch of weights
+#pragma unroll
+        for (int u = 0; u < kGemvUnroll; ++u)
+#pragma unroll
+            for (int r = 0; r < RB; ++r)
+                if (kt + kGemvUnroll + u < kt1) wa[u][r] = ld_stream_u4(wrow[r] + (kt + kGemvUnroll + u) * 32);
+    }
+#pragma unroll
+    for (int r = 0; r < RB; ++r)
+#pragma unroll
+        for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) red[warp][(r * NT + n) * 4 + i][lane] = acc[r][n][i];
+    __syncthreads();
+    // every thread finishes cells (value slot v, lane l) summing warps 0..7 in order
+    constexpr int CELLS = RB * NT * 4 * 32;
+    bool bad = false;
+    for (int c = threadIdx.x; c < CELLS; c += kGemvThreads) {
+        const int l = c & 31, v = c >> 5;
+        float s = red[0][v][l];
+#pragma unroll
+        for (int w = 1; w < kGemvWarps; ++w) s = __fadd_rn(s, red[w][v][l]);
+        const int i = v & 3, n = (v >> 2) % NT, r = (v >> 2) / NT;
+        const int g = l >> 2, t = l & 3;
+        const int64_t o = (rb0 + r) * 16 + g + 8 * (i >> 1);
+        const int token = n * 8 + 2 * t + (i & 1);
+        if (o >= a.rows || token >= a.tokens) continue;
+        if (a.residual) s = __fadd_rn(a.residual[token * a.ld_out + o], s);
+        if (a.out) a.out[token * a.ld_out + o] = s;
+        if (a.argmax) {
+            if (isfinite(s))
+                atomicMax(best + token, order_key(s, static_cast<uint32_t>(o)));
+            else
+                bad = true;
+        }
+    }
+    if (a.argmax) {
+        if (__any_sync(0xffffffffu, bad) && lane == 0) set_flag(a.flags, BD_FLAG_NONFINITE_STATE);
+        __syncthreads();
+        if (threadIdx.x < a.tokens && best[threadIdx.x]) atomicMax(a.argmax + threadIdx.x, best[threadIdx.x]);
+    }
+}
+
+// W16 tiles from fp32 or bf16 row-major weights; one thread per lane-slot (8 values).
+template <typename T>
+__global__ void tile_w16_kernel(const T *__restrict__ w, int64_t rows, int64_t cols, int64_t nkt,
+                                uint16_t *__restrict__ out) {
+    const int64_t nrb = (rows + 15) / 16;
+    const int64_t total = nrb * nkt * 32;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int lane = static_cast<int>(i & 31);
+        const int64_t rest = i >> 5;
+        const int64_t kt = rest % nkt, rb = rest / nkt;
+        const int g = lane >> 2, t = lane & 3;
+        uint16_t v[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const int64_t row = rb * 16 + g + 8 * ((e >> 1) & 1);
+            const int64_t col = kt * 16 + 2 * t + (e & 1) + 8 * (e >> 2);
+            float f = 0.0f;
+            if (row < rows && col < cols) {
+                if constexpr (sizeof(T) == 4)
+                    f = static_cast<float>(w[row * cols + col]);
+                else
+                    f = __uint_as_float(static_cast<uint32_t>(reinterpret_cast<const uint16_t *>(w)[row * cols + col]) << 16);
+            }
+            v[e] = __bfloat16_as_ushort(__float2bfloat16_rn(f));
+        }
+        uint4 packed;
+        packed.x = v[0] | (static_cast<uint32_t>(v[1]) << 16);
+        packed.y = v[2] | (static_cast<uint32_t>(v[3]) << 16);
+        packed.z = v[4] | (static_cast<uint32_t>(v[5]) << 16);
+        packed.w = v[6] | (static_cast<uint32_t>(v[7]) << 16);
+        reinterpret_cast<uint4 *>(out)[i] = packed;
+    }
+}
+
+// X16 activation fragments (hi/lo bf16 planes) of rows of x, optionally
+// rms-normalised first: y = x * rsqrt(mean(x^2) + eps) * weight (model.py:50-51).
+// One CTA per token; columns >= cols are written as zeros.
+__global__ void __launch_bounds__(256) pack_x16_kernel(const float *__restrict__ x, int64_t cols, int64_t ldx,
+                                                       int64_t nkt, int64_t ntb, const float *__restrict__ weight,
+                                                       float eps, uint16_t *__restrict__ out, float *normed,
+                                                       int64_t ld_normed, int32_t *flags) {
+    __shared__ float part[8];
+    grid_wait();
+    grid_launch_dependents();
+    const int token = blockIdx.x;
+    const float *row = x + token * ldx;
+    float scale = 1.0f;
+    bool bad = false;
+    if (weight) {
+        float ss = 0.0f;
+        for (int64_t k = threadIdx.x; k < cols; k += blockDim.x) {
+            const float v = row[k];
+            ss = fmaf(v, v, ss);
+        }
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, d);
+        if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+        __syncthreads();
+        float total = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) total += part[w];
+        scale = rsqrtf(total / static_cast<float>(cols) + eps);
+    }
+    const int nt = token >> 3, g = token & 7;
+    for (int64_t k = threadIdx.x; k < nkt * 16; k += blockDim.x) {
+        float y = 0.0f;
+        if (k < cols) {
+            y = row[k];
+            if (weight) y = y * scale * weight[k];
+            bad |= !isfinite(y);
+            if (normed) normed[token * ld_normed + k] = y;
+        }
+        const __nv_bfloat16 hi = __float2bfloat16_rn(y);
+        const __nv_bfloat16 lo = __float2bfloat16_rn(y - __bfloat162float(hi));
+        const int64_t kt = k >> 4;
+        const int kk = static_cast<int>(k & 15);
+        const int t = (kk & 7) >> 1, half = kk >> 3, e = kk & 1;
+        const int64_t off = (((nt * nkt + kt) * 32 + g * 4 + t) << 2) + half * 2 + e;  // in bf16 units
+        out[off] = __bfloat16_as_ushort(hi);
+        out[ntb * nkt * 32 * 4 + off] = __bfloat16_as_ushort(lo);
+    }
+    if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) set_flag(flags, BD_FLAG_NONFINITE_STATE);
+}
+
+// Decode argmax keys into token ids and reset the keys for the next use.
+__global__ void argmax_finish_kernel(unsigned long long *keys, int n, int32_t *out) {
+    grid_wait();
+    grid_launch_dependents();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) {
+        const unsigned long long k = keys[i];
+        out[i] = k ? static_cast<int32_t>(~static_cast<uint32_t>(k & 0xffffffffull)) : -1;
+        keys[i] = 0ull;
+    }
+}
+
+template <int NT, int RB>
+static int launch_gemv_t(const GemvArgs &a, cudaStream_t stream) {
+    const int64_t nrb = (a.rows + 15) / 16;
+    const unsigned grid = static_cast<unsigned>((nrb + RB - 1) / RB);
+    return launch_pdl(gemv_kernel<NT, RB>, dim3(grid), dim3(kGemvThreads), 0, stream, a);
+}
+
+int launch_gemv(const GemvArgs &a, cudaStream_t stream) {
+    const int64_t nrb = (a.rows + 15) / 16;
+    const bool wide = nrb >= 8 * 148;  // many row blocks: two per CTA halves activation traffic
+    const int nt = (a.tokens + 7) / 8;
+    if (a.tokens < 1 || a.tokens > 32 || nt > a.ntb) return BD_ERR_INVALID;
+    switch (nt * 2 + (wide ? 1 : 0)) {
+        case 2: return launch_gemv_t<1, 1>(a, stream);
+        case 3: return launch_gemv_t<1, 2>(a, stream);
+        case 4: return launch_gemv_t<2, 1>(a, stream);
+        case 5: return launch_gemv_t<2, 2>(a, stream);
+        case 6: return launch_gemv_t<3, 1>(a, stream);
+        case 7: return launch_gemv_t<3, 2>(a, stream);
+        case 8: return launch_gemv_t<4, 1>(a, stream);
+        default: return launch_gemv_t<4, 2>(a, stream);
+    }
+}
+
+}  // namespace bd
+
+using namespace bd;
+
+static int64_t nkt_of(int64_t cols) { return (cols + 15) / 16; }
+
+extern "C" int64_t bd_w16_bytes(int64_t rows, int64_t cols) {
+    if (rows < 0 || cols < 0) return -1;
+    return (rows + 15) / 16 * nkt_of(cols) * 512;
+}
+
+extern "C" int bd_tile_w16(const void *w, int dtype_bits, int64_t rows, int64_t cols, void *out,
+                           bd_stream_t stream) {
+    if (rows < 1 || cols < 1 || !w || !out || (dtype_bits != 32 && dtype_bits != 16)) return BD_ERR_INVALID;
+    const int64_t total = (rows + 15) / 16 * nkt_of(cols) * 32;
+    const int grid = static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 32));
+    if (dtype_bits == 32)
+        tile_w16_kernel<float><<<grid, 256, 0, stream>>>(static_cast<const float *>(w), rows, cols, nkt_of(cols),
+                                                        static_cast<uint16_t *>(out));
+    else
+        tile_w16_kernel<uint16_t><<<grid, 256, 0, stream>>>(static_cast<const uint16_t *>(w), rows, cols,
+                                                           nkt_of(cols), static_cast<uint16_t *>(out));
+    BD_CHECK_LAUNCH();
+    return BD_OK;
+}
+
+extern "C" int64_t bd_x16_bytes(int tokens, int64_t cols) {
+    if (tokens < 0 || cols < 0) return -1;
+    return 2 * static_cast<int64_t>((tokens + 7) / 8) * nkt_of(cols) * 32 * 8;
+}
+
+extern "C" int bd_pack_x16(const float *x, int tokens, int64_t cols, int64_t ldx, const float *rms_weight,
+                           float epsilon, void *out, float *normed, int64_t ld_normed, int32_t *flags,
+                           bd_stream_t stream) {
+    if (tokens < 1 || tokens > 32 || cols < 1 || ldx < cols || !x || !out) return BD_ERR_INVALID;
+    return launch_pdl(pack_x16_kernel, dim3(tokens), dim3(256), 0, stream, x, cols, ldx, nkt_of(cols),
+                      static_cast<int64_t>((tokens + 7) / 8), rms_weight, epsilon, static_cast<uint16_t *>(out),
+                      normed, ld_normed, flags);
+}
+
+extern "C" int bd_gemv_bf16(const void *w16, int64_t rows, int64_t cols, const void *x16, int tokens, float *out,
+                            int64_t ld_out, const float *residual, unsigned long long *argmax_keys, int32_t *flags,
+                            bd_stream_t stream) {
+    if (rows < 1 || cols < 1 || !w16 || !x16 || tokens < 1 || tokens > 32) return BD_ERR_INVALID;
+    if (!out && !argmax_keys) return BD_ERR_INVALID;
+    if ((out || residual) && ld_out < rows) return BD_ERR_INVALID;
+    GemvArgs a{};
+    a.w = static_cast<const uint4 *>(w16);
+    a.rows = rows;
+    a.cols = cols;
+    a.nkt = nkt_of(cols);
+    a.x = static_cast<const uint2 *>(x16);
+    a.ntb = (tokens + 7) / 8;
+    a.tokens = tokens;
+    a.out = out;
+    a.ld_out = ld_out;
+    a.residual = residual;
+    a.argmax = argmax_keys;
+    a.flags = flags;
+    return launch_gemv(a, stream);
+}
+
+extern "C" int bd_argmax_finish(unsigned long long *keys, int n, int32_t *out, bd_stream_t stream) {
+    if (n < 1 || !keys || !out) return BD_ERR_INVALID;
+    return launch_pdl(argmax_finish_kernel, dim3((n + 127) / 128), dim3(128), 0, stream, keys, n, out);
+}

@@ -1,0 +1,325 @@
+"""Block-drafter forward engine for the B200: HE4.forward of the reference as a
+device-resident, CUDA-graph-capturable draft step.
+
+Follows ``w1a1_eagle/model.py``: ``HE4.forward`` (369-396), ``Layer.context``
+(195-200) and ``Layer.forward`` (202-223).  The reference recomputes the fused
+context and every layer's context K/V on each call; the engine keeps them in an
+fp16 K/V cache (exactly the values ``cache_storage`` would produce) filled by
+``prefill`` and extended by ``ingest``, so a draft round reads each weight once.
+
+Device data (all on one GPU):
+  * dense matrices (fc, per-layer q|k|v and o, the tied vocabulary) as bf16
+    W16 tiles for ``bd_gemv_bf16``; the vocabulary also as a plain bf16 table
+    for the embedding gather;
+  * the one-bit feed-forward blocks as T16 sign tiles with fp32 scales,
+    midpoints and exponentiated gains/clip bounds (``ops.PackedFFN``);
+  * K/V caches fp16 ``[layers][positions][kv_heads][head_dim]``.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+from torch import Tensor
+from torch.nn import functional
+
+from . import _lib, ops
+from .ops import Flags, PackedFFN, _p, _stream
+
+
+def _w16(weight: Tensor) -> Tensor:
+    """W16 tiles (uint8 storage) of a row-major fp32/bf16 matrix."""
+    weight = weight.contiguous()
+    rows, cols = weight.shape
+    out = torch.empty(int(_lib.load().bd_w16_bytes(rows, cols)), dtype=torch.uint8, device=weight.device)
+    bits = 32 if weight.dtype == torch.float32 else 16
+    if weight.dtype not in (torch.float32, torch.bfloat16):
+        weight = weight.float()
+        bits = 32
+    _lib.call("bd_tile_w16", _p(weight), bits, rows, cols, _p(out), _stream(weight.device))
+    return out
+
+
+def _w16_rows(w16: Tensor, cols: int, row0: int, rows: int) -> int:
+    """Device address of rows [row0, row0 + rows) of a W16 buffer (row0 % 16 == 0)."""
+    if row0 % 16:
+        raise ValueError("W16 row ranges start on a 16-row block")
+    block = int(_lib.load().bd_w16_bytes(16, cols))
+    return w16.data_ptr() + (row0 // 16) * block
+
+
+@dataclass
+class LayerDevice:
+    qkv: Tensor            # W16 of cat(attn_q, attn_k, attn_v)
+    o: Tensor              # W16 of attn_output
+    attn_norm: Tensor
+    q_norm: Tensor
+    k_norm: Tensor
+    ffn_norm: Tensor
+    ffn: PackedFFN
+
+
+class DraftEngine:
+    """One drafter on one device.  ``tokens`` per call (block slots) <= 32."""
+
+    def __init__(self, tensors: dict[str, Tensor], vocabulary: Tensor, mask: int, geometry, quantizers: dict | None = None,
+                 device: torch.device | str = "cuda", max_positions: int | None = None):
+        cfg = self.cfg = geometry
+        self.device = torch.device(device)
+        self.mask = int(mask)
+        self.vocab_size, hidden = vocabulary.shape
+        if hidden != cfg.hidden:
+            raise ValueError("invalid frozen vocabulary geometry or mask")
+        self.max_positions = int(max_positions or (cfg.window + cfg.slots))
+        dev = self.device
+
+        def t(name):
+            return tensors[name].to(dev)
+
+        vocab = vocabulary.to(dev)
+        self.vocab16 = vocab.to(torch.bfloat16).contiguous()
+        self.head = _w16(self.vocab16)
+        self.fc = _w16(t("fc.weight").to(torch.bfloat16))
+        self.fc_bf16 = t("fc.weight").to(torch.bfloat16).contiguous()
+        self.enc_norm = t("enc.output_norm.weight").float().contiguous()
+        self.out_norm = t("output_norm.weight").float().contiguous()
+        quantizers = quantizers or {}
+        self.layers: list[LayerDevice] = []
+        self.kv_bf16: list[Tensor] = []
+        for i in range(cfg.layers):
+            p = f"blk.{i}."
+            q, k, v = t(p + "attn_q.weight"), t(p + "attn_k.weight"), t(p + "attn_v.weight")
+            qkv = torch.cat((q, k, v), 0).to(torch.bfloat16)
+            self.kv_bf16.append(torch.cat((k, v), 0).to(torch.bfloat16).contiguous())
+            gate, up, down = t(p + "ffn_gate.weight").float(), t(p + "ffn_up.weight").float(), t(p + "ffn_down.weight").float()
+
+            def qv(name, default):
+                value = quantizers.get(p + name)
+                return (default if value is None else value.to(dev).float()).contiguous().reshape(-1)
+
+            ffn = ops.pack_ffn(gate, up, down, qv("ffn_gate.scale", gate.abs().mean(-1)),
+                               qv("ffn_up.scale", up.abs().mean(-1)), qv("ffn_down.scale", down.abs().mean(-1)))
+            ffn.midpoint_gate = qv("ffn_gate.midpoint", torch.zeros(cfg.intermediate, device=dev))
+            ffn.midpoint_up = qv("ffn_up.midpoint", torch.zeros(cfg.intermediate, device=dev))
+            ffn.midpoint_down = qv("ffn_down.midpoint", torch.zeros(cfg.hidden, device=dev))
+            ffn.gain_gate_up = qv("ffn_gate_up.gain", torch.ones(cfg.hidden, device=dev))
+            ffn.bound_gate_up = qv("ffn_gate_up.bound", torch.ones(1, device=dev))
+            ffn.gain_down = qv("ffn_down.gain", torch.ones(cfg.intermediate, device=dev))
+            ffn.bound_down = qv("ffn_down.bound", torch.ones(1, device=dev))
+            self.layers.append(LayerDevice(
+                qkv=_w16(qkv), o=_w16(t(p + "attn_output.weight").to(torch.bfloat16)),
+                attn_norm=t(p + "attn_norm.weight").float().contiguous(), q_norm=t(p + "attn_q_norm.weight").float().contiguous(),
+                k_norm=t(p + "attn_k_norm.weight").float().contiguous(), ffn_norm=t(p + "ffn_norm.weight").float().contiguous(),
+                ffn=ffn))
+        kvd = cfg.kv_heads * cfg.head_dim
+        self.k_cache = torch.zeros((cfg.layers, self.max_positions, kvd), dtype=torch.float16, device=dev)
+        self.v_cache = torch.zeros_like(self.k_cache)
+        self.qkv_width = (cfg.heads + 2 * cfg.kv_heads) * cfg.head_dim
+        # per-call buffers (fixed addresses, so a draft step can be captured in a graph)
+        T = 32
+        self.ids = torch.zeros(T, dtype=torch.int32, device=dev)
+        self.state = torch.zeros((T, cfg.hidden), dtype=torch.float32, device=dev)
+        self.resid = torch.zeros_like(self.state)
+        self.normed = torch.zeros_like(self.state)
+        self.qkv_out = torch.zeros((T, self.qkv_width), dtype=torch.float32, device=dev)
+        self.q16 = torch.zeros((T, cfg.heads * cfg.head_dim), dtype=torch.float16, device=dev)
+        self.attn = torch.zeros((T, cfg.heads * cfg.head_dim), dtype=torch.float32, device=dev)
+        widest = max(cfg.hidden, cfg.heads * cfg.head_dim, cfg.taps * cfg.hidden)
+        self.x16 = torch.zeros(int(_lib.load().bd_x16_bytes(T, widest)), dtype=torch.uint8, device=dev)
+        self.keys = torch.zeros(T, dtype=torch.int64, device=dev)
+        self.drafted = torch.zeros(T, dtype=torch.int32, device=dev)
+        self.encoded = torch.zeros((T, cfg.hidden), dtype=torch.float32, device=dev)
+        self.fused = torch.zeros((T, cfg.hidden), dtype=torch.float32, device=dev)
+        self.kv_out = torch.zeros((T, 2 * kvd), dtype=torch.float32, device=dev)
+        self.flags = Flags(dev)
+        self._masks: dict[tuple[int, int, int], Tensor] = {}
+        self.positions = 0
+
+    # ------------------------------------------------------------------ helpers
+    def _stream(self) -> int:
+        return _stream(self.device)
+
+    def _pack(self, x: Tensor, n: int, cols: int, ld: int, weight: Tensor | None = None, normed: Tensor | None = None):
+        _lib.call("bd_pack_x16", _p(x), n, cols, ld, _p(weight), float(self.cfg.epsilon), _p(self.x16),
+                  _p(normed), normed.shape[1] if normed is not None else 0, self.flags.ptr, self._stream())
+
+    def _gemv(self, w16_ptr: int, rows: int, cols: int, n: int, out: Tensor | None, ld_out: int,
+              residual: Tensor | None = None, keys: Tensor | None = None):
+        _lib.call("bd_gemv_bf16", w16_ptr, rows, cols, _p(self.x16), n, _p(out), ld_out, _p(residual), _p(keys),
+                  self.flags.ptr, self._stream())
+
+    def _heads(self, src: Tensor, n: int, col0: int, heads: int, norm: Tensor | None, rope: bool, pos0: int,
+               dst_ptr: int, dst_ld: int):
+        cfg = self.cfg
+        _lib.call("bd_heads_post", _p(src), n, src.shape[1], col0, heads, cfg.head_dim, _p(norm), float(cfg.epsilon),
+                  int(rope), float(cfg.theta), pos0, dst_ptr, dst_ld, self.flags.ptr, self._stream())
+
+    def _cache_ptr(self, cache: Tensor, layer: int, pos: int) -> int:
+        return cache[layer, pos].data_ptr()
+
+    def check(self) -> None:
+        """Raise the reference's ValueError for any device-reported condition."""
+        self.flags.check()
+
+    # ------------------------------------------------------------------ context
+    def prefill(self, features: Tensor, anchor: int) -> None:
+        """Context K/V of positions [0, anchor) from target features (model.py:382-386, 195-200).
+
+        Large one-off matrix products (the fused context of all rows) use
+        cuBLAS bf16 GEMMs; normalisation, rotary embedding and fp16 storage are
+        this library's kernels.
+        """
+        cfg = self.cfg
+        if anchor > self.max_positions - cfg.slots:
+            raise ValueError("context longer than the engine's cache")
+        self.positions = anchor
+        if anchor == 0:
+            return
+        feats = features[:anchor].to(self.device, torch.bfloat16)
+        fused = (feats @ self.fc_bf16.T).float()
+        encoded = torch.empty_like(fused)
+        _lib.call("bd_rms_rows", _p(fused), anchor, cfg.hidden, cfg.hidden, _p(self.enc_norm), float(cfg.epsilon),
+                  _p(encoded), cfg.hidden, self._stream())
+        enc16 = encoded.to(torch.bfloat16)
+        kvd = cfg.kv_heads * cfg.head_dim
+        for i, layer in enumerate(self.layers):
+            kv = (enc16 @ self.kv_bf16[i].T).float().contiguous()
+            self._heads(kv, anchor, 0, cfg.kv_heads, layer.k_norm, True, 0, self._cache_ptr(self.k_cache, i, 0), kvd)
+            self._heads(kv, anchor, kvd, cfg.kv_heads, None, False, 0, self._cache_ptr(self.v_cache, i, 0), kvd)
+
+    def ingest(self, features: Tensor, pos0: int) -> None:
+        """Append up to 32 context rows at positions pos0.. through the GEMV path (one draft round)."""
+        cfg = self.cfg
+        n = features.shape[0]
+        if not 1 <= n <= 32 or pos0 + n > self.max_positions - cfg.slots:
+            raise ValueError("invalid context rows")
+        feats = features if features.dtype == torch.float32 else features.float()
+        feats = feats.to(self.device).contiguous()
+        width = cfg.taps * cfg.hidden
+        self._pack(feats, n, width, width)
+        self._gemv(self.fc.data_ptr(), cfg.hidden, width, n, self.fused, cfg.hidden)
+        self._pack(self.fused, n, cfg.hidden, cfg.hidden, self.enc_norm)
+        kvd = cfg.kv_heads * cfg.head_dim
+        q_rows = cfg.heads * cfg.head_dim
+        for i, layer in enumerate(self.layers):
+            self._gemv(_w16_rows(layer.qkv, cfg.hidden, q_rows, 2 * kvd), 2 * kvd, cfg.hidden, n, self.kv_out, 2 * kvd)
+            self._heads(self.kv_out, n, 0, cfg.kv_heads, layer.k_norm, True, pos0, self._cache_ptr(self.k_cache, i, pos0), kvd)
+            self._heads(self.kv_out, n, kvd, cfg.kv_heads, None, False, pos0, self._cache_ptr(self.v_cache, i, pos0), kvd)
+        self.positions = max(self.positions, pos0 + n)
+
+    # ------------------------------------------------------------------ draft
+    def _mask(self, anchor: int, size: int, layer: int) -> Tensor | None:
+        cfg = self.cfg
+        if layer == cfg.layers - 1 or anchor + size <= cfg.window:
+            return None  # every key is inside the window
+        key = (anchor, size, layer)
+        if key not in self._masks:
+            pos = torch.arange(anchor, anchor + size, device=self.device)
+            keys = torch.arange(anchor + size, device=self.device)
+            self._masks[key] = (pos[:, None] - keys[None, :]).abs() < cfg.window
+        return self._masks[key]
+
+    def set_tokens(self, first: int, size: int) -> None:
+        ids = torch.full((size,), self.mask, dtype=torch.int32)
+        ids[0] = first
+        self.ids[:size].copy_(ids, non_blocking=True)
+
+    def draft(self, anchor: int, size: int | None = None, logits: Tensor | None = None) -> Tensor:
+        """One block of the drafter over the cached context (model.py:369-396).
+
+        Slot tokens come from ``self.ids`` (``set_tokens``); returns the argmax
+        token of every slot (int32 [size], device) and fills ``logits`` [size, V]
+        when given.  Graph-capturable for fixed (anchor, size).
+        """
+        cfg = self.cfg
+        k = cfg.slots if size is None else size
+        H = cfg.hidden
+        qd = cfg.heads * cfg.head_dim
+        kvd = cfg.kv_heads * cfg.head_dim
+        L = anchor + k
+        st = self._stream()
+        _lib.call("bd_embed_rows", _p(self.vocab16), self.vocab_size, H, _p(self.ids), k, _p(self.state),
+                  self.flags.ptr, st)
+        scale = 1.0 / math.sqrt(cfg.head_dim)
+        for i, layer in enumerate(self.layers):
+            self._pack(self.state, k, H, H, layer.attn_norm)
+            self._gemv(layer.qkv.data_ptr(), self.qkv_width, H, k, self.qkv_out, self.qkv_width)
+            self._heads(self.qkv_out, k, 0, cfg.heads, layer.q_norm, True, anchor, self.q16.data_ptr(), qd)
+            self._heads(self.qkv_out, k, qd, cfg.kv_heads, layer.k_norm, True, anchor,
+                        self._cache_ptr(self.k_cache, i, anchor), kvd)
+            self._heads(self.qkv_out, k, qd + kvd, cfg.kv_heads, None, False, anchor,
+                        self._cache_ptr(self.v_cache, i, anchor), kvd)
+            q = self.q16[:k].view(k, cfg.heads, cfg.head_dim).transpose(0, 1).unsqueeze(0)
+            kk = self.k_cache[i, :L].view(L, cfg.kv_heads, cfg.head_dim).transpose(0, 1).unsqueeze(0)
+            vv = self.v_cache[i, :L].view(L, cfg.kv_heads, cfg.head_dim).transpose(0, 1).unsqueeze(0)
+            out = functional.scaled_dot_product_attention(q, kk, vv, attn_mask=self._mask(anchor, k, i), scale=scale,
+                                                          enable_gqa=cfg.heads != cfg.kv_heads)
+            self.attn[:k].copy_(out[0].transpose(0, 1).reshape(k, qd))
+            self._pack(self.attn, k, qd, qd)
+            self._gemv(layer.o.data_ptr(), H, qd, k, self.resid, H, residual=self.state)
+            _lib.call("bd_rms_rows", _p(self.resid), k, H, H, _p(layer.ffn_norm), float(cfg.epsilon), _p(self.normed),
+                      H, st)
+            ops.ffn_he4(self.normed[:k], layer.ffn, self.resid[:k], flags=self.flags, out=self.state[:k])
+        self._pack(self.state, k, H, H, self.out_norm)
+        self._gemv(self.head.data_ptr(), self.vocab_size, H, k, logits, self.vocab_size, keys=self.keys)
+        _lib.call("bd_argmax_finish", _p(self.keys), k, _p(self.drafted), st)
+        return self.drafted[:k]
+
+
+class DraftRound:
+    """A captured draft round: ingest ``rows`` new context rows ending at ``anchor``,
+    then draft a block of ``size`` slots.  ``__call__`` is the serving entry point:
+    host (pinned) rows and the anchor token in, drafted tokens (slots 1..size-1) out.
+    """
+
+    def __init__(self, engine: DraftEngine, anchor: int, size: int, rows: int):
+        cfg = engine.cfg
+        self.engine, self.anchor, self.size, self.rows = engine, anchor, size, rows
+        dev = engine.device
+        width = cfg.taps * cfg.hidden
+        self.dev_rows = torch.zeros((rows, width), dtype=torch.bfloat16, device=dev)
+        self.host_rows = torch.zeros((rows, width), dtype=torch.bfloat16).pin_memory()
+        self.host_first = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self.host_out = torch.zeros(size, dtype=torch.int32).pin_memory()
+        engine.set_tokens(engine.mask, size)
+        self.stream = torch.cuda.Stream(dev)
+        self.stream.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(self.stream):
+            for _ in range(2):
+                self._body()
+        self.stream.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=self.stream):
+            self._body()
+        self.stream.synchronize()
+        engine.check()
+
+    def _body(self) -> None:
+        self.engine.ingest(self.dev_rows, self.anchor - self.rows)
+        self.engine.draft(self.anchor, self.size)
+
+    def replay(self) -> None:
+        self.graph.replay()
+
+    @property
+    def h2d_bytes(self) -> int:
+        return self.host_rows.numel() * self.host_rows.element_size() + 4
+
+    @property
+    def d2h_bytes(self) -> int:
+        return self.size * 4
+
+    def __call__(self, first_token: int | None = None) -> Tensor:
+        """H2D of ``host_rows`` (+ the anchor token), one round, D2H of the drafted tokens."""
+        e = self.engine
+        with torch.cuda.stream(self.stream):
+            if first_token is not None:
+                self.host_first[0] = first_token
+            self.dev_rows.copy_(self.host_rows, non_blocking=True)
+            e.ids[:1].copy_(self.host_first, non_blocking=True)
+            self.graph.replay()
+            self.host_out.copy_(e.drafted[: self.size], non_blocking=True)
+        self.stream.synchronize()
+        return self.host_out[1:]

@@ -212,13 +212,13 @@ def pack_ffn(gate: Tensor, up: Tensor, down: Tensor, scale_gate: Tensor | None =
 
 
 def ffn_he4(x: Tensor, ffn: PackedFFN, residual: Tensor | None = None, hidden_out: bool = False,
-            flags: Flags | None = None):
+            flags: Flags | None = None, out: Tensor | None = None):
     """HE4 SwiGLU block ``residual + down(silu(gate(x)) * up(x))`` (model.py:220-223)."""
-    device = _require_cuda(x, residual)
+    device = _require_cuda(x, residual, out)
     tokens = x.shape[0]
     if not 1 <= tokens <= MAX_DECODE_TOKENS:
         raise ValueError("decode feed-forward takes 1 to 32 tokens")
-    y = torch.empty((tokens, ffn.hidden), dtype=torch.float32, device=device)
+    y = torch.empty((tokens, ffn.hidden), dtype=torch.float32, device=device) if out is None else out
     h = torch.empty((tokens, ffn.inter), dtype=torch.float32, device=device) if hidden_out else None
     nbytes = int(_lib.load().bd_ffn_workspace_bytes(tokens, ffn.hidden, ffn.inter))
     ws = workspace(device, "ffn", nbytes)

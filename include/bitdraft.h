@@ -162,6 +162,43 @@ int bd_accept_greedy(const uint16_t *logits, int requests, int drafts, int64_t v
 int bd_argmax_rows_bf16(const uint16_t *logits, int64_t rows, int64_t vocab, int32_t *out,
                         int32_t *flags, bd_stream_t stream);
 
+/* ============================================================ drafter forward
+ * The dense bf16 matrices of HE4.forward (w1a1_eagle/model.py:369-396): the
+ * attention projections FrozenLinear q/k/v/o (model.py:105-113, 207-219),
+ * the context fusion fc (model.py:382-386) and the tied vocabulary head
+ * (model.py:396), as y = W x for tokens <= 32.
+ * W16: weights re-tiled once (bd_tile_w16 from fp32 or bf16 row-major).
+ * X16: activations as bf16 hi/lo fragment planes (bd_pack_x16, optionally
+ * rms-normalised with weight, model.py:50-51; `normed` optionally receives the
+ * fp32 normalised rows).  bd_gemv_bf16 stores out[t * ld_out + o] (+ residual)
+ * and/or folds each row into argmax_keys[t] (largest value, lowest row index on
+ * ties; zero the keys before first use, bd_argmax_finish decodes them into token
+ * ids and re-zeroes them). */
+int64_t bd_w16_bytes(int64_t rows, int64_t cols);
+int bd_tile_w16(const void *w, int dtype_bits, int64_t rows, int64_t cols, void *out, bd_stream_t stream);
+int64_t bd_x16_bytes(int tokens, int64_t cols);
+int bd_pack_x16(const float *x, int tokens, int64_t cols, int64_t ldx, const float *rms_weight, float epsilon,
+                void *out, float *normed, int64_t ld_normed, int32_t *flags, bd_stream_t stream);
+int bd_gemv_bf16(const void *w16, int64_t rows, int64_t cols, const void *x16, int tokens, float *out,
+                 int64_t ld_out, const float *residual, unsigned long long *argmax_keys, int32_t *flags,
+                 bd_stream_t stream);
+int bd_argmax_finish(unsigned long long *keys, int n, int32_t *out, bd_stream_t stream);
+
+/* Embedding rows (HE4.forward's functional.embedding, model.py:380-381) from a
+ * bf16 [vocab, hidden] table; ids outside the vocabulary set BD_FLAG_BAD_TOKEN. */
+int bd_embed_rows(const uint16_t *table, int64_t vocab, int64_t hidden, const int32_t *ids, int n,
+                  float *out, int32_t *flags, bd_stream_t stream);
+/* rms(x, weight, eps) rows (model.py:50-51). */
+int bd_rms_rows(const float *x, int n, int64_t cols, int64_t ldx, const float *weight, float epsilon,
+                float *out, int64_t ldo, bd_stream_t stream);
+/* Per-head post-processing of projected q/k/v rows: optional rms over each head
+ * with norm_weight (Layer.context / Layer.forward, model.py:197-211), optional
+ * rotary embedding at positions pos0 + row (model.py:54-63), fp16 storage with
+ * the cache_storage overflow check (model.py:98-102, BD_FLAG_CACHE_OVERFLOW). */
+int bd_heads_post(const float *src, int n, int64_t ld_src, int64_t col0, int heads, int head_dim,
+                  const float *norm_weight, float epsilon, int rope, float theta, int64_t pos0,
+                  uint16_t *dst_f16, int64_t dst_ld, int32_t *flags, bd_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
