@@ -182,10 +182,12 @@ class DraftEngine:
         encoded = torch.empty_like(fused)
         _lib.call("bd_rms_rows", _p(fused), anchor, cfg.hidden, cfg.hidden, _p(self.enc_norm), float(cfg.epsilon),
                   _p(encoded), cfg.hidden, self._stream())
-        enc16 = encoded.to(torch.bfloat16)
+        # encoded rows as bf16 hi + lo (the same ~16-bit split the GEMV path uses)
+        enc_hi = encoded.to(torch.bfloat16)
+        enc_lo = (encoded - enc_hi.float()).to(torch.bfloat16)
         kvd = cfg.kv_heads * cfg.head_dim
         for i, layer in enumerate(self.layers):
-            kv = (enc16 @ self.kv_bf16[i].T).float().contiguous()
+            kv = ((enc_hi @ self.kv_bf16[i].T).float() + (enc_lo @ self.kv_bf16[i].T).float()).contiguous()
             self._heads(kv, anchor, 0, cfg.kv_heads, layer.k_norm, True, 0, self._cache_ptr(self.k_cache, i, 0), kvd)
             self._heads(kv, anchor, kvd, cfg.kv_heads, None, False, 0, self._cache_ptr(self.v_cache, i, 0), kvd)
 

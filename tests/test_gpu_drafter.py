@@ -1,0 +1,163 @@
+"""The drafter forward on the GPU against the CPU oracle (needs a B200)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import package, submodule
+from oracle import acceptance, drafter as od
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda:0")
+
+
+def rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def bf16(x):
+    return torch.as_tensor(x).to(torch.bfloat16).float()
+
+
+@pytest.mark.parametrize("rows,cols,tokens", [(1000, 300, 5), (9496 * 2, 2560, 16), (48, 16, 32), (17, 33, 9)])
+def test_gemv_store_and_argmax(rows, cols, tokens):
+    lib = package()._lib
+    g = torch.Generator().manual_seed(rows + cols)
+    w = bf16(torch.randn(rows, cols, generator=g) * 0.05)
+    x = torch.randn(tokens, cols, generator=g)
+    if rows >= 48:
+        w[7] = w[3]  # duplicated rows tie exactly: the lower index must win
+    drafter = submodule("drafter")
+    w16 = drafter._w16(w.to(DEV))
+    x16 = torch.zeros(int(lib.load().bd_x16_bytes(tokens, cols)), dtype=torch.uint8, device=DEV)
+    xd = x.to(DEV)
+    flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+    stream = torch.cuda.current_stream().cuda_stream
+    lib.call("bd_pack_x16", xd.data_ptr(), tokens, cols, cols, None, 1e-6, x16.data_ptr(), None, 0, flags.data_ptr(), stream)
+    out = torch.zeros(tokens, rows, device=DEV)
+    keys = torch.zeros(tokens, dtype=torch.int64, device=DEV)
+    lib.call("bd_gemv_bf16", w16.data_ptr(), rows, cols, x16.data_ptr(), tokens, out.data_ptr(), rows, None,
+             keys.data_ptr(), flags.data_ptr(), stream)
+    ids = torch.zeros(tokens, dtype=torch.int32, device=DEV)
+    lib.call("bd_argmax_finish", keys.data_ptr(), tokens, ids.data_ptr(), stream)
+    want = (x.double() @ w.double().T).numpy()
+    got = out.cpu().numpy()
+    assert rel(got, want) < 2e-5
+    # the argmax is exact on the device's own values (lowest index on ties)
+    assert np.array_equal(ids.cpu().numpy(), acceptance.argmax_rows(got))
+    assert int(flags.item()) == 0
+    assert not keys.any()
+
+
+def test_heads_post_rope_and_cache_overflow():
+    lib = package()._lib
+    n, heads, d = 5, 3, 64
+    g = torch.Generator().manual_seed(3)
+    src = torch.randn(n, heads * d, generator=g)
+    nw = 1 + 0.1 * torch.randn(d, generator=g)
+    dst = torch.zeros(n, heads * d, dtype=torch.float16, device=DEV)
+    flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+    srcd = src.to(DEV)
+    lib.call("bd_heads_post", srcd.data_ptr(), n, heads * d, 0, heads, d, nw.to(DEV).data_ptr(), 1e-6, 1, 1e6, 7,
+             dst.data_ptr(), heads * d, flags.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    v = src.numpy().reshape(n, heads, d)
+    want = od.rope(od.rms(v, nw.numpy(), 1e-6), np.arange(7, 7 + n), 1e6).astype(np.float16)
+    got = dst.cpu().numpy().reshape(n, heads, d)
+    np.testing.assert_allclose(got.astype(np.float32), want.astype(np.float32), rtol=2e-3, atol=2e-3)
+    assert int(flags.item()) == 0
+    big = torch.full((1, d), 70000.0, device=DEV)
+    lib.call("bd_heads_post", big.data_ptr(), 1, d, 0, 1, d, None, 1e-6, 0, 1e6, 0, dst.data_ptr(), d,
+             flags.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert int(flags.item()) & 64
+
+
+def small_model(seed=0, window=24, layers=3):
+    g = torch.Generator().manual_seed(seed)
+    cfg = dict(hidden=256, intermediate=512, heads=4, kv_heads=2, head_dim=64, layers=layers, slots=16, taps=2,
+               window=window, epsilon=1e-6, theta=1e6)
+    H, F, d = 256, 512, 64
+
+    def w(*shape, s=0.05):
+        return bf16(torch.randn(shape, generator=g) * s)
+
+    tensors = {"fc.weight": w(H, 2 * H), "enc.output_norm.weight": 1 + 0.1 * torch.randn(H, generator=g),
+               "output_norm.weight": 1 + 0.1 * torch.randn(H, generator=g)}
+    quant = {}
+    for i in range(layers):
+        p = f"blk.{i}."
+        tensors.update({
+            p + "attn_norm.weight": 1 + 0.1 * torch.randn(H, generator=g), p + "attn_q_norm.weight": torch.ones(d),
+            p + "attn_k_norm.weight": 1 + 0.1 * torch.randn(d, generator=g),
+            p + "ffn_norm.weight": 1 + 0.1 * torch.randn(H, generator=g),
+            p + "attn_q.weight": w(4 * d, H), p + "attn_k.weight": w(2 * d, H), p + "attn_v.weight": w(2 * d, H),
+            p + "attn_output.weight": w(H, 4 * d), p + "ffn_gate.weight": w(F, H), p + "ffn_up.weight": w(F, H),
+            p + "ffn_down.weight": w(H, F),
+        })
+        for name in ("ffn_gate", "ffn_up", "ffn_down"):
+            rows = tensors[p + name + ".weight"].shape[0]
+            quant[p + name + ".scale"] = tensors[p + name + ".weight"].abs().mean(-1) * (1 + 0.05 * torch.randn(rows, generator=g))
+            quant[p + name + ".midpoint"] = 0.01 * torch.randn(rows, generator=g)
+        quant[p + "ffn_gate_up.gain"] = torch.exp(0.2 * torch.randn(H, generator=g))
+        quant[p + "ffn_gate_up.bound"] = torch.tensor([1.7])
+        quant[p + "ffn_down.gain"] = torch.exp(0.2 * torch.randn(F, generator=g))
+        quant[p + "ffn_down.bound"] = torch.tensor([0.02])
+    vocab = w(1000, H, s=1.0)
+    features = torch.randn(64, 2 * H, generator=g).to(torch.bfloat16)
+    return cfg, tensors, quant, vocab, features
+
+
+def oracle_logits(cfg, tensors, quant, vocab, features, anchor, size):
+    t = {k: v.numpy().astype(np.float32) for k, v in tensors.items()}
+    for k, v in quant.items():
+        arr = v.numpy().astype(np.float32)
+        t[k] = np.float32(arr[0]) if k.endswith("bound") else arr
+    geo = od.Geometry(**cfg)
+    tokens = tuple(range(features.shape[0]))
+    return od.he4_forward(t, vocab.numpy(), 999, features.float().numpy(), tokens, anchor, geo, slots=size)
+
+
+@pytest.mark.parametrize("anchor,size,ingest", [(40, 16, 0), (40, 16, 8), (12, 16, 0), (40, 3, 5)])
+def test_engine_matches_oracle(anchor, size, ingest):
+    drafter = submodule("drafter")
+    model = submodule("model")
+    cfg, tensors, quant, vocab, features = small_model()
+    engine = drafter.DraftEngine(tensors, vocab, 999, model.Geometry(**cfg), quant, device=DEV, max_positions=128)
+    feats = features.to(DEV)
+    engine.prefill(feats, anchor - ingest)
+    if ingest:
+        engine.ingest(feats[anchor - ingest:anchor], anchor - ingest)
+    engine.set_tokens(anchor, size)  # token ids are positions in this test
+    logits = torch.zeros(size, 1000, device=DEV)
+    drafted = engine.draft(anchor, size, logits=logits)
+    torch.cuda.synchronize()
+    engine.check()
+    want = oracle_logits(cfg, tensors, quant, vocab, features, anchor, size)
+    got = logits.cpu().numpy()
+    assert rel(got, want) < 1e-2, rel(got, want)
+    agree = np.mean(np.argmax(got, -1) == np.argmax(want, -1))
+    assert agree >= 0.9, agree
+    assert np.array_equal(drafted.cpu().numpy(), acceptance.argmax_rows(got))
+
+
+def test_round_graph_replays_match_direct_calls():
+    drafter = submodule("drafter")
+    model = submodule("model")
+    cfg, tensors, quant, vocab, features = small_model(seed=1)
+    engine = drafter.DraftEngine(tensors, vocab, 999, model.Geometry(**cfg), quant, device=DEV, max_positions=128)
+    feats = features.to(DEV)
+    engine.prefill(feats, 32)
+    rnd = drafter.DraftRound(engine, 40, 16, 8)
+    rnd.host_rows.copy_(features[32:40])
+    out1 = rnd(40).clone()
+    out2 = rnd(40).clone()
+    assert torch.equal(out1, out2)
+    engine.prefill(feats, 32)
+    engine.ingest(feats[32:40], 32)
+    engine.set_tokens(40, 16)
+    direct = engine.draft(40, 16).cpu()
+    assert torch.equal(direct[1:], out1)
