@@ -44,7 +44,7 @@ class FfnHe4Args(ctypes.Structure):
         ("signs_gate_up", P), ("scale_gate", P), ("midpoint_gate", P), ("scale_up", P), ("midpoint_up", P),
         ("gain_gate_up", P), ("bound_gate_up", P), ("signs_down", P), ("scale_down", P), ("midpoint_down", P),
         ("gain_down", P), ("bound_down", P), ("hidden_out", P), ("workspace", P), ("workspace_bytes", c_size_t),
-        ("flags", P),
+        ("flags", P), ("norm_weight", P), ("epsilon", ctypes.c_float),
     ]
 
 
@@ -85,6 +85,11 @@ SIGNATURES = {
     "bd_rms_rows": (c_int, [P, c_int, c_int64, c_int64, P, ctypes.c_float, P, c_int64, P]),
     "bd_heads_post": (c_int, [P, c_int, c_int64, c_int64, c_int, c_int, P, ctypes.c_float, c_int,
                               ctypes.c_float, c_int64, P, c_int64, P, P]),
+    "bd_qkv_post": (c_int, [P, c_int, c_int64, c_int, c_int, c_int, P, P, ctypes.c_float, ctypes.c_float, c_int64,
+                            P, c_int64, P, P, c_int64, P, P]),
+    "bd_attention_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
+    "bd_attention_decode": (c_int, [P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int64, c_int64, P, P,
+                                    c_size_t, P]),
 }
 
 _lib = None
@@ -115,7 +120,7 @@ def load() -> ctypes.CDLL:
 
 
 # Kernel launches issued by each entry point (for launch accounting).
-KERNELS_PER_CALL = {"bd_ffn_he4": 3, "bd_ffn_w1": 4}
+KERNELS_PER_CALL = {"bd_ffn_he4": 3, "bd_ffn_w1": 4, "bd_attention_decode": 2}
 launches = 0
 
 

@@ -158,7 +158,8 @@ extern "C" int bd_ffn_he4(const bd_ffn_he4_args *p, bd_stream_t stream) {
     // The quantizer writes per-slice partial code sums of the gate/up input and
     // zeroes the down projection's code sums, which gate/up accumulate.
     int st = launch_quantize_codes(p->x, p->tokens, p->hidden, ld_h, p->gain_gate_up, p->bound_gate_up, 4,
-                                   w.codes_in, w.sum_in, true, p->flags, w.sum_mid, kMaxTokens, stream);
+                                   w.codes_in, w.sum_in, true, p->flags, w.sum_mid, kMaxTokens, stream,
+                                   p->norm_weight, p->epsilon);
     if (st) return st;
 
     ProjArgs gu{};

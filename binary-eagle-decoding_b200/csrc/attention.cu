@@ -1,0 +1,266 @@
+// Block-draft attention over the fp16 K/V cache (Layer.forward, w1a1_eagle/model.py:212-218):
+// softmax(q k^T / sqrt(d), masked to |pos_q - pos_k| < window on windowed layers) v
+// for up to 16 query slots per q head, grouped-query (q head h uses kv head
+// h / (heads / kv_heads)).
+//
+// Split over keys (flash decoding): CTA (kv head, chunk of 128 keys) stages its
+// K and V rows in shared memory with cp.async; warp w owns q head
+// kv * groups + w and its 16 query rows.  S = Q K^T and O = P V run on
+// m16n8k16 fp16 MMAs with fp32 accumulation (K fragments by ldmatrix, V by
+// ldmatrix.trans, P re-packed from the S accumulators).  Each CTA writes its
+// chunk's row maxima, row sums and un-normalised O; a combine kernel merges the
+// chunks.  No waits between CTAs: partials meet only in the combine launch.
+#include "kernels.cuh"
+
+#include <cuda_fp16.h>
+
+namespace bd {
+
+constexpr int kKeys = 128;  // keys per chunk
+// Padded fp16 row of a staged K/V row in shared memory (conflict-free ldmatrix).
+template <int D>
+constexpr int row_bytes() { return D * 2 + 16; }
+
+struct AttnArgs {
+    const __half *q;        // [tokens][heads][d]
+    const __half *k, *v;    // [positions][kv_heads][d] (cache rows 0 .. keys-1)
+    int tokens, heads, kv_heads, keys;
+    int windowed;           // apply |pos_q - pos_k| < window
+    int64_t anchor;         // position of query row 0
+    int64_t window;
+    float scale;            // 1 / sqrt(d)
+    int chunks;
+    float *part_o;          // [chunks][heads][16][d]
+    float *part_ml;         // [chunks][heads][16][2]
+    float *out;             // [tokens][heads * d]
+};
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void *p) {
+    const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(a));
+}
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void *p) {
+    const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(a));
+}
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+template <int kDim>
+__global__ void __launch_bounds__(128) attn_chunk_kernel(const AttnArgs a) {
+    constexpr int kRowBytes = row_bytes<kDim>();
+    extern __shared__ __align__(16) char sm[];
+    char *ks = sm;
+    char *vs = sm + kKeys * kRowBytes;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int kvh = blockIdx.x, chunk = blockIdx.y;
+    const int groups = a.heads / a.kv_heads;
+    const int key0 = chunk * kKeys;
+    const int nkeys = min(kKeys, a.keys - key0);
+    grid_wait();
+    grid_launch_dependents();
+    // stage K and V rows of this chunk (rows past the end are zero)
+    for (int i = threadIdx.x; i < kKeys * (kDim / 8); i += blockDim.x) {
+        const int r = i / (kDim / 8), c = i % (kDim / 8);
+        const bool live = r < nkeys;
+        const int64_t src = (static_cast<int64_t>(key0 + (live ? r : 0)) * a.kv_heads + kvh) * kDim + c * 8;
+        cp_async16(ks + r * kRowBytes + c * 16, a.k + src, live ? 16 : 0);
+        cp_async16(vs + r * kRowBytes + c * 16, a.v + src, live ? 16 : 0);
+    }
+    // Q fragments of this warp's head: rows are query slots (A operand, row-major 16 x 128)
+    const int head = kvh * groups + warp;
+    const bool head_live = warp < groups;
+    uint32_t qa[kDim / 16][4];
+#pragma unroll
+    for (int s = 0; s < kDim / 16; ++s) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int row = g + 8 * (j & 1);
+            const int col = s * 16 + 2 * t + 8 * (j >> 1);
+            qa[s][j] = (head_live && row < a.tokens)
+                           ? *reinterpret_cast<const uint32_t *>(a.q + (static_cast<int64_t>(row) * a.heads + head) * kDim + col)
+                           : 0u;
+        }
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    if (!head_live) return;
+
+    // S = Q K^T over the chunk: 16 n-tiles of 8 keys
+    float s_acc[kKeys / 8][4];
+#pragma unroll
+    for (int n = 0; n < kKeys / 8; ++n)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) s_acc[n][i] = 0.0f;
+#pragma unroll
+    for (int n = 0; n < kKeys / 8; ++n) {
+#pragma unroll
+        for (int s2 = 0; s2 < kDim / 32; ++s2) {
+            // x4: matrices (d 0-7, 8-15) of k-step 2*s2 and (d 0-7, 8-15) of k-step 2*s2+1 for keys 8n..8n+7
+            uint32_t b[4];
+            const int mi = lane >> 3, r = lane & 7;
+            ldmatrix_x4(b, ks + (n * 8 + r) * kRowBytes + (s2 * 32 + mi * 8) * 2);
+            mma_f16_16816(s_acc[n], qa[2 * s2][0], qa[2 * s2][1], qa[2 * s2][2], qa[2 * s2][3], b[0], b[1]);
+            mma_f16_16816(s_acc[n], qa[2 * s2 + 1][0], qa[2 * s2 + 1][1], qa[2 * s2 + 1][2], qa[2 * s2 + 1][3], b[2],
+                          b[3]);
+        }
+    }
+    // scale, mask, row maxima (rows g and g + 8 of this lane)
+    float m[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int n = 0; n < kKeys / 8; ++n)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int row = g + 8 * (i >> 1);
+            const int key = key0 + n * 8 + 2 * t + (i & 1);
+            bool ok = key < a.keys && row < a.tokens;
+            if (a.windowed) {
+                const int64_t dist = a.anchor + row - key;
+                ok = ok && (dist < a.window && -dist < a.window);
+            }
+            const float v = ok ? s_acc[n][i] * a.scale : -INFINITY;
+            s_acc[n][i] = v;
+            m[i >> 1] = fmaxf(m[i >> 1], v);
+        }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        m[r] = fmaxf(m[r], __shfl_xor_sync(0xffffffffu, m[r], 1));
+        m[r] = fmaxf(m[r], __shfl_xor_sync(0xffffffffu, m[r], 2));
+    }
+    float l[2] = {0.0f, 0.0f};
+#pragma unroll
+    for (int n = 0; n < kKeys / 8; ++n)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float mm = m[i >> 1];
+            const float p = mm == -INFINITY ? 0.0f : __expf(s_acc[n][i] - mm);
+            s_acc[n][i] = p;
+            l[i >> 1] += p;
+        }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        l[r] += __shfl_xor_sync(0xffffffffu, l[r], 1);
+        l[r] += __shfl_xor_sync(0xffffffffu, l[r], 2);
+    }
+    // O = P V: P (16 x 128 keys) re-packed from the S accumulators as A fragments
+    float o_acc[kDim / 8][4];
+#pragma unroll
+    for (int n = 0; n < kDim / 8; ++n)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o_acc[n][i] = 0.0f;
+#pragma unroll
+    for (int kk = 0; kk < kKeys / 16; ++kk) {
+        const uint32_t pa0 = pack_half2(s_acc[2 * kk][0], s_acc[2 * kk][1]);
+        const uint32_t pa1 = pack_half2(s_acc[2 * kk][2], s_acc[2 * kk][3]);
+        const uint32_t pa2 = pack_half2(s_acc[2 * kk + 1][0], s_acc[2 * kk + 1][1]);
+        const uint32_t pa3 = pack_half2(s_acc[2 * kk + 1][2], s_acc[2 * kk + 1][3]);
+#pragma unroll
+        for (int n2 = 0; n2 < kDim / 16; ++n2) {
+            // x4.trans: (keys 16kk..+7, d 16n2..+7), (keys +8..15, d 16n2..+7), (keys 16kk..+7, d +8..15), (keys +8..15, d +8..15)
+            uint32_t b[4];
+            const int mi = lane >> 3, r = lane & 7;
+            ldmatrix_x4_trans(b, vs + (kk * 16 + (mi & 1) * 8 + r) * kRowBytes + (n2 * 16 + (mi >> 1) * 8) * 2);
+            mma_f16_16816(o_acc[2 * n2], pa0, pa1, pa2, pa3, b[0], b[1]);
+            mma_f16_16816(o_acc[2 * n2 + 1], pa0, pa1, pa2, pa3, b[2], b[3]);
+        }
+    }
+    // partials: un-normalised O, row max and row sum of this chunk
+    float *po = a.part_o + ((static_cast<int64_t>(chunk) * a.heads + head) * 16) * kDim;
+#pragma unroll
+    for (int n = 0; n < kDim / 8; ++n) {
+        *reinterpret_cast<float2 *>(po + g * kDim + n * 8 + 2 * t) = make_float2(o_acc[n][0], o_acc[n][1]);
+        *reinterpret_cast<float2 *>(po + (g + 8) * kDim + n * 8 + 2 * t) = make_float2(o_acc[n][2], o_acc[n][3]);
+    }
+    if (t == 0) {
+        float *pml = a.part_ml + ((static_cast<int64_t>(chunk) * a.heads + head) * 16) * 2;
+        pml[g * 2] = m[0];
+        pml[g * 2 + 1] = l[0];
+        pml[(g + 8) * 2] = m[1];
+        pml[(g + 8) * 2 + 1] = l[1];
+    }
+}
+
+// out[token][head * d + j] = sum_c e^{m_c - M} O_c / sum_c e^{m_c - M} l_c.  Grid (tokens, heads), d threads.
+template <int kDim>
+__global__ void attn_combine_kernel(const AttnArgs a) {
+    grid_wait();
+    grid_launch_dependents();
+    const int token = blockIdx.x, head = blockIdx.y, j = threadIdx.x;
+    float M = -INFINITY;
+    for (int c = 0; c < a.chunks; ++c)
+        M = fmaxf(M, a.part_ml[((static_cast<int64_t>(c) * a.heads + head) * 16 + token) * 2]);
+    float num = 0.0f, den = 0.0f;
+    for (int c = 0; c < a.chunks; ++c) {
+        const int64_t base = (static_cast<int64_t>(c) * a.heads + head) * 16 + token;
+        const float mc = a.part_ml[base * 2];
+        if (mc == -INFINITY) continue;
+        const float w = __expf(mc - M);
+        den += w * a.part_ml[base * 2 + 1];
+        num += w * a.part_o[base * kDim + j];
+    }
+    a.out[static_cast<int64_t>(token) * a.heads * kDim + head * kDim + j] = num / den;
+}
+
+}  // namespace bd
+
+using namespace bd;
+
+extern "C" size_t bd_attention_workspace_bytes(int heads, int head_dim, int keys) {
+    const int chunks = (keys + kKeys - 1) / kKeys;
+    return static_cast<size_t>(chunks) * heads * 16 * (head_dim + 2) * sizeof(float) + 256;
+}
+
+template <int D>
+static int launch_attention(const AttnArgs &a, int kv_heads, int tokens, int heads, cudaStream_t stream) {
+    const size_t smem = 2 * kKeys * row_bytes<D>();
+    if (cudaFuncSetAttribute(attn_chunk_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+        return BD_ERR_LAUNCH;
+    int st = launch_pdl(attn_chunk_kernel<D>, dim3(kv_heads, a.chunks), dim3(128), smem, stream, a);
+    if (st) return st;
+    return launch_pdl(attn_combine_kernel<D>, dim3(tokens, heads), dim3(D), 0, stream, a);
+}
+
+extern "C" int bd_attention_decode(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache, int tokens,
+                                   int heads, int kv_heads, int head_dim, int keys, int windowed, int64_t anchor,
+                                   int64_t window, float *out, void *workspace, size_t workspace_bytes,
+                                   bd_stream_t stream) {
+    if (tokens < 1 || tokens > 16 || (head_dim != 64 && head_dim != 128) || heads < 1 || kv_heads < 1 ||
+        heads % kv_heads ||
+        heads / kv_heads > 4 || keys < 1 || !q || !k_cache || !v_cache || !out)
+        return BD_ERR_INVALID;
+    if (!workspace || workspace_bytes < bd_attention_workspace_bytes(heads, head_dim, keys)) return BD_ERR_WORKSPACE;
+    AttnArgs a{};
+    a.q = reinterpret_cast<const __half *>(q);
+    a.k = reinterpret_cast<const __half *>(k_cache);
+    a.v = reinterpret_cast<const __half *>(v_cache);
+    a.tokens = tokens;
+    a.heads = heads;
+    a.kv_heads = kv_heads;
+    a.keys = keys;
+    a.windowed = windowed;
+    a.anchor = anchor;
+    a.window = window;
+    a.scale = 1.0f / sqrtf(static_cast<float>(head_dim));
+    a.chunks = (keys + kKeys - 1) / kKeys;
+    a.part_ml = static_cast<float *>(workspace);
+    a.part_o = a.part_ml + static_cast<size_t>(a.chunks) * heads * 16 * 2;
+    a.out = out;
+    return head_dim == 64 ? launch_attention<64>(a, kv_heads, tokens, heads, stream)
+                          : launch_attention<128>(a, kv_heads, tokens, heads, stream);
+}

@@ -90,9 +90,66 @@ __global__ void heads_post_kernel(const float *__restrict__ src, int64_t ld_src,
     out[j + half] = hb;
 }
 
+// q, k and v of a projected row block in one launch: grid (rows, heads + 2 kv_heads);
+// q heads get q_norm + rope -> q (row stride q_ld), k heads k_norm + rope -> the
+// K cache row pos0 + r, v heads are stored as they are in the V cache.
+__global__ void qkv_post_kernel(const float *__restrict__ src, int64_t ld_src, int heads, int kv_heads, int d,
+                                const float *__restrict__ q_norm, const float *__restrict__ k_norm, float eps,
+                                float theta, int64_t pos0, __half *__restrict__ q, int64_t q_ld,
+                                __half *__restrict__ kc, __half *__restrict__ vc, int64_t kv_ld, int32_t *flags) {
+    __shared__ float part[32];
+    grid_wait();
+    grid_launch_dependents();
+    const int r = blockIdx.x, y = blockIdx.y, j = threadIdx.x, half = d >> 1;
+    const bool live = j < half;
+    const float *v = src + r * ld_src + static_cast<int64_t>(y) * d;
+    const float *nw = y < heads ? q_norm : (y < heads + kv_heads ? k_norm : nullptr);
+    const bool rope = y < heads + kv_heads;
+    __half *out = y < heads ? q + r * q_ld + y * d
+                            : (y < heads + kv_heads ? kc + r * kv_ld + (y - heads) * d
+                                                    : vc + r * kv_ld + (y - heads - kv_heads) * d);
+    float a = live ? v[j] : 0.0f, b = live ? v[j + half] : 0.0f;
+    if (nw) {
+        const float scale = rsqrtf(block_sum(fmaf(a, a, b * b), part) / static_cast<float>(d) + eps);
+        if (live) {
+            a = a * scale * nw[j];
+            b = b * scale * nw[j + half];
+        }
+    }
+    if (!live) return;
+    if (rope) {
+        const float freq = powf(theta, -static_cast<float>(2 * j) / static_cast<float>(d));
+        const float angle = static_cast<float>(pos0 + r) * freq;
+        float s, c;
+        sincosf(angle, &s, &c);
+        const float na = a * c + (-b) * s;
+        const float nb = b * c + a * s;
+        a = na;
+        b = nb;
+    }
+    const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+    if (!isfinite(__half2float(ha)) || !isfinite(__half2float(hb))) set_flag(flags, BD_FLAG_CACHE_OVERFLOW);
+    out[j] = ha;
+    out[j + half] = hb;
+}
+
 }  // namespace bd
 
 using namespace bd;
+
+extern "C" int bd_qkv_post(const float *src, int n, int64_t ld_src, int heads, int kv_heads, int head_dim,
+                           const float *q_norm, const float *k_norm, float epsilon, float theta, int64_t pos0,
+                           uint16_t *q_f16, int64_t q_ld, uint16_t *k_cache_f16, uint16_t *v_cache_f16, int64_t kv_ld,
+                           int32_t *flags, bd_stream_t stream) {
+    if (n < 1 || heads < 1 || kv_heads < 1 || head_dim < 2 || (head_dim & 1) || head_dim > 2048 || !src || !q_f16 ||
+        !k_cache_f16 || !v_cache_f16 || !q_norm || !k_norm)
+        return BD_ERR_INVALID;
+    const unsigned threads = static_cast<unsigned>((head_dim / 2 + 31) / 32 * 32);
+    return launch_pdl(qkv_post_kernel, dim3(n, heads + 2 * kv_heads), dim3(threads), 0, stream, src, ld_src, heads,
+                      kv_heads, head_dim, q_norm, k_norm, epsilon, theta, pos0, reinterpret_cast<__half *>(q_f16),
+                      q_ld, reinterpret_cast<__half *>(k_cache_f16), reinterpret_cast<__half *>(v_cache_f16), kv_ld,
+                      flags);
+}
 
 extern "C" int bd_embed_rows(const uint16_t *table, int64_t vocab, int64_t hidden, const int32_t *ids, int n,
                              float *out, int32_t *flags, bd_stream_t stream) {

@@ -170,53 +170,73 @@ __global__ void tile_w16_kernel(const T *__restrict__ w, int64_t rows, int64_t c
     }
 }
 
+// Row scale rsqrt(mean(x^2) + eps) of rms (model.py:50-51), by one 256-thread CTA.
+__device__ __forceinline__ float rms_scale(const float *row, int64_t cols, float eps, float *part) {
+    float ss = 0.0f;
+    for (int64_t k = threadIdx.x; k < cols; k += blockDim.x) ss = fmaf(row[k], row[k], ss);
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, d);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float total = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) total += part[w];
+    return rsqrtf(total / static_cast<float>(cols) + eps);
+}
+
+// Pack the 4 columns k0 .. k0 + 3 of one token row into both X16 planes.
+__device__ __forceinline__ void pack_four(const float *row, int64_t k0, int64_t cols, float scale,
+                                          const float *weight, float *normed_row, int token, int64_t nkt,
+                                          int64_t ntb, uint32_t *out, bool &bad) {
+    float y[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int64_t k = k0 + j;
+        y[j] = 0.0f;
+        if (k < cols) {
+            y[j] = row[k];
+            if (weight) y[j] = y[j] * scale * weight[k];
+            bad |= !isfinite(y[j]);
+            if (normed_row) normed_row[k] = y[j];
+        }
+    }
+    const int nt = token >> 3, g = token & 7;
+    const int64_t kt = k0 >> 4;
+    const int kk = static_cast<int>(k0 & 15);  // multiple of 4: pairs (kk, kk+1), (kk+2, kk+3)
+    const int half = kk >> 3;
+#pragma unroll
+    for (int pr = 0; pr < 2; ++pr) {
+        const int t = ((kk & 7) >> 1) + pr;
+        const __nv_bfloat16 h0 = __float2bfloat16_rn(y[2 * pr]), h1 = __float2bfloat16_rn(y[2 * pr + 1]);
+        const __nv_bfloat16 l0 = __float2bfloat16_rn(y[2 * pr] - __bfloat162float(h0));
+        const __nv_bfloat16 l1 = __float2bfloat16_rn(y[2 * pr + 1] - __bfloat162float(h1));
+        const int64_t off = ((nt * nkt + kt) * 32 + g * 4 + t) * 2 + half;  // in 32-bit words
+        out[off] = __bfloat16_as_ushort(h0) | (static_cast<uint32_t>(__bfloat16_as_ushort(h1)) << 16);
+        out[ntb * nkt * 32 * 2 + off] =
+            __bfloat16_as_ushort(l0) | (static_cast<uint32_t>(__bfloat16_as_ushort(l1)) << 16);
+    }
+}
+
 // X16 activation fragments (hi/lo bf16 planes) of rows of x, optionally
 // rms-normalised first: y = x * rsqrt(mean(x^2) + eps) * weight (model.py:50-51).
-// One CTA per token; columns >= cols are written as zeros.
+// Grid (tokens, column slices of 1024): each thread packs 4 consecutive columns
+// (two bf16 pairs per plane); columns >= cols are written as zeros.  With a
+// weight every CTA recomputes its row's rms scale (the row is L2-resident).
 __global__ void __launch_bounds__(256) pack_x16_kernel(const float *__restrict__ x, int64_t cols, int64_t ldx,
                                                        int64_t nkt, int64_t ntb, const float *__restrict__ weight,
-                                                       float eps, uint16_t *__restrict__ out, float *normed,
+                                                       float eps, uint32_t *__restrict__ out, float *normed,
                                                        int64_t ld_normed, int32_t *flags) {
     __shared__ float part[8];
     grid_wait();
     grid_launch_dependents();
     const int token = blockIdx.x;
     const float *row = x + token * ldx;
-    float scale = 1.0f;
+    const float scale = weight ? rms_scale(row, cols, eps, part) : 1.0f;
+    const int64_t k0 = static_cast<int64_t>(blockIdx.y) * 1024 + 4 * threadIdx.x;
     bool bad = false;
-    if (weight) {
-        float ss = 0.0f;
-        for (int64_t k = threadIdx.x; k < cols; k += blockDim.x) {
-            const float v = row[k];
-            ss = fmaf(v, v, ss);
-        }
-#pragma unroll
-        for (int d = 16; d > 0; d >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, d);
-        if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
-        __syncthreads();
-        float total = 0.0f;
-#pragma unroll
-        for (int w = 0; w < 8; ++w) total += part[w];
-        scale = rsqrtf(total / static_cast<float>(cols) + eps);
-    }
-    const int nt = token >> 3, g = token & 7;
-    for (int64_t k = threadIdx.x; k < nkt * 16; k += blockDim.x) {
-        float y = 0.0f;
-        if (k < cols) {
-            y = row[k];
-            if (weight) y = y * scale * weight[k];
-            bad |= !isfinite(y);
-            if (normed) normed[token * ld_normed + k] = y;
-        }
-        const __nv_bfloat16 hi = __float2bfloat16_rn(y);
-        const __nv_bfloat16 lo = __float2bfloat16_rn(y - __bfloat162float(hi));
-        const int64_t kt = k >> 4;
-        const int kk = static_cast<int>(k & 15);
-        const int t = (kk & 7) >> 1, half = kk >> 3, e = kk & 1;
-        const int64_t off = (((nt * nkt + kt) * 32 + g * 4 + t) << 2) + half * 2 + e;  // in bf16 units
-        out[off] = __bfloat16_as_ushort(hi);
-        out[ntb * nkt * 32 * 4 + off] = __bfloat16_as_ushort(lo);
-    }
+    if (k0 < nkt * 16)
+        pack_four(row, k0, cols, scale, weight, normed ? normed + token * ld_normed : nullptr, token, nkt, ntb, out,
+                  bad);
     if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) set_flag(flags, BD_FLAG_NONFINITE_STATE);
 }
 
@@ -291,8 +311,9 @@ extern "C" int bd_pack_x16(const float *x, int tokens, int64_t cols, int64_t ldx
                            float epsilon, void *out, float *normed, int64_t ld_normed, int32_t *flags,
                            bd_stream_t stream) {
     if (tokens < 1 || tokens > 32 || cols < 1 || ldx < cols || !x || !out) return BD_ERR_INVALID;
-    return launch_pdl(pack_x16_kernel, dim3(tokens), dim3(256), 0, stream, x, cols, ldx, nkt_of(cols),
-                      static_cast<int64_t>((tokens + 7) / 8), rms_weight, epsilon, static_cast<uint16_t *>(out),
+    const unsigned slices = static_cast<unsigned>((nkt_of(cols) * 16 + 1023) / 1024);
+    return launch_pdl(pack_x16_kernel, dim3(tokens, slices), dim3(256), 0, stream, x, cols, ldx, nkt_of(cols),
+                      static_cast<int64_t>((tokens + 7) / 8), rms_weight, epsilon, static_cast<uint32_t *>(out),
                       normed, ld_normed, flags);
 }
 

@@ -29,7 +29,8 @@ inline int quant_parts(int64_t cols) { return static_cast<int>((cols + 1023) / 1
 
 int launch_quantize_codes(const float *x, int64_t rows, int64_t cols, int64_t ld, const float *gain,
                           const float *bound, int bits, int8_t *codes, int32_t *sums, bool partial, int32_t *flags,
-                          int32_t *zero_sums, int zero_count, cudaStream_t stream);
+                          int32_t *zero_sums, int zero_count, cudaStream_t stream, const float *norm_w = nullptr,
+                          float eps = 0.0f);
 int launch_quantize_planes(const float *x, int64_t rows, int64_t cols, int64_t ld, int8_t *hi, int8_t *lo,
                            int32_t *sums_hi, int32_t *sums_lo, float *row_scale, int32_t *flags,
                            cudaStream_t stream);

@@ -31,11 +31,27 @@ __global__ void __launch_bounds__(256) quantize_codes_kernel(const float *__rest
                                                              const float *__restrict__ bound_ptr, int bits,
                                                              int8_t *__restrict__ codes, int32_t *__restrict__ sums,
                                                              bool partial, int32_t *flags, int32_t *zero_sums,
-                                                             int zero_count) {
+                                                             int zero_count, const float *__restrict__ norm_w,
+                                                             float eps) {
     __shared__ int scratch[8];
+    __shared__ float fpart[8];
     grid_wait();
     grid_launch_dependents();
     const int row = blockIdx.x;
+    // optional rms(x, norm_w, eps) of the whole row first (model.py:50-51, 220)
+    float scale = 1.0f;
+    if (norm_w) {
+        float ss = 0.0f;
+        for (int64_t k = threadIdx.x; k < cols; k += blockDim.x) ss = fmaf(x[row * cols + k], x[row * cols + k], ss);
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, d);
+        if ((threadIdx.x & 31) == 0) fpart[threadIdx.x >> 5] = ss;
+        __syncthreads();
+        float total = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) total += fpart[w];
+        scale = rsqrtf(total / static_cast<float>(cols) + eps);
+    }
     if (row == 0 && blockIdx.y == 0 && zero_sums)
         for (int i = threadIdx.x; i < zero_count; i += blockDim.x) zero_sums[i] = 0;
     const float b = *bound_ptr;
@@ -51,6 +67,7 @@ __global__ void __launch_bounds__(256) quantize_codes_kernel(const float *__rest
         for (int j = 0; j < 4; ++j) {
             const bool live = k0 + j < cols;
             xv[j] = live ? x[row * cols + k0 + j] : 0.0f;
+            if (norm_w && live) xv[j] = xv[j] * scale * norm_w[k0 + j];
             gv[j] = live ? gain[k0 + j] : 0.0f;
         }
         int c[4];
@@ -189,13 +206,13 @@ __global__ void __launch_bounds__(256) binarize_kernel(const float *__restrict__
 
 int launch_quantize_codes(const float *x, int64_t rows, int64_t cols, int64_t ld, const float *gain,
                           const float *bound, int bits, int8_t *codes, int32_t *sums, bool partial, int32_t *flags,
-                          int32_t *zero_sums, int zero_count, cudaStream_t stream) {
+                          int32_t *zero_sums, int zero_count, cudaStream_t stream, const float *norm_w, float eps) {
     if (rows == 0) return BD_OK;
     if (sums && !partial && cudaMemsetAsync(sums, 0, rows * sizeof(int32_t), stream) != cudaSuccess)
         return BD_ERR_LAUNCH;
     const dim3 grid(static_cast<unsigned>(rows), static_cast<unsigned>(quant_parts(cols)));
     return launch_pdl(quantize_codes_kernel, grid, dim3(256), 0, stream, x, cols, ld, gain, bound, bits, codes, sums,
-                      partial, flags, zero_sums, zero_count);
+                      partial, flags, zero_sums, zero_count, norm_w, eps);
 }
 
 int launch_quantize_planes(const float *x, int64_t rows, int64_t cols, int64_t ld, int8_t *hi, int8_t *lo,

@@ -18,12 +18,10 @@ Device data (all on one GPU):
 
 from __future__ import annotations
 
-import math
 from dataclasses import dataclass
 
 import torch
 from torch import Tensor
-from torch.nn import functional
 
 from . import _lib, ops
 from .ops import Flags, PackedFFN, _p, _stream
@@ -133,8 +131,12 @@ class DraftEngine:
         self.encoded = torch.zeros((T, cfg.hidden), dtype=torch.float32, device=dev)
         self.fused = torch.zeros((T, cfg.hidden), dtype=torch.float32, device=dev)
         self.kv_out = torch.zeros((T, 2 * kvd), dtype=torch.float32, device=dev)
+        if cfg.head_dim not in (64, 128) or cfg.heads // cfg.kv_heads > 4 or cfg.slots > 16:
+            raise ValueError("attention kernel geometry: head_dim 64/128, at most 4 q heads per kv head, <= 16 slots")
+        self.attn_ws = torch.zeros(int(_lib.load().bd_attention_workspace_bytes(cfg.heads, cfg.head_dim,
+                                                                                 self.max_positions)),
+                                   dtype=torch.uint8, device=dev)
         self.flags = Flags(dev)
-        self._masks: dict[tuple[int, int, int], Tensor] = {}
         self.positions = 0
 
     # ------------------------------------------------------------------ helpers
@@ -212,17 +214,6 @@ class DraftEngine:
         self.positions = max(self.positions, pos0 + n)
 
     # ------------------------------------------------------------------ draft
-    def _mask(self, anchor: int, size: int, layer: int) -> Tensor | None:
-        cfg = self.cfg
-        if layer == cfg.layers - 1 or anchor + size <= cfg.window:
-            return None  # every key is inside the window
-        key = (anchor, size, layer)
-        if key not in self._masks:
-            pos = torch.arange(anchor, anchor + size, device=self.device)
-            keys = torch.arange(anchor + size, device=self.device)
-            self._masks[key] = (pos[:, None] - keys[None, :]).abs() < cfg.window
-        return self._masks[key]
-
     def set_tokens(self, first: int, size: int) -> None:
         ids = torch.full((size,), self.mask, dtype=torch.int32)
         ids[0] = first
@@ -244,26 +235,21 @@ class DraftEngine:
         st = self._stream()
         _lib.call("bd_embed_rows", _p(self.vocab16), self.vocab_size, H, _p(self.ids), k, _p(self.state),
                   self.flags.ptr, st)
-        scale = 1.0 / math.sqrt(cfg.head_dim)
         for i, layer in enumerate(self.layers):
             self._pack(self.state, k, H, H, layer.attn_norm)
             self._gemv(layer.qkv.data_ptr(), self.qkv_width, H, k, self.qkv_out, self.qkv_width)
-            self._heads(self.qkv_out, k, 0, cfg.heads, layer.q_norm, True, anchor, self.q16.data_ptr(), qd)
-            self._heads(self.qkv_out, k, qd, cfg.kv_heads, layer.k_norm, True, anchor,
-                        self._cache_ptr(self.k_cache, i, anchor), kvd)
-            self._heads(self.qkv_out, k, qd + kvd, cfg.kv_heads, None, False, anchor,
-                        self._cache_ptr(self.v_cache, i, anchor), kvd)
-            q = self.q16[:k].view(k, cfg.heads, cfg.head_dim).transpose(0, 1).unsqueeze(0)
-            kk = self.k_cache[i, :L].view(L, cfg.kv_heads, cfg.head_dim).transpose(0, 1).unsqueeze(0)
-            vv = self.v_cache[i, :L].view(L, cfg.kv_heads, cfg.head_dim).transpose(0, 1).unsqueeze(0)
-            out = functional.scaled_dot_product_attention(q, kk, vv, attn_mask=self._mask(anchor, k, i), scale=scale,
-                                                          enable_gqa=cfg.heads != cfg.kv_heads)
-            self.attn[:k].copy_(out[0].transpose(0, 1).reshape(k, qd))
+            _lib.call("bd_qkv_post", _p(self.qkv_out), k, self.qkv_width, cfg.heads, cfg.kv_heads, cfg.head_dim,
+                      _p(layer.q_norm), _p(layer.k_norm), float(cfg.epsilon), float(cfg.theta), anchor,
+                      _p(self.q16), qd, self._cache_ptr(self.k_cache, i, anchor),
+                      self._cache_ptr(self.v_cache, i, anchor), kvd, self.flags.ptr, st)
+            windowed = int(i < cfg.layers - 1)
+            _lib.call("bd_attention_decode", _p(self.q16), self._cache_ptr(self.k_cache, i, 0),
+                      self._cache_ptr(self.v_cache, i, 0), k, cfg.heads, cfg.kv_heads, cfg.head_dim, L, windowed,
+                      anchor, cfg.window, _p(self.attn), _p(self.attn_ws), self.attn_ws.numel(), st)
             self._pack(self.attn, k, qd, qd)
             self._gemv(layer.o.data_ptr(), H, qd, k, self.resid, H, residual=self.state)
-            _lib.call("bd_rms_rows", _p(self.resid), k, H, H, _p(layer.ffn_norm), float(cfg.epsilon), _p(self.normed),
-                      H, st)
-            ops.ffn_he4(self.normed[:k], layer.ffn, self.resid[:k], flags=self.flags, out=self.state[:k])
+            ops.ffn_he4(self.resid[:k], layer.ffn, self.resid[:k], flags=self.flags, out=self.state[:k],
+                        norm=layer.ffn_norm, epsilon=cfg.epsilon)
         self._pack(self.state, k, H, H, self.out_norm)
         self._gemv(self.head.data_ptr(), self.vocab_size, H, k, logits, self.vocab_size, keys=self.keys)
         _lib.call("bd_argmax_finish", _p(self.keys), k, _p(self.drafted), st)

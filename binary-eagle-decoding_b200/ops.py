@@ -212,8 +212,13 @@ def pack_ffn(gate: Tensor, up: Tensor, down: Tensor, scale_gate: Tensor | None =
 
 
 def ffn_he4(x: Tensor, ffn: PackedFFN, residual: Tensor | None = None, hidden_out: bool = False,
-            flags: Flags | None = None, out: Tensor | None = None):
-    """HE4 SwiGLU block ``residual + down(silu(gate(x)) * up(x))`` (model.py:220-223)."""
+            flags: Flags | None = None, out: Tensor | None = None, norm: Tensor | None = None,
+            epsilon: float = 1e-6):
+    """HE4 SwiGLU block ``residual + down(silu(gate(n)) * up(n))`` (model.py:220-223).
+
+    ``n = x``, or ``n = rms(x, norm, epsilon)`` when ``norm`` is given (then
+    ``x`` is the residual stream itself).
+    """
     device = _require_cuda(x, residual, out)
     tokens = x.shape[0]
     if not 1 <= tokens <= MAX_DECODE_TOKENS:
@@ -228,7 +233,7 @@ def ffn_he4(x: Tensor, ffn: PackedFFN, residual: Tensor | None = None, hidden_ou
         _p(x), _p(residual), _p(y), tokens, ffn.hidden, ffn.inter, _p(ffn.signs_gate_up), _p(ffn.scale_gate),
         _p(ffn.midpoint_gate), _p(ffn.scale_up), _p(ffn.midpoint_up), _p(ffn.gain_gate_up), _p(ffn.bound_gate_up),
         _p(ffn.signs_down), _p(ffn.scale_down), _p(ffn.midpoint_down), _p(ffn.gain_down), _p(ffn.bound_down),
-        _p(h), _p(ws), ws.numel(), flags.ptr,
+        _p(h), _p(ws), ws.numel(), flags.ptr, _p(norm), float(epsilon),
     )
     _lib.call("bd_ffn_he4", _lib.ctypes.byref(args), _stream(device))
     if own:

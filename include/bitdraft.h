@@ -128,6 +128,9 @@ typedef struct {
     void *workspace;
     size_t workspace_bytes;
     int32_t *flags;
+    const float *norm_weight; /* optional: x is the raw residual stream and n = rms(x, norm_weight,
+                                 epsilon) is computed in the quantizer (model.py:220) */
+    float epsilon;
 } bd_ffn_he4_args;
 size_t bd_ffn_workspace_bytes(int tokens, int64_t hidden, int64_t inter);
 int bd_ffn_he4(const bd_ffn_he4_args *args, bd_stream_t stream);
@@ -198,6 +201,25 @@ int bd_rms_rows(const float *x, int n, int64_t cols, int64_t ldx, const float *w
 int bd_heads_post(const float *src, int n, int64_t ld_src, int64_t col0, int heads, int head_dim,
                   const float *norm_weight, float epsilon, int rope, float theta, int64_t pos0,
                   uint16_t *dst_f16, int64_t dst_ld, int32_t *flags, bd_stream_t stream);
+/* The same for a whole q|k|v row block in one launch (Layer.forward,
+ * model.py:207-213): q heads -> q_f16 [n][q_ld], k heads -> K cache rows
+ * pos0.., v heads -> V cache rows pos0.. (row stride kv_ld elements). */
+int bd_qkv_post(const float *src, int n, int64_t ld_src, int heads, int kv_heads, int head_dim,
+                const float *q_norm, const float *k_norm, float epsilon, float theta, int64_t pos0,
+                uint16_t *q_f16, int64_t q_ld, uint16_t *k_cache_f16, uint16_t *v_cache_f16, int64_t kv_ld,
+                int32_t *flags, bd_stream_t stream);
+
+/* Block-draft attention of Layer.forward (w1a1_eagle/model.py:212-218) over the
+ * fp16 K/V cache: out[t][h * d + j] = softmax_k(q_t,h . k_k / sqrt(d)) v_k,j
+ * with q head h reading kv head h / (heads / kv_heads), keys 0 .. keys-1 at
+ * positions equal to their index, query row t at position anchor + t, and, if
+ * `windowed`, only keys with |anchor + t - k| < window (all but the last layer,
+ * model.py:390-392).  q fp16 [tokens][heads][d], caches fp16
+ * [positions][kv_heads][d]; tokens <= 16, head_dim 64 or 128, heads/kv_heads <= 4. */
+size_t bd_attention_workspace_bytes(int heads, int head_dim, int keys);
+int bd_attention_decode(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache, int tokens, int heads,
+                        int kv_heads, int head_dim, int keys, int windowed, int64_t anchor, int64_t window,
+                        float *out, void *workspace, size_t workspace_bytes, bd_stream_t stream);
 
 #ifdef __cplusplus
 }

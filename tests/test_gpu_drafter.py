@@ -161,3 +161,31 @@ def test_round_graph_replays_match_direct_calls():
     engine.set_tokens(40, 16)
     direct = engine.draft(40, 16).cpu()
     assert torch.equal(direct[1:], out1)
+
+
+@pytest.mark.parametrize("d,heads,kvh,tokens,keys,windowed", [(128, 32, 8, 16, 4112, 1), (128, 32, 8, 16, 300, 0),
+                                                             (64, 4, 2, 5, 77, 1), (128, 8, 8, 1, 129, 0)])
+def test_attention_kernel_against_numpy(d, heads, kvh, tokens, keys, windowed):
+    lib = package()._lib
+    g = torch.Generator().manual_seed(keys)
+    anchor, window = keys - tokens, 64
+    q = torch.randn(tokens, heads, d, generator=g).half()
+    kc = torch.randn(keys, kvh, d, generator=g).half()
+    vc = torch.randn(keys, kvh, d, generator=g).half()
+    out = torch.zeros(tokens, heads * d, device=DEV)
+    ws = torch.zeros(int(lib.load().bd_attention_workspace_bytes(heads, d, keys)), dtype=torch.uint8, device=DEV)
+    qd, kd, vd = q.to(DEV), kc.to(DEV), vc.to(DEV)
+    lib.call("bd_attention_decode", qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), tokens, heads, kvh, d, keys, windowed,
+             anchor, window, out.data_ptr(), ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
+    groups = heads // kvh
+    qf, kf, vf = q.double().numpy(), kc.double().numpy(), vc.double().numpy()
+    want = np.zeros((tokens, heads, d))
+    for h in range(heads):
+        s = qf[:, h] @ kf[:, h // groups].T / np.sqrt(d)
+        if windowed:
+            pos = anchor + np.arange(tokens)[:, None]
+            s = np.where(np.abs(pos - np.arange(keys)[None, :]) < window, s, -np.inf)
+        p = np.exp(s - s.max(-1, keepdims=True))
+        want[:, h] = (p / p.sum(-1, keepdims=True)) @ vf[:, h // groups]
+    got = out.cpu().numpy().reshape(tokens, heads, d)
+    assert rel(got, want) < 3e-3, rel(got, want)
