@@ -79,7 +79,8 @@ SIGNATURES = {
     "bd_tile_w16": (c_int, [P, c_int, c_int64, c_int64, P, P]),
     "bd_x16_bytes": (c_int64, [c_int, c_int64]),
     "bd_pack_x16": (c_int, [P, c_int, c_int64, c_int64, P, ctypes.c_float, P, P, c_int64, P, P]),
-    "bd_gemv_bf16": (c_int, [P, c_int64, c_int64, P, c_int, P, c_int64, P, P, P, P]),
+    "bd_gemv_workspace_bytes": (c_size_t, [c_int, c_int64, c_int64]),
+    "bd_gemv_bf16": (c_int, [P, c_int64, c_int64, P, c_int, P, c_int64, P, P, P, P, c_size_t, P]),
     "bd_argmax_finish": (c_int, [P, c_int, P, P]),
     "bd_embed_rows": (c_int, [P, c_int64, c_int64, P, c_int, P, P, P]),
     "bd_rms_rows": (c_int, [P, c_int, c_int64, c_int64, P, ctypes.c_float, P, c_int64, P]),

@@ -195,25 +195,55 @@ __global__ void __launch_bounds__(128) attn_chunk_kernel(const AttnArgs a) {
     }
 }
 
-// out[token][head * d + j] = sum_c e^{m_c - M} O_c / sum_c e^{m_c - M} l_c.  Grid (tokens, heads), d threads.
+// out[token][head * d + j] = sum_c e^{m_c - M} O_c / sum_c e^{m_c - M} l_c.
+// Grid (tokens, heads), d threads: chunk weights are computed once into shared
+// memory, then every thread sums its column over the chunks with independent loads.
+constexpr int kMaxChunks = 1024;
+
 template <int kDim>
 __global__ void attn_combine_kernel(const AttnArgs a) {
+    __shared__ float wgt[kMaxChunks];
+    __shared__ float red[kDim / 32];
+    __shared__ float s_den;
     grid_wait();
     grid_launch_dependents();
     const int token = blockIdx.x, head = blockIdx.y, j = threadIdx.x;
-    float M = -INFINITY;
-    for (int c = 0; c < a.chunks; ++c)
-        M = fmaxf(M, a.part_ml[((static_cast<int64_t>(c) * a.heads + head) * 16 + token) * 2]);
-    float num = 0.0f, den = 0.0f;
-    for (int c = 0; c < a.chunks; ++c) {
+    const int lane = j & 31, warp = j >> 5;
+    float mloc = -INFINITY;
+    for (int c = j; c < a.chunks; c += kDim)
+        mloc = fmaxf(mloc, a.part_ml[((static_cast<int64_t>(c) * a.heads + head) * 16 + token) * 2]);
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, d));
+    if (lane == 0) red[warp] = mloc;
+    __syncthreads();
+    float M = red[0];
+#pragma unroll
+    for (int w = 1; w < kDim / 32; ++w) M = fmaxf(M, red[w]);
+    __syncthreads();
+    float dloc = 0.0f;
+    for (int c = j; c < a.chunks; c += kDim) {
         const int64_t base = (static_cast<int64_t>(c) * a.heads + head) * 16 + token;
         const float mc = a.part_ml[base * 2];
-        if (mc == -INFINITY) continue;
-        const float w = __expf(mc - M);
-        den += w * a.part_ml[base * 2 + 1];
-        num += w * a.part_o[base * kDim + j];
+        const float w = mc == -INFINITY ? 0.0f : __expf(mc - M);
+        wgt[c] = w;
+        dloc += w * a.part_ml[base * 2 + 1];
     }
-    a.out[static_cast<int64_t>(token) * a.heads * kDim + head * kDim + j] = num / den;
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) dloc += __shfl_xor_sync(0xffffffffu, dloc, d);
+    if (lane == 0) red[warp] = dloc;
+    __syncthreads();
+    if (j == 0) {
+        float den = 0.0f;
+        for (int w = 0; w < kDim / 32; ++w) den += red[w];
+        s_den = den;
+    }
+    __syncthreads();
+    const float *po = a.part_o + (static_cast<int64_t>(head) * 16 + token) * kDim + j;
+    const int64_t stride = static_cast<int64_t>(a.heads) * 16 * kDim;
+    float num = 0.0f;
+#pragma unroll 8
+    for (int c = 0; c < a.chunks; ++c) num += wgt[c] * po[c * stride];
+    a.out[static_cast<int64_t>(token) * a.heads * kDim + head * kDim + j] = num / s_den;
 }
 
 }  // namespace bd
@@ -242,7 +272,7 @@ extern "C" int bd_attention_decode(const uint16_t *q, const uint16_t *k_cache, c
                                    bd_stream_t stream) {
     if (tokens < 1 || tokens > 16 || (head_dim != 64 && head_dim != 128) || heads < 1 || kv_heads < 1 ||
         heads % kv_heads ||
-        heads / kv_heads > 4 || keys < 1 || !q || !k_cache || !v_cache || !out)
+        heads / kv_heads > 4 || keys < 1 || keys > kMaxChunks * kKeys || !q || !k_cache || !v_cache || !out)
         return BD_ERR_INVALID;
     if (!workspace || workspace_bytes < bd_attention_workspace_bytes(heads, head_dim, keys)) return BD_ERR_WORKSPACE;
     AttnArgs a{};

@@ -141,8 +141,9 @@ extern "C" int bd_qkv_post(const float *src, int n, int64_t ld_src, int heads, i
                            const float *q_norm, const float *k_norm, float epsilon, float theta, int64_t pos0,
                            uint16_t *q_f16, int64_t q_ld, uint16_t *k_cache_f16, uint16_t *v_cache_f16, int64_t kv_ld,
                            int32_t *flags, bd_stream_t stream) {
-    if (n < 1 || heads < 1 || kv_heads < 1 || head_dim < 2 || (head_dim & 1) || head_dim > 2048 || !src || !q_f16 ||
-        !k_cache_f16 || !v_cache_f16 || !q_norm || !k_norm)
+    // heads == 0: a k|v row block only (context rows), q pointers unused
+    if (n < 1 || heads < 0 || kv_heads < 1 || head_dim < 2 || (head_dim & 1) || head_dim > 2048 || !src ||
+        (heads > 0 && (!q_f16 || !q_norm)) || !k_cache_f16 || !v_cache_f16 || !k_norm)
         return BD_ERR_INVALID;
     const unsigned threads = static_cast<unsigned>((head_dim / 2 + 31) / 32 * 32);
     return launch_pdl(qkv_post_kernel, dim3(n, heads + 2 * kv_heads), dim3(threads), 0, stream, src, ld_src, heads,

@@ -17,7 +17,7 @@ namespace bd {
 
 constexpr int kGemvThreads = 256;
 constexpr int kGemvWarps = kGemvThreads / 32;
-constexpr int kGemvUnroll = 4;
+constexpr int kGemvUnroll = 4;  // K tiles per pipeline stage (two stages in flight)
 
 struct GemvArgs {
     const uint4 *w;              // W16 tiles
@@ -30,6 +30,9 @@ struct GemvArgs {
     const float *residual;       // [tokens][ld_out] or null
     unsigned long long *argmax;  // [tokens] running keys or null
     int32_t *flags;
+    int splits;                  // CTAs along K (blockIdx.y); > 1 needs partial + counters
+    float *partial;              // [splits][gridDim.x][cells]
+    int32_t *counters;           // [gridDim.x], zero on entry, left zero
 };
 
 __device__ __forceinline__ unsigned long long order_key(float v, uint32_t idx) {
@@ -38,14 +41,51 @@ __device__ __forceinline__ unsigned long long order_key(float v, uint32_t idx) {
     return (static_cast<unsigned long long>(b) << 32) | static_cast<unsigned long long>(~idx);
 }
 
+template <int RB>
+__device__ __forceinline__ void gemv_issue(uint4 (&wa)[kGemvUnroll][RB], const uint4 *const (&wrow)[RB], int64_t kt,
+                                           int64_t kt1) {
+#pragma unroll
+    for (int u = 0; u < kGemvUnroll; ++u)
+#pragma unroll
+        for (int r = 0; r < RB; ++r)
+            if (kt + u < kt1) wa[u][r] = ld_stream_u4(wrow[r] + (kt + u) * 32);
+}
+
+template <int NT, int RB>
+__device__ __forceinline__ void gemv_compute(float (&acc)[RB][NT][4], const uint4 (&wa)[kGemvUnroll][RB],
+                                             const uint2 *x, int64_t plane, int64_t nkt, int64_t kt, int64_t kt1,
+                                             int lane) {
+#pragma unroll
+    for (int u = 0; u < kGemvUnroll; ++u) {
+        if (kt + u < kt1) {
+            uint2 xb[2][NT];
+#pragma unroll
+            for (int p = 0; p < 2; ++p)
+#pragma unroll
+                for (int n = 0; n < NT; ++n) xb[p][n] = __ldg(x + p * plane + (n * nkt + kt + u) * 32 + lane);
+#pragma unroll
+            for (int r = 0; r < RB; ++r)
+#pragma unroll
+                for (int p = 0; p < 2; ++p)
+#pragma unroll
+                    for (int n = 0; n < NT; ++n)
+                        mma_bf16_16816(acc[r][n], wa[u][r].x, wa[u][r].y, wa[u][r].z, wa[u][r].w, xb[p][n].x,
+                                       xb[p][n].y);
+        }
+    }
+}
+
 template <int NT, int RB>
 __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
     __shared__ float red[kGemvWarps][RB * NT * 4][32];
     __shared__ unsigned long long best[32];
+    __shared__ int last;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t nrb = (a.rows + 15) / 16;
     const int64_t rb0 = static_cast<int64_t>(blockIdx.x) * RB;
-    const int64_t kt0 = warp * a.nkt / kGemvWarps, kt1 = (warp + 1) * a.nkt / kGemvWarps;
+    // this CTA's K range, split over its warps
+    const int64_t ck0 = blockIdx.y * a.nkt / a.splits, ck1 = (blockIdx.y + 1) * a.nkt / a.splits;
+    const int64_t kt0 = ck0 + warp * (ck1 - ck0) / kGemvWarps, kt1 = ck0 + (warp + 1) * (ck1 - ck0) / kGemvWarps;
     float acc[RB][NT][4];
 #pragma unroll
     for (int r = 0; r < RB; ++r)
@@ -59,45 +99,17 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
     for (int r = 0; r < RB; ++r) wrow[r] = a.w + (rb0 + r < nrb ? rb0 + r : nrb - 1) * a.nkt * 32 + lane;
     const int64_t plane = a.ntb * a.nkt * 32;
 
-    uint4 wa[kGemvUnroll][RB];
-    // first batch of weights before the dependency wait (weights are read-only)
-#pragma unroll
-    for (int u = 0; u < kGemvUnroll; ++u)
-#pragma unroll
-        for (int r = 0; r < RB; ++r)
-            if (kt0 + u < kt1) wa[u][r] = ld_stream_u4(wrow[r] + (kt0 + u) * 32);
+    // two register stages: the next stage's weights stream in while the current one multiplies
+    uint4 wa[kGemvUnroll][RB], wb[kGemvUnroll][RB];
+    gemv_issue<RB>(wa, wrow, kt0, kt1);  // weights are read-only: before the dependency wait
     grid_wait();
     grid_launch_dependents();
     if (threadIdx.x < 32) best[threadIdx.x] = 0ull;
-
-    for (int64_t kt = kt0; kt < kt1; kt += kGemvUnroll) {
-        uint2 xb[kGemvUnroll][2][NT];
-#pragma unroll
-        for (int u = 0; u < kGemvUnroll; ++u)
-            if (kt + u < kt1)
-#pragma unroll
-                for (int p = 0; p < 2; ++p)
-#pragma unroll
-                    for (int n = 0; n < NT; ++n) xb[u][p][n] = __ldg(a.x + p * plane + (n * a.nkt + kt + u) * 32 + lane);
-#pragma unroll
-        for (int u = 0; u < kGemvUnroll; ++u) {
-            if (kt + u < kt1) {
-#pragma unroll
-                for (int r = 0; r < RB; ++r)
-#pragma unroll
-                    for (int p = 0; p < 2; ++p)
-#pragma unroll
-                        for (int n = 0; n < NT; ++n)
-                            mma_bf16_16816(acc[r][n], wa[u][r].x, wa[u][r].y, wa[u][r].z, wa[u][r].w, xb[u][p][n].x,
-                                           xb[u][p][n].y);
-            }
-        }
-        // next batch of weights
-#pragma unroll
-        for (int u = 0; u < kGemvUnroll; ++u)
-#pragma unroll
-            for (int r = 0; r < RB; ++r)
-                if (kt + kGemvUnroll + u < kt1) wa[u][r] = ld_stream_u4(wrow[r] + (kt + kGemvUnroll + u) * 32);
+    for (int64_t kt = kt0; kt < kt1; kt += 2 * kGemvUnroll) {
+        gemv_issue<RB>(wb, wrow, kt + kGemvUnroll, kt1);
+        gemv_compute<NT, RB>(acc, wa, a.x, plane, a.nkt, kt, kt1, lane);
+        gemv_issue<RB>(wa, wrow, kt + 2 * kGemvUnroll, kt1);
+        gemv_compute<NT, RB>(acc, wb, a.x, plane, a.nkt, kt + kGemvUnroll, kt1, lane);
     }
 #pragma unroll
     for (int r = 0; r < RB; ++r)
@@ -108,12 +120,52 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
     __syncthreads();
     // every thread finishes cells (value slot v, lane l) summing warps 0..7 in order
     constexpr int CELLS = RB * NT * 4 * 32;
-    bool bad = false;
-    for (int c = threadIdx.x; c < CELLS; c += kGemvThreads) {
-        const int l = c & 31, v = c >> 5;
-        float s = red[0][v][l];
+    float sums[(CELLS + kGemvThreads - 1) / kGemvThreads];
 #pragma unroll
-        for (int w = 1; w < kGemvWarps; ++w) s = __fadd_rn(s, red[w][v][l]);
+    for (int q = 0; q < (CELLS + kGemvThreads - 1) / kGemvThreads; ++q) {
+        const int c = threadIdx.x + q * kGemvThreads;
+        float s = 0.0f;
+        if (c < CELLS) {
+            const int l = c & 31, v = c >> 5;
+            s = red[0][v][l];
+#pragma unroll
+            for (int w = 1; w < kGemvWarps; ++w) s = __fadd_rn(s, red[w][v][l]);
+        }
+        sums[q] = s;
+    }
+    if (a.splits > 1) {
+        // K split over CTAs: partials meet in global memory; the last CTA of this
+        // row group adds them in split order (deterministic) and finishes.
+        float *mine = a.partial + (static_cast<int64_t>(blockIdx.y) * gridDim.x + blockIdx.x) * CELLS;
+#pragma unroll
+        for (int q = 0; q < (CELLS + kGemvThreads - 1) / kGemvThreads; ++q) {
+            const int c = threadIdx.x + q * kGemvThreads;
+            if (c < CELLS) mine[c] = sums[q];
+        }
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) last = atomicAdd(a.counters + blockIdx.x, 1) == a.splits - 1;
+        __syncthreads();
+        if (!last) return;
+        __threadfence();
+#pragma unroll
+        for (int q = 0; q < (CELLS + kGemvThreads - 1) / kGemvThreads; ++q) {
+            const int c = threadIdx.x + q * kGemvThreads;
+            float s = 0.0f;
+            if (c < CELLS)
+                for (int ks = 0; ks < a.splits; ++ks)
+                    s = __fadd_rn(s, __ldcg(a.partial + (static_cast<int64_t>(ks) * gridDim.x + blockIdx.x) * CELLS + c));
+            sums[q] = s;
+        }
+        if (threadIdx.x == 0) atomicExch(a.counters + blockIdx.x, 0);
+    }
+    bool bad = false;
+#pragma unroll
+    for (int q = 0; q < (CELLS + kGemvThreads - 1) / kGemvThreads; ++q) {
+        const int c = threadIdx.x + q * kGemvThreads;
+        if (c >= CELLS) continue;
+        float s = sums[q];
+        const int l = c & 31, v = c >> 5;
         const int i = v & 3, n = (v >> 2) % NT, r = (v >> 2) / NT;
         const int g = l >> 2, t = l & 3;
         const int64_t o = (rb0 + r) * 16 + g + 8 * (i >> 1);
@@ -256,12 +308,38 @@ template <int NT, int RB>
 static int launch_gemv_t(const GemvArgs &a, cudaStream_t stream) {
     const int64_t nrb = (a.rows + 15) / 16;
     const unsigned grid = static_cast<unsigned>((nrb + RB - 1) / RB);
-    return launch_pdl(gemv_kernel<NT, RB>, dim3(grid), dim3(kGemvThreads), 0, stream, a);
+    return launch_pdl(gemv_kernel<NT, RB>, dim3(grid, a.splits), dim3(kGemvThreads), 0, stream, a);
+}
+
+// Wide matrices (many row blocks): two row blocks per CTA halve the activation traffic.
+static bool gemv_wide(int64_t rows) { return (rows + 15) / 16 >= 8 * 148; }
+
+// K splits over CTAs for a small matrix: enough CTAs for two per SM, at least
+// 8 K tiles per warp.
+static int gemv_splits(int64_t rows, int64_t cols, int sms) {
+    const int64_t groups = ((rows + 15) / 16 + (gemv_wide(rows) ? 1 : 0)) / (gemv_wide(rows) ? 2 : 1);
+    int64_t s = (2 * sms + groups - 1) / groups;
+    const int64_t cap = ((cols + 15) / 16) / (kGemvWarps * 8);
+    if (s > cap) s = cap;
+    return static_cast<int>(s < 1 ? 1 : s);
+}
+
+static int64_t gemv_cells(int tokens, int64_t rows) {
+    return static_cast<int64_t>(gemv_wide(rows) ? 2 : 1) * ((tokens + 7) / 8) * 4 * 32;
+}
+
+size_t gemv_workspace_bytes(int tokens, int64_t rows, int64_t cols, int sms) {
+    const int s = gemv_splits(rows, cols, sms);
+    if (s <= 1) return 0;
+    const int64_t groups = ((rows + 15) / 16 + (gemv_wide(rows) ? 1 : 0)) / (gemv_wide(rows) ? 2 : 1);
+    return static_cast<size_t>(s * groups * gemv_cells(tokens, rows)) * sizeof(float) + 256 +
+           static_cast<size_t>(groups) * sizeof(int32_t);
 }
 
 int launch_gemv(const GemvArgs &a, cudaStream_t stream) {
     const int64_t nrb = (a.rows + 15) / 16;
-    const bool wide = nrb >= 8 * 148;  // many row blocks: two per CTA halves activation traffic
+    const bool wide = gemv_wide(a.rows);
+    (void)nrb;
     const int nt = (a.tokens + 7) / 8;
     if (a.tokens < 1 || a.tokens > 32 || nt > a.ntb) return BD_ERR_INVALID;
     switch (nt * 2 + (wide ? 1 : 0)) {
@@ -317,13 +395,39 @@ extern "C" int bd_pack_x16(const float *x, int tokens, int64_t cols, int64_t ldx
                       normed, ld_normed, flags);
 }
 
+static int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0, v = 0;
+        n = (cudaGetDevice(&dev) == cudaSuccess &&
+             cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0)
+                ? v
+                : 148;
+    }
+    return n;
+}
+
+extern "C" size_t bd_gemv_workspace_bytes(int tokens, int64_t rows, int64_t cols) {
+    if (tokens < 1 || rows < 1 || cols < 1) return 0;
+    return gemv_workspace_bytes(tokens, rows, cols, sm_count());
+}
+
 extern "C" int bd_gemv_bf16(const void *w16, int64_t rows, int64_t cols, const void *x16, int tokens, float *out,
                             int64_t ld_out, const float *residual, unsigned long long *argmax_keys, int32_t *flags,
-                            bd_stream_t stream) {
+                            void *workspace, size_t workspace_bytes, bd_stream_t stream) {
     if (rows < 1 || cols < 1 || !w16 || !x16 || tokens < 1 || tokens > 32) return BD_ERR_INVALID;
     if (!out && !argmax_keys) return BD_ERR_INVALID;
     if ((out || residual) && ld_out < rows) return BD_ERR_INVALID;
     GemvArgs a{};
+    a.splits = 1;
+    const size_t need = gemv_workspace_bytes(tokens, rows, cols, sm_count());
+    if (need && workspace && workspace_bytes >= need) {  // without a workspace the K split is skipped
+        a.splits = gemv_splits(rows, cols, sm_count());
+        const int64_t groups = ((rows + 15) / 16 + (gemv_wide(rows) ? 1 : 0)) / (gemv_wide(rows) ? 2 : 1);
+        a.counters = static_cast<int32_t *>(workspace);
+        a.partial = reinterpret_cast<float *>(static_cast<char *>(workspace) +
+                                              ((groups * sizeof(int32_t) + 255) & ~static_cast<size_t>(255)));
+    }
     a.w = static_cast<const uint4 *>(w16);
     a.rows = rows;
     a.cols = cols;

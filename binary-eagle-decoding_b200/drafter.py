@@ -136,6 +136,11 @@ class DraftEngine:
         self.attn_ws = torch.zeros(int(_lib.load().bd_attention_workspace_bytes(cfg.heads, cfg.head_dim,
                                                                                  self.max_positions)),
                                    dtype=torch.uint8, device=dev)
+        lib = _lib.load()
+        shapes = [(cfg.hidden, cfg.taps * cfg.hidden), (2 * kvd, cfg.hidden), (self.qkv_width, cfg.hidden),
+                  (cfg.hidden, cfg.heads * cfg.head_dim), (self.vocab_size, cfg.hidden)]
+        self.gemv_ws = torch.zeros(max(256, max(int(lib.bd_gemv_workspace_bytes(T, r, c)) for r, c in shapes)),
+                                   dtype=torch.uint8, device=dev)
         self.flags = Flags(dev)
         self.positions = 0
 
@@ -150,7 +155,7 @@ class DraftEngine:
     def _gemv(self, w16_ptr: int, rows: int, cols: int, n: int, out: Tensor | None, ld_out: int,
               residual: Tensor | None = None, keys: Tensor | None = None):
         _lib.call("bd_gemv_bf16", w16_ptr, rows, cols, _p(self.x16), n, _p(out), ld_out, _p(residual), _p(keys),
-                  self.flags.ptr, self._stream())
+                  self.flags.ptr, _p(self.gemv_ws), self.gemv_ws.numel(), self._stream())
 
     def _heads(self, src: Tensor, n: int, col0: int, heads: int, norm: Tensor | None, rope: bool, pos0: int,
                dst_ptr: int, dst_ld: int):
@@ -209,8 +214,10 @@ class DraftEngine:
         q_rows = cfg.heads * cfg.head_dim
         for i, layer in enumerate(self.layers):
             self._gemv(_w16_rows(layer.qkv, cfg.hidden, q_rows, 2 * kvd), 2 * kvd, cfg.hidden, n, self.kv_out, 2 * kvd)
-            self._heads(self.kv_out, n, 0, cfg.kv_heads, layer.k_norm, True, pos0, self._cache_ptr(self.k_cache, i, pos0), kvd)
-            self._heads(self.kv_out, n, kvd, cfg.kv_heads, None, False, pos0, self._cache_ptr(self.v_cache, i, pos0), kvd)
+            _lib.call("bd_qkv_post", _p(self.kv_out), n, 2 * kvd, 0, cfg.kv_heads, cfg.head_dim, None,
+                      _p(layer.k_norm), float(cfg.epsilon), float(cfg.theta), pos0, None, 0,
+                      self._cache_ptr(self.k_cache, i, pos0), self._cache_ptr(self.v_cache, i, pos0), kvd,
+                      self.flags.ptr, self._stream())
         self.positions = max(self.positions, pos0 + n)
 
     # ------------------------------------------------------------------ draft

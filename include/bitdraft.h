@@ -182,9 +182,13 @@ int bd_tile_w16(const void *w, int dtype_bits, int64_t rows, int64_t cols, void 
 int64_t bd_x16_bytes(int tokens, int64_t cols);
 int bd_pack_x16(const float *x, int tokens, int64_t cols, int64_t ldx, const float *rms_weight, float epsilon,
                 void *out, float *normed, int64_t ld_normed, int32_t *flags, bd_stream_t stream);
+/* The optional workspace (bd_gemv_workspace_bytes; zero it once, it is left
+ * zeroed) lets small matrices split K over CTAs; partial sums are added in a
+ * fixed order, so results do not depend on scheduling. */
+size_t bd_gemv_workspace_bytes(int tokens, int64_t rows, int64_t cols);
 int bd_gemv_bf16(const void *w16, int64_t rows, int64_t cols, const void *x16, int tokens, float *out,
                  int64_t ld_out, const float *residual, unsigned long long *argmax_keys, int32_t *flags,
-                 bd_stream_t stream);
+                 void *workspace, size_t workspace_bytes, bd_stream_t stream);
 int bd_argmax_finish(unsigned long long *keys, int n, int32_t *out, bd_stream_t stream);
 
 /* Embedding rows (HE4.forward's functional.embedding, model.py:380-381) from a

@@ -24,7 +24,8 @@ def bf16(x):
     return torch.as_tensor(x).to(torch.bfloat16).float()
 
 
-@pytest.mark.parametrize("rows,cols,tokens", [(1000, 300, 5), (9496 * 2, 2560, 16), (48, 16, 32), (17, 33, 9)])
+@pytest.mark.parametrize("rows,cols,tokens", [(1000, 300, 5), (9496 * 2, 2560, 16), (48, 16, 32), (17, 33, 9),
+                                              (2560, 10240, 16), (2048, 2560, 16), (2560, 4096, 7)])
 def test_gemv_store_and_argmax(rows, cols, tokens):
     lib = package()._lib
     g = torch.Generator().manual_seed(rows + cols)
@@ -41,8 +42,12 @@ def test_gemv_store_and_argmax(rows, cols, tokens):
     lib.call("bd_pack_x16", xd.data_ptr(), tokens, cols, cols, None, 1e-6, x16.data_ptr(), None, 0, flags.data_ptr(), stream)
     out = torch.zeros(tokens, rows, device=DEV)
     keys = torch.zeros(tokens, dtype=torch.int64, device=DEV)
+    nbytes = max(256, int(lib.load().bd_gemv_workspace_bytes(tokens, rows, cols)))
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device=DEV)
     lib.call("bd_gemv_bf16", w16.data_ptr(), rows, cols, x16.data_ptr(), tokens, out.data_ptr(), rows, None,
-             keys.data_ptr(), flags.data_ptr(), stream)
+             keys.data_ptr(), flags.data_ptr(), ws.data_ptr(), ws.numel(), stream)
+    # the K-split workspace is left zeroed for the next call
+    assert not ws[:256].any() or int(lib.load().bd_gemv_workspace_bytes(tokens, rows, cols)) == 0
     ids = torch.zeros(tokens, dtype=torch.int32, device=DEV)
     lib.call("bd_argmax_finish", keys.data_ptr(), tokens, ids.data_ptr(), stream)
     want = (x.double() @ w.double().T).numpy()
