@@ -51,26 +51,31 @@ __device__ __forceinline__ void gemv_issue(uint4 (&wa)[kGemvUnroll][RB], const u
             if (kt + u < kt1) wa[u][r] = ld_stream_u4(wrow[r] + (kt + u) * 32);
 }
 
+// One batch of kGemvUnroll K tiles: the activation fragments of all tiles are
+// requested together (they are L2 hits, but each round trip is long), then the MMAs.
 template <int NT, int RB>
 __device__ __forceinline__ void gemv_compute(float (&acc)[RB][NT][4], const uint4 (&wa)[kGemvUnroll][RB],
                                              const uint2 *x, int64_t plane, int64_t nkt, int64_t kt, int64_t kt1,
                                              int lane) {
+    uint2 xb[kGemvUnroll][2][NT];
 #pragma unroll
-    for (int u = 0; u < kGemvUnroll; ++u) {
-        if (kt + u < kt1) {
-            uint2 xb[2][NT];
+    for (int u = 0; u < kGemvUnroll; ++u)
+        if (kt + u < kt1)
 #pragma unroll
             for (int p = 0; p < 2; ++p)
 #pragma unroll
-                for (int n = 0; n < NT; ++n) xb[p][n] = __ldg(x + p * plane + (n * nkt + kt + u) * 32 + lane);
+                for (int n = 0; n < NT; ++n) xb[u][p][n] = __ldg(x + p * plane + (n * nkt + kt + u) * 32 + lane);
+#pragma unroll
+    for (int u = 0; u < kGemvUnroll; ++u) {
+        if (kt + u < kt1) {
 #pragma unroll
             for (int r = 0; r < RB; ++r)
 #pragma unroll
                 for (int p = 0; p < 2; ++p)
 #pragma unroll
                     for (int n = 0; n < NT; ++n)
-                        mma_bf16_16816(acc[r][n], wa[u][r].x, wa[u][r].y, wa[u][r].z, wa[u][r].w, xb[p][n].x,
-                                       xb[p][n].y);
+                        mma_bf16_16816(acc[r][n], wa[u][r].x, wa[u][r].y, wa[u][r].z, wa[u][r].w, xb[u][p][n].x,
+                                       xb[u][p][n].y);
         }
     }
 }
@@ -99,17 +104,16 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
     for (int r = 0; r < RB; ++r) wrow[r] = a.w + (rb0 + r < nrb ? rb0 + r : nrb - 1) * a.nkt * 32 + lane;
     const int64_t plane = a.ntb * a.nkt * 32;
 
-    // two register stages: the next stage's weights stream in while the current one multiplies
-    uint4 wa[kGemvUnroll][RB], wb[kGemvUnroll][RB];
+    // one register stage per warp; HBM latency is hidden by the many resident
+    // warps (a second stage costs registers, hence occupancy, and measured slower)
+    uint4 wa[kGemvUnroll][RB];
     gemv_issue<RB>(wa, wrow, kt0, kt1);  // weights are read-only: before the dependency wait
     grid_wait();
     grid_launch_dependents();
     if (threadIdx.x < 32) best[threadIdx.x] = 0ull;
-    for (int64_t kt = kt0; kt < kt1; kt += 2 * kGemvUnroll) {
-        gemv_issue<RB>(wb, wrow, kt + kGemvUnroll, kt1);
+    for (int64_t kt = kt0; kt < kt1; kt += kGemvUnroll) {
         gemv_compute<NT, RB>(acc, wa, a.x, plane, a.nkt, kt, kt1, lane);
-        gemv_issue<RB>(wa, wrow, kt + 2 * kGemvUnroll, kt1);
-        gemv_compute<NT, RB>(acc, wb, a.x, plane, a.nkt, kt + kGemvUnroll, kt1, lane);
+        gemv_issue<RB>(wa, wrow, kt + kGemvUnroll, kt1);
     }
 #pragma unroll
     for (int r = 0; r < RB; ++r)
