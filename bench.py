@@ -170,32 +170,50 @@ class ClockSampler:
     def __init__(self, index: int):
         self.index = index
         self.proc = None
+        self.rows: list[tuple[float, list[str]]] = []
+        self.window = (0.0, 0.0)
 
-    def __enter__(self):
+    def start(self):
+        """Begin sampling (before the warm-up, so short timed regions still see samples)."""
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True, bufsize=1)
         except OSError:
             self.proc = None
+        if self.proc is not None:
+            import threading
+
+            def reader():
+                for line in self.proc.stdout:
+                    if line.strip():
+                        self.rows.append((time.time(), [v.strip() for v in line.split(",")]))
+
+            self.thread = threading.Thread(target=reader, daemon=True)
+            self.thread.start()
         return self
 
-    def __exit__(self, *exc):
-        self.lines = []
+    def stop(self):
         if self.proc is not None:
             self.proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [line for line in out.splitlines() if line.strip()]
+            self.thread.join(timeout=5)
 
     def summary(self) -> dict:
+        """Samples taken during the timed window; if it was shorter than the sampling
+        interval, the samples of the warm-up right before it (same workload)."""
+        t0, t1 = self.window
+        inside = [f for t, f in self.rows if t0 <= t <= t1]
+        scope = "timed"
+        if not inside:
+            inside = [f for t, f in self.rows if t <= t1][-5:]
+            scope = "warm-up and timed (timed region shorter than the 50 ms sampling interval)"
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in getattr(self, "lines", []):
-            f = [v.strip() for v in line.split(",")]
+        for f in inside:
             if len(f) < 9:
                 continue
             try:
@@ -207,7 +225,7 @@ class ClockSampler:
                 if flag.lower() == "active":
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "scope": scope}
 
 
 def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
@@ -237,6 +255,7 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
     engine.check()
 
     stream = rnd.stream
+    clocks = ClockSampler(local_rank).start()
     for _ in range(args.warmup):
         rnd.replay()
     stream.synchronize()
@@ -245,13 +264,15 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     before = lib.launches
-    with ClockSampler(local_rank) as clocks:
-        with torch.cuda.stream(stream):
-            start.record(stream)
-            for _ in range(args.steps):
-                rnd.replay()
-            end.record(stream)
-        end.synchronize()
+    wall0 = time.time()
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(args.steps):
+            rnd.replay()
+        end.record(stream)
+    end.synchronize()
+    clocks.window = (wall0, time.time())
+    clocks.stop()
     ms = start.elapsed_time(end)
     torch.cuda.synchronize()
     if dist:
@@ -333,8 +354,8 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=50)
-    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--steps", type=int, default=2000)
+    parser.add_argument("--warmup", type=int, default=50)
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     args = parser.parse_args()
