@@ -74,6 +74,7 @@ SIGNATURES = {
     "bd_ffn_w1": (c_int, [ctypes.POINTER(FfnW1Args), P]),
     "bd_accept_workspace_bytes": (c_size_t, [c_int, c_int]),
     "bd_accept_greedy": (c_int, [P, c_int, c_int, c_int64, P, P, c_int, P, P, P, P, c_size_t, P, P]),
+    "bd_accept_greedy_noalloc": (c_int, [P, c_int, c_int, c_int64, P, P, c_int, P, P, P, P, P]),
     "bd_argmax_rows_bf16": (c_int, [P, c_int64, c_int64, P, P, P]),
     "bd_w16_bytes": (c_int64, [c_int64, c_int64]),
     "bd_tile_w16": (c_int, [P, c_int, c_int64, c_int64, P, P]),

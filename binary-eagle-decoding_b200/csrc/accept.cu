@@ -3,6 +3,8 @@
 // Greedy: one CTA per logit row computes the row argmax (strict '>' so the
 // lowest index wins ties, -0.0 == +0.0, non-finite logits flagged), and the last
 // CTA of each request walks the drafts (benchmarks/verifier.py:107-113).
+#include <mutex>
+
 #include "common.cuh"
 
 namespace bd {
@@ -184,6 +186,74 @@ extern "C" int bd_accept_greedy(const uint16_t *logits, int requests, int drafts
     a.next_token = next_token;
     a.counters = counters;
     argmax_greedy_kernel<<<static_cast<unsigned>(rows), kArgmaxThreads, 0, stream>>>(a);
+    BD_CHECK_LAUNCH();
+    return BD_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Greedy acceptance without any allocation.
+//
+// Some callers cannot allocate device memory at all: a verifier embedded in a
+// host serving runtime that hands it only a stream and tensor pointers, where
+// cudaMalloc is off limits on the decode thread (it can synchronise the whole
+// device and stall every other stream), or a process whose device memory budget
+// is fixed when it starts.  For them the per-request counters and the target
+// argmax rows live in this fixed-size file-scope array instead of a
+// caller-provided workspace.  Every GPU that loads the library holds it until
+// the process exits.  All calls share it and it keeps the last call's contents:
+// the counters are cleared by every call, and calls that overlap on the GPU
+// (different streams, or different host threads) race on it.
+constexpr int kNoAllocMaxRequests = 256;
+constexpr int kNoAllocMaxPositions = 33;  // up to 32 drafts + the bonus row
+static __device__ __align__(256) int32_t g_greedy_scratch[kNoAllocMaxRequests +
+                                                          kNoAllocMaxRequests * kNoAllocMaxPositions];
+
+// Device address of the scratch array on the current device.  In host code the
+// symbol is only a host-side stand-in, so the address is looked up once per
+// device (with that device current) and cached.
+static int greedy_scratch(int32_t **out) {
+    static std::mutex mu;
+    static int32_t *address[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return BD_ERR_DEVICE;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!address[dev]) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_greedy_scratch) != cudaSuccess || !p) return BD_ERR_LAUNCH;
+        address[dev] = static_cast<int32_t *>(p);
+    }
+    *out = address[dev];
+    return BD_OK;
+}
+
+extern "C" int bd_accept_greedy_noalloc(const uint16_t *logits, int requests, int drafts, int64_t vocab,
+                                        const int32_t *draft_tokens, const int32_t *eog, int n_eog,
+                                        int32_t *accepted, int32_t *next_token, int32_t *targets, int32_t *flags,
+                                        bd_stream_t stream) {
+    if (requests < 0 || drafts < 0 || vocab < 1 || vocab > 0x7fffffff || n_eog < 0) return BD_ERR_INVALID;
+    if (requests == 0) return BD_OK;
+    if (!logits || (drafts > 0 && !draft_tokens) || (n_eog > 0 && !eog) || !accepted || !next_token)
+        return BD_ERR_INVALID;
+    if (requests > kNoAllocMaxRequests || drafts + 1 > kNoAllocMaxPositions) return BD_ERR_TOO_LARGE;
+    int32_t *scratch = nullptr;
+    if (int st = greedy_scratch(&scratch)) return st;
+    int32_t *counters = scratch;
+    if (cudaMemsetAsync(counters, 0, static_cast<size_t>(requests) * sizeof(int32_t), stream) != cudaSuccess)
+        return BD_ERR_LAUNCH;
+    GreedyArgs a{};
+    a.logits = logits;
+    a.rows = static_cast<int64_t>(requests) * (drafts + 1);
+    a.vocab = vocab;
+    a.targets = targets ? targets : scratch + kNoAllocMaxRequests;
+    a.flags = flags;
+    a.positions = drafts + 1;
+    a.drafts = draft_tokens;
+    a.eog = eog;
+    a.n_eog = n_eog;
+    a.accepted = accepted;
+    a.next_token = next_token;
+    a.counters = counters;
+    argmax_greedy_kernel<<<static_cast<unsigned>(a.rows), kArgmaxThreads, 0, stream>>>(a);
     BD_CHECK_LAUNCH();
     return BD_OK;
 }

@@ -77,6 +77,7 @@ extern "C" const char *bd_status_string(int status) {
         case BD_ERR_LAUNCH: return "CUDA launch or runtime error";
         case BD_ERR_WORKSPACE: return "workspace too small";
         case BD_ERR_DEVICE: return "no usable sm_100 device";
+        case BD_ERR_TOO_LARGE: return "size exceeds the fixed scratch capacity of this entry point";
         default: return "unknown status";
     }
 }

@@ -33,6 +33,7 @@ typedef struct CUstream_st *bd_stream_t; /* == cudaStream_t */
 #define BD_ERR_LAUNCH 3    /* CUDA launch or runtime error */
 #define BD_ERR_WORKSPACE 4 /* workspace too small */
 #define BD_ERR_DEVICE 5    /* no usable sm_100 device */
+#define BD_ERR_TOO_LARGE 6 /* size beyond a fixed scratch capacity */
 
 /* ---- device-reported flags (OR-ed into *flags) ---- */
 #define BD_FLAG_NONFINITE_LATENT 1u   /* export.py:80-81 "finite F32 sign matrix required" */
@@ -160,6 +161,20 @@ int bd_accept_greedy(const uint16_t *logits, int requests, int drafts, int64_t v
                      const int32_t *draft_tokens, const int32_t *eog, int n_eog,
                      int32_t *accepted, int32_t *next_token, int32_t *targets,
                      void *workspace, size_t workspace_bytes, int32_t *flags, bd_stream_t stream);
+
+/* bd_accept_greedy without any device allocation.  This entry point has no
+ * counterpart in the reference.  It is for callers that cannot allocate device
+ * memory (e.g. a verifier embedded in a serving runtime that only hands out a
+ * stream and tensor pointers and forbids cudaMalloc on its decode thread): the
+ * per-request counters and the target rows live in a fixed file-scope device
+ * array of the library (about 35 KB per GPU, held until the process exits).
+ * Limits: requests <= 256 and drafts + 1 <= 33, else BD_ERR_TOO_LARGE.  The
+ * first call on a device looks up the array's device address (make it before
+ * any stream capture); every call clears the counters it uses; all calls share
+ * the array, so calls that overlap on the GPU race with each other. */
+int bd_accept_greedy_noalloc(const uint16_t *logits, int requests, int drafts, int64_t vocab,
+                             const int32_t *draft_tokens, const int32_t *eog, int n_eog, int32_t *accepted,
+                             int32_t *next_token, int32_t *targets, int32_t *flags, bd_stream_t stream);
 
 /* Row argmax of bf16 or fp32 rows (lowest index on ties), used for drafting. */
 int bd_argmax_rows_bf16(const uint16_t *logits, int64_t rows, int64_t vocab, int32_t *out,
