@@ -351,6 +351,27 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def profile_round() -> None:
+    """One draft round between cudaProfilerStart/Stop (for ncu --profile-from-start off)."""
+    device = torch.device("cuda", 0)
+    drafter = importlib.import_module("binary-eagle-decoding_b200.drafter")
+    geom = importlib.import_module("binary-eagle-decoding_b200.model").Geometry(**GEOMETRY)
+    tensors, vocabulary, features, tokens = make_tensors()
+    engine = drafter.DraftEngine(tensors, vocabulary, VOCAB - 1, geom, device=device)
+    feats = features.to(device)
+    engine.prefill(feats, CONTEXT - INGEST)
+    for _ in range(3):  # the round of the last warm-up is the profiled one
+        engine.ingest(feats[CONTEXT - INGEST:CONTEXT], CONTEXT - INGEST)
+        engine.set_tokens(int(tokens[CONTEXT]), SLOTS)
+        engine.draft(CONTEXT, SLOTS)
+        torch.cuda.synchronize()
+        if _ == 1:
+            torch.cuda.cudart().cudaProfilerStart()
+    torch.cuda.cudart().cudaProfilerStop()
+    engine.check()
+    print("profiled one draft round")
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--gpus", type=int, default=1)
@@ -358,7 +379,12 @@ def main() -> None:
     parser.add_argument("--warmup", type=int, default=50)
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    parser.add_argument("--profile-round", action="store_true",
+                        help="run one draft round between cudaProfilerStart/Stop and exit")
     args = parser.parse_args()
+    if args.profile_round:
+        profile_round()
+        return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus if args.gpus == 1 else 1)))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
