@@ -75,6 +75,9 @@ SIGNATURES = {
     "bd_accept_workspace_bytes": (c_size_t, [c_int, c_int]),
     "bd_accept_greedy": (c_int, [P, c_int, c_int, c_int64, P, P, c_int, P, P, P, P, c_size_t, P, P]),
     "bd_accept_greedy_noalloc": (c_int, [P, c_int, c_int, c_int64, P, P, c_int, P, P, P, P, P]),
+    "bd_rejection_workspace_bytes": (c_size_t, [c_int, c_int]),
+    "bd_accept_rejection": (c_int, [P, P, c_int, c_int, c_int64, P, P, c_int, ctypes.c_ulonglong, ctypes.c_uint32,
+                                    P, P, P, c_size_t, P, P]),
     "bd_argmax_rows_bf16": (c_int, [P, c_int64, c_int64, P, P, P]),
     "bd_w16_bytes": (c_int64, [c_int64, c_int64]),
     "bd_tile_w16": (c_int, [P, c_int, c_int64, c_int64, P, P]),
@@ -122,7 +125,7 @@ def load() -> ctypes.CDLL:
 
 
 # Kernel launches issued by each entry point (for launch accounting).
-KERNELS_PER_CALL = {"bd_ffn_he4": 3, "bd_ffn_w1": 4, "bd_attention_decode": 2}
+KERNELS_PER_CALL = {"bd_ffn_he4": 3, "bd_ffn_w1": 4, "bd_attention_decode": 2, "bd_accept_rejection": 2}
 launches = 0
 
 

@@ -64,7 +64,8 @@ _workspaces: dict[tuple, Tensor] = {}
 
 
 def workspace(device: torch.device, kind: str, nbytes: int) -> Tensor:
-    """A zeroed, cached byte buffer; the kernels leave their workspaces zeroed."""
+    """A cached byte buffer per (device, kind), zeroed when created; kernels that keep
+    counters in their workspace leave them zeroed."""
     key = (device.index if device.index is not None else torch.cuda.current_device(), kind)
     buf = _workspaces.get(key)
     if buf is None or buf.numel() < nbytes:
@@ -292,6 +293,33 @@ def accept_greedy(logits: Tensor, drafts: Tensor, eog: Tensor | None = None, tar
     if own:
         flags.check()
     return (accepted, nxt, tg) if targets else (accepted, nxt)
+
+
+def accept_rejection(target_logits: Tensor, draft_logits: Tensor, drafts: Tensor, seed: int, offset: int = 0,
+                     eog: Tensor | None = None, flags: Flags | None = None):
+    """Temperature-1 speculative rejection sampling under the deterministic contract
+    of ``bd_accept_rejection``.  Returns ``(accepted [B], next_token [B])``."""
+    if target_logits.dtype != torch.bfloat16 or draft_logits.dtype != torch.bfloat16:
+        raise ValueError("logits must be bf16")
+    if drafts.dtype != torch.int32 or drafts.ndim != 2:
+        raise ValueError("drafts must be int32 [requests, drafts]")
+    requests, n = drafts.shape
+    if target_logits.shape[:2] != (requests, n + 1) or draft_logits.shape[:2] != (requests, n) \
+            or target_logits.shape[2] != draft_logits.shape[2]:
+        raise ValueError("logits must be [requests, drafts + 1, vocab] and [requests, drafts, vocab]")
+    device = _require_cuda(target_logits, draft_logits, drafts, eog)
+    accepted = torch.empty(requests, dtype=torch.int32, device=device)
+    nxt = torch.empty(requests, dtype=torch.int32, device=device)
+    ws = workspace(device, "rejection", int(_lib.load().bd_rejection_workspace_bytes(requests, n)))
+    own = flags is None
+    flags = flags or Flags(device)
+    n_eog = 0 if eog is None else eog.numel()
+    _lib.call("bd_accept_rejection", _p(target_logits), _p(draft_logits), requests, n, target_logits.shape[2],
+              _p(drafts), _p(eog), n_eog, seed & 0xFFFFFFFFFFFFFFFF, offset & 0xFFFFFFFF, _p(accepted), _p(nxt),
+              _p(ws), ws.numel(), flags.ptr, _stream(device))
+    if own:
+        flags.check()
+    return accepted, nxt
 
 
 def argmax_rows(logits: Tensor, flags: Flags | None = None) -> Tensor:

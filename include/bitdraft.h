@@ -176,6 +176,22 @@ int bd_accept_greedy_noalloc(const uint16_t *logits, int requests, int drafts, i
                              const int32_t *draft_tokens, const int32_t *eog, int n_eog, int32_t *accepted,
                              int32_t *next_token, int32_t *targets, int32_t *flags, bd_stream_t stream);
 
+/* Temperature-1 speculative rejection sampling (the reference's runtime uses
+ * llama.cpp's common_sampler_sample_and_accept_n_rejection, un-vendored; its
+ * in-tree pins are native/verifier-test.cpp:43-80 and the EOG break of
+ * benchmarks/native.py:19-38).  Deterministic contract: Philox4x32-10 uniforms
+ * (key = seed, counter = (request, position, purpose, offset)), a fixed-order
+ * fp32 exp and softmax sums; accept d_i iff u q(d_i) < p(d_i); on rejection at
+ * i sample from max(0, p_i - q_i), after n acceptances sample the bonus from
+ * p_n; an accepted EOG that is not the last draft ends the round.
+ * target_logits bf16 [requests][drafts+1][vocab], draft_logits bf16
+ * [requests][drafts][vocab]; vocab <= 524288.  Outputs as bd_accept_greedy. */
+size_t bd_rejection_workspace_bytes(int requests, int drafts);
+int bd_accept_rejection(const uint16_t *target_logits, const uint16_t *draft_logits, int requests, int drafts,
+                        int64_t vocab, const int32_t *draft_tokens, const int32_t *eog, int n_eog,
+                        unsigned long long seed, uint32_t offset, int32_t *accepted, int32_t *next_token,
+                        void *workspace, size_t workspace_bytes, int32_t *flags, bd_stream_t stream);
+
 /* Row argmax of bf16 or fp32 rows (lowest index on ties), used for drafting. */
 int bd_argmax_rows_bf16(const uint16_t *logits, int64_t rows, int64_t vocab, int32_t *out,
                         int32_t *flags, bd_stream_t stream);
