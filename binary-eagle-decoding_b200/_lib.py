@@ -72,6 +72,10 @@ SIGNATURES = {
     "bd_ffn_workspace_bytes": (c_size_t, [c_int, c_int64, c_int64]),
     "bd_ffn_he4": (c_int, [ctypes.POINTER(FfnHe4Args), P]),
     "bd_ffn_w1": (c_int, [ctypes.POINTER(FfnW1Args), P]),
+    "bd_binarize_rows": (c_int, [P, c_int64, c_int64, P, P, P, P]),
+    "bd_projection_w1a1_workspace_bytes": (c_size_t, [c_int64, c_int64]),
+    "bd_projection_w1a1": (c_int, [P, c_int, c_int64, c_int64, P, P, P, P, P, c_size_t, P, P]),
+    "bd_ffn_w1a1": (c_int, [ctypes.POINTER(FfnW1Args), P]),
     "bd_accept_workspace_bytes": (c_size_t, [c_int, c_int]),
     "bd_accept_greedy": (c_int, [P, c_int, c_int, c_int64, P, P, c_int, P, P, P, P, c_size_t, P, P]),
     "bd_accept_greedy_noalloc": (c_int, [P, c_int, c_int, c_int64, P, P, c_int, P, P, P, P, P]),
@@ -129,10 +133,11 @@ KERNELS_PER_CALL = {"bd_ffn_he4": 3, "bd_ffn_w1": 4, "bd_attention_decode": 2, "
 launches = 0
 
 
-def call(name: str, *args) -> None:
-    """Call an int-status entry point; raise on a non-zero status."""
+def call(name: str, *args, kernels: int | None = None) -> None:
+    """Call an int-status entry point; raise on a non-zero status.  ``kernels``
+    overrides the launch count of entry points whose count depends on sizes."""
     global launches
-    launches += KERNELS_PER_CALL.get(name, 1)
+    launches += KERNELS_PER_CALL.get(name, 1) if kernels is None else kernels
     status = getattr(load(), name)(*args)
     if status != BD_OK:
         message = load().bd_status_string(status).decode()

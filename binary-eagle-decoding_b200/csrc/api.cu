@@ -272,3 +272,125 @@ extern "C" int bd_ffn_w1(const bd_ffn_w1_args *p, bd_stream_t stream) {
     dn.flags = p->flags;
     return launch_proj(dn, EPI_W1, stream);
 }
+
+// ------------------------------------------------------------------------------------ W1A1
+// Sign-binarised activations (x >= 0 -> +1, per-token scale mean|x| in a fixed
+// summation order) against one-bit weights; the +-1 dot K - 2 popc(x ^ w) is
+// computed exactly as 2 * (codes . b01) - sum(codes) on the integer MMA pipe.
+// Token counts above 32 run in 32-token chunks on the same stream.
+
+extern "C" int bd_binarize_rows(const float *x, int64_t rows, int64_t cols, uint32_t *words, float *mean_abs,
+                                int32_t *flags, bd_stream_t stream) {
+    if (rows < 0 || cols < 1 || rows > 0x7fffffff) return BD_ERR_INVALID;
+    if (rows == 0) return BD_OK;
+    if (!x || !words || !mean_abs) return BD_ERR_INVALID;
+    return launch_binarize(x, rows, cols, bd_codes_ld(cols), nullptr, nullptr, mean_abs, words, (cols + 31) / 32,
+                           flags, stream);
+}
+
+struct W1a1Pieces {
+    int8_t *codes;
+    int32_t *sums;
+    float *mean;
+    int32_t *acc, *counters;
+};
+
+static W1a1Pieces carve_w1a1(void *ws, int64_t in, int64_t out, size_t *bytes) {
+    Carver c{static_cast<char *>(ws)};
+    W1a1Pieces p{};
+    p.codes = c.take<int8_t>(kMaxTokens * bd_codes_ld(in));
+    p.sums = c.take<int32_t>(kMaxTokens);
+    p.mean = c.take<float>(kMaxTokens);
+    p.acc = c.take<int32_t>(2 * ((out + 15) / 16 * 16) * kMaxTokens);
+    p.counters = c.take<int32_t>((out + 15) / 16);
+    *bytes = c.off;
+    return p;
+}
+
+extern "C" size_t bd_projection_w1a1_workspace_bytes(int64_t in_features, int64_t out_features) {
+    size_t bytes = 0;
+    carve_w1a1(nullptr, in_features, out_features, &bytes);
+    return bytes;
+}
+
+static ProjArgs w1a1_args(const uint32_t *signs, int64_t in, int64_t out, const W1a1Pieces &w, int tokens) {
+    ProjArgs a{};
+    a.bits = signs;
+    a.rows = out;
+    a.cols = in;
+    a.ncp = (in + 255) / 256;
+    a.codes0 = w.codes;
+    a.csum0 = w.sums;
+    a.nparts = 1;
+    a.ld = a.ncp * 256;
+    a.tokens = tokens;
+    a.kgroups = 1;
+    a.row_scale = w.mean;
+    return a;
+}
+
+extern "C" int bd_projection_w1a1(const float *x, int tokens, int64_t in_features, int64_t out_features,
+                                  const uint32_t *signs_t16, const float *scale, float *y, int32_t *raw_dot,
+                                  void *workspace, size_t workspace_bytes, int32_t *flags, bd_stream_t stream) {
+    if (tokens < 0 || in_features < 1 || out_features < 1) return BD_ERR_INVALID;
+    if (tokens == 0) return BD_OK;
+    if (!x || !signs_t16 || !scale || !y) return BD_ERR_INVALID;
+    size_t need = 0;
+    const W1a1Pieces w = carve_w1a1(workspace, in_features, out_features, &need);
+    if (!workspace || need > workspace_bytes) return BD_ERR_WORKSPACE;
+    for (int t0 = 0; t0 < tokens; t0 += kMaxTokens) {
+        const int n = tokens - t0 < kMaxTokens ? tokens - t0 : kMaxTokens;
+        int st = launch_binarize(x + t0 * in_features, n, in_features, bd_codes_ld(in_features), w.codes, w.sums,
+                                 w.mean, nullptr, 0, flags, stream);
+        if (st) return st;
+        ProjArgs a = w1a1_args(signs_t16, in_features, out_features, w, n);
+        a.scale0 = scale;
+        a.out = y + t0 * out_features;
+        a.raw_dot = raw_dot ? raw_dot + t0 * out_features : nullptr;
+        a.acc = w.acc;
+        a.counters = w.counters;
+        a.flags = flags;
+        st = launch_proj(a, EPI_W1A1, stream);
+        if (st) return st;
+    }
+    return BD_OK;
+}
+
+extern "C" int bd_ffn_w1a1(const bd_ffn_w1_args *p, bd_stream_t stream) {
+    if (!p || p->tokens < 0 || p->hidden < 1 || p->inter < 1) return BD_ERR_INVALID;
+    if (p->tokens == 0) return BD_OK;
+    if (!p->x || !p->y || !p->signs_gate_up || !p->signs_down || !p->scale_gate || !p->scale_up || !p->scale_down)
+        return BD_ERR_INVALID;
+    size_t need = 0;
+    FfnPieces w = carve_ffn(p->workspace, p->hidden, p->inter, true, &need);
+    if (!p->workspace || need > p->workspace_bytes) return BD_ERR_WORKSPACE;
+    const int64_t ld_h = bd_codes_ld(p->hidden), ld_f = bd_codes_ld(p->inter);
+    for (int t0 = 0; t0 < p->tokens; t0 += kMaxTokens) {
+        const int n = p->tokens - t0 < kMaxTokens ? p->tokens - t0 : kMaxTokens;
+        float *hidden = p->hidden_out ? p->hidden_out + t0 * p->inter : w.hidden;
+        int st = launch_binarize(p->x + t0 * p->hidden, n, p->hidden, ld_h, w.codes_in, w.sum_in, w.scale_in,
+                                 nullptr, 0, p->flags, stream);
+        if (st) return st;
+        W1a1Pieces in{w.codes_in, w.sum_in, w.scale_in, nullptr, nullptr};
+        ProjArgs gu = w1a1_args(p->signs_gate_up, p->hidden, p->inter, in, n);
+        gu.scale0 = p->scale_gate;
+        gu.scale1 = p->scale_up;
+        gu.out = hidden;
+        gu.flags = p->flags;
+        st = launch_gateup(gu, EPI_W1A1, stream);
+        if (st) return st;
+        st = launch_binarize(hidden, n, p->inter, ld_f, w.codes_mid, w.sum_mid, w.scale_mid, nullptr, 0, p->flags,
+                             stream);
+        if (st) return st;
+        W1a1Pieces mid{w.codes_mid, w.sum_mid, w.scale_mid, w.acc, w.counters};
+        ProjArgs dn = w1a1_args(p->signs_down, p->inter, p->hidden, mid, n);
+        dn.scale0 = p->scale_down;
+        dn.out = p->y + t0 * p->hidden;
+        dn.acc = w.acc;
+        dn.counters = w.counters;
+        dn.flags = p->flags;
+        st = launch_proj(dn, EPI_W1A1, stream);
+        if (st) return st;
+    }
+    return BD_OK;
+}

@@ -18,6 +18,9 @@
 // grid_wait(), so the kernel that started early can rely on every kernel
 // before its predecessor having completed.  A kernel that writes sign tiles
 // (the optimizer's re-pack) never triggers early starts.
+#include <mutex>
+#include <unordered_map>
+
 #include "kernels.cuh"
 
 namespace bd {
@@ -422,21 +425,56 @@ static int ctas_per_sm(Kern kern, int64_t smem) {
     return n;
 }
 
+// Launch plans depend only on (device, shape); the occupancy queries behind
+// them cost microseconds each, so each launcher caches its plans.
+struct PlanCache {
+    std::mutex mu;
+    std::unordered_map<uint64_t, uint64_t> plans;
+    static uint64_t key(int64_t rows, int64_t ncp, bool split) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        return (static_cast<uint64_t>(rows) << 24) ^ (static_cast<uint64_t>(ncp) << 4) ^
+               (static_cast<uint64_t>(dev) << 1) ^ (split ? 1u : 0u);
+    }
+    bool get(uint64_t k, uint64_t &v) {
+        std::lock_guard<std::mutex> g(mu);
+        auto it = plans.find(k);
+        if (it == plans.end()) return false;
+        v = it->second;
+        return true;
+    }
+    void put(uint64_t k, uint64_t v) {
+        std::lock_guard<std::mutex> g(mu);
+        plans[k] = v;
+    }
+};
+
 template <int NT, int PLANES, int EPI>
 static int launch_gateup_t(const ProjArgs &a, cudaStream_t stream) {
     const int64_t npairs = (a.rows + 15) / 16;
     const int sms = sms_cached();
     auto kern = gateup_kernel<NT, PLANES, EPI>;
-    // fewest pairs per CTA such that all CTAs are resident at once
+    static PlanCache cache;
+    const uint64_t key = PlanCache::key(a.rows, a.ncp, false);
+    uint64_t cached = 0;
     int per = 0;
-    for (int p = 1; p <= 64; ++p) {
-        const Plan pl(2, NT * 8, PLANES, p, static_cast<int>(a.ncp));
-        const int occ = ctas_per_sm(kern, pl.total);
-        if (occ == 0) break;
-        per = p;
-        if (static_cast<int64_t>(p) * occ * sms >= npairs) break;
+    if (cache.get(key, cached)) {
+        per = static_cast<int>(cached);
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemLimit)) !=
+            cudaSuccess)
+            return BD_ERR_LAUNCH;
+    } else {
+        // fewest pairs per CTA such that all CTAs are resident at once
+        for (int p = 1; p <= 64; ++p) {
+            const Plan pl(2, NT * 8, PLANES, p, static_cast<int>(a.ncp));
+            const int occ = ctas_per_sm(kern, pl.total);
+            if (occ == 0) break;
+            per = p;
+            if (static_cast<int64_t>(p) * occ * sms >= npairs) break;
+        }
+        if (per == 0) return BD_ERR_INVALID;
+        cache.put(key, static_cast<uint64_t>(per));
     }
-    if (per == 0) return BD_ERR_INVALID;
     const Plan pl(2, NT * 8, PLANES, per, static_cast<int>(a.ncp));
     const unsigned grid = static_cast<unsigned>((npairs + per - 1) / per);
     return launch_pdl(kern, dim3(grid), dim3(kThreads), static_cast<size_t>(pl.total), stream, a, per);
@@ -454,7 +492,18 @@ static int launch_proj_t(const ProjArgs &a0, cudaStream_t stream) {
     int best_per = 0, best_kg = 1;
     double best_cost = 1e30;
     const int max_kg = a.acc && a.counters ? static_cast<int>(a.ncp) : 1;
-    for (int per = 1; per <= 16; ++per) {
+    static PlanCache cache;
+    const uint64_t key = PlanCache::key(a.rows, a.ncp, max_kg > 1);
+    uint64_t cached = 0;
+    const bool hit = cache.get(key, cached);
+    if (hit) {
+        best_per = static_cast<int>(cached >> 32);
+        best_kg = static_cast<int>(cached & 0xffffffffu);
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemLimit)) !=
+            cudaSuccess)
+            return BD_ERR_LAUNCH;
+    }
+    for (int per = 1; per <= 16 && !hit; ++per) {
         for (int kg = 1; kg <= max_kg; ++kg) {
             const int ncpc = static_cast<int>((a.ncp + kg - 1) / kg);
             const Plan pl(1, NT * 8, PLANES, per, ncpc);
@@ -472,6 +521,7 @@ static int launch_proj_t(const ProjArgs &a0, cudaStream_t stream) {
         }
     }
     if (best_per == 0) return BD_ERR_INVALID;
+    if (!hit) cache.put(key, (static_cast<uint64_t>(best_per) << 32) | static_cast<uint64_t>(best_kg));
     a.blocks_per_cta = best_per;
     a.kgroups = best_kg;
     const int ncpc_max = static_cast<int>((a.ncp + a.kgroups - 1) / a.kgroups);

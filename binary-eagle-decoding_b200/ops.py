@@ -264,6 +264,64 @@ def ffn_w1(x: Tensor, ffn: PackedFFN, hidden_out: bool = False, flags: Flags | N
     return (y, h) if hidden_out else y
 
 
+# --------------------------------------------------------------------------- W1A1
+
+
+def binarize_rows(x: Tensor, flags: Flags | None = None):
+    """Sign words (bit j of word w = ``x[r, 32w+j] >= 0``) and fixed-order mean|x| per row."""
+    device = _require_cuda(x)
+    if x.dtype != torch.float32 or x.ndim != 2:
+        raise ValueError("binarize_rows takes F32 [rows, cols]")
+    rows, cols = x.shape
+    words = torch.empty((rows, (cols + 31) // 32), dtype=torch.int32, device=device)
+    mean = torch.empty(rows, dtype=torch.float32, device=device)
+    own = flags is None
+    flags = flags or Flags(device)
+    _lib.call("bd_binarize_rows", _p(x), rows, cols, _p(words), _p(mean), flags.ptr, _stream(device))
+    if own:
+        flags.check()
+    return words, mean
+
+
+def projection_w1a1(x: Tensor, signs_t16: Tensor, scale: Tensor, raw_dot: bool = False,
+                    flags: Flags | None = None):
+    """W1A1 projection ``(D * scale[o]) * mean|x_t|`` with the exact +-1 dot D."""
+    device = _require_cuda(x, signs_t16, scale)
+    tokens, in_features = x.shape
+    out_features = scale.shape[0]
+    y = torch.empty((tokens, out_features), dtype=torch.float32, device=device)
+    raw = torch.empty((tokens, out_features), dtype=torch.int32, device=device) if raw_dot else None
+    nbytes = int(_lib.load().bd_projection_w1a1_workspace_bytes(in_features, out_features))
+    ws = workspace(device, "w1a1", nbytes)
+    own = flags is None
+    flags = flags or Flags(device)
+    _lib.call("bd_projection_w1a1", _p(x), tokens, in_features, out_features, _p(signs_t16), _p(scale), _p(y),
+              _p(raw), _p(ws), ws.numel(), flags.ptr, _stream(device), kernels=2 * ((tokens + 31) // 32))
+    if own:
+        flags.check()
+    return (y, raw) if raw_dot else y
+
+
+def ffn_w1a1(x: Tensor, ffn: PackedFFN, hidden_out: bool = False, flags: Flags | None = None):
+    """W1A1 SwiGLU: each projection input is re-binarised with its own mean|x|."""
+    device = _require_cuda(x)
+    tokens = x.shape[0]
+    y = torch.empty((tokens, ffn.hidden), dtype=torch.float32, device=device)
+    h = torch.empty((tokens, ffn.inter), dtype=torch.float32, device=device) if hidden_out else None
+    nbytes = int(_lib.load().bd_ffn_workspace_bytes(MAX_DECODE_TOKENS, ffn.hidden, ffn.inter))
+    ws = workspace(device, "ffn", nbytes)
+    own = flags is None
+    flags = flags or Flags(device)
+    args = _lib.FfnW1Args(
+        _p(x), _p(y), tokens, ffn.hidden, ffn.inter, _p(ffn.signs_gate_up), _p(ffn.scale_gate), _p(ffn.scale_up),
+        _p(ffn.signs_down), _p(ffn.scale_down), _p(h), _p(ws), ws.numel(), flags.ptr,
+    )
+    _lib.call("bd_ffn_w1a1", _lib.ctypes.byref(args), _stream(device), kernels=4 * ((tokens + 31) // 32))
+    if own:
+        flags.check()
+    return (y, h) if hidden_out else y
+
+
 # --------------------------------------------------------------------------- acceptance
 
 

@@ -149,6 +149,30 @@ typedef struct {
 } bd_ffn_w1_args;
 int bd_ffn_w1(const bd_ffn_w1_args *args, bd_stream_t stream);
 
+/* ====================================================================== W1A1
+ * Sign-binarised activations against one-bit weights.  The reference has no
+ * W1A1 module; its export rule string
+ * "signed_pm_bound_threshold0_nonnegative_positive_zero_row_scale0"
+ * (w1a1_eagle/numerical/export.py:145) fixes the sign rule x >= 0 -> +1 and a
+ * per-token scale mean|x|, summed in a fixed order (lane l of 256 adds
+ * |x[l + 256 i]| sequentially, then a balanced tree of adjacent pairs).
+ *
+ * bd_binarize_rows: GGUF-style sign words of x (bit j of word w of row r =
+ * x[r, 32w+j] >= 0, padding 0; export.py:79-86 layout) and mean|x| per row. */
+int bd_binarize_rows(const float *x, int64_t rows, int64_t cols, uint32_t *words, float *mean_abs,
+                     int32_t *flags, bd_stream_t stream);
+/* One W1A1 projection y[t,o] = (D[t,o] * scale[o]) * mean|x_t|, with the exact
+ * +-1 dot D = K - 2 popc(sign_bits(x_t) ^ sign_bits(W_o)) (raw_dot optional).
+ * signs: T16 [out, in].  Any token count (32-token chunks). */
+size_t bd_projection_w1a1_workspace_bytes(int64_t in_features, int64_t out_features);
+int bd_projection_w1a1(const float *x, int tokens, int64_t in_features, int64_t out_features,
+                       const uint32_t *signs_t16, const float *scale, float *y, int32_t *raw_dot,
+                       void *workspace, size_t workspace_bytes, int32_t *flags, bd_stream_t stream);
+/* W1A1 SwiGLU: every projection input is re-binarised with its own mean|x|:
+ *   y = W1A1_down(silu(W1A1_gate(x)) * W1A1_up(x)).
+ * Same argument block as bd_ffn_w1; workspace bd_ffn_workspace_bytes. */
+int bd_ffn_w1a1(const bd_ffn_w1_args *args, bd_stream_t stream);
+
 /* ================================================================== acceptance
  * Greedy block acceptance (benchmarks/verifier.py:92-137 core loop 107-113,
  * argmax rule w1a1_eagle/contracts.py:130-137 and native/verifier-trace.hpp:28-34):

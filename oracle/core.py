@@ -320,9 +320,9 @@ def w1a1_projection(x, latent, scale):
     """
     x = _f32(x)
     s = fixed_mean_abs(x)
-    xs = np.where(x >= 0, 1, -1).astype(np.int64)
-    ws = np.where(_f32(latent) >= 0, 1, -1).astype(np.int64)
-    dot = xs @ ws.T
+    xs = np.where(x >= 0, 1.0, -1.0)
+    ws = np.where(_f32(latent) >= 0, 1.0, -1.0)
+    dot = (xs @ ws.T).astype(np.int64)  # float64 BLAS: +-1 sums below 2^53 are exact
     out = (dot.astype(np.float32) * _f32(scale)) * s[:, None]
     return out.astype(np.float32), dot, s
 
