@@ -8,3 +8,5 @@ The model/config API mirrors ``w1a1_eagle.model`` of the reference
 """
 
 from . import _lib, ops  # noqa: F401
+from .model import (HE4, FrozenLinear, Geometry, Layer, Projection, bound_latents, cache_storage,  # noqa: F401
+                    clamp_latents, hard_sign, rms, rope)

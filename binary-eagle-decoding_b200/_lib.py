@@ -25,6 +25,7 @@ FLAG_NONFINITE_LOGITS = 8
 FLAG_BAD_TOKEN = 16
 FLAG_NONFINITE_STATE = 32
 FLAG_CACHE_OVERFLOW = 64
+FLAG_SIGN_CHANGE = 128
 
 # Messages of the reference's ValueErrors for the same conditions.
 FLAG_MESSAGES = (
@@ -35,6 +36,7 @@ FLAG_MESSAGES = (
     (FLAG_BAD_TOKEN, "draft token outside the vocabulary"),
     (FLAG_NONFINITE_STATE, "nonfinite drafter state"),
     (FLAG_CACHE_OVERFLOW, "F16 cache storage overflow"),
+    (FLAG_SIGN_CHANGE, "bounded latent scale changed a sign"),
 )
 
 
@@ -76,6 +78,24 @@ SIGNATURES = {
     "bd_projection_w1a1_workspace_bytes": (c_size_t, [c_int64, c_int64]),
     "bd_projection_w1a1": (c_int, [P, c_int, c_int64, c_int64, P, P, P, P, P, c_size_t, P, P]),
     "bd_ffn_w1a1": (c_int, [ctypes.POINTER(FfnW1Args), P]),
+    "bd_quantize_rows_bf16": (c_int, [P, c_int64, c_int64, P, P, c_int, P, P, P, P]),
+    "bd_sign_rows": (c_int, [P, c_int64, P, P, P, P]),
+    "bd_he4_epilogue": (c_int, [P, c_int64, c_int64, P, P, P, c_int, P, P, P, P]),
+    "bd_ste_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64]),
+    "bd_ste_grad_prep": (c_int, [P, P, c_int64, c_int64, P, P, P, c_int, P, P, P, P, P, P, P, c_size_t, P]),
+    "bd_ste_input_backward": (c_int, [P, P, P, P, c_int64, c_int64, P, P, c_int, P, P, P, c_int, P, c_size_t,
+                                      P]),
+    "bd_ste_sumsq_count": (c_int, [c_int64]),
+    "bd_ste_sign_backward": (c_int, [P, P, P, c_int64, ctypes.c_float, P, c_int, P, P, P]),
+    "bd_sum_squares_count": (c_int, [c_int64]),
+    "bd_sum_squares": (c_int, [P, c_int64, P, P]),
+    "bd_grad_norm": (c_int, [P, c_int64, ctypes.c_float, P, P, P, P]),
+    "bd_adamw_latent": (c_int, [P, P, P, P, c_int64, c_int64, ctypes.c_double, ctypes.c_double, ctypes.c_double,
+                                ctypes.c_double, ctypes.c_longlong, P, c_int, P, c_int, c_int, P, P]),
+    "bd_adamw": (c_int, [P, P, P, P, c_int64, ctypes.c_double, ctypes.c_double, ctypes.c_double, ctypes.c_double,
+                         ctypes.c_longlong, P, ctypes.c_float, P, P]),
+    "bd_bound_latents": (c_int, [P, c_int64, c_int64, ctypes.c_float, P, P, P]),
+    "bd_clamp": (c_int, [P, c_int64, ctypes.c_float, ctypes.c_float, P]),
     "bd_accept_workspace_bytes": (c_size_t, [c_int, c_int]),
     "bd_accept_greedy": (c_int, [P, c_int, c_int, c_int64, P, P, c_int, P, P, P, P, c_size_t, P, P]),
     "bd_accept_greedy_noalloc": (c_int, [P, c_int, c_int, c_int64, P, P, c_int, P, P, P, P, P]),
@@ -129,7 +149,8 @@ def load() -> ctypes.CDLL:
 
 
 # Kernel launches issued by each entry point (for launch accounting).
-KERNELS_PER_CALL = {"bd_ffn_he4": 3, "bd_ffn_w1": 4, "bd_attention_decode": 2, "bd_accept_rejection": 2}
+KERNELS_PER_CALL = {"bd_ffn_he4": 3, "bd_ffn_w1": 4, "bd_attention_decode": 2, "bd_accept_rejection": 2,
+                    "bd_ste_grad_prep": 2, "bd_ste_input_backward": 2}
 launches = 0
 
 

@@ -1,0 +1,300 @@
+"""QAT update of the binary drafter (``w1a1_eagle/numerical/worker.py:300-392``).
+
+One update is: the windows' hidden states (``HE4.group_hidden``), the weighted
+cross-entropy of the drafted positions against the frozen vocabulary head in
+128-row chunks (``group_loss``), the straight-through backward of the binary
+projections (kernels in ``csrc/ste.cu``), an optional data-parallel gradient
+average (NCCL all-reduce of flat buckets), the global gradient-norm clip, and
+the fused AdamW + sign re-pack (``csrc/optim.cu``).
+
+``Optimization``, ``Schedule``, ``PARAMETER_GROUPS`` and ``label_weights``
+restate ``w1a1_eagle/training.py:8, 108-170`` and ``worker.py:41-50``.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+import torch.distributed as dist
+from torch import Tensor, nn
+
+from . import _lib, ops
+from .model import HE4, Projection, _bump, _need_cuda, _stream
+
+PARAMETER_GROUPS = ("sign", "scale", "midpoint", "gain", "clip", "norm")
+HEAD_ROWS = 128
+SUFFIX_GROUPS = {"latent_sign": "sign", "scale": "scale", "midpoint": "midpoint", "log_gain": "gain",
+                 "log_clip": "clip"}
+
+
+def default_step_sizes() -> dict[str, float]:
+    """Per-group AdamW step sizes (``training.py:108-109``)."""
+    return {"sign": 1e-3, "scale": 1e-5, "midpoint": 1e-5, "gain": 1e-5, "clip": 1e-5, "norm": 1e-5}
+
+
+@dataclass(frozen=True)
+class Schedule:
+    """Step-size multiplier: linear warm-up, then constant or cosine (``training.py:113-148``)."""
+
+    decay: str = "constant"
+    warmup_updates: int = 0
+    start_update: int = 0
+    final_update: int | None = None
+
+    def __post_init__(self) -> None:
+        if self.decay not in ("constant", "cosine"):
+            raise ValueError("schedule decay must be constant or cosine")
+        if any(type(v) is not int or v < 0 for v in (self.warmup_updates, self.start_update)):
+            raise ValueError("schedule start and warm-up must be nonnegative update counts")
+        if self.decay == "constant" and self.final_update is not None:
+            raise ValueError("a constant schedule has no final update")
+        if self.decay == "cosine" and (type(self.final_update) is not int
+                                       or self.final_update <= self.start_update + self.warmup_updates):
+            raise ValueError("cosine decay requires a final update after its warm-up")
+
+    def multiplier(self, updates: int) -> float:
+        if type(updates) is not int or updates < self.start_update:
+            raise ValueError("update precedes the schedule start")
+        elapsed = updates - self.start_update
+        if elapsed < self.warmup_updates:
+            return (elapsed + 1) / self.warmup_updates
+        if self.final_update is None:
+            return 1.0
+        span = self.final_update - self.start_update - self.warmup_updates
+        progress = (elapsed - self.warmup_updates) / span
+        if progress >= 1:
+            raise ValueError("update is at or beyond the schedule's final update")
+        return 0.5 * (1 + math.cos(math.pi * progress))
+
+
+@dataclass(frozen=True)
+class Optimization:
+    """Step sizes per group, schedule and the optional latent bound (``training.py:151-170``)."""
+
+    step_sizes: dict[str, float] = field(default_factory=default_step_sizes)
+    schedule: Schedule = Schedule()
+    latent_multiple: float | None = None
+
+    def __post_init__(self) -> None:
+        if tuple(sorted(self.step_sizes)) != tuple(sorted(PARAMETER_GROUPS)) or any(
+                type(v) is not float or not math.isfinite(v) or v <= 0 for v in self.step_sizes.values()):
+            raise ValueError("positive finite step sizes required for every parameter group")
+        if self.latent_multiple is not None and (type(self.latent_multiple) is not float
+                                                 or not math.isfinite(self.latent_multiple)
+                                                 or self.latent_multiple <= 0):
+            raise ValueError("bounded latent scale requires a positive finite multiple")
+
+
+def label_weights(lengths: tuple[int, ...], positions: tuple[float, ...] | None = None) -> Tensor:
+    """Per-label weights: ``exp(-i/7)`` (or the given position weights), normalised per
+    window and divided by the window count (``worker.py:41-50``)."""
+    parts = []
+    for length in lengths:
+        w = (torch.exp(-torch.arange(length) / 7) if positions is None
+             else torch.tensor(positions[:length], dtype=torch.float32))
+        parts.append(w / w.sum() / len(lengths))
+    return torch.cat(parts)
+
+
+def parameter_groups(model: nn.Module) -> dict[str, list[tuple[str, nn.Parameter]]]:
+    """Trainable parameters by group, keyed on the name suffix (``worker.py:111-121``)."""
+    groups: dict[str, list[tuple[str, nn.Parameter]]] = {key: [] for key in PARAMETER_GROUPS}
+    for name, parameter in model.named_parameters():
+        if parameter.requires_grad:
+            groups[SUFFIX_GROUPS.get(name.rsplit(".", 1)[-1], "norm")].append((name, parameter))
+    return groups
+
+
+# --------------------------------------------------------------------------- gradient norm
+
+
+def clip_grad_norm(parameters, max_norm: float = 1.0) -> tuple[Tensor, Tensor]:
+    """Global L2 norm of the gradients and the clip coefficient ``min(1, max / (norm + 1e-6))``
+    (``torch.nn.utils.clip_grad_norm_``, ``worker.py:372``), both device scalars.
+
+    The gradients are not rescaled here: the optimizer applies the coefficient as
+    it reads them.  A non-finite norm raises ``ValueError`` like ``error_if_nonfinite``.
+    """
+    grads = [p.grad for p in parameters if p.grad is not None]
+    if not grads:
+        raise ValueError("no gradients to clip")
+    device = _need_cuda(grads[0])
+    lib = _lib.load()
+    counts = [int(lib.bd_sum_squares_count(g.numel())) for g in grads]
+    partials = torch.empty(sum(counts), dtype=torch.float32, device=device)
+    stream = _stream(device)
+    offset = 0
+    for g, n in zip(grads, counts):
+        gc = g.contiguous()
+        _lib.call("bd_sum_squares", gc.data_ptr(), gc.numel(), partials.data_ptr() + 4 * offset, stream)
+        offset += n
+    total = torch.empty(1, dtype=torch.float32, device=device)
+    coef = torch.empty(1, dtype=torch.float32, device=device)
+    flags = ops.Flags(device)
+    _lib.call("bd_grad_norm", partials.data_ptr(), partials.numel(), float(max_norm), total.data_ptr(),
+              coef.data_ptr(), flags.ptr, stream)
+    if int(flags.tensor.item()):
+        raise ValueError("non-finite total norm of gradients")
+    return total, coef
+
+
+# --------------------------------------------------------------------------- optimizer
+
+
+class BitAdamW:
+    """``torch.optim.AdamW(groups, weight_decay=0, fused=True)`` over the drafter's
+    parameter groups (``worker.py:122-130``), with the post-step clamps of
+    ``worker.py:377-382`` fused in: ``scale`` is clamped at 0, latents optionally to
+    [-1, 1], and each latent's new signs are re-packed into its projection's T16
+    cache in the same pass."""
+
+    def __init__(self, model: nn.Module, optimization: Optimization | None = None, betas=(0.9, 0.999),
+                 eps: float = 1e-8) -> None:
+        self.model = model
+        self.optimization = optimization or Optimization()
+        self.betas = betas
+        self.eps = eps
+        self.groups = parameter_groups(model)
+        self.owner = {id(m.latent_sign): m for m in model.modules() if isinstance(m, Projection)}
+        self.state: dict[int, dict] = {}
+        self.lr = dict(self.optimization.step_sizes)
+
+    def zero_grad(self) -> None:
+        for params in self.groups.values():
+            for _, p in params:
+                p.grad = None
+
+    def set_multiplier(self, multiplier: float) -> None:
+        self.lr = {k: v * multiplier for k, v in self.optimization.step_sizes.items()}
+
+    @torch.no_grad()
+    def step(self, clip_coef: Tensor | None = None) -> None:
+        clamp = self.optimization.latent_multiple is not None
+        flags = None
+        for group, params in self.groups.items():
+            lr = float(self.lr[group])
+            for _, p in params:
+                if p.grad is None:
+                    continue
+                device = _need_cuda(p)
+                flags = flags or ops.Flags(device)
+                st = self.state.get(id(p))
+                if st is None:
+                    st = {"step": 0, "exp_avg": torch.zeros_like(p), "exp_avg_sq": torch.zeros_like(p)}
+                    self.state[id(p)] = st
+                st["step"] += 1
+                grad = p.grad.contiguous()
+                coef = None if clip_coef is None else clip_coef.data_ptr()
+                owner = self.owner.get(id(p))
+                stream = _stream(device)
+                if owner is not None:
+                    tiled = torch.zeros(ops.t16_words(*p.shape), dtype=torch.int32, device=device)
+                    _lib.call("bd_adamw_latent", p.data_ptr(), grad.data_ptr(), st["exp_avg"].data_ptr(),
+                              st["exp_avg_sq"].data_ptr(), p.shape[0], p.shape[1], lr, self.betas[0], self.betas[1],
+                              self.eps, st["step"], coef, int(clamp), tiled.data_ptr(), 1, 0, flags.ptr, stream)
+                    _bump(p)
+                    owner.adopt_t16(tiled)
+                else:
+                    lower = 0.0 if group == "scale" else -math.inf
+                    _lib.call("bd_adamw", p.data_ptr(), grad.data_ptr(), st["exp_avg"].data_ptr(),
+                              st["exp_avg_sq"].data_ptr(), p.numel(), lr, self.betas[0], self.betas[1], self.eps,
+                              st["step"], coef, lower, flags.ptr, stream)
+                    _bump(p)
+        if flags is not None and int(flags.tensor.item()):
+            raise ValueError("nonfinite post-update state")
+
+
+# --------------------------------------------------------------------------- data parallel
+
+
+def average_gradients(parameters, group=None, bucket_bytes: int = 256 << 20) -> None:
+    """Average gradients over the process group with NCCL all-reduces of flat fp32
+    buckets (sum, then divide by the world size), in parameter order."""
+    if not dist.is_available() or not dist.is_initialized():
+        return
+    world = dist.get_world_size(group)
+    if world == 1:
+        return
+    grads = [p.grad for p in parameters if p.grad is not None]
+    bucket: list[Tensor] = []
+    size = 0
+
+    def flush() -> None:
+        nonlocal bucket, size
+        if not bucket:
+            return
+        flat = torch.cat([g.reshape(-1) for g in bucket])
+        dist.all_reduce(flat, group=group)
+        flat.div_(world)
+        offset = 0
+        for g in bucket:
+            n = g.numel()
+            g.copy_(flat[offset:offset + n].view_as(g))
+            offset += n
+        bucket, size = [], 0
+
+    for g in grads:
+        bucket.append(g)
+        size += g.numel() * 4
+        if size >= bucket_bytes:
+            flush()
+    flush()
+
+
+# --------------------------------------------------------------------------- one update
+
+
+@dataclass(frozen=True)
+class Window:
+    """One supervised window: the anchor position and the labels of its drafted slots."""
+
+    anchor: int
+    labels: tuple[int, ...]
+
+
+def group_loss(model: HE4, features: Tensor, tokens: tuple[int, ...], windows: tuple[Window, ...],
+               slots: int | None = None, positions: tuple[float, ...] | None = None) -> Tensor:
+    """Weighted cross-entropy of the drafted positions (``worker.py:315-363``); runs the
+    backward of the vocabulary head in 128-row chunks, then through the drafter."""
+    if not windows or any(not w.labels for w in windows):
+        raise ValueError("an update requires supervised windows")
+    device = model.vocabulary.device
+    size = model.block(slots)
+    if size < 2:
+        raise ValueError("an update requires at least one drafted position")
+    hidden = model.group_hidden(features, tokens, tuple(w.anchor for w in windows), size)
+    lengths = tuple(min(len(w.labels), size - 1) for w in windows)
+    rows = torch.tensor([i * size + 1 + o for i, n in enumerate(lengths) for o in range(n)], device=device)
+    labels = torch.tensor([l for w, n in zip(windows, lengths) for l in w.labels[:n]], dtype=torch.int64,
+                          device=device)
+    weights = label_weights(lengths, positions).to(device)
+    selected = hidden.view(-1, hidden.shape[-1]).index_select(0, rows)
+    head = selected.detach().requires_grad_()
+    total = torch.zeros((), device=device)
+    for start in range(0, labels.numel(), HEAD_ROWS):
+        end = start + HEAD_ROWS
+        logits = torch.nn.functional.linear(head[start:end], model.vocabulary)
+        losses = torch.nn.functional.cross_entropy(logits, labels[start:end], reduction="none")
+        loss = (losses * weights[start:end]).sum()
+        torch.autograd.backward(loss)
+        total = total + loss.detach()
+    if not bool(torch.isfinite(total)) or head.grad is None:
+        raise ValueError("nonfinite loss")
+    torch.autograd.backward(selected, head.grad)
+    return total
+
+
+def update(model: HE4, optimizer: BitAdamW, features: Tensor, tokens: tuple[int, ...], windows: tuple[Window, ...],
+           updates: int = 0, slots: int | None = None, group=None) -> tuple[float, float]:
+    """One QAT update (``worker.py:365-392``).  Returns ``(loss, gradient norm)``; with an
+    initialised process group the gradients are averaged across ranks first."""
+    optimizer.zero_grad()
+    loss = group_loss(model, features, tokens, windows, slots)
+    params = [p for ps in optimizer.groups.values() for _, p in ps]
+    average_gradients(params, group)
+    norm, coef = clip_grad_norm(params, 1.0)
+    optimizer.set_multiplier(optimizer.optimization.schedule.multiplier(updates))
+    optimizer.step(coef)
+    return float(loss), float(norm)

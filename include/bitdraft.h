@@ -43,6 +43,7 @@ typedef struct CUstream_st *bd_stream_t; /* == cudaStream_t */
 #define BD_FLAG_BAD_TOKEN 16u         /* a draft token outside [0, vocab) */
 #define BD_FLAG_NONFINITE_STATE 32u   /* non-finite values in a forward / update */
 #define BD_FLAG_CACHE_OVERFLOW 64u    /* model.py:100-101 "F16 cache storage overflow" */
+#define BD_FLAG_SIGN_CHANGE 128u      /* model.py:162-163 "bounded latent scale changed a sign" */
 
 int bd_abi_version(void);
 const char *bd_status_string(int status);
@@ -57,7 +58,8 @@ int bd_device_info(int *sm_count, int *major, int *minor);
 int bd_pack_signs(const float *latent, int64_t rows, int64_t cols, int32_t *words,
                   int32_t *flags, bd_stream_t stream);
 
-/* T16 tiled sign layout used by the decode kernels (see DESIGN: "T16").  Words:
+/* T16 tiled sign layout used by the decode kernels (512-byte units of 16 rows by
+ * 256 columns, each lane's 16 bytes its m16n8k32 A-fragment bits).  Words:
  * bd_t16_words(rows, cols) uint32.  `block_stride`/`block_offset` interleave
  * several matrices' 16-row blocks into one buffer (stride 2, offset 0/1 puts
  * gate and up row blocks side by side); pass 1/0 for a plain matrix.  Replaces
@@ -279,6 +281,79 @@ size_t bd_attention_workspace_bytes(int heads, int head_dim, int keys);
 int bd_attention_decode(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache, int tokens, int heads,
                         int kv_heads, int head_dim, int keys, int windowed, int64_t anchor, int64_t window,
                         float *out, void *workspace, size_t workspace_bytes, bd_stream_t stream);
+
+/* ================================================================ QAT (training sizes)
+ * Projection.forward at any token count (w1a1_eagle/model.py:128-150): codes and
+ * +-1 signs are exact in bf16, so D = codes . signs^T is an exact bf16
+ * tensor-core GEMM with fp32 output (issued by the caller's GEMM, e.g. cuBLAS);
+ * these kernels produce its operands and apply the epilogue.
+ * bd_quantize_rows_bf16: codes bf16 [rows, cols] row-major and exact row sums
+ *   (model.py:128-139; gain and bound already exponentiated).
+ * bd_sign_rows: hard_sign (model.py:66-68, 92-95) of n latents as bf16 and/or
+ *   fp32 +-1 (x >= 0 -> +1).
+ * bd_he4_epilogue: y = (D * max(scale,0)) * step + (sums * step) * midpoint
+ *   (+ residual), D fp32 [tokens, out] holding exact integers. */
+int bd_quantize_rows_bf16(const float *x, int64_t rows, int64_t cols, const float *gain, const float *bound,
+                          int bits, uint16_t *codes, int32_t *code_sums, int32_t *flags, bd_stream_t stream);
+int bd_sign_rows(const float *latent, int64_t n, uint16_t *signs_bf16, float *signs_f32, int32_t *flags,
+                 bd_stream_t stream);
+int bd_he4_epilogue(const float *dot, int64_t tokens, int64_t out_features, const float *scale,
+                    const float *midpoint, const float *bound, int bits, const int32_t *code_sums,
+                    const float *residual, float *y, bd_stream_t stream);
+
+/* Straight-through backward of one projection (autograd of model.py:128-150
+ * with SIGN's backward, model.py:71-73).  With G = dLoss/dy [tokens, out]:
+ * bd_ste_grad_prep: dL = G * max(scale,0) split into bf16 hi + lo [tokens, out];
+ *   d_scale[o] = sum_t G (D step) * (scale >= 0); d_midpoint[o] = sum_t G (sums step);
+ *   gm[t] = sum_o G midpoint[o].  The caller then forms d_values = dL . signs
+ *   (hi and lo GEMMs, fp32) and d_signs = dL^T . codes.
+ * bd_ste_input_backward: the quantizer's backward (clip ties split 0.5/0.5):
+ *   dx [tokens, in], d_log_gain[in] and d_log_clip (scalar; both added to the
+ *   existing values when accumulate != 0, as for gate and up sharing them).
+ * bd_ste_sign_backward: out = ((grad + grad2) * step) * 1[|latent| <= window]
+ *   (step = bound / max when bound != NULL, else 1), with per-block sums of
+ *   squares (bd_ste_sumsq_count(n) of them) for the gradient-norm clip.
+ * Workspace: bd_ste_workspace_bytes(tokens, out, in).  Reductions are in a fixed
+ * order, so results are deterministic. */
+size_t bd_ste_workspace_bytes(int64_t tokens, int64_t out_features, int64_t in_features);
+int bd_ste_grad_prep(const float *grad, const float *dot, int64_t tokens, int64_t out_features, const float *scale,
+                     const float *midpoint, const float *bound, int bits, const int32_t *code_sums,
+                     uint16_t *dl_hi, uint16_t *dl_lo, float *d_scale, float *d_midpoint, float *gm,
+                     void *workspace, size_t workspace_bytes, bd_stream_t stream);
+int bd_ste_input_backward(const float *d_values, const float *d_values2, const float *gm, const float *x,
+                          int64_t tokens, int64_t in_features, const float *gain, const float *bound, int bits,
+                          float *dx, float *d_log_gain, float *d_log_clip, int accumulate, void *workspace,
+                          size_t workspace_bytes, bd_stream_t stream);
+int bd_ste_sumsq_count(int64_t n);
+int bd_ste_sign_backward(const float *grad, const float *grad2, const float *latent, int64_t n, float window,
+                         const float *bound, int bits, float *out, float *sumsq_partials, bd_stream_t stream);
+
+/* The update (w1a1_eagle/numerical/worker.py:365-392): clip_grad_norm_(1.0),
+ * AdamW(weight_decay=0, fused=True) per parameter group, scale.clamp_(min=0),
+ * optional clamp_latents (model.py:167-169).
+ * bd_sum_squares / bd_grad_norm: fixed-order sum of squares partials, then
+ *   total = sqrt(sum), clip_coef = min(1, max_norm / (total + 1e-6)).
+ * bd_adamw_latent: AdamW of a latent matrix [rows, cols] fused with the clamp and
+ *   the re-pack of its signs into T16 words (block_stride/offset as
+ *   bd_tile_signs_t16; signs_t16 may be NULL).  bd_adamw: element AdamW with a
+ *   lower clamp (-INFINITY for none).  clip_coef (device scalar) may be NULL.
+ * bd_bound_latents: out = clamp(latent / (multiple mean|row|), -1, 1)
+ *   (model.py:153-164); BD_FLAG_SIGN_CHANGE if a sign would change.
+ * bd_clamp: x = min(max(x, lo), hi). */
+int bd_sum_squares_count(int64_t n);
+int bd_sum_squares(const float *x, int64_t n, float *partials, bd_stream_t stream);
+int bd_grad_norm(const float *partials, int64_t count, float max_norm, float *total_norm, float *clip_coef,
+                 int32_t *flags, bd_stream_t stream);
+int bd_adamw_latent(float *param, const float *grad, float *exp_avg, float *exp_avg_sq, int64_t rows, int64_t cols,
+                    double lr, double beta1, double beta2, double eps, long long step, const float *clip_coef,
+                    int clamp_latents, uint32_t *signs_t16, int block_stride, int block_offset, int32_t *flags,
+                    bd_stream_t stream);
+int bd_adamw(float *param, const float *grad, float *exp_avg, float *exp_avg_sq, int64_t n, double lr, double beta1,
+             double beta2, double eps, long long step, const float *clip_coef, float lower, int32_t *flags,
+             bd_stream_t stream);
+int bd_bound_latents(const float *latent, int64_t rows, int64_t cols, float multiple, float *out, int32_t *flags,
+                     bd_stream_t stream);
+int bd_clamp(float *x, int64_t n, float lo, float hi, bd_stream_t stream);
 
 #ifdef __cplusplus
 }
