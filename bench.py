@@ -39,6 +39,8 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "drafted tokens/s/GPU (block-16 HE4 drafter)"
 UNIT = "drafted tokens/s"
+# DRAM bytes of one LM-head GEMV launch measured by ncu (read 778.10 MB + write 3.31 MB)
+LM_HEAD_DRAM_BYTES = 781_410_000
 GEOMETRY = dict(hidden=2560, intermediate=9728, heads=32, kv_heads=8, head_dim=128, layers=4, slots=16, taps=4,
                 window=4096, epsilon=1e-6, theta=1e6)
 VOCAB = 151936
@@ -335,7 +337,9 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
         "config": workload_config(),
         "roofline": {"bound": "hbm", "kernel": "gemv_kernel (tied LM head, 151936x2560 bf16, 16 tokens, fused argmax)",
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_source": f"{peak_kind} HBM copy bandwidth", "traffic": None,
+                     "peak_source": f"{peak_kind} HBM copy bandwidth", "traffic": LM_HEAD_DRAM_BYTES,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one LM-head launch "
+                                       "(profiles/gemv_lm_head.md)",
                      "algorithmic_bytes_per_launch": head_bytes, "launch_us": head_us},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": rnd.h2d_bytes,
                 "d2h_bytes_per_step": rnd.d2h_bytes, "ms_per_step": e2e_ms},
@@ -372,6 +376,177 @@ def profile_round() -> None:
     print("profiled one draft round")
 
 
+# --------------------------------------------------------------------------- other workloads (one GPU)
+# The headline is the draft round above; these lines measure the other hot-path
+# workloads on their own shapes (single binary FFN block, W1A1 at M = 1024,
+# block acceptance, the QAT update) for the kernel summaries.
+
+
+def _events_us(fn, reps: int) -> float:
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st.record()
+    for _ in range(reps):
+        fn()
+    en.record()
+    torch.cuda.synchronize()
+    return st.elapsed_time(en) * 1e3 / reps
+
+
+def _graph_us(fn, calls: int, reps: int) -> float:
+    """Capture `calls` invocations of fn(i) in one CUDA graph; time its replays."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for i in range(3):
+            fn(i)
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(calls):
+            fn(i)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    return _events_us(graph.replay, reps) / calls
+
+
+def workload_ffn(args, pkg, device) -> list[dict]:
+    """Config 1: one binary SwiGLU block, 16 tokens, 2560 -> 9728 -> 2560 (HE4, pure-W1, W1A1)."""
+    ops = pkg.ops
+    H, F, T = 2560, 9728, 16
+    sets = 16  # 16 x 9.34 MB of sign tiles rotate through the graph: more than L2
+    g = torch.Generator(device=device).manual_seed(0)
+    ffns = []
+    for _ in range(sets):
+        gate, up, down = (torch.randn(s, generator=g, device=device) * 0.02 for s in ((F, H), (F, H), (H, F)))
+        f = ops.pack_ffn(gate, up, down)
+        f.midpoint_gate, f.midpoint_up = torch.zeros(F, device=device), torch.zeros(F, device=device)
+        f.midpoint_down = torch.zeros(H, device=device)
+        f.gain_gate_up, f.gain_down = torch.ones(H, device=device), torch.ones(F, device=device)
+        f.bound_gate_up, f.bound_down = torch.ones(1, device=device), torch.ones(1, device=device)
+        ffns.append(f)
+    x = torch.randn((T, H), generator=g, device=device)
+    flags = ops.Flags(device)
+    algorithmic = 3 * F * H // 8 + (2 * F + H) * 4 + 2 * T * H * 4
+    lines = []
+    for mode, fn in (("he4", lambda i: ops.ffn_he4(x, ffns[i % sets], flags=flags)),
+                     ("w1", lambda i: ops.ffn_w1(x, ffns[i % sets], flags=flags)),
+                     ("w1a1", lambda i: ops.ffn_w1a1(x, ffns[i % sets], flags=flags))):
+        us = _graph_us(fn, sets, max(args.steps // 40, 20))
+        lines.append({"workload": f"binary SwiGLU FFN block ({mode}), 16 tokens, 2560x9728x2560",
+                      "metric": "packed-FFN HBM GB/s", "value": algorithmic / (us * 1e-6) / 1e9, "unit": "GB/s",
+                      "us_per_ffn": us, "algorithmic_bytes": algorithmic, "timing": "CUDA graph of 16 blocks over "
+                      "16 weight sets (150 MB > L2), CUDA events"})
+    flags.check()
+    return lines
+
+
+def workload_w1a1(args, pkg, device) -> list[dict]:
+    """Config 3: W1A1 SwiGLU block at M = 1024 (64 requests x 16 draft tokens)."""
+    ops = pkg.ops
+    H, F, M = 2560, 9728, 1024
+    g = torch.Generator(device=device).manual_seed(4)
+    gate, up, down = (torch.randn(s, generator=g, device=device) * 0.02 for s in ((F, H), (F, H), (H, F)))
+    ffn = ops.pack_ffn(gate, up, down)
+    x = torch.randn((M, H), generator=g, device=device)
+    flags = ops.Flags(device)
+    for _ in range(3):
+        ops.ffn_w1a1(x, ffn, flags=flags)
+    torch.cuda.synchronize()
+    us = _events_us(lambda: ops.ffn_w1a1(x, ffn, flags=flags), max(args.steps // 200, 5))
+    flags.check()
+    macs = 3 * M * F * H
+    return [{"workload": "W1A1 SwiGLU block, M = 1024, 2560x9728x2560", "metric": "+-1 TOP/s (MAC = 2 ops)",
+             "value": 2 * macs / (us * 1e-6) / 1e12, "unit": "TOP/s", "us_per_ffn": us}]
+
+
+def workload_accept(args, pkg, device) -> list[dict]:
+    """Config 4: block acceptance of 32 requests x 16 drafts over a 151936 vocabulary."""
+    ops = pkg.ops
+    B, n, V = 32, 16, 151936
+    g = torch.Generator(device=device).manual_seed(5)
+    target = (torch.randn((B, n + 1, V), generator=g, device=device) * 3).to(torch.bfloat16)
+    draft = (torch.randn((B, n, V), generator=g, device=device) * 3).to(torch.bfloat16)
+    drafts = torch.randint(0, V, (B, n), generator=g, device=device, dtype=torch.int32)
+    flags = ops.Flags(device)
+    reps = max(args.steps // 20, 20)
+    greedy = _events_us(lambda: ops.accept_greedy(target, drafts, flags=flags), reps)
+    rej = _events_us(lambda: ops.accept_rejection(target, draft, drafts, seed=8, flags=flags), reps)
+    flags.check()
+    gb, rb = target.numel() * 2 + drafts.numel() * 4, (target.numel() + draft.numel()) * 2 + drafts.numel() * 4
+    return [{"workload": "greedy block acceptance, logits bf16 [32, 17, 151936]", "metric": "HBM GB/s",
+             "value": gb / (greedy * 1e-6) / 1e9, "unit": "GB/s", "us_per_call": greedy, "algorithmic_bytes": gb},
+            {"workload": "rejection sampling, target [32, 17, 151936] + draft [32, 16, 151936] bf16",
+             "metric": "HBM GB/s (single-pass bytes)", "value": rb / (rej * 1e-6) / 1e9, "unit": "GB/s",
+             "us_per_call": rej, "algorithmic_bytes": rb}]
+
+
+def workload_qat(args, pkg, device, rank: int, world: int) -> list[dict]:
+    """Config 5: QAT update of the 4-layer drafter, per GPU 8 sequences x 2048 positions,
+    32 windows of 16 slots each; data parallel (NCCL all-reduce) under torchrun."""
+    qat = importlib.import_module("binary-eagle-decoding_b200.qat")
+    cfg = pkg.Geometry(**GEOMETRY)
+    tensors, vocabulary, _, _ = make_tensors()
+    model = pkg.HE4(tensors, vocabulary, VOCAB - 1, cfg).to(device)
+    del tensors, vocabulary
+    opt = qat.BitAdamW(model)
+    g = torch.Generator().manual_seed(100 + rank)
+    seqs, length, windows_per = args.qat_sequences, 2048, 32
+    samples = []
+    for _ in range(seqs):
+        feats = torch.randn((length, 4 * cfg.hidden), generator=g).half().to(device)
+        tokens = tuple(torch.randint(0, VOCAB, (length,), generator=g).tolist())
+        anchors = [16 + (length - 32) * i // windows_per for i in range(windows_per)]
+        samples.append((feats, tokens, tuple(qat.Window(a, tuple(tokens[a + 1:a + 16])) for a in anchors)))
+    params = [p for ps in opt.groups.values() for _, p in ps]
+
+    def step(u):
+        opt.zero_grad()
+        for feats, tokens, windows in samples:
+            qat.group_loss(model, feats, tokens, windows, scale=1.0 / seqs)
+        qat.average_gradients(params)
+        _, coef = qat.clip_grad_norm(params, 1.0)
+        opt.step(coef)
+
+    for u in range(2):
+        step(u)
+    torch.cuda.synchronize()
+    reps = 3
+    us = _events_us(lambda: step(0), reps)
+    t = torch.tensor([us], device=device)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    rows = seqs * windows_per * 16 * world
+    return [{"workload": f"QAT update, {seqs} sequences x 2048 positions x 32 windows of 16 slots per GPU, "
+                         f"4-layer drafter, {world} GPU(s)", "metric": "slot rows / s", "value": rows / (t.item() * 1e-6),
+             "unit": "rows/s", "ms_per_step": t.item() / 1e3, "n_gpus": world}]
+
+
+def run_workload(args, rank: int, world: int, local_rank: int) -> None:
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    pkg = importlib.import_module("binary-eagle-decoding_b200")
+    lib = pkg._lib
+    lib.load()
+    before = lib.launches
+    if args.workload == "ffn":
+        lines = workload_ffn(args, pkg, device)
+    elif args.workload == "w1a1":
+        lines = workload_w1a1(args, pkg, device)
+    elif args.workload == "accept":
+        lines = workload_accept(args, pkg, device)
+    else:
+        lines = workload_qat(args, pkg, device, rank, world)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    if rank == 0:
+        for line in lines:
+            line["kernel_launches_issued"] = lib.launches - before
+            print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--gpus", type=int, default=1)
@@ -381,6 +556,9 @@ def main() -> None:
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     parser.add_argument("--profile-round", action="store_true",
                         help="run one draft round between cudaProfilerStart/Stop and exit")
+    parser.add_argument("--workload", choices=("round", "ffn", "w1a1", "accept", "qat"), default="round",
+                        help="round: the headline draft round; the others measure one hot-path workload each")
+    parser.add_argument("--qat-sequences", type=int, default=8)
     args = parser.parse_args()
     if args.profile_round:
         profile_round()
@@ -388,6 +566,9 @@ def main() -> None:
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus if args.gpus == 1 else 1)))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.workload != "round":
+        run_workload(args, rank, world, local_rank)
+        return
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

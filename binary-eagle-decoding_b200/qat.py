@@ -255,9 +255,10 @@ class Window:
 
 
 def group_loss(model: HE4, features: Tensor, tokens: tuple[int, ...], windows: tuple[Window, ...],
-               slots: int | None = None, positions: tuple[float, ...] | None = None) -> Tensor:
+               slots: int | None = None, positions: tuple[float, ...] | None = None, scale: float = 1.0) -> Tensor:
     """Weighted cross-entropy of the drafted positions (``worker.py:315-363``); runs the
-    backward of the vocabulary head in 128-row chunks, then through the drafter."""
+    backward of the vocabulary head in 128-row chunks, then through the drafter.
+    ``scale`` multiplies the label weights (1/n to average n sequences into one update)."""
     if not windows or any(not w.labels for w in windows):
         raise ValueError("an update requires supervised windows")
     device = model.vocabulary.device
@@ -269,7 +270,7 @@ def group_loss(model: HE4, features: Tensor, tokens: tuple[int, ...], windows: t
     rows = torch.tensor([i * size + 1 + o for i, n in enumerate(lengths) for o in range(n)], device=device)
     labels = torch.tensor([l for w, n in zip(windows, lengths) for l in w.labels[:n]], dtype=torch.int64,
                           device=device)
-    weights = label_weights(lengths, positions).to(device)
+    weights = (label_weights(lengths, positions) * scale).to(device)
     selected = hidden.view(-1, hidden.shape[-1]).index_select(0, rows)
     head = selected.detach().requires_grad_()
     total = torch.zeros((), device=device)
