@@ -66,6 +66,8 @@ SIGNATURES = {
     "bd_t16_words": (c_int64, [c_int64, c_int64]),
     "bd_tile_signs_t16": (c_int, [P, c_int64, c_int64, P, c_int, c_int, P, P]),
     "bd_tile_gguf_t16": (c_int, [P, c_int64, c_int64, P, c_int, c_int, P]),
+    "bd_w8_words": (c_int64, [c_int64, c_int64]),
+    "bd_tile_signs_w8": (c_int, [P, c_int64, c_int64, P, c_int, c_int, P, P]),
     "bd_quantize_codes": (c_int, [P, c_int64, c_int64, c_int64, P, P, c_int, P, P, P, P]),
     "bd_codes_ld": (c_int64, [c_int64]),
     "bd_codes_bytes": (c_int64, [c_int64, c_int64]),

@@ -32,36 +32,6 @@ static int sm_count_cached() {
     return cached[dev];
 }
 
-struct FfnPieces {
-    int8_t *codes_in, *codes_in_lo, *codes_mid, *codes_mid_lo;
-    int32_t *sum_in, *sum_in_lo, *sum_mid, *sum_mid_lo;
-    float *scale_in, *scale_mid, *hidden;
-    int32_t *acc, *counters;
-};
-
-static FfnPieces carve_ffn(void *ws, int64_t hidden, int64_t inter, bool planes, size_t *bytes) {
-    Carver c{static_cast<char *>(ws)};
-    const int64_t ld_h = (hidden + 255) / 256 * 256, ld_f = (inter + 255) / 256 * 256;
-    const int64_t rows_pad_h = (hidden + 15) / 16 * 16;
-    FfnPieces p{};
-    p.codes_in = c.take<int8_t>(kMaxTokens * ld_h);
-    p.codes_mid = c.take<int8_t>(kMaxTokens * ld_f);
-    p.sum_in = c.take<int32_t>(kMaxTokens * quant_parts(hidden));
-    p.sum_mid = c.take<int32_t>(kMaxTokens);
-    if (planes) {
-        p.codes_in_lo = c.take<int8_t>(kMaxTokens * ld_h);
-        p.codes_mid_lo = c.take<int8_t>(kMaxTokens * ld_f);
-        p.sum_in_lo = c.take<int32_t>(kMaxTokens);
-        p.sum_mid_lo = c.take<int32_t>(kMaxTokens);
-        p.scale_in = c.take<float>(kMaxTokens);
-        p.scale_mid = c.take<float>(kMaxTokens);
-        p.hidden = c.take<float>(kMaxTokens * inter);
-    }
-    p.acc = c.take<int32_t>(2 * rows_pad_h * kMaxTokens);
-    p.counters = c.take<int32_t>((hidden + 15) / 16);
-    *bytes = c.off;
-    return p;
-}
 
 }  // namespace bd
 
@@ -137,9 +107,7 @@ extern "C" int bd_projection_he4(const int8_t *codes, const int32_t *code_sums, 
 
 extern "C" size_t bd_ffn_workspace_bytes(int tokens, int64_t hidden, int64_t inter) {
     (void)tokens;
-    size_t bytes = 0;
-    carve_ffn(nullptr, hidden, inter, true, &bytes);
-    return bytes;
+    return ffn_w8_workspace_bytes(hidden, inter);
 }
 
 static bool ffn_shapes_ok(int tokens, int64_t hidden, int64_t inter) {
@@ -152,65 +120,52 @@ extern "C" int bd_ffn_he4(const bd_ffn_he4_args *p, bd_stream_t stream) {
         !p->scale_up || !p->midpoint_up || !p->scale_down || !p->midpoint_down || !p->gain_gate_up ||
         !p->bound_gate_up || !p->gain_down || !p->bound_down)
         return BD_ERR_INVALID;
-    size_t need = 0;
-    FfnPieces w = carve_ffn(p->workspace, p->hidden, p->inter, false, &need);
-    if (!p->workspace || need > p->workspace_bytes) return BD_ERR_WORKSPACE;
-    const int64_t ld_h = (p->hidden + 255) / 256 * 256, ld_f = (p->inter + 255) / 256 * 256;
-    // The quantizer writes per-slice partial code sums of the gate/up input and
-    // zeroes the down projection's code sums, which gate/up accumulate.
-    int st = launch_quantize_codes(p->x, p->tokens, p->hidden, ld_h, p->gain_gate_up, p->bound_gate_up, 4,
-                                   w.codes_in, w.sum_in, true, p->flags, w.sum_mid, kMaxTokens, stream,
-                                   p->norm_weight, p->epsilon);
-    if (st) return st;
+    FfnW8 f{};
+    f.tokens = p->tokens;
+    f.hidden = p->hidden;
+    f.inter = p->inter;
+    f.signs_gate_up = p->signs_gate_up;
+    f.signs_down = p->signs_down;
+    f.scale_gate = p->scale_gate;
+    f.mid_gate = p->midpoint_gate;
+    f.scale_up = p->scale_up;
+    f.mid_up = p->midpoint_up;
+    f.scale_down = p->scale_down;
+    f.mid_down = p->midpoint_down;
+    f.gain_gate_up = p->gain_gate_up;
+    f.bound_gate_up = p->bound_gate_up;
+    f.gain_down = p->gain_down;
+    f.bound_down = p->bound_down;
+    f.x = p->x;
+    f.residual = p->residual;
+    f.norm_w = p->norm_weight;
+    f.eps = p->epsilon;
+    f.y = p->y;
+    f.hidden_out = p->hidden_out;
+    f.flags = p->flags;
+    f.workspace = p->workspace;
+    f.workspace_bytes = p->workspace_bytes;
+    return ffn_w8(f, EPI_HE4, stream);
+}
 
-    ProjArgs gu{};
-    gu.bits = p->signs_gate_up;
-    gu.rows = p->inter;
-    gu.cols = p->hidden;
-    gu.ncp = ld_h / 256;
-    gu.codes0 = w.codes_in;
-    gu.csum0 = w.sum_in;
-    gu.nparts = quant_parts(p->hidden);
-    gu.ld = ld_h;
-    gu.tokens = p->tokens;
-    gu.kgroups = 1;
-    gu.scale0 = p->scale_gate;
-    gu.mid0 = p->midpoint_gate;
-    gu.scale1 = p->scale_up;
-    gu.mid1 = p->midpoint_up;
-    gu.bound = p->bound_gate_up;
-    gu.code_bits = 4;
-    gu.out = p->hidden_out;
-    gu.next_gain = p->gain_down;
-    gu.next_bound = p->bound_down;
-    gu.next_codes = w.codes_mid;
-    gu.next_csum = w.sum_mid;
-    gu.next_ld = ld_f;
-    gu.flags = p->flags;
-    st = launch_gateup(gu, EPI_HE4, stream);
-    if (st) return st;
-
-    ProjArgs dn{};
-    dn.bits = p->signs_down;
-    dn.rows = p->hidden;
-    dn.cols = p->inter;
-    dn.ncp = ld_f / 256;
-    dn.codes0 = w.codes_mid;
-    dn.csum0 = w.sum_mid;
-    dn.nparts = 1;
-    dn.ld = ld_f;
-    dn.tokens = p->tokens;
-    plan_proj(dn, 1);
-    dn.scale0 = p->scale_down;
-    dn.mid0 = p->midpoint_down;
-    dn.bound = p->bound_down;
-    dn.code_bits = 8;
-    dn.residual = p->residual;
-    dn.out = p->y;
-    dn.acc = w.acc;
-    dn.counters = w.counters;
-    dn.flags = p->flags;
-    return launch_proj(dn, EPI_HE4, stream);
+static FfnW8 w1_block(const bd_ffn_w1_args *p, bd_stream_t stream) {
+    (void)stream;
+    FfnW8 f{};
+    f.tokens = p->tokens;
+    f.hidden = p->hidden;
+    f.inter = p->inter;
+    f.signs_gate_up = p->signs_gate_up;
+    f.signs_down = p->signs_down;
+    f.scale_gate = p->scale_gate;
+    f.scale_up = p->scale_up;
+    f.scale_down = p->scale_down;
+    f.x = p->x;
+    f.y = p->y;
+    f.hidden_out = p->hidden_out;
+    f.flags = p->flags;
+    f.workspace = p->workspace;
+    f.workspace_bytes = p->workspace_bytes;
+    return f;
 }
 
 extern "C" int bd_ffn_w1(const bd_ffn_w1_args *p, bd_stream_t stream) {
@@ -218,59 +173,7 @@ extern "C" int bd_ffn_w1(const bd_ffn_w1_args *p, bd_stream_t stream) {
     if (!p->x || !p->y || !p->signs_gate_up || !p->signs_down || !p->scale_gate || !p->scale_up ||
         !p->scale_down)
         return BD_ERR_INVALID;
-    size_t need = 0;
-    FfnPieces w = carve_ffn(p->workspace, p->hidden, p->inter, true, &need);
-    if (!p->workspace || need > p->workspace_bytes) return BD_ERR_WORKSPACE;
-    const int64_t ld_h = (p->hidden + 255) / 256 * 256, ld_f = (p->inter + 255) / 256 * 256;
-    int st = launch_quantize_planes(p->x, p->tokens, p->hidden, ld_h, w.codes_in, w.codes_in_lo, w.sum_in,
-                                    w.sum_in_lo, w.scale_in, p->flags, stream);
-    if (st) return st;
-    float *hidden = p->hidden_out ? p->hidden_out : w.hidden;
-
-    ProjArgs gu{};
-    gu.bits = p->signs_gate_up;
-    gu.rows = p->inter;
-    gu.cols = p->hidden;
-    gu.ncp = ld_h / 256;
-    gu.codes0 = w.codes_in;
-    gu.codes1 = w.codes_in_lo;
-    gu.csum0 = w.sum_in;
-    gu.csum1 = w.sum_in_lo;
-    gu.nparts = 1;
-    gu.ld = ld_h;
-    gu.tokens = p->tokens;
-    gu.kgroups = 1;
-    gu.scale0 = p->scale_gate;
-    gu.scale1 = p->scale_up;
-    gu.row_scale = w.scale_in;
-    gu.out = hidden;
-    gu.flags = p->flags;
-    st = launch_gateup(gu, EPI_W1, stream);
-    if (st) return st;
-    st = launch_quantize_planes(hidden, p->tokens, p->inter, ld_f, w.codes_mid, w.codes_mid_lo, w.sum_mid,
-                                w.sum_mid_lo, w.scale_mid, p->flags, stream);
-    if (st) return st;
-
-    ProjArgs dn{};
-    dn.bits = p->signs_down;
-    dn.rows = p->hidden;
-    dn.cols = p->inter;
-    dn.ncp = ld_f / 256;
-    dn.codes0 = w.codes_mid;
-    dn.codes1 = w.codes_mid_lo;
-    dn.csum0 = w.sum_mid;
-    dn.csum1 = w.sum_mid_lo;
-    dn.nparts = 1;
-    dn.ld = ld_f;
-    dn.tokens = p->tokens;
-    plan_proj(dn, 2);
-    dn.scale0 = p->scale_down;
-    dn.row_scale = w.scale_mid;
-    dn.out = p->y;
-    dn.acc = w.acc;
-    dn.counters = w.counters;
-    dn.flags = p->flags;
-    return launch_proj(dn, EPI_W1, stream);
+    return ffn_w8(w1_block(p, stream), EPI_W1, stream);
 }
 
 // ------------------------------------------------------------------------------------ W1A1
@@ -361,35 +264,13 @@ extern "C" int bd_ffn_w1a1(const bd_ffn_w1_args *p, bd_stream_t stream) {
     if (p->tokens == 0) return BD_OK;
     if (!p->x || !p->y || !p->signs_gate_up || !p->signs_down || !p->scale_gate || !p->scale_up || !p->scale_down)
         return BD_ERR_INVALID;
-    size_t need = 0;
-    FfnPieces w = carve_ffn(p->workspace, p->hidden, p->inter, true, &need);
-    if (!p->workspace || need > p->workspace_bytes) return BD_ERR_WORKSPACE;
-    const int64_t ld_h = bd_codes_ld(p->hidden), ld_f = bd_codes_ld(p->inter);
     for (int t0 = 0; t0 < p->tokens; t0 += kMaxTokens) {
-        const int n = p->tokens - t0 < kMaxTokens ? p->tokens - t0 : kMaxTokens;
-        float *hidden = p->hidden_out ? p->hidden_out + t0 * p->inter : w.hidden;
-        int st = launch_binarize(p->x + t0 * p->hidden, n, p->hidden, ld_h, w.codes_in, w.sum_in, w.scale_in,
-                                 nullptr, 0, p->flags, stream);
-        if (st) return st;
-        W1a1Pieces in{w.codes_in, w.sum_in, w.scale_in, nullptr, nullptr};
-        ProjArgs gu = w1a1_args(p->signs_gate_up, p->hidden, p->inter, in, n);
-        gu.scale0 = p->scale_gate;
-        gu.scale1 = p->scale_up;
-        gu.out = hidden;
-        gu.flags = p->flags;
-        st = launch_gateup(gu, EPI_W1A1, stream);
-        if (st) return st;
-        st = launch_binarize(hidden, n, p->inter, ld_f, w.codes_mid, w.sum_mid, w.scale_mid, nullptr, 0, p->flags,
-                             stream);
-        if (st) return st;
-        W1a1Pieces mid{w.codes_mid, w.sum_mid, w.scale_mid, w.acc, w.counters};
-        ProjArgs dn = w1a1_args(p->signs_down, p->inter, p->hidden, mid, n);
-        dn.scale0 = p->scale_down;
-        dn.out = p->y + t0 * p->hidden;
-        dn.acc = w.acc;
-        dn.counters = w.counters;
-        dn.flags = p->flags;
-        st = launch_proj(dn, EPI_W1A1, stream);
+        FfnW8 f = w1_block(p, stream);
+        f.tokens = p->tokens - t0 < kMaxTokens ? p->tokens - t0 : kMaxTokens;
+        f.x = p->x + t0 * p->hidden;
+        f.y = p->y + t0 * p->hidden;
+        f.hidden_out = p->hidden_out ? p->hidden_out + t0 * p->inter : nullptr;
+        const int st = ffn_w8(f, EPI_W1A1, stream);
         if (st) return st;
     }
     return BD_OK;

@@ -26,9 +26,12 @@ __device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) {
 }
 
 // Integer MMA m16n8k32: D(int32) += A(16x32 s8, row) * B(32x8 s8, col).
+// The MMA and weight-load helpers are not volatile: they touch only registers (or
+// read-only weights), so the compiler may interleave them freely; data written by
+// an earlier kernel is read with ordinary loads, which stay after grid_wait().
 __device__ __forceinline__ void mma_s8_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                              uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 "
         "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
@@ -38,7 +41,7 @@ __device__ __forceinline__ void mma_s8_16832(int (&d)[4], uint32_t a0, uint32_t 
 // bf16 MMA m16n8k16: D(f32) += A(16x16 bf16, row) * B(16x8 bf16, col).
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                                uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
         "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -48,7 +51,7 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
 // Streaming 16-byte global load that does not allocate in L1 (weights are read once).
 __device__ __forceinline__ uint4 ld_stream_u4(const void *p) {
     uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                  : "l"(p));
     return v;
@@ -81,6 +84,25 @@ __device__ __forceinline__ int64_t frag_offset(int token, int64_t k, int64_t nsp
     const int kk = static_cast<int>(k & 31);
     const int half = kk >> 4, t = (kk & 15) >> 2, j = kk & 3;
     return (((nt * nsp + (s >> 1)) * 32 + g * 4 + t) << 4) + ((s & 1) << 3) + (half << 2) + j;
+}
+
+// A-fragment layout of int8 activation codes ("C16"), tokens as the M side of
+// m16n8k32: [k-step s = k / 32][m-tile][lane][16 bytes]; lane 4 (r % 8) + (kk % 16) / 4
+// of m-tile token block holds register (r / 8) + 2 (kk / 16), byte kk % 4, for
+// token 16 m + r and column 32 s + kk.  One 16-byte load per lane per k-step is
+// the whole A fragment.
+__device__ __forceinline__ int64_t c16_offset(int token, int64_t k, int mtiles) {
+    const int64_t s = k >> 5;
+    const int kk = static_cast<int>(k & 31);
+    const int r = token & 15, m = token >> 4;
+    const int lane = ((r & 7) << 2) + ((kk & 15) >> 2);
+    const int reg = (r >> 3) + ((kk >> 4) << 1);
+    return (((s * mtiles + m) * 32 + lane) << 4) + (reg << 2) + (kk & 3);
+}
+
+// Byte offset of code (token, k): C16 when c16_mt > 0, else F8 with row stride ld.
+__device__ __forceinline__ int64_t code_offset(int token, int64_t k, int64_t ld, int c16_mt) {
+    return c16_mt > 0 ? c16_offset(token, k, c16_mt) : frag_offset(token, k, ld / 64);
 }
 
 // The quantizer of Projection.forward for one element (see bd_quantize_codes).

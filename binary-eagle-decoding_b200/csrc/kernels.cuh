@@ -30,12 +30,31 @@ inline int quant_parts(int64_t cols) { return static_cast<int>((cols + 1023) / 1
 int launch_quantize_codes(const float *x, int64_t rows, int64_t cols, int64_t ld, const float *gain,
                           const float *bound, int bits, int8_t *codes, int32_t *sums, bool partial, int32_t *flags,
                           int32_t *zero_sums, int zero_count, cudaStream_t stream, const float *norm_w = nullptr,
-                          float eps = 0.0f);
+                          float eps = 0.0f, int c16_mt = 0);
 int launch_quantize_planes(const float *x, int64_t rows, int64_t cols, int64_t ld, int8_t *hi, int8_t *lo,
                            int32_t *sums_hi, int32_t *sums_lo, float *row_scale, int32_t *flags,
-                           cudaStream_t stream);
+                           cudaStream_t stream, int c16_mt = 0);
 int launch_binarize(const float *x, int64_t rows, int64_t cols, int64_t ld, int8_t *codes, int32_t *sums,
-                    float *mean_abs, uint32_t *words, int64_t words_ld, int32_t *flags, cudaStream_t stream);
+                    float *mean_abs, uint32_t *words, int64_t words_ld, int32_t *flags, cudaStream_t stream,
+                    int c16_mt = 0);
+
+// ---- W8 / C16 decode feed-forward (ffn8.cu): tokens are the MMA's M side
+int64_t w8_words(int64_t rows, int64_t cols);  // uint32 words of one W8 matrix
+struct FfnW8 {
+    int tokens;
+    int64_t hidden, inter;
+    const uint32_t *signs_gate_up, *signs_down;  // W8; gate/up n-tiles interleaved
+    const float *scale_gate, *mid_gate, *scale_up, *mid_up, *scale_down, *mid_down;
+    const float *gain_gate_up, *bound_gate_up, *gain_down, *bound_down;
+    const float *x, *residual, *norm_w;
+    float eps;
+    float *y, *hidden_out;
+    int32_t *flags;
+    void *workspace;
+    size_t workspace_bytes;
+};
+size_t ffn_w8_workspace_bytes(int64_t hidden, int64_t inter);
+int ffn_w8(const FfnW8 &f, int epi, cudaStream_t stream);
 
 // Epilogue selectors of the T16 integer-MMA projection kernels.
 enum Epilogue : int {

@@ -3,7 +3,7 @@
 // weight decay 0 (torch.optim.AdamW(fused=True), worker.py:122-130), then
 // scale.clamp_(min=0) and the optional clamp_latents (model.py:167-169).
 //
-// The latent update is fused with the re-pack of the new signs into the T16
+// The latent update is fused with the re-pack of the new signs into the W8
 // decode layout, so one pass reads w, g, m, v and writes w, m, v and 1 bit per
 // weight.  bound_latents (model.py:153-164) is a row kernel of its own.
 #include <cmath>
@@ -29,20 +29,22 @@ __device__ __forceinline__ float adam_element(float p, float g, float &m, float 
 // Spread the 4 low bits of x to bit 0 of each byte.
 __device__ __forceinline__ uint32_t spread4_o(uint32_t x) { return (x * 0x00204081u) & 0x01010101u; }
 
-// T16 word of (row, chunk c, lane t) from the 8 sign words of a 256-column pair.
-__device__ __forceinline__ uint32_t t16_word_o(const uint32_t *g, int c, int t) {
+// W8 word of (row, 128-column half h of a 256-column pair, lane t) from the 8
+// ballot words g of the pair (bit l of g[i] = column 32 i + l): bit 8 j + 2 ks + r
+// is column 128 h + 32 ks + 16 r + 4 t + j.
+__device__ __forceinline__ uint32_t w8_word_o(const uint32_t *g, int h, int t) {
     uint32_t out = 0;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        const uint32_t word = g[4 * c + q];
-        out |= spread4_o((word >> (4 * t)) & 0xFu) << (2 * q);
-        out |= spread4_o((word >> (16 + 4 * t)) & 0xFu) << (2 * q + 1);
+    for (int ks = 0; ks < 4; ++ks) {
+        const uint32_t word = g[4 * h + ks];
+        out |= spread4_o((word >> (4 * t)) & 0xFu) << (2 * ks);
+        out |= spread4_o((word >> (16 + 4 * t)) & 0xFu) << (2 * ks + 1);
     }
     return out;
 }
 
 // One warp per (row, 256-column pair): update 256 latents, ballot their new
-// signs into eight words and emit the row's eight T16 words.
+// signs into eight words and emit the row's (up to) eight W8 words.
 __global__ void __launch_bounds__(256) adamw_latent_kernel(float *__restrict__ param, const float *__restrict__ grad,
                                                            float *__restrict__ m, float *__restrict__ v, int64_t rows,
                                                            int64_t cols, AdamScalars a,
@@ -51,7 +53,8 @@ __global__ void __launch_bounds__(256) adamw_latent_kernel(float *__restrict__ p
                                                            int32_t *flags) {
     const int lane = threadIdx.x & 31;
     const int64_t ncp = (cols + 255) / 256;
-    const int64_t rows_pad = (rows + 15) / 16 * 16;
+    const int64_t nw = (cols + 127) / 128;
+    const int64_t rows_pad = (rows + 7) / 8 * 8;
     const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
     const float coef = clip_coef ? __ldg(clip_coef) : 1.0f;
@@ -78,11 +81,13 @@ __global__ void __launch_bounds__(256) adamw_latent_kernel(float *__restrict__ p
             words[i] = __ballot_sync(0xffffffffu, bit);
         }
         if (tiled && lane < 8) {
-            const int c = lane >> 2, t = lane & 3;
-            const int64_t rb = (row >> 4) * stride + offset;
-            const int rr = static_cast<int>(row & 15);
-            const int64_t idx = (rb * ncp + cp) * 128 + ((rr & 7) * 4 + t) * 4 + (rr >> 3) + 2 * c;
-            tiled[idx] = t16_word_o(words, c, t);
+            const int h = lane >> 2, t = lane & 3;
+            const int64_t w = 2 * cp + h;
+            if (w < nw) {  // W8 stores words in groups of four per lane: [n][w / 4][lane][w % 4]
+                const int64_t n = (row >> 3) * stride + offset;
+                const int64_t ng = (nw + 3) / 4;
+                tiled[((n * ng + (w >> 2)) * 32 + (row & 7) * 4 + t) * 4 + (w & 3)] = w8_word_o(words, h, t);
+            }
         }
     }
     if (__any_sync(0xffffffffu, bad) && lane == 0) set_flag(flags, BD_FLAG_NONFINITE_STATE);
@@ -209,17 +214,17 @@ static AdamScalars adam_scalars(double lr, double beta1, double beta2, double ep
 
 extern "C" int bd_adamw_latent(float *param, const float *grad, float *exp_avg, float *exp_avg_sq, int64_t rows,
                                int64_t cols, double lr, double beta1, double beta2, double eps, long long step,
-                               const float *clip_coef, int clamp_latents, uint32_t *signs_t16, int block_stride,
+                               const float *clip_coef, int clamp_latents, uint32_t *signs_w8, int block_stride,
                                int block_offset, int32_t *flags, bd_stream_t stream) {
     if (rows < 0 || cols < 1 || !adam_ok(lr, beta1, beta2, eps, step) || block_stride < 1 || block_offset < 0 ||
         block_offset >= block_stride)
         return BD_ERR_INVALID;
     if (rows == 0) return BD_OK;
     if (!param || !grad || !exp_avg || !exp_avg_sq) return BD_ERR_INVALID;
-    const int64_t items = (rows + 15) / 16 * 16 * ((cols + 255) / 256);
+    const int64_t items = (rows + 7) / 8 * 8 * ((cols + 255) / 256);
     adamw_latent_kernel<<<grid_elems(items * 32), 256, 0, stream>>>(
         param, grad, exp_avg, exp_avg_sq, rows, cols, adam_scalars(lr, beta1, beta2, eps, step), clip_coef,
-        clamp_latents, signs_t16, block_stride, block_offset, flags);
+        clamp_latents, signs_w8, block_stride, block_offset, flags);
     BD_CHECK_LAUNCH();
     return BD_OK;
 }

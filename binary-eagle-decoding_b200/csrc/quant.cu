@@ -1,5 +1,6 @@
 // Activation quantizers feeding the integer-MMA projections.  All of them write
-// int8 codes in the F8 B-fragment layout (frag_offset in common.cuh).
+// int8 codes in the F8 B-fragment layout (frag_offset in common.cuh) or, when
+// c16_mt > 0, the C16 A-fragment layout of c16_mt token tiles (c16_offset).
 //   * HE4 learned-gain/clip codes (Projection.forward, w1a1_eagle/model.py:128-140)
 //   * per-token 16-bit fixed point as two int8 planes (pure one-bit-weight blocks)
 //   * W1A1 sign binarisation with the fixed-order per-token mean|x|
@@ -32,7 +33,7 @@ __global__ void __launch_bounds__(256) quantize_codes_kernel(const float *__rest
                                                              int8_t *__restrict__ codes, int32_t *__restrict__ sums,
                                                              bool partial, int32_t *flags, int32_t *zero_sums,
                                                              int zero_count, const float *__restrict__ norm_w,
-                                                             float eps) {
+                                                             float eps, int c16_mt) {
     __shared__ int scratch[8];
     __shared__ float fpart[8];
     grid_wait();
@@ -81,7 +82,7 @@ __global__ void __launch_bounds__(256) quantize_codes_kernel(const float *__rest
             }
             sum += c[j];
         }
-        *reinterpret_cast<char4 *>(codes + frag_offset(row, k0, ld / 64)) =
+        *reinterpret_cast<char4 *>(codes + code_offset(row, k0, ld, c16_mt)) =
             make_char4(static_cast<signed char>(c[0]), static_cast<signed char>(c[1]),
                        static_cast<signed char>(c[2]), static_cast<signed char>(c[3]));
     }
@@ -103,13 +104,13 @@ __global__ void __launch_bounds__(256) quantize_planes_kernel(const float *__res
                                                               int8_t *__restrict__ hi, int8_t *__restrict__ lo,
                                                               int32_t *__restrict__ sums_hi,
                                                               int32_t *__restrict__ sums_lo,
-                                                              float *__restrict__ row_scale, int32_t *flags) {
+                                                              float *__restrict__ row_scale, int32_t *flags,
+                                                              int c16_mt) {
     __shared__ float fscratch[8];
     __shared__ int iscratch[8];
     grid_wait();
     grid_launch_dependents();
     const int row = blockIdx.x;
-    const int64_t nsp = ld / 64;
     float m = 0.0f;
     bool bad = false;
     for (int64_t k0 = 4 * threadIdx.x; k0 < cols; k0 += 4 * blockDim.x) {
@@ -147,7 +148,7 @@ __global__ void __launch_bounds__(256) quantize_planes_kernel(const float *__res
             shi += h[j];
             slo += l[j];
         }
-        const int64_t off = frag_offset(row, k0, nsp);
+        const int64_t off = code_offset(row, k0, ld, c16_mt);
         *reinterpret_cast<char4 *>(hi + off) = make_char4(h[0], h[1], h[2], h[3]);
         *reinterpret_cast<char4 *>(lo + off) = make_char4(l[0], l[1], l[2], l[3]);
     }
@@ -165,13 +166,12 @@ __global__ void __launch_bounds__(256) quantize_planes_kernel(const float *__res
 __global__ void __launch_bounds__(256) binarize_kernel(const float *__restrict__ x, int64_t cols, int64_t ld,
                                                        int8_t *__restrict__ codes, int32_t *__restrict__ sums,
                                                        float *__restrict__ mean_abs, uint32_t *__restrict__ words,
-                                                       int64_t words_ld, int32_t *flags) {
+                                                       int64_t words_ld, int32_t *flags, int c16_mt) {
     __shared__ float fscratch[8];
     __shared__ int iscratch[8];
     grid_wait();
     grid_launch_dependents();
     const int row = blockIdx.x;
-    const int64_t nsp = ld / 64;
     float acc = 0.0f;
     int s = 0;
     bool bad = false;
@@ -183,7 +183,7 @@ __global__ void __launch_bounds__(256) binarize_kernel(const float *__restrict__
             acc = __fadd_rn(acc, fabsf(v));
             c = v >= 0.0f ? 1 : -1;
         }
-        if (codes) codes[frag_offset(row, k, nsp)] = static_cast<int8_t>(c);
+        if (codes) codes[code_offset(row, k, ld, c16_mt)] = static_cast<int8_t>(c);
         s += c;
         if (words) {
             const unsigned word = __ballot_sync(0xffffffffu, c > 0);
@@ -206,28 +206,33 @@ __global__ void __launch_bounds__(256) binarize_kernel(const float *__restrict__
 
 int launch_quantize_codes(const float *x, int64_t rows, int64_t cols, int64_t ld, const float *gain,
                           const float *bound, int bits, int8_t *codes, int32_t *sums, bool partial, int32_t *flags,
-                          int32_t *zero_sums, int zero_count, cudaStream_t stream, const float *norm_w, float eps) {
+                          int32_t *zero_sums, int zero_count, cudaStream_t stream, const float *norm_w, float eps,
+                          int c16_mt) {
     if (rows == 0) return BD_OK;
     if (sums && !partial && cudaMemsetAsync(sums, 0, rows * sizeof(int32_t), stream) != cudaSuccess)
         return BD_ERR_LAUNCH;
     const dim3 grid(static_cast<unsigned>(rows), static_cast<unsigned>(quant_parts(cols)));
+    // same shared-memory carveout as the projection kernels around it: no SM reconfiguration between them
+    if (cudaFuncSetAttribute(quantize_codes_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
+        return BD_ERR_LAUNCH;
     return launch_pdl(quantize_codes_kernel, grid, dim3(256), 0, stream, x, cols, ld, gain, bound, bits, codes, sums,
-                      partial, flags, zero_sums, zero_count, norm_w, eps);
+                      partial, flags, zero_sums, zero_count, norm_w, eps, c16_mt);
 }
 
 int launch_quantize_planes(const float *x, int64_t rows, int64_t cols, int64_t ld, int8_t *hi, int8_t *lo,
                            int32_t *sums_hi, int32_t *sums_lo, float *row_scale, int32_t *flags,
-                           cudaStream_t stream) {
+                           cudaStream_t stream, int c16_mt) {
     if (rows == 0) return BD_OK;
     return launch_pdl(quantize_planes_kernel, dim3(static_cast<unsigned>(rows)), dim3(256), 0, stream, x, cols, ld,
-                      hi, lo, sums_hi, sums_lo, row_scale, flags);
+                      hi, lo, sums_hi, sums_lo, row_scale, flags, c16_mt);
 }
 
 int launch_binarize(const float *x, int64_t rows, int64_t cols, int64_t ld, int8_t *codes, int32_t *sums,
-                    float *mean_abs, uint32_t *words, int64_t words_ld, int32_t *flags, cudaStream_t stream) {
+                    float *mean_abs, uint32_t *words, int64_t words_ld, int32_t *flags, cudaStream_t stream,
+                    int c16_mt) {
     if (rows == 0) return BD_OK;
     return launch_pdl(binarize_kernel, dim3(static_cast<unsigned>(rows)), dim3(256), 0, stream, x, cols, ld, codes,
-                      sums, mean_abs, words, words_ld, flags);
+                      sums, mean_abs, words, words_ld, flags, c16_mt);
 }
 
 }  // namespace bd

@@ -264,19 +264,19 @@ class Projection(nn.Module):
         self._signs["bf16"] = (key, out)
         return out
 
-    def signs_t16(self) -> Tensor:
-        """T16 decode-layout sign words (cached per latent version)."""
+    def signs_w8(self) -> Tensor:
+        """W8 decode-layout sign words (cached per latent version)."""
         key = self._key()
-        hit = self._signs.get("t16")
+        hit = self._signs.get("w8")
         if hit is not None and hit[0] == key:
             return hit[1]
-        out = ops.tile_t16(self.latent_sign.detach().contiguous())
-        self._signs["t16"] = (key, out)
+        out = ops.tile_w8(self.latent_sign.detach().contiguous())
+        self._signs["w8"] = (key, out)
         return out
 
-    def adopt_t16(self, tiled: Tensor) -> None:
-        """Install T16 words re-packed by the optimizer for the current latent version."""
-        self._signs = {"t16": (self._key(), tiled)}
+    def adopt_w8(self, tiled: Tensor) -> None:
+        """Install W8 words re-packed by the optimizer for the current latent version."""
+        self._signs = {"w8": (self._key(), tiled)}
 
     def forward(self, value: Tensor) -> Tensor:
         return _ProjectionFn.apply(value, self.latent_sign, self.scale, self.midpoint, self.log_gain, self.log_clip,
@@ -377,8 +377,8 @@ class Layer(nn.Module):
             gate, up, down = (p.latent_sign.detach().contiguous() for p in (self.gate, self.up, self.down))
             flags = ops.Flags(gate.device)
             packed = ops.PackedFFN(
-                hidden=gate.shape[1], inter=gate.shape[0], signs_gate_up=ops.tile_gate_up(gate, up, flags),
-                signs_down=self.down.signs_t16(), scale_gate=self.gate.scale.detach().contiguous(),
+                hidden=gate.shape[1], inter=gate.shape[0], signs_gate_up=ops.tile_gate_up_w8(gate, up, flags),
+                signs_down=self.down.signs_w8(), scale_gate=self.gate.scale.detach().contiguous(),
                 scale_up=self.up.scale.detach().contiguous(), scale_down=self.down.scale.detach().contiguous(),
                 midpoint_gate=self.gate.midpoint.detach().contiguous(),
                 midpoint_up=self.up.midpoint.detach().contiguous(),

@@ -197,12 +197,44 @@ class PackedFFN:
     bound_down: Tensor | None = None
 
 
+def w8_words(rows: int, cols: int) -> int:
+    return int(_lib.load().bd_w8_words(rows, cols))
+
+
+def tile_w8(latent: Tensor, block_stride: int = 1, block_offset: int = 0, out: Tensor | None = None,
+            flags: Flags | None = None) -> Tensor:
+    """W8 sign words of an F32 latent matrix (the decode feed-forward's B-fragment layout)."""
+    if latent.dtype != torch.float32 or latent.ndim != 2:
+        raise ValueError("finite F32 sign matrix required")
+    device = _require_cuda(latent)
+    rows, cols = latent.shape
+    if out is None:
+        out = torch.zeros(w8_words(rows, cols) * block_stride, dtype=torch.int32, device=device)
+    own = flags is None
+    flags = flags or Flags(device)
+    _lib.call("bd_tile_signs_w8", _p(latent), rows, cols, _p(out), block_stride, block_offset, flags.ptr,
+              _stream(device))
+    if own:
+        flags.check()
+    return out
+
+
+def tile_gate_up_w8(gate: Tensor, up: Tensor, flags: Flags | None = None) -> Tensor:
+    """Gate and up W8 signs with their 8-row n-tiles interleaved (gate, up, gate, up, ...)."""
+    if gate.shape != up.shape:
+        raise ValueError("gate and up must have one shape")
+    out = torch.zeros(w8_words(*gate.shape) * 2, dtype=torch.int32, device=gate.device)
+    tile_w8(gate, 2, 0, out, flags)
+    tile_w8(up, 2, 1, out, flags)
+    return out
+
+
 def pack_ffn(gate: Tensor, up: Tensor, down: Tensor, scale_gate: Tensor | None = None,
              scale_up: Tensor | None = None, scale_down: Tensor | None = None) -> PackedFFN:
-    """Pack latent F32 matrices; row scales default to ``mean|W|`` (model.py:123)."""
+    """Pack latent F32 matrices into W8 sign words; row scales default to ``mean|W|`` (model.py:123)."""
     flags = Flags(gate.device)
-    signs_gate_up = tile_gate_up(gate.contiguous(), up.contiguous(), flags)
-    signs_down = tile_t16(down.contiguous(), flags=flags)
+    signs_gate_up = tile_gate_up_w8(gate.contiguous(), up.contiguous(), flags)
+    signs_down = tile_w8(down.contiguous(), flags=flags)
     flags.check()
     return PackedFFN(
         hidden=gate.shape[1], inter=gate.shape[0], signs_gate_up=signs_gate_up, signs_down=signs_down,

@@ -147,7 +147,7 @@ class BitAdamW:
     """``torch.optim.AdamW(groups, weight_decay=0, fused=True)`` over the drafter's
     parameter groups (``worker.py:122-130``), with the post-step clamps of
     ``worker.py:377-382`` fused in: ``scale`` is clamped at 0, latents optionally to
-    [-1, 1], and each latent's new signs are re-packed into its projection's T16
+    [-1, 1], and each latent's new signs are re-packed into its projection's W8
     cache in the same pass."""
 
     def __init__(self, model: nn.Module, optimization: Optimization | None = None, betas=(0.9, 0.999),
@@ -190,12 +190,12 @@ class BitAdamW:
                 owner = self.owner.get(id(p))
                 stream = _stream(device)
                 if owner is not None:
-                    tiled = torch.zeros(ops.t16_words(*p.shape), dtype=torch.int32, device=device)
+                    tiled = torch.zeros(ops.w8_words(*p.shape), dtype=torch.int32, device=device)
                     _lib.call("bd_adamw_latent", p.data_ptr(), grad.data_ptr(), st["exp_avg"].data_ptr(),
                               st["exp_avg_sq"].data_ptr(), p.shape[0], p.shape[1], lr, self.betas[0], self.betas[1],
                               self.eps, st["step"], coef, int(clamp), tiled.data_ptr(), 1, 0, flags.ptr, stream)
                     _bump(p)
-                    owner.adopt_t16(tiled)
+                    owner.adopt_w8(tiled)
                 else:
                     lower = 0.0 if group == "scale" else -math.inf
                     _lib.call("bd_adamw", p.data_ptr(), grad.data_ptr(), st["exp_avg"].data_ptr(),

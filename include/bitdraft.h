@@ -72,6 +72,16 @@ int bd_tile_signs_t16(const float *latent, int64_t rows, int64_t cols, uint32_t 
 int bd_tile_gguf_t16(const int32_t *words, int64_t rows, int64_t cols, uint32_t *tiled,
                      int block_stride, int block_offset, bd_stream_t stream);
 
+/* W8 sign layout read by the decode feed-forward blocks (bd_ffn_*), the B
+ * fragments of int8 m16n8k32 with the tokens on the M side: n-tiles of 8 rows,
+ * words of 128 columns, [n-tile][word][lane] uint32 (bd_w8_words(rows, cols));
+ * lane 4 g + t, bit 8 j + 2 ks + r = sign of row 8 n + g, column 128 w + 32 ks +
+ * 16 r + 4 t + j (0 past the last column).  block_stride/offset interleave
+ * n-tiles of several matrices (2/0 and 2/1 for gate and up). */
+int64_t bd_w8_words(int64_t rows, int64_t cols);
+int bd_tile_signs_w8(const float *latent, int64_t rows, int64_t cols, uint32_t *tiled,
+                     int block_stride, int block_offset, int32_t *flags, bd_stream_t stream);
+
 /* =================================================================== quantizer
  * bd_quantize_codes replaces the activation quantizer of Projection.forward
  * (w1a1_eagle/model.py:128-140): code(t, k) = clamp(rint(clip(x*gain, +-bound)
@@ -110,9 +120,11 @@ int bd_projection_he4(const int8_t *codes, const int32_t *code_sums, int tokens,
  *   y = residual + down(silu(gate(n)) * up(n)),
  * gate/up: 4-bit codes with the shared gain/bound (model.py:184-187),
  * down: 8-bit codes with its own gain/bound (model.py:188-193).
- * signs_gate_up: T16 of gate and up interleaved (block_stride 2, offsets 0/1);
- * signs_down: T16 [hidden, inter].  tokens <= 32.  Workspace: see
- * bd_ffn_workspace_bytes; zero it once before first use (kernels leave it zeroed). */
+ * signs_gate_up: W8 of gate and up with n-tiles interleaved (block_stride 2,
+ * offsets 0/1); signs_down: W8 [hidden, inter].  tokens <= 32.  Three kernels:
+ * the quantizer (with the optional rms), gate/up + SwiGLU + the down
+ * projection's quantizer, and the down projection split over K by a 4-CTA
+ * cluster.  Workspace: bd_ffn_workspace_bytes. */
 typedef struct {
     const float *x;          /* [tokens, hidden] normalised input n            */
     const float *residual;   /* [tokens, hidden] or NULL                        */
@@ -334,8 +346,8 @@ int bd_ste_sign_backward(const float *grad, const float *grad2, const float *lat
  * bd_sum_squares / bd_grad_norm: fixed-order sum of squares partials, then
  *   total = sqrt(sum), clip_coef = min(1, max_norm / (total + 1e-6)).
  * bd_adamw_latent: AdamW of a latent matrix [rows, cols] fused with the clamp and
- *   the re-pack of its signs into T16 words (block_stride/offset as
- *   bd_tile_signs_t16; signs_t16 may be NULL).  bd_adamw: element AdamW with a
+ *   the re-pack of its signs into W8 words (block_stride/offset as
+ *   bd_tile_signs_w8; signs_w8 may be NULL).  bd_adamw: element AdamW with a
  *   lower clamp (-INFINITY for none).  clip_coef (device scalar) may be NULL.
  * bd_bound_latents: out = clamp(latent / (multiple mean|row|), -1, 1)
  *   (model.py:153-164); BD_FLAG_SIGN_CHANGE if a sign would change.
@@ -346,7 +358,7 @@ int bd_grad_norm(const float *partials, int64_t count, float max_norm, float *to
                  int32_t *flags, bd_stream_t stream);
 int bd_adamw_latent(float *param, const float *grad, float *exp_avg, float *exp_avg_sq, int64_t rows, int64_t cols,
                     double lr, double beta1, double beta2, double eps, long long step, const float *clip_coef,
-                    int clamp_latents, uint32_t *signs_t16, int block_stride, int block_offset, int32_t *flags,
+                    int clamp_latents, uint32_t *signs_w8, int block_stride, int block_offset, int32_t *flags,
                     bd_stream_t stream);
 int bd_adamw(float *param, const float *grad, float *exp_avg, float *exp_avg_sq, int64_t n, double lr, double beta1,
              double beta2, double eps, long long step, const float *clip_coef, float lower, int32_t *flags,

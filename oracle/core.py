@@ -169,6 +169,56 @@ def untile_codes_f8(buffer: np.ndarray, rows: int, cols: int) -> np.ndarray:
     return np.asarray(buffer, dtype=np.int8)[f8_offsets(rows, cols)]
 
 
+def c16_offsets(rows: int, cols: int, mtiles: int) -> np.ndarray:
+    """Byte offset of every (token, column) code in the C16 layout, ``[rows, cols]``.
+
+    C16 holds codes as int8 m16n8k32 A fragments with the tokens on the M side:
+    ``[k-step s = k // 32][m-tile][lane][16 bytes]``; lane ``4 (r % 8) + (kk % 16) // 4``
+    of token ``16 m + r`` holds register ``r // 8 + 2 (kk // 16)``, byte ``kk % 4``.
+    """
+    t = np.arange(rows)[:, None]
+    k = np.arange(cols)[None, :]
+    s, kk = k >> 5, k & 31
+    r, m = t & 15, t >> 4
+    lane = ((r & 7) << 2) + ((kk & 15) >> 2)
+    reg = (r >> 3) + ((kk >> 4) << 1)
+    return (((s * mtiles + m) * 32 + lane) << 4) + (reg << 2) + (kk & 3)
+
+
+def tile_codes_c16(codes: np.ndarray) -> np.ndarray:
+    """int8 C16 buffer of integer codes ``[tokens <= 32, cols]`` (padding zero)."""
+    rows, cols = codes.shape
+    mt = (rows + 15) // 16
+    out = np.zeros(codes_ld(cols) // 32 * mt * 512, dtype=np.int8)
+    out[c16_offsets(rows, cols, mt)] = codes.astype(np.int8)
+    return out
+
+
+def tile_signs_w8(latent: np.ndarray, stride: int = 1, offset: int = 0) -> np.ndarray:
+    """W8 sign words ``[n-tile][group][lane][4 words]`` (uint32) of an F32 matrix.
+
+    Lane ``4 g + t`` of n-tile ``n`` and 128-column word ``w`` (stored as word
+    ``w % 4`` of group ``w // 4``): bit ``8 j + 2 ks + r`` is
+    ``latent[8 n + g, 128 w + 32 ks + 16 r + 4 t + j] >= 0`` (0 past the matrix).
+    ``stride``/``offset`` interleave the n-tiles of several matrices.
+    """
+    latent = _f32(latent)
+    rows, cols = latent.shape
+    nt, ng = (rows + 7) // 8, ((cols + 127) // 128 + 3) // 4
+    nw = ng * 4
+    bits = np.zeros((nt * 8, nw * 128), dtype=np.uint64)
+    bits[:rows, :cols] = latent >= 0
+    b = bits.reshape(nt, 8, nw, 4, 2, 4, 4)  # n, g, w, ks, r, t, j
+    ks, r, j = np.meshgrid(np.arange(4), np.arange(2), np.arange(4), indexing="ij")
+    shifts = (8 * j + 2 * ks + r).astype(np.uint64)  # [ks, r, j]
+    ordered = b.transpose(0, 2, 1, 5, 3, 4, 6)  # n, w, g, t, ks, r, j
+    words = (ordered << shifts).sum(axis=(4, 5, 6)).astype(np.uint32).reshape(nt, ng, 4, 32)
+    words = words.transpose(0, 1, 3, 2)  # n, group, lane, word-in-group
+    out = np.zeros((nt * stride, ng, 32, 4), dtype=np.uint32)
+    out[offset::stride] = words
+    return out.reshape(-1)
+
+
 # --------------------------------------------------------------------------- quantizer
 
 

@@ -60,6 +60,18 @@ def test_tile_t16_matches_oracle(ops, shape):
     assert np.array_equal(got, core.tile_signs_t16(x))
 
 
+@pytest.mark.parametrize("shape", [(1, 1), (13, 300), (9728, 2560), (2560, 9728)])
+def test_tile_w8_matches_oracle(ops, shape):
+    latent = np.random.default_rng(shape[0] + shape[1]).standard_normal(shape).astype(np.float32)
+    latent.reshape(-1)[::7] = -0.0
+    got = ops.tile_w8(dev(latent)).cpu().numpy().view(np.uint32)
+    assert np.array_equal(got, core.tile_signs_w8(latent))
+    if shape[0] < 20000:
+        inter = ops.tile_gate_up_w8(dev(latent), dev(-latent)).cpu().numpy().view(np.uint32)
+        want = core.tile_signs_w8(latent, 2, 0) | core.tile_signs_w8(-latent, 2, 1)
+        assert np.array_equal(inter, want)
+
+
 def test_tile_from_gguf_equals_direct_full_size(ops):
     # size-independent property at the full gate shape: GGUF words -> T16 == latent -> T16
     g = torch.Generator(device=DEV).manual_seed(2)

@@ -206,8 +206,8 @@ def test_adamw_latent_matches_reference_and_repacks(bd):
         np.testing.assert_allclose(layer.latent_sign.detach().cpu().numpy(), f[f"param{step + 1}"], rtol=1e-6,
                                    atol=1e-7)
         # the fused re-pack equals a fresh tiling of the updated latent
-        fresh = bd.ops.tile_t16(layer.latent_sign.detach().contiguous())
-        assert torch.equal(layer.signs_t16(), fresh)
+        fresh = bd.ops.tile_w8(layer.latent_sign.detach().contiguous())
+        assert torch.equal(layer.signs_w8(), fresh)
 
 
 def test_grad_norm_and_clip_coefficient(bd):
@@ -238,6 +238,6 @@ def test_qat_update_smoke(bd):
     changed = [n for n, p in model.named_parameters() if not torch.equal(p.detach(), before[n])]
     assert any(n.endswith("latent_sign") for n in changed)
     assert any(n.endswith("log_gain") for n in changed)
-    for block in model.blocks:  # the T16 caches follow the updated latents
+    for block in model.blocks:  # the W8 caches follow the updated latents
         for proj in (block.gate, block.up, block.down):
-            assert torch.equal(proj.signs_t16(), bd.ops.tile_t16(proj.latent_sign.detach().contiguous()))
+            assert torch.equal(proj.signs_w8(), bd.ops.tile_w8(proj.latent_sign.detach().contiguous()))

@@ -73,6 +73,6 @@ def test_ffn_w1a1_config3_shapes(ops, tokens):
     assert err_h < 1e-5, err_h
     assert err_y < 1e-2, err_y
     # the down projection re-binarises the kernel's own hidden: its dots are exact
-    _, raw = ops.projection_w1a1(h, ffn.signs_down, ffn.scale_down, raw_dot=True)
+    _, raw = ops.projection_w1a1(h, ops.tile_t16(down.to(DEV)), ffn.scale_down, raw_dot=True)
     _, want_d, _ = core.w1a1_projection(h.cpu().numpy(), down.numpy(), ffn.scale_down.cpu().numpy())
     assert np.array_equal(raw.cpu().numpy(), want_d)

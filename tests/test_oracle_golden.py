@@ -338,3 +338,29 @@ def test_f8_layout_is_a_permutation(rows, cols):
     assert np.unique(off).size == rows * cols
     codes = np.random.default_rng(rows).integers(-127, 128, size=(rows, cols))
     assert np.array_equal(core.untile_codes_f8(core.tile_codes_f8(codes), rows, cols), codes.astype(np.int8))
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 1), (16, 256), (7, 300), (32, 2560)])
+def test_c16_layout_is_a_permutation(rows, cols):
+    mt = (rows + 15) // 16
+    off = core.c16_offsets(rows, cols, mt).reshape(-1)
+    assert len(np.unique(off)) == off.size and off.max() < core.codes_ld(cols) // 32 * mt * 512
+    codes = np.random.default_rng(rows * cols).integers(-127, 128, size=(rows, cols))
+    buf = core.tile_codes_c16(codes)
+    assert np.array_equal(buf[core.c16_offsets(rows, cols, mt)], codes)
+
+
+def test_w8_layout_bits():
+    rng = np.random.default_rng(5)
+    latent = rng.standard_normal((13, 300)).astype(np.float32)
+    words = core.tile_signs_w8(latent).reshape(2, 1, 32, 4)  # 3 words -> one group of 4
+    for row, col in [(0, 0), (7, 299), (12, 129), (8, 17), (3, 255)]:
+        n, g, w = row // 8, row % 8, col // 128
+        c = col % 128
+        ks, r, t, j = c // 32, (c % 32) // 16, (c % 16) // 4, c % 4
+        bit = (int(words[n, w // 4, 4 * g + t, w % 4]) >> (8 * j + 2 * ks + r)) & 1
+        assert bit == int(latent[row, col] >= 0)
+    assert words[1, :, 4 * 5:].sum() == 0  # rows 13..15 are padding
+    assert words[:, :, :, 3].sum() == 0    # the fourth word is past column 383
+    inter = core.tile_signs_w8(latent, 2, 1).reshape(4, 1, 32, 4)
+    assert np.array_equal(inter[1::2], words) and not inter[0::2].any()
