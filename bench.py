@@ -447,7 +447,7 @@ def workload_w1a1(args, pkg, device) -> list[dict]:
     H, F, M = 2560, 9728, 1024
     g = torch.Generator(device=device).manual_seed(4)
     gate, up, down = (torch.randn(s, generator=g, device=device) * 0.02 for s in ((F, H), (F, H), (H, F)))
-    ffn = ops.pack_ffn(gate, up, down)
+    ffn = ops.pack_ffn(gate, up, down, large=True)
     x = torch.randn((M, H), generator=g, device=device)
     flags = ops.Flags(device)
     for _ in range(3):

@@ -26,6 +26,7 @@ FLAG_BAD_TOKEN = 16
 FLAG_NONFINITE_STATE = 32
 FLAG_CACHE_OVERFLOW = 64
 FLAG_SIGN_CHANGE = 128
+FLAG_TIMEOUT = 256
 
 # Messages of the reference's ValueErrors for the same conditions.
 FLAG_MESSAGES = (
@@ -38,6 +39,8 @@ FLAG_MESSAGES = (
     (FLAG_CACHE_OVERFLOW, "F16 cache storage overflow"),
     (FLAG_SIGN_CHANGE, "bounded latent scale changed a sign"),
 )
+# Device-side failures that are not the reference's ValueErrors.
+FLAG_ERRORS = ((FLAG_TIMEOUT, "a bounded device wait timed out"),)
 
 
 class FfnHe4Args(ctypes.Structure):
@@ -54,6 +57,14 @@ class FfnW1Args(ctypes.Structure):
     _fields_ = [
         ("x", P), ("y", P), ("tokens", c_int), ("hidden", c_int64), ("inter", c_int64),
         ("signs_gate_up", P), ("scale_gate", P), ("scale_up", P), ("signs_down", P), ("scale_down", P),
+        ("hidden_out", P), ("workspace", P), ("workspace_bytes", c_size_t), ("flags", P),
+    ]
+
+
+class FfnLargeArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", P), ("y", P), ("tokens", c_int64), ("hidden", c_int64), ("inter", c_int64),
+        ("signs_gate_up_i8", P), ("scale_gate", P), ("scale_up", P), ("signs_down_i8", P), ("scale_down", P),
         ("hidden_out", P), ("workspace", P), ("workspace_bytes", c_size_t), ("flags", P),
     ]
 
@@ -80,6 +91,12 @@ SIGNATURES = {
     "bd_projection_w1a1_workspace_bytes": (c_size_t, [c_int64, c_int64]),
     "bd_projection_w1a1": (c_int, [P, c_int, c_int64, c_int64, P, P, P, P, P, c_size_t, P, P]),
     "bd_ffn_w1a1": (c_int, [ctypes.POINTER(FfnW1Args), P]),
+    "bd_i8_ld": (c_int64, [c_int64]),
+    "bd_i8_bytes": (c_int64, [c_int64, c_int64]),
+    "bd_tile_signs_i8": (c_int, [P, c_int64, c_int64, P, c_int, c_int, P, P]),
+    "bd_gemm_i8": (c_int, [P, c_int64, c_int64, P, c_int64, P, P]),
+    "bd_ffn_large_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64]),
+    "bd_ffn_w1a1_large": (c_int, [ctypes.POINTER(FfnLargeArgs), P]),
     "bd_quantize_rows_bf16": (c_int, [P, c_int64, c_int64, P, P, c_int, P, P, P, P]),
     "bd_sign_rows": (c_int, [P, c_int64, P, P, P, P]),
     "bd_he4_epilogue": (c_int, [P, c_int64, c_int64, P, P, P, c_int, P, P, P, P]),
@@ -170,7 +187,11 @@ def call(name: str, *args, kernels: int | None = None) -> None:
 
 
 def raise_flags(value: int) -> None:
-    """Turn device-reported flag bits into the reference's ValueError."""
+    """Turn device-reported flag bits into the reference's ValueError (RuntimeError
+    for device failures such as a timed-out wait)."""
+    for bit, message in FLAG_ERRORS:
+        if value & bit:
+            raise RuntimeError(message)
     for bit, message in FLAG_MESSAGES:
         if value & bit:
             raise ValueError(message)

@@ -100,8 +100,10 @@ __device__ __forceinline__ int64_t c16_offset(int token, int64_t k, int mtiles) 
     return (((s * mtiles + m) * 32 + lane) << 4) + (reg << 2) + (kk & 3);
 }
 
-// Byte offset of code (token, k): C16 when c16_mt > 0, else F8 with row stride ld.
+// Byte offset of code (token, k): C16 when c16_mt > 0, row-major int8 with row
+// stride ld when c16_mt < 0 (the tensor-core path), else F8 with row stride ld.
 __device__ __forceinline__ int64_t code_offset(int token, int64_t k, int64_t ld, int c16_mt) {
+    if (c16_mt < 0) return static_cast<int64_t>(token) * ld + k;
     return c16_mt > 0 ? c16_offset(token, k, c16_mt) : frag_offset(token, k, ld / 64);
 }
 

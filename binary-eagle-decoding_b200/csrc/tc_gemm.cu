@@ -1,0 +1,464 @@
+// Large-M projections on the 5th-generation tensor cores (tcgen05, TMEM accumulators).
+//
+// D[tokens x outs] = codes[tokens x K] . signs[outs x K]^T with int8 operands: codes are
+// the quantizer's integers (HE4 A4/A8) or +-1 (W1A1), signs are +-1 (an "I8" copy of
+// the latent signs, expanded once per latent version), so D is the exact +-1 dot in
+// int32 (kind::i8, s32 accumulators) -- bit-identical to the reference's fp32
+// linear of integers.  Both operands are 128-byte-swizzled K-major tiles loaded by
+// TMA (no multicast); K and the token / out edges beyond the tensors read as zeros.
+//
+// Persistent, warp-specialised CTA (one per SM): warp 0 issues TMA loads into a
+// 4-stage ring, warp 1 owns TMEM (two accumulator buffers of BN columns) and issues
+// tcgen05.mma (M = 128 tokens, N = BN outs, K = 32 per instruction) from one lane,
+// warps 2-5 drain an accumulator with tcgen05.ld (warp w reads TMEM lanes
+// 32 (w % 4) ..) and apply the fused epilogue while the next tile accumulates in
+// the other buffer.  Every mbarrier wait is bounded; a timeout raises
+// BD_FLAG_TIMEOUT, sets a CTA-wide abort flag that ends every role's loop, and the
+// CTA still frees its TMEM before it returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "kernels.cuh"
+
+namespace bd {
+
+constexpr int kTcBM = 128, kTcBK = 128, kTcStages = 4;
+constexpr uint32_t kTcSpin = 1u << 21;
+
+enum TcEpi : int {
+    TC_RAW = 0,           // out_i32 = D
+    TC_HE4 = 1,           // y = he4_value(D, scale[o], step, sums[t], mid[o]) (+ residual)
+    TC_W1A1 = 2,          // y = (D * scale[o]) * rs[t]
+    TC_W1A1_SWIGLU = 3,   // N tile = 128 gate + 128 up rows: h = silu(gate) * up, W1A1 values
+};
+
+struct TcArgs {
+    int64_t M, N, K;       // tokens, outs (as the reference sees them), reduction length
+    int64_t n_tiles;       // BN-column tiles of the (possibly interleaved) weight rows
+    int64_t m_tiles;
+    int64_t ld_out;        // output row stride (elements)
+    const float *scale, *scale2, *mid, *bound, *row_scale, *residual;
+    const int32_t *sums;
+    int code_bits;
+    float *out;
+    int32_t *out_i32;
+    int32_t *flags;
+};
+
+__device__ __forceinline__ uint32_t su32(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ void mb_init(uint64_t *b, uint32_t n) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(n));
+}
+__device__ __forceinline__ void mb_expect_tx(uint64_t *b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mb_arrive(uint64_t *b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+// Bounded parity wait: false after kTcSpin polls or once the CTA aborted.
+__device__ __forceinline__ bool mb_wait(uint64_t *b, uint32_t parity, volatile int *abort) {
+    for (uint32_t i = 0; i < kTcSpin; ++i) {
+        uint32_t ok;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(ok)
+            : "r"(su32(b)), "r"(parity)
+            : "memory");
+        if (ok) return true;
+        if ((i & 1023) == 1023 && *abort) return false;
+    }
+    *abort = 1;
+    return false;
+}
+__device__ __forceinline__ void tma_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            su32(dst)),
+        "l"(map), "r"(su32(bar)), "r"(c0), "r"(c1)
+        : "memory");
+}
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t sdesc(const void *p) {
+    const uint64_t a = su32(p);
+    return ((a >> 4) & 0x3FFFull) | (1ull << 16) | (static_cast<uint64_t>(1024 >> 4) << 32) | (1ull << 46) |
+           (2ull << 61);
+}
+// Instruction descriptor, kind::i8: s32 accumulators, signed A and B, K-major, N, M = 128.
+__host__ __device__ constexpr uint32_t idesc_i8(int n) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+           (static_cast<uint32_t>(kTcBM >> 4) << 24);
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const TcArgs a, const __grid_constant__ CUtensorMap ma,
+                                                         const __grid_constant__ CUtensorMap mb) {
+    extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sa = smem;                                // stages x 16 KB (tokens)
+    uint8_t *sb = smem + kTcStages * kTcBM * kTcBK;    // stages x BN x 128 B (weights)
+    __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], acc_full[2], acc_empty[2];
+    __shared__ uint32_t tmem_base;
+    __shared__ volatile int abort_flag;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t tiles = a.m_tiles * a.n_tiles;
+    const int nk = static_cast<int>((a.K + kTcBK - 1) / kTcBK);
+    constexpr uint32_t kCols = 2 * BN;  // two accumulator buffers
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kTcStages; ++s) {
+            mb_init(&full[s], 1);
+            mb_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mb_init(&acc_full[b], 1);
+            mb_init(&acc_empty[b], 4);  // one arrive per epilogue warp
+        }
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_base)),
+                     "n"(kCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = tmem_base;
+
+    if (warp == 0) {
+        if (lane == 0) {  // TMA producer
+            uint32_t it = 0;
+            for (int64_t t = blockIdx.x; t < tiles && !abort_flag; t += gridDim.x) {
+                const int m0 = static_cast<int>((t % a.m_tiles) * kTcBM);
+                const int n0 = static_cast<int>((t / a.m_tiles) * BN);
+                for (int k = 0; k < nk; ++k, ++it) {
+                    const int s = it % kTcStages;
+                    if (it >= kTcStages && !mb_wait(&empty[s], ((it / kTcStages) - 1) & 1, &abort_flag)) break;
+                    mb_expect_tx(&full[s], (kTcBM + BN) * kTcBK);
+                    tma_2d(sa + s * kTcBM * kTcBK, &ma, &full[s], k * kTcBK, m0);
+                    tma_2d(sb + s * BN * kTcBK, &mb, &full[s], k * kTcBK, n0);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {  // MMA issuer
+            constexpr uint32_t idesc = idesc_i8(BN);
+            uint32_t it = 0, lt = 0;
+            for (int64_t t = blockIdx.x; t < tiles && !abort_flag; t += gridDim.x, ++lt) {
+                const uint32_t b = lt & 1;
+                if (!mb_wait(&acc_empty[b], ((lt >> 1) & 1) ^ 1, &abort_flag)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t d = tmem + b * BN;
+                bool ok = true;
+                for (int k = 0; k < nk; ++k, ++it) {
+                    const int s = it % kTcStages;
+                    if (!mb_wait(&full[s], (it / kTcStages) & 1, &abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint64_t da = sdesc(sa + s * kTcBM * kTcBK), db = sdesc(sb + s * BN * kTcBK);
+#pragma unroll
+                    for (int kk = 0; kk < kTcBK / 32; ++kk) {
+                        const uint32_t accumulate = (k > 0 || kk > 0) ? 1u : 0u;
+                        asm volatile(
+                            "{\n .reg .pred p;\n setp.ne.u32 p, %4, 0;\n"
+                            " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+                            "l"(da + static_cast<uint64_t>(2 * kk)), "l"(db + static_cast<uint64_t>(2 * kk)), "r"(idesc),
+                            "r"(accumulate));
+                    }
+                    asm volatile(
+                        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(&empty[s]))
+                        : "memory");
+                }
+                asm volatile(
+                    "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(&acc_full[b]))
+                    : "memory");
+                if (!ok) break;
+            }
+        }
+    } else {  // epilogue warps 2..5
+        const int quarter = warp & 3;
+        const int row_in_tile = quarter * 32 + lane;
+        Quant q;
+        if (EPI == TC_HE4) q.init(__ldg(a.bound), a.code_bits);
+        uint32_t lt = 0;
+        for (int64_t t = blockIdx.x; t < tiles && !abort_flag; t += gridDim.x, ++lt) {
+            const uint32_t b = lt & 1;
+            if (!mb_wait(&acc_full[b], (lt >> 1) & 1, &abort_flag)) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const int64_t row = (t % a.m_tiles) * kTcBM + row_in_tile;
+            const int64_t n0 = (t / a.m_tiles) * BN;
+            const bool live_row = row < a.M;
+            const float rs = (EPI == TC_W1A1 || EPI == TC_W1A1_SWIGLU) && live_row ? __ldg(a.row_scale + row) : 0.0f;
+            const int cs = (EPI == TC_HE4 && live_row) ? __ldg(a.sums + row) : 0;
+            constexpr int OUT_COLS = EPI == TC_W1A1_SWIGLU ? BN / 2 : BN;
+            // in the SwiGLU tile, columns [0, BN/2) are gate rows and [BN/2, BN) the up rows of
+            // the same outputs (128-row blocks interleaved in the weight copy)
+            const int64_t o_base = EPI == TC_W1A1_SWIGLU ? (t / a.m_tiles) * (BN / 2) : n0;
+            for (int c = 0; c < OUT_COLS; c += 16) {
+                uint32_t v[16], u[16];
+                const uint32_t taddr = tmem + b * BN + (static_cast<uint32_t>(quarter * 32) << 16) + c;
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                    : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                      "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+                    : "r"(taddr));
+                if (EPI == TC_W1A1_SWIGLU) {
+                    asm volatile(
+                        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                        : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]), "=r"(u[7]),
+                          "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]), "=r"(u[14]),
+                          "=r"(u[15])
+                        : "r"(taddr + BN / 2));
+                }
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (!live_row) continue;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int64_t o = o_base + c + j;
+                    if (o >= a.N) break;
+                    const int D = static_cast<int>(v[j]);
+                    const int64_t idx = row * a.ld_out + o;
+                    if (EPI == TC_RAW) {
+                        a.out_i32[idx] = D;
+                    } else if (EPI == TC_HE4) {
+                        float y = he4_value(D, __ldg(a.scale + o), q.step, cs, __ldg(a.mid + o));
+                        if (a.residual) y = __fadd_rn(a.residual[idx], y);
+                        a.out[idx] = y;
+                    } else if (EPI == TC_W1A1) {
+                        a.out[idx] = __fmul_rn(__fmul_rn(static_cast<float>(D), __ldg(a.scale + o)), rs);
+                    } else {
+                        const float gv = __fmul_rn(__fmul_rn(static_cast<float>(D), __ldg(a.scale + o)), rs);
+                        const float uv =
+                            __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int>(u[j])), __ldg(a.scale2 + o)), rs);
+                        a.out[idx] = __fmul_rn(silu(gv), uv);
+                    }
+                }
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mb_arrive(&acc_empty[b]);
+        }
+    }
+    if (abort_flag && threadIdx.x == 0) set_flag(a.flags, BD_FLAG_TIMEOUT);
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(kCols));
+    }
+}
+
+// ------------------------------------------------------------------ host side
+
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void *p = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 2-D int8 tensor [rows, cols] with row stride ld bytes (multiple of 16), boxes of
+// box_rows x 128 bytes, 128-byte swizzle; reads past the tensor return zeros.
+static bool make_i8_map(CUtensorMap *m, const void *ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+    auto enc = tensor_map_encoder();
+    if (!enc || (reinterpret_cast<uintptr_t>(ptr) & 15) || (ld & 15)) return false;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld)};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(kTcBK), static_cast<cuuint32_t>(box_rows)};
+    cuuint32_t es[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(ptr), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static int sms_tc() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0, v = 0;
+        n = (cudaGetDevice(&dev) == cudaSuccess &&
+             cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0)
+                ? v
+                : 148;
+    }
+    return n;
+}
+
+template <int BN, int EPI>
+static int launch_tc_t(TcArgs a, const int8_t *codes, int64_t ld_codes, const int8_t *weights, int64_t w_rows,
+                       int64_t ld_w, cudaStream_t stream) {
+    CUtensorMap ma, mb;
+    if (!make_i8_map(&ma, codes, a.M, a.K, ld_codes, kTcBM) || !make_i8_map(&mb, weights, w_rows, a.K, ld_w, BN))
+        return BD_ERR_ALIGNMENT;
+    a.m_tiles = (a.M + kTcBM - 1) / kTcBM;
+    a.n_tiles = (w_rows + BN - 1) / BN;
+    const size_t smem = static_cast<size_t>(kTcStages) * (kTcBM + BN) * kTcBK + 1024;
+    auto kern = tc_gemm_kernel<BN, EPI>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
+        return BD_ERR_LAUNCH;
+    const int64_t tiles = a.m_tiles * a.n_tiles;
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(tiles, sms_tc()));
+    kern<<<grid, 192, smem, stream>>>(a, ma, mb);
+    BD_CHECK_LAUNCH();
+    return BD_OK;
+}
+
+int launch_tc_gemm(int epi, const TcArgs &a, const int8_t *codes, int64_t ld_codes, const int8_t *weights,
+                   int64_t w_rows, int64_t ld_w, cudaStream_t stream) {
+    if (a.M < 1 || a.N < 1 || a.K < 1) return BD_ERR_INVALID;
+    switch (epi) {
+        case TC_RAW:
+            return launch_tc_t<256, TC_RAW>(a, codes, ld_codes, weights, w_rows, ld_w, stream);
+        case TC_HE4:
+            return launch_tc_t<256, TC_HE4>(a, codes, ld_codes, weights, w_rows, ld_w, stream);
+        case TC_W1A1:
+            return launch_tc_t<256, TC_W1A1>(a, codes, ld_codes, weights, w_rows, ld_w, stream);
+        case TC_W1A1_SWIGLU:
+            return launch_tc_t<256, TC_W1A1_SWIGLU>(a, codes, ld_codes, weights, w_rows, ld_w, stream);
+        default:
+            return BD_ERR_INVALID;
+    }
+}
+
+// ------------------------------------------------------------------ I8 sign copies
+
+__global__ void tile_i8_kernel(const float *__restrict__ latent, int64_t rows, int64_t cols, int64_t ld,
+                               int8_t *__restrict__ out, int stride, int offset, int32_t *flags) {
+    const int64_t rows_pad = (rows + kTcBM - 1) / kTcBM * kTcBM;
+    const int64_t total = rows_pad * ld;
+    bool bad = false;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = i / ld, k = i - r * ld;
+        int8_t v = 0;
+        if (r < rows && k < cols) {
+            const float x = latent[r * cols + k];
+            bad |= !isfinite(x);
+            v = x >= 0.0f ? 1 : -1;
+        }
+        const int64_t orow = ((r / kTcBM) * stride + offset) * kTcBM + (r % kTcBM);
+        out[orow * ld + k] = v;
+    }
+    if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) set_flag(flags, BD_FLAG_NONFINITE_LATENT);
+}
+
+int64_t i8_ld(int64_t cols) { return (cols + 15) / 16 * 16; }
+
+}  // namespace bd
+
+using namespace bd;
+
+extern "C" int64_t bd_i8_ld(int64_t cols) { return cols < 1 ? 0 : i8_ld(cols); }
+
+extern "C" int64_t bd_i8_bytes(int64_t rows, int64_t cols) {
+    if (rows < 0 || cols < 0) return -1;
+    return (rows + kTcBM - 1) / kTcBM * kTcBM * i8_ld(cols);
+}
+
+extern "C" int bd_tile_signs_i8(const float *latent, int64_t rows, int64_t cols, int8_t *out, int block_stride,
+                                int block_offset, int32_t *flags, bd_stream_t stream) {
+    if (rows < 0 || cols < 1 || block_stride < 1 || block_offset < 0 || block_offset >= block_stride)
+        return BD_ERR_INVALID;
+    if (rows == 0) return BD_OK;
+    if (!latent || !out) return BD_ERR_INVALID;
+    const int64_t ld = i8_ld(cols);
+    const int64_t total = (rows + kTcBM - 1) / kTcBM * kTcBM * ld;
+    int64_t grid = (total + 255) / 256;
+    if (grid > 148 * 64) grid = 148 * 64;
+    tile_i8_kernel<<<static_cast<unsigned>(grid), 256, 0, stream>>>(latent, rows, cols, ld, out, block_stride,
+                                                                    block_offset, flags);
+    BD_CHECK_LAUNCH();
+    return BD_OK;
+}
+
+extern "C" int bd_gemm_i8(const int8_t *codes, int64_t tokens, int64_t k, const int8_t *signs_i8, int64_t outs,
+                          int32_t *dots, bd_stream_t stream) {
+    if (tokens < 1 || k < 1 || outs < 1 || !codes || !signs_i8 || !dots) return BD_ERR_INVALID;
+    TcArgs a{};
+    a.M = tokens;
+    a.N = outs;
+    a.K = k;
+    a.ld_out = outs;
+    a.out_i32 = dots;
+    return launch_tc_gemm(TC_RAW, a, codes, i8_ld(k), signs_i8, outs, i8_ld(k), stream);
+}
+
+// ------------------------------------------------------------------ W1A1 SwiGLU at any token count
+
+struct LargePieces {
+    int8_t *codes_x, *codes_h;
+    int32_t *sums;
+    float *mean_x, *mean_h, *hidden;
+    size_t bytes;
+};
+
+static LargePieces carve_large(void *ws, int64_t tokens, int64_t hidden, int64_t inter) {
+    char *base = static_cast<char *>(ws);
+    size_t off = 0;
+    auto take = [&](size_t n) {
+        off = (off + 255) & ~static_cast<size_t>(255);
+        char *p = base ? base + off : nullptr;
+        off += n;
+        return p;
+    };
+    LargePieces p{};
+    p.codes_x = reinterpret_cast<int8_t *>(take(static_cast<size_t>(tokens) * i8_ld(hidden)));
+    p.codes_h = reinterpret_cast<int8_t *>(take(static_cast<size_t>(tokens) * i8_ld(inter)));
+    p.sums = reinterpret_cast<int32_t *>(take(static_cast<size_t>(tokens) * sizeof(int32_t)));
+    p.mean_x = reinterpret_cast<float *>(take(static_cast<size_t>(tokens) * sizeof(float)));
+    p.mean_h = reinterpret_cast<float *>(take(static_cast<size_t>(tokens) * sizeof(float)));
+    p.hidden = reinterpret_cast<float *>(take(static_cast<size_t>(tokens) * inter * sizeof(float)));
+    p.bytes = off;
+    return p;
+}
+
+extern "C" size_t bd_ffn_large_workspace_bytes(int64_t tokens, int64_t hidden, int64_t inter) {
+    return carve_large(nullptr, tokens, hidden, inter).bytes;
+}
+
+extern "C" int bd_ffn_w1a1_large(const bd_ffn_large_args *p, bd_stream_t stream) {
+    if (!p || p->tokens < 1 || p->hidden < 1 || p->inter < 1 || p->tokens > 0x7fffffff) return BD_ERR_INVALID;
+    if (!p->x || !p->y || !p->signs_gate_up_i8 || !p->signs_down_i8 || !p->scale_gate || !p->scale_up ||
+        !p->scale_down)
+        return BD_ERR_INVALID;
+    const LargePieces w = carve_large(p->workspace, p->tokens, p->hidden, p->inter);
+    if (!p->workspace || w.bytes > p->workspace_bytes) return BD_ERR_WORKSPACE;
+    const int64_t T = p->tokens, H = p->hidden, F = p->inter;
+    float *hidden = p->hidden_out ? p->hidden_out : w.hidden;
+    int st = launch_binarize(p->x, T, H, i8_ld(H), w.codes_x, w.sums, w.mean_x, nullptr, 0, p->flags, stream, -1);
+    if (st) return st;
+    TcArgs g{};
+    g.M = T;
+    g.N = F;
+    g.K = H;
+    g.ld_out = F;
+    g.scale = p->scale_gate;
+    g.scale2 = p->scale_up;
+    g.row_scale = w.mean_x;
+    g.out = hidden;
+    g.flags = p->flags;
+    st = launch_tc_gemm(TC_W1A1_SWIGLU, g, w.codes_x, i8_ld(H), p->signs_gate_up_i8, 2 * ((F + kTcBM - 1) / kTcBM) * kTcBM,
+                        i8_ld(H), stream);
+    if (st) return st;
+    st = launch_binarize(hidden, T, F, i8_ld(F), w.codes_h, w.sums, w.mean_h, nullptr, 0, p->flags, stream, -1);
+    if (st) return st;
+    TcArgs d{};
+    d.M = T;
+    d.N = H;
+    d.K = F;
+    d.ld_out = H;
+    d.scale = p->scale_down;
+    d.row_scale = w.mean_h;
+    d.out = p->y;
+    d.flags = p->flags;
+    return launch_tc_gemm(TC_W1A1, d, w.codes_h, i8_ld(F), p->signs_down_i8, H, i8_ld(F), stream);
+}

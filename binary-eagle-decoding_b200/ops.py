@@ -16,6 +16,7 @@ from torch import Tensor
 from . import _lib
 
 MAX_DECODE_TOKENS = 32
+LARGE_M_TOKENS = 128  # token counts from here on go to the tensor cores when the weights allow it
 
 
 def _p(t: Tensor | None):
@@ -195,6 +196,8 @@ class PackedFFN:
     bound_gate_up: Tensor | None = None
     gain_down: Tensor | None = None
     bound_down: Tensor | None = None
+    signs_gate_up_i8: Tensor | None = None  # large-M copies (tensor-core path), see pack_ffn(large=True)
+    signs_down_i8: Tensor | None = None
 
 
 def w8_words(rows: int, cols: int) -> int:
@@ -230,18 +233,86 @@ def tile_gate_up_w8(gate: Tensor, up: Tensor, flags: Flags | None = None) -> Ten
 
 
 def pack_ffn(gate: Tensor, up: Tensor, down: Tensor, scale_gate: Tensor | None = None,
-             scale_up: Tensor | None = None, scale_down: Tensor | None = None) -> PackedFFN:
-    """Pack latent F32 matrices into W8 sign words; row scales default to ``mean|W|`` (model.py:123)."""
+             scale_up: Tensor | None = None, scale_down: Tensor | None = None, large: bool = False) -> PackedFFN:
+    """Pack latent F32 matrices into W8 sign words; row scales default to ``mean|W|`` (model.py:123).
+    ``large`` also keeps the +-1 int8 copies that the tensor-core path (token counts
+    in the hundreds) reads."""
     flags = Flags(gate.device)
     signs_gate_up = tile_gate_up_w8(gate.contiguous(), up.contiguous(), flags)
     signs_down = tile_w8(down.contiguous(), flags=flags)
+    gu_i8 = tile_gate_up_i8(gate.contiguous(), up.contiguous(), flags) if large else None
+    dn_i8 = tile_i8(down.contiguous(), flags=flags) if large else None
     flags.check()
     return PackedFFN(
         hidden=gate.shape[1], inter=gate.shape[0], signs_gate_up=signs_gate_up, signs_down=signs_down,
         scale_gate=(gate.abs().mean(-1) if scale_gate is None else scale_gate).contiguous(),
         scale_up=(up.abs().mean(-1) if scale_up is None else scale_up).contiguous(),
         scale_down=(down.abs().mean(-1) if scale_down is None else scale_down).contiguous(),
+        signs_gate_up_i8=gu_i8, signs_down_i8=dn_i8,
     )
+
+
+# --------------------------------------------------------------------------- tensor-core (large-M) path
+
+
+def tile_i8(latent: Tensor, block_stride: int = 1, block_offset: int = 0, out: Tensor | None = None,
+            flags: Flags | None = None) -> Tensor:
+    """+-1 int8 copy of the signs [rows padded to 128, bd_i8_ld(cols)] (tensor-core B operand)."""
+    if latent.dtype != torch.float32 or latent.ndim != 2:
+        raise ValueError("finite F32 sign matrix required")
+    device = _require_cuda(latent)
+    rows, cols = latent.shape
+    lib = _lib.load()
+    if out is None:
+        out = torch.zeros(int(lib.bd_i8_bytes(rows, cols)) * block_stride, dtype=torch.int8, device=device)
+    own = flags is None
+    flags = flags or Flags(device)
+    _lib.call("bd_tile_signs_i8", _p(latent), rows, cols, _p(out), block_stride, block_offset, flags.ptr,
+              _stream(device))
+    if own:
+        flags.check()
+    return out
+
+
+def tile_gate_up_i8(gate: Tensor, up: Tensor, flags: Flags | None = None) -> Tensor:
+    """Gate and up int8 signs with their 128-row blocks interleaved."""
+    out = torch.zeros(int(_lib.load().bd_i8_bytes(*gate.shape)) * 2, dtype=torch.int8, device=gate.device)
+    tile_i8(gate, 2, 0, out, flags)
+    tile_i8(up, 2, 1, out, flags)
+    return out
+
+
+def gemm_i8(codes: Tensor, k: int, signs_i8: Tensor, outs: int) -> Tensor:
+    """Exact int32 dots of int8 codes [tokens, bd_i8_ld(k)] (the first k columns) with +-1 signs."""
+    device = _require_cuda(codes, signs_i8)
+    if codes.dtype != torch.int8 or codes.ndim != 2 or codes.shape[1] != int(_lib.load().bd_i8_ld(k)):
+        raise ValueError("codes must be int8 [tokens, bd_i8_ld(k)]")
+    tokens = codes.shape[0]
+    dots = torch.empty((tokens, outs), dtype=torch.int32, device=device)
+    _lib.call("bd_gemm_i8", _p(codes), tokens, k, _p(signs_i8), outs, _p(dots), _stream(device))
+    return dots
+
+
+def ffn_w1a1_large(x: Tensor, ffn: PackedFFN, hidden_out: bool = False, flags: Flags | None = None):
+    """W1A1 SwiGLU block on the tensor cores (any token count; needs pack_ffn(large=True))."""
+    if ffn.signs_gate_up_i8 is None or ffn.signs_down_i8 is None:
+        raise ValueError("the tensor-core path needs pack_ffn(..., large=True)")
+    device = _require_cuda(x)
+    tokens = x.shape[0]
+    y = torch.empty((tokens, ffn.hidden), dtype=torch.float32, device=device)
+    h = torch.empty((tokens, ffn.inter), dtype=torch.float32, device=device) if hidden_out else None
+    nbytes = int(_lib.load().bd_ffn_large_workspace_bytes(tokens, ffn.hidden, ffn.inter))
+    ws = workspace(device, "ffn_large", nbytes)
+    own = flags is None
+    flags = flags or Flags(device)
+    args = _lib.FfnLargeArgs(
+        _p(x), _p(y), tokens, ffn.hidden, ffn.inter, _p(ffn.signs_gate_up_i8), _p(ffn.scale_gate),
+        _p(ffn.scale_up), _p(ffn.signs_down_i8), _p(ffn.scale_down), _p(h), _p(ws), ws.numel(), flags.ptr,
+    )
+    _lib.call("bd_ffn_w1a1_large", _lib.ctypes.byref(args), _stream(device), kernels=4)
+    if own:
+        flags.check()
+    return (y, h) if hidden_out else y
 
 
 def ffn_he4(x: Tensor, ffn: PackedFFN, residual: Tensor | None = None, hidden_out: bool = False,
@@ -335,7 +406,10 @@ def projection_w1a1(x: Tensor, signs_t16: Tensor, scale: Tensor, raw_dot: bool =
 
 
 def ffn_w1a1(x: Tensor, ffn: PackedFFN, hidden_out: bool = False, flags: Flags | None = None):
-    """W1A1 SwiGLU: each projection input is re-binarised with its own mean|x|."""
+    """W1A1 SwiGLU: each projection input is re-binarised with its own mean|x|.  Token
+    counts of 128 and more take the tensor-core path when the block was packed with it."""
+    if x.shape[0] >= LARGE_M_TOKENS and ffn.signs_gate_up_i8 is not None:
+        return ffn_w1a1_large(x, ffn, hidden_out, flags)
     device = _require_cuda(x)
     tokens = x.shape[0]
     y = torch.empty((tokens, ffn.hidden), dtype=torch.float32, device=device)

@@ -44,6 +44,7 @@ typedef struct CUstream_st *bd_stream_t; /* == cudaStream_t */
 #define BD_FLAG_NONFINITE_STATE 32u   /* non-finite values in a forward / update */
 #define BD_FLAG_CACHE_OVERFLOW 64u    /* model.py:100-101 "F16 cache storage overflow" */
 #define BD_FLAG_SIGN_CHANGE 128u      /* model.py:162-163 "bounded latent scale changed a sign" */
+#define BD_FLAG_TIMEOUT 256u          /* a bounded device wait ran out (the kernel returned early) */
 
 int bd_abi_version(void);
 const char *bd_status_string(int status);
@@ -186,6 +187,34 @@ int bd_projection_w1a1(const float *x, int tokens, int64_t in_features, int64_t 
  *   y = W1A1_down(silu(W1A1_gate(x)) * W1A1_up(x)).
  * Same argument block as bd_ffn_w1; workspace bd_ffn_workspace_bytes. */
 int bd_ffn_w1a1(const bd_ffn_w1_args *args, bd_stream_t stream);
+
+/* ============================================================ large-M (tensor cores)
+ * Token counts in the hundreds and more run on tcgen05 (int8 operands, s32 TMEM
+ * accumulators): activation codes [tokens, K] row-major int8 and an "I8" copy of
+ * the signs, +-1 int8 [rows, ld] with ld = bd_i8_ld(K) (a multiple of 16 bytes)
+ * and rows padded to 128 (bd_i8_bytes).  bd_tile_signs_i8 writes it from a latent
+ * matrix; block_stride/offset interleave 128-row blocks of several matrices (2/0
+ * and 2/1: gate and up rows of the same outputs side by side).  The dots are the
+ * exact +-1 dots (no rounding anywhere).
+ * bd_gemm_i8: dots[t, o] = sum_k codes[t, k] * signs[o, k] (int32).
+ * bd_ffn_w1a1_large: the W1A1 SwiGLU block of bd_ffn_w1a1 at any token count
+ * (x re-binarised per token, gate/up fused with silu(gate) * up, the hidden
+ * re-binarised, down). */
+int64_t bd_i8_ld(int64_t cols);
+int64_t bd_i8_bytes(int64_t rows, int64_t cols);
+int bd_tile_signs_i8(const float *latent, int64_t rows, int64_t cols, int8_t *out, int block_stride,
+                     int block_offset, int32_t *flags, bd_stream_t stream);
+int bd_gemm_i8(const int8_t *codes, int64_t tokens, int64_t k, const int8_t *signs_i8, int64_t outs,
+               int32_t *dots, bd_stream_t stream);
+typedef struct {
+    const float *x; float *y; int64_t tokens, hidden, inter;
+    const int8_t *signs_gate_up_i8;  /* gate and up interleaved by 128-row blocks */
+    const float *scale_gate, *scale_up;
+    const int8_t *signs_down_i8; const float *scale_down;
+    float *hidden_out; void *workspace; size_t workspace_bytes; int32_t *flags;
+} bd_ffn_large_args;
+size_t bd_ffn_large_workspace_bytes(int64_t tokens, int64_t hidden, int64_t inter);
+int bd_ffn_w1a1_large(const bd_ffn_large_args *args, bd_stream_t stream);
 
 /* ================================================================== acceptance
  * Greedy block acceptance (benchmarks/verifier.py:92-137 core loop 107-113,
