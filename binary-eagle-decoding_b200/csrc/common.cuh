@@ -135,6 +135,7 @@ __device__ __forceinline__ float he4_value(int dot, float scale, float step, int
     return __fadd_rn(a, b);
 }
 
-__device__ __forceinline__ float silu(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
+// x * sigmoid(x) through the fast exponential and a reciprocal (a few ulp from the exact value)
+__device__ __forceinline__ float silu(float x) { return __fmul_rn(x, __frcp_rn(__fadd_rn(1.0f, __expf(-x)))); }
 
 }  // namespace bd

@@ -10,8 +10,8 @@
 // Persistent, warp-specialised CTA (one per SM): warp 0 issues TMA loads into a
 // 4-stage ring, warp 1 owns TMEM (two accumulator buffers of BN columns) and issues
 // tcgen05.mma (M = 128 tokens, N = BN outs, K = 32 per instruction) from one lane,
-// warps 2-5 drain an accumulator with tcgen05.ld (warp w reads TMEM lanes
-// 32 (w % 4) ..) and apply the fused epilogue while the next tile accumulates in
+// warps 2-9 drain an accumulator with tcgen05.ld (warp w reads TMEM lanes
+// 32 (w % 4) .., one half of the columns) and apply the fused epilogue while the next tile accumulates in
 // the other buffer.  Every mbarrier wait is bounded; a timeout raises
 // BD_FLAG_TIMEOUT, sets a CTA-wide abort flag that ends every role's loop, and the
 // CTA still frees its TMEM before it returns.
@@ -93,7 +93,7 @@ __host__ __device__ constexpr uint32_t idesc_i8(int n) {
 }
 
 template <int BN, int EPI>
-__global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const TcArgs a, const __grid_constant__ CUtensorMap ma,
+__global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const __grid_constant__ CUtensorMap ma,
                                                          const __grid_constant__ CUtensorMap mb) {
     extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
@@ -113,7 +113,7 @@ __global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const TcArgs a, const _
         }
         for (int b = 0; b < 2; ++b) {
             mb_init(&acc_full[b], 1);
-            mb_init(&acc_empty[b], 4);  // one arrive per epilogue warp
+            mb_init(&acc_empty[b], 8);  // one arrive per epilogue warp
         }
         abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -179,28 +179,30 @@ __global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const TcArgs a, const _
                 if (!ok) break;
             }
         }
-    } else {  // epilogue warps 2..5
-        const int quarter = warp & 3;
+    } else {  // epilogue warps 2..9: warp w drains TMEM lanes 32 (w % 4) .., column half (w - 2) / 4
+        const int quarter = warp & 3, half = (warp - 2) >> 2;
         const int row_in_tile = quarter * 32 + lane;
         Quant q;
         if (EPI == TC_HE4) q.init(__ldg(a.bound), a.code_bits);
+        constexpr int OUT_COLS = EPI == TC_W1A1_SWIGLU ? BN / 2 : BN;
+        constexpr int HALF = OUT_COLS / 2;
+        const bool vec_out = (a.ld_out & 3) == 0 && (reinterpret_cast<uintptr_t>(EPI == TC_RAW ? static_cast<void *>(a.out_i32)
+                                                                                               : static_cast<void *>(a.out)) & 15) == 0;
         uint32_t lt = 0;
         for (int64_t t = blockIdx.x; t < tiles && !abort_flag; t += gridDim.x, ++lt) {
             const uint32_t b = lt & 1;
             if (!mb_wait(&acc_full[b], (lt >> 1) & 1, &abort_flag)) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const int64_t row = (t % a.m_tiles) * kTcBM + row_in_tile;
-            const int64_t n0 = (t / a.m_tiles) * BN;
             const bool live_row = row < a.M;
             const float rs = (EPI == TC_W1A1 || EPI == TC_W1A1_SWIGLU) && live_row ? __ldg(a.row_scale + row) : 0.0f;
             const int cs = (EPI == TC_HE4 && live_row) ? __ldg(a.sums + row) : 0;
-            constexpr int OUT_COLS = EPI == TC_W1A1_SWIGLU ? BN / 2 : BN;
             // in the SwiGLU tile, columns [0, BN/2) are gate rows and [BN/2, BN) the up rows of
             // the same outputs (128-row blocks interleaved in the weight copy)
-            const int64_t o_base = EPI == TC_W1A1_SWIGLU ? (t / a.m_tiles) * (BN / 2) : n0;
-            for (int c = 0; c < OUT_COLS; c += 16) {
+            const int64_t o_base = (EPI == TC_W1A1_SWIGLU ? (t / a.m_tiles) * (BN / 2) : (t / a.m_tiles) * BN) + half * HALF;
+            for (int c = 0; c < HALF; c += 16) {
                 uint32_t v[16], u[16];
-                const uint32_t taddr = tmem + b * BN + (static_cast<uint32_t>(quarter * 32) << 16) + c;
+                const uint32_t taddr = tmem + b * BN + (static_cast<uint32_t>(quarter * 32) << 16) + half * HALF + c;
                 asm volatile(
                     "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
                     : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
@@ -215,26 +217,56 @@ __global__ void __launch_bounds__(192, 1) tc_gemm_kernel(const TcArgs a, const _
                         : "r"(taddr + BN / 2));
                 }
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                if (!live_row) continue;
+                const int64_t o0 = o_base + c;
+                if (!live_row || o0 >= a.N) continue;
+                const bool full16 = o0 + 16 <= a.N;
+                // per-column parameters: the same 16 values for every lane (broadcast loads)
+                float s1[16], s2[16], md[16];
+                if (EPI != TC_RAW) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const bool live = full16 || o0 + j < a.N;
+                        s1[j] = live ? __ldg(a.scale + o0 + j) : 0.0f;
+                        s2[j] = (EPI == TC_W1A1_SWIGLU && live) ? __ldg(a.scale2 + o0 + j) : 0.0f;
+                        md[j] = (EPI == TC_HE4 && live) ? __ldg(a.mid + o0 + j) : 0.0f;
+                    }
+                }
+                float y[16];
+                int32_t di[16];
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
-                    const int64_t o = o_base + c + j;
-                    if (o >= a.N) break;
                     const int D = static_cast<int>(v[j]);
-                    const int64_t idx = row * a.ld_out + o;
-                    if (EPI == TC_RAW) {
-                        a.out_i32[idx] = D;
-                    } else if (EPI == TC_HE4) {
-                        float y = he4_value(D, __ldg(a.scale + o), q.step, cs, __ldg(a.mid + o));
-                        if (a.residual) y = __fadd_rn(a.residual[idx], y);
-                        a.out[idx] = y;
+                    di[j] = D;
+                    if (EPI == TC_HE4) {
+                        y[j] = he4_value(D, s1[j], q.step, cs, md[j]);
                     } else if (EPI == TC_W1A1) {
-                        a.out[idx] = __fmul_rn(__fmul_rn(static_cast<float>(D), __ldg(a.scale + o)), rs);
-                    } else {
-                        const float gv = __fmul_rn(__fmul_rn(static_cast<float>(D), __ldg(a.scale + o)), rs);
-                        const float uv =
-                            __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int>(u[j])), __ldg(a.scale2 + o)), rs);
-                        a.out[idx] = __fmul_rn(silu(gv), uv);
+                        y[j] = __fmul_rn(__fmul_rn(static_cast<float>(D), s1[j]), rs);
+                    } else if (EPI == TC_W1A1_SWIGLU) {
+                        const float gv = __fmul_rn(__fmul_rn(static_cast<float>(D), s1[j]), rs);
+                        const float uv = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int>(u[j])), s2[j]), rs);
+                        y[j] = __fmul_rn(silu(gv), uv);
+                    }
+                }
+                const int64_t idx = row * a.ld_out + o0;
+                if (EPI == TC_HE4 && a.residual) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        if (full16 || o0 + j < a.N) y[j] = __fadd_rn(a.residual[idx + j], y[j]);
+                }
+                if (full16 && vec_out) {
+#pragma unroll
+                    for (int j = 0; j < 16; j += 4) {
+                        if (EPI == TC_RAW)
+                            *reinterpret_cast<int4 *>(a.out_i32 + idx + j) = make_int4(di[j], di[j + 1], di[j + 2], di[j + 3]);
+                        else
+                            *reinterpret_cast<float4 *>(a.out + idx + j) = make_float4(y[j], y[j + 1], y[j + 2], y[j + 3]);
+                    }
+                } else {
+                    for (int j = 0; j < 16 && o0 + j < a.N; ++j) {
+                        if (EPI == TC_RAW)
+                            a.out_i32[idx + j] = di[j];
+                        else
+                            a.out[idx + j] = y[j];
                     }
                 }
             }
@@ -307,7 +339,7 @@ static int launch_tc_t(TcArgs a, const int8_t *codes, int64_t ld_codes, const in
         return BD_ERR_LAUNCH;
     const int64_t tiles = a.m_tiles * a.n_tiles;
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>(tiles, sms_tc()));
-    kern<<<grid, 192, smem, stream>>>(a, ma, mb);
+    kern<<<grid, 320, smem, stream>>>(a, ma, mb);
     BD_CHECK_LAUNCH();
     return BD_OK;
 }
