@@ -469,9 +469,10 @@ def workload_accept(args, pkg, device) -> list[dict]:
     draft = (torch.randn((B, n, V), generator=g, device=device) * 3).to(torch.bfloat16)
     drafts = torch.randint(0, V, (B, n), generator=g, device=device, dtype=torch.int32)
     flags = ops.Flags(device)
-    reps = max(args.steps // 20, 20)
-    greedy = _events_us(lambda: ops.accept_greedy(target, drafts, flags=flags), reps)
-    rej = _events_us(lambda: ops.accept_rejection(target, draft, drafts, seed=8, flags=flags), reps)
+    reps = max(args.steps // 200, 5)
+    # CUDA graphs of 8 calls each (the logits, 165 MB and 321 MB, exceed L2)
+    greedy = _graph_us(lambda i: ops.accept_greedy(target, drafts, flags=flags), 8, reps)
+    rej = _graph_us(lambda i: ops.accept_rejection(target, draft, drafts, seed=8 + i, flags=flags), 8, reps)
     flags.check()
     gb, rb = target.numel() * 2 + drafts.numel() * 4, (target.numel() + draft.numel()) * 2 + drafts.numel() * 4
     return [{"workload": "greedy block acceptance, logits bf16 [32, 17, 151936]", "metric": "HBM GB/s",

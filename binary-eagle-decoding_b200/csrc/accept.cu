@@ -1,8 +1,11 @@
 // Block-draft acceptance over vocabulary-sized bf16 logit rows.
 //
-// Greedy: one CTA per logit row computes the row argmax (strict '>' so the
-// lowest index wins ties, -0.0 == +0.0, non-finite logits flagged), and the last
-// CTA of each request walks the drafts (benchmarks/verifier.py:107-113).
+// Greedy: the grid streams all rows as equal contiguous ranges; each CTA folds
+// the argmax of every row piece it covers (strict '>' so the lowest index wins
+// ties, -0.0 == +0.0, non-finite logits flagged) into the row's 64-bit key with
+// an atomic max (the key order makes the result independent of arrival order),
+// and the last CTA to finish walks the drafts (benchmarks/verifier.py:107-113).
+// Plain row argmax keeps one CTA per row.
 #include <mutex>
 
 #include "common.cuh"
@@ -37,7 +40,8 @@ struct GreedyArgs {
     const int32_t *eog;
     int n_eog;
     int32_t *accepted, *next_token;
-    int32_t *counters;         // [requests], zero on entry, left zero
+    int32_t *counters;         // [requests] (per-row kernel) or [1] (stream kernel), zero on entry, left zero
+    unsigned long long *keys;  // [rows] argmax keys of the stream kernel, zero on entry, left zero
 };
 
 // Running maximum of one thread: indices arrive in increasing order, so a
@@ -151,13 +155,163 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_greedy_kernel(const Gre
     atomicExch(a.counters + request, 0);
 }
 
+
+constexpr int kStreamThreads = 512;
+
+// Greedy acceptance as one balanced stream: the grid (sized to the resident CTA
+// count) splits the rows' concatenated vectors into equal contiguous ranges; a
+// CTA folds each row piece of its range into the row's 64-bit key with an
+// atomic max (order-independent), and the last CTA to finish decodes every
+// key and walks every request's drafts.  VEC: 8 entries per unit (16-byte
+// loads), else one entry per unit.
+template <bool VEC>
+__global__ void __launch_bounds__(kStreamThreads) greedy_stream_kernel(const GreedyArgs a) {
+    __shared__ unsigned long long part[kStreamThreads / 32];
+    __shared__ int last;
+    const int64_t per_row = VEC ? a.vocab / 8 : a.vocab;
+    const int64_t total = a.rows * per_row;
+    const int64_t q = total / gridDim.x, rmd = total % gridDim.x;
+    const int64_t begin = q * blockIdx.x + min(static_cast<int64_t>(blockIdx.x), rmd);
+    const int64_t end = begin + q + (static_cast<int64_t>(blockIdx.x) < rmd ? 1 : 0);
+    __nv_bfloat162 hi = __float2bfloat162_rn(-1.0f), lo = __float2bfloat162_rn(1.0f);
+    for (int64_t seg = begin; seg < end;) {
+        const int64_t row = seg / per_row;
+        const int64_t seg_end = min(end, (row + 1) * per_row);
+        const int64_t row0 = row * per_row;
+        RunMax m;
+        if (VEC) {
+            const uint4 *p = reinterpret_cast<const uint4 *>(a.logits);
+            int64_t u = seg + threadIdx.x;
+            for (; u + 3 * kStreamThreads < seg_end; u += 4 * kStreamThreads) {
+                uint4 v[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) v[k] = ld_stream_u4(p + u + k * kStreamThreads);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const uint32_t base = static_cast<uint32_t>((u + k * kStreamThreads - row0) * 8);
+                    push_word(m, lo, hi, v[k].x, base);
+                    push_word(m, lo, hi, v[k].y, base + 2);
+                    push_word(m, lo, hi, v[k].z, base + 4);
+                    push_word(m, lo, hi, v[k].w, base + 6);
+                }
+            }
+            for (; u < seg_end; u += kStreamThreads) {
+                const uint4 v = ld_stream_u4(p + u);
+                const uint32_t base = static_cast<uint32_t>((u - row0) * 8);
+                push_word(m, lo, hi, v.x, base);
+                push_word(m, lo, hi, v.y, base + 2);
+                push_word(m, lo, hi, v.z, base + 4);
+                push_word(m, lo, hi, v.w, base + 6);
+            }
+        } else {
+            for (int64_t u = seg + threadIdx.x; u < seg_end; u += kStreamThreads) {
+                const uint32_t w = a.logits[u];
+                m.push(__uint_as_float(w << 16), static_cast<uint32_t>(u - row0));
+                const __nv_bfloat162 pair = *reinterpret_cast<const __nv_bfloat162 *>(&w);
+                hi = __hmax2_nan(hi, pair);
+                lo = __hmin2_nan(lo, pair);
+            }
+        }
+        unsigned long long best = m.i == 0xffffffffu ? 0ull : argmax_key(m.v, m.i);
+        best = warp_max_u64(best);
+        __syncthreads();  // the previous piece's reduction has read part[]
+        if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = best;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            unsigned long long k = part[0];
+#pragma unroll
+            for (int w = 1; w < kStreamThreads / 32; ++w) k = part[w] > k ? part[w] : k;
+            if (k) atomicMax(a.keys + row, k);
+        }
+        seg = seg_end;
+    }
+    const float2 hf = __bfloat1622float2(hi), lf = __bfloat1622float2(lo);
+    const bool bad = !isfinite(hf.x) || !isfinite(hf.y) || !isfinite(lf.x) || !isfinite(lf.y);
+    if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) set_flag(a.flags, BD_FLAG_NONFINITE_LOGITS);
+    if (threadIdx.x == 0) {
+        __threadfence();
+        last = atomicAdd(a.counters, 1) == static_cast<int>(gridDim.x) - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    // the last CTA: decode (and clear) every key, then walk every request
+    __threadfence();
+    for (int64_t r = threadIdx.x; r < a.rows; r += kStreamThreads) {
+        const unsigned long long k = atomicExch(a.keys + r, 0ull);
+        a.targets[r] = static_cast<int32_t>(~static_cast<uint32_t>(k & 0xffffffffull));
+    }
+    __syncthreads();
+    __threadfence_block();
+    const int64_t requests = a.rows / a.positions;
+    const int n = a.positions - 1;
+    for (int64_t request = threadIdx.x; request < requests; request += kStreamThreads) {
+        const int32_t *tg = a.targets + request * a.positions;
+        const int32_t *dr = a.drafts + request * n;
+        int acc = n;
+        int nxt = tg[n];
+        for (int i = 0; i < n; ++i) {
+            const int t = tg[i];
+            bool is_eog = false;
+            for (int e = 0; e < a.n_eog; ++e) is_eog |= a.eog[e] == t;
+            if (t != dr[i] || (is_eog && i + 1 < n)) {
+                acc = i;
+                nxt = t;
+                break;
+            }
+        }
+        a.accepted[request] = acc;
+        a.next_token[request] = nxt;
+    }
+    if (threadIdx.x == 0) atomicExch(a.counters, 0);
+}
+
 }  // namespace bd
 
 using namespace bd;
 
+namespace {
+size_t align256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+
+int launch_greedy_stream(GreedyArgs &a, bd_stream_t stream) {
+    static std::mutex mu;
+    static int grid[64][2] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return BD_ERR_DEVICE;
+    const bool vec = (a.vocab % 8) == 0 && (reinterpret_cast<uintptr_t>(a.logits) & 15) == 0;
+    int g = 0;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        int &cached = grid[dev][vec ? 1 : 0];
+        if (!cached) {
+            int sms = 0, per_sm = 0;
+            if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+                cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                    &per_sm, vec ? greedy_stream_kernel<true> : greedy_stream_kernel<false>, kStreamThreads, 0) !=
+                    cudaSuccess)
+                return BD_ERR_LAUNCH;
+            cached = sms * (per_sm > 0 ? per_sm : 1);
+        }
+        g = cached;
+    }
+    const int64_t units = a.rows * (vec ? a.vocab / 8 : a.vocab);
+    const int64_t min_units = vec ? 4 * kStreamThreads : 8 * kStreamThreads;  // at least a few loads per thread
+    int64_t blocks = (units + min_units - 1) / min_units;
+    if (blocks > g) blocks = g;
+    if (blocks < 1) blocks = 1;
+    if (vec)
+        greedy_stream_kernel<true><<<static_cast<unsigned>(blocks), kStreamThreads, 0, stream>>>(a);
+    else
+        greedy_stream_kernel<false><<<static_cast<unsigned>(blocks), kStreamThreads, 0, stream>>>(a);
+    BD_CHECK_LAUNCH();
+    return BD_OK;
+}
+}  // namespace
+
 extern "C" size_t bd_accept_workspace_bytes(int requests, int drafts) {
+    if (requests < 0 || drafts < 0) return 0;
     const size_t rows = static_cast<size_t>(requests) * (drafts + 1);
-    return ((rows * sizeof(int32_t) + 255) & ~static_cast<size_t>(255)) + static_cast<size_t>(requests) * 4 + 256;
+    return align256(rows * sizeof(int32_t)) + align256(static_cast<size_t>(requests) * sizeof(int32_t)) +
+           align256(rows * sizeof(unsigned long long));
 }
 
 extern "C" int bd_accept_greedy(const uint16_t *logits, int requests, int drafts, int64_t vocab,
@@ -171,7 +325,6 @@ extern "C" int bd_accept_greedy(const uint16_t *logits, int requests, int drafts
     if (!workspace || workspace_bytes < bd_accept_workspace_bytes(requests, drafts)) return BD_ERR_WORKSPACE;
     const size_t rows = static_cast<size_t>(requests) * (drafts + 1);
     char *ws = static_cast<char *>(workspace);
-    int32_t *counters = reinterpret_cast<int32_t *>(ws + ((rows * sizeof(int32_t) + 255) & ~static_cast<size_t>(255)));
     GreedyArgs a{};
     a.logits = logits;
     a.rows = static_cast<int64_t>(rows);
@@ -184,10 +337,10 @@ extern "C" int bd_accept_greedy(const uint16_t *logits, int requests, int drafts
     a.n_eog = n_eog;
     a.accepted = accepted;
     a.next_token = next_token;
-    a.counters = counters;
-    argmax_greedy_kernel<<<static_cast<unsigned>(rows), kArgmaxThreads, 0, stream>>>(a);
-    BD_CHECK_LAUNCH();
-    return BD_OK;
+    a.counters = reinterpret_cast<int32_t *>(ws + align256(rows * sizeof(int32_t)));
+    a.keys = reinterpret_cast<unsigned long long *>(ws + align256(rows * sizeof(int32_t)) +
+                                                    align256(static_cast<size_t>(requests) * sizeof(int32_t)));
+    return launch_greedy_stream(a, stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -205,7 +358,11 @@ extern "C" int bd_accept_greedy(const uint16_t *logits, int requests, int drafts
 // (different streams, or different host threads) race on it.
 constexpr int kNoAllocMaxRequests = 256;
 constexpr int kNoAllocMaxPositions = 33;  // up to 32 drafts + the bonus row
-static __device__ __align__(256) int32_t g_greedy_scratch[kNoAllocMaxRequests +
+// layout: counters [256] int32, argmax keys [256 x 33] u64, target rows [256 x 33] int32
+constexpr size_t kNoAllocKeysOffset = kNoAllocMaxRequests * sizeof(int32_t);
+constexpr size_t kNoAllocTargetsOffset =
+    kNoAllocKeysOffset + static_cast<size_t>(kNoAllocMaxRequests) * kNoAllocMaxPositions * sizeof(unsigned long long);
+static __device__ __align__(256) int32_t g_greedy_scratch[kNoAllocTargetsOffset / sizeof(int32_t) +
                                                           kNoAllocMaxRequests * kNoAllocMaxPositions];
 
 // Device address of the scratch array on the current device.  In host code the
@@ -237,14 +394,16 @@ extern "C" int bd_accept_greedy_noalloc(const uint16_t *logits, int requests, in
     if (requests > kNoAllocMaxRequests || drafts + 1 > kNoAllocMaxPositions) return BD_ERR_TOO_LARGE;
     int32_t *scratch = nullptr;
     if (int st = greedy_scratch(&scratch)) return st;
-    int32_t *counters = scratch;
-    if (cudaMemsetAsync(counters, 0, static_cast<size_t>(requests) * sizeof(int32_t), stream) != cudaSuccess)
+    const size_t rows = static_cast<size_t>(requests) * (drafts + 1);
+    char *base = reinterpret_cast<char *>(scratch);
+    // clear the counters and the keys this call uses (both are also left zero by every call)
+    if (cudaMemsetAsync(base, 0, kNoAllocKeysOffset + rows * sizeof(unsigned long long), stream) != cudaSuccess)
         return BD_ERR_LAUNCH;
     GreedyArgs a{};
     a.logits = logits;
-    a.rows = static_cast<int64_t>(requests) * (drafts + 1);
+    a.rows = static_cast<int64_t>(rows);
     a.vocab = vocab;
-    a.targets = targets ? targets : scratch + kNoAllocMaxRequests;
+    a.targets = targets ? targets : reinterpret_cast<int32_t *>(base + kNoAllocTargetsOffset);
     a.flags = flags;
     a.positions = drafts + 1;
     a.drafts = draft_tokens;
@@ -252,10 +411,9 @@ extern "C" int bd_accept_greedy_noalloc(const uint16_t *logits, int requests, in
     a.n_eog = n_eog;
     a.accepted = accepted;
     a.next_token = next_token;
-    a.counters = counters;
-    argmax_greedy_kernel<<<static_cast<unsigned>(a.rows), kArgmaxThreads, 0, stream>>>(a);
-    BD_CHECK_LAUNCH();
-    return BD_OK;
+    a.counters = scratch;
+    a.keys = reinterpret_cast<unsigned long long *>(base + kNoAllocKeysOffset);
+    return launch_greedy_stream(a, stream);
 }
 
 extern "C" int bd_argmax_rows_bf16(const uint16_t *logits, int64_t rows, int64_t vocab, int32_t *out,

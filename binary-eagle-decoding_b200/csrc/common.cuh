@@ -72,6 +72,43 @@ __device__ __forceinline__ void cp_async_wait_all() {
 __device__ __forceinline__ void grid_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 __device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n"); }
 
+// ---- mbarriers and 1-D bulk copies (global -> this CTA's shared memory, no multicast)
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+// Makes initialised mbarriers visible to the async proxy (bulk copies).
+__device__ __forceinline__ void mbar_init_fence() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+                 : "=r"(ok)
+                 : "r"(smem_u32(b)), "r"(parity)
+                 : "memory");
+    return ok != 0;
+}
+// Bounded wait for phase `parity` of an mbarrier: false after `polls` failed polls.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *b, uint32_t parity, uint32_t polls) {
+    for (uint32_t i = 0; i < polls; ++i)
+        if (mbar_try_wait(b, parity)) return true;
+    return false;
+}
+// Orders this thread's earlier generic-proxy shared-memory accesses before later bulk copies.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// `bytes` (a multiple of 16) from 16-byte aligned global `src` into 16-byte aligned
+// shared `dst`; completion is signalled on `bar` as transaction bytes.
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
 // B-fragment layout of int8 activation codes ("F8"): blocks of 8 tokens by 64
 // columns (a pair of 32-column k-steps), 512 bytes each, nt-major; inside a
 // block, lane l = 4 g + t (token 8 nt + g) holds 16 bytes: for k-step s of the

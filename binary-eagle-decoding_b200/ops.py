@@ -474,7 +474,7 @@ def accept_rejection(target_logits: Tensor, draft_logits: Tensor, drafts: Tensor
     device = _require_cuda(target_logits, draft_logits, drafts, eog)
     accepted = torch.empty(requests, dtype=torch.int32, device=device)
     nxt = torch.empty(requests, dtype=torch.int32, device=device)
-    ws = workspace(device, "rejection", int(_lib.load().bd_rejection_workspace_bytes(requests, n)))
+    ws = workspace(device, "rejection", int(_lib.load().bd_rejection_workspace_bytes(requests, n, target_logits.shape[2])))
     own = flags is None
     flags = flags or Flags(device)
     n_eog = 0 if eog is None else eog.numel()

@@ -247,13 +247,19 @@ int bd_accept_greedy_noalloc(const uint16_t *logits, int requests, int drafts, i
  * llama.cpp's common_sampler_sample_and_accept_n_rejection, un-vendored; its
  * in-tree pins are native/verifier-test.cpp:43-80 and the EOG break of
  * benchmarks/native.py:19-38).  Deterministic contract: Philox4x32-10 uniforms
- * (key = seed, counter = (request, position, purpose, offset)), a fixed-order
- * fp32 exp and softmax sums; accept d_i iff u q(d_i) < p(d_i); on rejection at
- * i sample from max(0, p_i - q_i), after n acceptances sample the bonus from
- * p_n; an accepted EOG that is not the last draft ends the round.
- * target_logits bf16 [requests][drafts+1][vocab], draft_logits bf16
- * [requests][drafts][vocab]; vocab <= 524288.  Outputs as bd_accept_greedy. */
-size_t bd_rejection_workspace_bytes(int requests, int drafts);
+ * (key = seed, counter = (request, position, purpose, offset)); e(x) by an
+ * exp2 range reduction with a degree-5 polynomial in fused multiply-adds;
+ * softmax statistics per 16384-entry chunk (max, fixed-order sum) combined per
+ * row; accept d_i iff u q(d_i) < p(d_i); on rejection at i sample from
+ * max(0, p_i - q_i) (p_i when that is zero), after n acceptances sample the
+ * bonus from p_n, by a fixed inverse-CDF search; an accepted EOG that is not
+ * the last draft ends the round.  target_logits bf16 [requests][drafts+1][vocab],
+ * draft_logits bf16 [requests][drafts][vocab]; vocab <= 524288; returns
+ * BD_ERR_TOO_LARGE when (drafts + 1) * 40 + (2 drafts + 1) * ceil(vocab / 16384)
+ * * 8 bytes exceed 160 KiB of shared memory.  Two kernels; the workspace holds
+ * per-chunk statistics and partial sums and needs no clearing.  Outputs as
+ * bd_accept_greedy. */
+size_t bd_rejection_workspace_bytes(int requests, int drafts, int64_t vocab);
 int bd_accept_rejection(const uint16_t *target_logits, const uint16_t *draft_logits, int requests, int drafts,
                         int64_t vocab, const int32_t *draft_tokens, const int32_t *eog, int n_eog,
                         unsigned long long seed, uint32_t offset, int32_t *accepted, int32_t *next_token,
