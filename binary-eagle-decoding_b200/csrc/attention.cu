@@ -5,7 +5,7 @@
 //
 // Split over keys (flash decoding): CTA (kv head, chunk of 128 keys) stages its
 // K and V rows in shared memory with cp.async; warp w owns q head
-// kv * groups + w and its 16 query rows.  S = Q K^T and O = P V run on
+// kv * groups + (w & 3), its 16 query rows and half (w >> 2) of the keys.  S = Q K^T and O = P V run on
 // m16n8k16 fp16 MMAs with fp32 accumulation (K fragments by ldmatrix, V by
 // ldmatrix.trans, P re-packed from the S accumulators).  Each CTA writes its
 // chunk's row maxima, row sums and un-normalised O; a combine kernel merges the
@@ -60,14 +60,30 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
+// 8 warps: warp w takes q head (w & 3) of the kv group and half (w >> 2) of the
+// chunk's keys; the two halves of a head merge through shared memory.
+constexpr int kAttnWarps = 8;
+constexpr int kHalfKeys = kKeys / 2;
+
 template <int kDim>
-__global__ void __launch_bounds__(128) attn_chunk_kernel(const AttnArgs a) {
+constexpr size_t attn_smem_bytes() {
+    // staged K and V rows, then the key-half exchange: per head 4 values per lane
+    // for every one of the kDim/8 O fragments plus (m, l) of its two rows
+    return 2 * static_cast<size_t>(kKeys) * row_bytes<kDim>() +
+           static_cast<size_t>(4) * (kDim / 8 * 4 + 4) * 32 * sizeof(float);
+}
+
+template <int kDim>
+__global__ void __launch_bounds__(kAttnWarps * 32) attn_chunk_kernel(const AttnArgs a) {
     constexpr int kRowBytes = row_bytes<kDim>();
+    constexpr int kX = kDim / 8 * 4 + 4;  // exchanged floats per lane
     extern __shared__ __align__(16) char sm[];
     char *ks = sm;
     char *vs = sm + kKeys * kRowBytes;
+    float *xch = reinterpret_cast<float *>(sm + 2 * kKeys * kRowBytes);  // [head][kX][32]
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
+    const int hw = warp & 3, kh = warp >> 2;
     const int kvh = blockIdx.x, chunk = blockIdx.y;
     const int groups = a.heads / a.kv_heads;
     const int key0 = chunk * kKeys;
@@ -82,9 +98,9 @@ __global__ void __launch_bounds__(128) attn_chunk_kernel(const AttnArgs a) {
         cp_async16(ks + r * kRowBytes + c * 16, a.k + src, live ? 16 : 0);
         cp_async16(vs + r * kRowBytes + c * 16, a.v + src, live ? 16 : 0);
     }
-    // Q fragments of this warp's head: rows are query slots (A operand, row-major 16 x 128)
-    const int head = kvh * groups + warp;
-    const bool head_live = warp < groups;
+    // Q fragments of this warp's head: rows are query slots (A operand, row-major 16 x kDim)
+    const int head = kvh * groups + hw;
+    const bool head_live = hw < groups;
     uint32_t qa[kDim / 16][4];
 #pragma unroll
     for (int s = 0; s < kDim / 16; ++s) {
@@ -99,85 +115,117 @@ __global__ void __launch_bounds__(128) attn_chunk_kernel(const AttnArgs a) {
     }
     cp_async_wait_all();
     __syncthreads();
-    if (!head_live) return;
 
-    // S = Q K^T over the chunk: 16 n-tiles of 8 keys
-    float s_acc[kKeys / 8][4];
-#pragma unroll
-    for (int n = 0; n < kKeys / 8; ++n)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) s_acc[n][i] = 0.0f;
-#pragma unroll
-    for (int n = 0; n < kKeys / 8; ++n) {
-#pragma unroll
-        for (int s2 = 0; s2 < kDim / 32; ++s2) {
-            // x4: matrices (d 0-7, 8-15) of k-step 2*s2 and (d 0-7, 8-15) of k-step 2*s2+1 for keys 8n..8n+7
-            uint32_t b[4];
-            const int mi = lane >> 3, r = lane & 7;
-            ldmatrix_x4(b, ks + (n * 8 + r) * kRowBytes + (s2 * 32 + mi * 8) * 2);
-            mma_f16_16816(s_acc[n], qa[2 * s2][0], qa[2 * s2][1], qa[2 * s2][2], qa[2 * s2][3], b[0], b[1]);
-            mma_f16_16816(s_acc[n], qa[2 * s2 + 1][0], qa[2 * s2 + 1][1], qa[2 * s2 + 1][2], qa[2 * s2 + 1][3], b[2],
-                          b[3]);
-        }
-    }
-    // scale, mask, row maxima (rows g and g + 8 of this lane)
-    float m[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-    for (int n = 0; n < kKeys / 8; ++n)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int row = g + 8 * (i >> 1);
-            const int key = key0 + n * 8 + 2 * t + (i & 1);
-            bool ok = key < a.keys && row < a.tokens;
-            if (a.windowed) {
-                const int64_t dist = a.anchor + row - key;
-                ok = ok && (dist < a.window && -dist < a.window);
-            }
-            const float v = ok ? s_acc[n][i] * a.scale : -INFINITY;
-            s_acc[n][i] = v;
-            m[i >> 1] = fmaxf(m[i >> 1], v);
-        }
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-        m[r] = fmaxf(m[r], __shfl_xor_sync(0xffffffffu, m[r], 1));
-        m[r] = fmaxf(m[r], __shfl_xor_sync(0xffffffffu, m[r], 2));
-    }
-    float l[2] = {0.0f, 0.0f};
-#pragma unroll
-    for (int n = 0; n < kKeys / 8; ++n)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float mm = m[i >> 1];
-            const float p = mm == -INFINITY ? 0.0f : __expf(s_acc[n][i] - mm);
-            s_acc[n][i] = p;
-            l[i >> 1] += p;
-        }
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-        l[r] += __shfl_xor_sync(0xffffffffu, l[r], 1);
-        l[r] += __shfl_xor_sync(0xffffffffu, l[r], 2);
-    }
-    // O = P V: P (16 x 128 keys) re-packed from the S accumulators as A fragments
+    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f};
     float o_acc[kDim / 8][4];
 #pragma unroll
     for (int n = 0; n < kDim / 8; ++n)
 #pragma unroll
         for (int i = 0; i < 4; ++i) o_acc[n][i] = 0.0f;
+    if (head_live) {
+        // S = Q K^T over this warp's 64 keys: 8 n-tiles of 8 keys
+        const int kbase = kh * kHalfKeys;
+        float s_acc[kHalfKeys / 8][4];
 #pragma unroll
-    for (int kk = 0; kk < kKeys / 16; ++kk) {
-        const uint32_t pa0 = pack_half2(s_acc[2 * kk][0], s_acc[2 * kk][1]);
-        const uint32_t pa1 = pack_half2(s_acc[2 * kk][2], s_acc[2 * kk][3]);
-        const uint32_t pa2 = pack_half2(s_acc[2 * kk + 1][0], s_acc[2 * kk + 1][1]);
-        const uint32_t pa3 = pack_half2(s_acc[2 * kk + 1][2], s_acc[2 * kk + 1][3]);
+        for (int n = 0; n < kHalfKeys / 8; ++n)
 #pragma unroll
-        for (int n2 = 0; n2 < kDim / 16; ++n2) {
-            // x4.trans: (keys 16kk..+7, d 16n2..+7), (keys +8..15, d 16n2..+7), (keys 16kk..+7, d +8..15), (keys +8..15, d +8..15)
-            uint32_t b[4];
-            const int mi = lane >> 3, r = lane & 7;
-            ldmatrix_x4_trans(b, vs + (kk * 16 + (mi & 1) * 8 + r) * kRowBytes + (n2 * 16 + (mi >> 1) * 8) * 2);
-            mma_f16_16816(o_acc[2 * n2], pa0, pa1, pa2, pa3, b[0], b[1]);
-            mma_f16_16816(o_acc[2 * n2 + 1], pa0, pa1, pa2, pa3, b[2], b[3]);
+            for (int i = 0; i < 4; ++i) s_acc[n][i] = 0.0f;
+#pragma unroll
+        for (int s2 = 0; s2 < kDim / 32; ++s2) {
+#pragma unroll
+            for (int n = 0; n < kHalfKeys / 8; ++n) {
+                // x4: matrices (d 0-7, 8-15) of k-step 2*s2 and (d 0-7, 8-15) of k-step 2*s2+1 for 8 keys
+                uint32_t b[4];
+                const int mi = lane >> 3, r = lane & 7;
+                ldmatrix_x4(b, ks + (kbase + n * 8 + r) * kRowBytes + (s2 * 32 + mi * 8) * 2);
+                mma_f16_16816(s_acc[n], qa[2 * s2][0], qa[2 * s2][1], qa[2 * s2][2], qa[2 * s2][3], b[0], b[1]);
+                mma_f16_16816(s_acc[n], qa[2 * s2 + 1][0], qa[2 * s2 + 1][1], qa[2 * s2 + 1][2], qa[2 * s2 + 1][3],
+                              b[2], b[3]);
+            }
         }
+        // scale, mask, row maxima (rows g and g + 8 of this lane)
+        const int kq0 = key0 + kbase + 2 * t;
+#pragma unroll
+        for (int n = 0; n < kHalfKeys / 8; ++n)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int row = g + 8 * (i >> 1);
+                const int key = kq0 + n * 8 + (i & 1);
+                bool ok = key < a.keys && row < a.tokens;
+                if (a.windowed) {
+                    const int64_t dist = a.anchor + row - key;
+                    ok = ok && (dist < a.window && -dist < a.window);
+                }
+                const float v = ok ? s_acc[n][i] * a.scale : -INFINITY;
+                s_acc[n][i] = v;
+                m[i >> 1] = fmaxf(m[i >> 1], v);
+            }
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            m[r] = fmaxf(m[r], __shfl_xor_sync(0xffffffffu, m[r], 1));
+            m[r] = fmaxf(m[r], __shfl_xor_sync(0xffffffffu, m[r], 2));
+        }
+#pragma unroll
+        for (int n = 0; n < kHalfKeys / 8; ++n)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float mm = m[i >> 1];
+                const float p = mm == -INFINITY ? 0.0f : __expf(s_acc[n][i] - mm);
+                s_acc[n][i] = p;
+                l[i >> 1] += p;
+            }
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            l[r] += __shfl_xor_sync(0xffffffffu, l[r], 1);
+            l[r] += __shfl_xor_sync(0xffffffffu, l[r], 2);
+        }
+        // O = P V over the 64 keys: P re-packed from the S accumulators as A fragments
+#pragma unroll
+        for (int kk = 0; kk < kHalfKeys / 16; ++kk) {
+            const uint32_t pa0 = pack_half2(s_acc[2 * kk][0], s_acc[2 * kk][1]);
+            const uint32_t pa1 = pack_half2(s_acc[2 * kk][2], s_acc[2 * kk][3]);
+            const uint32_t pa2 = pack_half2(s_acc[2 * kk + 1][0], s_acc[2 * kk + 1][1]);
+            const uint32_t pa3 = pack_half2(s_acc[2 * kk + 1][2], s_acc[2 * kk + 1][3]);
+#pragma unroll
+            for (int n2 = 0; n2 < kDim / 16; ++n2) {
+                uint32_t b[4];
+                const int mi = lane >> 3, r = lane & 7;
+                ldmatrix_x4_trans(b, vs + (kbase + kk * 16 + (mi & 1) * 8 + r) * kRowBytes + (n2 * 16 + (mi >> 1) * 8) * 2);
+                mma_f16_16816(o_acc[2 * n2], pa0, pa1, pa2, pa3, b[0], b[1]);
+                mma_f16_16816(o_acc[2 * n2 + 1], pa0, pa1, pa2, pa3, b[2], b[3]);
+            }
+        }
+        // the second key half hands its state to the first through shared memory
+        if (kh == 1) {
+            float *x = xch + hw * kX * 32 + lane;
+#pragma unroll
+            for (int n = 0; n < kDim / 8; ++n)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) x[(n * 4 + i) * 32] = o_acc[n][i];
+            x[(kX - 4) * 32] = m[0];
+            x[(kX - 3) * 32] = m[1];
+            x[(kX - 2) * 32] = l[0];
+            x[(kX - 1) * 32] = l[1];
+        }
+    }
+    __syncthreads();
+    if (!head_live || kh == 1) return;
+    {
+        const float *x = xch + hw * kX * 32 + lane;
+        float f0[2], f1[2];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const float m1 = x[(kX - 4 + r) * 32], l1 = x[(kX - 2 + r) * 32];
+            const float mx = fmaxf(m[r], m1);
+            f0[r] = mx == -INFINITY ? 0.0f : __expf(m[r] - mx);
+            f1[r] = mx == -INFINITY ? 0.0f : __expf(m1 - mx);
+            l[r] = l[r] * f0[r] + l1 * f1[r];
+            m[r] = mx;
+        }
+#pragma unroll
+        for (int n = 0; n < kDim / 8; ++n)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) o_acc[n][i] = o_acc[n][i] * f0[i >> 1] + x[(n * 4 + i) * 32] * f1[i >> 1];
     }
     // partials: un-normalised O, row max and row sum of this chunk
     float *po = a.part_o + ((static_cast<int64_t>(chunk) * a.heads + head) * 16) * kDim;
@@ -257,11 +305,11 @@ extern "C" size_t bd_attention_workspace_bytes(int heads, int head_dim, int keys
 
 template <int D>
 static int launch_attention(const AttnArgs &a, int kv_heads, int tokens, int heads, cudaStream_t stream) {
-    const size_t smem = 2 * kKeys * row_bytes<D>();
+    const size_t smem = attn_smem_bytes<D>();
     if (cudaFuncSetAttribute(attn_chunk_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess)
         return BD_ERR_LAUNCH;
-    int st = launch_pdl(attn_chunk_kernel<D>, dim3(kv_heads, a.chunks), dim3(128), smem, stream, a);
+    int st = launch_pdl(attn_chunk_kernel<D>, dim3(kv_heads, a.chunks), dim3(kAttnWarps * 32), smem, stream, a);
     if (st) return st;
     return launch_pdl(attn_combine_kernel<D>, dim3(tokens, heads), dim3(D), 0, stream, a);
 }
