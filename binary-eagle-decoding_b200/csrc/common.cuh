@@ -72,7 +72,7 @@ __device__ __forceinline__ void cp_async_wait_all() {
 __device__ __forceinline__ void grid_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 __device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n"); }
 
-// ---- mbarriers and 1-D bulk copies (global -> this CTA's shared memory, no multicast)
+// ---- mbarriers and 1-D bulk copies (global memory -> this CTA's own shared memory)
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

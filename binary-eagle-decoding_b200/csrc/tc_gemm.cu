@@ -5,7 +5,7 @@
 // the latent signs, expanded once per latent version), so D is the exact +-1 dot in
 // int32 (kind::i8, s32 accumulators) -- bit-identical to the reference's fp32
 // linear of integers.  Both operands are 128-byte-swizzled K-major tiles loaded by
-// TMA (no multicast); K and the token / out edges beyond the tensors read as zeros.
+// TMA, each CTA loading its own tiles; K and the token / out edges beyond the tensors read as zeros.
 //
 // Persistent, warp-specialised CTA (one per SM): warp 0 issues TMA loads into a
 // 4-stage ring, warp 1 owns TMEM (two accumulator buffers of BN columns) and issues
