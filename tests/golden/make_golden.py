@@ -239,6 +239,44 @@ def tiny_he4_fixture() -> None:
     np.savez(HERE / "tiny_he4.npz", **arrays)
 
 
+def export_fixture() -> None:
+    """The FFN payloads ``prepare`` (``w1a1_eagle/numerical/export.py:174-193``) exports for the
+    tiny six-layer HE4 with perturbed quantizers: packed signs, clamped scales, midpoints,
+    gains, and the per-projection bits / clip metadata."""
+    cfg = Geometry(hidden=4, intermediate=8, heads=2, kv_heads=1, head_dim=2, window=4096)
+    f = np.load(HERE / "tiny_he4.npz")
+    tensors = {k[2:]: torch.from_numpy(f[k]) for k in f.files if k.startswith("t_")}
+    model = HE4(tensors, torch.from_numpy(f["vocabulary"]), 19, cfg)
+    perturb = torch.Generator().manual_seed(29)
+    arrays = {}
+    with torch.no_grad():
+        for block in model.blocks:
+            block.gate.log_gain.copy_(0.3 * torch.randn(4, generator=perturb))
+            block.gate.log_clip.fill_(float(0.3 * torch.randn((), generator=perturb)))
+            block.down.log_gain.copy_(0.3 * torch.randn(8, generator=perturb))
+            block.down.log_clip.fill_(float(0.3 * torch.randn((), generator=perturb)))
+            for q in (block.gate, block.up, block.down):
+                q.midpoint.copy_(0.05 * torch.randn(q.midpoint.shape, generator=perturb))
+                q.scale.copy_(q.scale - 0.07)  # some scales below zero: the export clamps them
+                q.latent_sign.copy_(q.latent_sign + 0.05 * torch.randn(q.latent_sign.shape, generator=perturb))
+    for index, block in enumerate(model.blocks):
+        for name, q in (("gate", block.gate), ("up", block.up), ("down", block.down)):
+            base = f"blk.{index}.ffn_{name}"
+            arrays[base + ".latent"] = f32(q.latent_sign)
+            arrays[base + ".scale_param"] = f32(q.scale)
+            arrays[base + ".midpoint_param"] = f32(q.midpoint)
+            arrays[base + ".log_gain_param"] = f32(q.log_gain)
+            arrays[base + ".log_clip_param"] = f32(q.log_clip)
+            arrays[base + ".w1a1_packed"] = packed_signs(q.latent_sign)
+            arrays[base + ".w1a1_scale"] = f32(q.scale.clamp_min(0))
+            arrays[base + ".w1ax_midpoint"] = f32(q.midpoint)
+            if name != "up":
+                arrays[base + ".w1ax_gain"] = f32(q.log_gain.detach().float().cpu().exp())
+            arrays[base + ".w1ax.bits"] = np.array(q.bits, dtype=np.uint32)
+            arrays[base + ".w1ax.clip"] = np.array(float(q.log_clip.detach().float().cpu().exp()), dtype=np.float32)
+    np.savez(HERE / "export_ffn.npz", **arrays)
+
+
 def layer_fixture() -> None:
     """Inputs of the reference's cache-layer golden case (``test_model.py:555-581``)."""
     arrays = {}
@@ -348,6 +386,7 @@ def main() -> None:
     he4_ffn_fixture()
     w1_fixture()
     tiny_he4_fixture()
+    export_fixture()
     layer_fixture()
     arithmetic_fixture()
     greedy_fixture()
