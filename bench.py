@@ -482,6 +482,29 @@ def workload_accept(args, pkg, device) -> list[dict]:
              "us_per_call": rej, "algorithmic_bytes": rb}]
 
 
+def workload_ingest(args, pkg, device) -> list[dict]:
+    """Teacher-feature ingestion of config-5 captures: per sequence 4 taps x 2048 rows x 2560
+    fp16, tap-major -> token-major fp16 features with the finiteness scan."""
+    ops = pkg.ops
+    taps, rows, hidden, seqs = 4, 2048, 2560, 8
+    g = torch.Generator(device=device).manual_seed(9)
+    caps = [torch.randn((taps, rows, hidden), generator=g, device=device).half() for _ in range(seqs)]
+    flags = ops.Flags(device)
+    us = _graph_us(lambda i: ops.ingest_taps(caps[i % seqs], torch.float16, flags=flags), seqs,
+                   max(args.steps // 100, 10))
+    nbytes = 2 * taps * rows * hidden * 2  # read + write
+    host = caps[0].cpu().pin_memory()
+    for _ in range(3):
+        ops.ingest_taps(host, torch.float16, device=device, flags=flags)
+    torch.cuda.synchronize()
+    e2e = _events_us(lambda: ops.ingest_taps(host, torch.float16, device=device, flags=flags), 10)
+    flags.check()
+    return [{"workload": "teacher-feature ingestion, 4 taps x 2048 rows x 2560 fp16 per sequence",
+             "metric": "HBM GB/s (read + write)", "value": nbytes / (us * 1e-6) / 1e9, "unit": "GB/s",
+             "us_per_sequence": us, "e2e_us_per_sequence_from_pinned_host": e2e,
+             "h2d_bytes_per_sequence": nbytes // 2}]
+
+
 def workload_qat(args, pkg, device, rank: int, world: int) -> list[dict]:
     """Config 5: QAT update of the 4-layer drafter, per GPU 8 sequences x 2048 positions,
     32 windows of 16 slots each; data parallel (NCCL all-reduce) under torchrun."""
@@ -538,6 +561,8 @@ def run_workload(args, rank: int, world: int, local_rank: int) -> None:
         lines = workload_w1a1(args, pkg, device)
     elif args.workload == "accept":
         lines = workload_accept(args, pkg, device)
+    elif args.workload == "ingest":
+        lines = workload_ingest(args, pkg, device)
     else:
         lines = workload_qat(args, pkg, device, rank, world)
     if world > 1:
@@ -557,7 +582,7 @@ def main() -> None:
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     parser.add_argument("--profile-round", action="store_true",
                         help="run one draft round between cudaProfilerStart/Stop and exit")
-    parser.add_argument("--workload", choices=("round", "ffn", "w1a1", "accept", "qat"), default="round",
+    parser.add_argument("--workload", choices=("round", "ffn", "w1a1", "accept", "ingest", "qat"), default="round",
                         help="round: the headline draft round; the others measure one hot-path workload each")
     parser.add_argument("--qat-sequences", type=int, default=8)
     args = parser.parse_args()

@@ -27,6 +27,7 @@ FLAG_NONFINITE_STATE = 32
 FLAG_CACHE_OVERFLOW = 64
 FLAG_SIGN_CHANGE = 128
 FLAG_TIMEOUT = 256
+FLAG_NONFINITE_FEATURES = 512
 
 # Messages of the reference's ValueErrors for the same conditions.
 FLAG_MESSAGES = (
@@ -38,6 +39,7 @@ FLAG_MESSAGES = (
     (FLAG_NONFINITE_STATE, "nonfinite drafter state"),
     (FLAG_CACHE_OVERFLOW, "F16 cache storage overflow"),
     (FLAG_SIGN_CHANGE, "bounded latent scale changed a sign"),
+    (FLAG_NONFINITE_FEATURES, "nonfinite teacher features"),
 )
 # Device-side failures that are not the reference's ValueErrors.
 FLAG_ERRORS = ((FLAG_TIMEOUT, "a bounded device wait timed out"),)
@@ -119,6 +121,7 @@ SIGNATURES = {
     "bd_accept_greedy": (c_int, [P, c_int, c_int, c_int64, P, P, c_int, P, P, P, P, c_size_t, P, P]),
     "bd_accept_greedy_noalloc": (c_int, [P, c_int, c_int, c_int64, P, P, c_int, P, P, P, P, P]),
     "bd_rejection_workspace_bytes": (c_size_t, [c_int, c_int, c_int64]),
+    "bd_ingest_taps": (c_int, [P, c_int, c_int, c_int64, c_int64, P, c_int, P, P]),
     "bd_accept_rejection": (c_int, [P, P, c_int, c_int, c_int64, P, P, c_int, ctypes.c_ulonglong, ctypes.c_uint32,
                                     P, P, P, c_size_t, P, P]),
     "bd_argmax_rows_bf16": (c_int, [P, c_int64, c_int64, P, P, P]),

@@ -486,6 +486,34 @@ def accept_rejection(target_logits: Tensor, draft_logits: Tensor, drafts: Tensor
     return accepted, nxt
 
 
+_INGEST_OUT = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}
+
+
+def ingest_taps(captures: Tensor, out_dtype: torch.dtype = torch.float16, device: torch.device | None = None,
+                flags: Flags | None = None) -> Tensor:
+    """Tap-major teacher captures ``[taps, rows, hidden]`` (fp16 or fp32, on the GPU or in
+    pinned host memory) as token-major drafter features ``[rows, taps * hidden]``
+    (captures.py:124-137), with the loader's ``nonfinite teacher features`` check."""
+    if captures.ndim != 3 or captures.dtype not in (torch.float16, torch.float32) or out_dtype not in _INGEST_OUT:
+        raise ValueError("captures must be fp16/fp32 [taps, rows, hidden]; features fp16, bf16 or fp32")
+    taps, rows, hidden = captures.shape
+    if hidden % 8:
+        raise ValueError("capture hidden size must be a multiple of 8")
+    if captures.device.type != "cuda":
+        captures = captures.contiguous().to(device or torch.device("cuda", torch.cuda.current_device()),
+                                            non_blocking=True)
+    src = captures.contiguous()
+    dev = _require_cuda(src)
+    out = torch.empty((rows, taps * hidden), dtype=out_dtype, device=dev)
+    own = flags is None
+    flags = flags or Flags(dev)
+    _lib.call("bd_ingest_taps", _p(src), 16 if src.dtype == torch.float16 else 32, taps, rows, hidden, _p(out),
+              _INGEST_OUT[out_dtype], flags.ptr, _stream(dev))
+    if own:
+        flags.check()
+    return out
+
+
 def argmax_rows(logits: Tensor, flags: Flags | None = None) -> Tensor:
     """Row argmax of bf16 rows, lowest index on ties (contracts.py:130-137)."""
     if logits.dtype != torch.bfloat16:

@@ -45,6 +45,7 @@ typedef struct CUstream_st *bd_stream_t; /* == cudaStream_t */
 #define BD_FLAG_CACHE_OVERFLOW 64u    /* model.py:100-101 "F16 cache storage overflow" */
 #define BD_FLAG_SIGN_CHANGE 128u      /* model.py:162-163 "bounded latent scale changed a sign" */
 #define BD_FLAG_TIMEOUT 256u          /* a bounded device wait ran out (the kernel returned early) */
+#define BD_FLAG_NONFINITE_FEATURES 512u /* captures.py:129-130 "nonfinite teacher features" */
 
 int bd_abi_version(void);
 const char *bd_status_string(int status);
@@ -297,6 +298,14 @@ int bd_argmax_finish(unsigned long long *keys, int n, int32_t *out, bd_stream_t 
 
 /* Embedding rows (HE4.forward's functional.embedding, model.py:380-381) from a
  * bf16 [vocab, hidden] table; ids outside the vocabulary set BD_FLAG_BAD_TOKEN. */
+/* Teacher-feature ingestion (w1a1_eagle/numerical/captures.py:124-137): tap-major
+ * captures [taps][rows][hidden] of fp16 (in_dtype_bits 16) or fp32 (32) become
+ * token-major features [rows][taps * hidden] in fp16 (out_dtype 0), bf16 (1) or
+ * fp32 (2); a non-finite value sets BD_FLAG_NONFINITE_FEATURES (the loader's
+ * "nonfinite teacher features").  hidden % 8 == 0; both pointers 16-byte aligned. */
+int bd_ingest_taps(const void *taps_src, int in_dtype_bits, int taps, int64_t rows, int64_t hidden, void *features,
+                   int out_dtype, int32_t *flags, bd_stream_t stream);
+
 int bd_embed_rows(const uint16_t *table, int64_t vocab, int64_t hidden, const int32_t *ids, int n,
                   float *out, int32_t *flags, bd_stream_t stream);
 /* rms(x, weight, eps) rows (model.py:50-51). */
