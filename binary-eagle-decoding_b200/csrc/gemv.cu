@@ -315,34 +315,38 @@ static int launch_gemv_t(const GemvArgs &a, cudaStream_t stream) {
     return launch_pdl(gemv_kernel<NT, RB>, dim3(grid, a.splits), dim3(kGemvThreads), 0, stream, a);
 }
 
-// Wide matrices (many row blocks): two row blocks per CTA halve the activation traffic.
-static bool gemv_wide(int64_t rows) { return (rows + 15) / 16 >= 8 * 148; }
+// Two row blocks per CTA for the vocabulary-sized head (many row blocks) and for
+// long rows (the context fusion, K = taps x hidden): each warp keeps twice the
+// weight bytes in flight and the activation fragments serve both blocks.
+static bool gemv_wide(int64_t rows, int64_t cols) { return (rows + 15) / 16 >= 8 * 148 || cols >= 8192; }
 
 // K splits over CTAs for a small matrix: enough CTAs for two per SM, at least
 // 8 K tiles per warp.
 static int gemv_splits(int64_t rows, int64_t cols, int sms) {
-    const int64_t groups = ((rows + 15) / 16 + (gemv_wide(rows) ? 1 : 0)) / (gemv_wide(rows) ? 2 : 1);
+    const bool wide = gemv_wide(rows, cols);
+    const int64_t groups = ((rows + 15) / 16 + (wide ? 1 : 0)) / (wide ? 2 : 1);
     int64_t s = (2 * sms + groups - 1) / groups;
     const int64_t cap = ((cols + 15) / 16) / (kGemvWarps * 8);
     if (s > cap) s = cap;
     return static_cast<int>(s < 1 ? 1 : s);
 }
 
-static int64_t gemv_cells(int tokens, int64_t rows) {
-    return static_cast<int64_t>(gemv_wide(rows) ? 2 : 1) * ((tokens + 7) / 8) * 4 * 32;
+static int64_t gemv_cells(int tokens, int64_t rows, int64_t cols) {
+    return static_cast<int64_t>(gemv_wide(rows, cols) ? 2 : 1) * ((tokens + 7) / 8) * 4 * 32;
 }
 
 size_t gemv_workspace_bytes(int tokens, int64_t rows, int64_t cols, int sms) {
     const int s = gemv_splits(rows, cols, sms);
     if (s <= 1) return 0;
-    const int64_t groups = ((rows + 15) / 16 + (gemv_wide(rows) ? 1 : 0)) / (gemv_wide(rows) ? 2 : 1);
-    return static_cast<size_t>(s * groups * gemv_cells(tokens, rows)) * sizeof(float) + 256 +
+    const bool wide = gemv_wide(rows, cols);
+    const int64_t groups = ((rows + 15) / 16 + (wide ? 1 : 0)) / (wide ? 2 : 1);
+    return static_cast<size_t>(s * groups * gemv_cells(tokens, rows, cols)) * sizeof(float) + 256 +
            static_cast<size_t>(groups) * sizeof(int32_t);
 }
 
 int launch_gemv(const GemvArgs &a, cudaStream_t stream) {
     const int64_t nrb = (a.rows + 15) / 16;
-    const bool wide = gemv_wide(a.rows);
+    const bool wide = gemv_wide(a.rows, a.cols);
     (void)nrb;
     const int nt = (a.tokens + 7) / 8;
     if (a.tokens < 1 || a.tokens > 32 || nt > a.ntb) return BD_ERR_INVALID;
@@ -427,7 +431,8 @@ extern "C" int bd_gemv_bf16(const void *w16, int64_t rows, int64_t cols, const v
     const size_t need = gemv_workspace_bytes(tokens, rows, cols, sm_count());
     if (need && workspace && workspace_bytes >= need) {  // without a workspace the K split is skipped
         a.splits = gemv_splits(rows, cols, sm_count());
-        const int64_t groups = ((rows + 15) / 16 + (gemv_wide(rows) ? 1 : 0)) / (gemv_wide(rows) ? 2 : 1);
+        const bool wide = gemv_wide(rows, cols);
+        const int64_t groups = ((rows + 15) / 16 + (wide ? 1 : 0)) / (wide ? 2 : 1);
         a.counters = static_cast<int32_t *>(workspace);
         a.partial = reinterpret_cast<float *>(static_cast<char *>(workspace) +
                                               ((groups * sizeof(int32_t) + 255) & ~static_cast<size_t>(255)));
