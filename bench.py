@@ -505,6 +505,24 @@ def workload_ingest(args, pkg, device) -> list[dict]:
              "h2d_bytes_per_sequence": nbytes // 2}]
 
 
+def workload_fusion(args, pkg, device) -> list[dict]:
+    """Context fusion of a 4096-row prefill: features [4096, 4 x 2560] bf16 x fc [2560, 10240]^T
+    on the tensor cores (tcgen05 kind::f16), with torch's cuBLAS GEMM timed beside it."""
+    ops = pkg.ops
+    m, n, k = 4096, 2560, 10240
+    g = torch.Generator(device=device).manual_seed(10)
+    a = torch.randn((m, k), generator=g, device=device).to(torch.bfloat16)
+    b = (torch.randn((n, k), generator=g, device=device) * 0.02).to(torch.bfloat16)
+    out = torch.empty((m, n), dtype=torch.float32, device=device)
+    reps = max(args.steps // 100, 10)
+    us = _graph_us(lambda i: ops.gemm_bf16(a, b, out), 4, reps)
+    lib_us = _graph_us(lambda i: torch.mm(a, b.t(), out_dtype=torch.float32), 4, reps)
+    flops = 2 * m * n * k
+    return [{"workload": "context fusion GEMM of a 4096-row prefill, 4096 x 2560 x 10240 bf16 -> fp32",
+             "metric": "TFLOP/s", "value": flops / (us * 1e-6) / 1e12, "unit": "TFLOP/s", "us_per_gemm": us,
+             "cublas_tflops_same_shape": flops / (lib_us * 1e-6) / 1e12}]
+
+
 def workload_qat(args, pkg, device, rank: int, world: int) -> list[dict]:
     """Config 5: QAT update of the 4-layer drafter, per GPU 8 sequences x 2048 positions,
     32 windows of 16 slots each; data parallel (NCCL all-reduce) under torchrun."""
@@ -563,6 +581,8 @@ def run_workload(args, rank: int, world: int, local_rank: int) -> None:
         lines = workload_accept(args, pkg, device)
     elif args.workload == "ingest":
         lines = workload_ingest(args, pkg, device)
+    elif args.workload == "fusion":
+        lines = workload_fusion(args, pkg, device)
     else:
         lines = workload_qat(args, pkg, device, rank, world)
     if world > 1:
@@ -582,7 +602,7 @@ def main() -> None:
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     parser.add_argument("--profile-round", action="store_true",
                         help="run one draft round between cudaProfilerStart/Stop and exit")
-    parser.add_argument("--workload", choices=("round", "ffn", "w1a1", "accept", "ingest", "qat"), default="round",
+    parser.add_argument("--workload", choices=("round", "ffn", "w1a1", "accept", "ingest", "fusion", "qat"), default="round",
                         help="round: the headline draft round; the others measure one hot-path workload each")
     parser.add_argument("--qat-sequences", type=int, default=8)
     args = parser.parse_args()

@@ -32,7 +32,11 @@ enum TcEpi : int {
     TC_HE4 = 1,           // y = he4_value(D, scale[o], step, sums[t], mid[o]) (+ residual)
     TC_W1A1 = 2,          // y = (D * scale[o]) * rs[t]
     TC_W1A1_SWIGLU = 3,   // N tile = 128 gate + 128 up rows: h = silu(gate) * up, W1A1 values
+    TC_F32 = 4,           // bf16 operands (kind::f16), fp32 accumulators: out = D
 };
+
+// K elements per 128-byte shared-memory row (one TMA box width) of the operand type.
+__host__ __device__ constexpr int tc_bk(int epi) { return epi == TC_F32 ? 64 : 128; }
 
 struct TcArgs {
     int64_t M, N, K;       // tokens, outs (as the reference sees them), reduction length
@@ -86,6 +90,11 @@ __device__ __forceinline__ uint64_t sdesc(const void *p) {
     return ((a >> 4) & 0x3FFFull) | (1ull << 16) | (static_cast<uint64_t>(1024 >> 4) << 32) | (1ull << 46) |
            (2ull << 61);
 }
+// Instruction descriptor, kind::f16: f32 accumulators, bf16 A and B, K-major, N, M = 128.
+__host__ __device__ constexpr uint32_t idesc_bf16(int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+           (static_cast<uint32_t>(kTcBM >> 4) << 24);
+}
 // Instruction descriptor, kind::i8: s32 accumulators, signed A and B, K-major, N, M = 128.
 __host__ __device__ constexpr uint32_t idesc_i8(int n) {
     return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
@@ -104,7 +113,8 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
     __shared__ volatile int abort_flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t tiles = a.m_tiles * a.n_tiles;
-    const int nk = static_cast<int>((a.K + kTcBK - 1) / kTcBK);
+    constexpr int BKE = tc_bk(EPI);  // K elements per stage
+    const int nk = static_cast<int>((a.K + BKE - 1) / BKE);
     constexpr uint32_t kCols = 2 * BN;  // two accumulator buffers
     if (threadIdx.x == 0) {
         for (int s = 0; s < kTcStages; ++s) {
@@ -137,14 +147,14 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
                     const int s = it % kTcStages;
                     if (it >= kTcStages && !mb_wait(&empty[s], ((it / kTcStages) - 1) & 1, &abort_flag)) break;
                     mb_expect_tx(&full[s], (kTcBM + BN) * kTcBK);
-                    tma_2d(sa + s * kTcBM * kTcBK, &ma, &full[s], k * kTcBK, m0);
-                    tma_2d(sb + s * BN * kTcBK, &mb, &full[s], k * kTcBK, n0);
+                    tma_2d(sa + s * kTcBM * kTcBK, &ma, &full[s], k * BKE, m0);
+                    tma_2d(sb + s * BN * kTcBK, &mb, &full[s], k * BKE, n0);
                 }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {  // MMA issuer
-            constexpr uint32_t idesc = idesc_i8(BN);
+            constexpr uint32_t idesc = EPI == TC_F32 ? idesc_bf16(BN) : idesc_i8(BN);
             uint32_t it = 0, lt = 0;
             for (int64_t t = blockIdx.x; t < tiles && !abort_flag; t += gridDim.x, ++lt) {
                 const uint32_t b = lt & 1;
@@ -163,11 +173,19 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
 #pragma unroll
                     for (int kk = 0; kk < kTcBK / 32; ++kk) {
                         const uint32_t accumulate = (k > 0 || kk > 0) ? 1u : 0u;
-                        asm volatile(
-                            "{\n .reg .pred p;\n setp.ne.u32 p, %4, 0;\n"
-                            " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
-                            "l"(da + static_cast<uint64_t>(2 * kk)), "l"(db + static_cast<uint64_t>(2 * kk)), "r"(idesc),
-                            "r"(accumulate));
+                        // one instruction consumes 32 bytes of K (32 int8 or 16 bf16): descriptor +2
+                        if (EPI == TC_F32)
+                            asm volatile(
+                                "{\n .reg .pred p;\n setp.ne.u32 p, %4, 0;\n"
+                                " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+                                "l"(da + static_cast<uint64_t>(2 * kk)), "l"(db + static_cast<uint64_t>(2 * kk)),
+                                "r"(idesc), "r"(accumulate));
+                        else
+                            asm volatile(
+                                "{\n .reg .pred p;\n setp.ne.u32 p, %4, 0;\n"
+                                " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+                                "l"(da + static_cast<uint64_t>(2 * kk)), "l"(db + static_cast<uint64_t>(2 * kk)),
+                                "r"(idesc), "r"(accumulate));
                     }
                     asm volatile(
                         "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(&empty[s]))
@@ -222,7 +240,7 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
                 const bool full16 = o0 + 16 <= a.N;
                 // per-column parameters: the same 16 values for every lane (broadcast loads)
                 float s1[16], s2[16], md[16];
-                if (EPI != TC_RAW) {
+                if (EPI != TC_RAW && EPI != TC_F32) {
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         const bool live = full16 || o0 + j < a.N;
@@ -237,7 +255,9 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
                 for (int j = 0; j < 16; ++j) {
                     const int D = static_cast<int>(v[j]);
                     di[j] = D;
-                    if (EPI == TC_HE4) {
+                    if (EPI == TC_F32) {
+                        y[j] = __uint_as_float(v[j]);
+                    } else if (EPI == TC_HE4) {
                         y[j] = he4_value(D, s1[j], q.step, cs, md[j]);
                     } else if (EPI == TC_W1A1) {
                         y[j] = __fmul_rn(__fmul_rn(static_cast<float>(D), s1[j]), rs);
@@ -299,16 +319,19 @@ static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-// 2-D int8 tensor [rows, cols] with row stride ld bytes (multiple of 16), boxes of
-// box_rows x 128 bytes, 128-byte swizzle; reads past the tensor return zeros.
-static bool make_i8_map(CUtensorMap *m, const void *ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+// 2-D int8 (bf16 = false) or bf16 tensor [rows, cols] with row stride ld bytes
+// (multiple of 16), boxes of box_rows x 128 bytes, 128-byte swizzle; reads past
+// the tensor return zeros.
+static bool make_i8_map(CUtensorMap *m, const void *ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+                        bool bf16 = false) {
     auto enc = tensor_map_encoder();
     if (!enc || (reinterpret_cast<uintptr_t>(ptr) & 15) || (ld & 15)) return false;
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
     cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld)};
-    cuuint32_t box[2] = {static_cast<cuuint32_t>(kTcBK), static_cast<cuuint32_t>(box_rows)};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(bf16 ? 64 : kTcBK), static_cast<cuuint32_t>(box_rows)};
     cuuint32_t es[2] = {1, 1};
-    return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(ptr), dims, strides, box, es,
+    return enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+               const_cast<void *>(ptr), dims, strides, box, es,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -329,7 +352,9 @@ template <int BN, int EPI>
 static int launch_tc_t(TcArgs a, const int8_t *codes, int64_t ld_codes, const int8_t *weights, int64_t w_rows,
                        int64_t ld_w, cudaStream_t stream) {
     CUtensorMap ma, mb;
-    if (!make_i8_map(&ma, codes, a.M, a.K, ld_codes, kTcBM) || !make_i8_map(&mb, weights, w_rows, a.K, ld_w, BN))
+    const bool bf16 = EPI == TC_F32;
+    if (!make_i8_map(&ma, codes, a.M, a.K, ld_codes, kTcBM, bf16) ||
+        !make_i8_map(&mb, weights, w_rows, a.K, ld_w, BN, bf16))
         return BD_ERR_ALIGNMENT;
     a.m_tiles = (a.M + kTcBM - 1) / kTcBM;
     a.n_tiles = (w_rows + BN - 1) / BN;
@@ -356,6 +381,8 @@ int launch_tc_gemm(int epi, const TcArgs &a, const int8_t *codes, int64_t ld_cod
             return launch_tc_t<256, TC_W1A1>(a, codes, ld_codes, weights, w_rows, ld_w, stream);
         case TC_W1A1_SWIGLU:
             return launch_tc_t<256, TC_W1A1_SWIGLU>(a, codes, ld_codes, weights, w_rows, ld_w, stream);
+        case TC_F32:
+            return launch_tc_t<256, TC_F32>(a, codes, ld_codes, weights, w_rows, ld_w, stream);
         default:
             return BD_ERR_INVALID;
     }
@@ -410,6 +437,20 @@ extern "C" int bd_tile_signs_i8(const float *latent, int64_t rows, int64_t cols,
                                                                     block_offset, flags);
     BD_CHECK_LAUNCH();
     return BD_OK;
+}
+
+extern "C" int bd_gemm_bf16(const uint16_t *a, int64_t m, int64_t k, int64_t lda, const uint16_t *b, int64_t n,
+                            int64_t ldb, float *c, int64_t ldc, bd_stream_t stream) {
+    if (m < 1 || k < 1 || n < 1 || lda < k || ldb < k || ldc < n || !a || !b || !c) return BD_ERR_INVALID;
+    TcArgs t{};
+    t.M = m;
+    t.N = n;
+    t.K = k;
+    t.ld_out = ldc;
+    t.out = c;
+    // strides in bytes for the tensor maps (multiples of 16: lda, ldb multiples of 8)
+    return launch_tc_gemm(TC_F32, t, reinterpret_cast<const int8_t *>(a), lda * 2,
+                          reinterpret_cast<const int8_t *>(b), n, ldb * 2, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int bd_gemm_i8(const int8_t *codes, int64_t tokens, int64_t k, const int8_t *signs_i8, int64_t outs,

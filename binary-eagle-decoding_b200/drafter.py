@@ -86,11 +86,13 @@ class DraftEngine:
         quantizers = quantizers or {}
         self.layers: list[LayerDevice] = []
         self.kv_bf16: list[Tensor] = []
+        self.kv_bf16x2: list[Tensor] = []  # [K | K] for the hi + lo product of a prefill
         for i in range(cfg.layers):
             p = f"blk.{i}."
             q, k, v = t(p + "attn_q.weight"), t(p + "attn_k.weight"), t(p + "attn_v.weight")
             qkv = torch.cat((q, k, v), 0).to(torch.bfloat16)
             self.kv_bf16.append(torch.cat((k, v), 0).to(torch.bfloat16).contiguous())
+            self.kv_bf16x2.append(torch.cat((self.kv_bf16[-1], self.kv_bf16[-1]), 1).contiguous())
             gate, up, down = t(p + "ffn_gate.weight").float(), t(p + "ffn_up.weight").float(), t(p + "ffn_down.weight").float()
 
             def qv(name, default):
@@ -174,9 +176,11 @@ class DraftEngine:
     def prefill(self, features: Tensor, anchor: int) -> None:
         """Context K/V of positions [0, anchor) from target features (model.py:382-386, 195-200).
 
-        Large one-off matrix products (the fused context of all rows) use
-        cuBLAS bf16 GEMMs; normalisation, rotary embedding and fp16 storage are
-        this library's kernels.
+        The fusion and context K/V products run on the tensor cores
+        (``bd_gemm_bf16``: tcgen05 bf16 MMAs, fp32 accumulators in TMEM); the
+        K/V product takes the encoded rows as bf16 hi + lo halves along K, the
+        same ~16-bit split the GEMV path uses.  Normalisation, rotary embedding
+        and fp16 storage are this library's kernels.
         """
         cfg = self.cfg
         if anchor > self.max_positions - cfg.slots:
@@ -184,17 +188,17 @@ class DraftEngine:
         self.positions = anchor
         if anchor == 0:
             return
-        feats = features[:anchor].to(self.device, torch.bfloat16)
-        fused = (feats @ self.fc_bf16.T).float()
+        feats = features[:anchor].to(self.device, torch.bfloat16).contiguous()
+        fused = ops.gemm_bf16(feats, self.fc_bf16)
         encoded = torch.empty_like(fused)
         _lib.call("bd_rms_rows", _p(fused), anchor, cfg.hidden, cfg.hidden, _p(self.enc_norm), float(cfg.epsilon),
                   _p(encoded), cfg.hidden, self._stream())
-        # encoded rows as bf16 hi + lo (the same ~16-bit split the GEMV path uses)
+        # encoded rows as bf16 hi + lo (the same ~16-bit split the GEMV path uses), side by side along K
         enc_hi = encoded.to(torch.bfloat16)
-        enc_lo = (encoded - enc_hi.float()).to(torch.bfloat16)
+        enc = torch.cat((enc_hi, (encoded - enc_hi.float()).to(torch.bfloat16)), 1).contiguous()
         kvd = cfg.kv_heads * cfg.head_dim
         for i, layer in enumerate(self.layers):
-            kv = ((enc_hi @ self.kv_bf16[i].T).float() + (enc_lo @ self.kv_bf16[i].T).float()).contiguous()
+            kv = ops.gemm_bf16(enc, self.kv_bf16x2[i])
             self._heads(kv, anchor, 0, cfg.kv_heads, layer.k_norm, True, 0, self._cache_ptr(self.k_cache, i, 0), kvd)
             self._heads(kv, anchor, kvd, cfg.kv_heads, None, False, 0, self._cache_ptr(self.v_cache, i, 0), kvd)
 

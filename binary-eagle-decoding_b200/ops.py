@@ -293,6 +293,20 @@ def gemm_i8(codes: Tensor, k: int, signs_i8: Tensor, outs: int) -> Tensor:
     return dots
 
 
+def gemm_bf16(a: Tensor, b: Tensor, out: Tensor | None = None) -> Tensor:
+    """``a @ b.T`` for bf16 ``a [m, k]`` and ``b [n, k]`` on the tensor cores (fp32 accumulators, fp32 result)."""
+    if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16 or a.ndim != 2 or b.ndim != 2 or a.shape[1] != b.shape[1]:
+        raise ValueError("gemm_bf16 takes bf16 [m, k] and [n, k]")
+    m, k = a.shape
+    n = b.shape[0]
+    if a.stride(1) != 1 or b.stride(1) != 1 or a.stride(0) % 8 or b.stride(0) % 8:
+        raise ValueError("gemm_bf16 operands need unit column stride and row strides that are multiples of 8")
+    device = _require_cuda(a, b)
+    c = torch.empty((m, n), dtype=torch.float32, device=device) if out is None else out
+    _lib.call("bd_gemm_bf16", _p(a), m, k, a.stride(0), _p(b), n, b.stride(0), _p(c), c.stride(0), _stream(device))
+    return c
+
+
 def ffn_w1a1_large(x: Tensor, ffn: PackedFFN, hidden_out: bool = False, flags: Flags | None = None):
     """W1A1 SwiGLU block on the tensor cores (any token count; needs pack_ffn(large=True))."""
     if ffn.signs_gate_up_i8 is None or ffn.signs_down_i8 is None:

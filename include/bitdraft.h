@@ -205,6 +205,14 @@ int64_t bd_i8_ld(int64_t cols);
 int64_t bd_i8_bytes(int64_t rows, int64_t cols);
 int bd_tile_signs_i8(const float *latent, int64_t rows, int64_t cols, int8_t *out, int block_stride,
                      int block_offset, int32_t *flags, bd_stream_t stream);
+/* Plain bf16 GEMM on the tensor cores (tcgen05 kind::f16, fp32 accumulators in
+ * TMEM): c[m][n] = sum_k a[m][k] b[n][k], a and b row-major bf16 with row strides
+ * lda, ldb (elements, multiples of 8, 16-byte aligned bases), c fp32 with row
+ * stride ldc.  Used for the context fusion and the context K/V projections of a
+ * long prefill (model.py:349-351, 382-386). */
+int bd_gemm_bf16(const uint16_t *a, int64_t m, int64_t k, int64_t lda, const uint16_t *b, int64_t n, int64_t ldb,
+                 float *c, int64_t ldc, bd_stream_t stream);
+
 int bd_gemm_i8(const int8_t *codes, int64_t tokens, int64_t k, const int8_t *signs_i8, int64_t outs,
                int32_t *dots, bd_stream_t stream);
 typedef struct {

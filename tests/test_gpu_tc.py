@@ -62,3 +62,15 @@ def test_ffn_w1a1_large_config3(ops):
     # and the decode path (32-token chunks) gives the same block output
     y_small = ops.ffn_w1a1(x[:40].to(DEV), ops.pack_ffn(gate.to(DEV), up.to(DEV), down.to(DEV)))
     assert np.array_equal(y_small.cpu().numpy(), y[:40].cpu().numpy())
+
+
+@pytest.mark.parametrize("m,n,k", [(512, 2560, 10240), (100, 200, 72), (1, 8, 8), (300, 2048, 5120)])
+def test_gemm_bf16(ops, m, n, k):
+    g = torch.Generator().manual_seed(m + n + k)
+    a = torch.randn((m, k), generator=g).to(torch.bfloat16)
+    b = torch.randn((n, k), generator=g).to(torch.bfloat16)
+    got = ops.gemm_bf16(a.to(DEV), b.to(DEV)).cpu().double().numpy()
+    want = a.double().numpy() @ b.double().numpy().T  # bf16 inputs are exact in float64
+    # fp32 accumulation of up to 10240 products: relative error of the norm about 1e-5
+    assert np.linalg.norm(got - want) / np.linalg.norm(want) < 3e-5
+    assert np.abs(got - want).max() <= 1e-4 * np.abs(want).max() + 1e-6
