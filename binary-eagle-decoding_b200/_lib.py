@@ -140,8 +140,8 @@ SIGNATURES = {
     "bd_qkv_post": (c_int, [P, c_int, c_int64, c_int, c_int, c_int, P, P, ctypes.c_float, ctypes.c_float, c_int64,
                             P, c_int64, P, P, c_int64, P, P]),
     "bd_attention_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
-    "bd_attention_decode": (c_int, [P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int64, c_int64, P, P,
-                                    c_size_t, P]),
+    "bd_attention_decode": (c_int, [P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int64, c_int64, c_int64, P,
+                                    P, c_size_t, P]),
 }
 
 _lib = None

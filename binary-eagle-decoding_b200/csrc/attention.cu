@@ -28,6 +28,7 @@ struct AttnArgs {
     int windowed;           // apply |pos_q - pos_k| < window
     int64_t anchor;         // position of query row 0
     int64_t window;
+    int64_t stable_keys;    // keys [0, stable_keys) were not written by the immediately preceding kernel
     float scale;            // 1 / sqrt(d)
     int chunks;
     float *part_o;          // [chunks][heads][16][d]
@@ -88,16 +89,23 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_chunk_kernel(const AttnA
     const int groups = a.heads / a.kv_heads;
     const int key0 = chunk * kKeys;
     const int nkeys = min(kKeys, a.keys - key0);
+    // stage K and V rows of this chunk (rows past the end are zero); a chunk of
+    // context keys the preceding kernel did not write starts loading before the
+    // dependency wait, so the cache stream overlaps that kernel
+    auto stage = [&]() {
+        for (int i = threadIdx.x; i < kKeys * (kDim / 8); i += blockDim.x) {
+            const int r = i / (kDim / 8), c = i % (kDim / 8);
+            const bool live = r < nkeys;
+            const int64_t src = (static_cast<int64_t>(key0 + (live ? r : 0)) * a.kv_heads + kvh) * kDim + c * 8;
+            cp_async16(ks + r * kRowBytes + c * 16, a.k + src, live ? 16 : 0);
+            cp_async16(vs + r * kRowBytes + c * 16, a.v + src, live ? 16 : 0);
+        }
+    };
+    const bool early = static_cast<int64_t>(key0) + kKeys <= a.stable_keys;
+    if (early) stage();
     grid_wait();
     grid_launch_dependents();
-    // stage K and V rows of this chunk (rows past the end are zero)
-    for (int i = threadIdx.x; i < kKeys * (kDim / 8); i += blockDim.x) {
-        const int r = i / (kDim / 8), c = i % (kDim / 8);
-        const bool live = r < nkeys;
-        const int64_t src = (static_cast<int64_t>(key0 + (live ? r : 0)) * a.kv_heads + kvh) * kDim + c * 8;
-        cp_async16(ks + r * kRowBytes + c * 16, a.k + src, live ? 16 : 0);
-        cp_async16(vs + r * kRowBytes + c * 16, a.v + src, live ? 16 : 0);
-    }
+    if (!early) stage();
     // Q fragments of this warp's head: rows are query slots (A operand, row-major 16 x kDim)
     const int head = kvh * groups + hw;
     const bool head_live = hw < groups;
@@ -316,8 +324,8 @@ static int launch_attention(const AttnArgs &a, int kv_heads, int tokens, int hea
 
 extern "C" int bd_attention_decode(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache, int tokens,
                                    int heads, int kv_heads, int head_dim, int keys, int windowed, int64_t anchor,
-                                   int64_t window, float *out, void *workspace, size_t workspace_bytes,
-                                   bd_stream_t stream) {
+                                   int64_t window, int64_t stable_keys, float *out, void *workspace,
+                                   size_t workspace_bytes, bd_stream_t stream) {
     if (tokens < 1 || tokens > 16 || (head_dim != 64 && head_dim != 128) || heads < 1 || kv_heads < 1 ||
         heads % kv_heads ||
         heads / kv_heads > 4 || keys < 1 || keys > kMaxChunks * kKeys || !q || !k_cache || !v_cache || !out)
@@ -334,6 +342,7 @@ extern "C" int bd_attention_decode(const uint16_t *q, const uint16_t *k_cache, c
     a.windowed = windowed;
     a.anchor = anchor;
     a.window = window;
+    a.stable_keys = stable_keys < 0 ? 0 : stable_keys;
     a.scale = 1.0f / sqrtf(static_cast<float>(head_dim));
     a.chunks = (keys + kKeys - 1) / kKeys;
     a.part_ml = static_cast<float *>(workspace);

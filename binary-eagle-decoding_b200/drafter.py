@@ -254,9 +254,10 @@ class DraftEngine:
                       _p(self.q16), qd, self._cache_ptr(self.k_cache, i, anchor),
                       self._cache_ptr(self.v_cache, i, anchor), kvd, self.flags.ptr, st)
             windowed = int(i < cfg.layers - 1)
+            # rows below the anchor were written by the ingest step, several kernels earlier
             _lib.call("bd_attention_decode", _p(self.q16), self._cache_ptr(self.k_cache, i, 0),
                       self._cache_ptr(self.v_cache, i, 0), k, cfg.heads, cfg.kv_heads, cfg.head_dim, L, windowed,
-                      anchor, cfg.window, _p(self.attn), _p(self.attn_ws), self.attn_ws.numel(), st)
+                      anchor, cfg.window, anchor, _p(self.attn), _p(self.attn_ws), self.attn_ws.numel(), st)
             self._pack(self.attn, k, qd, qd)
             self._gemv(layer.o.data_ptr(), H, qd, k, self.resid, H, residual=self.state)
             ops.ffn_he4(self.resid[:k], layer.ffn, self.resid[:k], flags=self.flags, out=self.state[:k],

@@ -340,11 +340,15 @@ int bd_qkv_post(const float *src, int n, int64_t ld_src, int heads, int kv_heads
  * positions equal to their index, query row t at position anchor + t, and, if
  * `windowed`, only keys with |anchor + t - k| < window (all but the last layer,
  * model.py:390-392).  q fp16 [tokens][heads][d], caches fp16
- * [positions][kv_heads][d]; tokens <= 16, head_dim 64 or 128, heads/kv_heads <= 4. */
+ * [positions][kv_heads][d]; tokens <= 16, head_dim 64 or 128, heads/kv_heads <= 4.
+ * stable_keys: the caller's promise that cache rows [0, stable_keys) were not
+ * written by the kernel launched immediately before this call on the stream
+ * (they are then read before the launch waits for it; pass 0 when unsure). */
 size_t bd_attention_workspace_bytes(int heads, int head_dim, int keys);
 int bd_attention_decode(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache, int tokens, int heads,
                         int kv_heads, int head_dim, int keys, int windowed, int64_t anchor, int64_t window,
-                        float *out, void *workspace, size_t workspace_bytes, bd_stream_t stream);
+                        int64_t stable_keys, float *out, void *workspace, size_t workspace_bytes,
+                        bd_stream_t stream);
 
 /* ================================================================ QAT (training sizes)
  * Projection.forward at any token count (w1a1_eagle/model.py:128-150): codes and

@@ -180,8 +180,9 @@ def test_attention_kernel_against_numpy(d, heads, kvh, tokens, keys, windowed):
     out = torch.zeros(tokens, heads * d, device=DEV)
     ws = torch.zeros(int(lib.load().bd_attention_workspace_bytes(heads, d, keys)), dtype=torch.uint8, device=DEV)
     qd, kd, vd = q.to(DEV), kc.to(DEV), vc.to(DEV)
+    torch.cuda.synchronize()  # the cache is complete: every row may be read before the launch's wait
     lib.call("bd_attention_decode", qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), tokens, heads, kvh, d, keys, windowed,
-             anchor, window, out.data_ptr(), ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
+             anchor, window, keys, out.data_ptr(), ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
     groups = heads // kvh
     qf, kf, vf = q.double().numpy(), kc.double().numpy(), vc.double().numpy()
     want = np.zeros((tokens, heads, d))
