@@ -523,6 +523,60 @@ def workload_fusion(args, pkg, device) -> list[dict]:
              "cublas_tflops_same_shape": flops / (lib_us * 1e-6) / 1e12}]
 
 
+def workload_ste(args, pkg, device) -> list[dict]:
+    """Config-5 latent update of the drafter's binary FFN projections (gate, up, down of
+    each layer, 9728 x 2560 fp32 latents): the straight-through sign backward
+    (``bd_ste_sign_backward``: two fp32 gradient halves, the clip-window mask, the
+    HE4 step scale) and the fused AdamW + clamp + W8 re-pack (``bd_adamw_latent``)."""
+    lib = pkg._lib
+    ops = pkg.ops
+    rows, cols, count = 9728, 2560, args.ste_projections
+    n = rows * cols
+    g = torch.Generator(device=device).manual_seed(11)
+    mats = []
+    for _ in range(count):
+        latent = (torch.randn((rows, cols), generator=g, device=device) * 0.02).clamp_(-1, 1)
+        mats.append({"latent": latent, "g1": torch.randn((rows, cols), generator=g, device=device) * 1e-3,
+                     "g2": torch.randn((rows, cols), generator=g, device=device) * 1e-6,
+                     "out": torch.empty((rows, cols), device=device), "m": torch.zeros((rows, cols), device=device),
+                     "v": torch.zeros((rows, cols), device=device),
+                     "w8": torch.zeros(ops.w8_words(rows, cols), dtype=torch.int32, device=device)})
+    bound = torch.full((1,), 0.05, device=device)
+    flags = ops.Flags(device)
+    stream = torch.cuda.current_stream(device).cuda_stream
+
+    def sign_backward():
+        for t in mats:
+            lib.call("bd_ste_sign_backward", t["g1"].data_ptr(), t["g2"].data_ptr(), t["latent"].data_ptr(), n, 1.0,
+                     bound.data_ptr(), 8, t["out"].data_ptr(), None, stream)
+
+    def adamw():
+        for t in mats:
+            lib.call("bd_adamw_latent", t["latent"].data_ptr(), t["out"].data_ptr(), t["m"].data_ptr(),
+                     t["v"].data_ptr(), rows, cols, 1e-5, 0.9, 0.999, 1e-8, 1, None, 1, t["w8"].data_ptr(), 1, 0,
+                     flags.ptr, stream)
+
+    reps = max(args.steps // 200, 5)
+    for _ in range(3):
+        sign_backward()
+        adamw()
+    torch.cuda.synchronize()
+    ste_us = _events_us(sign_backward, reps) / count
+    adam_us = _events_us(adamw, reps) / count
+    flags.check()
+    ste_bytes = 16 * n  # read two gradient halves + latent, write the masked gradient
+    adam_bytes = 28 * n + 4 * ops.w8_words(rows, cols)  # read p, g, m, v; write p, m, v and the sign words
+    peak, peak_kind = peaks()
+    lines = []
+    for name, us, nbytes in (("straight-through sign backward", ste_us, ste_bytes),
+                             ("latent AdamW + clamp + W8 sign re-pack", adam_us, adam_bytes)):
+        gbs = nbytes / (us * 1e-6) / 1e9
+        lines.append({"workload": f"{name}, {count} x 9728 x 2560 fp32 latents (arrays larger than L2)",
+                      "metric": "HBM GB/s (algorithmic)", "value": gbs, "unit": "GB/s", "us_per_projection": us,
+                      "bytes_per_projection": nbytes, "frac_of_hbm": gbs / peak, "peak": f"{peak:.1f} GB/s ({peak_kind})"})
+    return lines
+
+
 def workload_qat(args, pkg, device, rank: int, world: int) -> list[dict]:
     """Config 5: QAT update of the 4-layer drafter, per GPU 8 sequences x 2048 positions,
     32 windows of 16 slots each; data parallel (NCCL all-reduce) under torchrun."""
@@ -583,6 +637,8 @@ def run_workload(args, rank: int, world: int, local_rank: int) -> None:
         lines = workload_ingest(args, pkg, device)
     elif args.workload == "fusion":
         lines = workload_fusion(args, pkg, device)
+    elif args.workload == "ste":
+        lines = workload_ste(args, pkg, device)
     else:
         lines = workload_qat(args, pkg, device, rank, world)
     if world > 1:
@@ -602,9 +658,10 @@ def main() -> None:
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     parser.add_argument("--profile-round", action="store_true",
                         help="run one draft round between cudaProfilerStart/Stop and exit")
-    parser.add_argument("--workload", choices=("round", "ffn", "w1a1", "accept", "ingest", "fusion", "qat"), default="round",
+    parser.add_argument("--workload", choices=("round", "ffn", "w1a1", "accept", "ingest", "fusion", "ste", "qat"), default="round",
                         help="round: the headline draft round; the others measure one hot-path workload each")
     parser.add_argument("--qat-sequences", type=int, default=8)
+    parser.add_argument("--ste-projections", type=int, default=12)
     args = parser.parse_args()
     if args.profile_round:
         profile_round()

@@ -61,6 +61,20 @@ __global__ void __launch_bounds__(256) adamw_latent_kernel(float *__restrict__ p
     bool bad = false;
     for (int64_t item = warp; item < rows_pad * ncp; item += nwarps) {
         const int64_t row = item / ncp, cp = item - row * ncp;
+        // all 32 loads of the item first (8 columns x p, g, m, v), so a warp keeps
+        // 4 KB in flight instead of one column's 512 B
+        float pv[8], gv[8], mv[8], vv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int64_t c = cp * 256 + i * 32 + lane;
+            if (row < rows && c < cols) {
+                const int64_t e = row * cols + c;
+                pv[i] = param[e];
+                gv[i] = grad[e];
+                mv[i] = m[e];
+                vv[i] = v[e];
+            }
+        }
         uint32_t words[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -68,14 +82,13 @@ __global__ void __launch_bounds__(256) adamw_latent_kernel(float *__restrict__ p
             bool bit = false;
             if (row < rows && c < cols) {
                 const int64_t e = row * cols + c;
-                float mm = m[e], vv = v[e];
-                const float g = __fmul_rn(grad[e], coef);
-                float p = adam_element(param[e], g, mm, vv, a);
+                float mm = mv[i], vvi = vv[i];
+                float p = adam_element(pv[i], __fmul_rn(gv[i], coef), mm, vvi, a);
                 if (clamp) p = fminf(fmaxf(p, -1.0f), 1.0f);
                 bad |= !isfinite(p);
                 param[e] = p;
                 m[e] = mm;
-                v[e] = vv;
+                v[e] = vvi;
                 bit = p >= 0.0f;
             }
             words[i] = __ballot_sync(0xffffffffu, bit);
