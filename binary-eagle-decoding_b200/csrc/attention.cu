@@ -7,7 +7,10 @@
 // K and V rows in shared memory with cp.async; warp w owns q head
 // kv * groups + (w & 3), its 16 query rows and half (w >> 2) of the keys.  S = Q K^T and O = P V run on
 // m16n8k16 fp16 MMAs with fp32 accumulation (K fragments by ldmatrix, V by
-// ldmatrix.trans, P re-packed from the S accumulators).  Each CTA writes its
+// ldmatrix.trans, P re-packed from the S accumulators).  The cached K and V are
+// fp16 values, exact as MMA operands; the fp32 queries and probabilities are
+// split into fp16 hi + lo halves (x = hi + lo to ~22 bits), two MMAs each, so
+// the products keep fp32 precision (the reference attends with fp32 queries).  Each CTA writes its
 // chunk's row maxima, row sums and un-normalised O; a combine kernel merges the
 // chunks.  No waits between CTAs: partials meet only in the combine launch.
 #include "kernels.cuh"
@@ -22,7 +25,7 @@ template <int D>
 constexpr int row_bytes() { return D * 2 + 16; }
 
 struct AttnArgs {
-    const __half *q;        // [tokens][heads][d]
+    const float *q;         // [tokens][heads][d] fp32
     const __half *k, *v;    // [positions][kv_heads][d] (cache rows 0 .. keys-1)
     int tokens, heads, kv_heads, keys;
     int windowed;           // apply |pos_q - pos_k| < window
@@ -56,9 +59,12 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
-__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
-    const __half2 h = __floats2half2_rn(lo, hi);
-    return *reinterpret_cast<const uint32_t *>(&h);
+// fp16 hi + lo halves of a pair: x ~= float(hi) + float(lo) to ~22 bits.
+__device__ __forceinline__ void split_half2(float x0, float x1, uint32_t &hi, uint32_t &lo) {
+    const __half2 h = __floats2half2_rn(x0, x1);
+    const __half2 l = __floats2half2_rn(x0 - __low2float(h), x1 - __high2float(h));
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+    lo = *reinterpret_cast<const uint32_t *>(&l);
 }
 
 // 8 warps: warp w takes q head (w & 3) of the kv group and half (w >> 2) of the
@@ -75,7 +81,7 @@ constexpr size_t attn_smem_bytes() {
 }
 
 template <int kDim>
-__global__ void __launch_bounds__(kAttnWarps * 32) attn_chunk_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_chunk_kernel(const AttnArgs a) {
     constexpr int kRowBytes = row_bytes<kDim>();
     constexpr int kX = kDim / 8 * 4 + 4;  // exchanged floats per lane
     extern __shared__ __align__(16) char sm[];
@@ -109,16 +115,17 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_chunk_kernel(const AttnA
     // Q fragments of this warp's head: rows are query slots (A operand, row-major 16 x kDim)
     const int head = kvh * groups + hw;
     const bool head_live = hw < groups;
-    uint32_t qa[kDim / 16][4];
+    uint32_t qa[kDim / 16][4], ql[kDim / 16][4];
 #pragma unroll
     for (int s = 0; s < kDim / 16; ++s) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int row = g + 8 * (j & 1);
             const int col = s * 16 + 2 * t + 8 * (j >> 1);
-            qa[s][j] = (head_live && row < a.tokens)
-                           ? *reinterpret_cast<const uint32_t *>(a.q + (static_cast<int64_t>(row) * a.heads + head) * kDim + col)
-                           : 0u;
+            float2 x = make_float2(0.0f, 0.0f);
+            if (head_live && row < a.tokens)
+                x = *reinterpret_cast<const float2 *>(a.q + (static_cast<int64_t>(row) * a.heads + head) * kDim + col);
+            split_half2(x.x, x.y, qa[s][j], ql[s][j]);
         }
     }
     cp_async_wait_all();
@@ -147,7 +154,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_chunk_kernel(const AttnA
                 const int mi = lane >> 3, r = lane & 7;
                 ldmatrix_x4(b, ks + (kbase + n * 8 + r) * kRowBytes + (s2 * 32 + mi * 8) * 2);
                 mma_f16_16816(s_acc[n], qa[2 * s2][0], qa[2 * s2][1], qa[2 * s2][2], qa[2 * s2][3], b[0], b[1]);
+                mma_f16_16816(s_acc[n], ql[2 * s2][0], ql[2 * s2][1], ql[2 * s2][2], ql[2 * s2][3], b[0], b[1]);
                 mma_f16_16816(s_acc[n], qa[2 * s2 + 1][0], qa[2 * s2 + 1][1], qa[2 * s2 + 1][2], qa[2 * s2 + 1][3],
+                              b[2], b[3]);
+                mma_f16_16816(s_acc[n], ql[2 * s2 + 1][0], ql[2 * s2 + 1][1], ql[2 * s2 + 1][2], ql[2 * s2 + 1][3],
                               b[2], b[3]);
             }
         }
@@ -190,17 +200,20 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_chunk_kernel(const AttnA
         // O = P V over the 64 keys: P re-packed from the S accumulators as A fragments
 #pragma unroll
         for (int kk = 0; kk < kHalfKeys / 16; ++kk) {
-            const uint32_t pa0 = pack_half2(s_acc[2 * kk][0], s_acc[2 * kk][1]);
-            const uint32_t pa1 = pack_half2(s_acc[2 * kk][2], s_acc[2 * kk][3]);
-            const uint32_t pa2 = pack_half2(s_acc[2 * kk + 1][0], s_acc[2 * kk + 1][1]);
-            const uint32_t pa3 = pack_half2(s_acc[2 * kk + 1][2], s_acc[2 * kk + 1][3]);
+            uint32_t pa0, pa1, pa2, pa3, pl0, pl1, pl2, pl3;
+            split_half2(s_acc[2 * kk][0], s_acc[2 * kk][1], pa0, pl0);
+            split_half2(s_acc[2 * kk][2], s_acc[2 * kk][3], pa1, pl1);
+            split_half2(s_acc[2 * kk + 1][0], s_acc[2 * kk + 1][1], pa2, pl2);
+            split_half2(s_acc[2 * kk + 1][2], s_acc[2 * kk + 1][3], pa3, pl3);
 #pragma unroll
             for (int n2 = 0; n2 < kDim / 16; ++n2) {
                 uint32_t b[4];
                 const int mi = lane >> 3, r = lane & 7;
                 ldmatrix_x4_trans(b, vs + (kbase + kk * 16 + (mi & 1) * 8 + r) * kRowBytes + (n2 * 16 + (mi >> 1) * 8) * 2);
                 mma_f16_16816(o_acc[2 * n2], pa0, pa1, pa2, pa3, b[0], b[1]);
+                mma_f16_16816(o_acc[2 * n2], pl0, pl1, pl2, pl3, b[0], b[1]);
                 mma_f16_16816(o_acc[2 * n2 + 1], pa0, pa1, pa2, pa3, b[2], b[3]);
+                mma_f16_16816(o_acc[2 * n2 + 1], pl0, pl1, pl2, pl3, b[2], b[3]);
             }
         }
         // the second key half hands its state to the first through shared memory
@@ -322,7 +335,7 @@ static int launch_attention(const AttnArgs &a, int kv_heads, int tokens, int hea
     return launch_pdl(attn_combine_kernel<D>, dim3(tokens, heads), dim3(D), 0, stream, a);
 }
 
-extern "C" int bd_attention_decode(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache, int tokens,
+extern "C" int bd_attention_decode(const float *q, const uint16_t *k_cache, const uint16_t *v_cache, int tokens,
                                    int heads, int kv_heads, int head_dim, int keys, int windowed, int64_t anchor,
                                    int64_t window, int64_t stable_keys, float *out, void *workspace,
                                    size_t workspace_bytes, bd_stream_t stream) {
@@ -332,7 +345,7 @@ extern "C" int bd_attention_decode(const uint16_t *q, const uint16_t *k_cache, c
         return BD_ERR_INVALID;
     if (!workspace || workspace_bytes < bd_attention_workspace_bytes(heads, head_dim, keys)) return BD_ERR_WORKSPACE;
     AttnArgs a{};
-    a.q = reinterpret_cast<const __half *>(q);
+    a.q = q;
     a.k = reinterpret_cast<const __half *>(k_cache);
     a.v = reinterpret_cast<const __half *>(v_cache);
     a.tokens = tokens;

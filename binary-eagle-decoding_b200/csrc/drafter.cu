@@ -2,11 +2,34 @@
 // embedding gather, rms rows, and the per-head q/k/v post-processing
 // (rms over the head with its norm weight, rotary embedding, fp16 storage with
 // the cache_storage overflow check).
+#include <cmath>
+
 #include "kernels.cuh"
 
 #include <cuda_fp16.h>
 
 namespace bd {
+
+// Rotary frequencies theta^(-2j/d) for j < d/2, computed once on the host
+// (model.py:56-57: the exponent 2j/d as fp32, then the power), so every kernel and
+// every position uses the same fp32 frequency and the fp32 angle pos * f_j is
+// exactly the reference's.
+constexpr int kRopeMax = 128;  // head_dim <= 256
+struct RopeTable {
+    float f[kRopeMax];
+};
+
+// out_j = v_j cos(a) - v_{j+d/2} sin(a), out_{j+d/2} = v_{j+d/2} cos(a) + v_j sin(a),
+// a = pos * f_j, each product rounded as in the reference (no fused multiply-add).
+__device__ __forceinline__ void rotate_pair(float &a, float &b, int64_t pos, float freq) {
+    const float angle = __fmul_rn(static_cast<float>(pos), freq);
+    float s, c;
+    sincosf(angle, &s, &c);
+    const float na = __fadd_rn(__fmul_rn(a, c), __fmul_rn(-b, s));
+    const float nb = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
+    a = na;
+    b = nb;
+}
 
 // state[t] = vocabulary[ids[t]] (bf16 table -> fp32), HE4.forward's embedding (model.py:380-381).
 __global__ void embed_kernel(const uint16_t *__restrict__ table, int64_t vocab, int64_t hidden,
@@ -56,7 +79,7 @@ __global__ void rms_rows_kernel(const float *__restrict__ x, int64_t cols, int64
 // at dst[(r * heads + h) * d + j] of a row stride dst_ld (elements).
 // Grid (rows, heads), d/2 threads.
 __global__ void heads_post_kernel(const float *__restrict__ src, int64_t ld_src, int64_t col0, int heads, int d,
-                                  const float *__restrict__ nw, float eps, int rope, float theta, int64_t pos0,
+                                  const float *__restrict__ nw, float eps, int rope, const RopeTable freqs, int64_t pos0,
                                   __half *__restrict__ dst, int64_t dst_ld, int32_t *flags) {
     __shared__ float part[32];
     grid_wait();
@@ -73,16 +96,7 @@ __global__ void heads_post_kernel(const float *__restrict__ src, int64_t ld_src,
         }
     }
     if (!live) return;
-    if (rope) {
-        const float freq = powf(theta, -static_cast<float>(2 * j) / static_cast<float>(d));
-        const float angle = static_cast<float>(pos0 + r) * freq;
-        float s, c;
-        sincosf(angle, &s, &c);
-        const float na = a * c + (-b) * s;
-        const float nb = b * c + a * s;
-        a = na;
-        b = nb;
-    }
+    if (rope) rotate_pair(a, b, pos0 + r, freqs.f[j]);
     const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
     if (!isfinite(__half2float(ha)) || !isfinite(__half2float(hb))) set_flag(flags, BD_FLAG_CACHE_OVERFLOW);
     __half *out = dst + r * dst_ld + h * d;
@@ -95,7 +109,7 @@ __global__ void heads_post_kernel(const float *__restrict__ src, int64_t ld_src,
 // K cache row pos0 + r, v heads are stored as they are in the V cache.
 __global__ void qkv_post_kernel(const float *__restrict__ src, int64_t ld_src, int heads, int kv_heads, int d,
                                 const float *__restrict__ q_norm, const float *__restrict__ k_norm, float eps,
-                                float theta, int64_t pos0, __half *__restrict__ q, int64_t q_ld,
+                                const RopeTable freqs, int64_t pos0, float *__restrict__ q, int64_t q_ld,
                                 __half *__restrict__ kc, __half *__restrict__ vc, int64_t kv_ld, int32_t *flags) {
     __shared__ float part[32];
     grid_wait();
@@ -105,7 +119,9 @@ __global__ void qkv_post_kernel(const float *__restrict__ src, int64_t ld_src, i
     const float *v = src + r * ld_src + static_cast<int64_t>(y) * d;
     const float *nw = y < heads ? q_norm : (y < heads + kv_heads ? k_norm : nullptr);
     const bool rope = y < heads + kv_heads;
-    __half *out = y < heads ? q + r * q_ld + y * d
+    // q rows stay fp32 (the attention splits them into fp16 hi + lo); k and v
+    // rows are stored in the fp16 cache
+    __half *out = y < heads ? nullptr
                             : (y < heads + kv_heads ? kc + r * kv_ld + (y - heads) * d
                                                     : vc + r * kv_ld + (y - heads - kv_heads) * d);
     float a = live ? v[j] : 0.0f, b = live ? v[j + half] : 0.0f;
@@ -117,20 +133,26 @@ __global__ void qkv_post_kernel(const float *__restrict__ src, int64_t ld_src, i
         }
     }
     if (!live) return;
-    if (rope) {
-        const float freq = powf(theta, -static_cast<float>(2 * j) / static_cast<float>(d));
-        const float angle = static_cast<float>(pos0 + r) * freq;
-        float s, c;
-        sincosf(angle, &s, &c);
-        const float na = a * c + (-b) * s;
-        const float nb = b * c + a * s;
-        a = na;
-        b = nb;
+    if (rope) rotate_pair(a, b, pos0 + r, freqs.f[j]);
+    if (y < heads) {
+        float *qo = q + r * q_ld + static_cast<int64_t>(y) * d;
+        qo[j] = a;
+        qo[j + half] = b;
+        return;
     }
     const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
     if (!isfinite(__half2float(ha)) || !isfinite(__half2float(hb))) set_flag(flags, BD_FLAG_CACHE_OVERFLOW);
     out[j] = ha;
     out[j + half] = hb;
+}
+
+static RopeTable rope_table(float theta, int d) {
+    RopeTable r{};
+    for (int j = 0; j < d / 2 && j < kRopeMax; ++j) {
+        const float e = -(static_cast<float>(2 * j) / static_cast<float>(d));
+        r.f[j] = static_cast<float>(std::pow(static_cast<double>(theta), static_cast<double>(e)));
+    }
+    return r;
 }
 
 }  // namespace bd
@@ -139,17 +161,16 @@ using namespace bd;
 
 extern "C" int bd_qkv_post(const float *src, int n, int64_t ld_src, int heads, int kv_heads, int head_dim,
                            const float *q_norm, const float *k_norm, float epsilon, float theta, int64_t pos0,
-                           uint16_t *q_f16, int64_t q_ld, uint16_t *k_cache_f16, uint16_t *v_cache_f16, int64_t kv_ld,
+                           float *q_out, int64_t q_ld, uint16_t *k_cache_f16, uint16_t *v_cache_f16, int64_t kv_ld,
                            int32_t *flags, bd_stream_t stream) {
     // heads == 0: a k|v row block only (context rows), q pointers unused
-    if (n < 1 || heads < 0 || kv_heads < 1 || head_dim < 2 || (head_dim & 1) || head_dim > 2048 || !src ||
-        (heads > 0 && (!q_f16 || !q_norm)) || !k_cache_f16 || !v_cache_f16 || !k_norm)
+    if (n < 1 || heads < 0 || kv_heads < 1 || head_dim < 2 || (head_dim & 1) || head_dim > 2 * kRopeMax || !src ||
+        (heads > 0 && (!q_out || !q_norm)) || !k_cache_f16 || !v_cache_f16 || !k_norm)
         return BD_ERR_INVALID;
     const unsigned threads = static_cast<unsigned>((head_dim / 2 + 31) / 32 * 32);
     return launch_pdl(qkv_post_kernel, dim3(n, heads + 2 * kv_heads), dim3(threads), 0, stream, src, ld_src, heads,
-                      kv_heads, head_dim, q_norm, k_norm, epsilon, theta, pos0, reinterpret_cast<__half *>(q_f16),
-                      q_ld, reinterpret_cast<__half *>(k_cache_f16), reinterpret_cast<__half *>(v_cache_f16), kv_ld,
-                      flags);
+                      kv_heads, head_dim, q_norm, k_norm, epsilon, rope_table(theta, head_dim), pos0, q_out, q_ld,
+                      reinterpret_cast<__half *>(k_cache_f16), reinterpret_cast<__half *>(v_cache_f16), kv_ld, flags);
 }
 
 extern "C" int bd_embed_rows(const uint16_t *table, int64_t vocab, int64_t hidden, const int32_t *ids, int n,
@@ -167,10 +188,12 @@ extern "C" int bd_rms_rows(const float *x, int n, int64_t cols, int64_t ldx, con
 extern "C" int bd_heads_post(const float *src, int n, int64_t ld_src, int64_t col0, int heads, int head_dim,
                              const float *norm_weight, float epsilon, int rope, float theta, int64_t pos0,
                              uint16_t *dst_f16, int64_t dst_ld, int32_t *flags, bd_stream_t stream) {
-    if (n < 1 || heads < 1 || head_dim < 2 || (head_dim & 1) || head_dim > 2048 || !src || !dst_f16)
+    if (n < 1 || heads < 1 || head_dim < 2 || (head_dim & 1) || head_dim > 2048 || !src || !dst_f16 ||
+        (rope && head_dim > 2 * kRopeMax))
         return BD_ERR_INVALID;
     const unsigned threads = static_cast<unsigned>((head_dim / 2 + 31) / 32 * 32);
     return launch_pdl(heads_post_kernel, dim3(n, heads), dim3(threads), 0, stream, src, ld_src, col0, heads,
-                      head_dim, norm_weight, epsilon, rope, theta, pos0, reinterpret_cast<__half *>(dst_f16), dst_ld,
+                      head_dim, norm_weight, epsilon, rope, rope_table(theta, head_dim), pos0,
+                      reinterpret_cast<__half *>(dst_f16), dst_ld,
                       flags);
 }

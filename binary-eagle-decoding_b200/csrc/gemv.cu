@@ -15,9 +15,7 @@
 
 namespace bd {
 
-constexpr int kGemvThreads = 256;
-constexpr int kGemvWarps = kGemvThreads / 32;
-constexpr int kGemvUnroll = 4;  // K tiles per pipeline stage (two stages in flight)
+constexpr int kGemvUnroll = 4;  // K tiles per register stage
 
 struct GemvArgs {
     const uint4 *w;              // W16 tiles
@@ -80,8 +78,9 @@ __device__ __forceinline__ void gemv_compute(float (&acc)[RB][NT][4], const uint
     }
 }
 
-template <int NT, int RB>
-__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
+template <int NT, int RB, int W>
+__global__ void __launch_bounds__(W * 32) gemv_kernel(const GemvArgs a) {
+    constexpr int kGemvWarps = W, kGemvThreads = W * 32;
     __shared__ float red[kGemvWarps][RB * NT * 4][32];
     __shared__ unsigned long long best[32];
     __shared__ int last;
@@ -308,57 +307,109 @@ __global__ void argmax_finish_kernel(unsigned long long *keys, int n, int32_t *o
     }
 }
 
-template <int NT, int RB>
+template <int NT, int RB, int W>
 static int launch_gemv_t(const GemvArgs &a, cudaStream_t stream) {
     const int64_t nrb = (a.rows + 15) / 16;
     const unsigned grid = static_cast<unsigned>((nrb + RB - 1) / RB);
-    return launch_pdl(gemv_kernel<NT, RB>, dim3(grid, a.splits), dim3(kGemvThreads), 0, stream, a);
+    return launch_pdl(gemv_kernel<NT, RB, W>, dim3(grid, a.splits), dim3(W * 32), 0, stream, a);
 }
 
-// Two row blocks per CTA for the vocabulary-sized head (many row blocks) and for
-// long rows (the context fusion, K = taps x hidden): each warp keeps twice the
-// weight bytes in flight and the activation fragments serve both blocks.
-static bool gemv_wide(int64_t rows, int64_t cols) { return (rows + 15) / 16 >= 8 * 148 || cols >= 8192; }
+// Launch plan (measured on the drafter's shapes, 16 tokens, each GEMV behind its
+// activation pack in a CUDA graph).  Every warp's chain of dependent register
+// stages is what bounds these small, latency-bound products:
+//  - vocabulary-sized heads (>= 8 row blocks per SM): two row blocks per 8-warp
+//    CTA, so one K tile of activations serves both;
+//  - >= 2 row blocks per SM (the q|k|v projection): the same, one wave;
+//  - long rows (K >= 8192, the context fusion): one row block per 4-warp CTA and
+//    K split over CTAs to fill every resident slot (shorter chains per warp);
+//    the partial sums meet in the workspace;
+//  - otherwise one row block per 8-warp CTA over whole rows.
+// The workspace starts with a fixed block of counters (one per row group of a
+// split matrix; zero on entry, left zero) followed by scratch for the partial
+// sums, so one workspace serves calls of any shape in any order.
+constexpr int64_t kGemvCounters = 4096;
+constexpr size_t kGemvCounterBytes = kGemvCounters * sizeof(int32_t);
 
-// K splits over CTAs for a small matrix: enough CTAs for two per SM, at least
-// 8 K tiles per warp.
-static int gemv_splits(int64_t rows, int64_t cols, int sms) {
-    const bool wide = gemv_wide(rows, cols);
-    const int64_t groups = ((rows + 15) / 16 + (wide ? 1 : 0)) / (wide ? 2 : 1);
-    int64_t s = (2 * sms + groups - 1) / groups;
-    const int64_t cap = ((cols + 15) / 16) / (kGemvWarps * 8);
-    if (s > cap) s = cap;
-    return static_cast<int>(s < 1 ? 1 : s);
+struct GemvPlan {
+    int rb, warps, splits;
+    int64_t groups;
+};
+
+template <int NT, int RB, int W>
+static int gemv_occupancy_t() {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_kernel<NT, RB, W>, W * 32, 0) != cudaSuccess || n < 1)
+        n = 1;
+    return n;
 }
 
-static int64_t gemv_cells(int tokens, int64_t rows, int64_t cols) {
-    return static_cast<int64_t>(gemv_wide(rows, cols) ? 2 : 1) * ((tokens + 7) / 8) * 4 * 32;
+static int gemv_occupancy(int nt) {  // 4-warp, one-row-block CTAs resident per SM
+    static int cache[5] = {};
+    int &c = cache[nt];
+    if (!c) {
+        switch (nt) {
+            case 1: c = gemv_occupancy_t<1, 1, 4>(); break;
+            case 2: c = gemv_occupancy_t<2, 1, 4>(); break;
+            case 3: c = gemv_occupancy_t<3, 1, 4>(); break;
+            default: c = gemv_occupancy_t<4, 1, 4>(); break;
+        }
+    }
+    return c;
 }
+
+static GemvPlan gemv_plan(int tokens, int64_t rows, int64_t cols, int sms) {
+    const int nt = (tokens + 7) / 8;
+    const int64_t nrb = (rows + 15) / 16, nkt = (cols + 15) / 16;
+    GemvPlan p{};
+    p.warps = 8;
+    p.splits = 1;
+    p.rb = nrb >= 2 * static_cast<int64_t>(sms) ? 2 : 1;
+    p.groups = (nrb + p.rb - 1) / p.rb;
+    if (p.rb == 1 && nkt >= 512 && p.groups <= kGemvCounters) {
+        p.warps = 4;
+        int64_t s = static_cast<int64_t>(gemv_occupancy(nt)) * sms / p.groups;
+        const int64_t cap = nkt / (p.warps * kGemvUnroll);  // at least one full stage per warp
+        if (s > cap) s = cap;
+        p.splits = static_cast<int>(s < 1 ? 1 : s);
+    }
+    return p;
+}
+
+static int64_t gemv_cells(int tokens, const GemvPlan &p) { return static_cast<int64_t>(p.rb) * ((tokens + 7) / 8) * 4 * 32; }
+
+static size_t gemv_counter_bytes(const GemvPlan &) { return kGemvCounterBytes; }
 
 size_t gemv_workspace_bytes(int tokens, int64_t rows, int64_t cols, int sms) {
-    const int s = gemv_splits(rows, cols, sms);
-    if (s <= 1) return 0;
-    const bool wide = gemv_wide(rows, cols);
-    const int64_t groups = ((rows + 15) / 16 + (wide ? 1 : 0)) / (wide ? 2 : 1);
-    return static_cast<size_t>(s * groups * gemv_cells(tokens, rows, cols)) * sizeof(float) + 256 +
-           static_cast<size_t>(groups) * sizeof(int32_t);
+    const GemvPlan p = gemv_plan(tokens, rows, cols, sms);
+    if (p.splits <= 1) return 0;
+    return gemv_counter_bytes(p) +
+           static_cast<size_t>(p.splits) * static_cast<size_t>(p.groups * gemv_cells(tokens, p)) * sizeof(float);
 }
 
-int launch_gemv(const GemvArgs &a, cudaStream_t stream) {
-    const int64_t nrb = (a.rows + 15) / 16;
-    const bool wide = gemv_wide(a.rows, a.cols);
-    (void)nrb;
+int launch_gemv(const GemvArgs &a, int rb, int warps, cudaStream_t stream) {
     const int nt = (a.tokens + 7) / 8;
     if (a.tokens < 1 || a.tokens > 32 || nt > a.ntb) return BD_ERR_INVALID;
-    switch (nt * 2 + (wide ? 1 : 0)) {
-        case 2: return launch_gemv_t<1, 1>(a, stream);
-        case 3: return launch_gemv_t<1, 2>(a, stream);
-        case 4: return launch_gemv_t<2, 1>(a, stream);
-        case 5: return launch_gemv_t<2, 2>(a, stream);
-        case 6: return launch_gemv_t<3, 1>(a, stream);
-        case 7: return launch_gemv_t<3, 2>(a, stream);
-        case 8: return launch_gemv_t<4, 1>(a, stream);
-        default: return launch_gemv_t<4, 2>(a, stream);
+    if (warps == 8 && rb == 1) {
+        switch (nt) {
+            case 1: return launch_gemv_t<1, 1, 8>(a, stream);
+            case 2: return launch_gemv_t<2, 1, 8>(a, stream);
+            case 3: return launch_gemv_t<3, 1, 8>(a, stream);
+            default: return launch_gemv_t<4, 1, 8>(a, stream);
+        }
+    }
+    if (warps == 8) {
+        switch (nt) {
+            case 1: return launch_gemv_t<1, 2, 8>(a, stream);
+            case 2: return launch_gemv_t<2, 2, 8>(a, stream);
+            case 3: return launch_gemv_t<3, 2, 8>(a, stream);
+            default: return launch_gemv_t<4, 2, 8>(a, stream);
+        }
+    }
+    switch (nt) {  // 4-warp CTAs: one row block, K split (long rows)
+        case 1: return launch_gemv_t<1, 1, 4>(a, stream);
+        case 2: return launch_gemv_t<2, 1, 4>(a, stream);
+        case 3: return launch_gemv_t<3, 1, 4>(a, stream);
+        default: return launch_gemv_t<4, 1, 4>(a, stream);
     }
 }
 
@@ -428,14 +479,12 @@ extern "C" int bd_gemv_bf16(const void *w16, int64_t rows, int64_t cols, const v
     if ((out || residual) && ld_out < rows) return BD_ERR_INVALID;
     GemvArgs a{};
     a.splits = 1;
+    const GemvPlan plan = gemv_plan(tokens, rows, cols, sm_count());
     const size_t need = gemv_workspace_bytes(tokens, rows, cols, sm_count());
     if (need && workspace && workspace_bytes >= need) {  // without a workspace the K split is skipped
-        a.splits = gemv_splits(rows, cols, sm_count());
-        const bool wide = gemv_wide(rows, cols);
-        const int64_t groups = ((rows + 15) / 16 + (wide ? 1 : 0)) / (wide ? 2 : 1);
+        a.splits = plan.splits;
         a.counters = static_cast<int32_t *>(workspace);
-        a.partial = reinterpret_cast<float *>(static_cast<char *>(workspace) +
-                                              ((groups * sizeof(int32_t) + 255) & ~static_cast<size_t>(255)));
+        a.partial = reinterpret_cast<float *>(static_cast<char *>(workspace) + gemv_counter_bytes(plan));
     }
     a.w = static_cast<const uint4 *>(w16);
     a.rows = rows;
@@ -449,7 +498,7 @@ extern "C" int bd_gemv_bf16(const void *w16, int64_t rows, int64_t cols, const v
     a.residual = residual;
     a.argmax = argmax_keys;
     a.flags = flags;
-    return launch_gemv(a, stream);
+    return launch_gemv(a, plan.rb, plan.warps, stream);
 }
 
 extern "C" int bd_argmax_finish(unsigned long long *keys, int n, int32_t *out, bd_stream_t stream) {

@@ -124,7 +124,7 @@ class DraftEngine:
         self.resid = torch.zeros_like(self.state)
         self.normed = torch.zeros_like(self.state)
         self.qkv_out = torch.zeros((T, self.qkv_width), dtype=torch.float32, device=dev)
-        self.q16 = torch.zeros((T, cfg.heads * cfg.head_dim), dtype=torch.float16, device=dev)
+        self.q_rows = torch.zeros((T, cfg.heads * cfg.head_dim), dtype=torch.float32, device=dev)
         self.attn = torch.zeros((T, cfg.heads * cfg.head_dim), dtype=torch.float32, device=dev)
         widest = max(cfg.hidden, cfg.heads * cfg.head_dim, cfg.taps * cfg.hidden)
         self.x16 = torch.zeros(int(_lib.load().bd_x16_bytes(T, widest)), dtype=torch.uint8, device=dev)
@@ -230,6 +230,38 @@ class DraftEngine:
         ids[0] = first
         self.ids[:size].copy_(ids, non_blocking=True)
 
+    def embed(self, k: int) -> None:
+        """``state[:k]`` = embedding rows of ``ids[:k]`` (model.py:380-381)."""
+        _lib.call("bd_embed_rows", _p(self.vocab16), self.vocab_size, self.cfg.hidden, _p(self.ids), k,
+                  _p(self.state), self.flags.ptr, self._stream())
+
+    def attention_half(self, i: int, anchor: int, k: int) -> None:
+        """``resid[:k] = state + o(attention)`` of layer i (model.py:202-219); the block's
+        K/V rows go to cache positions anchor.."""
+        cfg = self.cfg
+        layer = self.layers[i]
+        H, qd, kvd = cfg.hidden, cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
+        st = self._stream()
+        self._pack(self.state, k, H, H, layer.attn_norm)
+        self._gemv(layer.qkv.data_ptr(), self.qkv_width, H, k, self.qkv_out, self.qkv_width)
+        _lib.call("bd_qkv_post", _p(self.qkv_out), k, self.qkv_width, cfg.heads, cfg.kv_heads, cfg.head_dim,
+                  _p(layer.q_norm), _p(layer.k_norm), float(cfg.epsilon), float(cfg.theta), anchor,
+                  _p(self.q_rows), qd, self._cache_ptr(self.k_cache, i, anchor),
+                  self._cache_ptr(self.v_cache, i, anchor), kvd, self.flags.ptr, st)
+        windowed = int(i < cfg.layers - 1)
+        # rows below the anchor were written by the ingest step, several kernels earlier
+        _lib.call("bd_attention_decode", _p(self.q_rows), self._cache_ptr(self.k_cache, i, 0),
+                  self._cache_ptr(self.v_cache, i, 0), k, cfg.heads, cfg.kv_heads, cfg.head_dim, anchor + k,
+                  windowed, anchor, cfg.window, anchor, _p(self.attn), _p(self.attn_ws), self.attn_ws.numel(), st)
+        self._pack(self.attn, k, qd, qd)
+        self._gemv(layer.o.data_ptr(), H, qd, k, self.resid, H, residual=self.state)
+
+    def ffn_half(self, i: int, k: int) -> None:
+        """``state[:k] = resid + ffn(rms(resid))`` of layer i (model.py:220-223)."""
+        layer = self.layers[i]
+        ops.ffn_he4(self.resid[:k], layer.ffn, self.resid[:k], flags=self.flags, out=self.state[:k],
+                    norm=layer.ffn_norm, epsilon=self.cfg.epsilon)
+
     def draft(self, anchor: int, size: int | None = None, logits: Tensor | None = None) -> Tensor:
         """One block of the drafter over the cached context (model.py:369-396).
 
@@ -240,28 +272,11 @@ class DraftEngine:
         cfg = self.cfg
         k = cfg.slots if size is None else size
         H = cfg.hidden
-        qd = cfg.heads * cfg.head_dim
-        kvd = cfg.kv_heads * cfg.head_dim
-        L = anchor + k
         st = self._stream()
-        _lib.call("bd_embed_rows", _p(self.vocab16), self.vocab_size, H, _p(self.ids), k, _p(self.state),
-                  self.flags.ptr, st)
-        for i, layer in enumerate(self.layers):
-            self._pack(self.state, k, H, H, layer.attn_norm)
-            self._gemv(layer.qkv.data_ptr(), self.qkv_width, H, k, self.qkv_out, self.qkv_width)
-            _lib.call("bd_qkv_post", _p(self.qkv_out), k, self.qkv_width, cfg.heads, cfg.kv_heads, cfg.head_dim,
-                      _p(layer.q_norm), _p(layer.k_norm), float(cfg.epsilon), float(cfg.theta), anchor,
-                      _p(self.q16), qd, self._cache_ptr(self.k_cache, i, anchor),
-                      self._cache_ptr(self.v_cache, i, anchor), kvd, self.flags.ptr, st)
-            windowed = int(i < cfg.layers - 1)
-            # rows below the anchor were written by the ingest step, several kernels earlier
-            _lib.call("bd_attention_decode", _p(self.q16), self._cache_ptr(self.k_cache, i, 0),
-                      self._cache_ptr(self.v_cache, i, 0), k, cfg.heads, cfg.kv_heads, cfg.head_dim, L, windowed,
-                      anchor, cfg.window, anchor, _p(self.attn), _p(self.attn_ws), self.attn_ws.numel(), st)
-            self._pack(self.attn, k, qd, qd)
-            self._gemv(layer.o.data_ptr(), H, qd, k, self.resid, H, residual=self.state)
-            ops.ffn_he4(self.resid[:k], layer.ffn, self.resid[:k], flags=self.flags, out=self.state[:k],
-                        norm=layer.ffn_norm, epsilon=cfg.epsilon)
+        self.embed(k)
+        for i in range(len(self.layers)):
+            self.attention_half(i, anchor, k)
+            self.ffn_half(i, k)
         self._pack(self.state, k, H, H, self.out_norm)
         self._gemv(self.head.data_ptr(), self.vocab_size, H, k, logits, self.vocab_size, keys=self.keys)
         _lib.call("bd_argmax_finish", _p(self.keys), k, _p(self.drafted), st)

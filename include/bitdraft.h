@@ -295,9 +295,11 @@ int bd_tile_w16(const void *w, int dtype_bits, int64_t rows, int64_t cols, void 
 int64_t bd_x16_bytes(int tokens, int64_t cols);
 int bd_pack_x16(const float *x, int tokens, int64_t cols, int64_t ldx, const float *rms_weight, float epsilon,
                 void *out, float *normed, int64_t ld_normed, int32_t *flags, bd_stream_t stream);
-/* The optional workspace (bd_gemv_workspace_bytes; zero it once, it is left
- * zeroed) lets small matrices split K over CTAs; partial sums are added in a
- * fixed order, so results do not depend on scheduling. */
+/* The optional workspace (bd_gemv_workspace_bytes) lets long-row matrices
+ * split K over CTAs; partial sums are added in a fixed order, so results do not
+ * depend on scheduling.  Zero it once: its first 16 KB hold per-row-group
+ * counters that every call leaves zeroed, the rest is scratch, so one workspace
+ * (sized for the largest need) serves calls of every shape in stream order. */
 size_t bd_gemv_workspace_bytes(int tokens, int64_t rows, int64_t cols);
 int bd_gemv_bf16(const void *w16, int64_t rows, int64_t cols, const void *x16, int tokens, float *out,
                  int64_t ld_out, const float *residual, unsigned long long *argmax_keys, int32_t *flags,
@@ -327,11 +329,12 @@ int bd_heads_post(const float *src, int n, int64_t ld_src, int64_t col0, int hea
                   const float *norm_weight, float epsilon, int rope, float theta, int64_t pos0,
                   uint16_t *dst_f16, int64_t dst_ld, int32_t *flags, bd_stream_t stream);
 /* The same for a whole q|k|v row block in one launch (Layer.forward,
- * model.py:207-213): q heads -> q_f16 [n][q_ld], k heads -> K cache rows
- * pos0.., v heads -> V cache rows pos0.. (row stride kv_ld elements). */
+ * model.py:207-213): q heads -> fp32 q_out [n][q_ld] (normalised and rotated,
+ * not rounded: the reference attends with fp32 queries), k heads -> K cache
+ * rows pos0.., v heads -> V cache rows pos0.. (fp16, row stride kv_ld elements). */
 int bd_qkv_post(const float *src, int n, int64_t ld_src, int heads, int kv_heads, int head_dim,
                 const float *q_norm, const float *k_norm, float epsilon, float theta, int64_t pos0,
-                uint16_t *q_f16, int64_t q_ld, uint16_t *k_cache_f16, uint16_t *v_cache_f16, int64_t kv_ld,
+                float *q_out, int64_t q_ld, uint16_t *k_cache_f16, uint16_t *v_cache_f16, int64_t kv_ld,
                 int32_t *flags, bd_stream_t stream);
 
 /* Block-draft attention of Layer.forward (w1a1_eagle/model.py:212-218) over the
@@ -339,13 +342,15 @@ int bd_qkv_post(const float *src, int n, int64_t ld_src, int heads, int kv_heads
  * with q head h reading kv head h / (heads / kv_heads), keys 0 .. keys-1 at
  * positions equal to their index, query row t at position anchor + t, and, if
  * `windowed`, only keys with |anchor + t - k| < window (all but the last layer,
- * model.py:390-392).  q fp16 [tokens][heads][d], caches fp16
+ * model.py:390-392).  q fp32 [tokens][heads][d], caches fp16
  * [positions][kv_heads][d]; tokens <= 16, head_dim 64 or 128, heads/kv_heads <= 4.
+ * The products keep fp32 precision: q and the probabilities enter the fp16
+ * tensor-core MMAs as hi + lo halves.
  * stable_keys: the caller's promise that cache rows [0, stable_keys) were not
  * written by the kernel launched immediately before this call on the stream
  * (they are then read before the launch waits for it; pass 0 when unsure). */
 size_t bd_attention_workspace_bytes(int heads, int head_dim, int keys);
-int bd_attention_decode(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache, int tokens, int heads,
+int bd_attention_decode(const float *q, const uint16_t *k_cache, const uint16_t *v_cache, int tokens, int heads,
                         int kv_heads, int head_dim, int keys, int windowed, int64_t anchor, int64_t window,
                         int64_t stable_keys, float *out, void *workspace, size_t workspace_bytes,
                         bd_stream_t stream);

@@ -87,6 +87,20 @@ def ffn_params(tensors, index):
 
 def layer_forward(tensors, index, state, context, positions, allowed, cfg):
     """``Layer.forward`` (``model.py:202-223``)."""
+    residual = attention_residual(tensors, index, state, context, positions, allowed, cfg)
+    return ffn_residual(tensors, index, residual, cfg)
+
+
+def ffn_residual(tensors, index, residual, cfg):
+    """The feed-forward half of ``Layer.forward`` (``model.py:220-223``)."""
+    p = f"blk.{index}."
+    norm = rms(residual, tensors[p + "ffn_norm.weight"], cfg.epsilon)
+    gate, up, down = ffn_params(tensors, index)
+    return he4_ffn(norm, residual, gate, up, down)
+
+
+def attention_residual(tensors, index, state, context, positions, allowed, cfg):
+    """The attention half of ``Layer.forward`` (``model.py:202-219``): ``state + o(attn)``."""
     p = f"blk.{index}."
     norm = rms(state, tensors[p + "attn_norm.weight"], cfg.epsilon)
     query = _linear(norm, tensors[p + "attn_q.weight"]).reshape(-1, cfg.heads, cfg.head_dim)
@@ -105,10 +119,7 @@ def layer_forward(tensors, index, state, context, positions, allowed, cfg):
     weights = np.exp(scores - top).astype(np.float32)
     weights = (weights / weights.sum(-1, keepdims=True)).astype(np.float32)
     attended = np.einsum("hgqk,khd->qhgd", weights, value).astype(np.float32)
-    residual = (state + _linear(attended.reshape(slots, -1), tensors[p + "attn_output.weight"])).astype(np.float32)
-    norm = rms(residual, tensors[p + "ffn_norm.weight"], cfg.epsilon)
-    gate, up, down = ffn_params(tensors, index)
-    return he4_ffn(norm, residual, gate, up, down)
+    return (state + _linear(attended.reshape(slots, -1), tensors[p + "attn_output.weight"])).astype(np.float32)
 
 
 def encode_context(tensors, features, anchor, cfg):

@@ -24,9 +24,15 @@ def bf16(x):
     return torch.as_tensor(x).to(torch.bfloat16).float()
 
 
-@pytest.mark.parametrize("rows,cols,tokens", [(1000, 300, 5), (9496 * 2, 2560, 16), (48, 16, 32), (17, 33, 9),
-                                              (2560, 10240, 16), (2048, 2560, 16), (2560, 4096, 7)])
-def test_gemv_store_and_argmax(rows, cols, tokens):
+@pytest.mark.parametrize("rows,cols,tokens,workspace", [
+    (1000, 300, 5, True), (9496 * 2, 2560, 16, True), (48, 16, 32, True), (17, 33, 9, True),
+    (2560, 10240, 16, True), (2048, 2560, 16, True), (2560, 4096, 7, True), (6144, 2560, 16, True),
+    (1000, 1300, 24, True), (77, 5000, 32, True), (1000, 8200, 9, True),
+    # vocabulary-sized row counts run 8-warp CTAs over whole rows
+    (80000, 1300, 16, True),
+    # without a workspace K is not split over CTAs
+    (1000, 300, 5, False), (2048, 2560, 16, False)])
+def test_gemv_store_and_argmax(rows, cols, tokens, workspace):
     lib = package()._lib
     g = torch.Generator().manual_seed(rows + cols)
     w = bf16(torch.randn(rows, cols, generator=g) * 0.05)
@@ -45,7 +51,8 @@ def test_gemv_store_and_argmax(rows, cols, tokens):
     nbytes = max(256, int(lib.load().bd_gemv_workspace_bytes(tokens, rows, cols)))
     ws = torch.zeros(nbytes, dtype=torch.uint8, device=DEV)
     lib.call("bd_gemv_bf16", w16.data_ptr(), rows, cols, x16.data_ptr(), tokens, out.data_ptr(), rows, None,
-             keys.data_ptr(), flags.data_ptr(), ws.data_ptr(), ws.numel(), stream)
+             keys.data_ptr(), flags.data_ptr(), ws.data_ptr() if workspace else None, ws.numel() if workspace else 0,
+             stream)
     # the K-split workspace is left zeroed for the next call
     assert not ws[:256].any() or int(lib.load().bd_gemv_workspace_bytes(tokens, rows, cols)) == 0
     ids = torch.zeros(tokens, dtype=torch.int32, device=DEV)
@@ -168,13 +175,97 @@ def test_round_graph_replays_match_direct_calls():
     assert torch.equal(direct[1:], out1)
 
 
+def _full_geometry():
+    import bench
+
+    drafter = submodule("drafter")
+    model = submodule("model")
+    tensors, vocabulary, features, tokens = bench.make_tensors(seed=0)
+    engine = drafter.DraftEngine(tensors, vocabulary, bench.VOCAB - 1, model.Geometry(**bench.GEOMETRY), device=DEV)
+    cfg = od.Geometry(**bench.GEOMETRY)
+    t = {k: v.numpy() for k, v in tensors.items()}
+    for i in range(cfg.layers):  # the engine's default quantizer state, as the oracle's tensors
+        p = f"blk.{i}."
+        for name in ("ffn_gate", "ffn_up", "ffn_down"):
+            t[p + name + ".scale"] = np.abs(t[p + name + ".weight"]).mean(-1, dtype=np.float32)
+            t[p + name + ".midpoint"] = np.zeros(t[p + name + ".weight"].shape[0], np.float32)
+        t[p + "ffn_gate_up.gain"] = np.ones(cfg.hidden, np.float32)
+        t[p + "ffn_gate_up.bound"] = np.float32(1.0)
+        t[p + "ffn_down.gain"] = np.ones(cfg.intermediate, np.float32)
+        t[p + "ffn_down.bound"] = np.float32(1.0)
+    return bench, engine, cfg, t, vocabulary, features, tokens
+
+
+def test_full_geometry_layers_match_oracle():
+    """Every half-layer of the drafter at its own sizes (hidden 2560, 4 layers, GQA
+    32/8, 4096 cached positions, 16 slots, all GEMVs sharing one workspace), each
+    fed the engine's own input state, against the oracle's.
+
+    End-to-end logits are not compared at this size: the 4-bit activation codes
+    of the HE4 feed-forward make the randomly initialised network chaotic; in the
+    oracle alone, scaling every linear output by (1 + 1e-6) moves the logits by
+    ~6% and flips ~7% of the argmaxes.  Per half-layer the comparison is tight."""
+    bench, engine, cfg, t, vocabulary, features, tokens = _full_geometry()
+    A, k = bench.CONTEXT, bench.SLOTS
+    engine.prefill(features.to(DEV), A)
+    feats = features.float().numpy()
+    enc = od.encode_context(t, feats, A, cfg)
+    positions, keys = np.arange(A, A + k), np.arange(A + k)
+    engine.set_tokens(int(tokens[A]), k)
+    engine.embed(k)
+    for i in range(cfg.layers):
+        context = od.layer_context(t, i, enc, np.arange(A), cfg)
+        got_k = engine.k_cache[i, :A].float().cpu().numpy().reshape(context[0].shape)
+        assert rel(got_k, context[0]) < 2e-4  # fp16 storage: rounding-boundary flips only
+        allowed = np.ones((k, A + k), dtype=bool)
+        if i < cfg.layers - 1:
+            allowed &= np.abs(positions[:, None] - keys[None, :]) < cfg.window
+        before = engine.state[:k].cpu().numpy()
+        engine.attention_half(i, A, k)
+        resid = engine.resid[:k].cpu().numpy()
+        want = od.attention_residual(t, i, before, context, positions, allowed, cfg)
+        assert rel(resid - before, want - before) < 1e-4, (i, rel(resid - before, want - before))
+        engine.ffn_half(i, k)
+        state = engine.state[:k].cpu().numpy()
+        want = od.ffn_residual(t, i, resid, cfg)
+        # a code at an exact rounding boundary may flip: the feed-forward tolerance
+        assert rel(state - resid, want - resid) < 1e-2, (i, rel(state - resid, want - resid))
+    torch.cuda.synchronize()
+    engine.check()
+
+
+def test_full_geometry_round_is_deterministic():
+    """The served round at full size: replays draft identical tokens, equal to the
+    argmax of the same round's logits, and mostly the oracle's (see above)."""
+    bench, engine, cfg, t, vocabulary, features, tokens = _full_geometry()
+    drafter = submodule("drafter")
+    engine.prefill(features.to(DEV), bench.CONTEXT - bench.INGEST)
+    rnd = drafter.DraftRound(engine, bench.CONTEXT, bench.SLOTS, bench.INGEST)
+    rnd.host_rows.copy_(features[bench.CONTEXT - bench.INGEST:bench.CONTEXT])
+    rounds = [rnd(int(tokens[bench.CONTEXT])).clone() for _ in range(3)]
+    logits = torch.zeros((bench.SLOTS, bench.VOCAB), device=DEV)
+    engine.draft(bench.CONTEXT, bench.SLOTS, logits=logits)
+    torch.cuda.synchronize()
+    engine.check()
+    got = logits.cpu().numpy()
+    drafted = acceptance.argmax_rows(got)[1:]
+    for r in rounds:
+        assert np.array_equal(r.cpu().numpy(), drafted)
+    feats = features.float().numpy()
+    enc = od.encode_context(t, feats, bench.CONTEXT, cfg)
+    contexts = [od.layer_context(t, i, enc, np.arange(bench.CONTEXT), cfg) for i in range(cfg.layers)]
+    want = od.he4_forward(t, vocabulary.numpy(), bench.VOCAB - 1, feats, tuple(int(v) for v in tokens),
+                          bench.CONTEXT, cfg, contexts=contexts)
+    assert np.mean(drafted == np.argmax(want[1:], -1)) >= 0.7
+
+
 @pytest.mark.parametrize("d,heads,kvh,tokens,keys,windowed", [(128, 32, 8, 16, 4112, 1), (128, 32, 8, 16, 300, 0),
                                                              (64, 4, 2, 5, 77, 1), (128, 8, 8, 1, 129, 0)])
 def test_attention_kernel_against_numpy(d, heads, kvh, tokens, keys, windowed):
     lib = package()._lib
     g = torch.Generator().manual_seed(keys)
     anchor, window = keys - tokens, 64
-    q = torch.randn(tokens, heads, d, generator=g).half()
+    q = torch.randn(tokens, heads, d, generator=g)
     kc = torch.randn(keys, kvh, d, generator=g).half()
     vc = torch.randn(keys, kvh, d, generator=g).half()
     out = torch.zeros(tokens, heads * d, device=DEV)
@@ -194,4 +285,6 @@ def test_attention_kernel_against_numpy(d, heads, kvh, tokens, keys, windowed):
         p = np.exp(s - s.max(-1, keepdims=True))
         want[:, h] = (p / p.sum(-1, keepdims=True)) @ vf[:, h // groups]
     got = out.cpu().numpy().reshape(tokens, heads, d)
-    assert rel(got, want) < 3e-3, rel(got, want)
+    # K and V are exact fp16 operands, q and the probabilities enter as hi + lo
+    # halves: the result keeps fp32 precision
+    assert rel(got, want) < 2e-5, rel(got, want)
