@@ -16,10 +16,8 @@
 // Early-start invariant: before grid_wait() a kernel reads only weights and
 // parameters; kernels call grid_launch_dependents() only after their own
 // grid_wait(), so the kernel that started early can rely on every kernel
-// before its predecessor having completed.  The one exception is the X16
-// activation pack (gemv.cu), which triggers before its wait: its dependents are
-// GEMVs that read nothing but weights before their own wait.  A kernel that
-// writes sign tiles (the optimizer's re-pack) never triggers early starts.
+// before its predecessor having completed.  A kernel that writes sign tiles
+// (the optimizer's re-pack) never triggers early starts.
 #include <mutex>
 #include <unordered_map>
 
