@@ -40,14 +40,6 @@ def _w16(weight: Tensor) -> Tensor:
     return out
 
 
-def _w16_rows(w16: Tensor, cols: int, row0: int, rows: int) -> int:
-    """Device address of rows [row0, row0 + rows) of a W16 buffer (row0 % 16 == 0)."""
-    if row0 % 16:
-        raise ValueError("W16 row ranges start on a 16-row block")
-    block = int(_lib.load().bd_w16_bytes(16, cols))
-    return w16.data_ptr() + (row0 // 16) * block
-
-
 @dataclass
 class LayerDevice:
     qkv: Tensor            # W16 of cat(attn_q, attn_k, attn_v)
@@ -114,6 +106,9 @@ class DraftEngine:
                 k_norm=t(p + "attn_k_norm.weight").float().contiguous(), ffn_norm=t(p + "ffn_norm.weight").float().contiguous(),
                 ffn=ffn))
         kvd = cfg.kv_heads * cfg.head_dim
+        # every layer's k|v rows stacked: the context rows of an ingest step are one
+        # GEMV over all layers (they share the encoded input)
+        self.kv_all = _w16(torch.cat(self.kv_bf16, 0))
         self.k_cache = torch.zeros((cfg.layers, self.max_positions, kvd), dtype=torch.float16, device=dev)
         self.v_cache = torch.zeros_like(self.k_cache)
         self.qkv_width = (cfg.heads + 2 * cfg.kv_heads) * cfg.head_dim
@@ -132,14 +127,14 @@ class DraftEngine:
         self.drafted = torch.zeros(T, dtype=torch.int32, device=dev)
         self.encoded = torch.zeros((T, cfg.hidden), dtype=torch.float32, device=dev)
         self.fused = torch.zeros((T, cfg.hidden), dtype=torch.float32, device=dev)
-        self.kv_out = torch.zeros((T, 2 * kvd), dtype=torch.float32, device=dev)
+        self.kv_out = torch.zeros((T, cfg.layers * 2 * kvd), dtype=torch.float32, device=dev)
         if cfg.head_dim not in (64, 128) or cfg.heads // cfg.kv_heads > 4 or cfg.slots > 16:
             raise ValueError("attention kernel geometry: head_dim 64/128, at most 4 q heads per kv head, <= 16 slots")
         self.attn_ws = torch.zeros(int(_lib.load().bd_attention_workspace_bytes(cfg.heads, cfg.head_dim,
                                                                                  self.max_positions)),
                                    dtype=torch.uint8, device=dev)
         lib = _lib.load()
-        shapes = [(cfg.hidden, cfg.taps * cfg.hidden), (2 * kvd, cfg.hidden), (self.qkv_width, cfg.hidden),
+        shapes = [(cfg.hidden, cfg.taps * cfg.hidden), (cfg.layers * 2 * kvd, cfg.hidden), (self.qkv_width, cfg.hidden),
                   (cfg.hidden, cfg.heads * cfg.head_dim), (self.vocab_size, cfg.hidden)]
         self.gemv_ws = torch.zeros(max(256, max(int(lib.bd_gemv_workspace_bytes(T, r, c)) for r, c in shapes)),
                                    dtype=torch.uint8, device=dev)
@@ -215,10 +210,11 @@ class DraftEngine:
         self._gemv(self.fc.data_ptr(), cfg.hidden, width, n, self.fused, cfg.hidden)
         self._pack(self.fused, n, cfg.hidden, cfg.hidden, self.enc_norm)
         kvd = cfg.kv_heads * cfg.head_dim
-        q_rows = cfg.heads * cfg.head_dim
+        width_kv = cfg.layers * 2 * kvd
+        self._gemv(self.kv_all.data_ptr(), width_kv, cfg.hidden, n, self.kv_out, width_kv)
         for i, layer in enumerate(self.layers):
-            self._gemv(_w16_rows(layer.qkv, cfg.hidden, q_rows, 2 * kvd), 2 * kvd, cfg.hidden, n, self.kv_out, 2 * kvd)
-            _lib.call("bd_qkv_post", _p(self.kv_out), n, 2 * kvd, 0, cfg.kv_heads, cfg.head_dim, None,
+            _lib.call("bd_qkv_post", self.kv_out.data_ptr() + i * 2 * kvd * 4, n, width_kv, 0, cfg.kv_heads,
+                      cfg.head_dim, None,
                       _p(layer.k_norm), float(cfg.epsilon), float(cfg.theta), pos0, None, 0,
                       self._cache_ptr(self.k_cache, i, pos0), self._cache_ptr(self.v_cache, i, pos0), kvd,
                       self.flags.ptr, self._stream())
