@@ -139,6 +139,8 @@ SIGNATURES = {
                               ctypes.c_float, c_int64, P, c_int64, P, P]),
     "bd_qkv_post": (c_int, [P, c_int, c_int64, c_int, c_int, c_int, P, P, ctypes.c_float, ctypes.c_float, c_int64,
                             P, c_int64, P, P, c_int64, P, P]),
+    "bd_context_kv_post": (c_int, [P, c_int, c_int64, c_int, c_int64, c_int, c_int, P, ctypes.c_float, ctypes.c_float,
+                                   c_int64, P, P, c_int64, c_int64, P, P]),
     "bd_attention_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "bd_attention_decode": (c_int, [P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int64, c_int64, c_int64, P,
                                     P, c_size_t, P]),

@@ -104,17 +104,24 @@ __global__ void heads_post_kernel(const float *__restrict__ src, int64_t ld_src,
     out[j + half] = hb;
 }
 
-// q, k and v of a projected row block in one launch: grid (rows, heads + 2 kv_heads);
-// q heads get q_norm + rope -> q (row stride q_ld), k heads k_norm + rope -> the
-// K cache row pos0 + r, v heads are stored as they are in the V cache.
+// q, k and v of a projected row block in one launch: grid (rows, heads + 2 kv_heads,
+// layers); q heads get q_norm + rope -> q (row stride q_ld), k heads k_norm + rope
+// -> the K cache row pos0 + r, v heads are stored as they are in the V cache.
+// Layer z reads columns from z * src_layer, norm weights from z * norm_layer and
+// writes cache rows at z * cache_layer (context rows of every layer at once).
 __global__ void qkv_post_kernel(const float *__restrict__ src, int64_t ld_src, int heads, int kv_heads, int d,
                                 const float *__restrict__ q_norm, const float *__restrict__ k_norm, float eps,
                                 const RopeTable freqs, int64_t pos0, float *__restrict__ q, int64_t q_ld,
-                                __half *__restrict__ kc, __half *__restrict__ vc, int64_t kv_ld, int32_t *flags) {
+                                __half *__restrict__ kc, __half *__restrict__ vc, int64_t kv_ld, int64_t src_layer,
+                                int64_t norm_layer, int64_t cache_layer, int32_t *flags) {
     __shared__ float part[32];
     grid_wait();
     grid_launch_dependents();
     const int r = blockIdx.x, y = blockIdx.y, j = threadIdx.x, half = d >> 1;
+    src += blockIdx.z * src_layer;
+    k_norm += blockIdx.z * norm_layer;
+    kc += blockIdx.z * cache_layer;
+    vc += blockIdx.z * cache_layer;
     const bool live = j < half;
     const float *v = src + r * ld_src + static_cast<int64_t>(y) * d;
     const float *nw = y < heads ? q_norm : (y < heads + kv_heads ? k_norm : nullptr);
@@ -168,9 +175,28 @@ extern "C" int bd_qkv_post(const float *src, int n, int64_t ld_src, int heads, i
         (heads > 0 && (!q_out || !q_norm)) || !k_cache_f16 || !v_cache_f16 || !k_norm)
         return BD_ERR_INVALID;
     const unsigned threads = static_cast<unsigned>((head_dim / 2 + 31) / 32 * 32);
-    return launch_pdl(qkv_post_kernel, dim3(n, heads + 2 * kv_heads), dim3(threads), 0, stream, src, ld_src, heads,
+    return launch_pdl(qkv_post_kernel, dim3(n, heads + 2 * kv_heads, 1), dim3(threads), 0, stream, src, ld_src, heads,
                       kv_heads, head_dim, q_norm, k_norm, epsilon, rope_table(theta, head_dim), pos0, q_out, q_ld,
-                      reinterpret_cast<__half *>(k_cache_f16), reinterpret_cast<__half *>(v_cache_f16), kv_ld, flags);
+                      reinterpret_cast<__half *>(k_cache_f16), reinterpret_cast<__half *>(v_cache_f16), kv_ld,
+                      int64_t{0}, int64_t{0}, int64_t{0}, flags);
+}
+
+extern "C" int bd_context_kv_post(const float *src, int n, int64_t ld_src, int layers, int64_t layer_cols,
+                                  int kv_heads, int head_dim, const float *k_norms, float epsilon, float theta,
+                                  int64_t pos0, uint16_t *k_cache_f16, uint16_t *v_cache_f16, int64_t kv_ld,
+                                  int64_t cache_layer_stride, int32_t *flags, bd_stream_t stream) {
+    if (n < 1 || layers < 1 || layers > 65535 || kv_heads < 1 || head_dim < 2 || (head_dim & 1) ||
+        head_dim > 2 * kRopeMax || !src || !k_norms || !k_cache_f16 || !v_cache_f16 ||
+        layer_cols < 2 * kv_heads * static_cast<int64_t>(head_dim) ||
+        ld_src < (layers - 1) * layer_cols + 2 * kv_heads * static_cast<int64_t>(head_dim) ||
+        kv_ld < kv_heads * static_cast<int64_t>(head_dim) || cache_layer_stride < 0)
+        return BD_ERR_INVALID;
+    const unsigned threads = static_cast<unsigned>((head_dim / 2 + 31) / 32 * 32);
+    return launch_pdl(qkv_post_kernel, dim3(n, 2 * kv_heads, layers), dim3(threads), 0, stream, src, ld_src, 0,
+                      kv_heads, head_dim, static_cast<const float *>(nullptr), k_norms, epsilon,
+                      rope_table(theta, head_dim), pos0, static_cast<float *>(nullptr), int64_t{0},
+                      reinterpret_cast<__half *>(k_cache_f16), reinterpret_cast<__half *>(v_cache_f16), kv_ld,
+                      layer_cols, static_cast<int64_t>(head_dim), cache_layer_stride, flags);
 }
 
 extern "C" int bd_embed_rows(const uint16_t *table, int64_t vocab, int64_t hidden, const int32_t *ids, int n,

@@ -109,6 +109,7 @@ class DraftEngine:
         # every layer's k|v rows stacked: the context rows of an ingest step are one
         # GEMV over all layers (they share the encoded input)
         self.kv_all = _w16(torch.cat(self.kv_bf16, 0))
+        self.k_norms = torch.stack([layer.k_norm for layer in self.layers]).contiguous()
         self.k_cache = torch.zeros((cfg.layers, self.max_positions, kvd), dtype=torch.float16, device=dev)
         self.v_cache = torch.zeros_like(self.k_cache)
         self.qkv_width = (cfg.heads + 2 * cfg.kv_heads) * cfg.head_dim
@@ -212,12 +213,10 @@ class DraftEngine:
         kvd = cfg.kv_heads * cfg.head_dim
         width_kv = cfg.layers * 2 * kvd
         self._gemv(self.kv_all.data_ptr(), width_kv, cfg.hidden, n, self.kv_out, width_kv)
-        for i, layer in enumerate(self.layers):
-            _lib.call("bd_qkv_post", self.kv_out.data_ptr() + i * 2 * kvd * 4, n, width_kv, 0, cfg.kv_heads,
-                      cfg.head_dim, None,
-                      _p(layer.k_norm), float(cfg.epsilon), float(cfg.theta), pos0, None, 0,
-                      self._cache_ptr(self.k_cache, i, pos0), self._cache_ptr(self.v_cache, i, pos0), kvd,
-                      self.flags.ptr, self._stream())
+        _lib.call("bd_context_kv_post", _p(self.kv_out), n, width_kv, cfg.layers, 2 * kvd, cfg.kv_heads, cfg.head_dim,
+                  _p(self.k_norms), float(cfg.epsilon), float(cfg.theta), pos0, self._cache_ptr(self.k_cache, 0, pos0),
+                  self._cache_ptr(self.v_cache, 0, pos0), kvd, self.max_positions * kvd, self.flags.ptr,
+                  self._stream())
         self.positions = max(self.positions, pos0 + n)
 
     # ------------------------------------------------------------------ draft

@@ -337,6 +337,16 @@ int bd_qkv_post(const float *src, int n, int64_t ld_src, int heads, int kv_heads
                 float *q_out, int64_t q_ld, uint16_t *k_cache_f16, uint16_t *v_cache_f16, int64_t kv_ld,
                 int32_t *flags, bd_stream_t stream);
 
+/* Context k|v rows of `layers` layers in one launch (Layer.context,
+ * model.py:195-200, for every layer of an ingest step): layer l's k|v block
+ * (k heads then v heads) starts at column l * layer_cols of src, its k norm
+ * weights at k_norms + l * head_dim, and its cache rows pos0.. at
+ * k_cache/v_cache + l * cache_layer_stride elements (row stride kv_ld). */
+int bd_context_kv_post(const float *src, int n, int64_t ld_src, int layers, int64_t layer_cols, int kv_heads,
+                       int head_dim, const float *k_norms, float epsilon, float theta, int64_t pos0,
+                       uint16_t *k_cache_f16, uint16_t *v_cache_f16, int64_t kv_ld, int64_t cache_layer_stride,
+                       int32_t *flags, bd_stream_t stream);
+
 /* Block-draft attention of Layer.forward (w1a1_eagle/model.py:212-218) over the
  * fp16 K/V cache: out[t][h * d + j] = softmax_k(q_t,h . k_k / sqrt(d)) v_k,j
  * with q head h reading kv head h / (heads / kv_heads), keys 0 .. keys-1 at

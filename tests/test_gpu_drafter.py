@@ -88,6 +88,31 @@ def test_heads_post_rope_and_cache_overflow():
     assert int(flags.item()) & 64
 
 
+def test_context_kv_post_matches_per_layer_calls():
+    """One launch over every layer's context k|v block writes exactly the cache rows
+    that per-layer ``bd_qkv_post`` calls write."""
+    lib = package()._lib
+    n, layers, kvh, d, positions, pos0 = 7, 3, 2, 64, 40, 11
+    g = torch.Generator().manual_seed(5)
+    width = layers * 2 * kvh * d
+    src = torch.randn(n, width, generator=g).to(DEV)
+    norms = (1 + 0.1 * torch.randn(layers, d, generator=g)).to(DEV)
+    caches = [torch.zeros(layers, positions, kvh * d, dtype=torch.float16, device=DEV) for _ in range(4)]
+    flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+    stream = torch.cuda.current_stream().cuda_stream
+    for i in range(layers):
+        lib.call("bd_qkv_post", src.data_ptr() + i * 2 * kvh * d * 4, n, width, 0, kvh, d, None,
+                 norms[i].data_ptr(), 1e-6, 1e6, pos0, None, 0, caches[0][i, pos0].data_ptr(),
+                 caches[1][i, pos0].data_ptr(), kvh * d, flags.data_ptr(), stream)
+    lib.call("bd_context_kv_post", src.data_ptr(), n, width, layers, 2 * kvh * d, kvh, d, norms.data_ptr(), 1e-6, 1e6,
+             pos0, caches[2][0, pos0].data_ptr(), caches[3][0, pos0].data_ptr(), kvh * d, positions * kvh * d,
+             flags.data_ptr(), stream)
+    torch.cuda.synchronize()
+    assert torch.equal(caches[0], caches[2]) and torch.equal(caches[1], caches[3])
+    assert caches[2][:, pos0:pos0 + n].abs().sum() > 0 and not caches[2][:, :pos0].any()
+    assert int(flags.item()) == 0
+
+
 def small_model(seed=0, window=24, layers=3):
     g = torch.Generator().manual_seed(seed)
     cfg = dict(hidden=256, intermediate=512, heads=4, kv_heads=2, head_dim=64, layers=layers, slots=16, taps=2,
