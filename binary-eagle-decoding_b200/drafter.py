@@ -124,6 +124,10 @@ class DraftEngine:
         self.attn = torch.zeros((T, cfg.heads * cfg.head_dim), dtype=torch.float32, device=dev)
         widest = max(cfg.hidden, cfg.heads * cfg.head_dim, cfg.taps * cfg.hidden)
         self.x16 = torch.zeros(int(_lib.load().bd_x16_bytes(T, widest)), dtype=torch.uint8, device=dev)
+        # the ingest step packs into its own buffer, so a round can run it beside the
+        # draft's first kernels (only the context fusion splits K over the shared GEMV
+        # workspace; no draft GEMV does)
+        self.x16_ctx = torch.zeros_like(self.x16)
         self.keys = torch.zeros(T, dtype=torch.int64, device=dev)
         self.drafted = torch.zeros(T, dtype=torch.int32, device=dev)
         self.encoded = torch.zeros((T, cfg.hidden), dtype=torch.float32, device=dev)
@@ -146,14 +150,16 @@ class DraftEngine:
     def _stream(self) -> int:
         return _stream(self.device)
 
-    def _pack(self, x: Tensor, n: int, cols: int, ld: int, weight: Tensor | None = None, normed: Tensor | None = None):
-        _lib.call("bd_pack_x16", _p(x), n, cols, ld, _p(weight), float(self.cfg.epsilon), _p(self.x16),
-                  _p(normed), normed.shape[1] if normed is not None else 0, self.flags.ptr, self._stream())
+    def _pack(self, x: Tensor, n: int, cols: int, ld: int, weight: Tensor | None = None, normed: Tensor | None = None,
+              x16: Tensor | None = None):
+        _lib.call("bd_pack_x16", _p(x), n, cols, ld, _p(weight), float(self.cfg.epsilon),
+                  _p(self.x16 if x16 is None else x16), _p(normed), normed.shape[1] if normed is not None else 0,
+                  self.flags.ptr, self._stream())
 
     def _gemv(self, w16_ptr: int, rows: int, cols: int, n: int, out: Tensor | None, ld_out: int,
-              residual: Tensor | None = None, keys: Tensor | None = None):
-        _lib.call("bd_gemv_bf16", w16_ptr, rows, cols, _p(self.x16), n, _p(out), ld_out, _p(residual), _p(keys),
-                  self.flags.ptr, _p(self.gemv_ws), self.gemv_ws.numel(), self._stream())
+              residual: Tensor | None = None, keys: Tensor | None = None, x16: Tensor | None = None):
+        _lib.call("bd_gemv_bf16", w16_ptr, rows, cols, _p(self.x16 if x16 is None else x16), n, _p(out), ld_out,
+                  _p(residual), _p(keys), self.flags.ptr, _p(self.gemv_ws), self.gemv_ws.numel(), self._stream())
 
     def _heads(self, src: Tensor, n: int, col0: int, heads: int, norm: Tensor | None, rope: bool, pos0: int,
                dst_ptr: int, dst_ld: int):
@@ -207,12 +213,13 @@ class DraftEngine:
         feats = features if features.dtype == torch.float32 else features.float()
         feats = feats.to(self.device).contiguous()
         width = cfg.taps * cfg.hidden
-        self._pack(feats, n, width, width)
-        self._gemv(self.fc.data_ptr(), cfg.hidden, width, n, self.fused, cfg.hidden)
-        self._pack(self.fused, n, cfg.hidden, cfg.hidden, self.enc_norm)
+        x16 = self.x16_ctx
+        self._pack(feats, n, width, width, x16=x16)
+        self._gemv(self.fc.data_ptr(), cfg.hidden, width, n, self.fused, cfg.hidden, x16=x16)
+        self._pack(self.fused, n, cfg.hidden, cfg.hidden, self.enc_norm, x16=x16)
         kvd = cfg.kv_heads * cfg.head_dim
         width_kv = cfg.layers * 2 * kvd
-        self._gemv(self.kv_all.data_ptr(), width_kv, cfg.hidden, n, self.kv_out, width_kv)
+        self._gemv(self.kv_all.data_ptr(), width_kv, cfg.hidden, n, self.kv_out, width_kv, x16=x16)
         _lib.call("bd_context_kv_post", _p(self.kv_out), n, width_kv, cfg.layers, 2 * kvd, cfg.kv_heads, cfg.head_dim,
                   _p(self.k_norms), float(cfg.epsilon), float(cfg.theta), pos0, self._cache_ptr(self.k_cache, 0, pos0),
                   self._cache_ptr(self.v_cache, 0, pos0), kvd, self.max_positions * kvd, self.flags.ptr,
@@ -233,16 +240,27 @@ class DraftEngine:
     def attention_half(self, i: int, anchor: int, k: int) -> None:
         """``resid[:k] = state + o(attention)`` of layer i (model.py:202-219); the block's
         K/V rows go to cache positions anchor.."""
+        self.qkv_rows(i, anchor, k)
+        self.attend(i, anchor, k)
+
+    def qkv_rows(self, i: int, anchor: int, k: int) -> None:
+        """q rows of layer i and the block's K/V cache rows at anchor.. (model.py:202-213)."""
         cfg = self.cfg
         layer = self.layers[i]
         H, qd, kvd = cfg.hidden, cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
-        st = self._stream()
         self._pack(self.state, k, H, H, layer.attn_norm)
         self._gemv(layer.qkv.data_ptr(), self.qkv_width, H, k, self.qkv_out, self.qkv_width)
         _lib.call("bd_qkv_post", _p(self.qkv_out), k, self.qkv_width, cfg.heads, cfg.kv_heads, cfg.head_dim,
                   _p(layer.q_norm), _p(layer.k_norm), float(cfg.epsilon), float(cfg.theta), anchor,
                   _p(self.q_rows), qd, self._cache_ptr(self.k_cache, i, anchor),
-                  self._cache_ptr(self.v_cache, i, anchor), kvd, self.flags.ptr, st)
+                  self._cache_ptr(self.v_cache, i, anchor), kvd, self.flags.ptr, self._stream())
+
+    def attend(self, i: int, anchor: int, k: int) -> None:
+        """``resid[:k] = state + o(attention)`` from the q rows and the cache (model.py:212-219)."""
+        cfg = self.cfg
+        H, qd = cfg.hidden, cfg.heads * cfg.head_dim
+        layer = self.layers[i]
+        st = self._stream()
         windowed = int(i < cfg.layers - 1)
         # rows below the anchor were written by the ingest step, several kernels earlier
         _lib.call("bd_attention_decode", _p(self.q_rows), self._cache_ptr(self.k_cache, i, 0),
@@ -257,12 +275,15 @@ class DraftEngine:
         ops.ffn_he4(self.resid[:k], layer.ffn, self.resid[:k], flags=self.flags, out=self.state[:k],
                     norm=layer.ffn_norm, epsilon=self.cfg.epsilon)
 
-    def draft(self, anchor: int, size: int | None = None, logits: Tensor | None = None) -> Tensor:
+    def draft(self, anchor: int, size: int | None = None, logits: Tensor | None = None, join=None) -> Tensor:
         """One block of the drafter over the cached context (model.py:369-396).
 
         Slot tokens come from ``self.ids`` (``set_tokens``); returns the argmax
         token of every slot (int32 [size], device) and fills ``logits`` [size, V]
-        when given.  Graph-capturable for fixed (anchor, size).
+        when given.  Graph-capturable for fixed (anchor, size).  ``join`` (optional) is
+        called after layer 0's q|k|v rows and before its attention, the first kernel
+        that reads cache rows below the anchor: a round that ingests context rows on
+        another stream waits for them there.
         """
         cfg = self.cfg
         k = cfg.slots if size is None else size
@@ -270,7 +291,10 @@ class DraftEngine:
         st = self._stream()
         self.embed(k)
         for i in range(len(self.layers)):
-            self.attention_half(i, anchor, k)
+            self.qkv_rows(i, anchor, k)
+            if i == 0 and join is not None:
+                join()  # the context rows the attention reads are complete from here on
+            self.attend(i, anchor, k)
             self.ffn_half(i, k)
         self._pack(self.state, k, H, H, self.out_norm)
         self._gemv(self.head.data_ptr(), self.vocab_size, H, k, logits, self.vocab_size, keys=self.keys)
@@ -295,6 +319,7 @@ class DraftRound:
         self.host_out = torch.zeros(size, dtype=torch.int32).pin_memory()
         engine.set_tokens(engine.mask, size)
         self.stream = torch.cuda.Stream(dev)
+        self.side = torch.cuda.Stream(dev)
         self.stream.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(self.stream):
             for _ in range(2):
@@ -307,8 +332,13 @@ class DraftRound:
         engine.check()
 
     def _body(self) -> None:
-        self.engine.ingest(self.dev_rows, self.anchor - self.rows)
-        self.engine.draft(self.anchor, self.size)
+        # the ingest step (fusion + context k|v of the new rows) runs beside the draft's
+        # embedding and layer-0 q|k|v rows, which do not read the context
+        main = torch.cuda.current_stream(self.engine.device)
+        self.side.wait_stream(main)
+        with torch.cuda.stream(self.side):
+            self.engine.ingest(self.dev_rows, self.anchor - self.rows)
+        self.engine.draft(self.anchor, self.size, join=lambda: main.wait_stream(self.side))
 
     def replay(self) -> None:
         self.graph.replay()
