@@ -19,7 +19,7 @@
 
 namespace bd {
 
-constexpr int kKeys = 128;  // keys per chunk
+constexpr int kKeys = 256;  // keys per chunk
 // Padded fp16 row of a staged K/V row in shared memory (conflict-free ldmatrix).
 template <int D>
 constexpr int row_bytes() { return D * 2 + 16; }
@@ -67,30 +67,35 @@ __device__ __forceinline__ void split_half2(float x0, float x1, uint32_t &hi, ui
     lo = *reinterpret_cast<const uint32_t *>(&l);
 }
 
-// 8 warps: warp w takes q head (w & 3) of the kv group and half (w >> 2) of the
-// chunk's keys; the two halves of a head merge through shared memory.
-constexpr int kAttnWarps = 8;
-constexpr int kHalfKeys = kKeys / 2;
+// 16 warps: warp w takes q head (w & 3) of the kv group and quarter (w >> 2) of
+// the chunk's keys; the quarters of a head merge through shared memory (the
+// staged K/V area, free once P V is done).  One CTA per SM.
+constexpr int kAttnWarps = 16;
+constexpr int kKeyParts = kAttnWarps / 4;
+constexpr int kPartKeys = kKeys / kKeyParts;  // 64
 
 template <int kDim>
 constexpr size_t attn_smem_bytes() {
-    // staged K and V rows, then the key-half exchange: per head 4 values per lane
-    // for every one of the kDim/8 O fragments plus (m, l) of its two rows
-    return 2 * static_cast<size_t>(kKeys) * row_bytes<kDim>() +
-           static_cast<size_t>(4) * (kDim / 8 * 4 + 4) * 32 * sizeof(float);
+    // staged K and V rows; the key-part exchange (per head and part 1..3, 4 values
+    // per lane for every one of the kDim/8 O fragments plus (m, l) of its two
+    // rows) reuses them
+    return 2 * static_cast<size_t>(kKeys) * row_bytes<kDim>();
 }
+static_assert(static_cast<size_t>(4) * (kKeyParts - 1) * (128 / 8 * 4 + 4) * 32 * sizeof(float) <=
+                  2 * static_cast<size_t>(kKeys) * row_bytes<128>(),
+              "the key-part exchange fits in the staged K/V area");
 
 template <int kDim>
-__global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_chunk_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(kAttnWarps * 32, 1) attn_chunk_kernel(const AttnArgs a) {
     constexpr int kRowBytes = row_bytes<kDim>();
     constexpr int kX = kDim / 8 * 4 + 4;  // exchanged floats per lane
     extern __shared__ __align__(16) char sm[];
     char *ks = sm;
     char *vs = sm + kKeys * kRowBytes;
-    float *xch = reinterpret_cast<float *>(sm + 2 * kKeys * kRowBytes);  // [head][kX][32]
+    float *xch = reinterpret_cast<float *>(sm);  // [part - 1][head][kX][32], after P V
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
-    const int hw = warp & 3, kh = warp >> 2;
+    const int hw = warp & 3, kh = warp >> 2;  // head of the group, key part
     const int kvh = blockIdx.x, chunk = blockIdx.y;
     const int groups = a.heads / a.kv_heads;
     const int key0 = chunk * kKeys;
@@ -139,16 +144,16 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_chunk_kernel(const At
         for (int i = 0; i < 4; ++i) o_acc[n][i] = 0.0f;
     if (head_live) {
         // S = Q K^T over this warp's 64 keys: 8 n-tiles of 8 keys
-        const int kbase = kh * kHalfKeys;
-        float s_acc[kHalfKeys / 8][4];
+        const int kbase = kh * kPartKeys;
+        float s_acc[kPartKeys / 8][4];
 #pragma unroll
-        for (int n = 0; n < kHalfKeys / 8; ++n)
+        for (int n = 0; n < kPartKeys / 8; ++n)
 #pragma unroll
             for (int i = 0; i < 4; ++i) s_acc[n][i] = 0.0f;
 #pragma unroll
         for (int s2 = 0; s2 < kDim / 32; ++s2) {
 #pragma unroll
-            for (int n = 0; n < kHalfKeys / 8; ++n) {
+            for (int n = 0; n < kPartKeys / 8; ++n) {
                 // x4: matrices (d 0-7, 8-15) of k-step 2*s2 and (d 0-7, 8-15) of k-step 2*s2+1 for 8 keys
                 uint32_t b[4];
                 const int mi = lane >> 3, r = lane & 7;
@@ -164,7 +169,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_chunk_kernel(const At
         // scale, mask, row maxima (rows g and g + 8 of this lane)
         const int kq0 = key0 + kbase + 2 * t;
 #pragma unroll
-        for (int n = 0; n < kHalfKeys / 8; ++n)
+        for (int n = 0; n < kPartKeys / 8; ++n)
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const int row = g + 8 * (i >> 1);
@@ -184,7 +189,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_chunk_kernel(const At
             m[r] = fmaxf(m[r], __shfl_xor_sync(0xffffffffu, m[r], 2));
         }
 #pragma unroll
-        for (int n = 0; n < kHalfKeys / 8; ++n)
+        for (int n = 0; n < kPartKeys / 8; ++n)
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const float mm = m[i >> 1];
@@ -199,7 +204,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_chunk_kernel(const At
         }
         // O = P V over the 64 keys: P re-packed from the S accumulators as A fragments
 #pragma unroll
-        for (int kk = 0; kk < kHalfKeys / 16; ++kk) {
+        for (int kk = 0; kk < kPartKeys / 16; ++kk) {
             uint32_t pa0, pa1, pa2, pa3, pl0, pl1, pl2, pl3;
             split_half2(s_acc[2 * kk][0], s_acc[2 * kk][1], pa0, pl0);
             split_half2(s_acc[2 * kk][2], s_acc[2 * kk][3], pa1, pl1);
@@ -216,23 +221,25 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_chunk_kernel(const At
                 mma_f16_16816(o_acc[2 * n2 + 1], pl0, pl1, pl2, pl3, b[2], b[3]);
             }
         }
-        // the second key half hands its state to the first through shared memory
-        if (kh == 1) {
-            float *x = xch + hw * kX * 32 + lane;
+    }
+    // key parts 1..3 hand their state to part 0 through shared memory (the staged
+    // K/V area: every warp has finished P V at the barrier)
+    __syncthreads();
+    if (head_live && kh > 0) {
+        float *x = xch + ((kh - 1) * 4 + hw) * kX * 32 + lane;
 #pragma unroll
-            for (int n = 0; n < kDim / 8; ++n)
+        for (int n = 0; n < kDim / 8; ++n)
 #pragma unroll
-                for (int i = 0; i < 4; ++i) x[(n * 4 + i) * 32] = o_acc[n][i];
-            x[(kX - 4) * 32] = m[0];
-            x[(kX - 3) * 32] = m[1];
-            x[(kX - 2) * 32] = l[0];
-            x[(kX - 1) * 32] = l[1];
-        }
+            for (int i = 0; i < 4; ++i) x[(n * 4 + i) * 32] = o_acc[n][i];
+        x[(kX - 4) * 32] = m[0];
+        x[(kX - 3) * 32] = m[1];
+        x[(kX - 2) * 32] = l[0];
+        x[(kX - 1) * 32] = l[1];
     }
     __syncthreads();
-    if (!head_live || kh == 1) return;
-    {
-        const float *x = xch + hw * kX * 32 + lane;
+    if (!head_live || kh > 0) return;
+    for (int part = 1; part < kKeyParts; ++part) {  // fixed order
+        const float *x = xch + ((part - 1) * 4 + hw) * kX * 32 + lane;
         float f0[2], f1[2];
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
