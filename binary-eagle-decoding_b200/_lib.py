@@ -144,6 +144,8 @@ SIGNATURES = {
     "bd_attention_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "bd_attention_decode": (c_int, [P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int64, c_int64, c_int64, P,
                                     P, c_size_t, P]),
+    "bd_attention_decode_x16": (c_int, [P, P, P, c_int, c_int, c_int, c_int, c_int, c_int, c_int64, c_int64,
+                                        c_int64, P, P, P, c_size_t, P]),
 }
 
 _lib = None
@@ -174,7 +176,8 @@ def load() -> ctypes.CDLL:
 
 
 # Kernel launches issued by each entry point (for launch accounting).
-KERNELS_PER_CALL = {"bd_ffn_he4": 3, "bd_ffn_w1": 4, "bd_attention_decode": 2, "bd_accept_rejection": 2,
+KERNELS_PER_CALL = {"bd_ffn_he4": 3, "bd_ffn_w1": 4, "bd_attention_decode": 2, "bd_attention_decode_x16": 2,
+                    "bd_accept_rejection": 2,
                     "bd_ste_grad_prep": 2, "bd_ste_input_backward": 2}
 launches = 0
 

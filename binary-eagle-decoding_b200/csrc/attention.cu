@@ -15,6 +15,7 @@
 // chunks.  No waits between CTAs: partials meet only in the combine launch.
 #include "kernels.cuh"
 
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 namespace bd {
@@ -36,7 +37,9 @@ struct AttnArgs {
     int chunks;
     float *part_o;          // [chunks][heads][16][d]
     float *part_ml;         // [chunks][heads][16][2]
-    float *out;             // [tokens][heads * d]
+    float *out;             // [tokens][heads * d], or null when x16 is set
+    uint16_t *x16;          // X16 fragments of the output rows (the GEMV's activation layout), or null
+    int32_t *flags;
 };
 
 __device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void *p) {
@@ -319,7 +322,22 @@ __global__ void attn_combine_kernel(const AttnArgs a) {
     float num = 0.0f;
 #pragma unroll 8
     for (int c = 0; c < a.chunks; ++c) num += wgt[c] * po[c * stride];
-    a.out[static_cast<int64_t>(token) * a.heads * kDim + head * kDim + j] = num / s_den;
+    const float y = num / s_den;
+    if (a.out) a.out[static_cast<int64_t>(token) * a.heads * kDim + head * kDim + j] = y;
+    if (a.x16) {
+        // the element's slot in both bf16 planes of the X16 layout (as bd_pack_x16 writes it)
+        const int64_t cols = static_cast<int64_t>(a.heads) * kDim, nkt = cols / 16;
+        const int64_t ntb = (a.tokens + 7) / 8;
+        const int64_t col = static_cast<int64_t>(head) * kDim + j;
+        const int kk = static_cast<int>(col & 15);
+        const int64_t word = (((token >> 3) * nkt + (col >> 4)) * 32 + (token & 7) * 4 + ((kk & 7) >> 1)) * 2 + (kk >> 3);
+        const int64_t slot = word * 2 + (kk & 1);
+        const __nv_bfloat16 hi = __float2bfloat16_rn(y);
+        const __nv_bfloat16 lo = __float2bfloat16_rn(y - __bfloat162float(hi));
+        a.x16[slot] = __bfloat16_as_ushort(hi);
+        a.x16[ntb * nkt * 32 * 4 + slot] = __bfloat16_as_ushort(lo);
+        if (!isfinite(y)) set_flag(a.flags, BD_FLAG_NONFINITE_STATE);
+    }
 }
 
 }  // namespace bd
@@ -342,13 +360,13 @@ static int launch_attention(const AttnArgs &a, int kv_heads, int tokens, int hea
     return launch_pdl(attn_combine_kernel<D>, dim3(tokens, heads), dim3(D), 0, stream, a);
 }
 
-extern "C" int bd_attention_decode(const float *q, const uint16_t *k_cache, const uint16_t *v_cache, int tokens,
-                                   int heads, int kv_heads, int head_dim, int keys, int windowed, int64_t anchor,
-                                   int64_t window, int64_t stable_keys, float *out, void *workspace,
-                                   size_t workspace_bytes, bd_stream_t stream) {
+static int attention_decode(const float *q, const uint16_t *k_cache, const uint16_t *v_cache, int tokens, int heads,
+                            int kv_heads, int head_dim, int keys, int windowed, int64_t anchor, int64_t window,
+                            int64_t stable_keys, float *out, void *x16, int32_t *flags, void *workspace,
+                            size_t workspace_bytes, bd_stream_t stream) {
     if (tokens < 1 || tokens > 16 || (head_dim != 64 && head_dim != 128) || heads < 1 || kv_heads < 1 ||
         heads % kv_heads ||
-        heads / kv_heads > 4 || keys < 1 || keys > kMaxChunks * kKeys || !q || !k_cache || !v_cache || !out)
+        heads / kv_heads > 4 || keys < 1 || keys > kMaxChunks * kKeys || !q || !k_cache || !v_cache || (!out && !x16))
         return BD_ERR_INVALID;
     if (!workspace || workspace_bytes < bd_attention_workspace_bytes(heads, head_dim, keys)) return BD_ERR_WORKSPACE;
     AttnArgs a{};
@@ -368,6 +386,26 @@ extern "C" int bd_attention_decode(const float *q, const uint16_t *k_cache, cons
     a.part_ml = static_cast<float *>(workspace);
     a.part_o = a.part_ml + static_cast<size_t>(a.chunks) * heads * 16 * 2;
     a.out = out;
+    a.x16 = static_cast<uint16_t *>(x16);
+    a.flags = flags;
     return head_dim == 64 ? launch_attention<64>(a, kv_heads, tokens, heads, stream)
                           : launch_attention<128>(a, kv_heads, tokens, heads, stream);
+}
+
+extern "C" int bd_attention_decode(const float *q, const uint16_t *k_cache, const uint16_t *v_cache, int tokens,
+                                   int heads, int kv_heads, int head_dim, int keys, int windowed, int64_t anchor,
+                                   int64_t window, int64_t stable_keys, float *out, void *workspace,
+                                   size_t workspace_bytes, bd_stream_t stream) {
+    if (!out) return BD_ERR_INVALID;
+    return attention_decode(q, k_cache, v_cache, tokens, heads, kv_heads, head_dim, keys, windowed, anchor, window,
+                            stable_keys, out, nullptr, nullptr, workspace, workspace_bytes, stream);
+}
+
+extern "C" int bd_attention_decode_x16(const float *q, const uint16_t *k_cache, const uint16_t *v_cache, int tokens,
+                                       int heads, int kv_heads, int head_dim, int keys, int windowed, int64_t anchor,
+                                       int64_t window, int64_t stable_keys, void *x16, int32_t *flags,
+                                       void *workspace, size_t workspace_bytes, bd_stream_t stream) {
+    if (!x16) return BD_ERR_INVALID;
+    return attention_decode(q, k_cache, v_cache, tokens, heads, kv_heads, head_dim, keys, windowed, anchor, window,
+                            stable_keys, nullptr, x16, flags, workspace, workspace_bytes, stream);
 }

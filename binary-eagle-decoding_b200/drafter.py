@@ -262,11 +262,12 @@ class DraftEngine:
         layer = self.layers[i]
         st = self._stream()
         windowed = int(i < cfg.layers - 1)
-        # rows below the anchor were written by the ingest step, several kernels earlier
-        _lib.call("bd_attention_decode", _p(self.q_rows), self._cache_ptr(self.k_cache, i, 0),
+        # rows below the anchor were written by the ingest step, several kernels earlier;
+        # the attention writes its rows as the output projection's X16 activations
+        _lib.call("bd_attention_decode_x16", _p(self.q_rows), self._cache_ptr(self.k_cache, i, 0),
                   self._cache_ptr(self.v_cache, i, 0), k, cfg.heads, cfg.kv_heads, cfg.head_dim, anchor + k,
-                  windowed, anchor, cfg.window, anchor, _p(self.attn), _p(self.attn_ws), self.attn_ws.numel(), st)
-        self._pack(self.attn, k, qd, qd)
+                  windowed, anchor, cfg.window, anchor, _p(self.x16), self.flags.ptr, _p(self.attn_ws),
+                  self.attn_ws.numel(), st)
         self._gemv(layer.o.data_ptr(), H, qd, k, self.resid, H, residual=self.state)
 
     def ffn_half(self, i: int, k: int) -> None:

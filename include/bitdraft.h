@@ -360,6 +360,14 @@ int bd_context_kv_post(const float *src, int n, int64_t ld_src, int layers, int6
  * written by the kernel launched immediately before this call on the stream
  * (they are then read before the launch waits for it; pass 0 when unsure). */
 size_t bd_attention_workspace_bytes(int heads, int head_dim, int keys);
+/* The same attention writing its output rows straight into the X16 activation
+ * layout of bd_pack_x16 (unnormalised, tokens rows of heads * head_dim columns)
+ * for the output-projection GEMV, instead of fp32 rows; a non-finite output sets
+ * BD_FLAG_NONFINITE_STATE in flags (may be NULL). */
+int bd_attention_decode_x16(const float *q, const uint16_t *k_cache, const uint16_t *v_cache, int tokens, int heads,
+                            int kv_heads, int head_dim, int keys, int windowed, int64_t anchor, int64_t window,
+                            int64_t stable_keys, void *x16, int32_t *flags, void *workspace, size_t workspace_bytes,
+                            bd_stream_t stream);
 int bd_attention_decode(const float *q, const uint16_t *k_cache, const uint16_t *v_cache, int tokens, int heads,
                         int kv_heads, int head_dim, int keys, int windowed, int64_t anchor, int64_t window,
                         int64_t stable_keys, float *out, void *workspace, size_t workspace_bytes,

@@ -313,3 +313,15 @@ def test_attention_kernel_against_numpy(d, heads, kvh, tokens, keys, windowed):
     # K and V are exact fp16 operands, q and the probabilities enter as hi + lo
     # halves: the result keeps fp32 precision
     assert rel(got, want) < 2e-5, rel(got, want)
+    # the variant that writes the output-projection GEMV's X16 activations: the
+    # same bytes bd_pack_x16 makes from the fp32 rows
+    x16 = torch.zeros(int(lib.load().bd_x16_bytes(tokens, heads * d)), dtype=torch.uint8, device=DEV)
+    packed = torch.zeros_like(x16)
+    flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+    stream = torch.cuda.current_stream().cuda_stream
+    lib.call("bd_attention_decode_x16", qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), tokens, heads, kvh, d, keys,
+             windowed, anchor, window, keys, x16.data_ptr(), flags.data_ptr(), ws.data_ptr(), ws.numel(), stream)
+    lib.call("bd_pack_x16", out.data_ptr(), tokens, heads * d, heads * d, None, 1e-6, packed.data_ptr(), None, 0,
+             flags.data_ptr(), stream)
+    torch.cuda.synchronize()
+    assert torch.equal(x16, packed) and int(flags.item()) == 0
