@@ -278,37 +278,53 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1) attn_chunk_kernel(const At
 // Grid (tokens, heads), d threads: chunk weights are computed once into shared
 // memory, then every thread sums its column over the chunks with independent loads.
 constexpr int kMaxChunks = 1024;
+constexpr int kCombineBatch = 20;  // chunk partials per thread requested at once
 
 template <int kDim>
-__global__ void attn_combine_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(kDim) attn_combine_kernel(const AttnArgs a) {
     __shared__ float wgt[kMaxChunks];
     __shared__ float red[kDim / 32];
-    __shared__ float s_den;
+    __shared__ float s_max, s_den;
     grid_wait();
     grid_launch_dependents();
     const int token = blockIdx.x, head = blockIdx.y, j = threadIdx.x;
     const int lane = j & 31, warp = j >> 5;
+    // the first kCombineBatch chunks' O values are requested with the chunk maxima
+    // and sums, so the combine costs about one L2 round trip
+    const float *po = a.part_o + (static_cast<int64_t>(head) * 16 + token) * kDim + j;
+    const int64_t stride = static_cast<int64_t>(a.heads) * 16 * kDim;
+    float ov[kCombineBatch];
+#pragma unroll
+    for (int c = 0; c < kCombineBatch; ++c) ov[c] = c < a.chunks ? po[c * stride] : 0.0f;
     float mloc = -INFINITY;
-    for (int c = j; c < a.chunks; c += kDim)
-        mloc = fmaxf(mloc, a.part_ml[((static_cast<int64_t>(c) * a.heads + head) * 16 + token) * 2]);
+    for (int c = j; c < a.chunks; c += kDim) {
+        const float mc = a.part_ml[((static_cast<int64_t>(c) * a.heads + head) * 16 + token) * 2];
+        wgt[c] = mc;
+        mloc = fmaxf(mloc, mc);
+    }
 #pragma unroll
     for (int d = 16; d > 0; d >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, d));
     if (lane == 0) red[warp] = mloc;
     __syncthreads();
-    float M = red[0];
+    if (j == 0) {
+        float M = red[0];
 #pragma unroll
-    for (int w = 1; w < kDim / 32; ++w) M = fmaxf(M, red[w]);
+        for (int w = 1; w < kDim / 32; ++w) M = fmaxf(M, red[w]);
+        s_max = M;
+    }
     __syncthreads();
+    const float M = s_max;
     float dloc = 0.0f;
     for (int c = j; c < a.chunks; c += kDim) {
         const int64_t base = (static_cast<int64_t>(c) * a.heads + head) * 16 + token;
-        const float mc = a.part_ml[base * 2];
+        const float mc = wgt[c];
         const float w = mc == -INFINITY ? 0.0f : __expf(mc - M);
         wgt[c] = w;
         dloc += w * a.part_ml[base * 2 + 1];
     }
 #pragma unroll
     for (int d = 16; d > 0; d >>= 1) dloc += __shfl_xor_sync(0xffffffffu, dloc, d);
+    __syncthreads();  // red is reused; wgt is complete
     if (lane == 0) red[warp] = dloc;
     __syncthreads();
     if (j == 0) {
@@ -317,11 +333,12 @@ __global__ void attn_combine_kernel(const AttnArgs a) {
         s_den = den;
     }
     __syncthreads();
-    const float *po = a.part_o + (static_cast<int64_t>(head) * 16 + token) * kDim + j;
-    const int64_t stride = static_cast<int64_t>(a.heads) * 16 * kDim;
     float num = 0.0f;
+#pragma unroll
+    for (int c = 0; c < kCombineBatch; ++c)
+        if (c < a.chunks) num += wgt[c] * ov[c];
 #pragma unroll 8
-    for (int c = 0; c < a.chunks; ++c) num += wgt[c] * po[c * stride];
+    for (int c = kCombineBatch; c < a.chunks; ++c) num += wgt[c] * po[c * stride];
     const float y = num / s_den;
     if (a.out) a.out[static_cast<int64_t>(token) * a.heads * kDim + head * kDim + j] = y;
     if (a.x16) {
