@@ -121,7 +121,6 @@ class DraftEngine:
         self.normed = torch.zeros_like(self.state)
         self.qkv_out = torch.zeros((T, self.qkv_width), dtype=torch.float32, device=dev)
         self.q_rows = torch.zeros((T, cfg.heads * cfg.head_dim), dtype=torch.float32, device=dev)
-        self.attn = torch.zeros((T, cfg.heads * cfg.head_dim), dtype=torch.float32, device=dev)
         widest = max(cfg.hidden, cfg.heads * cfg.head_dim, cfg.taps * cfg.hidden)
         self.x16 = torch.zeros(int(_lib.load().bd_x16_bytes(T, widest)), dtype=torch.uint8, device=dev)
         # the ingest step packs into its own buffer, so a round can run it beside the
