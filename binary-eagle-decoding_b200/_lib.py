@@ -134,6 +134,7 @@ SIGNATURES = {
     "bd_gemv_bf16": (c_int, [P, c_int64, c_int64, P, c_int, P, c_int64, P, P, P, P, c_size_t, P]),
     "bd_argmax_finish": (c_int, [P, c_int, P, P]),
     "bd_embed_rows": (c_int, [P, c_int64, c_int64, P, c_int, P, P, P]),
+    "bd_round_submit": (c_int, [P, P, P, c_size_t, P, P, P, P, c_int, P]),
     "bd_rms_rows": (c_int, [P, c_int, c_int64, c_int64, P, ctypes.c_float, P, c_int64, P]),
     "bd_heads_post": (c_int, [P, c_int, c_int64, c_int64, c_int, c_int, P, ctypes.c_float, c_int,
                               ctypes.c_float, c_int64, P, c_int64, P, P]),

@@ -223,3 +223,21 @@ extern "C" int bd_heads_post(const float *src, int n, int64_t ld_src, int64_t co
                       reinterpret_cast<__half *>(dst_f16), dst_ld,
                       flags);
 }
+
+extern "C" int bd_round_submit(void *graph_exec, const void *host_rows, void *dev_rows, size_t row_bytes,
+                               const int32_t *host_first, int32_t *dev_first, const int32_t *dev_drafted,
+                               int32_t *host_drafted, int drafted, bd_stream_t stream) {
+    if (!graph_exec || (row_bytes && (!host_rows || !dev_rows)) || (host_first && !dev_first) || drafted < 0 ||
+        (drafted && (!dev_drafted || !host_drafted)))
+        return BD_ERR_INVALID;
+    if (row_bytes && cudaMemcpyAsync(dev_rows, host_rows, row_bytes, cudaMemcpyHostToDevice, stream) != cudaSuccess)
+        return BD_ERR_LAUNCH;
+    if (host_first &&
+        cudaMemcpyAsync(dev_first, host_first, sizeof(int32_t), cudaMemcpyHostToDevice, stream) != cudaSuccess)
+        return BD_ERR_LAUNCH;
+    if (cudaGraphLaunch(static_cast<cudaGraphExec_t>(graph_exec), stream) != cudaSuccess) return BD_ERR_LAUNCH;
+    if (drafted && cudaMemcpyAsync(host_drafted, dev_drafted, drafted * sizeof(int32_t), cudaMemcpyDeviceToHost,
+                                   stream) != cudaSuccess)
+        return BD_ERR_LAUNCH;
+    return cudaStreamSynchronize(stream) == cudaSuccess ? BD_OK : BD_ERR_LAUNCH;
+}

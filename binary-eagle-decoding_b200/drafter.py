@@ -352,14 +352,12 @@ class DraftRound:
         return self.size * 4
 
     def __call__(self, first_token: int | None = None) -> Tensor:
-        """H2D of ``host_rows`` (+ the anchor token), one round, D2H of the drafted tokens."""
+        """H2D of ``host_rows`` (+ the anchor token), one round, D2H of the drafted tokens
+        (``bd_round_submit``: the copies, the graph launch and the wait in one C call)."""
         e = self.engine
-        with torch.cuda.stream(self.stream):
-            if first_token is not None:
-                self.host_first[0] = first_token
-            self.dev_rows.copy_(self.host_rows, non_blocking=True)
-            e.ids[:1].copy_(self.host_first, non_blocking=True)
-            self.graph.replay()
-            self.host_out.copy_(e.drafted[: self.size], non_blocking=True)
-        self.stream.synchronize()
+        if first_token is not None:
+            self.host_first[0] = first_token
+        _lib.call("bd_round_submit", self.graph.raw_cuda_graph_exec(), self.host_rows.data_ptr(),
+                  self.dev_rows.data_ptr(), self.h2d_bytes - 4, self.host_first.data_ptr(), e.ids.data_ptr(),
+                  e.drafted.data_ptr(), self.host_out.data_ptr(), self.size, self.stream.cuda_stream, kernels=0)
         return self.host_out[1:]

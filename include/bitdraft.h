@@ -316,6 +316,14 @@ int bd_argmax_finish(unsigned long long *keys, int n, int32_t *out, bd_stream_t 
 int bd_ingest_taps(const void *taps_src, int in_dtype_bits, int taps, int64_t rows, int64_t hidden, void *features,
                    int out_dtype, int32_t *flags, bd_stream_t stream);
 
+/* One served draft round from host buffers: copy row_bytes of pinned host rows
+ * to dev_rows and the anchor token to dev_first, launch the captured round
+ * (a cudaGraphExec_t), copy `drafted` token ids back to pinned host memory and
+ * wait for the stream.  The host side of DraftRound.__call__ in one call. */
+int bd_round_submit(void *graph_exec, const void *host_rows, void *dev_rows, size_t row_bytes,
+                    const int32_t *host_first, int32_t *dev_first, const int32_t *dev_drafted, int32_t *host_drafted,
+                    int drafted, bd_stream_t stream);
+
 int bd_embed_rows(const uint16_t *table, int64_t vocab, int64_t hidden, const int32_t *ids, int n,
                   float *out, int32_t *flags, bd_stream_t stream);
 /* rms(x, weight, eps) rows (model.py:50-51). */
