@@ -328,17 +328,29 @@ class DraftRound:
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph, stream=self.stream):
             self._body()
+        # the served round: the same work with its host copies inside the graph, the
+        # rows' host-to-device copy on the ingest's stream beside the draft's first kernels
+        self.served = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.served, stream=self.stream):
+            self._body(host=True)
         self.stream.synchronize()
         engine.check()
 
-    def _body(self) -> None:
+    def _body(self, host: bool = False) -> None:
         # the ingest step (fusion + context k|v of the new rows) runs beside the draft's
         # embedding and layer-0 q|k|v rows, which do not read the context
-        main = torch.cuda.current_stream(self.engine.device)
+        e = self.engine
+        main = torch.cuda.current_stream(e.device)
+        if host:
+            e.ids[:1].copy_(self.host_first, non_blocking=True)
         self.side.wait_stream(main)
         with torch.cuda.stream(self.side):
-            self.engine.ingest(self.dev_rows, self.anchor - self.rows)
-        self.engine.draft(self.anchor, self.size, join=lambda: main.wait_stream(self.side))
+            if host:
+                self.dev_rows.copy_(self.host_rows, non_blocking=True)
+            e.ingest(self.dev_rows, self.anchor - self.rows)
+        e.draft(self.anchor, self.size, join=lambda: main.wait_stream(self.side))
+        if host:
+            self.host_out.copy_(e.drafted[: self.size], non_blocking=True)
 
     def replay(self) -> None:
         self.graph.replay()
@@ -353,11 +365,10 @@ class DraftRound:
 
     def __call__(self, first_token: int | None = None) -> Tensor:
         """H2D of ``host_rows`` (+ the anchor token), one round, D2H of the drafted tokens
-        (``bd_round_submit``: the copies, the graph launch and the wait in one C call)."""
-        e = self.engine
+        (``bd_round_submit``: one launch of the served graph, which holds the copies,
+        and the wait, in one C call)."""
         if first_token is not None:
             self.host_first[0] = first_token
-        _lib.call("bd_round_submit", self.graph.raw_cuda_graph_exec(), self.host_rows.data_ptr(),
-                  self.dev_rows.data_ptr(), self.h2d_bytes - 4, self.host_first.data_ptr(), e.ids.data_ptr(),
-                  e.drafted.data_ptr(), self.host_out.data_ptr(), self.size, self.stream.cuda_stream, kernels=0)
+        _lib.call("bd_round_submit", self.served.raw_cuda_graph_exec(), None, None, 0, None, None, None, None, 0,
+                  self.stream.cuda_stream, kernels=0)
         return self.host_out[1:]

@@ -319,7 +319,9 @@ int bd_ingest_taps(const void *taps_src, int in_dtype_bits, int taps, int64_t ro
 /* One served draft round from host buffers: copy row_bytes of pinned host rows
  * to dev_rows and the anchor token to dev_first, launch the captured round
  * (a cudaGraphExec_t), copy `drafted` token ids back to pinned host memory and
- * wait for the stream.  The host side of DraftRound.__call__ in one call. */
+ * wait for the stream.  row_bytes 0, a NULL host_first and drafted 0 skip the
+ * copies (DraftRound.__call__ launches a graph that holds its own copies, the
+ * rows' copy beside the draft's first kernels). */
 int bd_round_submit(void *graph_exec, const void *host_rows, void *dev_rows, size_t row_bytes,
                     const int32_t *host_first, int32_t *dev_first, const int32_t *dev_drafted, int32_t *host_drafted,
                     int drafted, bd_stream_t stream);
