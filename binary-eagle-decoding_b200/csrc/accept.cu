@@ -66,6 +66,63 @@ __device__ __forceinline__ void push_word(RunMax &m, __nv_bfloat162 &lo, __nv_bf
     lo = __hmin2_nan(lo, pair);
 }
 
+// Running maximum over 8-element vectors: the maximum of each vector comes from
+// three packed bf16 max operations, and only the vector that holds the running
+// maximum is remembered (its value and the index of its first element); the
+// element index inside it is resolved once at the end (resolve_vec).  Indices
+// arrive in increasing order, so a strict '>' keeps the first vector with the
+// maximum.  A vector whose maximum is +inf (never a winner) goes through the
+// exact per-element path instead; NaN maxima lose every comparison.
+struct RunVec {
+    float v = -INFINITY;
+    uint32_t base = 0xffffffffu;
+    const uint4 *at = nullptr;
+};
+
+__device__ __forceinline__ void push_vec(RunVec &m, RunMax &slow, __nv_bfloat162 &lo, __nv_bfloat162 &hi,
+                                         const uint4 &v, const uint4 *at, uint32_t base) {
+    const __nv_bfloat162 p0 = *reinterpret_cast<const __nv_bfloat162 *>(&v.x);
+    const __nv_bfloat162 p1 = *reinterpret_cast<const __nv_bfloat162 *>(&v.y);
+    const __nv_bfloat162 p2 = *reinterpret_cast<const __nv_bfloat162 *>(&v.z);
+    const __nv_bfloat162 p3 = *reinterpret_cast<const __nv_bfloat162 *>(&v.w);
+    const __nv_bfloat162 c = __hmax2(__hmax2(p0, p1), __hmax2(p2, p3));
+    const float bm = fmaxf(__low2float(c), __high2float(c));
+    if (bm > m.v) {
+        if (bm != INFINITY) {
+            m.v = bm;
+            m.base = base;
+            m.at = at;
+        } else {
+            push_word(slow, lo, hi, v.x, base);
+            push_word(slow, lo, hi, v.y, base + 2);
+            push_word(slow, lo, hi, v.z, base + 4);
+            push_word(slow, lo, hi, v.w, base + 6);
+            return;
+        }
+    }
+    hi = __hmax2_nan(hi, __hmax2_nan(__hmax2_nan(p0, p1), __hmax2_nan(p2, p3)));
+    lo = __hmin2_nan(lo, __hmin2_nan(__hmin2_nan(p0, p1), __hmin2_nan(p2, p3)));
+}
+
+// The key of a lane's best vector (its first element equal to the maximum) merged
+// with the exact path's key.
+__device__ __forceinline__ unsigned long long resolve_vec(const RunVec &m, const RunMax &slow) {
+    unsigned long long best = slow.i == 0xffffffffu ? 0ull : argmax_key(slow.v, slow.i);
+    if (m.base != 0xffffffffu) {
+        const uint4 v = *m.at;  // re-read one 16-byte vector
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        uint32_t j = 8;
+#pragma unroll
+        for (int k = 7; k >= 0; --k) {
+            const uint32_t bits = (k & 1) ? (w[k >> 1] & 0xffff0000u) : (w[k >> 1] << 16);
+            if (__uint_as_float(bits) == m.v) j = static_cast<uint32_t>(k);
+        }
+        const unsigned long long kv = argmax_key(m.v, m.base + j);
+        best = kv > best ? kv : best;
+    }
+    return best;
+}
+
 __global__ void __launch_bounds__(kArgmaxThreads) argmax_greedy_kernel(const GreedyArgs a) {
     __shared__ unsigned long long part[kArgmaxThreads / 32];
     __shared__ int last;
@@ -179,6 +236,7 @@ __global__ void __launch_bounds__(kStreamThreads) greedy_stream_kernel(const Gre
         const int64_t seg_end = min(end, (row + 1) * per_row);
         const int64_t row0 = row * per_row;
         RunMax m;
+        RunVec mv;
         if (VEC) {
             const uint4 *p = reinterpret_cast<const uint4 *>(a.logits);
             int64_t u = seg + threadIdx.x;
@@ -187,22 +245,12 @@ __global__ void __launch_bounds__(kStreamThreads) greedy_stream_kernel(const Gre
 #pragma unroll
                 for (int k = 0; k < 4; ++k) v[k] = ld_stream_u4(p + u + k * kStreamThreads);
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const uint32_t base = static_cast<uint32_t>((u + k * kStreamThreads - row0) * 8);
-                    push_word(m, lo, hi, v[k].x, base);
-                    push_word(m, lo, hi, v[k].y, base + 2);
-                    push_word(m, lo, hi, v[k].z, base + 4);
-                    push_word(m, lo, hi, v[k].w, base + 6);
-                }
+                for (int k = 0; k < 4; ++k)
+                    push_vec(mv, m, lo, hi, v[k], p + u + k * kStreamThreads,
+                             static_cast<uint32_t>((u + k * kStreamThreads - row0) * 8));
             }
-            for (; u < seg_end; u += kStreamThreads) {
-                const uint4 v = ld_stream_u4(p + u);
-                const uint32_t base = static_cast<uint32_t>((u - row0) * 8);
-                push_word(m, lo, hi, v.x, base);
-                push_word(m, lo, hi, v.y, base + 2);
-                push_word(m, lo, hi, v.z, base + 4);
-                push_word(m, lo, hi, v.w, base + 6);
-            }
+            for (; u < seg_end; u += kStreamThreads)
+                push_vec(mv, m, lo, hi, ld_stream_u4(p + u), p + u, static_cast<uint32_t>((u - row0) * 8));
         } else {
             for (int64_t u = seg + threadIdx.x; u < seg_end; u += kStreamThreads) {
                 const uint32_t w = a.logits[u];
@@ -212,7 +260,7 @@ __global__ void __launch_bounds__(kStreamThreads) greedy_stream_kernel(const Gre
                 lo = __hmin2_nan(lo, pair);
             }
         }
-        unsigned long long best = m.i == 0xffffffffu ? 0ull : argmax_key(m.v, m.i);
+        unsigned long long best = resolve_vec(mv, m);
         best = warp_max_u64(best);
         __syncthreads();  // the previous piece's reduction has read part[]
         if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = best;
