@@ -21,7 +21,7 @@ import torch.distributed as dist
 from torch import Tensor, nn
 
 from . import _lib, ops
-from .model import HE4, Projection, _bump, _need_cuda, _stream
+from .model import HE4, Projection, _bump, _need_cuda, _stream, frozen_linear
 
 PARAMETER_GROUPS = ("sign", "scale", "midpoint", "gain", "clip", "norm")
 HEAD_ROWS = 128
@@ -276,7 +276,7 @@ def group_loss(model: HE4, features: Tensor, tokens: tuple[int, ...], windows: t
     total = torch.zeros((), device=device)
     for start in range(0, labels.numel(), HEAD_ROWS):
         end = start + HEAD_ROWS
-        logits = torch.nn.functional.linear(head[start:end], model.vocabulary)
+        logits = frozen_linear(head[start:end], model.vocabulary, model)
         losses = torch.nn.functional.cross_entropy(logits, labels[start:end], reduction="none")
         loss = (losses * weights[start:end]).sum()
         torch.autograd.backward(loss)

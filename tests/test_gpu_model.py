@@ -125,6 +125,12 @@ def tiny_model(bd, window):
     return f, model
 
 
+# The frozen projections (q, k, v, o, fc, the tied head) run on bf16 tensor cores
+# with split operands (hi + lo, fp32 accumulation): within ~1e-5 of the
+# reference's fp32 products, hence the absolute tolerance on the O(1) logits.
+LOGITS_ATOL = 3e-5
+
+
 @pytest.mark.parametrize("window", [4096, 5])
 def test_he4_forward_matches_reference_logits(bd, window):
     f, model = tiny_model(bd, window)
@@ -133,12 +139,14 @@ def test_he4_forward_matches_reference_logits(bd, window):
     with torch.no_grad():
         for anchor in (2, 7, 19):
             logits = model.forward(features, tokens, anchor)
-            np.testing.assert_allclose(logits.cpu().numpy(), f[f"w{window}_logits_{anchor}"], rtol=1e-4, atol=1e-5)
+            np.testing.assert_allclose(logits.cpu().numpy(), f[f"w{window}_logits_{anchor}"], rtol=1e-4,
+                                       atol=LOGITS_ATOL)
         logits = model.forward(features, tokens, 7, 3)
-        np.testing.assert_allclose(logits.cpu().numpy(), f[f"w{window}_logits_7_s3"], rtol=1e-4, atol=1e-5)
+        np.testing.assert_allclose(logits.cpu().numpy(), f[f"w{window}_logits_7_s3"], rtol=1e-4,
+                                   atol=LOGITS_ATOL)
     # with gradients enabled the projections take the training path: same logits
     logits = model.forward(features, tokens, 7)
-    np.testing.assert_allclose(logits.detach().cpu().numpy(), f[f"w{window}_logits_7"], rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(logits.detach().cpu().numpy(), f[f"w{window}_logits_7"], rtol=1e-4, atol=LOGITS_ATOL)
 
 
 def test_group_hidden_matches_single_windows(bd):
