@@ -97,8 +97,13 @@ def peaks() -> tuple[float, str]:
 # --------------------------------------------------------------------------- CPU (oracle) arm
 
 
-def cpu_round_rate(tensors, vocabulary, features, tokens, steps: int, budget_s: float = 30.0):
-    """The CPU restatement of the same draft round (cached context), drafted tokens/s."""
+def cpu_round_rate(tensors, vocabulary, features, tokens, steps: int, budget_s: float = 30.0, warmup: int = 0):
+    """The CPU restatement of the same draft round (cached context), drafted tokens/s.
+
+    ``warmup`` untimed rounds run first, on the same set-up; then up to ``steps``
+    timed rounds, stopping once ``budget_s`` seconds of rounds have been timed.
+    Returns (rate, median seconds per round, timed rounds).
+    """
     from oracle import drafter as od
 
     cfg = od.Geometry(**GEOMETRY)
@@ -119,9 +124,7 @@ def cpu_round_rate(tensors, vocabulary, features, tokens, steps: int, budget_s: 
     # context K/V of positions [0, anchor - INGEST): set-up, not timed
     enc = od.encode_context(t, feats, anchor - INGEST, cfg)
     contexts = [od.layer_context(t, i, enc, np.arange(anchor - INGEST), cfg) for i in range(cfg.layers)]
-    times = []
-    for _ in range(max(1, steps)):
-        start = time.perf_counter()
+    def round_once():
         # ingest INGEST rows: fusion + per-layer context K/V of the new rows
         new = od.encode_context(t, feats[anchor - INGEST:anchor], INGEST, cfg)
         full = []
@@ -129,7 +132,14 @@ def cpu_round_rate(tensors, vocabulary, features, tokens, steps: int, budget_s: 
             k, v = od.layer_context(t, i, new, np.arange(anchor - INGEST, anchor), cfg)
             full.append((np.concatenate((contexts[i][0], k)), np.concatenate((contexts[i][1], v))))
         logits = od.he4_forward(t, vocab, VOCAB - 1, feats, tok, anchor, cfg, contexts=full)
-        np.argmax(logits[1:], -1)
+        return np.argmax(logits[1:], -1)
+
+    for _ in range(warmup):
+        round_once()
+    times = []
+    for _ in range(max(1, steps)):
+        start = time.perf_counter()
+        round_once()
         times.append(time.perf_counter() - start)
         if sum(times) > budget_s:
             break
@@ -142,13 +152,14 @@ def reference_arm(args, rank: int, world: int) -> None:
         return
     torch.set_num_threads(os.cpu_count() or 1)
     tensors, vocabulary, features, tokens = make_tensors()
+    # a bounded sample: at most 3 timed rounds (~3 s each on 16 cores) after 3 untimed ones
     steps = max(1, min(args.steps, 3))
-    cpu_round_rate(tensors, vocabulary, features, tokens, 1, budget_s=10.0)  # warm-up (one step)
-    rate, per_step, n = cpu_round_rate(tensors, vocabulary, features, tokens, steps)
+    warmup = 3
+    rate, per_step, n = cpu_round_rate(tensors, vocabulary, features, tokens, steps, warmup=warmup)
     cores = os.cpu_count() or 1
     line = {
         "impl": "reference", "metric": METRIC, "value": rate, "unit": UNIT, "n_gpus": world, "steps": n,
-        "warmup": 1, "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "weak",
+        "warmup": warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (random-init weights, N(0,1) features)",
         "config": workload_config(),
         "cpu_baseline": {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
