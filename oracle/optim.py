@@ -9,7 +9,11 @@ Test infrastructure only (see ``oracle/__init__.py``).
     ``weight_decay=0`` in the single-tensor order used by the reference's
     golden test (``tests/numerical/test_model.py:544-553``) and the fused
     update of ``w1a1_eagle/numerical/worker.py:365-392``;
-  * :func:`bound_latents` / :func:`clamp_latents` restate ``model.py:153-169``.
+  * :func:`bound_latents` / :func:`clamp_latents` restate ``model.py:153-169``;
+  * :func:`label_weights` and :func:`group_loss` restate the weighted
+    cross-entropy of the drafted positions,
+    ``w1a1_eagle/numerical/worker.py:41-50, 315-363`` (its value; the gradients
+    are pinned by the reference's own fixture).
 """
 
 from __future__ import annotations
@@ -115,3 +119,48 @@ def bound_latents(latent, multiple: float):
 
 def clamp_latents(latent):
     return np.clip(np.asarray(latent, dtype=np.float32), F32(-1.0), F32(1.0))
+
+
+def label_weights(lengths, positions=None) -> np.ndarray:
+    """``label_weights`` (``worker.py:41-50``): per window ``exp(-i / 7)`` for its
+    ``i``-th label (or the given per-position weights), each window normalised to
+    sum ``1 / len(lengths)``; fp32 as in torch."""
+    parts = []
+    for length in lengths:
+        if positions is None:
+            weights = np.exp(-np.arange(length).astype(F32) / F32(7)).astype(F32)
+        else:
+            weights = np.asarray(positions[:length], dtype=F32)
+        parts.append((weights / weights.sum(dtype=F32) / F32(len(lengths))).astype(F32))
+    return np.concatenate(parts)
+
+
+def group_loss(tensors, vocabulary, mask, features, tokens, windows, cfg, slots=None, positions=None) -> float:
+    """Value of ``TensorWorker.group_loss`` (``worker.py:315-363``).
+
+    ``windows`` is a sequence of ``(anchor, labels)``.  Each window drafts a
+    block of ``size`` slots (``HE4.block``, ``model.py:323-327``); its label rows
+    are slots ``1 .. min(len(labels), size - 1)`` of that block, whose logits
+    equal ``HE4.forward`` at the window's anchor (``group_hidden`` masks each
+    window to its own context, ``model.py:329-367``).  The loss is the
+    label-weighted sum of the rows' cross-entropies, accumulated here in fp64.
+    """
+    from .drafter import he4_forward
+
+    size = cfg.slots if slots is None else slots
+    if not windows or any(not labels for _, labels in windows):
+        raise ValueError("an update requires supervised windows")
+    if not 2 <= size <= cfg.slots:
+        raise ValueError("an update requires at least one drafted position")
+    lengths = tuple(min(len(labels), size - 1) for _, labels in windows)
+    weights = label_weights(lengths, positions).astype(np.float64)
+    total, row = 0.0, 0
+    for (anchor, labels), length in zip(windows, lengths):
+        logits = he4_forward(tensors, vocabulary, mask, features, tokens, anchor, cfg, slots=size)
+        rows = logits[1:1 + length].astype(np.float64)
+        peak = rows.max(-1, keepdims=True)
+        lse = peak[:, 0] + np.log(np.exp(rows - peak).sum(-1))
+        picked = rows[np.arange(length), np.asarray(labels[:length])]
+        total += float((weights[row:row + length] * (lse - picked)).sum())
+        row += length
+    return total

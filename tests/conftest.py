@@ -32,3 +32,17 @@ def submodule(name: str):
 @pytest.fixture(scope="session")
 def bd():
     return package()
+
+
+def group_loss_case(fixture, case: str):
+    """``(windows, slots, positions)`` of one case of ``golden/group_loss.npz``:
+    ``windows`` as ``(anchor, labels)`` pairs, ``slots`` None for the model's
+    default block, ``positions`` the per-position label weights or None."""
+    labels = fixture[f"{case}_labels"].tolist()
+    windows, at = [], 0
+    for anchor, length in zip(fixture[f"{case}_anchors"].tolist(), fixture[f"{case}_lengths"].tolist()):
+        windows.append((anchor, tuple(labels[at:at + length])))
+        at += length
+    slots = int(fixture[f"{case}_slots"])
+    positions = tuple(fixture[f"{case}_positions"].tolist()) if f"{case}_positions" in fixture.files else None
+    return tuple(windows), (None if slots < 0 else slots), positions

@@ -379,6 +379,59 @@ def bound_fixture() -> None:
     np.savez(HERE / "bound.npz", value=f32(value), bounded=f32(projection.latent_sign), kat=f32(kat.latent_sign))
 
 
+def group_loss_fixture() -> None:
+    """The reference's own ``TensorWorker.group_loss`` (``worker.py:315-363``) on the tiny HE4
+    (window 4096, the quantizer perturbation of ``tiny_he4_fixture``): the weighted loss
+    and every parameter gradient, for exponential label weights (one head chunk) and
+    per-position ("reach") weights over 132 label rows (two 128-row head chunks)."""
+    from types import SimpleNamespace
+
+    from w1a1_eagle.numerical.worker import TensorWorker
+
+    f = np.load(HERE / "tiny_he4.npz")
+    cfg = Geometry(hidden=4, intermediate=8, heads=2, kv_heads=1, head_dim=2, window=4096)
+    tensors = {k[2:]: torch.from_numpy(f[k]) for k in f.files if k.startswith("t_")}
+    model = HE4(tensors, torch.from_numpy(f["vocabulary"]), 19, cfg)
+    perturb = torch.Generator().manual_seed(23)  # the draw order of tiny_he4_fixture
+    with torch.no_grad():
+        for block in model.blocks:
+            block.gate.log_gain.copy_(0.3 * torch.randn(4, generator=perturb))
+            block.gate.log_clip.fill_(float(0.3 * torch.randn((), generator=perturb)))
+            block.down.log_gain.copy_(0.3 * torch.randn(8, generator=perturb))
+            block.down.log_clip.fill_(float(0.3 * torch.randn((), generator=perturb)))
+            for p in (block.gate, block.up, block.down):
+                p.midpoint.copy_(0.05 * torch.randn(p.midpoint.shape, generator=perturb))
+    capture = SimpleNamespace(features=torch.from_numpy(f["features"]), tokens=tuple(range(20)))
+    g = torch.Generator().manual_seed(47)
+    reach_windows = []
+    for index, anchor in enumerate(range(1, 20, 2)):
+        count = 6 if index in (3, 7) else 15
+        reach_windows.append((anchor, tuple(int(v) for v in torch.randint(0, 20, (count,), generator=g))))
+    reach = tuple(float(v) for v in (0.95 ** torch.arange(15, dtype=torch.float64)))
+    cases = {
+        "exp": (((3, (4, 5, 6)), (10, (11, 12, 13, 14, 15))), 6, "uniform", None),
+        "reach": (tuple(reach_windows), None, "reach", reach),
+    }
+    arrays = {}
+    for tag, (windows, slots, kind, positions) in cases.items():
+        worker = SimpleNamespace(model=model, blocks=SimpleNamespace(position_weights=kind),
+                                 position_weights=positions)
+        supervision = tuple(SimpleNamespace(anchor=a, labels=labels) for a, labels in windows)
+        model.zero_grad(set_to_none=True)
+        loss = TensorWorker.group_loss(worker, capture, supervision, slots)
+        arrays[f"{tag}_loss"] = f32(loss)
+        arrays[f"{tag}_anchors"] = np.array([a for a, _ in windows], np.int64)
+        arrays[f"{tag}_labels"] = np.array([l for _, labels in windows for l in labels], np.int64)
+        arrays[f"{tag}_lengths"] = np.array([len(labels) for _, labels in windows], np.int64)
+        arrays[f"{tag}_slots"] = np.int64(slots if slots is not None else -1)
+        if positions is not None:
+            arrays[f"{tag}_positions"] = np.array(positions, np.float64)
+        for name, parameter in model.named_parameters():
+            if parameter.grad is not None:
+                arrays[f"{tag}_grad_{name}"] = f32(parameter.grad)
+    np.savez(HERE / "group_loss.npz", **arrays)
+
+
 def main() -> None:
     signs_fixture()
     packing_fixture()
@@ -392,6 +445,7 @@ def main() -> None:
     greedy_fixture()
     adamw_fixture()
     bound_fixture()
+    group_loss_fixture()
     meta = {"reference": "philippesic/binary-eagle-decoding", "torch": torch.__version__, "numpy": np.__version__,
             "generator": "tests/golden/make_golden.py", "math": {"pi": math.pi}}
     (HERE / "meta.json").write_text(json.dumps(meta, indent=1))

@@ -8,7 +8,7 @@ import struct
 import numpy as np
 import pytest
 
-from conftest import GOLDEN
+from conftest import GOLDEN, group_loss_case
 from oracle import acceptance, core, drafter, optim
 
 
@@ -177,6 +177,27 @@ def test_tiny_he4_forward_against_reference(window):
         np.testing.assert_allclose(logits, f[f"w{window}_logits_{anchor}"], rtol=1e-4, atol=1e-5)
     logits = drafter.he4_forward(tensors, f["vocabulary"], 19, f["features"], tokens, 7, cfg, slots=3)
     np.testing.assert_allclose(logits, f[f"w{window}_logits_7_s3"], rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("case", ["exp", "reach"])
+def test_group_loss_against_reference(case):
+    # the reference's own TensorWorker.group_loss on the tiny HE4 (worker.py:315-363)
+    f, g = load("tiny_he4.npz"), load("group_loss.npz")
+    cfg = drafter.Geometry(hidden=4, intermediate=8, heads=2, kv_heads=1, head_dim=2, window=4096)
+    windows, slots, positions = group_loss_case(g, case)
+    loss = optim.group_loss(tiny_tensors(f, 4096), f["vocabulary"], 19, f["features"], tuple(range(20)), windows,
+                            cfg, slots, positions)
+    assert loss == pytest.approx(float(g[f"{case}_loss"]), rel=1e-5)
+
+
+def test_label_weights_rule():
+    # worker.py:41-50: exp(-i/7) per window (or the given weights), each window summing to 1/len
+    w = optim.label_weights((3, 1, 2))
+    assert w.dtype == np.float32 and w.shape == (6,)
+    np.testing.assert_allclose([w[:3].sum(), w[3:4].sum(), w[4:].sum()], [1 / 3] * 3, rtol=1e-6)
+    np.testing.assert_allclose(w[1] / w[0], np.exp(-1 / 7), rtol=1e-6)
+    p = optim.label_weights((2, 3), positions=(4.0, 2.0, 1.0))
+    np.testing.assert_allclose(p, [2 / 6, 1 / 6, 4 / 14, 2 / 14, 1 / 14], rtol=1e-6)
 
 
 def test_cache_layer_golden():
