@@ -7,7 +7,7 @@ import subprocess
 
 import pytest
 
-from conftest import submodule
+from conftest import ROOT, submodule
 
 
 def test_library_exports_every_header_symbol():
@@ -19,6 +19,16 @@ def test_library_exports_every_header_symbol():
     assert not missing, missing
     # every declared symbol has a Python signature and vice versa
     assert set(names) == set(lib.SIGNATURES), set(names) ^ set(lib.SIGNATURES)
+
+
+def test_integration_table_names_every_entry_point():
+    # each declared entry point has a row in the integration guide's table of
+    # the reference interfaces they replace
+    lib = submodule("_lib")
+    text = (ROOT / "INTEGRATION.md").read_text()
+    table = "\n".join(line for line in text.splitlines() if line.startswith("| `bd_"))
+    missing = [n for n in lib.header_symbols() if f"`{n}`" not in table]
+    assert not missing, missing
 
 
 def test_library_is_sm100a_and_pure_c_abi():
