@@ -94,6 +94,14 @@ def peaks() -> tuple[float, str]:
         return 6650.0, "fallback"
 
 
+def bf16_peak() -> tuple[float, str]:
+    """Dense bf16 burst TFLOP/s (cuBLAS), for a GEMM timed alone."""
+    try:
+        return float(json.loads(PEAKS.read_text())["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
 # --------------------------------------------------------------------------- CPU (oracle) arm
 
 
@@ -529,9 +537,13 @@ def workload_fusion(args, pkg, device) -> list[dict]:
     us = _graph_us(lambda i: ops.gemm_bf16(a, b, out), 4, reps)
     lib_us = _graph_us(lambda i: torch.mm(a, b.t(), out_dtype=torch.float32), 4, reps)
     flops = 2 * m * n * k
+    achieved = flops / (us * 1e-6) / 1e12
+    peak, peak_kind = bf16_peak()
     return [{"workload": "context fusion GEMM of a 4096-row prefill, 4096 x 2560 x 10240 bf16 -> fp32",
-             "metric": "TFLOP/s", "value": flops / (us * 1e-6) / 1e12, "unit": "TFLOP/s", "us_per_gemm": us,
-             "cublas_tflops_same_shape": flops / (lib_us * 1e-6) / 1e12}]
+             "metric": "TFLOP/s", "value": achieved, "unit": "TFLOP/s", "us_per_gemm": us,
+             "cublas_tflops_same_shape": flops / (lib_us * 1e-6) / 1e12,
+             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                          "frac": achieved / peak, "peak_source": f"{peak_kind} bf16 burst GEMM throughput"}}]
 
 
 def workload_ste(args, pkg, device) -> list[dict]:
