@@ -192,7 +192,12 @@ class _FrozenLinearFn(torch.autograd.Function):
 
 def frozen_linear(value: Tensor, operand: Tensor, owner) -> Tensor:
     """``functional.linear(value, operand)`` for a frozen operand held by ``owner``
-    (its bf16 halves are cached on the owner, outside its parameters and buffers)."""
+    (its bf16 halves are cached on the owner, outside its parameters and buffers).
+
+    CUDA tensors take the split-bf16 tensor-core GEMMs.  CPU tensors (host-side
+    checks of the loss head's bookkeeping; no kernel of this package runs on
+    them, and the binary projections refuse them) get the reference's own fp32
+    ``linear``, since torch has no bf16 -> fp32 ``mm`` on the CPU."""
     if not value.is_cuda:
         return functional.linear(value, operand)
     return _FrozenLinearFn.apply(value, operand, _frozen_halves(owner, operand))
