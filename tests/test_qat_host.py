@@ -114,3 +114,78 @@ def test_average_gradients_without_process_group_is_a_no_op(qat):
     p.grad = torch.ones(3)
     qat.average_gradients([p])
     assert torch.equal(p.grad, torch.ones(3))
+
+
+class _TableDrafter(nn.Module):
+    """A stand-in for ``HE4`` exposing what the loss head uses: ``block``,
+    ``group_hidden`` (here a trainable table of hidden states per anchor) and the
+    frozen ``vocabulary``.  On CPU tensors the head is the reference's fp32 linear."""
+
+    def __init__(self, anchors: int, slots: int, hidden: int, vocab: int, seed: int = 5) -> None:
+        super().__init__()
+        g = torch.Generator().manual_seed(seed)
+        self.slots = slots
+        self.table = nn.Parameter(torch.randn(anchors, slots, hidden, generator=g))
+        self.register_buffer("vocabulary", torch.randn(vocab, hidden, generator=g))
+
+    def block(self, slots):
+        size = self.slots if slots is None else slots
+        if type(size) is not int or not 1 <= size <= self.slots:
+            raise ValueError("block size must be between one slot and the model's slots")
+        return size
+
+    def group_hidden(self, features, tokens, anchors, size):
+        return self.table[list(anchors), :size]
+
+
+def _closed_form_loss(model, windows, size, positions, scale):
+    """Weighted cross-entropy of the label rows and its gradient w.r.t. the table, in fp64
+    (``worker.py:41-50, 315-363``)."""
+    table = model.table.detach().double()
+    vocab = model.vocabulary.double()
+    grad = torch.zeros_like(table)
+    lengths = [min(len(labels), size - 1) for _, labels in windows]
+    total = 0.0
+    for (anchor, labels), length in zip(windows, lengths):
+        if positions is None:
+            w = torch.exp(-torch.arange(length, dtype=torch.float64) / 7)
+        else:
+            w = torch.tensor(positions[:length], dtype=torch.float64)
+        w = w / w.sum() / len(windows) * scale
+        for offset in range(length):
+            row = table[anchor, 1 + offset]
+            logits = vocab @ row
+            p = torch.softmax(logits, 0)
+            total += float(w[offset] * (torch.logsumexp(logits, 0) - logits[labels[offset]]))
+            p[labels[offset]] -= 1
+            grad[anchor, 1 + offset] += w[offset] * (vocab.t() @ p)
+    return total, grad
+
+
+@pytest.mark.parametrize("slots,positions,scale", [(6, None, 1.0), (None, tuple(0.9 ** i for i in range(15)), 0.5)])
+def test_group_loss_bookkeeping_matches_closed_form(qat, slots, positions, scale):
+    # 12 windows x up to 15 label rows: 150+ rows cross the 128-row head chunks
+    model = _TableDrafter(anchors=24, slots=16, hidden=8, vocab=37)
+    g = torch.Generator().manual_seed(11)
+    windows = tuple((2 * i, tuple(int(v) for v in torch.randint(0, 37, (15 if i % 4 else 3,), generator=g)))
+                    for i in range(12))
+    size = model.block(slots)
+    loss = qat.group_loss(model, torch.zeros(1), (), tuple(qat.Window(a, l) for a, l in windows), slots, positions,
+                          scale)
+    want, want_grad = _closed_form_loss(model, windows, size, positions, scale)
+    assert float(loss) == pytest.approx(want, rel=1e-5)
+    torch.testing.assert_close(model.table.grad.double(), want_grad, rtol=1e-4, atol=1e-6)
+
+
+def test_group_loss_rejects_what_the_reference_rejects(qat):
+    model = _TableDrafter(anchors=4, slots=16, hidden=4, vocab=7)
+    with pytest.raises(ValueError, match="an update requires supervised windows"):
+        qat.group_loss(model, torch.zeros(1), (), ())
+    with pytest.raises(ValueError, match="an update requires supervised windows"):
+        qat.group_loss(model, torch.zeros(1), (), (qat.Window(1, ()),))
+    with pytest.raises(ValueError, match="an update requires at least one drafted position"):
+        qat.group_loss(model, torch.zeros(1), (), (qat.Window(1, (2,)),), slots=1)
+    with torch.no_grad():
+        model.vocabulary[3] = float("inf")
+    with pytest.raises(ValueError, match="nonfinite loss"):
+        qat.group_loss(model, torch.zeros(1), (), (qat.Window(1, (2, 3)),), slots=4)
