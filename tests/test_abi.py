@@ -49,6 +49,18 @@ def test_host_only_entry_points():
     # host-side validation happens before any device work
     assert lib.bd_pack_signs(None, -1, 4, None, None, None) == 1
     assert lib.bd_quantize_codes(None, 1, 8, 8, None, None, 5, None, None, None, None) == 1
+    # the serving submit rejects missing buffers before any CUDA call
+    assert lib.bd_round_submit(None, None, None, 0, None, None, None, None, 0, None) == 1
+    assert lib.bd_round_submit(8, None, None, 16, None, None, None, None, 0, None) == 1
+    assert lib.bd_round_submit(8, None, None, 0, None, None, None, None, -1, None) == 1
+    # the allocation-free greedy entry: nothing to do, missing pointers, and sizes beyond
+    # its fixed scratch (256 requests, 33 positions) refused before any CUDA call; the
+    # stand-in address is never dereferenced
+    assert lib.bd_accept_greedy_noalloc(None, 0, 4, 100, None, None, 0, None, None, None, None, None) == 0
+    assert lib.bd_accept_greedy_noalloc(None, 1, 4, 100, None, None, 0, None, None, None, None, None) == 1
+    addr = 256
+    assert lib.bd_accept_greedy_noalloc(addr, 257, 4, 100, addr, None, 0, addr, addr, None, None, None) == 6
+    assert lib.bd_accept_greedy_noalloc(addr, 1, 33, 100, addr, None, 0, addr, addr, None, None, None) == 6
 
 
 def test_missing_library_fails_loudly(monkeypatch, tmp_path):
