@@ -4,7 +4,7 @@ Run in a checkout that has the reference (philippesic/binary-eagle-decoding)
 available read-only; it imports ``w1a1_eagle`` and ``benchmarks`` from there
 and writes small ``.npz``/``.json`` fixtures next to this script:
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py /path/to/reference
 
 The fixtures pin the CPU oracle (``oracle/``) to the reference's own outputs
 on seeded inputs; the GPU parity tests then compare the CUDA path with the
@@ -23,7 +23,9 @@ import torch
 from torch import nn
 
 HERE = Path(__file__).resolve().parent
-REFERENCE = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+if len(sys.argv) != 2:
+    raise SystemExit("usage: python tests/golden/make_golden.py /path/to/reference-checkout")
+REFERENCE = Path(sys.argv[1])
 sys.path.insert(0, str(REFERENCE))
 
 from benchmarks.acceptance import reduce_rounds  # noqa: E402
@@ -183,6 +185,45 @@ def w1_fixture() -> None:
     with torch.no_grad():
         y = project(torch.nn.functional.silu(project(x, wg)) * project(x, wu), wd)
     np.savez(HERE / "w1_ffn.npz", x=f32(x), w_gate=f32(wg), w_up=f32(wu), w_down=f32(wd), y=f32(y))
+
+
+def w1a1_fixture() -> None:
+    """W1A1 SwiGLU from the reference's parts: ``hard_sign`` for weights and
+    activations (x >= 0 -> +1, -0.0 -> +1), ``packed_signs`` for the bit words,
+    torch ``linear`` of the +-1 operands for the dots, the ``Projection.scale``
+    initialiser ``mean|W|`` per row and a per-token ``mean|x|`` scale; the
+    intermediate ``silu(gate) * up`` is re-binarised before the down projection."""
+    g = torch.Generator().manual_seed(12)
+    tokens, hidden, inner = 5, 96, 160
+    x = torch.randn(tokens, hidden, generator=g)
+    x[0, 0] = -0.0
+    x[1, 5] = 0.0
+    wg = torch.randn(inner, hidden, generator=g) * 0.02
+    wu = torch.randn(inner, hidden, generator=g) * 0.02
+    wd = torch.randn(hidden, inner, generator=g) * 0.02
+    wg[0, 0] = -0.0
+    arrays = {"x": f32(x), "w_gate": f32(wg), "w_up": f32(wu), "w_down": f32(wd)}
+
+    def project(v, w, tag):
+        with torch.no_grad():
+            signs_v, signs_w = hard_sign(v), hard_sign(w)
+            dot = torch.nn.functional.linear(signs_v, signs_w)
+            mean = v.abs().mean(-1)
+            out = (dot * w.abs().mean(-1)) * mean[:, None]
+        arrays[tag + "_words_in"] = packed_signs(v)
+        arrays[tag + "_words_w"] = packed_signs(w)
+        arrays[tag + "_dot"] = dot.numpy().astype(np.int64)
+        arrays[tag + "_mean"] = f32(mean)
+        arrays[tag + "_out"] = f32(out)
+        return out
+
+    gate = project(x, wg, "gate")
+    up = project(x, wu, "up")
+    with torch.no_grad():
+        h = torch.nn.functional.silu(gate) * up
+    arrays["hidden"] = f32(h)
+    arrays["y"] = f32(project(h, wd, "down"))
+    np.savez(HERE / "w1a1_ffn.npz", **arrays)
 
 
 def tiny_he4_fixture() -> None:
@@ -438,6 +479,7 @@ def main() -> None:
     projection_fixture()
     he4_ffn_fixture()
     w1_fixture()
+    w1a1_fixture()
     tiny_he4_fixture()
     export_fixture()
     layer_fixture()

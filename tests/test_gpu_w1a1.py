@@ -7,7 +7,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import package
+from conftest import GOLDEN, package
 from oracle import core
 
 pytestmark = pytest.mark.gpu
@@ -76,3 +76,21 @@ def test_ffn_w1a1_config3_shapes(ops, tokens):
     _, raw = ops.projection_w1a1(h, ops.tile_t16(down.to(DEV)), ffn.scale_down, raw_dot=True)
     _, want_d, _ = core.w1a1_projection(h.cpu().numpy(), down.numpy(), ffn.scale_down.cpu().numpy())
     assert np.array_equal(raw.cpu().numpy(), want_d)
+
+
+@pytest.mark.parametrize("repeat", [1, 40])
+def test_ffn_w1a1_against_reference_fixture(ops, repeat):
+    """The W1A1 block on the fixture made from the reference's hard_sign /
+    packed_signs / linear: decode rows (5 tokens) and, repeated to 200 rows, the
+    tcgen05 large-M path.  Gate and up dots are exact, so the hidden state equals
+    the fixture's to the last bit of the fixed-order mean; y within 1e-5."""
+    f = np.load(GOLDEN / "w1a1_ffn.npz")
+    x = torch.from_numpy(np.tile(f["x"], (repeat, 1)))
+    gate, up, down = (torch.from_numpy(f[k]).to(DEV) for k in ("w_gate", "w_up", "w_down"))
+    ffn = ops.pack_ffn(gate, up, down, large=repeat > 1)
+    y, h = ops.ffn_w1a1(x.to(DEV), ffn, hidden_out=True)
+    want_h, want_y = np.tile(f["hidden"], (repeat, 1)), np.tile(f["y"], (repeat, 1))
+    np.testing.assert_allclose(h.cpu().numpy(), want_h, rtol=1e-5, atol=1e-7)
+    np.testing.assert_allclose(y.cpu().numpy(), want_y, rtol=1e-5, atol=1e-7)
+    _, raw = ops.projection_w1a1(x[:5].to(DEV), ops.tile_t16(gate), ffn.scale_gate, raw_dot=True)
+    assert np.array_equal(raw.cpu().numpy(), f["gate_dot"])

@@ -144,6 +144,25 @@ def test_w1_ffn_against_reference_parts():
     np.testing.assert_allclose(y, f["y"], rtol=1e-5, atol=1e-6)
 
 
+def test_w1a1_ffn_against_reference_parts():
+    """Words, popcount dots, per-token means and outputs of the W1A1 block against
+    the fixture built from the reference's hard_sign / packed_signs / linear."""
+    f = load("w1a1_ffn.npz")
+    x = f["x"]
+    y, dots = core.w1a1_ffn(x, f["w_gate"], f["w_up"], f["w_down"])
+    for tag, v, w in (("gate", x, f["w_gate"]), ("up", x, f["w_up"]), ("down", f["hidden"], f["w_down"])):
+        assert np.array_equal(core.pack_bits_rows(v).view(np.int32), f[tag + "_words_in"]), tag
+        assert np.array_equal(core.pack_bits_rows(w).view(np.int32), f[tag + "_words_w"]), tag
+        words_dot = core.popcount_dot(core.pack_bits_rows(v), core.pack_bits_rows(w), v.shape[1])
+        assert np.array_equal(words_dot, f[tag + "_dot"]), tag
+        # torch's mean and the kernel's fixed-order mean may differ in the last bit
+        np.testing.assert_allclose(core.fixed_mean_abs(v), f[tag + "_mean"], rtol=2e-7, atol=0)
+    assert np.array_equal(dots["gate"], f["gate_dot"]) and np.array_equal(dots["up"], f["up_dot"])
+    assert np.array_equal(dots["down"], f["down_dot"])
+    np.testing.assert_allclose(dots["hidden"], f["hidden"], rtol=1e-6, atol=1e-9)
+    np.testing.assert_allclose(y, f["y"], rtol=1e-6, atol=1e-9)
+
+
 def test_w1a1_popcount_equals_pm_dot():
     rng = np.random.default_rng(3)
     for t, k, o in ((1, 1, 1), (5, 33, 7), (16, 2560, 40), (3, 97, 65)):

@@ -2,9 +2,11 @@
 
 ``bd_accept_greedy_noalloc`` serves callers that cannot allocate device memory
 (a verifier living inside a serving runtime that only lends it a stream and
-tensor pointers): its scratch is a fixed device array inside the library.  This
-file is collected last so that a run stopping at the first failure has run every
-other test first; it also passes alone in a fresh process.
+tensor pointers): its scratch is a fixed device array inside the library.  Its
+results are checked against the CPU oracle of the reference's greedy rule and
+against the workspace entry point, on calls made back to back.  This file is
+collected last so that a run stopping at the first failure has run every other
+test first; it also passes alone in a fresh process.
 """
 
 from __future__ import annotations
@@ -14,6 +16,7 @@ import pytest
 import torch
 
 from conftest import package
+from oracle import acceptance
 
 pytestmark = pytest.mark.gpu
 
@@ -69,12 +72,21 @@ def test_noalloc_greedy_matches_workspace_entry_point_twice():
         ref = with_workspace(lib, ld, dd, ed)
         got = without_allocation(lib, ld, dd, ed, targets=call == 0)
         torch.cuda.synchronize()
+        bits = logits.view(torch.int16).numpy().view(np.uint16)
+        want_acc, want_next, want_tg = acceptance.accept_greedy(acceptance.bf16_to_f32(bits), drafts.numpy(),
+                                                                eog.tolist())
+        assert np.array_equal(got[0].cpu().numpy(), want_acc), call
+        assert np.array_equal(got[1].cpu().numpy(), want_next), call
+        if got[2] is not None:
+            assert np.array_equal(got[2].cpu().numpy().reshape(B, P), want_tg)
         assert torch.equal(got[0], ref[0]) and torch.equal(got[1], ref[1]), call
         if got[2] is not None:
             assert torch.equal(got[2], ref[2])
         assert int(got[3].item()) == 0 and int(ref[3].item()) == 0
     # the same inputs again: the shared scratch keeps no state between calls
     again = without_allocation(lib, ld, dd, ed, targets=False)
+    torch.cuda.synchronize()
+    assert np.array_equal(again[0].cpu().numpy(), want_acc) and np.array_equal(again[1].cpu().numpy(), want_next)
     assert torch.equal(again[0], ref[0]) and torch.equal(again[1], ref[1])
 
 
