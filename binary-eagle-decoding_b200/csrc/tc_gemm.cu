@@ -13,8 +13,12 @@
 // warps 2-9 drain an accumulator with tcgen05.ld (warp w reads TMEM lanes
 // 32 (w % 4) .., one half of the columns) and apply the fused epilogue while the next tile accumulates in
 // the other buffer.  Every mbarrier wait is bounded; a timeout raises
-// BD_FLAG_TIMEOUT, sets a CTA-wide abort flag that ends every role's loop, and the
-// CTA still frees its TMEM before it returns.
+// BD_FLAG_TIMEOUT and sets a CTA-wide abort flag that ends every role's loop.
+// Before the CTA frees its TMEM and exits, the producer waits (bounded again)
+// for the TMA loads it already issued to land in shared memory, and the MMA
+// issuer commits its issued MMAs to a drain barrier and waits for that; if
+// either of those waits also runs out, the tile data is lost (the flag already
+// reports the failure) and the CTA exits anyway rather than hang.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -77,6 +81,18 @@ __device__ __forceinline__ bool mb_wait(uint64_t *b, uint32_t parity, volatile i
     *abort = 1;
     return false;
 }
+// Bounded wait used on the abort path only (ignores the abort flag).
+__device__ __forceinline__ void mb_drain(uint64_t *b, uint32_t parity) {
+    for (uint32_t i = 0; i < kTcSpin; ++i) {
+        uint32_t ok;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(ok)
+            : "r"(su32(b)), "r"(parity)
+            : "memory");
+        if (ok) return;
+    }
+}
 __device__ __forceinline__ void tma_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int c0, int c1) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
@@ -108,7 +124,7 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sa = smem;                                // stages x 16 KB (tokens)
     uint8_t *sb = smem + kTcStages * kTcBM * kTcBK;    // stages x BN x 128 B (weights)
-    __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], acc_full[2], acc_empty[2];
+    __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], acc_full[2], acc_empty[2], drain;
     __shared__ uint32_t tmem_base;
     __shared__ volatile int abort_flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -125,6 +141,7 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
             mb_init(&acc_full[b], 1);
             mb_init(&acc_empty[b], 8);  // one arrive per epilogue warp
         }
+        mb_init(&drain, 1);
         abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -150,6 +167,10 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
                     tma_2d(sa + s * kTcBM * kTcBK, &ma, &full[s], k * BKE, m0);
                     tma_2d(sb + s * BN * kTcBK, &mb, &full[s], k * BKE, n0);
                 }
+            }
+            if (abort_flag) {  // let the loads already issued (stages it - S .. it - 1) land
+                for (uint32_t j = it > static_cast<uint32_t>(kTcStages) ? it - kTcStages : 0; j < it; ++j)
+                    mb_drain(&full[j % kTcStages], (j / kTcStages) & 1);
             }
         }
     } else if (warp == 1) {
@@ -195,6 +216,12 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
                     "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(&acc_full[b]))
                     : "memory");
                 if (!ok) break;
+            }
+            if (abort_flag) {  // every MMA this thread issued completes before TMEM is freed
+                asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                 su32(&drain))
+                             : "memory");
+                mb_drain(&drain, 0);
             }
         }
     } else {  // epilogue warps 2..9: warp w drains TMEM lanes 32 (w % 4) .., column half (w - 2) / 4

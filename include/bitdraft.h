@@ -231,7 +231,10 @@ int bd_ffn_w1a1_large(const bd_ffn_large_args *args, bd_stream_t stream);
  * logits bf16 [requests, drafts+1, vocab] (row-major, raw uint16 bits),
  * drafts int32 [requests, drafts]; eog int32 [n_eog] (sorted or not).
  * Outputs accepted[requests], next_token[requests], targets[requests*(drafts+1)]
- * (targets may be NULL).  emitted = drafts[:accepted] + [next_token]. */
+ * (targets may be NULL).  emitted = drafts[:accepted] + [next_token].
+ * The workspace (bd_accept_workspace_bytes) must be zeroed once before its
+ * first use: the kernel needs its counters and argmax keys at zero on entry
+ * and every call leaves them zero again. */
 size_t bd_accept_workspace_bytes(int requests, int drafts);
 int bd_accept_greedy(const uint16_t *logits, int requests, int drafts, int64_t vocab,
                      const int32_t *draft_tokens, const int32_t *eog, int n_eog,
@@ -242,12 +245,16 @@ int bd_accept_greedy(const uint16_t *logits, int requests, int drafts, int64_t v
  * counterpart in the reference.  It is for callers that cannot allocate device
  * memory (e.g. a verifier embedded in a serving runtime that only hands out a
  * stream and tensor pointers and forbids cudaMalloc on its decode thread): the
- * per-request counters and the target rows live in a fixed file-scope device
- * array of the library (about 35 KB per GPU, held until the process exits).
- * Limits: requests <= 256 and drafts + 1 <= 33, else BD_ERR_TOO_LARGE.  The
- * first call on a device looks up the array's device address (make it before
- * any stream capture); every call clears the counters it uses; all calls share
- * the array, so calls that overlap on the GPU race with each other. */
+ * per-request counters, the argmax keys and the target rows live in a fixed
+ * file-scope device array of the library: 102,400 bytes (100 KiB) per GPU,
+ * laid out as counters int32 [256], argmax keys u64 [256 x 33], target rows
+ * int32 [256 x 33], held until the process exits.  Limits: requests <= 256 and
+ * drafts + 1 <= 33, else BD_ERR_TOO_LARGE.  The first call on a device looks up
+ * the array's device address and caches it (make that call before any stream
+ * capture; do not keep using the library on a device across cudaDeviceReset,
+ * which would leave the cached address stale); every call clears the counters
+ * and keys it uses; all calls share the array, so calls that overlap on the GPU
+ * race with each other. */
 int bd_accept_greedy_noalloc(const uint16_t *logits, int requests, int drafts, int64_t vocab,
                              const int32_t *draft_tokens, const int32_t *eog, int n_eog, int32_t *accepted,
                              int32_t *next_token, int32_t *targets, int32_t *flags, bd_stream_t stream);
