@@ -1,10 +1,10 @@
 #!/usr/bin/env python
 """Drafted tokens/s of the 4-layer block-16 HE4 drafter on B200.
 
-One step = one serving draft round on a resident 4096-position context:
-ingest 16 new context rows (fusion + per-layer context K/V into the fp16
-cache), then the 4-layer block forward over 4096 + 16 keys, the tied LM head
-and the per-slot argmax -> 15 drafted tokens.  Geometry of the headline
+One draft round on a resident 4096-position context: ingest 16 new context
+rows (fusion + per-layer context K/V into the fp16 cache), then the 4-layer
+block forward over 4096 + 16 keys, the tied LM head and the per-slot argmax ->
+15 drafted tokens.  One timed step = 128 consecutive rounds (--rounds-per-step).  Geometry of the headline
 workload: hidden 2560, FFN inner 9728 (one-bit SwiGLU, HE4 A4/A8 codes), 32 q /
 8 kv heads of 128, RoPE theta 1e6, window 4096, taps 4, vocabulary 151936,
 batch 1 per GPU.  Weights are random N(0, 0.02) (bf16-representable), features
@@ -37,10 +37,15 @@ import torch
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-METRIC = "drafted tokens/s/GPU (block-16 HE4 drafter)"
+METRIC = "drafted tokens/s (block-16 HE4 drafter, summed over GPUs)"
 UNIT = "drafted tokens/s"
-# DRAM bytes of one LM-head GEMV launch measured by ncu (read 778.10 MB + write 3.31 MB)
+# DRAM bytes of one LM-head GEMV launch, from one ncu capture of that launch
+# (read 778.10 MB + write 3.31 MB); a constant, not re-measured by this script
 LM_HEAD_DRAM_BYTES = 781_410_000
+# One step = this many consecutive draft rounds of the request (graph replays),
+# so that the default 20 timed steps span about a second of device time and the
+# clock sampler sees the timed region.
+ROUNDS_PER_STEP = 128
 GEOMETRY = dict(hidden=2560, intermediate=9728, heads=32, kv_heads=8, head_dim=128, layers=4, slots=16, taps=4,
                 window=4096, epsilon=1e-6, theta=1e6)
 VOCAB = 151936
@@ -155,16 +160,31 @@ def cpu_round_rate(tensors, vocabulary, features, tokens, steps: int, budget_s: 
     return (SLOTS - 1) / per_step, per_step, len(times)
 
 
+def host_threads() -> int:
+    """Use every host core for the CPU legs (torchrun sets OMP_NUM_THREADS=1 for
+    its ranks): torch's intra-op pool and numpy's BLAS pool.  Returns the BLAS
+    thread count actually in effect."""
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    try:
+        from threadpoolctl import threadpool_info, threadpool_limits
+
+        threadpool_limits(cores)
+        counts = [int(p.get("num_threads", 1)) for p in threadpool_info() if p.get("user_api") == "blas"]
+        return max(counts) if counts else 1
+    except Exception:
+        return 1
+
+
 def reference_arm(args, rank: int, world: int) -> None:
     if rank != 0:
         return
-    torch.set_num_threads(os.cpu_count() or 1)
+    cores = host_threads()
     tensors, vocabulary, features, tokens = make_tensors()
     # a bounded sample: at most 3 timed rounds (~3 s each on 16 cores) after 3 untimed ones
     steps = max(1, min(args.steps, 3))
     warmup = 3
     rate, per_step, n = cpu_round_rate(tensors, vocabulary, features, tokens, steps, warmup=warmup)
-    cores = os.cpu_count() or 1
     line = {
         "impl": "reference", "metric": METRIC, "value": rate, "unit": UNIT, "n_gpus": world, "steps": n,
         "warmup": warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "weak",
@@ -172,7 +192,8 @@ def reference_arm(args, rank: int, world: int) -> None:
         "config": workload_config(),
         "cpu_baseline": {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": f"{n} draft round(s) of the workload on the numpy restatement of HE4.forward "
-                                   "(oracle/drafter.py) with the same cached-context semantics"},
+                                   "(oracle/drafter.py) with the same cached-context semantics; a step here is "
+                                   "one round, the value is per round"},
         "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -276,8 +297,9 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
     engine.check()
 
     stream = rnd.stream
+    rounds = args.rounds_per_step
     clocks = ClockSampler(local_rank).start()
-    for _ in range(args.warmup):
+    for _ in range(args.warmup * rounds):
         rnd.replay()
     stream.synchronize()
     if dist:
@@ -288,7 +310,7 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
     wall0 = time.time()
     with torch.cuda.stream(stream):
         start.record(stream)
-        for _ in range(args.steps):
+        for _ in range(args.steps * rounds):
             rnd.replay()
         end.record(stream)
     end.synchronize()
@@ -296,13 +318,16 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
     clocks.stop()
     ms = start.elapsed_time(end)
     torch.cuda.synchronize()
+    rank_ms = [ms]
     if dist:
         t = torch.tensor([ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        gathered = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(gathered, t)
+        rank_ms = [float(v.item()) for v in gathered]
+        ms = max(rank_ms)
         dist.barrier()
     ms_per_step = ms / args.steps
-    value = world * (SLOTS - 1) * args.steps / (ms / 1e3)
+    value = world * (SLOTS - 1) * rounds * args.steps / (ms / 1e3)
 
     # launches of this library's kernels in one captured round
     lib.launches = 0
@@ -313,18 +338,21 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
     torch.cuda.synchronize()
     engine.check()
 
-    # end to end through the serving entry point: pinned H2D, round, D2H
-    e2e_times = []
-    for _ in range(max(3, args.steps)):
-        t0 = time.perf_counter()
+    # end to end through the serving entry point, every round: pinned H2D of the
+    # new rows, the round, D2H of the drafted tokens (the call returns them)
+    for _ in range(3):
         rnd()
-        e2e_times.append(time.perf_counter() - t0)
-    e2e_ms = statistics.median(e2e_times) * 1e3
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps * rounds):
+        rnd()
+    e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
     if dist:
         t = torch.tensor([e2e_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
-    e2e_value = world * (SLOTS - 1) / (e2e_ms / 1e3)
+    e2e_value = world * (SLOTS - 1) * rounds / (e2e_ms / 1e3)
 
     # roofline of the dominant kernel: the tied LM head (vocab x hidden bf16 GEMV + argmax)
     H = GEOMETRY["hidden"]
@@ -349,26 +377,38 @@ def gpu_arm(args, rank: int, world: int, local_rank: int) -> None:
         dist.destroy_process_group()
     if rank != 0:
         return
+    config = workload_config()
+    config["rounds_per_step"] = rounds
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic (random-init N(0,0.02) bf16 weights, N(0,1) bf16 features)",
-        "config": workload_config(),
+        "config": config,
+        "per_gpu_value": value / world,
+        "rank_ms_per_step": [v / args.steps for v in rank_ms],
         "roofline": {"bound": "hbm", "kernel": "gemv_kernel (tied LM head, 151936x2560 bf16, 16 tokens, fused argmax)",
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_source": f"{peak_kind} HBM copy bandwidth", "traffic": LM_HEAD_DRAM_BYTES,
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one LM-head launch "
-                                       "(profiles/gemv_lm_head.md)",
+                     "peak_source": f"{peak_kind} HBM copy bandwidth (burst; the head is timed alone)",
+                     "traffic": LM_HEAD_DRAM_BYTES,
+                     "traffic_source": "constant from one earlier ncu capture of this launch "
+                                       "(dram__bytes_read.sum + dram__bytes_write.sum), not measured in this run",
                      "algorithmic_bytes_per_launch": head_bytes, "launch_us": head_us},
-        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": rnd.h2d_bytes,
-                "d2h_bytes_per_step": rnd.d2h_bytes, "ms_per_step": e2e_ms},
-        "gpu_launches": per_round * args.steps,
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": rnd.h2d_bytes * rounds,
+                "d2h_bytes_per_step": rnd.d2h_bytes * rounds, "ms_per_step": e2e_ms,
+                "step": f"{rounds} calls of DraftRound.__call__, each: pinned host rows in, one round, drafted "
+                        "tokens out (host wall clock, max over ranks)"},
+        "gpu_launches": per_round * rounds * args.steps,
         "clocks": clocks.summary(),
     }
+    if world == 1 and not args.no_sub:
+        pkg_ = importlib.import_module("binary-eagle-decoding_b200")
+        line["ffn"] = ffn_record(pkg_, device, peak, peak_kind)
+        line["accept"] = accept_record(pkg_, device, peak, peak_kind)
+        line["w1a1"] = w1a1_record(pkg_, device)
     if world == 1 and not args.no_cpu:
-        torch.set_num_threads(os.cpu_count() or 1)
+        cores = host_threads()
         rate, per_step, n = cpu_round_rate(tensors, vocabulary, features, tokens, 2, budget_s=25.0)
-        line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": os.cpu_count() or 1, "kind": "port",
+        line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
                                 "sample": f"{n} draft round(s) of the workload on the numpy restatement "
                                           "(oracle/drafter.py), cached context"}
     print(json.dumps(line), flush=True)
@@ -427,6 +467,76 @@ def _graph_us(fn, calls: int, reps: int) -> float:
         graph.replay()
     torch.cuda.synchronize()
     return _events_us(graph.replay, reps) / calls
+
+
+def _ffn_sets(pkg, device, sets: int, seed: int = 0):
+    """`sets` independent config-1 FFN weight sets (W8 sign words + HE4 defaults)."""
+    ops = pkg.ops
+    H, F = 2560, 9728
+    g = torch.Generator(device=device).manual_seed(seed)
+    ffns = []
+    for _ in range(sets):
+        gate, up, down = (torch.randn(s, generator=g, device=device) * 0.02 for s in ((F, H), (F, H), (H, F)))
+        f = ops.pack_ffn(gate, up, down)
+        del gate, up, down
+        f.midpoint_gate, f.midpoint_up = torch.zeros(F, device=device), torch.zeros(F, device=device)
+        f.midpoint_down = torch.zeros(H, device=device)
+        f.gain_gate_up, f.gain_down = torch.ones(H, device=device), torch.ones(F, device=device)
+        f.bound_gate_up, f.bound_down = torch.ones(1, device=device), torch.ones(1, device=device)
+        ffns.append(f)
+    return ffns
+
+
+FFN_SETS = 48  # 48 x 9.34 MB of sign words = 448 MB: more than three times the 126 MB L2
+
+
+def ffn_record(pkg, device, peak: float, peak_kind: str) -> dict:
+    """Config 1 (one binary SwiGLU block, 16 tokens, 2560 -> 9728 -> 2560): pure-W1
+    (fp32 activations) and HE4 (A4/A8 codes), each timed as a CUDA graph of one
+    block per weight set over 48 sets (> 3 x L2), CUDA events on the replay stream."""
+    ops = pkg.ops
+    H, F, T = 2560, 9728, 16
+    ffns = _ffn_sets(pkg, device, FFN_SETS)
+    x = torch.randn((T, H), generator=torch.Generator(device=device).manual_seed(1), device=device)
+    flags = ops.Flags(device)
+    algorithmic = 3 * F * H // 8 + (2 * F + H) * 4 + 2 * T * H * 4
+    out = {"workload": "config 1: one binary SwiGLU block, 16 tokens, 2560 -> 9728 -> 2560, fp32 in/out",
+           "algorithmic_bytes": algorithmic,
+           "timing": f"CUDA graph of {FFN_SETS} blocks over {FFN_SETS} weight sets (448 MB > 3 x L2), CUDA events"}
+    for mode, fn in (("w1", lambda i: ops.ffn_w1(x, ffns[i % FFN_SETS], flags=flags)),
+                     ("he4", lambda i: ops.ffn_he4(x, ffns[i % FFN_SETS], flags=flags))):
+        us = _graph_us(fn, FFN_SETS, 20)
+        gbs = algorithmic / (us * 1e-6) / 1e9
+        out[mode] = {"us_per_block": us, "GB/s": gbs, "frac": gbs / peak}
+    out["peak"] = peak
+    out["peak_source"] = f"{peak_kind} HBM copy bandwidth"
+    flags.check()
+    del ffns
+    torch.cuda.empty_cache()
+    return out
+
+
+def accept_record(pkg, device, peak: float, peak_kind: str) -> dict:
+    """Config 4: greedy and rejection block acceptance, 32 requests x 16 drafts,
+    vocabulary 151936; bf16 logits of 165 MB / 321 MB (> L2) per call."""
+    lines = workload_accept(argparse.Namespace(steps=1000), pkg, device)
+    out = {"peak": peak, "peak_source": f"{peak_kind} HBM copy bandwidth"}
+    for name, line in zip(("greedy", "rejection"), lines):
+        out[name] = {"us_per_call": line["us_per_call"], "GB/s": line["value"], "frac": line["value"] / peak,
+                     "algorithmic_bytes": line["algorithmic_bytes"]}
+    torch.cuda.empty_cache()
+    return out
+
+
+def w1a1_record(pkg, device) -> dict:
+    """Config 3: the W1A1 block at M = 1024 on tcgen05 kind::i8."""
+    line = workload_w1a1(argparse.Namespace(steps=2000), pkg, device)[0]
+    peak, peak_kind = bf16_peak()
+    i8_peak = 2 * peak
+    torch.cuda.empty_cache()
+    return {"us_per_block": line["us_per_ffn"], "TOP/s": line["value"], "frac": line["value"] / i8_peak,
+            "peak": i8_peak, "peak_source": f"twice the {peak_kind} dense bf16 burst (no int8 peak is measured; "
+                                            "kind::i8 issues at twice the kind::f16 rate)"}
 
 
 def workload_ffn(args, pkg, device) -> list[dict]:
@@ -675,10 +785,13 @@ def run_workload(args, rank: int, world: int, local_rank: int) -> None:
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=2000)
-    parser.add_argument("--warmup", type=int, default=50)
+    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    parser.add_argument("--no-sub", action="store_true", help="skip the per-config sub-records (ffn, accept, w1a1)")
+    parser.add_argument("--rounds-per-step", type=int, default=ROUNDS_PER_STEP,
+                        help="consecutive draft rounds in one timed step")
     parser.add_argument("--profile-round", action="store_true",
                         help="run one draft round between cudaProfilerStart/Stop and exit")
     parser.add_argument("--workload", choices=("round", "ffn", "w1a1", "accept", "ingest", "fusion", "ste", "qat"), default="round",
