@@ -332,11 +332,14 @@ def test_full_geometry_logits_end_to_end():
     4 layers over 4096 + 16 keys, tied head) against the oracle's HE4.forward
     logits within 1e-2, and its drafted tokens equal to the oracle's argmax.
 
-    The gate/up quantizer bound is 4 (the reference's Projection takes any
-    learned clip): with the default bound 1 the 4-bit codes sit densely on
-    rounding boundaries and a relative 1e-6 perturbation already moves the
-    oracle's own logits by ~6 %; with bound 4, random relative perturbations of
-    the context keys up to 1e-5 move them by < 1e-6 (measured with the oracle)."""
+    The down projections' row scales are 0.02 mean|W| (the reference's
+    Projection learns its scales).  With the default mean|W| the randomly
+    initialised network is chaotic: in the oracle alone, relative noise of 1e-5
+    added to each layer's residual stream moves the logits by ~4 %, because
+    4-bit gate/up codes flip at rounding boundaries.  At 0.02 mean|W| the same
+    noise moves them by 0.15 % (1e-4 noise: 0.4 %), while the feed-forward
+    still carries ~19 % of the logits (measured with the oracle by zeroing the
+    down scales), so the test still checks the feed-forward path."""
     import bench
 
     drafter = submodule("drafter")
@@ -348,10 +351,11 @@ def test_full_geometry_logits_end_to_end():
         p = f"blk.{i}."
         for name in ("ffn_gate", "ffn_up", "ffn_down"):
             weight = tensors[p + name + ".weight"]
-            quant[p + name + ".scale"] = weight.abs().mean(-1)
+            scale = weight.abs().mean(-1)
+            quant[p + name + ".scale"] = scale * 0.02 if name == "ffn_down" else scale
             quant[p + name + ".midpoint"] = torch.zeros(weight.shape[0])
         quant[p + "ffn_gate_up.gain"] = torch.ones(cfg.hidden)
-        quant[p + "ffn_gate_up.bound"] = torch.tensor([4.0])
+        quant[p + "ffn_gate_up.bound"] = torch.tensor([1.0])
         quant[p + "ffn_down.gain"] = torch.ones(cfg.intermediate)
         quant[p + "ffn_down.bound"] = torch.tensor([1.0])
     engine = drafter.DraftEngine(tensors, vocabulary, bench.VOCAB - 1, model.Geometry(**bench.GEOMETRY), quant,
