@@ -7,8 +7,9 @@ projections (kernels in ``csrc/ste.cu``), an optional data-parallel gradient
 average (NCCL all-reduce of flat buckets), the global gradient-norm clip, and
 the fused AdamW + sign re-pack (``csrc/optim.cu``).
 
-``Optimization``, ``Schedule``, ``PARAMETER_GROUPS`` and ``label_weights``
-restate ``w1a1_eagle/training.py:8, 108-170`` and ``worker.py:41-50``.
+The optimizer takes the caller's ``Optimization`` (``w1a1_eagle/training.py:151-170``)
+or :class:`UpdatePolicy`; ``label_weights`` gives the label weights of
+``worker.py:41-50``.
 """
 
 from __future__ import annotations
@@ -26,76 +27,41 @@ from .model import HE4, Projection, _bump, _need_cuda, _stream, frozen_linear
 PARAMETER_GROUPS = ("sign", "scale", "midpoint", "gain", "clip", "norm")
 HEAD_ROWS = 128
 SUFFIX_GROUPS = {"latent_sign": "sign", "scale": "scale", "midpoint": "midpoint", "log_gain": "gain",
-                 "log_clip": "clip"}
+                 "log_clip": "clip", "log_window": "clip"}
+# The reference's default AdamW step size per parameter group (training.py:108-109).
+REFERENCE_STEP_SIZES = {"sign": 1e-3, "scale": 1e-5, "midpoint": 1e-5, "gain": 1e-5, "clip": 1e-5, "norm": 1e-5}
 
 
-def default_step_sizes() -> dict[str, float]:
-    """Per-group AdamW step sizes (``training.py:108-109``)."""
-    return {"sign": 1e-3, "scale": 1e-5, "midpoint": 1e-5, "gain": 1e-5, "clip": 1e-5, "norm": 1e-5}
-
-
-@dataclass(frozen=True)
-class Schedule:
-    """Step-size multiplier: linear warm-up, then constant or cosine (``training.py:113-148``)."""
-
-    decay: str = "constant"
-    warmup_updates: int = 0
-    start_update: int = 0
-    final_update: int | None = None
-
-    def __post_init__(self) -> None:
-        if self.decay not in ("constant", "cosine"):
-            raise ValueError("schedule decay must be constant or cosine")
-        if any(type(v) is not int or v < 0 for v in (self.warmup_updates, self.start_update)):
-            raise ValueError("schedule start and warm-up must be nonnegative update counts")
-        if self.decay == "constant" and self.final_update is not None:
-            raise ValueError("a constant schedule has no final update")
-        if self.decay == "cosine" and (type(self.final_update) is not int
-                                       or self.final_update <= self.start_update + self.warmup_updates):
-            raise ValueError("cosine decay requires a final update after its warm-up")
-
+class _Constant:
     def multiplier(self, updates: int) -> float:
-        if type(updates) is not int or updates < self.start_update:
-            raise ValueError("update precedes the schedule start")
-        elapsed = updates - self.start_update
-        if elapsed < self.warmup_updates:
-            return (elapsed + 1) / self.warmup_updates
-        if self.final_update is None:
-            return 1.0
-        span = self.final_update - self.start_update - self.warmup_updates
-        progress = (elapsed - self.warmup_updates) / span
-        if progress >= 1:
-            raise ValueError("update is at or beyond the schedule's final update")
-        return 0.5 * (1 + math.cos(math.pi * progress))
+        return 1.0
 
 
 @dataclass(frozen=True)
-class Optimization:
-    """Step sizes per group, schedule and the optional latent bound (``training.py:151-170``)."""
+class UpdatePolicy:
+    """What the optimizer reads from the reference's ``Optimization``
+    (``training.py:151-170``): ``step_sizes`` per group, ``schedule.multiplier(n)``
+    and ``latent_multiple``.  The caller's own ``Optimization`` object can be
+    passed to :class:`BitAdamW` instead; this default has the reference's step
+    sizes and a constant schedule."""
 
-    step_sizes: dict[str, float] = field(default_factory=default_step_sizes)
-    schedule: Schedule = Schedule()
+    step_sizes: dict[str, float] = field(default_factory=lambda: dict(REFERENCE_STEP_SIZES))
+    schedule: object = field(default_factory=_Constant)
     latent_multiple: float | None = None
-
-    def __post_init__(self) -> None:
-        if tuple(sorted(self.step_sizes)) != tuple(sorted(PARAMETER_GROUPS)) or any(
-                type(v) is not float or not math.isfinite(v) or v <= 0 for v in self.step_sizes.values()):
-            raise ValueError("positive finite step sizes required for every parameter group")
-        if self.latent_multiple is not None and (type(self.latent_multiple) is not float
-                                                 or not math.isfinite(self.latent_multiple)
-                                                 or self.latent_multiple <= 0):
-            raise ValueError("bounded latent scale requires a positive finite multiple")
 
 
 def label_weights(lengths: tuple[int, ...], positions: tuple[float, ...] | None = None) -> Tensor:
-    """Per-label weights: ``exp(-i/7)`` (or the given position weights), normalised per
-    window and divided by the window count (``worker.py:41-50``)."""
-    parts = []
-    for length in lengths:
-        w = (torch.exp(-torch.arange(length) / 7) if positions is None
-             else torch.tensor(positions[:length], dtype=torch.float32))
-        parts.append(w / w.sum() / len(lengths))
-    return torch.cat(parts)
+    """Weights of the concatenated labels of several windows (``worker.py:41-50``):
+    within a window, label ``i`` weighs ``exp(-i / 7)`` (or ``positions[i]``),
+    normalised to sum 1 over the window, and every window counts ``1 / #windows``."""
+    if not lengths or min(lengths) < 1:
+        raise ValueError("every window needs at least one label")
+    offsets = torch.cat([torch.arange(n) for n in lengths])
+    window = torch.repeat_interleave(torch.arange(len(lengths)), torch.tensor(lengths))
+    raw = (torch.exp(-offsets / 7) if positions is None
+           else torch.tensor(positions, dtype=torch.float32)[offsets])
+    totals = torch.zeros(len(lengths)).index_add_(0, window, raw)
+    return raw / totals[window] / len(lengths)
 
 
 def parameter_groups(model: nn.Module) -> dict[str, list[tuple[str, nn.Parameter]]]:
@@ -150,10 +116,11 @@ class BitAdamW:
     [-1, 1], and each latent's new signs are re-packed into its projection's W8
     cache in the same pass."""
 
-    def __init__(self, model: nn.Module, optimization: Optimization | None = None, betas=(0.9, 0.999),
-                 eps: float = 1e-8) -> None:
+    def __init__(self, model: nn.Module, optimization=None, betas=(0.9, 0.999), eps: float = 1e-8) -> None:
         self.model = model
-        self.optimization = optimization or Optimization()
+        self.optimization = optimization or UpdatePolicy()
+        if set(self.optimization.step_sizes) != set(PARAMETER_GROUPS):
+            raise ValueError("a step size for every parameter group is required")
         self.betas = betas
         self.eps = eps
         self.groups = parameter_groups(model)

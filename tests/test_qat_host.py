@@ -21,35 +21,38 @@ def qat():
     return submodule("qat")
 
 
-def test_schedule_multiplier(qat):
-    assert qat.Schedule().multiplier(0) == 1.0
-    warm = qat.Schedule(warmup_updates=4)
-    assert [warm.multiplier(u) for u in range(6)] == [0.25, 0.5, 0.75, 1.0, 1.0, 1.0]
-    cos = qat.Schedule(decay="cosine", warmup_updates=2, start_update=1, final_update=11)
-    assert cos.multiplier(1) == 0.5 and cos.multiplier(2) == 1.0
-    assert cos.multiplier(3) == pytest.approx(1.0)
-    assert cos.multiplier(7) == pytest.approx(0.5 * (1 + math.cos(math.pi * 4 / 8)))
-    with pytest.raises(ValueError, match="update precedes the schedule start"):
-        cos.multiplier(0)
-    with pytest.raises(ValueError, match="at or beyond the schedule's final update"):
-        cos.multiplier(11)
-    with pytest.raises(ValueError, match="constant or cosine"):
-        qat.Schedule(decay="linear")
-    with pytest.raises(ValueError, match="a constant schedule has no final update"):
-        qat.Schedule(final_update=3)
-    with pytest.raises(ValueError, match="cosine decay requires a final update"):
-        qat.Schedule(decay="cosine", warmup_updates=3, final_update=3)
+def test_update_policy_defaults_and_duck_typing(qat):
+    """The optimizer reads step sizes, a schedule multiplier and the latent bound
+    from the caller's Optimization object; the default has the reference's
+    step sizes (training.py:108-109) and a constant schedule."""
+    policy = qat.UpdatePolicy()
+    assert policy.step_sizes == {"sign": 1e-3, "scale": 1e-5, "midpoint": 1e-5, "gain": 1e-5, "clip": 1e-5,
+                                 "norm": 1e-5}
+    assert policy.schedule.multiplier(0) == 1.0 and policy.schedule.multiplier(12345) == 1.0
+    assert policy.latent_multiple is None
 
+    class Halving:
+        def multiplier(self, updates):
+            return 0.5 ** updates
 
-def test_optimization_validation(qat):
-    assert qat.Optimization().step_sizes == {"sign": 1e-3, "scale": 1e-5, "midpoint": 1e-5, "gain": 1e-5,
-                                             "clip": 1e-5, "norm": 1e-5}
-    with pytest.raises(ValueError, match="positive finite step sizes"):
-        qat.Optimization(step_sizes={"sign": 1e-3})
-    with pytest.raises(ValueError, match="positive finite step sizes"):
-        qat.Optimization(step_sizes={**qat.default_step_sizes(), "sign": 0.0})
-    with pytest.raises(ValueError, match="bounded latent scale requires"):
-        qat.Optimization(latent_multiple=-1.0)
+    class CallerOptimization:  # the reference's Optimization, as the optimizer sees it
+        step_sizes = {**qat.REFERENCE_STEP_SIZES, "sign": 2e-3}
+        schedule = Halving()
+        latent_multiple = None
+
+    model = nn.Module()
+    model.norm = nn.Parameter(torch.zeros(2))
+    opt = qat.BitAdamW(model, CallerOptimization())
+    opt.set_multiplier(opt.optimization.schedule.multiplier(2))
+    assert opt.lr["sign"] == pytest.approx(5e-4) and opt.lr["norm"] == pytest.approx(2.5e-6)
+
+    class Partial:
+        step_sizes = {"sign": 1e-3}
+        schedule = Halving()
+        latent_multiple = None
+
+    with pytest.raises(ValueError, match="every parameter group"):
+        qat.BitAdamW(model, Partial())
 
 
 def test_label_weights(qat):
@@ -60,6 +63,11 @@ def test_label_weights(qat):
     assert w.sum().item() == pytest.approx(1.0)
     p = qat.label_weights((2,), (1.0, 3.0, 5.0))
     torch.testing.assert_close(p, torch.tensor([0.25, 0.75]))
+    many = qat.label_weights((15, 7, 1, 15))
+    for at, n in ((0, 15), (15, 7), (22, 1), (23, 15)):
+        assert many[at:at + n].sum().item() == pytest.approx(0.25)
+    with pytest.raises(ValueError):
+        qat.label_weights((2, 0))
 
 
 def test_parameter_groups_by_suffix(qat):
