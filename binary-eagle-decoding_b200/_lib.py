@@ -88,6 +88,11 @@ SIGNATURES = {
     "bd_projection_he4": (c_int, [P, P, c_int, c_int64, c_int64, P, P, P, P, c_int, P, P, P, P, c_size_t, P]),
     "bd_ffn_workspace_bytes": (c_size_t, [c_int, c_int64, c_int64]),
     "bd_ffn_he4": (c_int, [ctypes.POINTER(FfnHe4Args), P]),
+    "bd_d8_bytes": (c_int64, [c_int64, c_int64]),
+    "bd_tile_signs_d8": (c_int, [P, c_int64, c_int64, P, P, P]),
+    "bd_ffn_fused_workspace_bytes": (c_size_t, [c_int64, c_int64]),
+    "bd_ffn_fused_shape": (c_int, [c_int64, c_int64, P]),
+    "bd_ffn_he4_fused": (c_int, [ctypes.POINTER(FfnHe4Args), P, P]),
     "bd_ffn_w1": (c_int, [ctypes.POINTER(FfnW1Args), P]),
     "bd_binarize_rows": (c_int, [P, c_int64, c_int64, P, P, P, P]),
     "bd_projection_w1a1_workspace_bytes": (c_size_t, [c_int64, c_int64]),
@@ -103,7 +108,16 @@ SIGNATURES = {
     "bd_sign_rows": (c_int, [P, c_int64, P, P, P, P]),
     "bd_he4_epilogue": (c_int, [P, c_int64, c_int64, P, P, P, c_int, P, P, P, P]),
     "bd_ste_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64]),
-    "bd_ste_grad_prep": (c_int, [P, P, c_int64, c_int64, P, P, P, c_int, P, P, P, P, P, P, P, c_size_t, P]),
+    "bd_ste_grad_prep": (c_int, [P, P, c_int64, c_int64, P, P, P, c_int, P, P, P, c_int64, P, P, c_int64, P, P, P,
+                                 P, c_size_t, P]),
+    "bd_quantize_rows_i8": (c_int, [P, c_int64, c_int64, P, P, c_int, P, c_int64, P, P, P]),
+    "bd_projection_he4_tc": (c_int, [P, c_int64, P, c_int64, c_int64, P, c_int64, P, P, P, c_int, P, P, P, P, P]),
+    "bd_sign_cols_bf16": (c_int, [P, c_int64, c_int64, P, c_int64, P, P]),
+    "bd_codes_transpose_bf16": (c_int, [P, c_int64, c_int64, c_int64, P, c_int64, P]),
+    "bd_gemm_bf16_split": (c_int, [P, P, c_int64, c_int64, c_int64, P, c_int64, c_int64, P, c_int64, P]),
+    "bd_ste_weight_grad_partials": (c_int64, [c_int64, c_int64]),
+    "bd_ste_weight_grad": (c_int, [P, P, c_int64, c_int64, c_int64, P, c_int64, P, P, ctypes.c_float, P, c_int, P, P,
+                                   P, P]),
     "bd_ste_input_backward": (c_int, [P, P, P, P, c_int64, c_int64, P, P, c_int, P, P, P, c_int, P, c_size_t,
                                       P]),
     "bd_ste_sumsq_count": (c_int, [c_int64]),
@@ -177,7 +191,7 @@ def load() -> ctypes.CDLL:
 
 
 # Kernel launches issued by each entry point (for launch accounting).
-KERNELS_PER_CALL = {"bd_ffn_he4": 3, "bd_ffn_w1": 4, "bd_attention_decode": 2, "bd_attention_decode_x16": 2,
+KERNELS_PER_CALL = {"bd_ffn_he4": 3, "bd_ffn_he4_fused": 2, "bd_ffn_w1": 4, "bd_attention_decode": 2, "bd_attention_decode_x16": 2,
                     "bd_accept_rejection": 2,
                     "bd_ste_grad_prep": 2, "bd_ste_input_backward": 2}
 launches = 0

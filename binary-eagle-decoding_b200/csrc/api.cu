@@ -114,12 +114,13 @@ static bool ffn_shapes_ok(int tokens, int64_t hidden, int64_t inter) {
     return tokens >= 1 && tokens <= kMaxTokens && hidden >= 1 && inter >= 1;
 }
 
-extern "C" int bd_ffn_he4(const bd_ffn_he4_args *p, bd_stream_t stream) {
-    if (!p || !ffn_shapes_ok(p->tokens, p->hidden, p->inter)) return BD_ERR_INVALID;
-    if (!p->x || !p->y || !p->signs_gate_up || !p->signs_down || !p->scale_gate || !p->midpoint_gate ||
-        !p->scale_up || !p->midpoint_up || !p->scale_down || !p->midpoint_down || !p->gain_gate_up ||
-        !p->bound_gate_up || !p->gain_down || !p->bound_down)
-        return BD_ERR_INVALID;
+static bool he4_args_ok(const bd_ffn_he4_args *p) {
+    return p && ffn_shapes_ok(p->tokens, p->hidden, p->inter) && p->x && p->y && p->signs_gate_up && p->scale_gate &&
+           p->midpoint_gate && p->scale_up && p->midpoint_up && p->scale_down && p->midpoint_down &&
+           p->gain_gate_up && p->bound_gate_up && p->gain_down && p->bound_down;
+}
+
+static FfnW8 he4_block(const bd_ffn_he4_args *p) {
     FfnW8 f{};
     f.tokens = p->tokens;
     f.hidden = p->hidden;
@@ -145,7 +146,17 @@ extern "C" int bd_ffn_he4(const bd_ffn_he4_args *p, bd_stream_t stream) {
     f.flags = p->flags;
     f.workspace = p->workspace;
     f.workspace_bytes = p->workspace_bytes;
-    return ffn_w8(f, EPI_HE4, stream);
+    return f;
+}
+
+extern "C" int bd_ffn_he4(const bd_ffn_he4_args *p, bd_stream_t stream) {
+    if (!he4_args_ok(p) || !p->signs_down) return BD_ERR_INVALID;
+    return ffn_w8(he4_block(p), EPI_HE4, stream);
+}
+
+extern "C" int bd_ffn_he4_fused(const bd_ffn_he4_args *p, const uint8_t *signs_down_d8, bd_stream_t stream) {
+    if (!he4_args_ok(p) || !signs_down_d8) return BD_ERR_INVALID;
+    return ffn_fused_he4(he4_block(p), signs_down_d8, stream);
 }
 
 static FfnW8 w1_block(const bd_ffn_w1_args *p, bd_stream_t stream) {

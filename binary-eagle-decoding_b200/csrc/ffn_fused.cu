@@ -1,0 +1,683 @@
+// HE4 SwiGLU block for decode sizes (tokens <= 16) in two launches:
+//   y = residual + down(silu(gate(n)) * up(n)),  n = rms(x, norm) (w1a1_eagle/model.py:220-223),
+// every projection an HE4 Projection.forward (model.py:128-150) on packed signs.
+//
+// Gate/up kernel (clusters of CA CTAs, one CTA per SM):
+//   * before griddepcontrol.wait: each CTA bulk-copies its gate/up sign slice
+//     (W8 words of its n-tile pairs, all of K) from this GPU's own memory into
+//     shared memory;
+//   * the cluster quantizes x: CTA r reads columns [r H / CA, (r + 1) H / CA),
+//     the per-token sums of squares of the rms are exchanged through
+//     distributed shared memory, and every CTA pushes its A4 codes (C16 layout)
+//     into every CTA of the cluster;
+//   * int8 m16n8k32 MMAs from shared memory (warps take (pair, 512-column
+//     group) units and meet in shared-memory integer sums); SwiGLU and the A8
+//     quantizer of the down input in the epilogue, which writes the codes to a
+//     C16 buffer in global memory and this CTA's per-token code sums.
+// Down kernel (PDL: its CTAs stream their D8 down signs into shared memory
+// while the gate/up kernel runs; clusters of CB CTAs):
+//   * a cluster owns a range of output n-tiles; its CTAs split K (the F rows)
+//     in 4-k-step groups, each reads its slice of the codes, multiplies all of
+//     the cluster's n-tiles, and the CTAs' exact integer partial dots meet
+//     through distributed shared memory; each CTA finishes a share of the
+//     n-tiles (HE4 epilogue + residual).
+// No atomics leave a CTA, nothing is left in the workspace between calls, and
+// every sum is exact or in a fixed order, so results are deterministic.  The
+// only waits are the bounded waits of each CTA for its own bulk copies
+// (BD_FLAG_TIMEOUT when one runs out) and the cluster barriers.
+#include <algorithm>
+#include <map>
+#include <mutex>
+#include <tuple>
+
+#include "kernels.cuh"
+
+namespace bd {
+
+constexpr int kFuWarps = 8;
+constexpr int kFuThreads = kFuWarps * 32;
+constexpr int kFuTokens = 16;
+constexpr int kDnNt = 12;  // output n-tiles per cluster of the down kernel, at most
+constexpr uint32_t kFuSpin = 1u << 22;
+
+struct GuArgs {
+    int tokens;
+    int64_t hidden, inter;
+    const uint32_t *gu;   // W8 gate/up words, n-tile pairs interleaved: [np][2][ng][32][4]
+    int64_t np, ng;       // n-tile pairs, W8 word groups of K
+    const float *x, *norm_w;
+    float eps;
+    const float *gain_gu, *bound_gu, *gain_dn, *bound_dn;
+    const float *scale_g, *mid_g, *scale_u, *mid_u;
+    float *hidden_out;
+    int8_t *hcodes;       // C16 codes of the down input: [inter / 32][32][16]
+    int32_t *hsum;        // [gridDim][16] per-CTA code sums of the down input
+    int32_t *flags;
+    int pairs_max;
+};
+
+struct DnArgs {
+    int tokens;
+    int64_t hidden, inter;
+    const uint8_t *dn;    // D8 down bytes: [hidden / 8][g4][32][4]
+    int64_t nt, g4;       // output n-tiles, 4-k-step groups of K
+    const int8_t *hcodes;
+    const int32_t *hsum;
+    int gu_ctas;
+    const float *bound_dn, *scale_d, *mid_d, *residual;
+    float *y;
+    int32_t *flags;
+    int groups_max;
+};
+
+// ---- cluster helpers
+__device__ __forceinline__ uint32_t fu_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void fu_cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ uint32_t fu_remote(const void *local, uint32_t rank) {
+    uint32_t out;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(out) : "r"(smem_u32(local)), "r"(rank));
+    return out;
+}
+__device__ __forceinline__ void fu_st_u32(uint32_t addr, uint32_t v) {
+    asm volatile("st.shared::cluster.u32 [%0], %1;\n" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fu_st_f32(uint32_t addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;\n" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ int fu_ld_s32(uint32_t addr) {
+    int v;
+    asm volatile("ld.shared::cluster.s32 %0, [%1];\n" : "=r"(v) : "r"(addr) : "memory");
+    return v;
+}
+// D8 nibble -> one B register of an m16n8k32 k-step: bit j -> byte j (0 or 1).
+__device__ __forceinline__ uint32_t fu_nibble(uint32_t nib) { return (nib * 0x00204081u) & 0x01010101u; }
+__device__ __forceinline__ uint32_t fu_word(const uint4 &v, int q) { return q == 0 ? v.x : q == 1 ? v.y : q == 2 ? v.z : v.w; }
+
+// ------------------------------------------------------------------ gate/up kernel
+
+// Dynamic shared memory: W8 words of this CTA's pairs, C16 codes of x, the
+// gate/up integer accumulators [pairs_max][2][4][32].
+__host__ __device__ inline uint32_t gu_xc_offset(int pairs_max, int64_t ng) {
+    return (static_cast<uint32_t>(pairs_max) * 2u * static_cast<uint32_t>(ng) * 512u + 127u) & ~127u;
+}
+__host__ __device__ inline uint32_t gu_red_offset(int pairs_max, int64_t ng) {
+    return gu_xc_offset(pairs_max, ng) + static_cast<uint32_t>(ng) * 16u * 512u;
+}
+__host__ __device__ inline uint32_t gu_smem_bytes(int pairs_max, int64_t ng) {
+    return gu_red_offset(pairs_max, ng) + static_cast<uint32_t>(pairs_max) * 2u * 4u * 32u * 4u;
+}
+
+template <int C>
+__global__ void __launch_bounds__(kFuThreads, 1) ffn_gu_kernel(const GuArgs a) {
+    extern __shared__ __align__(128) uint8_t fu_raw[];
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ float ssq[C][kFuTokens];
+    __shared__ int csx[C][kFuTokens];
+    __shared__ int cs_loc[kFuTokens], hs_loc[kFuTokens];
+    __shared__ int abort_copy;
+    uint8_t *sgu = fu_raw, *sxc = fu_raw + gu_xc_offset(a.pairs_max, a.ng);
+    int *red = reinterpret_cast<int *>(fu_raw + gu_red_offset(a.pairs_max, a.ng));
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t4 = lane & 3;
+    const int T = a.tokens;
+    const int64_t H = a.hidden, F = a.inter;
+    const uint32_t r = fu_rank();
+    const int64_t p0 = blockIdx.x * a.np / gridDim.x, p1 = (blockIdx.x + 1) * a.np / gridDim.x;
+    const int npc = static_cast<int>(p1 - p0);
+
+    // ---------------- prologue: weights only (nothing an earlier kernel writes)
+    const uint32_t gu_bytes = static_cast<uint32_t>(npc) * 2u * static_cast<uint32_t>(a.ng) * 512u;
+    if (tid == 0) {
+        mbar_init(&bar, 1);
+        mbar_init_fence();
+        abort_copy = 0;
+        mbar_expect_tx(&bar, gu_bytes);
+        if (gu_bytes) bulk_load(sgu, a.gu + p0 * 2 * a.ng * 128, gu_bytes, &bar);
+    }
+    for (int i = tid; i < npc * 2 * 4 * 32; i += kFuThreads) red[i] = 0;
+    if (tid < kFuTokens) cs_loc[tid] = hs_loc[tid] = 0;
+    // x k-steps beyond H (inside the last 512-column group) read as zero codes
+    for (int64_t i = H / 32 * 512 + tid * 16; i < a.ng * 16 * 512; i += kFuThreads * 16)
+        *reinterpret_cast<uint4 *>(sxc + i) = make_uint4(0u, 0u, 0u, 0u);
+    __syncthreads();
+    fu_cluster_sync();  // every CTA of the cluster runs before any distributed shared-memory store
+    grid_wait();
+    grid_launch_dependents();
+
+    // ---------------- x: sums of squares of this CTA's columns, shared with the cluster
+    const int64_t c0 = r * H / C, c1 = (r + 1) * H / C;
+    const int groups = static_cast<int>((c1 - c0) / 4);
+    const float b_gu = __ldg(a.bound_gu), b_dn = __ldg(a.bound_dn);
+    if ((bad_bound(b_gu) || bad_bound(b_dn)) && blockIdx.x == 0 && tid == 0) set_flag(a.flags, BD_FLAG_BAD_BOUND);
+    if (a.norm_w) {
+        for (int t = warp; t < T; t += kFuWarps) {
+            float ss = 0.0f;
+            for (int gi = lane; gi < groups; gi += 32) {
+                const float4 v = *reinterpret_cast<const float4 *>(a.x + t * H + c0 + 4 * gi);
+                ss = fmaf(v.x, v.x, ss);
+                ss = fmaf(v.y, v.y, ss);
+                ss = fmaf(v.z, v.z, ss);
+                ss = fmaf(v.w, v.w, ss);
+            }
+#pragma unroll
+            for (int d = 16; d > 0; d >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, d);
+            if (lane < C) fu_st_f32(fu_remote(&ssq[r][t], static_cast<uint32_t>(lane)), ss);
+        }
+    }
+    fu_cluster_sync();
+
+    // ---------------- x: A4 codes of this CTA's columns into every CTA's C16 buffer
+    Quant qin;
+    qin.init(b_gu, 4);
+    bool bad = false;
+    for (int e = tid; e < T * groups; e += kFuThreads) {
+        const int t = e / groups, gi = e - t * groups;
+        const int64_t k = c0 + 4 * gi;
+        float scale = 1.0f;
+        if (a.norm_w) {
+            float total = 0.0f;
+#pragma unroll
+            for (int rr = 0; rr < C; ++rr) total += ssq[rr][t];
+            scale = rsqrtf(total / static_cast<float>(H) + a.eps);
+        }
+        const float4 v = *reinterpret_cast<const float4 *>(a.x + t * H + k);
+        const float4 gn = __ldg(reinterpret_cast<const float4 *>(a.gain_gu + k));
+        float xv[4] = {v.x, v.y, v.z, v.w};
+        if (a.norm_w) {
+            const float4 w = __ldg(reinterpret_cast<const float4 *>(a.norm_w + k));
+            xv[0] = xv[0] * scale * w.x;
+            xv[1] = xv[1] * scale * w.y;
+            xv[2] = xv[2] * scale * w.z;
+            xv[3] = xv[3] * scale * w.w;
+        }
+        const float gv[4] = {gn.x, gn.y, gn.z, gn.w};
+        uint32_t packed = 0;
+        int sum = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float gained = __fmul_rn(xv[j], gv[j]);
+            bad |= !isfinite(gained);
+            const int c = qin.code(gained);
+            sum += c;
+            packed |= (static_cast<uint32_t>(c) & 0xFFu) << (8 * j);
+        }
+        if (sum) atomicAdd(&cs_loc[t], sum);
+        const uint8_t *dst = sxc + c16_offset(t, k, 1);
+#pragma unroll
+        for (int rr = 0; rr < C; ++rr) fu_st_u32(fu_remote(dst, static_cast<uint32_t>(rr)), packed);
+    }
+    if (__any_sync(0xffffffffu, bad) && lane == 0) set_flag(a.flags, BD_FLAG_NONFINITE_INPUT);
+    __syncthreads();
+    if (tid < kFuTokens) {
+#pragma unroll
+        for (int rr = 0; rr < C; ++rr)
+            fu_st_u32(fu_remote(&csx[r][tid], static_cast<uint32_t>(rr)), static_cast<uint32_t>(cs_loc[tid]));
+    }
+    fu_cluster_sync();  // no distributed shared-memory access after this point
+
+    // ---------------- gate/up: (pair, 512-column group) units over the warps
+    if (!mbar_wait_bounded(&bar, 0, kFuSpin)) abort_copy = 1;
+    __syncthreads();
+    const bool aborted = abort_copy != 0;
+    if (aborted && tid == 0) set_flag(a.flags, BD_FLAG_TIMEOUT);
+    const int units = aborted ? 0 : npc * static_cast<int>(a.ng);
+    for (int u = warp; u < units; u += kFuWarps) {
+        const int p = u / static_cast<int>(a.ng), j = u - p * static_cast<int>(a.ng);
+        const uint4 bg = *reinterpret_cast<const uint4 *>(sgu + ((static_cast<int64_t>(p * 2 + 0) * a.ng + j) * 32 + lane) * 16);
+        const uint4 bu = *reinterpret_cast<const uint4 *>(sgu + ((static_cast<int64_t>(p * 2 + 1) * a.ng + j) * 32 + lane) * 16);
+        int acc[2][4] = {};
+#pragma unroll
+        for (int s = 0; s < 16; ++s) {
+            const uint4 A = *reinterpret_cast<const uint4 *>(sxc + ((static_cast<int64_t>(j) * 16 + s) * 32 + lane) * 16);
+            const uint32_t wg = fu_word(bg, s >> 2), wu = fu_word(bu, s >> 2);
+            const int sh = 2 * (s & 3);
+            mma_s8_16832(acc[0], A.x, A.y, A.z, A.w, (wg >> sh) & 0x01010101u, (wg >> (sh + 1)) & 0x01010101u);
+            mma_s8_16832(acc[1], A.x, A.y, A.z, A.w, (wu >> sh) & 0x01010101u, (wu >> (sh + 1)) & 0x01010101u);
+        }
+#pragma unroll
+        for (int m = 0; m < 2; ++m)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) atomicAdd(&red[((p * 2 + m) * 4 + i) * 32 + lane], acc[m][i]);
+    }
+    __syncthreads();
+
+    // ---------------- epilogue: h = silu(g) * u, A8 codes of h (C16, global) and their sums
+    Quant qdn;
+    qdn.init(b_dn, 8);
+    int csin[2], lsum[2] = {0, 0};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int tok = g + 8 * h;
+        int s = 0;
+        if (tok < T)
+#pragma unroll
+            for (int rr = 0; rr < C; ++rr) s += csx[rr][tok];
+        csin[h] = s;
+    }
+    bad = false;
+    for (int p = warp; p < npc; p += kFuWarps) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int64_t o = (p0 + p) * 8 + 2 * t4 + e;
+            if (o >= F) continue;
+            const float sg = __ldg(a.scale_g + o), mg = __ldg(a.mid_g + o);
+            const float su = __ldg(a.scale_u + o), mu = __ldg(a.mid_u + o);
+            const float gd = __ldg(a.gain_dn + o);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int tok = g + 8 * h;
+                if (tok >= T) continue;
+                const int i = 2 * h + e;
+                const int Dg = 2 * red[((p * 2 + 0) * 4 + i) * 32 + lane] - csin[h];
+                const int Du = 2 * red[((p * 2 + 1) * 4 + i) * 32 + lane] - csin[h];
+                const float gv = he4_value(Dg, sg, qin.step, csin[h], mg);
+                const float uv = he4_value(Du, su, qin.step, csin[h], mu);
+                const float hv = __fmul_rn(silu(gv), uv);
+                if (a.hidden_out) a.hidden_out[tok * F + o] = hv;
+                const float gained = __fmul_rn(hv, gd);
+                bad |= !isfinite(gained);
+                const int code = qdn.code(gained);
+                lsum[h] += code;
+                a.hcodes[c16_offset(tok, o, 1)] = static_cast<int8_t>(code);
+            }
+        }
+    }
+    if (__any_sync(0xffffffffu, bad) && lane == 0) set_flag(a.flags, BD_FLAG_NONFINITE_INPUT);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        int v = lsum[h];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        if (t4 == 0 && g + 8 * h < T && v) atomicAdd(&hs_loc[g + 8 * h], v);  // shared, exact
+    }
+    __syncthreads();
+    if (tid < kFuTokens) a.hsum[blockIdx.x * kFuTokens + tid] = hs_loc[tid];
+    if (aborted && tid == 0) mbar_wait_bounded(&bar, 0, kFuSpin);  // copies still in flight land before exit
+}
+
+// ------------------------------------------------------------------ down kernel
+
+// Dynamic shared memory: D8 bytes of the cluster's n-tiles x this CTA's groups
+// [kDnNt][groups_max][32][4], the codes of this CTA's k-steps [4 groups_max][32][16],
+// the integer partial dots [kDnNt][4][32].
+__host__ __device__ inline uint32_t dn_hc_offset(int groups_max) {
+    return static_cast<uint32_t>(kDnNt) * static_cast<uint32_t>(groups_max) * 128u;
+}
+__host__ __device__ inline uint32_t dn_red_offset(int groups_max) {
+    return dn_hc_offset(groups_max) + static_cast<uint32_t>(groups_max) * 4u * 512u;
+}
+__host__ __device__ inline uint32_t dn_smem_bytes(int groups_max) {
+    return dn_red_offset(groups_max) + static_cast<uint32_t>(kDnNt) * 4u * 32u * 4u;
+}
+
+template <int C>
+__global__ void __launch_bounds__(kFuThreads, 1) ffn_dn_kernel(const DnArgs a) {
+    extern __shared__ __align__(128) uint8_t fu_raw[];
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int hsum[kFuTokens];
+    __shared__ int abort_copy;
+    uint8_t *sdn = fu_raw, *shc = fu_raw + dn_hc_offset(a.groups_max);
+    int *red = reinterpret_cast<int *>(fu_raw + dn_red_offset(a.groups_max));
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t4 = lane & 3;
+    const int T = a.tokens;
+    const int64_t H = a.hidden;
+    const uint32_t r = fu_rank();
+    const int64_t Q = gridDim.x / C, cl = blockIdx.x / C;
+    const int64_t n0 = cl * a.nt / Q, n1 = (cl + 1) * a.nt / Q;
+    const int ntc = static_cast<int>(n1 - n0);
+    const int64_t g0 = r * a.g4 / C, g1 = (r + 1) * a.g4 / C;
+    const int ngc = static_cast<int>(g1 - g0);
+    const int64_t nks = a.inter / 32;
+    const int64_t s0 = 4 * g0, s1 = std::min<int64_t>(4 * g1, nks);
+
+    // ---------------- prologue: the down signs (weights) before the dependency wait
+    const uint32_t row_bytes = static_cast<uint32_t>(ngc) * 128u;
+    if (tid == 0) {
+        mbar_init(&bar, 1);
+        mbar_init_fence();
+        abort_copy = 0;
+        mbar_expect_tx(&bar, row_bytes * static_cast<uint32_t>(ntc));
+        if (row_bytes)
+            for (int n = 0; n < ntc; ++n)
+                bulk_load(sdn + n * row_bytes, a.dn + ((n0 + n) * a.g4 + g0) * 128, row_bytes, &bar);
+    }
+    for (int i = tid; i < kDnNt * 4 * 32; i += kFuThreads) red[i] = 0;
+    __syncthreads();
+    grid_wait();
+    grid_launch_dependents();
+
+    // ---------------- the codes of this CTA's k-steps and the total code sums
+    for (int64_t i = tid; i < (s1 - s0) * 32; i += kFuThreads)
+        reinterpret_cast<uint4 *>(shc)[i] = __ldcg(reinterpret_cast<const uint4 *>(a.hcodes + s0 * 512) + i);
+    if (tid < 16 * kFuTokens) {  // 16 threads per token, then a fixed-order tree
+        const int t = tid >> 4, part = tid & 15;
+        int s = 0;
+        for (int b = part; b < a.gu_ctas; b += 16) s += __ldcg(a.hsum + b * kFuTokens + t);
+#pragma unroll
+        for (int d = 8; d > 0; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);
+        if (part == 0) hsum[t] = s;
+    }
+    if (!mbar_wait_bounded(&bar, 0, kFuSpin)) abort_copy = 1;
+    __syncthreads();
+    const bool aborted = abort_copy != 0;
+    if (aborted && tid == 0) set_flag(a.flags, BD_FLAG_TIMEOUT);
+
+    // ---------------- partial dots: warps split this CTA's groups, all n-tiles of the cluster
+    const int wg0 = warp * ngc / kFuWarps, wg1 = (warp + 1) * ngc / kFuWarps;
+    int acc[kDnNt][4] = {};
+    if (!aborted) {
+        for (int gl = wg0; gl < wg1; ++gl) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int sl = 4 * gl + q;  // local k-step
+                if (s0 + sl >= s1) break;
+                const uint4 A = *reinterpret_cast<const uint4 *>(shc + (sl * 32 + lane) * 16);
+#pragma unroll
+                for (int n = 0; n < kDnNt; ++n) {
+                    if (n < ntc) {
+                        const uint32_t byte = sdn[(n * ngc + gl) * 128 + lane * 4 + q];
+                        mma_s8_16832(acc[n], A.x, A.y, A.z, A.w, fu_nibble(byte & 0xFu), fu_nibble(byte >> 4));
+                    }
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int n = 0; n < kDnNt; ++n)
+        if (n < ntc)
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                if (acc[n][i]) atomicAdd(&red[(n * 4 + i) * 32 + lane], acc[n][i]);
+    __syncthreads();
+    fu_cluster_sync();  // every CTA's partial dots are complete
+
+    // ---------------- CTA r finishes n-tiles [r ntc / C, (r + 1) ntc / C) of the cluster
+    Quant qd;
+    qd.init(__ldg(a.bound_dn), 8);
+    const int f0 = static_cast<int>(r * ntc / C), f1 = static_cast<int>((r + 1) * ntc / C);
+    for (int n = f0 + warp; n < f1; n += kFuWarps) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int tok = g + 8 * (i >> 1);
+            const int64_t o = (n0 + n) * 8 + 2 * t4 + (i & 1);
+            int d01 = 0;
+#pragma unroll
+            for (int rr = 0; rr < C; ++rr) d01 += fu_ld_s32(fu_remote(&red[(n * 4 + i) * 32 + lane], static_cast<uint32_t>(rr)));
+            if (tok >= T || o >= H) continue;
+            const int cs = hsum[tok];
+            float yv = he4_value(2 * d01 - cs, __ldg(a.scale_d + o), qd.step, cs, __ldg(a.mid_d + o));
+            if (a.residual) yv = __fadd_rn(a.residual[tok * H + o], yv);
+            a.y[tok * H + o] = yv;
+        }
+    }
+    fu_cluster_sync();  // no CTA leaves while another still reads its partial dots
+    if (aborted && tid == 0) mbar_wait_bounded(&bar, 0, kFuSpin);
+}
+
+// ------------------------------------------------------------------ D8 sign bytes of the down matrix
+
+// Byte ((n * g4 + s / 4) * 32 + lane) * 4 + s % 4, lane = 4 g + t: bit 4 r + j is
+// latent[8 n + g, 32 s + 16 r + 4 t + j] >= 0 (0 past the matrix).
+__global__ void tile_d8_kernel(const float *__restrict__ latent, int64_t rows, int64_t cols, int64_t nt, int64_t g4,
+                               uint32_t *__restrict__ out, int32_t *flags) {
+    const int64_t total = nt * g4 * 32;
+    bool bad = false;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int lane = static_cast<int>(i & 31);
+        const int64_t rest = i >> 5;
+        const int64_t gq = rest % g4, n = rest / g4;
+        const int g = lane >> 2, t = lane & 3;
+        const int64_t row = n * 8 + g;
+        uint32_t word = 0;
+        if (row < rows) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int64_t s = gq * 4 + q;
+                uint32_t byte = 0;
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int64_t col = 32 * s + 16 * h + 4 * t + j;
+                        if (col < cols) {
+                            const float v = latent[row * cols + col];
+                            bad |= !isfinite(v);
+                            if (v >= 0.0f) byte |= 1u << (4 * h + j);
+                        }
+                    }
+                word |= byte << (8 * q);
+            }
+        }
+        out[i] = word;
+    }
+    if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) set_flag(flags, BD_FLAG_NONFINITE_LATENT);
+}
+
+int64_t d8_bytes(int64_t rows, int64_t cols) { return (rows + 7) / 8 * (((cols + 31) / 32 + 3) / 4) * 128; }
+
+// ------------------------------------------------------------------ launch
+
+namespace {
+struct FuPlan {
+    int ca = 0, cb = 0;      // cluster sizes of the two kernels
+    int64_t ga = 0, gb = 0;  // grids (CTAs)
+    int pairs_max = 0, groups_max = 0;
+    size_t smem_a = 0, smem_b = 0;
+};
+
+template <typename Kern>
+int active_clusters(Kern kern, int c, size_t smem, int64_t want) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
+        return 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(want * c));
+    cfg.blockDim = dim3(kFuThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(c);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) return 0;
+    return n;
+}
+
+template <typename Kern, typename Args>
+int launch_cluster_pdl(Kern kern, const Args &a, int c, int64_t grid, size_t smem, cudaStream_t stream) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
+        return BD_ERR_LAUNCH;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(kFuThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = static_cast<unsigned>(c);
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, kern, a) == cudaSuccess ? BD_OK : BD_ERR_LAUNCH;
+}
+
+// Launch shapes: for each kernel the cluster size (4 or 2) whose co-resident
+// grid has the most CTAs; the down kernel's clusters never own more than kDnNt
+// n-tiles.  Cached per (device, shape).
+int fu_plan(FuPlan &out, int64_t hidden, int64_t inter) {
+    static std::mutex mu;
+    static std::map<std::tuple<int, int64_t, int64_t>, FuPlan> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return BD_ERR_DEVICE;
+    std::lock_guard<std::mutex> lock(mu);
+    const auto key = std::make_tuple(dev, hidden, inter);
+    const auto it = cache.find(key);
+    if (it != cache.end()) {
+        out = it->second;
+        return BD_OK;
+    }
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1) return BD_ERR_DEVICE;
+    const int64_t np = inter / 8, ng = (hidden + 511) / 512, nt = hidden / 8, g4 = (inter / 32 + 3) / 4;
+    FuPlan best;
+    for (int c : {4, 2}) {
+        const int64_t grid = std::min<int64_t>(sms / c, np / c) * c;  // at least one pair per CTA
+        if (grid < c) continue;
+        const int pm = static_cast<int>((np + grid - 1) / grid);
+        const size_t smem = gu_smem_bytes(pm, ng);
+        if (smem > 200 * 1024) continue;
+        const int act = c == 4 ? active_clusters(ffn_gu_kernel<4>, 4, smem, grid / c)
+                               : active_clusters(ffn_gu_kernel<2>, 2, smem, grid / c);
+        const int64_t g = std::min<int64_t>(grid, static_cast<int64_t>(act) * c);
+        if (g > best.ga) {
+            best.ca = c;
+            best.ga = g;
+            best.pairs_max = static_cast<int>((np + g - 1) / g);
+            best.smem_a = gu_smem_bytes(best.pairs_max, ng);
+        }
+    }
+    // down kernel: clusters of 4 first (the smaller shared-memory slice lets its CTAs
+    // sit beside the gate/up kernel's and stream their signs while it runs)
+    for (int c : {4, 2}) {
+        const int gm = static_cast<int>((g4 + c - 1) / c);
+        const size_t smem = dn_smem_bytes(gm);
+        if (smem > 200 * 1024) continue;
+        const int64_t qmin = (nt + kDnNt - 1) / kDnNt;
+        const int act = c == 4 ? active_clusters(ffn_dn_kernel<4>, 4, smem, std::max<int64_t>(qmin, sms / c))
+                               : active_clusters(ffn_dn_kernel<2>, 2, smem, std::max<int64_t>(qmin, sms / c));
+        if (act < 1) continue;
+        const int64_t q = std::min<int64_t>(std::max<int64_t>(act, qmin), nt);
+        best.cb = c;
+        best.gb = q * c;
+        best.groups_max = gm;
+        best.smem_b = smem;
+        break;
+    }
+    if (best.ca == 0 || best.cb == 0) return BD_ERR_LAUNCH;
+    cache[key] = best;
+    out = best;
+    return BD_OK;
+}
+}  // namespace
+
+size_t ffn_fused_workspace_bytes(int64_t hidden, int64_t inter) {
+    (void)hidden;
+    const size_t codes = (static_cast<size_t>(inter / 32) * 512 + 255) / 256 * 256;
+    return codes + 1024 * kFuTokens * sizeof(int32_t);  // code sums of up to 1024 gate/up CTAs
+}
+
+int ffn_fused_he4(const FfnW8 &f, const uint8_t *signs_down_d8, cudaStream_t stream) {
+    if (f.tokens < 1 || f.tokens > kFuTokens || f.hidden < 32 || f.inter < 32 || f.hidden % 32 || f.inter % 32)
+        return BD_ERR_INVALID;
+    if (reinterpret_cast<uintptr_t>(f.x) & 15 || reinterpret_cast<uintptr_t>(f.gain_gate_up) & 15 ||
+        reinterpret_cast<uintptr_t>(f.norm_w) & 15 || reinterpret_cast<uintptr_t>(f.signs_gate_up) & 15 ||
+        reinterpret_cast<uintptr_t>(signs_down_d8) & 15 || reinterpret_cast<uintptr_t>(f.workspace) & 255)
+        return BD_ERR_ALIGNMENT;
+    if (!f.workspace || f.workspace_bytes < ffn_fused_workspace_bytes(f.hidden, f.inter)) return BD_ERR_WORKSPACE;
+    FuPlan pl;
+    if (int st = fu_plan(pl, f.hidden, f.inter)) return st;
+    if (pl.ga > 1024) return BD_ERR_INVALID;
+    char *ws = static_cast<char *>(f.workspace);
+    const size_t codes_bytes = (static_cast<size_t>(f.inter / 32) * 512 + 255) / 256 * 256;
+    GuArgs a{};
+    a.tokens = f.tokens;
+    a.hidden = f.hidden;
+    a.inter = f.inter;
+    a.gu = f.signs_gate_up;
+    a.np = f.inter / 8;
+    a.ng = (f.hidden + 511) / 512;
+    a.x = f.x;
+    a.norm_w = f.norm_w;
+    a.eps = f.eps;
+    a.gain_gu = f.gain_gate_up;
+    a.bound_gu = f.bound_gate_up;
+    a.gain_dn = f.gain_down;
+    a.bound_dn = f.bound_down;
+    a.scale_g = f.scale_gate;
+    a.mid_g = f.mid_gate;
+    a.scale_u = f.scale_up;
+    a.mid_u = f.mid_up;
+    a.hidden_out = f.hidden_out;
+    a.hcodes = reinterpret_cast<int8_t *>(ws);
+    a.hsum = reinterpret_cast<int32_t *>(ws + codes_bytes);
+    a.flags = f.flags;
+    a.pairs_max = pl.pairs_max;
+    int st = pl.ca == 4 ? launch_cluster_pdl(ffn_gu_kernel<4>, a, 4, pl.ga, pl.smem_a, stream)
+                        : launch_cluster_pdl(ffn_gu_kernel<2>, a, 2, pl.ga, pl.smem_a, stream);
+    if (st) return st;
+    DnArgs d{};
+    d.tokens = f.tokens;
+    d.hidden = f.hidden;
+    d.inter = f.inter;
+    d.dn = signs_down_d8;
+    d.nt = f.hidden / 8;
+    d.g4 = (f.inter / 32 + 3) / 4;
+    d.hcodes = a.hcodes;
+    d.hsum = a.hsum;
+    d.gu_ctas = static_cast<int>(pl.ga);
+    d.bound_dn = f.bound_down;
+    d.scale_d = f.scale_down;
+    d.mid_d = f.mid_down;
+    d.residual = f.residual;
+    d.y = f.y;
+    d.flags = f.flags;
+    d.groups_max = pl.groups_max;
+    return pl.cb == 4 ? launch_cluster_pdl(ffn_dn_kernel<4>, d, 4, pl.gb, pl.smem_b, stream)
+                      : launch_cluster_pdl(ffn_dn_kernel<2>, d, 2, pl.gb, pl.smem_b, stream);
+}
+
+int ffn_fused_shape(int64_t hidden, int64_t inter, int *shape) {
+    FuPlan pl;
+    if (int st = fu_plan(pl, hidden, inter)) return st;
+    shape[0] = pl.ca;
+    shape[1] = static_cast<int>(pl.ga);
+    shape[2] = pl.cb;
+    shape[3] = static_cast<int>(pl.gb);
+    return BD_OK;
+}
+
+}  // namespace bd
+
+using namespace bd;
+
+extern "C" int64_t bd_d8_bytes(int64_t rows, int64_t cols) {
+    if (rows < 0 || cols < 0) return -1;
+    return d8_bytes(rows, cols);
+}
+
+extern "C" int bd_tile_signs_d8(const float *latent, int64_t rows, int64_t cols, uint8_t *tiled, int32_t *flags,
+                                bd_stream_t stream) {
+    if (rows < 0 || cols < 1) return BD_ERR_INVALID;
+    if (rows == 0) return BD_OK;
+    if (!latent || !tiled || (reinterpret_cast<uintptr_t>(tiled) & 3)) return BD_ERR_INVALID;
+    const int64_t nt = (rows + 7) / 8, g4 = ((cols + 31) / 32 + 3) / 4;
+    const int64_t total = nt * g4 * 32;
+    int64_t grid = (total + 255) / 256;
+    if (grid > 148 * 32) grid = 148 * 32;
+    tile_d8_kernel<<<static_cast<unsigned>(grid), 256, 0, stream>>>(latent, rows, cols, nt, g4,
+                                                                    reinterpret_cast<uint32_t *>(tiled), flags);
+    BD_CHECK_LAUNCH();
+    return BD_OK;
+}
+
+extern "C" size_t bd_ffn_fused_workspace_bytes(int64_t hidden, int64_t inter) {
+    return hidden < 1 || inter < 1 ? 0 : ffn_fused_workspace_bytes(hidden, inter);
+}
+
+extern "C" int bd_ffn_fused_shape(int64_t hidden, int64_t inter, int *shape) {
+    if (hidden < 32 || inter < 32 || hidden % 32 || inter % 32 || !shape) return BD_ERR_INVALID;
+    return ffn_fused_shape(hidden, inter, shape);
+}

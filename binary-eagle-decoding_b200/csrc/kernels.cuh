@@ -56,6 +56,12 @@ struct FfnW8 {
 size_t ffn_w8_workspace_bytes(int64_t hidden, int64_t inter);
 int ffn_w8(const FfnW8 &f, int epi, cudaStream_t stream);
 
+// ---- two-launch HE4 block for tokens <= 16 (ffn_fused.cu): W8 gate/up words, D8 down bytes
+int64_t d8_bytes(int64_t rows, int64_t cols);
+size_t ffn_fused_workspace_bytes(int64_t hidden, int64_t inter);
+int ffn_fused_he4(const FfnW8 &f, const uint8_t *signs_down_d8, cudaStream_t stream);
+int ffn_fused_shape(int64_t hidden, int64_t inter, int *shape);
+
 // Epilogue selectors of the T16 integer-MMA projection kernels.
 enum Epilogue : int {
     EPI_HE4 = 0,   // HE4 projection value (+ residual)

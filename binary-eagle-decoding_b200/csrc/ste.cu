@@ -43,12 +43,16 @@ __device__ __forceinline__ float block_sum_f(float v, float *scratch) {
 
 // ------------------------------------------------------------------ forward pieces
 
-// x [rows, cols] -> bf16 codes [rows, cols] (row-major) and exact per-row code sums.
-__global__ void __launch_bounds__(256) quantize_rows_bf16_kernel(const float *__restrict__ x, int64_t cols,
-                                                                 const float *__restrict__ gain,
-                                                                 const float *__restrict__ bound, int bits,
-                                                                 __nv_bfloat16 *__restrict__ codes,
-                                                                 int32_t *__restrict__ sums, int32_t *flags) {
+__device__ __forceinline__ void store_code(__nv_bfloat16 *p, int c) { *p = __int2bfloat16_rn(c); }
+__device__ __forceinline__ void store_code(int8_t *p, int c) { *p = static_cast<int8_t>(c); }
+
+// x [rows, cols] -> codes [rows, ld] (row-major, bf16 or int8) and exact per-row code sums.
+template <typename Code>
+__global__ void __launch_bounds__(256) quantize_rows_kernel(const float *__restrict__ x, int64_t cols, int64_t ld,
+                                                            const float *__restrict__ gain,
+                                                            const float *__restrict__ bound, int bits,
+                                                            Code *__restrict__ codes, int32_t *__restrict__ sums,
+                                                            int32_t *flags) {
     __shared__ int scratch[8];
     const int64_t row = blockIdx.x;
     const float b = __ldg(bound);
@@ -68,7 +72,7 @@ __global__ void __launch_bounds__(256) quantize_rows_bf16_kernel(const float *__
             const float g = __fmul_rn(x[row * cols + c], __ldg(gain + c));
             bad |= !isfinite(g);
             const int code = q.code(g);
-            codes[row * cols + c] = __int2bfloat16_rn(code);
+            store_code(codes + row * ld + c, code);
             s += code;
         }
     }
@@ -99,6 +103,39 @@ __global__ void sign_rows_kernel(const float *__restrict__ latent, int64_t n, __
     if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) set_flag(flags, BD_FLAG_NONFINITE_LATENT);
 }
 
+// Tiled transpose into bf16: dst[c][r] = f(src[r][c]) for r < rows, c < cols (32 x 32 tiles).
+// SIGNS = true: f = +-1 of an fp32 latent (x >= 0 -> +1, -0.0 -> +1), with the finiteness check;
+// SIGNS = false: f = the int8 code itself (exact in bf16).
+template <bool SIGNS, typename In>
+__global__ void __launch_bounds__(256) transpose_bf16_kernel(const In *__restrict__ src, int64_t rows, int64_t cols,
+                                                             int64_t lds, __nv_bfloat16 *__restrict__ dst,
+                                                             int64_t ldd, int32_t *flags) {
+    __shared__ float tile[32][33];
+    const int64_t r0 = static_cast<int64_t>(blockIdx.y) * 32, c0 = static_cast<int64_t>(blockIdx.x) * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    bool bad = false;
+    for (int i = ty; i < 32; i += 8) {
+        const int64_t r = r0 + i, c = c0 + tx;
+        float v = 0.0f;
+        if (r < rows && c < cols) {
+            const float x = static_cast<float>(src[r * lds + c]);
+            if (SIGNS) {
+                bad |= !isfinite(x);
+                v = x >= 0.0f ? 1.0f : -1.0f;
+            } else {
+                v = x;
+            }
+        }
+        tile[i][tx] = v;
+    }
+    if (SIGNS && __any_sync(0xffffffffu, bad) && tx == 0) set_flag(flags, BD_FLAG_NONFINITE_LATENT);
+    __syncthreads();
+    for (int i = ty; i < 32; i += 8) {
+        const int64_t c = c0 + i, r = r0 + tx;
+        if (c < cols && r < rows) dst[c * ldd + r] = __float2bfloat16_rn(tile[tx][i]);
+    }
+}
+
 // y[t, o] = he4_value(D[t, o], scale[o], step, sums[t], midpoint[o]) (+ residual).
 __global__ void he4_epilogue_kernel(const float *__restrict__ dot, int64_t tokens, int64_t outs,
                                     const float *__restrict__ scale, const float *__restrict__ midpoint,
@@ -127,6 +164,8 @@ __global__ void __launch_bounds__(kCols) grad_prep_kernel(const float *__restric
                                                           const float *__restrict__ bound, int bits,
                                                           const int32_t *__restrict__ sums,
                                                           __nv_bfloat16 *__restrict__ hi, __nv_bfloat16 *__restrict__ lo,
+                                                          int64_t ld_dl, __nv_bfloat16 *__restrict__ hi_t,
+                                                          __nv_bfloat16 *__restrict__ lo_t, int64_t ld_t,
                                                           float *__restrict__ colpart, float *__restrict__ rowpart) {
     __shared__ float wsum[kCols / 32][kRowChunk];
     Quant q;
@@ -138,23 +177,35 @@ __global__ void __launch_bounds__(kCols) grad_prep_kernel(const float *__restric
     const float mid = live ? __ldg(midpoint + o) : 0.0f;
     const int64_t t0 = static_cast<int64_t>(blockIdx.y) * kRowChunk;
     float acc_scale = 0.0f, acc_mid = 0.0f;
-    for (int r = 0; r < kRowChunk; ++r) {
-        const int64_t t = t0 + r;
-        float gm = 0.0f;
-        if (t < tokens && live) {
-            const int64_t i = t * outs + o;
-            const float g = grad[i];
-            const float d = __fmul_rn(dot[i], q.step);
-            acc_scale = __fadd_rn(acc_scale, __fmul_rn(g, d));
-            acc_mid = __fadd_rn(acc_mid, __fmul_rn(g, __fmul_rn(static_cast<float>(__ldg(sums + t)), q.step)));
-            const float dl = __fmul_rn(g, sc);
-            const __nv_bfloat16 h = __float2bfloat16_rn(dl);
-            hi[i] = h;
-            lo[i] = __float2bfloat16_rn(__fsub_rn(dl, __bfloat162float(h)));
-            gm = __fmul_rn(g, mid);
+    for (int r8 = 0; r8 < kRowChunk; r8 += 8) {
+        uint32_t th[4] = {0u, 0u, 0u, 0u}, tl[4] = {0u, 0u, 0u, 0u};  // eight tokens of the transposed rows
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int r = r8 + j;
+            const int64_t t = t0 + r;
+            float gm = 0.0f;
+            if (t < tokens && live) {
+                const int64_t i = t * outs + o;
+                const float g = grad[i];
+                const float d = __fmul_rn(dot[i], q.step);
+                acc_scale = __fadd_rn(acc_scale, __fmul_rn(g, d));
+                acc_mid = __fadd_rn(acc_mid, __fmul_rn(g, __fmul_rn(static_cast<float>(__ldg(sums + t)), q.step)));
+                const float dl = __fmul_rn(g, sc);
+                const __nv_bfloat16 h = __float2bfloat16_rn(dl);
+                const __nv_bfloat16 l = __float2bfloat16_rn(__fsub_rn(dl, __bfloat162float(h)));
+                hi[t * ld_dl + o] = h;
+                lo[t * ld_dl + o] = l;
+                th[j >> 1] |= static_cast<uint32_t>(__bfloat16_as_ushort(h)) << (16 * (j & 1));
+                tl[j >> 1] |= static_cast<uint32_t>(__bfloat16_as_ushort(l)) << (16 * (j & 1));
+                gm = __fmul_rn(g, mid);
+            }
+            gm = warp_sum(gm);
+            if ((threadIdx.x & 31) == 0) wsum[threadIdx.x >> 5][r] = gm;
         }
-        gm = warp_sum(gm);
-        if ((threadIdx.x & 31) == 0) wsum[threadIdx.x >> 5][r] = gm;
+        if (hi_t && live && t0 + r8 < tokens) {
+            *reinterpret_cast<uint4 *>(hi_t + o * ld_t + t0 + r8) = make_uint4(th[0], th[1], th[2], th[3]);
+            *reinterpret_cast<uint4 *>(lo_t + o * ld_t + t0 + r8) = make_uint4(tl[0], tl[1], tl[2], tl[3]);
+        }
     }
     if (live) {
         colpart[(static_cast<int64_t>(blockIdx.y) * 2 + 0) * outs + o] = acc_scale;
@@ -336,8 +387,47 @@ extern "C" int bd_quantize_rows_bf16(const float *x, int64_t rows, int64_t cols,
     if (!x || !gain || !bound || !codes || !code_sums) return BD_ERR_INVALID;
     if (cudaMemsetAsync(code_sums, 0, rows * sizeof(int32_t), stream) != cudaSuccess) return BD_ERR_LAUNCH;
     dim3 grid(static_cast<unsigned>(rows), static_cast<unsigned>((cols + 1023) / 1024));
-    quantize_rows_bf16_kernel<<<grid, 256, 0, stream>>>(x, cols, gain, bound, bits,
-                                                         reinterpret_cast<__nv_bfloat16 *>(codes), code_sums, flags);
+    quantize_rows_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
+        x, cols, cols, gain, bound, bits, reinterpret_cast<__nv_bfloat16 *>(codes), code_sums, flags);
+    BD_CHECK_LAUNCH();
+    return BD_OK;
+}
+
+extern "C" int bd_quantize_rows_i8(const float *x, int64_t rows, int64_t cols, const float *gain, const float *bound,
+                                   int bits, int8_t *codes, int64_t ld, int32_t *code_sums, int32_t *flags,
+                                   bd_stream_t stream) {
+    if (rows < 0 || cols < 1 || ld < cols || (bits != 4 && bits != 8) || rows > 0x7fffffff ||
+        (cols + 1023) / 1024 > 65535)
+        return BD_ERR_INVALID;
+    if (rows == 0) return BD_OK;
+    if (!x || !gain || !bound || !codes || !code_sums) return BD_ERR_INVALID;
+    if (cudaMemsetAsync(code_sums, 0, rows * sizeof(int32_t), stream) != cudaSuccess) return BD_ERR_LAUNCH;
+    dim3 grid(static_cast<unsigned>(rows), static_cast<unsigned>((cols + 1023) / 1024));
+    quantize_rows_kernel<int8_t><<<grid, 256, 0, stream>>>(x, cols, ld, gain, bound, bits, codes, code_sums, flags);
+    BD_CHECK_LAUNCH();
+    return BD_OK;
+}
+
+// codes int8 [rows][ld] -> bf16 [cols][ld_t] (the weight-gradient GEMM's K-major operand)
+extern "C" int bd_codes_transpose_bf16(const int8_t *codes, int64_t rows, int64_t cols, int64_t ld, uint16_t *out,
+                                       int64_t ld_t, bd_stream_t stream) {
+    if (rows < 1 || cols < 1 || ld < cols || ld_t < rows || (rows + 31) / 32 > 65535 || !codes || !out)
+        return BD_ERR_INVALID;
+    dim3 grid(static_cast<unsigned>((cols + 31) / 32), static_cast<unsigned>((rows + 31) / 32));
+    transpose_bf16_kernel<false, int8_t><<<grid, 256, 0, stream>>>(codes, rows, cols, ld,
+                                                                   reinterpret_cast<__nv_bfloat16 *>(out), ld_t,
+                                                                   nullptr);
+    BD_CHECK_LAUNCH();
+    return BD_OK;
+}
+
+// latent fp32 [rows][cols] -> +-1 bf16 [cols][ld_t] (the input-gradient GEMM's K-major operand)
+extern "C" int bd_sign_cols_bf16(const float *latent, int64_t rows, int64_t cols, uint16_t *out, int64_t ld_t,
+                                 int32_t *flags, bd_stream_t stream) {
+    if (rows < 1 || cols < 1 || ld_t < rows || (rows + 31) / 32 > 65535 || !latent || !out) return BD_ERR_INVALID;
+    dim3 grid(static_cast<unsigned>((cols + 31) / 32), static_cast<unsigned>((rows + 31) / 32));
+    transpose_bf16_kernel<true, float><<<grid, 256, 0, stream>>>(latent, rows, cols, cols,
+                                                                 reinterpret_cast<__nv_bfloat16 *>(out), ld_t, flags);
     BD_CHECK_LAUNCH();
     return BD_OK;
 }
@@ -402,10 +492,14 @@ static SteWs carve_ste(void *ws, int64_t tokens, int64_t outs, int64_t ins) {
 
 extern "C" int bd_ste_grad_prep(const float *grad, const float *dot, int64_t tokens, int64_t out_features,
                                 const float *scale, const float *midpoint, const float *bound, int bits,
-                                const int32_t *code_sums, uint16_t *dl_hi, uint16_t *dl_lo, float *d_scale,
+                                const int32_t *code_sums, uint16_t *dl_hi, uint16_t *dl_lo, int64_t ld_dl,
+                                uint16_t *dl_t_hi, uint16_t *dl_t_lo, int64_t ld_t, float *d_scale,
                                 float *d_midpoint, float *gm, void *workspace, size_t workspace_bytes,
                                 bd_stream_t stream) {
-    if (tokens < 1 || out_features < 1 || (bits != 4 && bits != 8)) return BD_ERR_INVALID;
+    if (tokens < 1 || out_features < 1 || (bits != 4 && bits != 8) || ld_dl < out_features) return BD_ERR_INVALID;
+    if ((dl_t_hi || dl_t_lo) && (!dl_t_hi || !dl_t_lo || ld_t < tokens || ld_t % 8 ||
+                                 (reinterpret_cast<uintptr_t>(dl_t_hi) & 15) || (reinterpret_cast<uintptr_t>(dl_t_lo) & 15)))
+        return BD_ERR_INVALID;
     if (ceil_div(tokens, kRowChunk) > 65535) return BD_ERR_INVALID;
     if (!grad || !dot || !scale || !midpoint || !bound || !code_sums || !dl_hi || !dl_lo || !d_scale ||
         !d_midpoint || !gm)
@@ -416,7 +510,9 @@ extern "C" int bd_ste_grad_prep(const float *grad, const float *dot, int64_t tok
     const int ctiles = static_cast<int>(ceil_div(out_features, kCols));
     grad_prep_kernel<<<dim3(ctiles, rchunks), kCols, 0, stream>>>(
         grad, dot, tokens, out_features, scale, midpoint, bound, bits, code_sums,
-        reinterpret_cast<__nv_bfloat16 *>(dl_hi), reinterpret_cast<__nv_bfloat16 *>(dl_lo), w.colpart, w.rowpart);
+        reinterpret_cast<__nv_bfloat16 *>(dl_hi), reinterpret_cast<__nv_bfloat16 *>(dl_lo), ld_dl,
+        reinterpret_cast<__nv_bfloat16 *>(dl_t_hi), reinterpret_cast<__nv_bfloat16 *>(dl_t_lo), ld_t, w.colpart,
+        w.rowpart);
     BD_CHECK_LAUNCH();
     const int64_t n = out_features > tokens ? out_features : tokens;
     grad_prep_reduce_kernel<<<static_cast<unsigned>(ceil_div(n, 256)), 256, 0, stream>>>(

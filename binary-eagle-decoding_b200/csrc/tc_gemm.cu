@@ -37,10 +37,12 @@ enum TcEpi : int {
     TC_W1A1 = 2,          // y = (D * scale[o]) * rs[t]
     TC_W1A1_SWIGLU = 3,   // N tile = 128 gate + 128 up rows: h = silu(gate) * up, W1A1 values
     TC_F32 = 4,           // bf16 operands (kind::f16), fp32 accumulators: out = D
+    TC_STE = 5,           // bf16 operands: out = (D * step) * 1[|latent| <= window] (+ per-warp partial sums)
 };
 
 // K elements per 128-byte shared-memory row (one TMA box width) of the operand type.
-__host__ __device__ constexpr int tc_bk(int epi) { return epi == TC_F32 ? 64 : 128; }
+__host__ __device__ constexpr int tc_bf16(int epi) { return epi == TC_F32 || epi == TC_STE; }
+__host__ __device__ constexpr int tc_bk(int epi) { return tc_bf16(epi) ? 64 : 128; }
 
 struct TcArgs {
     int64_t M, N, K;       // tokens, outs (as the reference sees them), reduction length
@@ -53,6 +55,14 @@ struct TcArgs {
     float *out;
     int32_t *out_i32;
     int32_t *flags;
+    int split_a;            // bf16 kinds: 2 = A given as hi + lo halves (second tensor map), 1 = one A
+    float *out_dot;         // TC_HE4: the exact integer dot as fp32 as well (optional)
+    // TC_STE: the straight-through sign gradient of the latent [M][N] (row stride ld_latent)
+    const float *latent;
+    int64_t ld_latent;
+    const float *window;    // learned window (device scalar) or null: window_value
+    float window_value;
+    float *partials;        // optional [tiles][8 warps][2]: sum of out^2, sum over |w| > window of D * step * sign(w)
 };
 
 __device__ __forceinline__ uint32_t su32(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
@@ -119,7 +129,8 @@ __host__ __device__ constexpr uint32_t idesc_i8(int n) {
 
 template <int BN, int EPI>
 __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const __grid_constant__ CUtensorMap ma,
-                                                         const __grid_constant__ CUtensorMap mb) {
+                                                         const __grid_constant__ CUtensorMap mb,
+                                                         const __grid_constant__ CUtensorMap ma2) {
     extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sa = smem;                                // stages x 16 KB (tokens)
@@ -130,7 +141,8 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t tiles = a.m_tiles * a.n_tiles;
     constexpr int BKE = tc_bk(EPI);  // K elements per stage
-    const int nk = static_cast<int>((a.K + BKE - 1) / BKE);
+    const int nk1 = static_cast<int>((a.K + BKE - 1) / BKE);
+    const int nk = nk1 * (a.split_a == 2 ? 2 : 1);  // the lo half of A follows the hi half along K
     constexpr uint32_t kCols = 2 * BN;  // two accumulator buffers
     if (threadIdx.x == 0) {
         for (int s = 0; s < kTcStages; ++s) {
@@ -164,8 +176,9 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
                     const int s = it % kTcStages;
                     if (it >= kTcStages && !mb_wait(&empty[s], ((it / kTcStages) - 1) & 1, &abort_flag)) break;
                     mb_expect_tx(&full[s], (kTcBM + BN) * kTcBK);
-                    tma_2d(sa + s * kTcBM * kTcBK, &ma, &full[s], k * BKE, m0);
-                    tma_2d(sb + s * BN * kTcBK, &mb, &full[s], k * BKE, n0);
+                    const int kc = k < nk1 ? k : k - nk1;
+                    tma_2d(sa + s * kTcBM * kTcBK, k < nk1 ? &ma : &ma2, &full[s], kc * BKE, m0);
+                    tma_2d(sb + s * BN * kTcBK, &mb, &full[s], kc * BKE, n0);
                 }
             }
             if (abort_flag) {  // let the loads already issued (stages it - S .. it - 1) land
@@ -175,7 +188,7 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
         }
     } else if (warp == 1) {
         if (lane == 0) {  // MMA issuer
-            constexpr uint32_t idesc = EPI == TC_F32 ? idesc_bf16(BN) : idesc_i8(BN);
+            constexpr uint32_t idesc = tc_bf16(EPI) ? idesc_bf16(BN) : idesc_i8(BN);
             uint32_t it = 0, lt = 0;
             for (int64_t t = blockIdx.x; t < tiles && !abort_flag; t += gridDim.x, ++lt) {
                 const uint32_t b = lt & 1;
@@ -195,7 +208,7 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
                     for (int kk = 0; kk < kTcBK / 32; ++kk) {
                         const uint32_t accumulate = (k > 0 || kk > 0) ? 1u : 0u;
                         // one instruction consumes 32 bytes of K (32 int8 or 16 bf16): descriptor +2
-                        if (EPI == TC_F32)
+                        if (tc_bf16(EPI))
                             asm volatile(
                                 "{\n .reg .pred p;\n setp.ne.u32 p, %4, 0;\n"
                                 " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
@@ -228,7 +241,9 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
         const int quarter = warp & 3, half = (warp - 2) >> 2;
         const int row_in_tile = quarter * 32 + lane;
         Quant q;
-        if (EPI == TC_HE4) q.init(__ldg(a.bound), a.code_bits);
+        if (EPI == TC_HE4 || (EPI == TC_STE && a.bound)) q.init(__ldg(a.bound), a.code_bits);
+        const float ste_step = (EPI == TC_STE && a.bound) ? q.step : 1.0f;
+        const float ste_window = EPI == TC_STE ? (a.window ? __ldg(a.window) : a.window_value) : 0.0f;
         constexpr int OUT_COLS = EPI == TC_W1A1_SWIGLU ? BN / 2 : BN;
         constexpr int HALF = OUT_COLS / 2;
         const bool vec_out = (a.ld_out & 3) == 0 && (reinterpret_cast<uintptr_t>(EPI == TC_RAW ? static_cast<void *>(a.out_i32)
@@ -245,6 +260,7 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
             // in the SwiGLU tile, columns [0, BN/2) are gate rows and [BN/2, BN) the up rows of
             // the same outputs (128-row blocks interleaved in the weight copy)
             const int64_t o_base = (EPI == TC_W1A1_SWIGLU ? (t / a.m_tiles) * (BN / 2) : (t / a.m_tiles) * BN) + half * HALF;
+            float ss = 0.0f, sc = 0.0f;  // TC_STE partial sums of this thread, in column order
             for (int c = 0; c < HALF; c += 16) {
                 uint32_t v[16], u[16];
                 const uint32_t taddr = tmem + b * BN + (static_cast<uint32_t>(quarter * 32) << 16) + half * HALF + c;
@@ -267,7 +283,7 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
                 const bool full16 = o0 + 16 <= a.N;
                 // per-column parameters: the same 16 values for every lane (broadcast loads)
                 float s1[16], s2[16], md[16];
-                if (EPI != TC_RAW && EPI != TC_F32) {
+                if (EPI != TC_RAW && EPI != TC_F32 && EPI != TC_STE) {
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         const bool live = full16 || o0 + j < a.N;
@@ -284,6 +300,8 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
                     di[j] = D;
                     if (EPI == TC_F32) {
                         y[j] = __uint_as_float(v[j]);
+                    } else if (EPI == TC_STE) {
+                        y[j] = __fmul_rn(__uint_as_float(v[j]), ste_step);
                     } else if (EPI == TC_HE4) {
                         y[j] = he4_value(D, s1[j], q.step, cs, md[j]);
                     } else if (EPI == TC_W1A1) {
@@ -295,6 +313,24 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
                     }
                 }
                 const int64_t idx = row * a.ld_out + o0;
+                if (EPI == TC_STE) {
+                    // mask by the straight-through window; the two sums the update needs
+                    const float *lat = a.latent + row * a.ld_latent + o0;
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        if (!(full16 || o0 + j < a.N)) continue;
+                        const float w = lat[j];
+                        const bool inside = fabsf(w) <= ste_window;
+                        if (!inside) sc = __fadd_rn(sc, w >= 0.0f ? y[j] : -y[j]);
+                        y[j] = inside ? y[j] : 0.0f;
+                        ss = __fadd_rn(ss, __fmul_rn(y[j], y[j]));
+                    }
+                }
+                if (EPI == TC_HE4 && a.out_dot) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        if (full16 || o0 + j < a.N) a.out_dot[idx + j] = static_cast<float>(di[j]);
+                }
                 if (EPI == TC_HE4 && a.residual) {
 #pragma unroll
                     for (int j = 0; j < 16; ++j)
@@ -320,6 +356,17 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
             if (lane == 0) mb_arrive(&acc_empty[b]);
+            if (EPI == TC_STE && a.partials) {  // fixed butterfly: deterministic per (tile, warp)
+#pragma unroll
+                for (int d = 16; d > 0; d >>= 1) {
+                    ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, d));
+                    sc = __fadd_rn(sc, __shfl_xor_sync(0xffffffffu, sc, d));
+                }
+                if (lane == 0) {
+                    a.partials[(t * 8 + (warp - 2)) * 2 + 0] = ss;
+                    a.partials[(t * 8 + (warp - 2)) * 2 + 1] = sc;
+                }
+            }
         }
     }
     if (abort_flag && threadIdx.x == 0) set_flag(a.flags, BD_FLAG_TIMEOUT);
@@ -377,12 +424,14 @@ static int sms_tc() {
 
 template <int BN, int EPI>
 static int launch_tc_t(TcArgs a, const int8_t *codes, int64_t ld_codes, const int8_t *weights, int64_t w_rows,
-                       int64_t ld_w, cudaStream_t stream) {
-    CUtensorMap ma, mb;
-    const bool bf16 = EPI == TC_F32;
+                       int64_t ld_w, cudaStream_t stream, const int8_t *codes_lo = nullptr) {
+    CUtensorMap ma, mb, ma2;
+    const bool bf16 = tc_bf16(EPI);
     if (!make_i8_map(&ma, codes, a.M, a.K, ld_codes, kTcBM, bf16) ||
-        !make_i8_map(&mb, weights, w_rows, a.K, ld_w, BN, bf16))
+        !make_i8_map(&mb, weights, w_rows, a.K, ld_w, BN, bf16) ||
+        !make_i8_map(&ma2, codes_lo ? codes_lo : codes, a.M, a.K, ld_codes, kTcBM, bf16))
         return BD_ERR_ALIGNMENT;
+    a.split_a = codes_lo ? 2 : 1;
     a.m_tiles = (a.M + kTcBM - 1) / kTcBM;
     a.n_tiles = (w_rows + BN - 1) / BN;
     const size_t smem = static_cast<size_t>(kTcStages) * (kTcBM + BN) * kTcBK + 1024;
@@ -391,14 +440,17 @@ static int launch_tc_t(TcArgs a, const int8_t *codes, int64_t ld_codes, const in
         return BD_ERR_LAUNCH;
     const int64_t tiles = a.m_tiles * a.n_tiles;
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>(tiles, sms_tc()));
-    kern<<<grid, 320, smem, stream>>>(a, ma, mb);
+    kern<<<grid, 320, smem, stream>>>(a, ma, mb, ma2);
     BD_CHECK_LAUNCH();
     return BD_OK;
 }
 
+int64_t tc_tiles(int64_t m, int64_t n) { return (m + kTcBM - 1) / kTcBM * ((n + 255) / 256); }
+
 int launch_tc_gemm(int epi, const TcArgs &a, const int8_t *codes, int64_t ld_codes, const int8_t *weights,
-                   int64_t w_rows, int64_t ld_w, cudaStream_t stream) {
+                   int64_t w_rows, int64_t ld_w, cudaStream_t stream, const int8_t *codes_lo = nullptr) {
     if (a.M < 1 || a.N < 1 || a.K < 1) return BD_ERR_INVALID;
+    if (codes_lo && epi != TC_F32 && epi != TC_STE) return BD_ERR_INVALID;
     switch (epi) {
         case TC_RAW:
             return launch_tc_t<256, TC_RAW>(a, codes, ld_codes, weights, w_rows, ld_w, stream);
@@ -409,7 +461,9 @@ int launch_tc_gemm(int epi, const TcArgs &a, const int8_t *codes, int64_t ld_cod
         case TC_W1A1_SWIGLU:
             return launch_tc_t<256, TC_W1A1_SWIGLU>(a, codes, ld_codes, weights, w_rows, ld_w, stream);
         case TC_F32:
-            return launch_tc_t<256, TC_F32>(a, codes, ld_codes, weights, w_rows, ld_w, stream);
+            return launch_tc_t<256, TC_F32>(a, codes, ld_codes, weights, w_rows, ld_w, stream, codes_lo);
+        case TC_STE:
+            return launch_tc_t<256, TC_STE>(a, codes, ld_codes, weights, w_rows, ld_w, stream, codes_lo);
         default:
             return BD_ERR_INVALID;
     }
@@ -561,4 +615,79 @@ extern "C" int bd_ffn_w1a1_large(const bd_ffn_large_args *p, bd_stream_t stream)
     d.out = p->y;
     d.flags = p->flags;
     return launch_tc_gemm(TC_W1A1, d, w.codes_h, i8_ld(F), p->signs_down_i8, H, i8_ld(F), stream);
+}
+
+// ------------------------------------------------------------------ training-size HE4 projection and its
+// straight-through gradients on tcgen05 (w1a1_eagle/model.py:71-73, 128-150)
+
+extern "C" int bd_projection_he4_tc(const int8_t *codes, int64_t ld_codes, const int32_t *code_sums, int64_t tokens,
+                                    int64_t in_features, const int8_t *signs_i8, int64_t out_features,
+                                    const float *scale, const float *midpoint, const float *bound, int bits,
+                                    const float *residual, float *y, float *dot, int32_t *flags, bd_stream_t stream) {
+    if (tokens < 1 || in_features < 1 || out_features < 1 || (bits != 4 && bits != 8) || ld_codes < in_features ||
+        tokens > 0x7fffffff)
+        return BD_ERR_INVALID;
+    if (!codes || !code_sums || !signs_i8 || !scale || !midpoint || !bound || !y) return BD_ERR_INVALID;
+    TcArgs a{};
+    a.M = tokens;
+    a.N = out_features;
+    a.K = in_features;
+    a.ld_out = out_features;
+    a.scale = scale;
+    a.mid = midpoint;
+    a.bound = bound;
+    a.code_bits = bits;
+    a.sums = code_sums;
+    a.residual = residual;
+    a.out = y;
+    a.out_dot = dot;
+    a.flags = flags;
+    return launch_tc_gemm(TC_HE4, a, codes, ld_codes, signs_i8, out_features, i8_ld(in_features), stream);
+}
+
+extern "C" int bd_gemm_bf16_split(const uint16_t *a_hi, const uint16_t *a_lo, int64_t m, int64_t k, int64_t lda,
+                                  const uint16_t *b, int64_t n, int64_t ldb, float *c, int64_t ldc,
+                                  bd_stream_t stream) {
+    if (m < 1 || k < 1 || n < 1 || lda < k || ldb < k || ldc < n || !a_hi || !b || !c) return BD_ERR_INVALID;
+    TcArgs t{};
+    t.M = m;
+    t.N = n;
+    t.K = k;
+    t.ld_out = ldc;
+    t.out = c;
+    return launch_tc_gemm(TC_F32, t, reinterpret_cast<const int8_t *>(a_hi), lda * 2,
+                          reinterpret_cast<const int8_t *>(b), n, ldb * 2, static_cast<cudaStream_t>(stream),
+                          reinterpret_cast<const int8_t *>(a_lo));
+}
+
+extern "C" int64_t bd_ste_weight_grad_partials(int64_t out_features, int64_t in_features) {
+    if (out_features < 1 || in_features < 1) return 0;
+    return tc_tiles(out_features, in_features) * 8 * 2;
+}
+
+extern "C" int bd_ste_weight_grad(const uint16_t *grad_t_hi, const uint16_t *grad_t_lo, int64_t out_features,
+                                  int64_t tokens, int64_t ld_t, const uint16_t *codes_t, int64_t in_features,
+                                  const float *latent, const float *window, float window_value, const float *bound,
+                                  int bits, float *d_latent, float *partials, int32_t *flags, bd_stream_t stream) {
+    if (out_features < 1 || tokens < 1 || in_features < 1 || ld_t < tokens || (bound && bits != 4 && bits != 8) ||
+        (!window && !(window_value >= 0.0f)))
+        return BD_ERR_INVALID;
+    if (!grad_t_hi || !codes_t || !latent || !d_latent) return BD_ERR_INVALID;
+    TcArgs a{};
+    a.M = out_features;
+    a.N = in_features;
+    a.K = tokens;
+    a.ld_out = in_features;
+    a.bound = bound;
+    a.code_bits = bits;
+    a.latent = latent;
+    a.ld_latent = in_features;
+    a.window = window;
+    a.window_value = window_value;
+    a.partials = partials;
+    a.out = d_latent;
+    a.flags = flags;
+    return launch_tc_gemm(TC_STE, a, reinterpret_cast<const int8_t *>(grad_t_hi), ld_t * 2,
+                          reinterpret_cast<const int8_t *>(codes_t), in_features, ld_t * 2, stream,
+                          reinterpret_cast<const int8_t *>(grad_t_lo));
 }

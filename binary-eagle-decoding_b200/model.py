@@ -3,10 +3,10 @@
 Same names, constructor arguments, parameter names and ValueError messages as
 the reference.  The binary projections run in ``libbitdraft.so``:
 
-* ``Projection`` quantizes with ``bd_quantize_rows_bf16``, multiplies exact
-  bf16 codes by exact bf16 signs on the tensor cores (fp32 accumulation, so the
-  integer dot is exact), applies ``bd_he4_epilogue``, and back-propagates with
-  the straight-through kernels (``bd_ste_*``);
+* ``Projection`` quantizes with ``bd_quantize_rows_i8``, multiplies int8 codes
+  by the int8 signs on the tcgen05 tensor cores (exact s32 accumulation) with
+  the HE4 epilogue in the same kernel, and back-propagates with the
+  straight-through kernels and tcgen05 GEMMs (``bd_ste_*``);
 * ``Layer`` runs its SwiGLU tail through the fused decode block
   (``bd_ffn_he4``) when no gradient is needed and at most 32 rows come in;
 * ``hard_sign``, ``bound_latents`` and ``clamp_latents`` are kernels too.
@@ -221,96 +221,145 @@ class FrozenLinear(nn.Module):
 # --------------------------------------------------------------------------- binary projection
 
 
+def _round8(n: int) -> int:
+    return (n + 7) // 8 * 8
+
+
 class _ProjectionFn(torch.autograd.Function):
     """Forward value and straight-through gradients of ``Projection.forward``
-    (``model.py:128-150``); see ``csrc/ste.cu`` for the operation order."""
+    (``model.py:128-150``), every product on the tcgen05 tensor cores:
+
+    * forward: int8 codes (``bd_quantize_rows_i8``) times the +-1 int8 signs,
+      ``kind::i8`` with exact s32 accumulators and the HE4 epilogue in the TMEM
+      drain (``bd_projection_he4_tc``), bit-identical to the reference's fp32
+      ``linear`` of integers;
+    * backward: ``dL = G * scale`` as bf16 hi + lo halves (``bd_ste_grad_prep``),
+      the input-side product ``dL . signs`` (``bd_gemm_bf16_split``) into the
+      quantizer's straight-through backward (``bd_ste_input_backward``), and the
+      latent gradient ``dL^T . codes`` with the step scale and the clip-window
+      mask of ``SIGN`` (``model.py:71-73``) in the GEMM's epilogue
+      (``bd_ste_weight_grad``), which also sums the gradient of a learned window.
+    """
 
     @staticmethod
-    def forward(ctx, value, latent, scale, midpoint, log_gain, log_clip, module):
+    def forward(ctx, value, latent, scale, midpoint, log_gain, log_clip, log_window, module):
         device = _need_cuda(value)
         x = value.reshape(-1, value.shape[-1]).float().contiguous()
         tokens, inner = x.shape
         outer = latent.shape[0]
         bits = module.bits
+        lib = _lib.load()
         gain = log_gain.detach().exp().contiguous()
         bound = log_clip.detach().exp().reshape(1).contiguous()
         stream = _stream(device)
         flags = ops.Flags(device)
-        codes = torch.empty((tokens, inner), dtype=torch.bfloat16, device=device)
+        ld = int(lib.bd_i8_ld(inner))
+        codes = torch.empty((tokens, ld), dtype=torch.int8, device=device)
         sums = torch.empty(tokens, dtype=torch.int32, device=device)
-        _lib.call("bd_quantize_rows_bf16", x.data_ptr(), tokens, inner, gain.data_ptr(), bound.data_ptr(), bits,
-                  codes.data_ptr(), sums.data_ptr(), flags.ptr, stream)
+        _lib.call("bd_quantize_rows_i8", x.data_ptr(), tokens, inner, gain.data_ptr(), bound.data_ptr(), bits,
+                  codes.data_ptr(), ld, sums.data_ptr(), flags.ptr, stream)
         flags.check()
-        signs = module.signs_bf16()
-        dot = torch.mm(codes, signs.t(), out_dtype=torch.float32)
+        signs = module.signs_i8()
         y = torch.empty((tokens, outer), dtype=torch.float32, device=device)
-        _lib.call("bd_he4_epilogue", dot.data_ptr(), tokens, outer, scale.detach().contiguous().data_ptr(),
-                  midpoint.detach().contiguous().data_ptr(), bound.data_ptr(), bits, sums.data_ptr(), None,
-                  y.data_ptr(), stream)
+        dot = torch.empty((tokens, outer), dtype=torch.float32, device=device)
+        _lib.call("bd_projection_he4_tc", codes.data_ptr(), ld, sums.data_ptr(), tokens, inner, signs.data_ptr(), outer,
+                  scale.detach().contiguous().data_ptr(), midpoint.detach().contiguous().data_ptr(), bound.data_ptr(),
+                  bits, None, y.data_ptr(), dot.data_ptr(), flags.ptr, stream)
+        flags.check()
+        window = None if log_window is None else log_window.detach().exp().reshape(1).contiguous()
         ctx.module = module
         ctx.value_shape = value.shape
-        ctx.save_for_backward(x, latent, scale, midpoint, gain, bound, dot, codes, sums)
+        ctx.ld = ld
+        ctx.learned = log_window is not None
+        ctx.save_for_backward(x, latent, scale, midpoint, gain, bound, dot, codes, sums, window)
         return y.view(*value.shape[:-1], outer)
 
     @staticmethod
     def backward(ctx, grad_out):
-        x, latent, scale, midpoint, gain, bound, dot, codes, sums = ctx.saved_tensors
+        x, latent, scale, midpoint, gain, bound, dot, codes, sums, window = ctx.saved_tensors
         module = ctx.module
         device = x.device
         stream = _stream(device)
+        lib = _lib.load()
         tokens, inner = x.shape
         outer = latent.shape[0]
         bits = module.bits
+        need = ctx.needs_input_grad
+        need_latent = need[1] or (ctx.learned and need[6])
         g = grad_out.reshape(tokens, outer).float().contiguous()
-        hi = torch.empty((tokens, outer), dtype=torch.bfloat16, device=device)
+        ld_o, ld_t = _round8(outer), _round8(tokens)
+        hi = torch.empty((tokens, ld_o), dtype=torch.bfloat16, device=device)
         lo = torch.empty_like(hi)
+        hi_t = torch.empty((outer, ld_t), dtype=torch.bfloat16, device=device) if need_latent else None
+        lo_t = torch.empty_like(hi_t) if need_latent else None
         d_scale = torch.empty(outer, dtype=torch.float32, device=device)
         d_mid = torch.empty_like(d_scale)
         gm = torch.empty(tokens, dtype=torch.float32, device=device)
-        nbytes = int(_lib.load().bd_ste_workspace_bytes(tokens, outer, inner))
+        nbytes = int(lib.bd_ste_workspace_bytes(tokens, outer, inner))
         ws = ops.workspace(device, "ste", nbytes)
         sc, mid = scale.detach().contiguous(), midpoint.detach().contiguous()
         _lib.call("bd_ste_grad_prep", g.data_ptr(), dot.data_ptr(), tokens, outer, sc.data_ptr(), mid.data_ptr(),
-                  bound.data_ptr(), bits, sums.data_ptr(), hi.data_ptr(), lo.data_ptr(), d_scale.data_ptr(),
-                  d_mid.data_ptr(), gm.data_ptr(), ws.data_ptr(), ws.numel(), stream)
-        need = ctx.needs_input_grad
-        dx = d_gain = d_clip = d_latent = None
+                  bound.data_ptr(), bits, sums.data_ptr(), hi.data_ptr(), lo.data_ptr(), ld_o,
+                  None if hi_t is None else hi_t.data_ptr(), None if lo_t is None else lo_t.data_ptr(), ld_t,
+                  d_scale.data_ptr(), d_mid.data_ptr(), gm.data_ptr(), ws.data_ptr(), ws.numel(), stream)
+        dx = d_gain = d_clip = d_latent = d_window = None
         if need[0] or need[4] or need[5]:
-            signs = module.signs_bf16()
-            dv1 = torch.mm(hi, signs, out_dtype=torch.float32)
-            dv2 = torch.mm(lo, signs, out_dtype=torch.float32)
+            signs_t = module.signs_t_bf16(ld_o)
+            dv = torch.empty((tokens, inner), dtype=torch.float32, device=device)
+            _lib.call("bd_gemm_bf16_split", hi.data_ptr(), lo.data_ptr(), tokens, outer, ld_o, signs_t.data_ptr(),
+                      inner, ld_o, dv.data_ptr(), inner, stream)
             dx = torch.empty_like(x)
             d_gain = torch.empty(inner, dtype=torch.float32, device=device)
             d_clip = torch.empty(1, dtype=torch.float32, device=device)
-            _lib.call("bd_ste_input_backward", dv1.data_ptr(), dv2.data_ptr(), gm.data_ptr(), x.data_ptr(), tokens,
-                      inner, gain.data_ptr(), bound.data_ptr(), bits, dx.data_ptr(), d_gain.data_ptr(),
-                      d_clip.data_ptr(), 0, ws.data_ptr(), ws.numel(), stream)
+            _lib.call("bd_ste_input_backward", dv.data_ptr(), None, gm.data_ptr(), x.data_ptr(), tokens, inner,
+                      gain.data_ptr(), bound.data_ptr(), bits, dx.data_ptr(), d_gain.data_ptr(), d_clip.data_ptr(), 0,
+                      ws.data_ptr(), ws.numel(), stream)
             dx = dx.view(ctx.value_shape)
             d_clip = d_clip.reshape(())
-        if need[1]:
-            ds1 = torch.mm(hi.t(), codes, out_dtype=torch.float32)
-            ds2 = torch.mm(lo.t(), codes, out_dtype=torch.float32)
+        if need_latent:
+            codes_t = torch.empty((inner, ld_t), dtype=torch.bfloat16, device=device)
+            _lib.call("bd_codes_transpose_bf16", codes.data_ptr(), tokens, inner, ctx.ld, codes_t.data_ptr(), ld_t,
+                      stream)
             d_latent = torch.empty((outer, inner), dtype=torch.float32, device=device)
-            _lib.call("bd_ste_sign_backward", ds1.data_ptr(), ds2.data_ptr(), latent.data_ptr(), outer * inner,
-                      float(module.window), bound.data_ptr(), bits, d_latent.data_ptr(), None, stream)
-        return (dx if need[0] else None, d_latent, d_scale if need[2] else None, d_mid if need[3] else None,
-                d_gain if need[4] else None, d_clip if need[5] else None, None)
+            partials = None
+            if ctx.learned:
+                partials = torch.empty(int(lib.bd_ste_weight_grad_partials(outer, inner)), dtype=torch.float32,
+                                       device=device)
+            flags = ops.Flags(device)
+            _lib.call("bd_ste_weight_grad", hi_t.data_ptr(), lo_t.data_ptr(), outer, tokens, ld_t, codes_t.data_ptr(),
+                      inner, latent.detach().contiguous().data_ptr(),
+                      None if window is None else window.data_ptr(), float(module.window), bound.data_ptr(), bits,
+                      d_latent.data_ptr(), None if partials is None else partials.data_ptr(), flags.ptr, stream)
+            flags.check()
+            if ctx.learned:
+                # d/d(log window) = window * sum over |w| > window of the unmasked gradient * sign(w)
+                d_window = (partials.view(-1, 2)[:, 1].sum() * window[0]).reshape(1)
+        return (dx if need[0] else None, d_latent if need[1] else None, d_scale if need[2] else None,
+                d_mid if need[3] else None, d_gain if need[4] else None, d_clip if need[5] else None,
+                d_window if ctx.learned and need[6] else None, None)
 
 
 class Projection(nn.Module):
     """HE4 binary projection (``model.py:116-150``) with the reference's parameters
     ``latent_sign``, ``scale``, ``midpoint``, ``log_gain``, ``log_clip``.
 
-    ``window`` is the sign straight-through window (1.0 in the reference).  Packed
+    ``window`` is the sign straight-through window: the reference's fixed 1.0
+    (``model.py:71-73``), or, with ``learned_window=True``, the initial value of a
+    learned clip ``|w| <= alpha`` held as the parameter ``log_window`` (``alpha =
+    exp(log_window)``); its gradient is the sum over the latents outside the
+    window of their straight-through gradient times ``sign(w)``, the weight-side
+    counterpart of the learned activation clip of ``model.py:136-139``.  Packed
     and expanded signs are caches outside the module's parameters and buffers,
     keyed by the latent's version counter.
     """
 
     def __init__(self, weight: Tensor, bits: int, gain: nn.Parameter, clip: nn.Parameter,
-                 window: float = 1.0) -> None:
+                 window: float = 1.0, learned_window: bool = False) -> None:
         super().__init__()
         if bits not in (4, 8) or weight.ndim != 2 or not bool(torch.isfinite(weight).all()):
             raise ValueError("invalid HE4 projection")
+        if not (math.isfinite(window) and window > 0):
+            raise ValueError("the straight-through window must be positive and finite")
         self.bits = bits
         self.window = float(window)
         self.latent_sign = nn.Parameter(weight.detach().float().clone())
@@ -318,25 +367,38 @@ class Projection(nn.Module):
         self.midpoint = nn.Parameter(torch.zeros(weight.shape[0]))
         self.log_gain = gain
         self.log_clip = clip
+        self.log_window = nn.Parameter(torch.tensor(math.log(window))) if learned_window else None
         self._signs: dict[str, tuple[tuple[int, int], Tensor]] = {}
 
     def _key(self) -> tuple[int, int]:
         return self.latent_sign.data_ptr(), self.latent_sign._version
 
-    def signs_bf16(self) -> Tensor:
-        """+-1 bf16 copy of the signs [out, in] (cached per latent version)."""
+    def signs_i8(self) -> Tensor:
+        """+-1 int8 copy of the signs, rows padded to 128 (the tensor-core forward's
+        operand; cached per latent version)."""
         key = self._key()
-        hit = self._signs.get("bf16")
+        hit = self._signs.get("i8")
         if hit is not None and hit[0] == key:
             return hit[1]
-        latent = self.latent_sign.detach()
+        out = ops.tile_i8(self.latent_sign.detach().contiguous())
+        self._signs["i8"] = (key, out)
+        return out
+
+    def signs_t_bf16(self, ld: int) -> Tensor:
+        """+-1 bf16 signs transposed ``[in][ld]`` (the input-gradient GEMM's operand;
+        cached per latent version)."""
+        key = self._key()
+        hit = self._signs.get("t_bf16")
+        if hit is not None and hit[0] == key and hit[1].shape[1] == ld:
+            return hit[1]
+        latent = self.latent_sign.detach().contiguous()
         device = _need_cuda(latent)
-        out = torch.empty(latent.shape, dtype=torch.bfloat16, device=device)
+        rows, cols = latent.shape
+        out = torch.empty((cols, ld), dtype=torch.bfloat16, device=device)
         flags = ops.Flags(device)
-        _lib.call("bd_sign_rows", latent.contiguous().data_ptr(), latent.numel(), out.data_ptr(), None, flags.ptr,
-                  _stream(device))
+        _lib.call("bd_sign_cols_bf16", latent.data_ptr(), rows, cols, out.data_ptr(), ld, flags.ptr, _stream(device))
         flags.check()
-        self._signs["bf16"] = (key, out)
+        self._signs["t_bf16"] = (key, out)
         return out
 
     def signs_w8(self) -> Tensor:
@@ -355,7 +417,7 @@ class Projection(nn.Module):
 
     def forward(self, value: Tensor) -> Tensor:
         return _ProjectionFn.apply(value, self.latent_sign, self.scale, self.midpoint, self.log_gain, self.log_clip,
-                                   self)
+                                   self.log_window, self)
 
 
 def _projections(model: nn.Module):
@@ -453,7 +515,8 @@ class Layer(nn.Module):
             flags = ops.Flags(gate.device)
             packed = ops.PackedFFN(
                 hidden=gate.shape[1], inter=gate.shape[0], signs_gate_up=ops.tile_gate_up_w8(gate, up, flags),
-                signs_down=self.down.signs_w8(), scale_gate=self.gate.scale.detach().contiguous(),
+                signs_down=self.down.signs_w8(), signs_down_d8=ops.tile_d8(down, flags),
+                scale_gate=self.gate.scale.detach().contiguous(),
                 scale_up=self.up.scale.detach().contiguous(), scale_down=self.down.scale.detach().contiguous(),
                 midpoint_gate=self.gate.midpoint.detach().contiguous(),
                 midpoint_up=self.up.midpoint.detach().contiguous(),

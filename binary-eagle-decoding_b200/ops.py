@@ -198,6 +198,7 @@ class PackedFFN:
     bound_down: Tensor | None = None
     signs_gate_up_i8: Tensor | None = None  # large-M copies (tensor-core path), see pack_ffn(large=True)
     signs_down_i8: Tensor | None = None
+    signs_down_d8: Tensor | None = None  # down signs of the two-launch HE4 block (tokens <= 16)
 
 
 def w8_words(rows: int, cols: int) -> int:
@@ -222,6 +223,27 @@ def tile_w8(latent: Tensor, block_stride: int = 1, block_offset: int = 0, out: T
     return out
 
 
+def tile_d8(latent: Tensor, flags: Flags | None = None) -> Tensor | None:
+    """D8 sign bytes of the down matrix ``[hidden, inter]`` for the two-launch HE4
+    block: ``[hidden / 8][ceil(inter / 128)][32 lanes][4]``: lane ``4 g + t``,
+    byte ``s % 4`` of 4-k-step group ``s / 4`` of n-tile ``n`` has bit ``4 r + j`` =
+    ``latent[8 n + g, 32 s + 16 r + 4 t + j] >= 0``.  None when a dimension is not
+    a multiple of 32 (the block then takes the three-kernel path)."""
+    if latent.dtype != torch.float32 or latent.ndim != 2:
+        raise ValueError("finite F32 sign matrix required")
+    device = _require_cuda(latent)
+    rows, cols = latent.shape
+    if rows % 32 or cols % 32:
+        return None
+    out = torch.zeros(int(_lib.load().bd_d8_bytes(rows, cols)), dtype=torch.uint8, device=device)
+    own = flags is None
+    flags = flags or Flags(device)
+    _lib.call("bd_tile_signs_d8", _p(latent), rows, cols, _p(out), flags.ptr, _stream(device))
+    if own:
+        flags.check()
+    return out
+
+
 def tile_gate_up_w8(gate: Tensor, up: Tensor, flags: Flags | None = None) -> Tensor:
     """Gate and up W8 signs with their 8-row n-tiles interleaved (gate, up, gate, up, ...)."""
     if gate.shape != up.shape:
@@ -240,6 +262,7 @@ def pack_ffn(gate: Tensor, up: Tensor, down: Tensor, scale_gate: Tensor | None =
     flags = Flags(gate.device)
     signs_gate_up = tile_gate_up_w8(gate.contiguous(), up.contiguous(), flags)
     signs_down = tile_w8(down.contiguous(), flags=flags)
+    signs_down_d8 = tile_d8(down.contiguous(), flags=flags)
     gu_i8 = tile_gate_up_i8(gate.contiguous(), up.contiguous(), flags) if large else None
     dn_i8 = tile_i8(down.contiguous(), flags=flags) if large else None
     flags.check()
@@ -248,7 +271,7 @@ def pack_ffn(gate: Tensor, up: Tensor, down: Tensor, scale_gate: Tensor | None =
         scale_gate=(gate.abs().mean(-1) if scale_gate is None else scale_gate).contiguous(),
         scale_up=(up.abs().mean(-1) if scale_up is None else scale_up).contiguous(),
         scale_down=(down.abs().mean(-1) if scale_down is None else scale_down).contiguous(),
-        signs_gate_up_i8=gu_i8, signs_down_i8=dn_i8,
+        signs_gate_up_i8=gu_i8, signs_down_i8=dn_i8, signs_down_d8=signs_down_d8,
     )
 
 
@@ -329,13 +352,18 @@ def ffn_w1a1_large(x: Tensor, ffn: PackedFFN, hidden_out: bool = False, flags: F
     return (y, h) if hidden_out else y
 
 
+FUSED_MAX_TOKENS = 16
+
+
 def ffn_he4(x: Tensor, ffn: PackedFFN, residual: Tensor | None = None, hidden_out: bool = False,
             flags: Flags | None = None, out: Tensor | None = None, norm: Tensor | None = None,
-            epsilon: float = 1e-6):
+            epsilon: float = 1e-6, fused: bool = False):
     """HE4 SwiGLU block ``residual + down(silu(gate(n)) * up(n))`` (model.py:220-223).
 
     ``n = x``, or ``n = rms(x, norm, epsilon)`` when ``norm`` is given (then
-    ``x`` is the residual stream itself).
+    ``x`` is the residual stream itself).  Up to 16 tokens with D8 down signs
+    run as two cluster launches (``bd_ffn_he4_fused``) when ``fused`` is
+    True; otherwise the three-kernel path (``bd_ffn_he4``).
     """
     device = _require_cuda(x, residual, out)
     tokens = x.shape[0]
@@ -343,8 +371,13 @@ def ffn_he4(x: Tensor, ffn: PackedFFN, residual: Tensor | None = None, hidden_ou
         raise ValueError("decode feed-forward takes 1 to 32 tokens")
     y = torch.empty((tokens, ffn.hidden), dtype=torch.float32, device=device) if out is None else out
     h = torch.empty((tokens, ffn.inter), dtype=torch.float32, device=device) if hidden_out else None
-    nbytes = int(_lib.load().bd_ffn_workspace_bytes(tokens, ffn.hidden, ffn.inter))
-    ws = workspace(device, "ffn", nbytes)
+    one_launch = fused and ffn.signs_down_d8 is not None and tokens <= FUSED_MAX_TOKENS
+    if one_launch:
+        nbytes = int(_lib.load().bd_ffn_fused_workspace_bytes(ffn.hidden, ffn.inter))
+        ws = workspace(device, "ffn_fused", nbytes)
+    else:
+        nbytes = int(_lib.load().bd_ffn_workspace_bytes(tokens, ffn.hidden, ffn.inter))
+        ws = workspace(device, "ffn", nbytes)
     own = flags is None
     flags = flags or Flags(device)
     args = _lib.FfnHe4Args(
@@ -353,7 +386,10 @@ def ffn_he4(x: Tensor, ffn: PackedFFN, residual: Tensor | None = None, hidden_ou
         _p(ffn.signs_down), _p(ffn.scale_down), _p(ffn.midpoint_down), _p(ffn.gain_down), _p(ffn.bound_down),
         _p(h), _p(ws), ws.numel(), flags.ptr, _p(norm), float(epsilon),
     )
-    _lib.call("bd_ffn_he4", _lib.ctypes.byref(args), _stream(device))
+    if one_launch:
+        _lib.call("bd_ffn_he4_fused", _lib.ctypes.byref(args), _p(ffn.signs_down_d8), _stream(device))
+    else:
+        _lib.call("bd_ffn_he4", _lib.ctypes.byref(args), _stream(device))
     if own:
         flags.check()
     return (y, h) if hidden_out else y

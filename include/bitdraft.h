@@ -152,6 +152,30 @@ typedef struct {
 size_t bd_ffn_workspace_bytes(int tokens, int64_t hidden, int64_t inter);
 int bd_ffn_he4(const bd_ffn_he4_args *args, bd_stream_t stream);
 
+/* The same HE4 block (w1a1_eagle/model.py:128-150, 220-223) in two launches
+ * for tokens <= 16, hidden and inter multiples of 32.  Gate/up: clusters of
+ * CTAs quantize x together (rms shared through distributed shared memory),
+ * each CTA streams its gate/up W8 words into shared memory before the
+ * dependency wait and writes the A8 codes of the down input.  Down (launched
+ * with programmatic dependent launch, so its CTAs stream their signs from
+ * signs_down_d8 while gate/up runs): clusters own output rows, their CTAs
+ * split K and meet through distributed shared memory.  args->signs_down is not
+ * read.  Workspace: bd_ffn_fused_workspace_bytes(hidden, inter) (no zeroing
+ * needed; calls sharing one must not overlap on the GPU).
+ * bd_tile_signs_d8: down signs [rows = hidden][cols = inter] as D8 bytes
+ *   ((n * g4 + s / 4) * 32 + lane) * 4 + s % 4 (n = 8-row tile, s = 32-column
+ *   k-step, g4 = ceil(k-steps / 4), lane = 4 g + t): bit 4 r + j is
+ *   latent[8 n + g][32 s + 16 r + 4 t + j] >= 0.
+ * bd_ffn_fused_shape: the launch shape chosen for these sizes on the current
+ *   device, shape[4] = {gate/up cluster size, gate/up CTAs, down cluster size,
+ *   down CTAs} (a diagnostic; it has no counterpart in the reference). */
+int64_t bd_d8_bytes(int64_t rows, int64_t cols);
+int bd_tile_signs_d8(const float *latent, int64_t rows, int64_t cols, uint8_t *tiled, int32_t *flags,
+                     bd_stream_t stream);
+size_t bd_ffn_fused_workspace_bytes(int64_t hidden, int64_t inter);
+int bd_ffn_fused_shape(int64_t hidden, int64_t inter, int *shape);
+int bd_ffn_he4_fused(const bd_ffn_he4_args *args, const uint8_t *signs_down_d8, bd_stream_t stream);
+
 /* Pure one-bit-weight SwiGLU (fp32 activations; no reference module -- built
  * from hard_sign (model.py:92-95) and the mean|W| row scale (model.py:123)):
  *   y = sd * sign(Wd) . (silu(sg * sign(Wg) x) * (su * sign(Wu) x)).
@@ -426,7 +450,8 @@ int bd_he4_epilogue(const float *dot, int64_t tokens, int64_t out_features, cons
 size_t bd_ste_workspace_bytes(int64_t tokens, int64_t out_features, int64_t in_features);
 int bd_ste_grad_prep(const float *grad, const float *dot, int64_t tokens, int64_t out_features, const float *scale,
                      const float *midpoint, const float *bound, int bits, const int32_t *code_sums,
-                     uint16_t *dl_hi, uint16_t *dl_lo, float *d_scale, float *d_midpoint, float *gm,
+                     uint16_t *dl_hi, uint16_t *dl_lo, int64_t ld_dl, uint16_t *dl_t_hi, uint16_t *dl_t_lo,
+                     int64_t ld_t, float *d_scale, float *d_midpoint, float *gm,
                      void *workspace, size_t workspace_bytes, bd_stream_t stream);
 int bd_ste_input_backward(const float *d_values, const float *d_values2, const float *gm, const float *x,
                           int64_t tokens, int64_t in_features, const float *gain, const float *bound, int bits,
@@ -435,6 +460,45 @@ int bd_ste_input_backward(const float *d_values, const float *d_values2, const f
 int bd_ste_sumsq_count(int64_t n);
 int bd_ste_sign_backward(const float *grad, const float *grad2, const float *latent, int64_t n, float window,
                          const float *bound, int bits, float *out, float *sumsq_partials, bd_stream_t stream);
+
+/* The same projection and backward with every product on the 5th-generation
+ * tensor cores (tcgen05, TMEM accumulators, TMA-loaded operands), replacing
+ * the dense fp32 GEMMs autograd runs for Projection.forward
+ * (w1a1_eagle/model.py:141-150) and its backward with SIGN (model.py:71-73):
+ * bd_quantize_rows_i8: int8 codes [rows][ld] (ld >= cols, a multiple of 16)
+ *   and exact row sums (model.py:128-139).
+ * bd_projection_he4_tc: y = HE4 epilogue of D = codes . signs^T (kind::i8, exact
+ *   s32), signs as bd_tile_signs_i8; optionally D itself (fp32, exact) in dot.
+ * bd_sign_cols_bf16 / bd_codes_transpose_bf16: the +-1 signs [in][ld_t] and the
+ *   codes [in][ld_t] (ld_t >= rows, a multiple of 8) as K-major bf16 operands.
+ * bd_gemm_bf16_split: c = (a_hi + a_lo) . b^T in fp32 (kind::f16; the two
+ *   halves of a are one reduction of twice the length): d_values = dL . signs.
+ * bd_ste_weight_grad: d_latent[o][i] = ((dL^T . codes)[o][i] * step) *
+ *   1[|latent[o][i]| <= window] (window = *window when window != NULL, else
+ *   window_value), dL^T given as bf16 halves [out][ld_t] (bd_ste_grad_prep's
+ *   transposed outputs), codes^T as bf16 [in][ld_t].  The clip mask, the step
+ *   scale and two sums (of d_latent^2, and of the unmasked gradient times
+ *   sign(latent) where |latent| > window: the gradient of a learned window)
+ *   are in the GEMM's epilogue; the sums come per (tile, epilogue warp) in
+ *   partials [bd_ste_weight_grad_partials(out, in)] as (sum, sum) pairs. */
+int bd_quantize_rows_i8(const float *x, int64_t rows, int64_t cols, const float *gain, const float *bound,
+                        int bits, int8_t *codes, int64_t ld, int32_t *code_sums, int32_t *flags,
+                        bd_stream_t stream);
+int bd_projection_he4_tc(const int8_t *codes, int64_t ld_codes, const int32_t *code_sums, int64_t tokens,
+                         int64_t in_features, const int8_t *signs_i8, int64_t out_features, const float *scale,
+                         const float *midpoint, const float *bound, int bits, const float *residual, float *y,
+                         float *dot, int32_t *flags, bd_stream_t stream);
+int bd_sign_cols_bf16(const float *latent, int64_t rows, int64_t cols, uint16_t *out, int64_t ld_t, int32_t *flags,
+                      bd_stream_t stream);
+int bd_codes_transpose_bf16(const int8_t *codes, int64_t rows, int64_t cols, int64_t ld, uint16_t *out,
+                            int64_t ld_t, bd_stream_t stream);
+int bd_gemm_bf16_split(const uint16_t *a_hi, const uint16_t *a_lo, int64_t m, int64_t k, int64_t lda,
+                       const uint16_t *b, int64_t n, int64_t ldb, float *c, int64_t ldc, bd_stream_t stream);
+int64_t bd_ste_weight_grad_partials(int64_t out_features, int64_t in_features);
+int bd_ste_weight_grad(const uint16_t *grad_t_hi, const uint16_t *grad_t_lo, int64_t out_features, int64_t tokens,
+                       int64_t ld_t, const uint16_t *codes_t, int64_t in_features, const float *latent,
+                       const float *window, float window_value, const float *bound, int bits, float *d_latent,
+                       float *partials, int32_t *flags, bd_stream_t stream);
 
 /* The update (w1a1_eagle/numerical/worker.py:365-392): clip_grad_norm_(1.0),
  * AdamW(weight_decay=0, fused=True) per parameter group, scale.clamp_(min=0),

@@ -219,6 +219,28 @@ def tile_signs_w8(latent: np.ndarray, stride: int = 1, offset: int = 0) -> np.nd
     return out.reshape(-1)
 
 
+def tile_signs_d8(latent: np.ndarray) -> np.ndarray:
+    """D8 sign bytes ``[n-tile][4-k-step group][lane][4]`` (uint8) of an F32 ``[rows, cols]`` matrix.
+
+    Byte ``s % 4`` of lane ``4 g + t`` at (n-tile ``n``, group ``s // 4``): bit
+    ``4 r + j`` is ``latent[8 n + g, 32 s + 16 r + 4 t + j] >= 0`` (0 past the
+    matrix); the m16n8k32 B register ``r`` of that n-tile and k-step is nibble
+    ``r`` spread to one bit per byte.
+    """
+    latent = _f32(latent)
+    rows, cols = latent.shape
+    nt, ksteps = (rows + 7) // 8, (cols + 31) // 32
+    g4 = (ksteps + 3) // 4
+    bits = np.zeros((nt * 8, g4 * 4 * 32), dtype=np.uint8)
+    bits[:rows, :cols] = latent >= 0
+    b = bits.reshape(nt, 8, g4, 4, 2, 4, 4)  # n, g, group, q, r, t, j
+    r, j = np.meshgrid(np.arange(2), np.arange(4), indexing="ij")
+    shifts = (4 * r + j).astype(np.uint8)  # [r, j]
+    ordered = b.transpose(0, 2, 1, 5, 3, 4, 6)  # n, group, g, t, q, r, j
+    out = (ordered << shifts).sum(axis=(5, 6)).astype(np.uint8)  # n, group, g, t, q
+    return out.reshape(-1)
+
+
 # --------------------------------------------------------------------------- quantizer
 
 

@@ -29,8 +29,12 @@ def projection_backward(grad_out, value, latent, scale, midpoint, log_gain, log_
     """Gradients of ``sum(grad_out * Projection(value))`` w.r.t. every input.
 
     Returns a dict with ``input``, ``latent_sign``, ``scale``, ``midpoint``,
-    ``log_gain`` and ``log_clip``.  ``log_gain``/``log_clip`` are the raw
-    parameters (exponentiated here with numpy).
+    ``log_gain``, ``log_clip`` and ``log_window``.  ``log_gain``/``log_clip`` are
+    the raw parameters (exponentiated here with numpy).  ``log_window`` is the
+    gradient of a learned straight-through window ``window = exp(log_window)``:
+    the clip ``|w| <= window`` passes the sign gradient inside the window, and
+    outside it the clip's output moves with the window, by ``sign(w)``
+    (the weight-side counterpart of the activation clip of ``model.py:136-139``).
     """
     G = np.asarray(grad_out, dtype=np.float32)
     x = np.asarray(value, dtype=np.float32)
@@ -55,7 +59,10 @@ def projection_backward(grad_out, value, latent, scale, midpoint, log_gain, log_
     vsum = values.sum(-1, keepdims=True).astype(np.float32)
     d_mid = (G * vsum).sum(0).astype(np.float32)
     d_values = (d_values + (G * midpoint).sum(-1, keepdims=True)).astype(np.float32)
-    d_latent = (d_signs * (np.abs(latent) <= F32(window))).astype(np.float32)
+    inside = np.abs(latent) <= F32(window)
+    d_latent = (d_signs * inside).astype(np.float32)
+    d_window = F32(np.where(inside, 0.0, d_signs * np.where(latent >= 0, 1.0, -1.0)).sum(dtype=np.float64))
+    d_log_window = F32(d_window * F32(window))
     d_scale = (d_scale_c * (scale >= 0)).astype(np.float32)
     d_codes = (d_values * step).astype(np.float32)
     d_step = F32((d_values * codes).sum())
@@ -77,6 +84,7 @@ def projection_backward(grad_out, value, latent, scale, midpoint, log_gain, log_
     d_x = (d_gained * gain).astype(np.float32)
     d_gain = (d_gained * x).sum(0).astype(np.float32)
     return {
+        "log_window": d_log_window,
         "input": d_x,
         "latent_sign": d_latent,
         "scale": d_scale,

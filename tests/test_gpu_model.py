@@ -100,6 +100,34 @@ def test_projection_large_shapes_against_oracle(bd, tokens):
         assert err < 1e-3, (name, err)
 
 
+def test_projection_learned_window_against_oracle(bd):
+    """The learned straight-through window |w| <= alpha (alpha = 0.05 initially):
+    the latent gradient masked by the window and the gradient of log alpha (the
+    sum over latents outside the window of their gradient times sign(w)), both
+    from the epilogue of the tcgen05 latent-gradient GEMM, against the oracle."""
+    g = torch.Generator().manual_seed(5)
+    inner, outer, tokens = 2560, 9728, 256
+    latent = torch.randn((outer, inner), generator=g) * 0.02
+    log_gain = torch.randn(inner, generator=g) * 0.2
+    layer = bd.Projection(latent, 8, nn.Parameter(log_gain.clone()), nn.Parameter(torch.tensor(0.1)), window=0.05,
+                          learned_window=True).to(DEV)
+    value = torch.randn((tokens, inner), generator=g)
+    out = layer(value.to(DEV))
+    upstream = torch.randn((tokens, outer), generator=g)
+    (out * upstream.to(DEV)).sum().backward()
+    alpha = np.float32(layer.log_window.detach().exp().cpu().numpy())  # the device's exp, as the kernel used
+    ref = optim.projection_backward(upstream.numpy(), value.numpy(), latent.numpy(),
+                                    layer.scale.detach().cpu().numpy(), layer.midpoint.detach().cpu().numpy(),
+                                    log_gain.numpy(), np.float32(0.1), 8, window=alpha)
+    got = layer.latent_sign.grad.cpu().numpy().astype(np.float64)
+    want = np.asarray(ref["latent_sign"], np.float64)
+    assert np.linalg.norm(got - want) / np.linalg.norm(want) < 1e-3
+    outside = np.abs(latent.numpy()) > alpha
+    assert outside.any() and not got[outside].any()  # masked exactly outside the window
+    gw, ww = float(layer.log_window.grad.cpu()), float(ref["log_window"])
+    assert abs(gw - ww) <= 1e-3 * abs(ww), (gw, ww)
+
+
 def test_hard_sign_forward_backward(bd):
     x = torch.tensor([-2.0, -1.0, -0.0, 0.0, 0.5, 1.0, 1.5], device=DEV, requires_grad=True)
     y = bd.hard_sign(x)
@@ -205,7 +233,7 @@ def test_adamw_latent_matches_reference_and_repacks(bd):
                           nn.Parameter(torch.tensor(0.0))).to(DEV)
     for p in layer.parameters():
         p.requires_grad_(p is layer.latent_sign)
-    opt = qat.BitAdamW(layer, qat.Optimization(step_sizes={**qat.default_step_sizes(), "sign": 1e-3}))
+    opt = qat.BitAdamW(layer, qat.UpdatePolicy(step_sizes={**qat.REFERENCE_STEP_SIZES, "sign": 1e-3}))
     for step in range(3):
         layer.latent_sign.grad = t(f[f"grad{step}"])
         opt.step()
