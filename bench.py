@@ -504,7 +504,8 @@ def ffn_record(pkg, device, peak: float, peak_kind: str) -> dict:
            "algorithmic_bytes": algorithmic,
            "timing": f"CUDA graph of {FFN_SETS} blocks over {FFN_SETS} weight sets (448 MB > 3 x L2), CUDA events"}
     for mode, fn in (("w1", lambda i: ops.ffn_w1(x, ffns[i % FFN_SETS], flags=flags)),
-                     ("he4", lambda i: ops.ffn_he4(x, ffns[i % FFN_SETS], flags=flags))):
+                     ("he4", lambda i: ops.ffn_he4(x, ffns[i % FFN_SETS], flags=flags)),
+                     ("he4_clusters", lambda i: ops.ffn_he4(x, ffns[i % FFN_SETS], flags=flags, fused=True))):
         us = _graph_us(fn, FFN_SETS, 20)
         gbs = algorithmic / (us * 1e-6) / 1e9
         out[mode] = {"us_per_block": us, "GB/s": gbs, "frac": gbs / peak}
@@ -716,7 +717,8 @@ def workload_qat(args, pkg, device, rank: int, world: int) -> list[dict]:
     qat = importlib.import_module("binary-eagle-decoding_b200.qat")
     cfg = pkg.Geometry(**GEOMETRY)
     tensors, vocabulary, _, _ = make_tensors()
-    model = pkg.HE4(tensors, vocabulary, VOCAB - 1, cfg).to(device)
+    # the straight-through window is a learned clip |w| <= alpha, alpha = 0.05 at the start
+    model = pkg.HE4(tensors, vocabulary, VOCAB - 1, cfg, window=0.05, learned_window=True).to(device)
     del tensors, vocabulary
     opt = qat.BitAdamW(model)
     g = torch.Generator().manual_seed(100 + rank)
@@ -728,12 +730,15 @@ def workload_qat(args, pkg, device, rank: int, world: int) -> list[dict]:
         anchors = [16 + (length - 32) * i // windows_per for i in range(windows_per)]
         samples.append((feats, tokens, tuple(qat.Window(a, tuple(tokens[a + 1:a + 16])) for a in anchors)))
     params = [p for ps in opt.groups.values() for _, p in ps]
+    # the gradient all-reduce runs in buckets during the last sequence's backward pass
+    exchange = qat.GradientExchange(params)
 
     def step(u):
         opt.zero_grad()
-        for feats, tokens, windows in samples:
+        for i, (feats, tokens, windows) in enumerate(samples):
+            exchange.armed = i == len(samples) - 1
             qat.group_loss(model, feats, tokens, windows, scale=1.0 / seqs)
-        qat.average_gradients(params)
+        exchange.finish()
         _, coef = qat.clip_grad_norm(params, 1.0)
         opt.step(coef)
 
@@ -743,12 +748,26 @@ def workload_qat(args, pkg, device, rank: int, world: int) -> list[dict]:
     reps = 3
     us = _events_us(lambda: step(0), reps)
     t = torch.tensor([us], device=device)
+    allreduce_ms = None
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        # the same payload reduced on its own, for the breakdown
+        flat = torch.cat([p.grad.reshape(-1) for p in params])
+        for _ in range(2):
+            torch.distributed.all_reduce(flat)
+        torch.cuda.synchronize()
+        ar = torch.tensor([_events_us(lambda: torch.distributed.all_reduce(flat), 3) / 1e3], device=device)
+        torch.distributed.all_reduce(ar, op=torch.distributed.ReduceOp.MAX)
+        allreduce_ms = ar.item()
+        del flat
     rows = seqs * windows_per * 16 * world
+    n_params = sum(p.numel() for p in params)
     return [{"workload": f"QAT update, {seqs} sequences x 2048 positions x 32 windows of 16 slots per GPU, "
-                         f"4-layer drafter, {world} GPU(s)", "metric": "slot rows / s", "value": rows / (t.item() * 1e-6),
-             "unit": "rows/s", "ms_per_step": t.item() / 1e3, "n_gpus": world}]
+                         f"4-layer drafter, learned straight-through window (alpha 0.05 at the start), {world} GPU(s)",
+             "metric": "slot rows / s", "value": rows / (t.item() * 1e-6),
+             "unit": "rows/s", "ms_per_step": t.item() / 1e3, "n_gpus": world,
+             "gradient_bytes": 4 * n_params, "allreduce_buckets_per_step": exchange.buckets // (reps + 2),
+             "allreduce_ms_standalone": allreduce_ms}]
 
 
 def run_workload(args, rank: int, world: int, local_rank: int) -> None:

@@ -136,6 +136,39 @@ __global__ void __launch_bounds__(256) transpose_bf16_kernel(const In *__restric
     }
 }
 
+// fp32 [rows][cols] (row stride lds) -> bf16 halves hi = bf16(x), lo = bf16(x - hi) with row
+// stride ldd; TRANSPOSE writes them as [cols][ldd] instead (32 x 32 tiles through shared memory).
+template <bool TRANSPOSE>
+__global__ void __launch_bounds__(256) split_bf16_kernel(const float *__restrict__ src, int64_t rows, int64_t cols,
+                                                         int64_t lds, __nv_bfloat16 *__restrict__ hi,
+                                                         __nv_bfloat16 *__restrict__ lo, int64_t ldd) {
+    __shared__ float tile[32][33];
+    const int64_t r0 = static_cast<int64_t>(blockIdx.y) * 32, c0 = static_cast<int64_t>(blockIdx.x) * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    for (int i = ty; i < 32; i += 8) {
+        const int64_t r = r0 + i, c = c0 + tx;
+        const float v = (r < rows && c < cols) ? src[r * lds + c] : 0.0f;
+        if (TRANSPOSE) {
+            tile[i][tx] = v;
+        } else if (r < rows && c < cols) {
+            const __nv_bfloat16 h = __float2bfloat16_rn(v);
+            hi[r * ldd + c] = h;
+            lo[r * ldd + c] = __float2bfloat16_rn(__fsub_rn(v, __bfloat162float(h)));
+        }
+    }
+    if (!TRANSPOSE) return;
+    __syncthreads();
+    for (int i = ty; i < 32; i += 8) {
+        const int64_t c = c0 + i, r = r0 + tx;
+        if (c < cols && r < rows) {
+            const float v = tile[tx][i];
+            const __nv_bfloat16 h = __float2bfloat16_rn(v);
+            hi[c * ldd + r] = h;
+            lo[c * ldd + r] = __float2bfloat16_rn(__fsub_rn(v, __bfloat162float(h)));
+        }
+    }
+}
+
 // y[t, o] = he4_value(D[t, o], scale[o], step, sums[t], midpoint[o]) (+ residual).
 __global__ void he4_epilogue_kernel(const float *__restrict__ dot, int64_t tokens, int64_t outs,
                                     const float *__restrict__ scale, const float *__restrict__ midpoint,
@@ -417,6 +450,23 @@ extern "C" int bd_codes_transpose_bf16(const int8_t *codes, int64_t rows, int64_
     transpose_bf16_kernel<false, int8_t><<<grid, 256, 0, stream>>>(codes, rows, cols, ld,
                                                                    reinterpret_cast<__nv_bfloat16 *>(out), ld_t,
                                                                    nullptr);
+    BD_CHECK_LAUNCH();
+    return BD_OK;
+}
+
+// fp32 x [rows][cols] (row stride ldx) -> bf16 hi + lo halves [rows][ld] (or, transposed, [cols][ld])
+extern "C" int bd_split_bf16(const float *x, int64_t rows, int64_t cols, int64_t ldx, int transpose, uint16_t *hi,
+                             uint16_t *lo, int64_t ld, bd_stream_t stream) {
+    if (rows < 1 || cols < 1 || ldx < cols || ld < (transpose ? rows : cols) || (rows + 31) / 32 > 65535 || !x ||
+        !hi || !lo)
+        return BD_ERR_INVALID;
+    dim3 grid(static_cast<unsigned>((cols + 31) / 32), static_cast<unsigned>((rows + 31) / 32));
+    auto *h = reinterpret_cast<__nv_bfloat16 *>(hi);
+    auto *l = reinterpret_cast<__nv_bfloat16 *>(lo);
+    if (transpose)
+        split_bf16_kernel<true><<<grid, 256, 0, stream>>>(x, rows, cols, ldx, h, l, ld);
+    else
+        split_bf16_kernel<false><<<grid, 256, 0, stream>>>(x, rows, cols, ldx, h, l, ld);
     BD_CHECK_LAUNCH();
     return BD_OK;
 }

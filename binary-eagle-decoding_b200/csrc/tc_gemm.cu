@@ -38,10 +38,14 @@ enum TcEpi : int {
     TC_W1A1_SWIGLU = 3,   // N tile = 128 gate + 128 up rows: h = silu(gate) * up, W1A1 values
     TC_F32 = 4,           // bf16 operands (kind::f16), fp32 accumulators: out = D
     TC_STE = 5,           // bf16 operands: out = (D * step) * 1[|latent| <= window] (+ per-warp partial sums)
+    TC_CE_STATS = 6,      // bf16 operands, D = logits: per (row, 128-column half tile) max and sum of exp; target logit
+    TC_CE_GRAD = 7,       // bf16 operands, D = logits: dl = w * (exp(D - lse) - onehot) as bf16 hi + lo halves
 };
 
 // K elements per 128-byte shared-memory row (one TMA box width) of the operand type.
-__host__ __device__ constexpr int tc_bf16(int epi) { return epi == TC_F32 || epi == TC_STE; }
+__host__ __device__ constexpr int tc_bf16(int epi) {
+    return epi == TC_F32 || epi == TC_STE || epi == TC_CE_STATS || epi == TC_CE_GRAD;
+}
 __host__ __device__ constexpr int tc_bk(int epi) { return tc_bf16(epi) ? 64 : 128; }
 
 struct TcArgs {
@@ -55,7 +59,8 @@ struct TcArgs {
     float *out;
     int32_t *out_i32;
     int32_t *flags;
-    int split_a;            // bf16 kinds: 2 = A given as hi + lo halves (second tensor map), 1 = one A
+    int parts;              // bf16 kinds: the product is a sum of 1-3 (A, B) operand pairs (split-bf16
+                            // halves), each a full K reduction, issued as one reduction of parts x K
     float *out_dot;         // TC_HE4: the exact integer dot as fp32 as well (optional)
     // TC_STE: the straight-through sign gradient of the latent [M][N] (row stride ld_latent)
     const float *latent;
@@ -63,6 +68,13 @@ struct TcArgs {
     const float *window;    // learned window (device scalar) or null: window_value
     float window_value;
     float *partials;        // optional [tiles][8 warps][2]: sum of out^2, sum over |w| > window of D * step * sign(w)
+    // TC_CE_STATS / TC_CE_GRAD (rows = labelled positions, columns = vocabulary)
+    const int32_t *labels;  // [M]
+    const float *row_w;     // [M] label weights (GRAD)
+    const float *row_lse;   // [M] log-sum-exp of each row (GRAD)
+    float *stats;           // [M][2 n_tiles][2]: max, sum of exp(D - max) per half tile (STATS)
+    float *target;          // [M] the label's logit (STATS)
+    __nv_bfloat16 *dl_hi, *dl_lo;  // [M][ld_out] (GRAD)
 };
 
 __device__ __forceinline__ uint32_t su32(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
@@ -130,7 +142,10 @@ __host__ __device__ constexpr uint32_t idesc_i8(int n) {
 template <int BN, int EPI>
 __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const __grid_constant__ CUtensorMap ma,
                                                          const __grid_constant__ CUtensorMap mb,
-                                                         const __grid_constant__ CUtensorMap ma2) {
+                                                         const __grid_constant__ CUtensorMap ma2,
+                                                         const __grid_constant__ CUtensorMap mb2,
+                                                         const __grid_constant__ CUtensorMap ma3,
+                                                         const __grid_constant__ CUtensorMap mb3) {
     extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sa = smem;                                // stages x 16 KB (tokens)
@@ -142,7 +157,7 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
     const int64_t tiles = a.m_tiles * a.n_tiles;
     constexpr int BKE = tc_bk(EPI);  // K elements per stage
     const int nk1 = static_cast<int>((a.K + BKE - 1) / BKE);
-    const int nk = nk1 * (a.split_a == 2 ? 2 : 1);  // the lo half of A follows the hi half along K
+    const int nk = nk1 * (a.parts > 1 ? a.parts : 1);  // part p covers k-blocks [p nk1, (p + 1) nk1)
     constexpr uint32_t kCols = 2 * BN;  // two accumulator buffers
     if (threadIdx.x == 0) {
         for (int s = 0; s < kTcStages; ++s) {
@@ -176,9 +191,9 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
                     const int s = it % kTcStages;
                     if (it >= kTcStages && !mb_wait(&empty[s], ((it / kTcStages) - 1) & 1, &abort_flag)) break;
                     mb_expect_tx(&full[s], (kTcBM + BN) * kTcBK);
-                    const int kc = k < nk1 ? k : k - nk1;
-                    tma_2d(sa + s * kTcBM * kTcBK, k < nk1 ? &ma : &ma2, &full[s], kc * BKE, m0);
-                    tma_2d(sb + s * BN * kTcBK, &mb, &full[s], kc * BKE, n0);
+                    const int part = k / nk1, kc = k - part * nk1;
+                    tma_2d(sa + s * kTcBM * kTcBK, part == 0 ? &ma : (part == 1 ? &ma2 : &ma3), &full[s], kc * BKE, m0);
+                    tma_2d(sb + s * BN * kTcBK, part == 0 ? &mb : (part == 1 ? &mb2 : &mb3), &full[s], kc * BKE, n0);
                 }
             }
             if (abort_flag) {  // let the loads already issued (stages it - S .. it - 1) land
@@ -261,6 +276,11 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
             // the same outputs (128-row blocks interleaved in the weight copy)
             const int64_t o_base = (EPI == TC_W1A1_SWIGLU ? (t / a.m_tiles) * (BN / 2) : (t / a.m_tiles) * BN) + half * HALF;
             float ss = 0.0f, sc = 0.0f;  // TC_STE partial sums of this thread, in column order
+            const bool ce = EPI == TC_CE_STATS || EPI == TC_CE_GRAD;
+            const int label = ce && live_row ? __ldg(a.labels + row) : -1;
+            const float rw = EPI == TC_CE_GRAD && live_row ? __ldg(a.row_w + row) : 0.0f;
+            const float lse = EPI == TC_CE_GRAD && live_row ? __ldg(a.row_lse + row) : 0.0f;
+            float run_max = -INFINITY, run_sum = 0.0f;  // TC_CE_STATS, over this thread's half tile
             for (int c = 0; c < HALF; c += 16) {
                 uint32_t v[16], u[16];
                 const uint32_t taddr = tmem + b * BN + (static_cast<uint32_t>(quarter * 32) << 16) + half * HALF + c;
@@ -283,7 +303,7 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
                 const bool full16 = o0 + 16 <= a.N;
                 // per-column parameters: the same 16 values for every lane (broadcast loads)
                 float s1[16], s2[16], md[16];
-                if (EPI != TC_RAW && EPI != TC_F32 && EPI != TC_STE) {
+                if (EPI != TC_RAW && EPI != TC_F32 && EPI != TC_STE && EPI != TC_CE_STATS && EPI != TC_CE_GRAD) {
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         const bool live = full16 || o0 + j < a.N;
@@ -313,6 +333,51 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
                     }
                 }
                 const int64_t idx = row * a.ld_out + o0;
+                if (EPI == TC_CE_STATS) {
+                    // online max and sum of exp over the live columns of this chunk
+                    float cmax = -INFINITY;
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        if (full16 || o0 + j < a.N) cmax = fmaxf(cmax, __uint_as_float(v[j]));
+                    const float m = fmaxf(run_max, cmax);
+                    float sum = run_max == -INFINITY ? 0.0f : run_sum * exp2f((run_max - m) * 1.4426950408889634f);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        if (full16 || o0 + j < a.N) sum += exp2f((__uint_as_float(v[j]) - m) * 1.4426950408889634f);
+                    run_max = m;
+                    run_sum = sum;
+                    if (label >= o0 && label < o0 + 16) a.target[row] = __uint_as_float(v[label - o0]);
+                    continue;
+                }
+                if (EPI == TC_CE_GRAD) {
+                    uint32_t hp[8] = {}, lp[8] = {};  // bf16 pairs, column 2 i in the low half
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const float p = exp2f((__uint_as_float(v[j]) - lse) * 1.4426950408889634f);
+                        const float d = __fmul_rn(rw, o0 + j == label ? __fsub_rn(p, 1.0f) : p);
+                        const __nv_bfloat16 h = __float2bfloat16_rn(d);
+                        const __nv_bfloat16 l = __float2bfloat16_rn(__fsub_rn(d, __bfloat162float(h)));
+                        hp[j >> 1] |= static_cast<uint32_t>(__bfloat16_as_ushort(h)) << (16 * (j & 1));
+                        lp[j >> 1] |= static_cast<uint32_t>(__bfloat16_as_ushort(l)) << (16 * (j & 1));
+                    }
+                    if (full16 && (a.ld_out & 7) == 0) {
+                        uint4 *ph = reinterpret_cast<uint4 *>(a.dl_hi + idx), *pl = reinterpret_cast<uint4 *>(a.dl_lo + idx);
+                        ph[0] = make_uint4(hp[0], hp[1], hp[2], hp[3]);
+                        ph[1] = make_uint4(hp[4], hp[5], hp[6], hp[7]);
+                        pl[0] = make_uint4(lp[0], lp[1], lp[2], lp[3]);
+                        pl[1] = make_uint4(lp[4], lp[5], lp[6], lp[7]);
+                    } else {
+                        uint16_t *qh = reinterpret_cast<uint16_t *>(a.dl_hi + idx);
+                        uint16_t *ql = reinterpret_cast<uint16_t *>(a.dl_lo + idx);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            if (o0 + j < a.N) {
+                                qh[j] = static_cast<uint16_t>(hp[j >> 1] >> (16 * (j & 1)));
+                                ql[j] = static_cast<uint16_t>(lp[j >> 1] >> (16 * (j & 1)));
+                            }
+                    }
+                    continue;
+                }
                 if (EPI == TC_STE) {
                     // mask by the straight-through window; the two sums the update needs
                     const float *lat = a.latent + row * a.ld_latent + o0;
@@ -356,6 +421,11 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
             if (lane == 0) mb_arrive(&acc_empty[b]);
+            if (EPI == TC_CE_STATS && live_row) {
+                float *st = a.stats + (row * (2 * a.n_tiles) + (t / a.m_tiles) * 2 + half) * 2;
+                st[0] = run_max;
+                st[1] = run_sum;
+            }
             if (EPI == TC_STE && a.partials) {  // fixed butterfly: deterministic per (tile, warp)
 #pragma unroll
                 for (int d = 16; d > 0; d >>= 1) {
@@ -422,16 +492,25 @@ static int sms_tc() {
     return n;
 }
 
+// Operands of a product of up to three parts: D = sum_p A_p . B_p^T (parts 2 and 3
+// optional; every A_p has the row stride ld_codes, every B_p the stride ld_w).
+struct TcParts {
+    const int8_t *a2 = nullptr, *b2 = nullptr, *a3 = nullptr, *b3 = nullptr;
+};
+
 template <int BN, int EPI>
 static int launch_tc_t(TcArgs a, const int8_t *codes, int64_t ld_codes, const int8_t *weights, int64_t w_rows,
-                       int64_t ld_w, cudaStream_t stream, const int8_t *codes_lo = nullptr) {
-    CUtensorMap ma, mb, ma2;
+                       int64_t ld_w, cudaStream_t stream, const TcParts &more = TcParts{}) {
+    CUtensorMap ma, mb, ma2, mb2, ma3, mb3;
     const bool bf16 = tc_bf16(EPI);
+    a.parts = more.a3 ? 3 : (more.a2 ? 2 : 1);
     if (!make_i8_map(&ma, codes, a.M, a.K, ld_codes, kTcBM, bf16) ||
         !make_i8_map(&mb, weights, w_rows, a.K, ld_w, BN, bf16) ||
-        !make_i8_map(&ma2, codes_lo ? codes_lo : codes, a.M, a.K, ld_codes, kTcBM, bf16))
+        !make_i8_map(&ma2, more.a2 ? more.a2 : codes, a.M, a.K, ld_codes, kTcBM, bf16) ||
+        !make_i8_map(&mb2, more.b2 ? more.b2 : weights, w_rows, a.K, ld_w, BN, bf16) ||
+        !make_i8_map(&ma3, more.a3 ? more.a3 : codes, a.M, a.K, ld_codes, kTcBM, bf16) ||
+        !make_i8_map(&mb3, more.b3 ? more.b3 : weights, w_rows, a.K, ld_w, BN, bf16))
         return BD_ERR_ALIGNMENT;
-    a.split_a = codes_lo ? 2 : 1;
     a.m_tiles = (a.M + kTcBM - 1) / kTcBM;
     a.n_tiles = (w_rows + BN - 1) / BN;
     const size_t smem = static_cast<size_t>(kTcStages) * (kTcBM + BN) * kTcBK + 1024;
@@ -440,7 +519,7 @@ static int launch_tc_t(TcArgs a, const int8_t *codes, int64_t ld_codes, const in
         return BD_ERR_LAUNCH;
     const int64_t tiles = a.m_tiles * a.n_tiles;
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>(tiles, sms_tc()));
-    kern<<<grid, 320, smem, stream>>>(a, ma, mb, ma2);
+    kern<<<grid, 320, smem, stream>>>(a, ma, mb, ma2, mb2, ma3, mb3);
     BD_CHECK_LAUNCH();
     return BD_OK;
 }
@@ -448,9 +527,10 @@ static int launch_tc_t(TcArgs a, const int8_t *codes, int64_t ld_codes, const in
 int64_t tc_tiles(int64_t m, int64_t n) { return (m + kTcBM - 1) / kTcBM * ((n + 255) / 256); }
 
 int launch_tc_gemm(int epi, const TcArgs &a, const int8_t *codes, int64_t ld_codes, const int8_t *weights,
-                   int64_t w_rows, int64_t ld_w, cudaStream_t stream, const int8_t *codes_lo = nullptr) {
+                   int64_t w_rows, int64_t ld_w, cudaStream_t stream, const TcParts &more = TcParts{}) {
     if (a.M < 1 || a.N < 1 || a.K < 1) return BD_ERR_INVALID;
-    if (codes_lo && epi != TC_F32 && epi != TC_STE) return BD_ERR_INVALID;
+    if ((more.a2 || more.a3) && !tc_bf16(epi)) return BD_ERR_INVALID;
+    if (more.a3 && !more.a2) return BD_ERR_INVALID;
     switch (epi) {
         case TC_RAW:
             return launch_tc_t<256, TC_RAW>(a, codes, ld_codes, weights, w_rows, ld_w, stream);
@@ -461,9 +541,13 @@ int launch_tc_gemm(int epi, const TcArgs &a, const int8_t *codes, int64_t ld_cod
         case TC_W1A1_SWIGLU:
             return launch_tc_t<256, TC_W1A1_SWIGLU>(a, codes, ld_codes, weights, w_rows, ld_w, stream);
         case TC_F32:
-            return launch_tc_t<256, TC_F32>(a, codes, ld_codes, weights, w_rows, ld_w, stream, codes_lo);
+            return launch_tc_t<256, TC_F32>(a, codes, ld_codes, weights, w_rows, ld_w, stream, more);
         case TC_STE:
-            return launch_tc_t<256, TC_STE>(a, codes, ld_codes, weights, w_rows, ld_w, stream, codes_lo);
+            return launch_tc_t<256, TC_STE>(a, codes, ld_codes, weights, w_rows, ld_w, stream, more);
+        case TC_CE_STATS:
+            return launch_tc_t<256, TC_CE_STATS>(a, codes, ld_codes, weights, w_rows, ld_w, stream, more);
+        case TC_CE_GRAD:
+            return launch_tc_t<256, TC_CE_GRAD>(a, codes, ld_codes, weights, w_rows, ld_w, stream, more);
         default:
             return BD_ERR_INVALID;
     }
@@ -655,9 +739,35 @@ extern "C" int bd_gemm_bf16_split(const uint16_t *a_hi, const uint16_t *a_lo, in
     t.K = k;
     t.ld_out = ldc;
     t.out = c;
+    TcParts more;
+    if (a_lo) {
+        more.a2 = reinterpret_cast<const int8_t *>(a_lo);
+        more.b2 = reinterpret_cast<const int8_t *>(b);
+    }
     return launch_tc_gemm(TC_F32, t, reinterpret_cast<const int8_t *>(a_hi), lda * 2,
-                          reinterpret_cast<const int8_t *>(b), n, ldb * 2, static_cast<cudaStream_t>(stream),
-                          reinterpret_cast<const int8_t *>(a_lo));
+                          reinterpret_cast<const int8_t *>(b), n, ldb * 2, static_cast<cudaStream_t>(stream), more);
+}
+
+extern "C" int bd_gemm_bf16_split3(const uint16_t *a_hi, const uint16_t *a_lo, int64_t m, int64_t k, int64_t lda,
+                                   const uint16_t *b_hi, const uint16_t *b_lo, int64_t n, int64_t ldb, float *c,
+                                   int64_t ldc, bd_stream_t stream) {
+    if (m < 1 || k < 1 || n < 1 || lda < k || ldb < k || ldc < n || !a_hi || !a_lo || !b_hi || !c)
+        return BD_ERR_INVALID;
+    TcArgs t{};
+    t.M = m;
+    t.N = n;
+    t.K = k;
+    t.ld_out = ldc;
+    t.out = c;
+    TcParts more;
+    more.a2 = reinterpret_cast<const int8_t *>(a_lo);
+    more.b2 = reinterpret_cast<const int8_t *>(b_hi);
+    if (b_lo) {
+        more.a3 = reinterpret_cast<const int8_t *>(a_hi);
+        more.b3 = reinterpret_cast<const int8_t *>(b_lo);
+    }
+    return launch_tc_gemm(TC_F32, t, reinterpret_cast<const int8_t *>(a_hi), lda * 2,
+                          reinterpret_cast<const int8_t *>(b_hi), n, ldb * 2, static_cast<cudaStream_t>(stream), more);
 }
 
 extern "C" int64_t bd_ste_weight_grad_partials(int64_t out_features, int64_t in_features) {
@@ -687,7 +797,124 @@ extern "C" int bd_ste_weight_grad(const uint16_t *grad_t_hi, const uint16_t *gra
     a.partials = partials;
     a.out = d_latent;
     a.flags = flags;
+    TcParts more;
+    if (grad_t_lo) {
+        more.a2 = reinterpret_cast<const int8_t *>(grad_t_lo);
+        more.b2 = reinterpret_cast<const int8_t *>(codes_t);
+    }
     return launch_tc_gemm(TC_STE, a, reinterpret_cast<const int8_t *>(grad_t_hi), ld_t * 2,
-                          reinterpret_cast<const int8_t *>(codes_t), in_features, ld_t * 2, stream,
-                          reinterpret_cast<const int8_t *>(grad_t_lo));
+                          reinterpret_cast<const int8_t *>(codes_t), in_features, ld_t * 2, stream, more);
+}
+
+// ------------------------------------------------------------------ fused cross-entropy head
+// (w1a1_eagle/numerical/worker.py:315-363: cross_entropy(linear(head, vocabulary)) per label,
+// weighted and summed); the logits are never written: one pass keeps per-row softmax
+// statistics, a second recomputes them into the gradient in place.
+
+__global__ void ce_reduce_kernel(const float *__restrict__ stats, const float *__restrict__ target, int64_t rows,
+                                 int64_t nsplit, const float *__restrict__ weights, float *__restrict__ lse_out,
+                                 float *__restrict__ loss_rows, int32_t *flags) {
+    const int warp = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    if (warp >= rows) return;
+    const float *st = stats + static_cast<int64_t>(warp) * nsplit * 2;
+    float m = -INFINITY;
+    for (int64_t i = lane; i < nsplit; i += 32) m = fmaxf(m, st[2 * i]);
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, d));
+    float s = 0.0f;
+    for (int64_t i = lane; i < nsplit; i += 32) {
+        const float mi = st[2 * i];
+        if (mi != -INFINITY) s = __fadd_rn(s, __fmul_rn(st[2 * i + 1], exp2f((mi - m) * 1.4426950408889634f)));
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, d));
+    if (lane == 0) {
+        const float lse = __fadd_rn(m, logf(s));
+        const float loss = __fsub_rn(lse, target[warp]);
+        if (!isfinite(loss)) set_flag(flags, BD_FLAG_NONFINITE_STATE);
+        lse_out[warp] = lse;
+        loss_rows[warp] = __fmul_rn(weights[warp], loss);
+    }
+}
+
+// total = sum of loss_rows in a fixed order (one block)
+__global__ void ce_total_kernel(const float *__restrict__ loss_rows, int64_t rows, float *__restrict__ total) {
+    __shared__ float part[256];
+    float s = 0.0f;
+    for (int64_t i = threadIdx.x; i < rows; i += 256) s = __fadd_rn(s, loss_rows[i]);
+    part[threadIdx.x] = s;
+    __syncthreads();
+    for (int w = 128; w > 0; w >>= 1) {
+        if (threadIdx.x < w) part[threadIdx.x] = __fadd_rn(part[threadIdx.x], part[threadIdx.x + w]);
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) total[0] = part[0];
+}
+
+extern "C" int64_t bd_loss_head_stats_count(int64_t rows, int64_t vocab) {
+    if (rows < 1 || vocab < 1) return 0;
+    return rows * 2 * ((vocab + 255) / 256) * 2;
+}
+
+extern "C" int bd_loss_head_forward(const uint16_t *h_hi, const uint16_t *h_lo, int64_t rows, int64_t hidden,
+                                    int64_t ld_h, const uint16_t *v_hi, const uint16_t *v_lo, int64_t vocab,
+                                    const int32_t *labels, const float *weights, float *stats, float *target,
+                                    float *lse, float *loss_rows, float *loss, int32_t *flags, bd_stream_t stream) {
+    if (rows < 1 || hidden < 1 || vocab < 1 || ld_h < hidden || (ld_h & 7) || !h_hi || !h_lo || !v_hi || !labels ||
+        !weights || !stats || !target || !lse || !loss_rows || !loss)
+        return BD_ERR_INVALID;
+    TcArgs a{};
+    a.M = rows;
+    a.N = vocab;
+    a.K = hidden;
+    a.ld_out = vocab;
+    a.labels = labels;
+    a.stats = stats;
+    a.target = target;
+    a.flags = flags;
+    TcParts more;
+    more.a2 = reinterpret_cast<const int8_t *>(h_lo);
+    more.b2 = reinterpret_cast<const int8_t *>(v_hi);
+    if (v_lo) {
+        more.a3 = reinterpret_cast<const int8_t *>(h_hi);
+        more.b3 = reinterpret_cast<const int8_t *>(v_lo);
+    }
+    int st = launch_tc_gemm(TC_CE_STATS, a, reinterpret_cast<const int8_t *>(h_hi), ld_h * 2,
+                            reinterpret_cast<const int8_t *>(v_hi), vocab, ld_h * 2, stream, more);
+    if (st) return st;
+    const int64_t nsplit = 2 * ((vocab + 255) / 256);
+    ce_reduce_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, stream>>>(stats, target, rows, nsplit, weights,
+                                                                                 lse, loss_rows, flags);
+    BD_CHECK_LAUNCH();
+    ce_total_kernel<<<1, 256, 0, stream>>>(loss_rows, rows, loss);
+    BD_CHECK_LAUNCH();
+    return BD_OK;
+}
+
+extern "C" int bd_loss_head_grad(const uint16_t *h_hi, const uint16_t *h_lo, int64_t rows, int64_t hidden,
+                                 int64_t ld_h, const uint16_t *v_hi, const uint16_t *v_lo, int64_t vocab,
+                                 const int32_t *labels, const float *weights, const float *lse, uint16_t *dl_hi,
+                                 uint16_t *dl_lo, int64_t ld_dl, bd_stream_t stream) {
+    if (rows < 1 || hidden < 1 || vocab < 1 || ld_h < hidden || (ld_h & 7) || ld_dl < vocab || (ld_dl & 7) || !h_hi ||
+        !h_lo || !v_hi || !labels || !weights || !lse || !dl_hi || !dl_lo)
+        return BD_ERR_INVALID;
+    TcArgs a{};
+    a.M = rows;
+    a.N = vocab;
+    a.K = hidden;
+    a.ld_out = ld_dl;
+    a.labels = labels;
+    a.row_w = weights;
+    a.row_lse = lse;
+    a.dl_hi = reinterpret_cast<__nv_bfloat16 *>(dl_hi);
+    a.dl_lo = reinterpret_cast<__nv_bfloat16 *>(dl_lo);
+    TcParts more;
+    more.a2 = reinterpret_cast<const int8_t *>(h_lo);
+    more.b2 = reinterpret_cast<const int8_t *>(v_hi);
+    if (v_lo) {
+        more.a3 = reinterpret_cast<const int8_t *>(h_hi);
+        more.b3 = reinterpret_cast<const int8_t *>(v_lo);
+    }
+    return launch_tc_gemm(TC_CE_GRAD, a, reinterpret_cast<const int8_t *>(h_hi), ld_h * 2,
+                          reinterpret_cast<const int8_t *>(v_hi), vocab, ld_h * 2, stream, more);
 }

@@ -130,22 +130,42 @@ def hard_sign(value: Tensor) -> Tensor:
     return _Sign.apply(value)
 
 
-def _bf16_split(value: Tensor) -> tuple[Tensor, Tensor]:
-    """fp32 ``value`` as bf16 hi + lo halves (value ~= hi + lo to ~16 bits)."""
-    hi = value.to(torch.bfloat16)
-    return hi, (value - hi.float()).to(torch.bfloat16)
+def _round8(n: int) -> int:
+    return (n + 7) // 8 * 8
+
+
+def _split(value: Tensor, transpose: bool = False) -> tuple[Tensor, Tensor, int]:
+    """fp32 ``value [rows, cols]`` as bf16 halves ``hi + lo`` (``bd_split_bf16``), row
+    stride a multiple of 8 (transposed: ``[cols, ld]``).  Returns ``(hi, lo, ld)``."""
+    v = value.reshape(-1, value.shape[-1]).float().contiguous()
+    rows, cols = v.shape
+    ld = _round8(rows if transpose else cols)
+    shape = (cols, ld) if transpose else (rows, ld)
+    hi = torch.empty(shape, dtype=torch.bfloat16, device=v.device)
+    lo = torch.empty_like(hi)
+    _lib.call("bd_split_bf16", v.data_ptr(), rows, cols, cols, int(transpose), hi.data_ptr(), lo.data_ptr(), ld,
+              _stream(v.device))
+    return hi, lo, ld
 
 
 class _FrozenOperand:
-    """bf16 hi + lo halves of a frozen fp32 operand ``[out, in]``, made once (the
-    buffer itself is never replaced or written).  ``lo`` is None when the operand
-    is exactly representable in bf16 (the drafter's bf16 checkpoints)."""
+    """bf16 hi + lo halves of a frozen fp32 operand ``[out, in]`` (and, for the input
+    gradient, of its transpose), made once; the buffer itself is never replaced
+    or written.  ``lo`` is None when the operand is exactly representable in
+    bf16 (the drafter's bf16 checkpoints)."""
 
     def __init__(self, operand: Tensor) -> None:
         self.source = operand
         self.version = operand._version
-        self.hi, lo = _bf16_split(operand.detach())
+        self.hi, lo, self.ld = _split(operand.detach())
         self.lo = lo if bool(lo.any()) else None
+        self._t: tuple[Tensor, Tensor | None, int] | None = None
+
+    def transposed(self) -> tuple[Tensor, Tensor | None, int]:
+        if self._t is None:
+            hi, lo, ld = _split(self.source.detach(), transpose=True)
+            self._t = (hi, lo if self.lo is not None else None, ld)
+        return self._t
 
     def valid_for(self, operand: Tensor) -> bool:
         return self.source is operand and self.version == operand._version
@@ -159,25 +179,29 @@ def _frozen_halves(owner, operand: Tensor) -> _FrozenOperand:
     return cache
 
 
-def _mm_split(a_hi: Tensor, a_lo: Tensor, b_hi: Tensor, b_lo: Tensor | None) -> Tensor:
-    """(a_hi + a_lo) @ (b_hi + b_lo) on bf16 tensor cores with fp32 accumulation,
-    leaving out only lo x lo (fp32-level accuracy: ~2^-16 relative per product)."""
-    out = torch.mm(a_hi, b_hi, out_dtype=torch.float32)
-    out += torch.mm(a_lo, b_hi, out_dtype=torch.float32)
-    if b_lo is not None:
-        out += torch.mm(a_hi, b_lo, out_dtype=torch.float32)
+def _product(x: Tensor, b_hi: Tensor, b_lo: Tensor | None, ld_b: int, n: int) -> Tensor:
+    """``x [m, k] @ (b_hi + b_lo)^T`` at fp32 accuracy on the tcgen05 tensor cores:
+    ``x`` split into bf16 halves, ``b`` given as halves ``[n, ld_b]``
+    (``bd_gemm_bf16_split3``: hi.hi + lo.hi + hi.lo, lo.lo left out)."""
+    m, k = x.shape
+    x_hi, x_lo, ld = _split(x)
+    if ld != ld_b:
+        raise ValueError("operand strides differ")
+    out = torch.empty((m, n), dtype=torch.float32, device=x.device)
+    _lib.call("bd_gemm_bf16_split3", x_hi.data_ptr(), x_lo.data_ptr(), m, k, ld, b_hi.data_ptr(),
+              None if b_lo is None else b_lo.data_ptr(), n, ld_b, out.data_ptr(), n, _stream(x.device))
     return out
 
 
 class _FrozenLinearFn(torch.autograd.Function):
-    """``linear(value, operand)`` of a frozen fp32 operand as split-bf16 tensor-core
-    GEMMs, forward and input gradient (the operand gets no gradient)."""
+    """``linear(value, operand)`` of a frozen fp32 operand on the tcgen05 tensor
+    cores (split-bf16 halves), forward and input gradient (the operand gets no
+    gradient)."""
 
     @staticmethod
     def forward(ctx, value, operand, halves):
         x = value.reshape(-1, value.shape[-1]).float()
-        x_hi, x_lo = _bf16_split(x)
-        y = _mm_split(x_hi, x_lo, halves.hi.t(), None if halves.lo is None else halves.lo.t())
+        y = _product(x, halves.hi, halves.lo, halves.ld, operand.shape[0])
         ctx.halves = halves
         ctx.in_shape = value.shape
         return y.reshape(*value.shape[:-1], operand.shape[0])
@@ -185,8 +209,8 @@ class _FrozenLinearFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad):
         g = grad.reshape(-1, grad.shape[-1]).float()
-        g_hi, g_lo = _bf16_split(g)
-        dx = _mm_split(g_hi, g_lo, ctx.halves.hi, ctx.halves.lo)
+        hi_t, lo_t, ld_t = ctx.halves.transposed()
+        dx = _product(g, hi_t, lo_t, ld_t, ctx.in_shape[-1])
         return dx.reshape(ctx.in_shape), None, None
 
 
@@ -194,10 +218,10 @@ def frozen_linear(value: Tensor, operand: Tensor, owner) -> Tensor:
     """``functional.linear(value, operand)`` for a frozen operand held by ``owner``
     (its bf16 halves are cached on the owner, outside its parameters and buffers).
 
-    CUDA tensors take the split-bf16 tensor-core GEMMs.  CPU tensors (host-side
+    CUDA tensors take the split-bf16 tcgen05 GEMMs.  CPU tensors (host-side
     checks of the loss head's bookkeeping; no kernel of this package runs on
     them, and the binary projections refuse them) get the reference's own fp32
-    ``linear``, since torch has no bf16 -> fp32 ``mm`` on the CPU."""
+    ``linear``."""
     if not value.is_cuda:
         return functional.linear(value, operand)
     return _FrozenLinearFn.apply(value, operand, _frozen_halves(owner, operand))
@@ -205,8 +229,8 @@ def frozen_linear(value: Tensor, operand: Tensor, owner) -> Tensor:
 
 class FrozenLinear(nn.Module):
     """A frozen dense projection; the operand is a buffer (``model.py:105-113``).
-    On the GPU the product runs on bf16 tensor cores with split operands
-    (``_mm_split``), within ~1e-5 of the fp32 product."""
+    On the GPU the product runs on the tcgen05 tensor cores with split-bf16
+    operands (``_product``), within ~1e-5 of the fp32 product."""
 
     operand: Tensor
 
@@ -219,10 +243,6 @@ class FrozenLinear(nn.Module):
 
 
 # --------------------------------------------------------------------------- binary projection
-
-
-def _round8(n: int) -> int:
-    return (n + 7) // 8 * 8
 
 
 class _ProjectionFn(torch.autograd.Function):
@@ -452,20 +472,65 @@ def clamp_latents(model: nn.Module) -> None:
 # --------------------------------------------------------------------------- layers
 
 
-def _attend(query: Tensor, keys: Tensor, values: Tensor, allowed: Tensor, head_dim: int) -> Tensor:
-    """Grouped-query attention.  ``query [n, kvh, g, d]``, ``keys/values [m, kvh, d]``,
-    ``allowed [n, m]`` -> ``[n, kvh * g * d]``."""
-    scores = torch.einsum("nhgd,mhd->hgnm", query, keys) / math.sqrt(head_dim)
-    scores = scores.masked_fill(~allowed[None, None], -torch.inf)
-    weights = functional.softmax(scores, -1)
-    return torch.einsum("hgnm,mhd->nhgd", weights, values).reshape(query.shape[0], -1)
+class _Stacked:
+    """Several frozen operands stacked along their output rows, as one frozen
+    operand (one split-bf16 GEMM computes all of them); rebuilt when any source
+    buffer is replaced or written."""
+
+    def __init__(self, operands: tuple[Tensor, ...]) -> None:
+        self.key = tuple((id(o), o._version) for o in operands)
+        self.operand = torch.cat([o.detach() for o in operands], 0)
+        self.sizes = tuple(o.shape[0] for o in operands)
+
+
+def _stacked(owner, name: str, operands: tuple[Tensor, ...]) -> _Stacked:
+    cache = owner.__dict__.get(name)
+    key = tuple((id(o), o._version) for o in operands)
+    if cache is None or cache.key != key:
+        cache = _Stacked(operands)
+        owner.__dict__[name] = cache
+    return cache
+
+
+def _stacked_linear(value: Tensor, owner, name: str, operands: tuple[Tensor, ...]) -> tuple[Tensor, ...]:
+    """``(linear(value, o) for o in operands)`` as one product of the stacked operands."""
+    stack = _stacked(owner, name, operands)
+    return frozen_linear(value, stack.operand, stack).split(stack.sizes, -1)
+
+
+def _window_attention(query: Tensor, ctx_k: Tensor, ctx_v: Tensor, slot_k: Tensor, slot_v: Tensor,
+                      ctx_allowed: Tensor, slot_allowed: Tensor | None, head_dim: int) -> Tensor:
+    """Grouped-query attention of a block of windows: ``query [W, k, kvh, g, d]`` over the
+    shared context ``ctx_k/ctx_v [L, kvh, d]`` (rows allowed by ``ctx_allowed
+    [W, k, L]``) and each window's own slots ``slot_k/slot_v [W, k, kvh, d]``
+    (``slot_allowed [k, k]`` or all), one softmax over both parts.  Returns
+    ``[W * k, kvh * g * d]``."""
+    windows, slots = query.shape[:2]
+    scale = 1.0 / math.sqrt(head_dim)
+    logits = torch.cat((torch.einsum("wshgd,lhd->whgsl", query, ctx_k),
+                        torch.einsum("wshgd,wthd->whgst", query, slot_k)), -1) * scale
+    mask = ctx_allowed[:, None, None]
+    if slot_allowed is None:
+        slot_mask = torch.ones((1, 1, 1, slots, slots), dtype=torch.bool, device=query.device)
+    else:
+        slot_mask = slot_allowed[None, None, None]
+    mask = torch.cat((mask.expand(-1, 1, 1, -1, -1), slot_mask.expand(windows, 1, 1, -1, -1)), -1)
+    weights = functional.softmax(logits.masked_fill(~mask, -torch.inf), -1)
+    ctx_w, slot_w = weights.split((ctx_k.shape[0], slots), -1)
+    out = torch.einsum("whgsl,lhd->wshgd", ctx_w, ctx_v) + torch.einsum("whgst,wthd->wshgd", slot_w, slot_v)
+    return out.reshape(windows * slots, -1)
 
 
 class Layer(nn.Module):
     """One drafter block (``model.py:172-274``): attention over cached context plus
-    the block's slots, then the binary SwiGLU ``down(silu(gate(n)) * up(n))``."""
+    the block's slots, then the binary SwiGLU ``down(silu(gate(n)) * up(n))``.
 
-    def __init__(self, tensors: dict[str, Tensor], prefix: str, geometry: Geometry) -> None:
+    The context keys and values of a block come from one stacked frozen product
+    (``k|v``), the slots' queries, keys and values from another (``q|k|v``);
+    the single-window ``forward`` is the window-block ``group`` with one window."""
+
+    def __init__(self, tensors: dict[str, Tensor], prefix: str, geometry: Geometry, window: float = 1.0,
+                 learned_window: bool = False) -> None:
         super().__init__()
         self.geometry = geometry
         self.attn_norm = nn.Parameter(tensors[prefix + "attn_norm.weight"].clone())
@@ -478,29 +543,26 @@ class Layer(nn.Module):
         self.output = FrozenLinear(tensors[prefix + "attn_output.weight"])
         gain = nn.Parameter(torch.zeros(geometry.hidden))
         clip = nn.Parameter(torch.tensor(0.0))
-        self.gate = Projection(tensors[prefix + "ffn_gate.weight"], 4, gain, clip)
-        self.up = Projection(tensors[prefix + "ffn_up.weight"], 4, gain, clip)
+        straight = dict(window=window, learned_window=learned_window)
+        self.gate = Projection(tensors[prefix + "ffn_gate.weight"], 4, gain, clip, **straight)
+        self.up = Projection(tensors[prefix + "ffn_up.weight"], 4, gain, clip, **straight)
         self.down = Projection(tensors[prefix + "ffn_down.weight"], 8, nn.Parameter(torch.zeros(geometry.intermediate)),
-                               nn.Parameter(torch.tensor(0.0)))
+                               nn.Parameter(torch.tensor(0.0)), **straight)
         self._packed: tuple[tuple, ops.PackedFFN] | None = None
+
+    def _heads(self, flat: Tensor, heads: int) -> Tensor:
+        return flat.reshape(-1, heads, self.geometry.head_dim)
+
+    def _keys(self, key: Tensor, positions: Tensor) -> Tensor:
+        """Head rms, rotary, fp16 storage of raw keys ``[n, kvh, d]`` (``model.py:196-200, 211-213``)."""
+        cfg = self.geometry
+        return cache_storage(rope(rms(key, self.k_norm, cfg.epsilon), positions, cfg.theta))
 
     def context(self, encoded: Tensor, positions: Tensor) -> tuple[Tensor, Tensor]:
         """Context keys (normed, rotated) and values through fp16 storage (``model.py:195-200``)."""
         cfg = self.geometry
-        key = self.key.forward(encoded).view(-1, cfg.kv_heads, cfg.head_dim)
-        value = self.value.forward(encoded).view(-1, cfg.kv_heads, cfg.head_dim)
-        key = rope(rms(key, self.k_norm, cfg.epsilon), positions, cfg.theta)
-        return cache_storage(key), cache_storage(value)
-
-    def _slot_qkv(self, state: Tensor, positions: Tensor):
-        cfg = self.geometry
-        norm = rms(state, self.attn_norm, cfg.epsilon)
-        query = self.query.forward(norm).view(-1, cfg.heads, cfg.head_dim)
-        key = self.key.forward(norm).view(-1, cfg.kv_heads, cfg.head_dim)
-        value = self.value.forward(norm).view(-1, cfg.kv_heads, cfg.head_dim)
-        query = rope(rms(query, self.q_norm, cfg.epsilon), positions, cfg.theta)
-        key = rope(rms(key, self.k_norm, cfg.epsilon), positions, cfg.theta)
-        return query, cache_storage(key), cache_storage(value)
+        key, value = _stacked_linear(encoded, self, "_kv", (self.key.operand, self.value.operand))
+        return self._keys(self._heads(key, cfg.kv_heads), positions), cache_storage(self._heads(value, cfg.kv_heads))
 
     def packed_ffn(self) -> ops.PackedFFN:
         """The SwiGLU operands in the fused decode block's layout (cached per parameter versions)."""
@@ -543,15 +605,10 @@ class Layer(nn.Module):
         return residual + self.down.forward(functional.silu(self.gate.forward(norm)) * self.up.forward(norm))
 
     def forward(self, state: Tensor, context: tuple[Tensor, Tensor], positions: Tensor, allowed: Tensor) -> Tensor:
-        """One block over a single window's slots (``model.py:202-223``)."""
-        cfg = self.geometry
-        query, key, value = self._slot_qkv(state, positions)
-        keys = torch.cat((context[0], key), 0)
-        values = torch.cat((context[1], value), 0)
-        groups = cfg.heads // cfg.kv_heads
-        query = query.view(positions.shape[0], cfg.kv_heads, groups, cfg.head_dim)
-        attended = _attend(query, keys, values, allowed, cfg.head_dim)
-        return self.feed_forward(state + self.output.forward(attended))
+        """One block over a single window's slots (``model.py:202-223``): ``allowed
+        [k, L + k]`` over the context keys and then the slots."""
+        length = context[0].shape[0]
+        return self.group(state, context, positions[None], allowed[None, :, :length], allowed[:, length:])
 
     def group(self, state: Tensor, context: tuple[Tensor, Tensor], positions: Tensor, allowed: Tensor,
               slot_allowed: Tensor | None) -> Tensor:
@@ -559,34 +616,31 @@ class Layer(nn.Module):
         context of length L, ``allowed [W, k, L]``, ``slot_allowed [k, k]`` or None."""
         cfg = self.geometry
         windows, slots = positions.shape
-        length = context[0].shape[0]
-        groups, kvh, d = cfg.heads // cfg.kv_heads, cfg.kv_heads, cfg.head_dim
-        query, key, value = self._slot_qkv(state, positions.reshape(-1))
-        query = query.view(windows, slots, kvh, groups, d)
-        key = key.view(windows, slots, kvh, d)
-        value = value.view(windows, slots, kvh, d)
-        scale = math.sqrt(d)
-        ctx_scores = torch.einsum("wshgd,lhd->whgsl", query, context[0]) / scale
-        ctx_scores = ctx_scores.masked_fill(~allowed[:, None, None], -torch.inf)
-        slot_scores = torch.einsum("wshgd,wthd->whgst", query, key) / scale
-        if slot_allowed is not None:
-            slot_scores = slot_scores.masked_fill(~slot_allowed, -torch.inf)
-        weights = functional.softmax(torch.cat((ctx_scores, slot_scores), -1), -1)
-        ctx_w, slot_w = weights.split((length, slots), -1)
-        attended = (torch.einsum("whgsl,lhd->wshgd", ctx_w, context[1])
-                    + torch.einsum("whgst,wthd->wshgd", slot_w, value))
-        attended = attended.reshape(windows * slots, -1)
-        return self.feed_forward(state + self.output.forward(attended))
+        groups = cfg.heads // cfg.kv_heads
+        norm = rms(state, self.attn_norm, cfg.epsilon)
+        query, key, value = _stacked_linear(norm, self, "_qkv",
+                                            (self.query.operand, self.key.operand, self.value.operand))
+        flat = positions.reshape(-1)
+        query = rope(rms(self._heads(query, cfg.heads), self.q_norm, cfg.epsilon), flat, cfg.theta)
+        key = self._keys(self._heads(key, cfg.kv_heads), flat)
+        value = cache_storage(self._heads(value, cfg.kv_heads))
+        attended = _window_attention(
+            query.view(windows, slots, cfg.kv_heads, groups, cfg.head_dim), context[0], context[1],
+            key.view(windows, slots, cfg.kv_heads, cfg.head_dim), value.view(windows, slots, cfg.kv_heads, cfg.head_dim),
+            allowed, slot_allowed, cfg.head_dim)
+        return self.feed_forward(state.reshape(windows * slots, -1) + self.output.forward(attended))
 
 
 class HE4(nn.Module):
     """The block drafter (``model.py:277-396``): fused target features, ``layers``
-    blocks, tied vocabulary head."""
+    blocks, tied vocabulary head.  ``window`` / ``learned_window`` set the
+    straight-through window of every binary projection (the reference's fixed
+    1.0 by default; see ``Projection``)."""
 
     vocabulary: Tensor
 
     def __init__(self, tensors: dict[str, Tensor], vocabulary: Tensor, mask: int,
-                 geometry: Geometry = Geometry()) -> None:
+                 geometry: Geometry = Geometry(), window: float = 1.0, learned_window: bool = False) -> None:
         super().__init__()
         self.geometry = geometry
         self.mask = mask
@@ -599,7 +653,8 @@ class HE4(nn.Module):
         self.fusion = FrozenLinear(tensors["fc.weight"])
         self.encoder_norm = nn.Parameter(tensors["enc.output_norm.weight"].clone())
         self.output_norm = nn.Parameter(tensors["output_norm.weight"].clone())
-        self.blocks = nn.ModuleList([Layer(tensors, f"blk.{i}.", geometry) for i in range(geometry.layers)])
+        self.blocks = nn.ModuleList([Layer(tensors, f"blk.{i}.", geometry, window, learned_window)
+                                     for i in range(geometry.layers)])
 
     def check(self, features: Tensor, tokens: tuple[int, ...], anchors: tuple[int, ...]) -> None:
         cfg = self.geometry
@@ -617,52 +672,57 @@ class HE4(nn.Module):
         return size
 
     def _encode(self, features: Tensor, length: int) -> Tensor:
-        device = self.vocabulary.device
-        fused = self.fusion.forward(features[:length].to(device).float())
+        """Fused, normalised target features of the first ``length`` positions (``model.py:349-351``)."""
+        fused = self.fusion.forward(features[:length].to(self.vocabulary.device).float())
         return rms(fused, self.encoder_norm, self.geometry.epsilon)
+
+    def _contexts(self, encoded: Tensor, positions: Tensor) -> list[tuple[Tensor, Tensor]]:
+        """Every layer's context keys and values (``Layer.context``), all layers' k|v rows
+        as one stacked frozen product of the encoded context."""
+        cfg = self.geometry
+        operands = tuple(o for b in self.blocks for o in (b.key.operand, b.value.operand))
+        parts = _stacked_linear(encoded, self, "_context_kv", operands)
+        out = []
+        for index, block in enumerate(self.blocks):
+            key, value = parts[2 * index], parts[2 * index + 1]
+            out.append((block._keys(block._heads(key, cfg.kv_heads), positions),
+                        cache_storage(block._heads(value, cfg.kv_heads))))
+        return out
 
     def group_hidden(self, features: Tensor, tokens: tuple[int, ...], anchors: tuple[int, ...],
                      slots: int | None = None) -> Tensor:
-        """Hidden states ``[W, k, hidden]`` of several windows (``model.py:329-367``)."""
+        """Hidden states ``[W, k, hidden]`` of several windows (``model.py:329-367``): each
+        window is its anchor token then ``k - 1`` mask slots at positions anchor ..
+        anchor + k - 1, attending to the context before its anchor (and, except in
+        the last layer, within the sliding window) and to its own slots."""
         self.check(features, tokens, anchors)
         cfg = self.geometry
         size = self.block(slots)
         device = self.vocabulary.device
-        starts = torch.tensor(anchors, device=device)
-        offsets = torch.arange(size, device=device)
-        positions = starts[:, None] + offsets[None, :]
-        last = max(anchors)
-        ctx_positions = torch.arange(last, device=device)
-        ids = torch.full((len(anchors), size), self.mask, device=device)
-        ids[:, 0] = torch.tensor([tokens[a] for a in anchors], device=device)
+        windows = len(anchors)
+        first = torch.tensor([tokens[a] for a in anchors], device=device)
+        ids = torch.cat((first[:, None], torch.full((windows, size - 1), self.mask, device=device)), 1)
         state = functional.embedding(ids.reshape(-1), self.vocabulary)
-        encoded = self._encode(features, last)
-        visible = ctx_positions[None, None, :] < starts[:, None, None]
-        local = visible & ((positions[:, :, None] - ctx_positions[None, None, :]).abs() < cfg.window)
-        slot_local = (offsets[:, None] - offsets[None, :]).abs() < cfg.window
+        start = torch.tensor(anchors, device=device)
+        offset = torch.arange(size, device=device)
+        positions = start[:, None] + offset[None, :]
+        length = max(anchors)
+        keys = torch.arange(length, device=device)
+        visible = keys[None, None, :] < start[:, None, None]
+        near = (positions[:, :, None] - keys[None, None, :]).abs() < cfg.window
+        slot_near = (offset[:, None] - offset[None, :]).abs() < cfg.window
+        contexts = self._contexts(self._encode(features, length), keys)
         for index, block in enumerate(self.blocks):
-            final = index == cfg.layers - 1
-            state = block.group(state, block.context(encoded, ctx_positions), positions,
-                                visible if final else local, None if final else slot_local)
-        return rms(state, self.output_norm, cfg.epsilon).view(len(anchors), size, cfg.hidden)
+            last = index == cfg.layers - 1
+            state = block.group(state, contexts[index], positions, visible if last else visible & near,
+                                None if last else slot_near)
+        return rms(state, self.output_norm, cfg.epsilon).view(windows, size, cfg.hidden)
 
     def forward(self, features: Tensor, tokens: tuple[int, ...], anchor: int, slots: int | None = None) -> Tensor:
-        """Logits ``[k, vocabulary]`` of one block anchored at ``anchor`` (``model.py:369-396``)."""
-        cfg = self.geometry
+        """Logits ``[k, vocabulary]`` of one block anchored at ``anchor`` (``model.py:369-396``):
+        the one-window case of ``group_hidden`` (the reference checks the two agree,
+        ``tests/numerical/test_model.py:586-604``), then the tied vocabulary head."""
         if type(anchor) is not int:
             raise ValueError("invalid model inputs")
-        self.check(features, tokens, (anchor,))
-        size = self.block(slots)
-        device = self.vocabulary.device
-        positions = torch.arange(anchor, anchor + size, device=device)
-        ctx_positions = torch.arange(anchor, device=device)
-        ids = torch.tensor((tokens[anchor],) + (self.mask,) * (size - 1), device=device)
-        state = functional.embedding(ids, self.vocabulary)
-        encoded = self._encode(features, anchor)
-        keys = torch.cat((ctx_positions, positions))
-        for index, block in enumerate(self.blocks):
-            allowed = torch.ones((size, anchor + size), dtype=torch.bool, device=device)
-            if index < cfg.layers - 1:
-                allowed &= (positions[:, None] - keys[None, :]).abs() < cfg.window
-            state = block.forward(state, block.context(encoded, ctx_positions), positions, allowed)
-        return frozen_linear(rms(state, self.output_norm, cfg.epsilon), self.vocabulary, self)
+        hidden = self.group_hidden(features, tokens, (anchor,), slots)[0]
+        return frozen_linear(hidden, self.vocabulary, self)

@@ -22,7 +22,7 @@ import torch.distributed as dist
 from torch import Tensor, nn
 
 from . import _lib, ops
-from .model import HE4, Projection, _bump, _need_cuda, _stream, frozen_linear
+from .model import HE4, Projection, _bump, _frozen_halves, _need_cuda, _split, _stream, frozen_linear
 
 PARAMETER_GROUPS = ("sign", "scale", "midpoint", "gain", "clip", "norm")
 HEAD_ROWS = 128
@@ -210,6 +210,67 @@ def average_gradients(parameters, group=None, bucket_bytes: int = 256 << 20) -> 
     flush()
 
 
+class GradientExchange:
+    """Data-parallel gradient average overlapped with the backward pass.
+
+    Each trainable parameter gets a post-accumulate hook; while the exchange is
+    ``armed`` (during the last backward pass of an update), every gradient that
+    becomes final joins the current bucket, and a full bucket (``bucket_bytes``
+    of fp32) is flattened and all-reduced asynchronously (NCCL on GPUs, gloo on
+    CPUs) while autograd goes on with the earlier layers.  ``finish()`` flushes
+    the last bucket, waits for every reduction and writes back the averages
+    (sum / world size), before the gradient-norm clip (``worker.py:372``).  All
+    ranks build the same graph, so their hooks fire in the same order and they
+    issue the same collectives."""
+
+    def __init__(self, parameters, group=None, bucket_bytes: int = 64 << 20) -> None:
+        self.group = group
+        self.bucket_bytes = bucket_bytes
+        self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+        self.armed = False
+        self._bucket: list[nn.Parameter] = []
+        self._size = 0
+        self._pending: list[tuple[object, Tensor, list[Tensor]]] = []
+        self.buckets = 0
+        self._hooks = [p.register_post_accumulate_grad_hook(self._ready) for p in parameters if p.requires_grad]
+
+    def _ready(self, parameter: nn.Parameter) -> None:
+        if not self.armed or self.world == 1 or parameter.grad is None:
+            return
+        self._bucket.append(parameter)
+        self._size += parameter.grad.numel() * 4
+        if self._size >= self.bucket_bytes:
+            self._flush()
+
+    def _flush(self) -> None:
+        if not self._bucket:
+            return
+        grads = [p.grad for p in self._bucket]
+        flat = torch.cat([g.reshape(-1) for g in grads])
+        handle = dist.all_reduce(flat, group=self.group, async_op=True)
+        self._pending.append((handle, flat, grads))
+        self._bucket, self._size = [], 0
+        self.buckets += 1
+
+    def finish(self) -> None:
+        self._flush()
+        for handle, flat, grads in self._pending:
+            handle.wait()
+            flat.div_(self.world)
+            offset = 0
+            for g in grads:
+                n = g.numel()
+                g.copy_(flat[offset:offset + n].view_as(g))
+                offset += n
+        self._pending = []
+        self.armed = False
+
+    def remove(self) -> None:
+        for h in self._hooks:
+            h.remove()
+        self._hooks = []
+
+
 # --------------------------------------------------------------------------- one update
 
 
@@ -239,19 +300,64 @@ def group_loss(model: HE4, features: Tensor, tokens: tuple[int, ...], windows: t
                           device=device)
     weights = (label_weights(lengths, positions) * scale).to(device)
     selected = hidden.view(-1, hidden.shape[-1]).index_select(0, rows)
-    head = selected.detach().requires_grad_()
-    total = torch.zeros((), device=device)
-    for start in range(0, labels.numel(), HEAD_ROWS):
-        end = start + HEAD_ROWS
-        logits = frozen_linear(head[start:end], model.vocabulary, model)
-        losses = torch.nn.functional.cross_entropy(logits, labels[start:end], reduction="none")
-        loss = (losses * weights[start:end]).sum()
-        torch.autograd.backward(loss)
-        total = total + loss.detach()
-    if not bool(torch.isfinite(total)) or head.grad is None:
-        raise ValueError("nonfinite loss")
-    torch.autograd.backward(selected, head.grad)
+    if not selected.is_cuda:
+        # host-side bookkeeping checks only: the reference's own chunked expression
+        head = selected.detach().requires_grad_()
+        total = torch.zeros((), device=device)
+        for start in range(0, labels.numel(), HEAD_ROWS):
+            end = start + HEAD_ROWS
+            logits = frozen_linear(head[start:end], model.vocabulary, model)
+            losses = torch.nn.functional.cross_entropy(logits, labels[start:end], reduction="none")
+            loss = (losses * weights[start:end]).sum()
+            torch.autograd.backward(loss)
+            total = total + loss.detach()
+        if not bool(torch.isfinite(total)) or head.grad is None:
+            raise ValueError("nonfinite loss")
+        torch.autograd.backward(selected, head.grad)
+        return total
+    total, d_head = loss_head(selected.detach(), model, labels, weights)
+    torch.autograd.backward(selected, d_head)
     return total
+
+
+def loss_head(head: Tensor, model: HE4, labels: Tensor, weights: Tensor) -> tuple[Tensor, Tensor]:
+    """``sum_r w_r cross_entropy(head_r . vocabulary^T, label_r)`` and its gradient with
+    respect to ``head`` (``worker.py:350-359``), on the tcgen05 tensor cores
+    without writing the logits: ``bd_loss_head_forward`` keeps per-row softmax
+    statistics in the GEMM epilogue, ``bd_loss_head_grad`` recomputes the logits
+    into ``w (softmax - onehot)`` as bf16 halves, and one split GEMM with the
+    transposed vocabulary gives the gradient.  Raises ``ValueError("nonfinite
+    loss")`` like the reference (``worker.py:360-361``)."""
+    device = _need_cuda(head)
+    lib = _lib.load()
+    halves = _frozen_halves(model, model.vocabulary)
+    rows, hidden = head.shape
+    vocab = model.vocabulary.shape[0]
+    h_hi, h_lo, ld_h = _split(head)
+    lab = labels.to(device=device, dtype=torch.int32).contiguous()
+    w = weights.to(device=device, dtype=torch.float32).contiguous()
+    stats = torch.empty(int(lib.bd_loss_head_stats_count(rows, vocab)), dtype=torch.float32, device=device)
+    target = torch.empty(rows, dtype=torch.float32, device=device)
+    lse = torch.empty(rows, dtype=torch.float32, device=device)
+    loss_rows = torch.empty(rows, dtype=torch.float32, device=device)
+    total = torch.empty(1, dtype=torch.float32, device=device)
+    flags = ops.Flags(device)
+    stream = _stream(device)
+    v_lo = None if halves.lo is None else halves.lo.data_ptr()
+    _lib.call("bd_loss_head_forward", h_hi.data_ptr(), h_lo.data_ptr(), rows, hidden, ld_h, halves.hi.data_ptr(), v_lo,
+              vocab, lab.data_ptr(), w.data_ptr(), stats.data_ptr(), target.data_ptr(), lse.data_ptr(),
+              loss_rows.data_ptr(), total.data_ptr(), flags.ptr, stream)
+    if int(flags.tensor.item()):
+        raise ValueError("nonfinite loss")
+    hi_t, lo_t, ld_v = halves.transposed()
+    dl_hi = torch.empty((rows, ld_v), dtype=torch.bfloat16, device=device)
+    dl_lo = torch.empty_like(dl_hi)
+    _lib.call("bd_loss_head_grad", h_hi.data_ptr(), h_lo.data_ptr(), rows, hidden, ld_h, halves.hi.data_ptr(), v_lo,
+              vocab, lab.data_ptr(), w.data_ptr(), lse.data_ptr(), dl_hi.data_ptr(), dl_lo.data_ptr(), ld_v, stream)
+    d_head = torch.empty((rows, hidden), dtype=torch.float32, device=device)
+    _lib.call("bd_gemm_bf16_split3", dl_hi.data_ptr(), dl_lo.data_ptr(), rows, vocab, ld_v, hi_t.data_ptr(),
+              None if lo_t is None else lo_t.data_ptr(), hidden, ld_v, d_head.data_ptr(), hidden, stream)
+    return total.reshape(()), d_head
 
 
 def update(model: HE4, optimizer: BitAdamW, features: Tensor, tokens: tuple[int, ...], windows: tuple[Window, ...],

@@ -494,6 +494,41 @@ int bd_codes_transpose_bf16(const int8_t *codes, int64_t rows, int64_t cols, int
                             int64_t ld_t, bd_stream_t stream);
 int bd_gemm_bf16_split(const uint16_t *a_hi, const uint16_t *a_lo, int64_t m, int64_t k, int64_t lda,
                        const uint16_t *b, int64_t n, int64_t ldb, float *c, int64_t ldc, bd_stream_t stream);
+
+/* fp32-accurate products of frozen fp32 operands on the bf16 tensor cores, for
+ * FrozenLinear (w1a1_eagle/model.py:105-113) and the tied vocabulary head
+ * forward and input gradient: each fp32 operand is split into bf16 halves
+ * hi + lo (bd_split_bf16, optionally transposed to K-major), and
+ * bd_gemm_bf16_split3 computes c = a_hi b_hi^T + a_lo b_hi^T + a_hi b_lo^T in
+ * fp32 (lo x lo is left out: about 2^-16 relative per product; b_lo NULL for a
+ * bf16-exact b) as one tcgen05 reduction of two or three times K. */
+int bd_split_bf16(const float *x, int64_t rows, int64_t cols, int64_t ldx, int transpose, uint16_t *hi, uint16_t *lo,
+                  int64_t ld, bd_stream_t stream);
+
+/* The loss head of TensorWorker.group_loss (w1a1_eagle/numerical/worker.py:315-363):
+ * loss = sum_r w[r] * (logsumexp_v(h[r] . vocab[v]) - h[r] . vocab[labels[r]]),
+ * with h and the frozen vocabulary as bf16 halves (hi, lo; v_lo NULL for a
+ * bf16-exact vocabulary), the products on tcgen05 at fp32 accuracy, and the
+ * logits never written to memory:
+ * bd_loss_head_forward: per-row softmax statistics in the GEMM's epilogue
+ *   (stats: bd_loss_head_stats_count(rows, vocab) floats), then lse[r],
+ *   loss_rows[r] = w[r] (lse - target logit) and their fixed-order sum *loss;
+ *   BD_FLAG_NONFINITE_STATE for a non-finite row loss ("nonfinite loss").
+ * bd_loss_head_grad: the logits recomputed into dLoss/dlogits = w (softmax -
+ *   onehot) in place, as bf16 halves [rows][ld_dl]; dLoss/dh is then
+ *   bd_gemm_bf16_split3 of those halves with the transposed vocabulary halves. */
+int64_t bd_loss_head_stats_count(int64_t rows, int64_t vocab);
+int bd_loss_head_forward(const uint16_t *h_hi, const uint16_t *h_lo, int64_t rows, int64_t hidden, int64_t ld_h,
+                         const uint16_t *v_hi, const uint16_t *v_lo, int64_t vocab, const int32_t *labels,
+                         const float *weights, float *stats, float *target, float *lse, float *loss_rows, float *loss,
+                         int32_t *flags, bd_stream_t stream);
+int bd_loss_head_grad(const uint16_t *h_hi, const uint16_t *h_lo, int64_t rows, int64_t hidden, int64_t ld_h,
+                      const uint16_t *v_hi, const uint16_t *v_lo, int64_t vocab, const int32_t *labels,
+                      const float *weights, const float *lse, uint16_t *dl_hi, uint16_t *dl_lo, int64_t ld_dl,
+                      bd_stream_t stream);
+int bd_gemm_bf16_split3(const uint16_t *a_hi, const uint16_t *a_lo, int64_t m, int64_t k, int64_t lda,
+                        const uint16_t *b_hi, const uint16_t *b_lo, int64_t n, int64_t ldb, float *c, int64_t ldc,
+                        bd_stream_t stream);
 int64_t bd_ste_weight_grad_partials(int64_t out_features, int64_t in_features);
 int bd_ste_weight_grad(const uint16_t *grad_t_hi, const uint16_t *grad_t_lo, int64_t out_features, int64_t tokens,
                        int64_t ld_t, const uint16_t *codes_t, int64_t in_features, const float *latent,

@@ -313,3 +313,37 @@ def test_group_loss_matches_reference_loss_and_gradients(bd, case):
     num = sum(float(np.square(got[n].astype(np.float64) - want[n]).sum()) for n in want)
     den = sum(float(np.square(want[n].astype(np.float64)).sum()) for n in want)
     assert math.sqrt(num / den) <= GROUP_GRAD_RTOL
+
+
+@pytest.mark.parametrize("vocab_bf16", [False, True])
+def test_loss_head_against_fp64(bd, vocab_bf16):
+    """The fused cross-entropy head (tcgen05 products of split-bf16 operands, the
+    logits never written) against a float64 evaluation of the reference's
+    weighted cross_entropy(linear(head, vocabulary)) and its gradient."""
+    qat = submodule("qat")
+    g = torch.Generator().manual_seed(21)
+    rows, hidden, vocab = 300, 2560, 50000
+    vocabulary = torch.randn((vocab, hidden), generator=g) * 0.02
+    if vocab_bf16:
+        vocabulary = vocabulary.to(torch.bfloat16).float()
+    head = torch.randn((rows, hidden), generator=g)
+    labels = torch.randint(0, vocab, (rows,), generator=g)
+    weights = torch.rand(rows, generator=g) / rows
+
+    class Owner(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.register_buffer("vocabulary", vocabulary.to(DEV))
+
+    owner = Owner()
+    loss, d_head = qat.loss_head(head.to(DEV), owner, labels.to(DEV), weights.to(DEV))
+    h64, v64 = head.double().to(DEV), vocabulary.double().to(DEV)
+    logits = h64 @ v64.T
+    lse = torch.logsumexp(logits, -1)
+    want = (weights.double().to(DEV) * (lse - logits[torch.arange(rows), labels.to(DEV)])).sum()
+    p = torch.softmax(logits, -1)
+    p[torch.arange(rows), labels.to(DEV)] -= 1
+    want_d = (p * weights.double().to(DEV)[:, None]) @ v64
+    assert abs(float(loss) - float(want)) <= 1e-5 * abs(float(want))
+    err = float((d_head.double() - want_d).norm() / want_d.norm())
+    assert err < 1e-4, err

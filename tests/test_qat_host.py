@@ -117,6 +117,50 @@ def test_average_gradients_two_gloo_ranks(qat):
             assert torch.all(g == 1.5 * (i + 1)), (rank, i)
 
 
+def _exchange_rank_main(rank, world, port, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        qat = submodule("qat")
+        torch.manual_seed(0)
+        model = nn.Sequential(nn.Linear(6, 5), nn.Tanh(), nn.Linear(5, 3))
+        params = list(model.parameters())
+        exchange = qat.GradientExchange(params, bucket_bytes=32)  # several buckets
+        x = torch.randn(4, 6, generator=torch.Generator().manual_seed(10 + rank))
+        for step in range(2):  # two backward passes; only the last one is exchanged
+            exchange.armed = step == 1
+            model(x * (step + 1)).square().sum().backward()
+        exchange.finish()
+        out[rank] = ([p.grad.clone() for p in params], exchange.buckets)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gradient_exchange_overlapped_two_gloo_ranks(qat):
+    """The hook-driven exchange equals the average of the ranks' accumulated
+    gradients, reduced in several buckets during the last backward pass."""
+    port = _free_port()
+    manager = mp.Manager()
+    out = manager.dict()
+    mp.spawn(_exchange_rank_main, args=(2, port, out), nprocs=2, join=True)
+    torch.manual_seed(0)
+    model = nn.Sequential(nn.Linear(6, 5), nn.Tanh(), nn.Linear(5, 3))
+    expected = [torch.zeros_like(p) for p in model.parameters()]
+    for rank in range(2):
+        model.zero_grad()
+        x = torch.randn(4, 6, generator=torch.Generator().manual_seed(10 + rank))
+        for step in range(2):
+            model(x * (step + 1)).square().sum().backward()
+        for e, p in zip(expected, model.parameters()):
+            e += p.grad / 2
+    for rank in range(2):
+        grads, buckets = out[rank]
+        assert buckets >= 2
+        for g, e in zip(grads, expected):
+            torch.testing.assert_close(g, e)
+
+
 def test_average_gradients_without_process_group_is_a_no_op(qat):
     p = nn.Parameter(torch.zeros(3))
     p.grad = torch.ones(3)
