@@ -560,6 +560,7 @@ def workload_ffn(args, pkg, device) -> list[dict]:
     algorithmic = 3 * F * H // 8 + (2 * F + H) * 4 + 2 * T * H * 4
     lines = []
     for mode, fn in (("he4", lambda i: ops.ffn_he4(x, ffns[i % sets], flags=flags)),
+                     ("he4_clusters", lambda i: ops.ffn_he4(x, ffns[i % sets], flags=flags, fused=True)),
                      ("w1", lambda i: ops.ffn_w1(x, ffns[i % sets], flags=flags)),
                      ("w1a1", lambda i: ops.ffn_w1a1(x, ffns[i % sets], flags=flags))):
         us = _graph_us(fn, sets, max(args.steps // 40, 20))
@@ -571,23 +572,34 @@ def workload_ffn(args, pkg, device) -> list[dict]:
     return lines
 
 
-def workload_w1a1(args, pkg, device) -> list[dict]:
-    """Config 3: W1A1 SwiGLU block at M = 1024 (64 requests x 16 draft tokens)."""
+def workload_w1a1(args, pkg, device, world: int = 1) -> list[dict]:
+    """Config 3: W1A1 SwiGLU block at M = 1024 (64 requests x 16 draft tokens) per GPU;
+    under torchrun every rank serves its own 64 requests (data parallel by
+    request, no collective on the data path), time = max over ranks."""
     ops = pkg.ops
     H, F, M = 2560, 9728, 1024
     g = torch.Generator(device=device).manual_seed(4)
     gate, up, down = (torch.randn(s, generator=g, device=device) * 0.02 for s in ((F, H), (F, H), (H, F)))
     ffn = ops.pack_ffn(gate, up, down, large=True)
-    x = torch.randn((M, H), generator=g, device=device)
+    x = torch.randn((M, H), generator=torch.Generator(device=device).manual_seed(40 + (device.index or 0)),
+                    device=device)
     flags = ops.Flags(device)
     for _ in range(3):
         ops.ffn_w1a1(x, ffn, flags=flags)
     torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
     us = _events_us(lambda: ops.ffn_w1a1(x, ffn, flags=flags), max(args.steps // 200, 5))
     flags.check()
+    if world > 1:
+        t = torch.tensor([us], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        us = float(t.item())
     macs = 3 * M * F * H
-    return [{"workload": "W1A1 SwiGLU block, M = 1024, 2560x9728x2560", "metric": "+-1 TOP/s (MAC = 2 ops)",
-             "value": 2 * macs / (us * 1e-6) / 1e12, "unit": "TOP/s", "us_per_ffn": us}]
+    return [{"workload": f"W1A1 SwiGLU block, M = 1024 per GPU (64 requests x 16 tokens), 2560x9728x2560, "
+                         f"{world} GPU(s)", "metric": "+-1 TOP/s (MAC = 2 ops), summed over GPUs",
+             "value": world * 2 * macs / (us * 1e-6) / 1e12, "unit": "TOP/s", "us_per_ffn": us, "n_gpus": world,
+             "requests_per_s": world * 64 / (us * 1e-6)}]
 
 
 def workload_accept(args, pkg, device) -> list[dict]:
@@ -782,7 +794,7 @@ def run_workload(args, rank: int, world: int, local_rank: int) -> None:
     if args.workload == "ffn":
         lines = workload_ffn(args, pkg, device)
     elif args.workload == "w1a1":
-        lines = workload_w1a1(args, pkg, device)
+        lines = workload_w1a1(args, pkg, device, world)
     elif args.workload == "accept":
         lines = workload_accept(args, pkg, device)
     elif args.workload == "ingest":

@@ -503,18 +503,19 @@ def _window_attention(query: Tensor, ctx_k: Tensor, ctx_v: Tensor, slot_k: Tenso
     """Grouped-query attention of a block of windows: ``query [W, k, kvh, g, d]`` over the
     shared context ``ctx_k/ctx_v [L, kvh, d]`` (rows allowed by ``ctx_allowed
     [W, k, L]``) and each window's own slots ``slot_k/slot_v [W, k, kvh, d]``
-    (``slot_allowed [k, k]`` or all), one softmax over both parts.  Returns
+    (``slot_allowed [k, k]`` or all; both masks broadcast), one softmax over both parts.  Returns
     ``[W * k, kvh * g * d]``."""
     windows, slots = query.shape[:2]
     scale = 1.0 / math.sqrt(head_dim)
     logits = torch.cat((torch.einsum("wshgd,lhd->whgsl", query, ctx_k),
                         torch.einsum("wshgd,wthd->whgst", query, slot_k)), -1) * scale
-    mask = ctx_allowed[:, None, None]
+    length = ctx_k.shape[0]
+    ctx_mask = ctx_allowed.expand(windows, slots, length)[:, None, None]
     if slot_allowed is None:
-        slot_mask = torch.ones((1, 1, 1, slots, slots), dtype=torch.bool, device=query.device)
+        slot_mask = torch.ones((windows, 1, 1, slots, slots), dtype=torch.bool, device=query.device)
     else:
-        slot_mask = slot_allowed[None, None, None]
-    mask = torch.cat((mask.expand(-1, 1, 1, -1, -1), slot_mask.expand(windows, 1, 1, -1, -1)), -1)
+        slot_mask = slot_allowed.expand(slots, slots)[None, None, None].expand(windows, 1, 1, slots, slots)
+    mask = torch.cat((ctx_mask, slot_mask), -1)
     weights = functional.softmax(logits.masked_fill(~mask, -torch.inf), -1)
     ctx_w, slot_w = weights.split((ctx_k.shape[0], slots), -1)
     out = torch.einsum("whgsl,lhd->wshgd", ctx_w, ctx_v) + torch.einsum("whgst,wthd->wshgd", slot_w, slot_v)
