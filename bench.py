@@ -749,7 +749,7 @@ def workload_qat(args, pkg, device, rank: int, world: int) -> list[dict]:
         opt.zero_grad()
         for i, (feats, tokens, windows) in enumerate(samples):
             exchange.armed = i == len(samples) - 1
-            qat.group_loss(model, feats, tokens, windows, scale=1.0 / seqs)
+            qat.group_loss_deferred(model, feats, tokens, windows, scale=1.0 / seqs)
         exchange.finish()
         _, coef = qat.clip_grad_norm(params, 1.0)
         opt.step(coef)

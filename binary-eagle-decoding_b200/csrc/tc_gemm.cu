@@ -381,10 +381,24 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
                 if (EPI == TC_STE) {
                     // mask by the straight-through window; the two sums the update needs
                     const float *lat = a.latent + row * a.ld_latent + o0;
+                    float wl[16];
+                    if (full16 && (a.ld_latent & 3) == 0 && (reinterpret_cast<uintptr_t>(a.latent) & 15) == 0) {
+#pragma unroll
+                        for (int j = 0; j < 16; j += 4) {
+                            const float4 q4 = __ldg(reinterpret_cast<const float4 *>(lat + j));
+                            wl[j] = q4.x;
+                            wl[j + 1] = q4.y;
+                            wl[j + 2] = q4.z;
+                            wl[j + 3] = q4.w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) wl[j] = (full16 || o0 + j < a.N) ? __ldg(lat + j) : 0.0f;
+                    }
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         if (!(full16 || o0 + j < a.N)) continue;
-                        const float w = lat[j];
+                        const float w = wl[j];
                         const bool inside = fabsf(w) <= ste_window;
                         if (!inside) sc = __fadd_rn(sc, w >= 0.0f ? y[j] : -y[j]);
                         y[j] = inside ? y[j] : 0.0f;
@@ -392,9 +406,17 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
                     }
                 }
                 if (EPI == TC_HE4 && a.out_dot) {
+                    if (full16 && vec_out && (reinterpret_cast<uintptr_t>(a.out_dot) & 15) == 0) {
 #pragma unroll
-                    for (int j = 0; j < 16; ++j)
-                        if (full16 || o0 + j < a.N) a.out_dot[idx + j] = static_cast<float>(di[j]);
+                        for (int j = 0; j < 16; j += 4)
+                            *reinterpret_cast<float4 *>(a.out_dot + idx + j) =
+                                make_float4(static_cast<float>(di[j]), static_cast<float>(di[j + 1]),
+                                            static_cast<float>(di[j + 2]), static_cast<float>(di[j + 3]));
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            if (full16 || o0 + j < a.N) a.out_dot[idx + j] = static_cast<float>(di[j]);
+                    }
                 }
                 if (EPI == TC_HE4 && a.residual) {
 #pragma unroll

@@ -28,6 +28,7 @@ from torch.nn import functional
 from . import _lib, ops
 
 MAX_DECODE_ROWS = ops.MAX_DECODE_TOKENS
+_DEFERRED: list[ops.Flags] = []  # flags words of the active deferred_checks contexts
 
 
 @dataclass(frozen=True)
@@ -78,11 +79,24 @@ def rope(value: Tensor, positions: Tensor, theta: float) -> Tensor:
 
 
 def cache_storage(value: Tensor) -> Tensor:
-    """Round through fp16 storage with a straight-through gradient (``model.py:98-102``)."""
+    """Round through fp16 storage with a straight-through gradient (``model.py:98-102``).
+    Inside ``deferred_checks`` an overflow is recorded on the device and raised
+    when the context ends."""
     rounded = value.half().float()
-    if not bool(torch.isfinite(rounded).all()):
+    if _DEFERRED and value.is_cuda and _DEFERRED[-1].tensor.device == value.device:
+        flags = _DEFERRED[-1].tensor
+        flags.bitwise_or_((~torch.isfinite(rounded)).any().to(torch.int32) * _lib.FLAG_CACHE_OVERFLOW)
+    elif not bool(torch.isfinite(rounded).all()):
         raise ValueError("F16 cache storage overflow")
     return value + (rounded - value).detach()
+
+
+def _to_device(values: list[int], device: torch.device) -> Tensor:
+    """A small int64 tensor on ``device`` without a host synchronisation (pinned copy)."""
+    host = torch.tensor(values, dtype=torch.int64)
+    if device.type != "cuda":
+        return host.to(device)
+    return host.pin_memory().to(device, non_blocking=True)
 
 
 def _need_cuda(t: Tensor) -> torch.device:
@@ -93,6 +107,32 @@ def _need_cuda(t: Tensor) -> torch.device:
 
 def _stream(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
+
+
+class deferred_checks:
+    """Within this context the projections OR their device error bits into one
+    flags word instead of reading them back after every launch (each read is a
+    host synchronisation); leaving the context reads it once and raises the same
+    ``ValueError`` / ``RuntimeError`` the immediate checks would have raised."""
+
+    def __init__(self, device: torch.device) -> None:
+        self.flags = ops.Flags(device)
+
+    def __enter__(self) -> "deferred_checks":
+        _DEFERRED.append(self.flags)
+        return self
+
+    def __exit__(self, *exc) -> None:
+        _DEFERRED.remove(self.flags)
+        if exc[0] is None:
+            self.flags.check()
+
+
+def _flags(device: torch.device) -> tuple[ops.Flags, bool]:
+    """The flags word to use and whether to check it right away."""
+    if _DEFERRED and _DEFERRED[-1].tensor.device == device:
+        return _DEFERRED[-1], False
+    return ops.Flags(device), True
 
 
 def _bump(t: Tensor) -> None:
@@ -272,20 +312,22 @@ class _ProjectionFn(torch.autograd.Function):
         gain = log_gain.detach().exp().contiguous()
         bound = log_clip.detach().exp().reshape(1).contiguous()
         stream = _stream(device)
-        flags = ops.Flags(device)
+        flags, now = _flags(device)
         ld = int(lib.bd_i8_ld(inner))
         codes = torch.empty((tokens, ld), dtype=torch.int8, device=device)
         sums = torch.empty(tokens, dtype=torch.int32, device=device)
         _lib.call("bd_quantize_rows_i8", x.data_ptr(), tokens, inner, gain.data_ptr(), bound.data_ptr(), bits,
                   codes.data_ptr(), ld, sums.data_ptr(), flags.ptr, stream)
-        flags.check()
+        if now:
+            flags.check()
         signs = module.signs_i8()
         y = torch.empty((tokens, outer), dtype=torch.float32, device=device)
         dot = torch.empty((tokens, outer), dtype=torch.float32, device=device)
         _lib.call("bd_projection_he4_tc", codes.data_ptr(), ld, sums.data_ptr(), tokens, inner, signs.data_ptr(), outer,
                   scale.detach().contiguous().data_ptr(), midpoint.detach().contiguous().data_ptr(), bound.data_ptr(),
                   bits, None, y.data_ptr(), dot.data_ptr(), flags.ptr, stream)
-        flags.check()
+        if now:
+            flags.check()
         window = None if log_window is None else log_window.detach().exp().reshape(1).contiguous()
         ctx.module = module
         ctx.value_shape = value.shape
@@ -345,12 +387,13 @@ class _ProjectionFn(torch.autograd.Function):
             if ctx.learned:
                 partials = torch.empty(int(lib.bd_ste_weight_grad_partials(outer, inner)), dtype=torch.float32,
                                        device=device)
-            flags = ops.Flags(device)
+            flags, now = _flags(device)
             _lib.call("bd_ste_weight_grad", hi_t.data_ptr(), lo_t.data_ptr(), outer, tokens, ld_t, codes_t.data_ptr(),
                       inner, latent.detach().contiguous().data_ptr(),
                       None if window is None else window.data_ptr(), float(module.window), bound.data_ptr(), bits,
                       d_latent.data_ptr(), None if partials is None else partials.data_ptr(), flags.ptr, stream)
-            flags.check()
+            if now:
+                flags.check()
             if ctx.learned:
                 # d/d(log window) = window * sum over |w| > window of the unmasked gradient * sign(w)
                 d_window = (partials.view(-1, 2)[:, 1].sum() * window[0]).reshape(1)
@@ -701,10 +744,10 @@ class HE4(nn.Module):
         size = self.block(slots)
         device = self.vocabulary.device
         windows = len(anchors)
-        first = torch.tensor([tokens[a] for a in anchors], device=device)
+        first = _to_device([tokens[a] for a in anchors], device)
         ids = torch.cat((first[:, None], torch.full((windows, size - 1), self.mask, device=device)), 1)
         state = functional.embedding(ids.reshape(-1), self.vocabulary)
-        start = torch.tensor(anchors, device=device)
+        start = _to_device(list(anchors), device)
         offset = torch.arange(size, device=device)
         positions = start[:, None] + offset[None, :]
         length = max(anchors)

@@ -22,7 +22,8 @@ import torch.distributed as dist
 from torch import Tensor, nn
 
 from . import _lib, ops
-from .model import HE4, Projection, _bump, _frozen_halves, _need_cuda, _split, _stream, frozen_linear
+from .model import (HE4, Projection, _bump, _frozen_halves, _need_cuda, _split, _stream, _to_device, deferred_checks,
+                    frozen_linear)
 
 PARAMETER_GROUPS = ("sign", "scale", "midpoint", "gain", "clip", "norm")
 HEAD_ROWS = 128
@@ -295,9 +296,8 @@ def group_loss(model: HE4, features: Tensor, tokens: tuple[int, ...], windows: t
         raise ValueError("an update requires at least one drafted position")
     hidden = model.group_hidden(features, tokens, tuple(w.anchor for w in windows), size)
     lengths = tuple(min(len(w.labels), size - 1) for w in windows)
-    rows = torch.tensor([i * size + 1 + o for i, n in enumerate(lengths) for o in range(n)], device=device)
-    labels = torch.tensor([l for w, n in zip(windows, lengths) for l in w.labels[:n]], dtype=torch.int64,
-                          device=device)
+    rows = _to_device([i * size + 1 + o for i, n in enumerate(lengths) for o in range(n)], device)
+    labels = _to_device([l for w, n in zip(windows, lengths) for l in w.labels[:n]], device)
     weights = (label_weights(lengths, positions) * scale).to(device)
     selected = hidden.view(-1, hidden.shape[-1]).index_select(0, rows)
     if not selected.is_cuda:
@@ -318,6 +318,15 @@ def group_loss(model: HE4, features: Tensor, tokens: tuple[int, ...], windows: t
     total, d_head = loss_head(selected.detach(), model, labels, weights)
     torch.autograd.backward(selected, d_head)
     return total
+
+
+def group_loss_deferred(model: HE4, features: Tensor, tokens: tuple[int, ...], windows: tuple[Window, ...],
+                        slots: int | None = None, positions: tuple[float, ...] | None = None,
+                        scale: float = 1.0) -> Tensor:
+    """``group_loss`` with the projections' device error checks read once at the end
+    (``model.deferred_checks``) instead of after every launch."""
+    with deferred_checks(model.vocabulary.device):
+        return group_loss(model, features, tokens, windows, slots, positions, scale)
 
 
 def loss_head(head: Tensor, model: HE4, labels: Tensor, weights: Tensor) -> tuple[Tensor, Tensor]:
@@ -365,7 +374,7 @@ def update(model: HE4, optimizer: BitAdamW, features: Tensor, tokens: tuple[int,
     """One QAT update (``worker.py:365-392``).  Returns ``(loss, gradient norm)``; with an
     initialised process group the gradients are averaged across ranks first."""
     optimizer.zero_grad()
-    loss = group_loss(model, features, tokens, windows, slots)
+    loss = group_loss_deferred(model, features, tokens, windows, slots)
     params = [p for ps in optimizer.groups.values() for _, p in ps]
     average_gradients(params, group)
     norm, coef = clip_grad_norm(params, 1.0)
