@@ -782,6 +782,61 @@ def workload_qat(args, pkg, device, rank: int, world: int) -> list[dict]:
              "allreduce_ms_standalone": allreduce_ms}]
 
 
+def workload_qat_kernels(args, pkg, device) -> list[dict]:
+    """The tcgen05 products of the QAT update at config-5 sizes: one binary projection
+    (9728 x 2560, 4096 slot rows: the forward kind::i8 GEMM with the HE4 epilogue, the
+    input gradient and the latent gradient with the straight-through mask, both split
+    bf16) and the fused cross-entropy head (480 labelled rows x 151936 x 2560, bf16
+    vocabulary)."""
+    from torch import nn
+
+    qat = importlib.import_module("binary-eagle-decoding_b200.qat")
+    T, K, O = 4096, 2560, 9728
+    g = torch.Generator().manual_seed(12)
+    layer = pkg.Projection(torch.randn((O, K), generator=g) * 0.02, 4, nn.Parameter(torch.zeros(K)),
+                           nn.Parameter(torch.tensor(0.0)), window=0.05, learned_window=True).to(device)
+    x = torch.randn((T, K), generator=g).to(device).requires_grad_()
+    upstream = torch.randn((T, O), generator=g).to(device)
+
+    def projection():
+        layer.zero_grad()
+        x.grad = None
+        (layer(x) * upstream).sum().backward()
+
+    for _ in range(3):
+        projection()
+    torch.cuda.synchronize()
+    reps = max(args.steps // 4, 5)
+    us = _events_us(projection, reps)
+    flop = 2 * T * O * K * 5  # forward (one int8 product), input and latent gradients (two bf16 halves each)
+    R, H, V = 480, 2560, VOCAB
+
+    class Head(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.register_buffer("vocabulary", (torch.randn((V, H), generator=g) * 0.02).to(torch.bfloat16)
+                                 .float().to(device))
+
+    head_owner = Head()
+    head = torch.randn((R, H), generator=g).to(device)
+    labels = torch.randint(0, V, (R,), generator=g).to(device)
+    weights = torch.full((R,), 1.0 / R, device=device)
+    for _ in range(3):
+        qat.loss_head(head, head_owner, labels, weights)
+    torch.cuda.synchronize()
+    head_us = _events_us(lambda: qat.loss_head(head, head_owner, labels, weights), reps)
+    head_flop = 2 * R * V * H * 2 * 3  # logits twice and the gradient product, two halves each
+    peak, kind = bf16_peak()
+    lines = []
+    for name, t, f in (("binary projection 9728 x 2560, 4096 rows: forward + input and latent gradients", us, flop),
+                       ("fused cross-entropy head, 480 rows x 151936 x 2560", head_us, head_flop)):
+        tf = f / (t * 1e-6) / 1e12
+        lines.append({"workload": name, "metric": "tensor TFLOP/s (bf16-equivalent products)", "value": tf,
+                      "unit": "TFLOP/s", "us_per_call": t, "frac_of_bf16_peak": tf / peak,
+                      "peak": f"{peak:.1f} TFLOP/s ({kind} bf16 burst)"})
+    return lines
+
+
 def run_workload(args, rank: int, world: int, local_rank: int) -> None:
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
@@ -803,6 +858,8 @@ def run_workload(args, rank: int, world: int, local_rank: int) -> None:
         lines = workload_fusion(args, pkg, device)
     elif args.workload == "ste":
         lines = workload_ste(args, pkg, device)
+    elif args.workload == "qat_kernels":
+        lines = workload_qat_kernels(args, pkg, device)
     else:
         lines = workload_qat(args, pkg, device, rank, world)
     if world > 1:
@@ -825,7 +882,8 @@ def main() -> None:
                         help="consecutive draft rounds in one timed step")
     parser.add_argument("--profile-round", action="store_true",
                         help="run one draft round between cudaProfilerStart/Stop and exit")
-    parser.add_argument("--workload", choices=("round", "ffn", "w1a1", "accept", "ingest", "fusion", "ste", "qat"), default="round",
+    parser.add_argument("--workload", choices=("round", "ffn", "w1a1", "accept", "ingest", "fusion", "ste", "qat",
+                                               "qat_kernels"), default="round",
                         help="round: the headline draft round; the others measure one hot-path workload each")
     parser.add_argument("--qat-sequences", type=int, default=8)
     parser.add_argument("--ste-projections", type=int, default=12)
