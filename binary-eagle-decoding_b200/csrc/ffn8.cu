@@ -127,7 +127,7 @@ __global__ void __launch_bounds__(320) gateup_w8_kernel(const GuW8Args a) {
     constexpr int PMAX = gu_pmax(MT, PLANES, GMAX);
     constexpr int ACC = 2 * PLANES * MT * 4;  // accumulator ints per pair per lane
     extern __shared__ __align__(16) int red[];
-    __shared__ int csum_in[2][32];
+    __shared__ int csum_part[2][10][32];  // input code sums: [plane][warp][token], summed in the epilogue
     __shared__ int csum_next[32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     const int64_t p0 = static_cast<int64_t>(blockIdx.x) * a.np / gridDim.x;
@@ -168,18 +168,15 @@ __global__ void __launch_bounds__(320) gateup_w8_kernel(const GuW8Args a) {
     }
     grid_wait();
     grid_launch_dependents();
-    if (threadIdx.x < 32) {
-        const int t = threadIdx.x;
-        int s0 = 0, s1 = 0;
-        if (t < a.tokens) {
-            for (int i = 0; i < a.cs_parts; ++i) s0 += a.csum0[t * a.cs_parts + i];
-            if (PLANES == 2)
-                for (int i = 0; i < a.cs_parts; ++i) s1 += a.csum1[t * a.cs_parts + i];
+    // input code sums: warp w requests partials w, w + nwarps, ... of token `lane`
+    // now and files them after the MMAs, so no warp waits on them before its MMAs
+    int cs_v0 = 0, cs_v1 = 0;
+    if (lane < a.tokens)
+        for (int i = warp; i < a.cs_parts; i += nwarps) {
+            cs_v0 += a.csum0[lane * a.cs_parts + i];
+            if (PLANES == 2) cs_v1 += a.csum1[lane * a.cs_parts + i];
         }
-        csum_in[0][t] = s0;
-        csum_in[1][t] = s1;
-        csum_next[t] = 0;
-    }
+    if (threadIdx.x < 32) csum_next[threadIdx.x] = 0;
     int acc[PMAX][2][PLANES][MT][4];
 #pragma unroll
     for (int p = 0; p < PMAX; ++p)
@@ -223,6 +220,8 @@ __global__ void __launch_bounds__(320) gateup_w8_kernel(const GuW8Args a) {
                 }
         }
     }
+    csum_part[0][warp][lane] = cs_v0;
+    csum_part[1][warp][lane] = cs_v1;
 #pragma unroll
     for (int p = 0; p < PMAX; ++p) {
         if (p < npc) {
@@ -263,8 +262,13 @@ __global__ void __launch_bounds__(320) gateup_w8_kernel(const GuW8Args a) {
         for (int h = 0; h < 2; ++h) {
             const int tok = mt * 16 + g + 8 * h;
             rs[mt][h] = (EPI != EPI_HE4 && tok < a.tokens) ? __ldg(a.row_scale + tok) : 0.0f;
-            cin0[mt][h] = csum_in[0][tok];
-            cin1[mt][h] = csum_in[1][tok];
+            int c0 = 0, c1 = 0;
+            for (int w = 0; w < nwarps; ++w) {
+                c0 += csum_part[0][w][tok];
+                c1 += csum_part[1][w][tok];
+            }
+            cin0[mt][h] = c0;
+            cin1[mt][h] = c1;
         }
     for (int p = warp; p < npc; p += nwarps) {
         int d[2][PLANES][MT][4];
@@ -400,6 +404,7 @@ __global__ void __launch_bounds__(kDnMaxWarps * 32) down_w8_kernel(const DnW8Arg
     constexpr int NTMAX = dn_ntmax(MT, PLANES);
     constexpr int ACCD = PLANES * MT * 4;  // accumulator ints per n-tile per lane
     extern __shared__ __align__(16) int dsm[];  // [warps][NTMAX][ACCD][32] then [NTMAX][ACCD][32]
+    __shared__ int csum_part[2][kDnMaxWarps][32];  // input code sums: [plane][warp][token]
     __shared__ int csum_s[2][32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     const uint32_t rank = cluster_rank();
@@ -434,17 +439,14 @@ __global__ void __launch_bounds__(kDnMaxWarps * 32) down_w8_kernel(const DnW8Arg
     }
     grid_wait();
     grid_launch_dependents();
-    if (threadIdx.x < 32) {
-        const int t = threadIdx.x;
-        int s0 = 0, s1 = 0;
-        if (t < a.tokens) {
-            for (int c = 0; c < a.cs_parts; ++c) s0 += a.csum0[c * 32 + t];
-            if (PLANES == 2)
-                for (int c = 0; c < a.cs_parts; ++c) s1 += a.csum1[c * 32 + t];
+    // input code sums: warp w requests copies w, w + nwarps, ... of token `lane`
+    // now and files them after the MMAs, off the MMA path
+    int cs_v0 = 0, cs_v1 = 0;
+    if (lane < a.tokens)
+        for (int c = warp; c < a.cs_parts; c += nwarps) {
+            cs_v0 += a.csum0[c * 32 + lane];
+            if (PLANES == 2) cs_v1 += a.csum1[c * 32 + lane];
         }
-        csum_s[0][t] = s0;
-        csum_s[1][t] = s1;
-    }
     int acc[NTMAX][PLANES][MT][4];
 #pragma unroll
     for (int n = 0; n < NTMAX; ++n)
@@ -483,6 +485,8 @@ __global__ void __launch_bounds__(kDnMaxWarps * 32) down_w8_kernel(const DnW8Arg
                 }
         }
     }
+    csum_part[0][warp][lane] = cs_v0;
+    csum_part[1][warp][lane] = cs_v1;
     int *wpart = dsm;                                                        // per-warp partials
     int *cpart = dsm + static_cast<size_t>(kDnMaxWarps) * NTMAX * ACCD * 32;  // this CTA's sums
 #pragma unroll
@@ -497,6 +501,15 @@ __global__ void __launch_bounds__(kDnMaxWarps * 32) down_w8_kernel(const DnW8Arg
                         wpart[((warp * NTMAX + n) * ACCD + (pl * MT + mt) * 4 + r) * 32 + lane] = acc[n][pl][mt][r];
         }
     __syncthreads();
+    if (threadIdx.x < 32) {
+        int s0 = 0, s1 = 0;
+        for (int w = 0; w < nwarps; ++w) {
+            s0 += csum_part[0][w][threadIdx.x];
+            s1 += csum_part[1][w][threadIdx.x];
+        }
+        csum_s[0][threadIdx.x] = s0;  // read after the cluster barrier below
+        csum_s[1][threadIdx.x] = s1;
+    }
     for (int n = warp; n < ncl; n += nwarps)
 #pragma unroll
         for (int i = 0; i < ACCD; ++i) {
@@ -521,8 +534,13 @@ __global__ void __launch_bounds__(kDnMaxWarps * 32) down_w8_kernel(const DnW8Arg
 #pragma unroll
                 for (int r = 0; r < 4; ++r) {
                     const int *s = cpart + (n * ACCD + (pl * MT + mt) * 4 + r) * 32 + lane;
+                    // every CTA's partial requested at once (cluster of 8 at most)
+                    int part[8];
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) part[c] = c < a.cs ? ld_cluster_i32(s, static_cast<uint32_t>(c)) : 0;
                     int v = 0;
-                    for (int c = 0; c < a.cs; ++c) v += ld_cluster_i32(s, static_cast<uint32_t>(c));
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) v += part[c];
                     d[pl][mt][r] = v;
                 }
 #pragma unroll

@@ -23,10 +23,12 @@ __device__ __forceinline__ T block_sum_256(T v, T *scratch) {
     return total;
 }
 
-// Grid (rows, ceil(cols / 1024)): each thread quantizes 4 consecutive columns
-// with all loads in flight at once.  Code sums go either to partial[row][y]
-// (partial = true, no zeroing needed) or, with integer atomics, to a zeroed
-// full[row].
+// Grid (rows, ceil(cols / 1024)): each thread quantizes 4 consecutive columns.
+// The parameters (gain, norm weight, bound) are read before the dependency
+// wait; after it, one round trip brings the thread's columns 4 (t + 256 i) + j
+// of the row (i < 4, so rows up to 4096 columns stay in registers) for both the
+// rms and the codes.  Code sums go either to partial[row][y] (partial = true,
+// no zeroing needed) or, with integer atomics, to a zeroed full[row].
 __global__ void __launch_bounds__(256) quantize_codes_kernel(const float *__restrict__ x, int64_t cols, int64_t ld,
                                                              const float *__restrict__ gain,
                                                              const float *__restrict__ bound_ptr, int bits,
@@ -36,14 +38,36 @@ __global__ void __launch_bounds__(256) quantize_codes_kernel(const float *__rest
                                                              float eps, int c16_mt) {
     __shared__ int scratch[8];
     __shared__ float fpart[8];
+    const int row = blockIdx.x;
+    const int64_t k0 = static_cast<int64_t>(blockIdx.y) * 1024 + 4 * threadIdx.x;
+    float gv[4], nv[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const bool live = k0 + j < cols;
+        gv[j] = live ? __ldg(gain + k0 + j) : 0.0f;
+        nv[j] = (norm_w && live) ? __ldg(norm_w + k0 + j) : 0.0f;
+    }
+    const float b = __ldg(bound_ptr);
     grid_wait();
     grid_launch_dependents();
-    const int row = blockIdx.x;
+    const float *xr = x + row * cols;
+    float v[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int64_t k = 4 * (threadIdx.x + 256 * i) + j;
+            v[i][j] = (k < cols && (norm_w || i == static_cast<int>(blockIdx.y))) ? xr[k] : 0.0f;
+        }
     // optional rms(x, norm_w, eps) of the whole row first (model.py:50-51, 220)
     float scale = 1.0f;
     if (norm_w) {
         float ss = 0.0f;
-        for (int64_t k = threadIdx.x; k < cols; k += blockDim.x) ss = fmaf(x[row * cols + k], x[row * cols + k], ss);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) ss = fmaf(v[i][j], v[i][j], ss);
+        for (int64_t k = 4096 + threadIdx.x; k < cols; k += blockDim.x) ss = fmaf(xr[k], xr[k], ss);
 #pragma unroll
         for (int d = 16; d > 0; d >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, d);
         if ((threadIdx.x & 31) == 0) fpart[threadIdx.x >> 5] = ss;
@@ -55,21 +79,22 @@ __global__ void __launch_bounds__(256) quantize_codes_kernel(const float *__rest
     }
     if (row == 0 && blockIdx.y == 0 && zero_sums)
         for (int i = threadIdx.x; i < zero_count; i += blockDim.x) zero_sums[i] = 0;
-    const float b = *bound_ptr;
     if (bad_bound(b) && threadIdx.x == 0 && blockIdx.y == 0) set_flag(flags, BD_FLAG_BAD_BOUND);
     Quant q;
     q.init(b, bits);
-    const int64_t k0 = static_cast<int64_t>(blockIdx.y) * 1024 + 4 * threadIdx.x;
     int sum = 0;
     bool bad = false;
     if (k0 < cols) {
-        float xv[4], gv[4];
+        float xv[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
+            xv[j] = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                if (i == static_cast<int>(blockIdx.y)) xv[j] = v[i][j];
             const bool live = k0 + j < cols;
-            xv[j] = live ? x[row * cols + k0 + j] : 0.0f;
-            if (norm_w && live) xv[j] = xv[j] * scale * norm_w[k0 + j];
-            gv[j] = live ? gain[k0 + j] : 0.0f;
+            if (blockIdx.y >= 4 && live) xv[j] = xr[k0 + j];
+            if (norm_w && live) xv[j] = xv[j] * scale * nv[j];
         }
         int c[4];
 #pragma unroll
