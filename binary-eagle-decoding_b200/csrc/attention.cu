@@ -42,34 +42,6 @@ struct AttnArgs {
     int32_t *flags;
 };
 
-__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void *p) {
-    const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(a));
-}
-__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void *p) {
-    const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(a));
-}
-__device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                              uint32_t b0, uint32_t b1) {
-    asm(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
-        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-// fp16 hi + lo halves of a pair: x ~= float(hi) + float(lo) to ~22 bits.
-__device__ __forceinline__ void split_half2(float x0, float x1, uint32_t &hi, uint32_t &lo) {
-    const __half2 h = __floats2half2_rn(x0, x1);
-    const __half2 l = __floats2half2_rn(x0 - __low2float(h), x1 - __high2float(h));
-    hi = *reinterpret_cast<const uint32_t *>(&h);
-    lo = *reinterpret_cast<const uint32_t *>(&l);
-}
-
 // 16 warps: warp w takes q head (w & 3) of the kv group and quarter (w >> 2) of
 // the chunk's keys; the quarters of a head merge through shared memory (the
 // staged K/V area, free once P V is done).  One CTA per SM.

@@ -414,6 +414,38 @@ int bd_attention_decode(const float *q, const uint16_t *k_cache, const uint16_t 
                         int64_t stable_keys, float *out, void *workspace, size_t workspace_bytes,
                         bd_stream_t stream);
 
+/* ================================================================ training attention
+ * Layer.group's block attention at training sizes (w1a1_eagle/model.py:225-270,
+ * the reference's torch einsum / masked_fill / softmax over [W, heads, k, L + k]
+ * scores): W windows of k <= 16 slots; groups = heads / kv_heads <= 4 query heads
+ * per kv head; head_dim <= 128; keys = L shared context keys.  Each slot attends
+ * to the context keys its ctx_mask row allows and to the slots its slot_mask row
+ * allows, one softmax over both.
+ * Operands are fp16 rows of DP = head_dim rounded up to 16, 32, 64 or 128 (zero
+ * padded), 16-byte aligned:
+ *   q_hi, q_lo       [kv_heads][W][groups][16][DP]  fp32 query = hi + lo (rows >= k zero)
+ *   ctx_k, ctx_v     [kv_heads][Lp][DP]             Lp = keys rounded up to 64 (fp16 values)
+ *   slot_k, slot_v   [kv_heads][W][16][DP]
+ *   ctx_mask         [W][16][Lp] uint8 (0 = masked; padding 0), slot_mask [16][16] uint8
+ * scale = 1 / sqrt(head_dim).  Forward: out fp32 [W][k][kv_heads][groups][head_dim],
+ * lse fp32 [kv_heads][W][groups][16] (the rows' log-sum-exp, +inf for a row with no
+ * allowed key).  Backward: dout_hi/lo = the output gradient times a power of two
+ * (1 / *unscale) in the q layout; dr [kv_heads][W][groups][16] = rowsum(scaled dout
+ * x out); writes dq (out's layout), d_ctx_k/v fp32 [keys][kv_heads][head_dim] and
+ * d_slot_k/v fp32 [W][k][kv_heads][head_dim].  fp16 tensor-core products with
+ * fp32 accumulation; the fp32 operands enter as hi + lo halves.  Deterministic
+ * (no atomics).  No reference C counterpart: the reference is torch autograd. */
+int bd_train_attention_forward(const void *q_hi, const void *q_lo, const void *ctx_k, const void *ctx_v,
+                               const void *slot_k, const void *slot_v, const uint8_t *ctx_mask,
+                               const uint8_t *slot_mask, int windows, int slots, int kv_heads, int groups,
+                               int head_dim, int keys, float scale, float *out, float *lse, bd_stream_t stream);
+int bd_train_attention_backward(const void *q_hi, const void *q_lo, const void *ctx_k, const void *ctx_v,
+                                const void *slot_k, const void *slot_v, const uint8_t *ctx_mask,
+                                const uint8_t *slot_mask, const void *dout_hi, const void *dout_lo, const float *lse,
+                                const float *dr, const float *unscale, int windows, int slots, int kv_heads,
+                                int groups, int head_dim, int keys, float scale, float *dq, float *d_ctx_k,
+                                float *d_ctx_v, float *d_slot_k, float *d_slot_v, bd_stream_t stream);
+
 /* ================================================================ QAT (training sizes)
  * Projection.forward at any token count (w1a1_eagle/model.py:128-150): codes and
  * +-1 signs are exact in bf16, so D = codes . signs^T is an exact bf16
