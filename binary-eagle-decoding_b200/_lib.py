@@ -28,6 +28,7 @@ FLAG_CACHE_OVERFLOW = 64
 FLAG_SIGN_CHANGE = 128
 FLAG_TIMEOUT = 256
 FLAG_NONFINITE_FEATURES = 512
+FLAG_NONFINITE_LOSS = 1024
 
 # Messages of the reference's ValueErrors for the same conditions.
 FLAG_MESSAGES = (
@@ -40,6 +41,7 @@ FLAG_MESSAGES = (
     (FLAG_CACHE_OVERFLOW, "F16 cache storage overflow"),
     (FLAG_SIGN_CHANGE, "bounded latent scale changed a sign"),
     (FLAG_NONFINITE_FEATURES, "nonfinite teacher features"),
+    (FLAG_NONFINITE_LOSS, "nonfinite loss"),
 )
 # Device-side failures that are not the reference's ValueErrors.
 FLAG_ERRORS = ((FLAG_TIMEOUT, "a bounded device wait timed out"),)

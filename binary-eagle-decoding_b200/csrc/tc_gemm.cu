@@ -853,7 +853,7 @@ __global__ void ce_reduce_kernel(const float *__restrict__ stats, const float *_
     if (lane == 0) {
         const float lse = __fadd_rn(m, logf(s));
         const float loss = __fsub_rn(lse, target[warp]);
-        if (!isfinite(loss)) set_flag(flags, BD_FLAG_NONFINITE_STATE);
+        if (!isfinite(loss)) set_flag(flags, BD_FLAG_NONFINITE_LOSS);
         lse_out[warp] = lse;
         loss_rows[warp] = __fmul_rn(weights[warp], loss);
     }

@@ -67,11 +67,25 @@ def rms(value: Tensor, weight: Tensor, epsilon: float) -> Tensor:
     return value * torch.rsqrt(value.square().mean(-1, keepdim=True) + epsilon) * weight
 
 
+_FREQUENCIES: dict[tuple[int, float, torch.device], Tensor] = {}
+
+
+def _frequencies(width: int, theta: float, device: torch.device) -> Tensor:
+    """``theta^(-2i/width)`` in fp32, evaluated once on the host (as the reference does)
+    and kept on ``device``: no host round trip per call."""
+    key = (width, float(theta), device)
+    hit = _FREQUENCIES.get(key)
+    if hit is None:
+        exponents = torch.arange(0, width, 2, dtype=torch.float32) / width
+        hit = torch.tensor(theta, dtype=torch.float32).pow(-exponents).to(device)
+        _FREQUENCIES[key] = hit
+    return hit
+
+
 def rope(value: Tensor, positions: Tensor, theta: float) -> Tensor:
     """Rotate-half rotary embedding with frequencies ``theta^(-2i/width)`` (``model.py:54-63``)."""
     width = value.shape[-1]
-    exponents = torch.arange(0, width, 2, dtype=torch.float32, device=value.device) / width
-    frequency = torch.tensor(theta, dtype=torch.float32, device=value.device).pow(-exponents)
+    frequency = _frequencies(width, theta, value.device)
     angle = positions.float()[:, None] * frequency
     angle = torch.cat((angle, angle), -1).unsqueeze(1)
     first, second = value[..., : width // 2], value[..., width // 2:]
@@ -443,7 +457,11 @@ class Projection(nn.Module):
         hit = self._signs.get("i8")
         if hit is not None and hit[0] == key:
             return hit[1]
-        out = ops.tile_i8(self.latent_sign.detach().contiguous())
+        latent = self.latent_sign.detach().contiguous()
+        flags, now = _flags(latent.device)
+        out = ops.tile_i8(latent, flags=flags)
+        if now:
+            flags.check()
         self._signs["i8"] = (key, out)
         return out
 
@@ -458,9 +476,10 @@ class Projection(nn.Module):
         device = _need_cuda(latent)
         rows, cols = latent.shape
         out = torch.empty((cols, ld), dtype=torch.bfloat16, device=device)
-        flags = ops.Flags(device)
+        flags, now = _flags(device)
         _lib.call("bd_sign_cols_bf16", latent.data_ptr(), rows, cols, out.data_ptr(), ld, flags.ptr, _stream(device))
-        flags.check()
+        if now:
+            flags.check()
         self._signs["t_bf16"] = (key, out)
         return out
 

@@ -22,8 +22,8 @@ import torch.distributed as dist
 from torch import Tensor, nn
 
 from . import _lib, ops
-from .model import (HE4, Projection, _bump, _frozen_halves, _need_cuda, _split, _stream, _to_device, deferred_checks,
-                    frozen_linear)
+from .model import (HE4, Projection, _bump, _flags, _frozen_halves, _need_cuda, _split, _stream, _to_device,
+                    deferred_checks, frozen_linear)
 
 PARAMETER_GROUPS = ("sign", "scale", "midpoint", "gain", "clip", "norm")
 HEAD_ROWS = 128
@@ -298,7 +298,8 @@ def group_loss(model: HE4, features: Tensor, tokens: tuple[int, ...], windows: t
     lengths = tuple(min(len(w.labels), size - 1) for w in windows)
     rows = _to_device([i * size + 1 + o for i, n in enumerate(lengths) for o in range(n)], device)
     labels = _to_device([l for w, n in zip(windows, lengths) for l in w.labels[:n]], device)
-    weights = (label_weights(lengths, positions) * scale).to(device)
+    weights = label_weights(lengths, positions) * scale
+    weights = weights.pin_memory().to(device, non_blocking=True) if device.type == "cuda" else weights.to(device)
     selected = hidden.view(-1, hidden.shape[-1]).index_select(0, rows)
     if not selected.is_cuda:
         # host-side bookkeeping checks only: the reference's own chunked expression
@@ -350,14 +351,14 @@ def loss_head(head: Tensor, model: HE4, labels: Tensor, weights: Tensor) -> tupl
     lse = torch.empty(rows, dtype=torch.float32, device=device)
     loss_rows = torch.empty(rows, dtype=torch.float32, device=device)
     total = torch.empty(1, dtype=torch.float32, device=device)
-    flags = ops.Flags(device)
+    flags, now = _flags(device)
     stream = _stream(device)
     v_lo = None if halves.lo is None else halves.lo.data_ptr()
     _lib.call("bd_loss_head_forward", h_hi.data_ptr(), h_lo.data_ptr(), rows, hidden, ld_h, halves.hi.data_ptr(), v_lo,
               vocab, lab.data_ptr(), w.data_ptr(), stats.data_ptr(), target.data_ptr(), lse.data_ptr(),
               loss_rows.data_ptr(), total.data_ptr(), flags.ptr, stream)
-    if int(flags.tensor.item()):
-        raise ValueError("nonfinite loss")
+    if now:
+        flags.check()
     hi_t, lo_t, ld_v = halves.transposed()
     dl_hi = torch.empty((rows, ld_v), dtype=torch.bfloat16, device=device)
     dl_lo = torch.empty_like(dl_hi)

@@ -46,6 +46,7 @@ typedef struct CUstream_st *bd_stream_t; /* == cudaStream_t */
 #define BD_FLAG_SIGN_CHANGE 128u      /* model.py:162-163 "bounded latent scale changed a sign" */
 #define BD_FLAG_TIMEOUT 256u          /* a bounded device wait ran out (the kernel returned early) */
 #define BD_FLAG_NONFINITE_FEATURES 512u /* captures.py:129-130 "nonfinite teacher features" */
+#define BD_FLAG_NONFINITE_LOSS 1024u    /* worker.py:360-361 "nonfinite loss" */
 
 int bd_abi_version(void);
 const char *bd_status_string(int status);
