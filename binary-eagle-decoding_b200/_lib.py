@@ -116,9 +116,12 @@ SIGNATURES = {
     "bd_projection_he4_tc": (c_int, [P, c_int64, P, c_int64, c_int64, P, c_int64, P, P, P, c_int, P, P, P, P, P]),
     "bd_sign_cols_bf16": (c_int, [P, c_int64, c_int64, P, c_int64, P, P]),
     "bd_codes_transpose_bf16": (c_int, [P, c_int64, c_int64, c_int64, P, c_int64, P]),
-    "bd_gemm_bf16_split": (c_int, [P, P, c_int64, c_int64, c_int64, P, c_int64, c_int64, P, c_int64, P]),
+    "bd_gemm_bf16_split": (c_int, [P, P, c_int64, c_int64, c_int64, P, c_int64, c_int64, P, c_int64, P, c_size_t,
+                                   P]),
+    "bd_gemm_split_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64, c_int]),
     "bd_split_bf16": (c_int, [P, c_int64, c_int64, c_int64, c_int, P, P, c_int64, P]),
-    "bd_gemm_bf16_split3": (c_int, [P, P, c_int64, c_int64, c_int64, P, P, c_int64, c_int64, P, c_int64, P]),
+    "bd_gemm_bf16_split3": (c_int, [P, P, c_int64, c_int64, c_int64, P, P, c_int64, c_int64, P, c_int64, P,
+                                    c_size_t, P]),
     "bd_loss_head_stats_count": (c_int64, [c_int64, c_int64]),
     "bd_loss_head_forward": (c_int, [P, P, c_int64, c_int64, c_int64, P, P, c_int64, P, P, P, P, P, P, P, P, P]),
     "bd_loss_head_grad": (c_int, [P, P, c_int64, c_int64, c_int64, P, P, c_int64, P, P, P, P, P, c_int64, P]),

@@ -75,7 +75,33 @@ struct TcArgs {
     float *stats;           // [M][2 n_tiles][2]: max, sum of exp(D - max) per half tile (STATS)
     float *target;          // [M] the label's logit (STATS)
     __nv_bfloat16 *dl_hi, *dl_lo;  // [M][ld_out] (GRAD)
+    // TC_F32 split over K: work unit u = tile u / splits, K slice u % splits; every
+    // unit writes its fp32 partial tile, and per (tile, epilogue warp) the last of
+    // the splits to arrive adds them in slice order (deterministic) into out
+    int splits;
+    float *split_part;      // [tiles][splits][kTcBM][BN]
+    int32_t *split_count;   // [tiles][8] at the start of the workspace, zero on entry and left zero
+    void *split_ws;         // caller's workspace for the above (host side only), or null: no split
+    size_t split_ws_bytes;
 };
+
+// K slices per tile of a TC_F32 product: enough units to fill the GPU when the
+// tiles alone leave more than half of it idle, at least 4 k-blocks per slice.
+// The counters sit at a fixed place (the first kTcSplitCounts words) whatever the
+// shape, so that a workspace shared by products of different shapes never sees an
+// earlier call's partial sums where this call keeps its counters.
+constexpr int64_t kTcSplitCounts = 2048;  // 8 per tile: up to 256 split tiles
+
+static int tc_split_slices(int64_t tiles, int64_t nk, int sms) {
+    if (tiles * 2 > sms || tiles * 8 > kTcSplitCounts) return 1;
+    int64_t s = sms / tiles;
+    s = s < nk / 4 ? s : nk / 4;
+    s = s < 16 ? s : 16;
+    return s > 1 ? static_cast<int>(s) : 1;
+}
+static size_t tc_split_bytes(int64_t tiles, int slices, int bn) {
+    return kTcSplitCounts * sizeof(int32_t) + static_cast<size_t>(tiles) * slices * kTcBM * bn * sizeof(float);
+}
 
 __device__ __forceinline__ uint32_t su32(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
@@ -158,6 +184,8 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
     constexpr int BKE = tc_bk(EPI);  // K elements per stage
     const int nk1 = static_cast<int>((a.K + BKE - 1) / BKE);
     const int nk = nk1 * (a.parts > 1 ? a.parts : 1);  // part p covers k-blocks [p nk1, (p + 1) nk1)
+    const int S = (EPI == TC_F32 && a.splits > 1) ? a.splits : 1;  // K slices per tile (at most nk)
+    const int64_t units = tiles * S;
     constexpr uint32_t kCols = 2 * BN;  // two accumulator buffers
     if (threadIdx.x == 0) {
         for (int s = 0; s < kTcStages; ++s) {
@@ -184,10 +212,12 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
     if (warp == 0) {
         if (lane == 0) {  // TMA producer
             uint32_t it = 0;
-            for (int64_t t = blockIdx.x; t < tiles && !abort_flag; t += gridDim.x) {
+            for (int64_t u = blockIdx.x; u < units && !abort_flag; u += gridDim.x) {
+                const int64_t t = u / S;
                 const int m0 = static_cast<int>((t % a.m_tiles) * kTcBM);
                 const int n0 = static_cast<int>((t / a.m_tiles) * BN);
-                for (int k = 0; k < nk; ++k, ++it) {
+                const int kb = static_cast<int>((u % S) * nk / S), ke = static_cast<int>((u % S + 1) * nk / S);
+                for (int k = kb; k < ke; ++k, ++it) {
                     const int s = it % kTcStages;
                     if (it >= kTcStages && !mb_wait(&empty[s], ((it / kTcStages) - 1) & 1, &abort_flag)) break;
                     mb_expect_tx(&full[s], (kTcBM + BN) * kTcBK);
@@ -205,13 +235,14 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
         if (lane == 0) {  // MMA issuer
             constexpr uint32_t idesc = tc_bf16(EPI) ? idesc_bf16(BN) : idesc_i8(BN);
             uint32_t it = 0, lt = 0;
-            for (int64_t t = blockIdx.x; t < tiles && !abort_flag; t += gridDim.x, ++lt) {
+            for (int64_t u = blockIdx.x; u < units && !abort_flag; u += gridDim.x, ++lt) {
                 const uint32_t b = lt & 1;
                 if (!mb_wait(&acc_empty[b], ((lt >> 1) & 1) ^ 1, &abort_flag)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t d = tmem + b * BN;
                 bool ok = true;
-                for (int k = 0; k < nk; ++k, ++it) {
+                const int kb = static_cast<int>((u % S) * nk / S), ke = static_cast<int>((u % S + 1) * nk / S);
+                for (int k = kb; k < ke; ++k, ++it) {
                     const int s = it % kTcStages;
                     if (!mb_wait(&full[s], (it / kTcStages) & 1, &abort_flag)) {
                         ok = false;
@@ -221,7 +252,7 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
                     const uint64_t da = sdesc(sa + s * kTcBM * kTcBK), db = sdesc(sb + s * BN * kTcBK);
 #pragma unroll
                     for (int kk = 0; kk < kTcBK / 32; ++kk) {
-                        const uint32_t accumulate = (k > 0 || kk > 0) ? 1u : 0u;
+                        const uint32_t accumulate = (k > kb || kk > 0) ? 1u : 0u;
                         // one instruction consumes 32 bytes of K (32 int8 or 16 bf16): descriptor +2
                         if (tc_bf16(EPI))
                             asm volatile(
@@ -264,7 +295,11 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
         const bool vec_out = (a.ld_out & 3) == 0 && (reinterpret_cast<uintptr_t>(EPI == TC_RAW ? static_cast<void *>(a.out_i32)
                                                                                                : static_cast<void *>(a.out)) & 15) == 0;
         uint32_t lt = 0;
-        for (int64_t t = blockIdx.x; t < tiles && !abort_flag; t += gridDim.x, ++lt) {
+        for (int64_t u = blockIdx.x; u < units && !abort_flag; u += gridDim.x, ++lt) {
+            const int64_t t = u / S;
+            const int sp = static_cast<int>(u % S);
+            // this unit's partial tile (split K): rows of this thread, its half of the columns
+            float *part = S > 1 ? a.split_part + ((t * S + sp) * kTcBM + row_in_tile) * BN + half * HALF : nullptr;
             const uint32_t b = lt & 1;
             if (!mb_wait(&acc_full[b], (lt >> 1) & 1, &abort_flag)) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -333,6 +368,12 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
                     }
                 }
                 const int64_t idx = row * a.ld_out + o0;
+                if (EPI == TC_F32 && S > 1) {
+#pragma unroll
+                    for (int j = 0; j < 16; j += 4)
+                        *reinterpret_cast<float4 *>(part + c + j) = make_float4(y[j], y[j + 1], y[j + 2], y[j + 3]);
+                    continue;
+                }
                 if (EPI == TC_CE_STATS) {
                     // online max and sum of exp over the live columns of this chunk
                     float cmax = -INFINITY;
@@ -443,6 +484,47 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
             if (lane == 0) mb_arrive(&acc_empty[b]);
+            if (EPI == TC_F32 && S > 1) {
+                // the last split of this (tile, warp region) to arrive sums the partials in slice
+                // order; no thread waits on another CTA
+                __threadfence();
+                __syncwarp();
+                int old = 0;
+                int32_t *count = a.split_count + t * 8 + (warp - 2);
+                if (lane == 0) old = atomicAdd(count, 1);
+                old = __shfl_sync(0xffffffffu, old, 0);
+                if (old == S - 1) {
+                    __threadfence();
+                    const float *p0 = a.split_part + (t * S * kTcBM + row_in_tile) * BN + half * HALF;
+                    for (int c = 0; c < HALF && live_row; c += 16) {
+                        const int64_t o0 = o_base + c;
+                        if (o0 >= a.N) break;
+                        float y[16];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) y[j] = 0.0f;
+                        for (int s = 0; s < S; ++s) {
+                            const float *src = p0 + static_cast<int64_t>(s) * kTcBM * BN + c;
+#pragma unroll
+                            for (int j = 0; j < 16; j += 4) {
+                                const float4 v4 = __ldcg(reinterpret_cast<const float4 *>(src + j));
+                                y[j] = __fadd_rn(y[j], v4.x);
+                                y[j + 1] = __fadd_rn(y[j + 1], v4.y);
+                                y[j + 2] = __fadd_rn(y[j + 2], v4.z);
+                                y[j + 3] = __fadd_rn(y[j + 3], v4.w);
+                            }
+                        }
+                        const int64_t idx = row * a.ld_out + o0;
+                        if (o0 + 16 <= a.N && vec_out) {
+#pragma unroll
+                            for (int j = 0; j < 16; j += 4)
+                                *reinterpret_cast<float4 *>(a.out + idx + j) = make_float4(y[j], y[j + 1], y[j + 2], y[j + 3]);
+                        } else {
+                            for (int j = 0; j < 16 && o0 + j < a.N; ++j) a.out[idx + j] = y[j];
+                        }
+                    }
+                    if (lane == 0) *count = 0;
+                }
+            }
             if (EPI == TC_CE_STATS && live_row) {
                 float *st = a.stats + (row * (2 * a.n_tiles) + (t / a.m_tiles) * 2 + half) * 2;
                 st[0] = run_max;
@@ -540,7 +622,17 @@ static int launch_tc_t(TcArgs a, const int8_t *codes, int64_t ld_codes, const in
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
         return BD_ERR_LAUNCH;
     const int64_t tiles = a.m_tiles * a.n_tiles;
-    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(tiles, sms_tc()));
+    a.splits = 1;
+    if (EPI == TC_F32 && a.split_ws && (reinterpret_cast<uintptr_t>(a.split_ws) & 255) == 0) {
+        const int64_t nk = (a.K + tc_bk(EPI) - 1) / tc_bk(EPI) * a.parts;
+        const int s = tc_split_slices(tiles, nk, sms_tc());
+        if (s > 1 && tc_split_bytes(tiles, s, BN) <= a.split_ws_bytes) {
+            a.splits = s;
+            a.split_count = static_cast<int32_t *>(a.split_ws);
+            a.split_part = reinterpret_cast<float *>(static_cast<char *>(a.split_ws) + kTcSplitCounts * sizeof(int32_t));
+        }
+    }
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(tiles * a.splits, sms_tc()));
     kern<<<grid, 320, smem, stream>>>(a, ma, mb, ma2, mb2, ma3, mb3);
     BD_CHECK_LAUNCH();
     return BD_OK;
@@ -751,9 +843,16 @@ extern "C" int bd_projection_he4_tc(const int8_t *codes, int64_t ld_codes, const
     return launch_tc_gemm(TC_HE4, a, codes, ld_codes, signs_i8, out_features, i8_ld(in_features), stream);
 }
 
+extern "C" size_t bd_gemm_split_workspace_bytes(int64_t m, int64_t n, int64_t k, int parts) {
+    if (m < 1 || n < 1 || k < 1 || parts < 1 || parts > 3) return 0;
+    const int64_t tiles = tc_tiles(m, n);
+    const int s = tc_split_slices(tiles, (k + 63) / 64 * parts, sms_tc());
+    return s > 1 ? tc_split_bytes(tiles, s, 256) : 0;
+}
+
 extern "C" int bd_gemm_bf16_split(const uint16_t *a_hi, const uint16_t *a_lo, int64_t m, int64_t k, int64_t lda,
-                                  const uint16_t *b, int64_t n, int64_t ldb, float *c, int64_t ldc,
-                                  bd_stream_t stream) {
+                                  const uint16_t *b, int64_t n, int64_t ldb, float *c, int64_t ldc, void *workspace,
+                                  size_t workspace_bytes, bd_stream_t stream) {
     if (m < 1 || k < 1 || n < 1 || lda < k || ldb < k || ldc < n || !a_hi || !b || !c) return BD_ERR_INVALID;
     TcArgs t{};
     t.M = m;
@@ -761,6 +860,8 @@ extern "C" int bd_gemm_bf16_split(const uint16_t *a_hi, const uint16_t *a_lo, in
     t.K = k;
     t.ld_out = ldc;
     t.out = c;
+    t.split_ws = workspace;
+    t.split_ws_bytes = workspace_bytes;
     TcParts more;
     if (a_lo) {
         more.a2 = reinterpret_cast<const int8_t *>(a_lo);
@@ -772,7 +873,7 @@ extern "C" int bd_gemm_bf16_split(const uint16_t *a_hi, const uint16_t *a_lo, in
 
 extern "C" int bd_gemm_bf16_split3(const uint16_t *a_hi, const uint16_t *a_lo, int64_t m, int64_t k, int64_t lda,
                                    const uint16_t *b_hi, const uint16_t *b_lo, int64_t n, int64_t ldb, float *c,
-                                   int64_t ldc, bd_stream_t stream) {
+                                   int64_t ldc, void *workspace, size_t workspace_bytes, bd_stream_t stream) {
     if (m < 1 || k < 1 || n < 1 || lda < k || ldb < k || ldc < n || !a_hi || !a_lo || !b_hi || !c)
         return BD_ERR_INVALID;
     TcArgs t{};
@@ -781,6 +882,8 @@ extern "C" int bd_gemm_bf16_split3(const uint16_t *a_hi, const uint16_t *a_lo, i
     t.K = k;
     t.ld_out = ldc;
     t.out = c;
+    t.split_ws = workspace;
+    t.split_ws_bytes = workspace_bytes;
     TcParts more;
     more.a2 = reinterpret_cast<const int8_t *>(a_lo);
     more.b2 = reinterpret_cast<const int8_t *>(b_hi);

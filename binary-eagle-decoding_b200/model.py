@@ -233,6 +233,16 @@ def _frozen_halves(owner, operand: Tensor) -> _FrozenOperand:
     return cache
 
 
+def _split_workspace(device: torch.device, m: int, n: int, k: int, parts: int) -> tuple[int | None, int]:
+    """The split-K workspace of a bf16 split product (one per device, used in stream
+    order), or (None, 0) when the shape runs unsplit."""
+    nbytes = int(_lib.load().bd_gemm_split_workspace_bytes(m, n, k, parts))
+    if nbytes == 0:
+        return None, 0
+    buf = ops.workspace(device, "gemm_split", nbytes)
+    return buf.data_ptr(), buf.numel()
+
+
 def _product(x: Tensor, b_hi: Tensor, b_lo: Tensor | None, ld_b: int, n: int) -> Tensor:
     """``x [m, k] @ (b_hi + b_lo)^T`` at fp32 accuracy on the tcgen05 tensor cores:
     ``x`` split into bf16 halves, ``b`` given as halves ``[n, ld_b]``
@@ -242,8 +252,9 @@ def _product(x: Tensor, b_hi: Tensor, b_lo: Tensor | None, ld_b: int, n: int) ->
     if ld != ld_b:
         raise ValueError("operand strides differ")
     out = torch.empty((m, n), dtype=torch.float32, device=x.device)
+    ws, nbytes = _split_workspace(x.device, m, n, k, 2 if b_lo is None else 3)
     _lib.call("bd_gemm_bf16_split3", x_hi.data_ptr(), x_lo.data_ptr(), m, k, ld, b_hi.data_ptr(),
-              None if b_lo is None else b_lo.data_ptr(), n, ld_b, out.data_ptr(), n, _stream(x.device))
+              None if b_lo is None else b_lo.data_ptr(), n, ld_b, out.data_ptr(), n, ws, nbytes, _stream(x.device))
     return out
 
 
@@ -382,8 +393,9 @@ class _ProjectionFn(torch.autograd.Function):
         if need[0] or need[4] or need[5]:
             signs_t = module.signs_t_bf16(ld_o)
             dv = torch.empty((tokens, inner), dtype=torch.float32, device=device)
+            sws, snb = _split_workspace(device, tokens, inner, outer, 2)
             _lib.call("bd_gemm_bf16_split", hi.data_ptr(), lo.data_ptr(), tokens, outer, ld_o, signs_t.data_ptr(),
-                      inner, ld_o, dv.data_ptr(), inner, stream)
+                      inner, ld_o, dv.data_ptr(), inner, sws, snb, stream)
             dx = torch.empty_like(x)
             d_gain = torch.empty(inner, dtype=torch.float32, device=device)
             d_clip = torch.empty(1, dtype=torch.float32, device=device)

@@ -22,8 +22,8 @@ import torch.distributed as dist
 from torch import Tensor, nn
 
 from . import _lib, ops
-from .model import (HE4, Projection, _bump, _flags, _frozen_halves, _need_cuda, _split, _stream, _to_device,
-                    deferred_checks, frozen_linear)
+from .model import (HE4, Projection, _bump, _flags, _frozen_halves, _need_cuda, _split, _split_workspace, _stream,
+                    _to_device, deferred_checks, frozen_linear)
 
 PARAMETER_GROUPS = ("sign", "scale", "midpoint", "gain", "clip", "norm")
 HEAD_ROWS = 128
@@ -365,8 +365,9 @@ def loss_head(head: Tensor, model: HE4, labels: Tensor, weights: Tensor) -> tupl
     _lib.call("bd_loss_head_grad", h_hi.data_ptr(), h_lo.data_ptr(), rows, hidden, ld_h, halves.hi.data_ptr(), v_lo,
               vocab, lab.data_ptr(), w.data_ptr(), lse.data_ptr(), dl_hi.data_ptr(), dl_lo.data_ptr(), ld_v, stream)
     d_head = torch.empty((rows, hidden), dtype=torch.float32, device=device)
+    ws, nbytes = _split_workspace(device, rows, hidden, vocab, 2 if lo_t is None else 3)
     _lib.call("bd_gemm_bf16_split3", dl_hi.data_ptr(), dl_lo.data_ptr(), rows, vocab, ld_v, hi_t.data_ptr(),
-              None if lo_t is None else lo_t.data_ptr(), hidden, ld_v, d_head.data_ptr(), hidden, stream)
+              None if lo_t is None else lo_t.data_ptr(), hidden, ld_v, d_head.data_ptr(), hidden, ws, nbytes, stream)
     return total.reshape(()), d_head
 
 

@@ -526,7 +526,17 @@ int bd_sign_cols_bf16(const float *latent, int64_t rows, int64_t cols, uint16_t 
 int bd_codes_transpose_bf16(const int8_t *codes, int64_t rows, int64_t cols, int64_t ld, uint16_t *out,
                             int64_t ld_t, bd_stream_t stream);
 int bd_gemm_bf16_split(const uint16_t *a_hi, const uint16_t *a_lo, int64_t m, int64_t k, int64_t lda,
-                       const uint16_t *b, int64_t n, int64_t ldb, float *c, int64_t ldc, bd_stream_t stream);
+                       const uint16_t *b, int64_t n, int64_t ldb, float *c, int64_t ldc, void *workspace,
+                       size_t workspace_bytes, bd_stream_t stream);
+/* Split-K workspace of bd_gemm_bf16_split / bd_gemm_bf16_split3 (parts = 2 or 3
+ * operand pairs) for an m x n x k product: when the 128 x 256 output tiles
+ * leave more than half of the GPU idle, the K reduction is cut into slices on
+ * more CTAs, each writing an fp32 partial tile, and the last slice of a tile to
+ * finish adds them in slice order (deterministic).  0 = no split for this
+ * shape.  The workspace (256-byte aligned) must be zero when first used; the
+ * calls leave its counters zero.  Calls sharing one workspace must be ordered
+ * (one stream); a NULL or smaller workspace runs the product unsplit. */
+size_t bd_gemm_split_workspace_bytes(int64_t m, int64_t n, int64_t k, int parts);
 
 /* fp32-accurate products of frozen fp32 operands on the bf16 tensor cores, for
  * FrozenLinear (w1a1_eagle/model.py:105-113) and the tied vocabulary head
@@ -546,7 +556,7 @@ int bd_split_bf16(const float *x, int64_t rows, int64_t cols, int64_t ldx, int t
  * bd_loss_head_forward: per-row softmax statistics in the GEMM's epilogue
  *   (stats: bd_loss_head_stats_count(rows, vocab) floats), then lse[r],
  *   loss_rows[r] = w[r] (lse - target logit) and their fixed-order sum *loss;
- *   BD_FLAG_NONFINITE_STATE for a non-finite row loss ("nonfinite loss").
+ *   BD_FLAG_NONFINITE_LOSS for a non-finite row loss ("nonfinite loss").
  * bd_loss_head_grad: the logits recomputed into dLoss/dlogits = w (softmax -
  *   onehot) in place, as bf16 halves [rows][ld_dl]; dLoss/dh is then
  *   bd_gemm_bf16_split3 of those halves with the transposed vocabulary halves. */
@@ -561,7 +571,7 @@ int bd_loss_head_grad(const uint16_t *h_hi, const uint16_t *h_lo, int64_t rows, 
                       bd_stream_t stream);
 int bd_gemm_bf16_split3(const uint16_t *a_hi, const uint16_t *a_lo, int64_t m, int64_t k, int64_t lda,
                         const uint16_t *b_hi, const uint16_t *b_lo, int64_t n, int64_t ldb, float *c, int64_t ldc,
-                        bd_stream_t stream);
+                        void *workspace, size_t workspace_bytes, bd_stream_t stream);
 int64_t bd_ste_weight_grad_partials(int64_t out_features, int64_t in_features);
 int bd_ste_weight_grad(const uint16_t *grad_t_hi, const uint16_t *grad_t_lo, int64_t out_features, int64_t tokens,
                        int64_t ld_t, const uint16_t *codes_t, int64_t in_features, const float *latent,
