@@ -783,11 +783,13 @@ def workload_qat(args, pkg, device, rank: int, world: int) -> list[dict]:
 
 
 def workload_qat_kernels(args, pkg, device) -> list[dict]:
-    """The tcgen05 products of the QAT update at config-5 sizes: one binary projection
-    (9728 x 2560, 4096 slot rows: the forward kind::i8 GEMM with the HE4 epilogue, the
-    input gradient and the latent gradient with the straight-through mask, both split
-    bf16) and the fused cross-entropy head (480 labelled rows x 151936 x 2560, bf16
-    vocabulary)."""
+    """The kernels of the QAT update at config-5 sizes: one binary projection (9728 x
+    2560, 4096 slot rows: the forward kind::i8 GEMM with the HE4 epilogue, the input
+    gradient and the latent gradient with the straight-through mask, both split bf16),
+    the fused cross-entropy head (480 labelled rows x 151936 x 2560, bf16 vocabulary)
+    and one layer's window attention (32 windows of 16 slots, 32 / 8 heads of 128,
+    2048 context keys, each window seeing the context before its anchor) forward and
+    backward."""
     from torch import nn
 
     qat = importlib.import_module("binary-eagle-decoding_b200.qat")
@@ -834,7 +836,47 @@ def workload_qat_kernels(args, pkg, device) -> list[dict]:
         lines.append({"workload": name, "metric": "tensor TFLOP/s (bf16-equivalent products)", "value": tf,
                       "unit": "TFLOP/s", "us_per_call": t, "frac_of_bf16_peak": tf / peak,
                       "peak": f"{peak:.1f} TFLOP/s ({kind} bf16 burst)"})
+    lines.append(train_attention_record(pkg, device, reps))
     return lines
+
+
+def train_attention_record(pkg, device, reps: int) -> dict:
+    """One layer's window attention of the QAT update on the training-attention kernels."""
+    model = importlib.import_module("binary-eagle-decoding_b200.model")
+    W, k, kvh, g, d, L = 32, 16, 8, 4, 128, 2048
+    gen = torch.Generator().manual_seed(13)
+    query = torch.randn((W, k, kvh, g, d), generator=gen).to(device).requires_grad_()
+    ctx_k, ctx_v = (torch.randn((L, kvh, d), generator=gen).half().float().to(device).requires_grad_()
+                    for _ in range(2))
+    slot_k, slot_v = (torch.randn((W, k, kvh, d), generator=gen).half().float().to(device).requires_grad_()
+                      for _ in range(2))
+    anchors = torch.tensor([16 + (L - 32) * i // W for i in range(W)], device=device)
+    allowed = torch.arange(L, device=device)[None, None, :] < anchors[:, None, None]
+    upstream = torch.randn((W, k, kvh, g, d), generator=gen).to(device)
+    inputs = (query, ctx_k, ctx_v, slot_k, slot_v)
+
+    def forward():
+        return model.train_attention(*inputs, allowed, None)
+
+    def both():
+        for t in inputs:
+            t.grad = None
+        (forward() * upstream).sum().backward()
+
+    for _ in range(3):
+        both()
+    torch.cuda.synchronize()
+    with torch.no_grad():
+        fwd_us = _events_us(forward, reps)
+    both_us = _events_us(both, reps)
+    # query-key pairs the mask allows (context before each anchor, plus the 16 slots), x 32 heads
+    pairs = int(((anchors + k) * k).sum()) * kvh * g
+    flop = pairs * d * 2 * 2  # S = q k and O = p v, 2 flops per multiply-add
+    return {"workload": "window attention of one layer, 32 windows x 16 slots, 32 / 8 heads of 128, 2048 context "
+                        "keys: forward, forward + backward", "metric": "us per call", "value": both_us, "unit": "us",
+            "forward_us": fwd_us, "forward_backward_us": both_us, "visible_pairs": pairs,
+            "forward_TFLOP/s": flop / (fwd_us * 1e-6) / 1e12,
+            "note": "fp32-precision products as fp16 hi + lo mma.sync pairs: 2 MMAs per product forward"}
 
 
 def run_workload(args, rank: int, world: int, local_rank: int) -> None:
