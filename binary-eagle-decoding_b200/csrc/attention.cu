@@ -3,9 +3,9 @@
 // for up to 16 query slots per q head, grouped-query (q head h uses kv head
 // h / (heads / kv_heads)).
 //
-// Split over keys (flash decoding): CTA (kv head, chunk of 128 keys) stages its
+// Split over keys (flash decoding): CTA (kv head, chunk of 256 keys) stages its
 // K and V rows in shared memory with cp.async; warp w owns q head
-// kv * groups + (w & 3), its 16 query rows and half (w >> 2) of the keys.  S = Q K^T and O = P V run on
+// kv * groups + (w & 3), its 16 query rows and quarter (w >> 2) of the keys.  S = Q K^T and O = P V run on
 // m16n8k16 fp16 MMAs with fp32 accumulation (K fragments by ldmatrix, V by
 // ldmatrix.trans, P re-packed from the S accumulators).  The cached K and V are
 // fp16 values, exact as MMA operands; the fp32 queries and probabilities are
