@@ -85,19 +85,28 @@ struct TcArgs {
     size_t split_ws_bytes;
 };
 
-// K slices per tile of a TC_F32 product: enough units to fill the GPU when the
-// tiles alone leave more than half of it idle, at least 4 k-blocks per slice.
+// K slices per tile of a TC_F32 product: the count that minimises the
+// waves of (tile, slice) units per full-K tile time, plus 5 % of a tile time per
+// slice for writing and adding the partial tiles; at least 4 k-blocks per slice,
+// at most 8 slices, and the partial tiles within half of L2.
 // The counters sit at a fixed place (the first kTcSplitCounts words) whatever the
 // shape, so that a workspace shared by products of different shapes never sees an
 // earlier call's partial sums where this call keeps its counters.
 constexpr int64_t kTcSplitCounts = 2048;  // 8 per tile: up to 256 split tiles
 
 static int tc_split_slices(int64_t tiles, int64_t nk, int sms) {
-    if (tiles * 2 > sms || tiles * 8 > kTcSplitCounts) return 1;
-    int64_t s = sms / tiles;
-    s = s < nk / 4 ? s : nk / 4;
-    s = s < 16 ? s : 16;
-    return s > 1 ? static_cast<int>(s) : 1;
+    if (tiles * 8 > kTcSplitCounts) return 1;
+    int best = 1;
+    double best_cost = static_cast<double>((tiles + sms - 1) / sms) + 0.05;
+    for (int s = 2; s <= 8 && s <= nk / 4; ++s) {
+        if (static_cast<double>(tiles) * s * kTcBM * 256 * sizeof(float) > 64.0 * (1 << 20)) break;
+        const double cost = static_cast<double>((tiles * s + sms - 1) / sms) / s + 0.05 * s;
+        if (cost < best_cost - 1e-9) {
+            best = s;
+            best_cost = cost;
+        }
+    }
+    return best;
 }
 static size_t tc_split_bytes(int64_t tiles, int slices, int bn) {
     return kTcSplitCounts * sizeof(int32_t) + static_cast<size_t>(tiles) * slices * kTcBM * bn * sizeof(float);

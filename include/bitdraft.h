@@ -530,10 +530,11 @@ int bd_gemm_bf16_split(const uint16_t *a_hi, const uint16_t *a_lo, int64_t m, in
                        size_t workspace_bytes, bd_stream_t stream);
 /* Split-K workspace of bd_gemm_bf16_split / bd_gemm_bf16_split3 (parts = 2 or 3
  * operand pairs) for an m x n x k product: when the 128 x 256 output tiles
- * leave more than half of the GPU idle, the K reduction is cut into slices on
+ * leave SMs idle in their last wave, the K reduction is cut into slices on
  * more CTAs, each writing an fp32 partial tile, and the last slice of a tile to
- * finish adds them in slice order (deterministic).  0 = no split for this
- * shape.  The workspace (256-byte aligned) must be zero when first used; the
+ * finish adds them in slice order (deterministic).  The slice count minimises
+ * the waves of (tile, slice) units per tile, at most 8 slices and partial tiles
+ * within half of L2.  0 = no split for this shape.  The workspace (256-byte aligned) must be zero when first used; the
  * calls leave its counters zero.  Calls sharing one workspace must be ordered
  * (one stream); a NULL or smaller workspace runs the product unsplit. */
 size_t bd_gemm_split_workspace_bytes(int64_t m, int64_t n, int64_t k, int parts);
