@@ -1,0 +1,352 @@
+// Row-wise elementwise chains of the training forward and their backward, one
+// launch each instead of torch's chains of small kernels:
+//   rms_rows_*   rms(x, w) = x * rsqrt(mean(x^2) + eps) * w over the last axis
+//                (w1a1_eagle/model.py:50-51): attn/ffn/encoder/output norms;
+//   head_post_*  per (row, head) of d values: the head rms with its weight
+//                (q_norm / k_norm), the rotate-half rotary of the row's position
+//                (model.py:54-63), and optionally the fp16 storage rounding with
+//                a straight-through gradient (cache_storage, model.py:98-102).
+// The elementwise operations keep the reference's order and roundings (no
+// contraction: every product and sum rounds as torch's separate kernels do);
+// only the mean's summation order is this kernel's.  The weight gradients come
+// as per-CTA partial rows summed afterwards in a fixed order.
+#include "kernels.cuh"
+
+namespace bd {
+
+constexpr int kRowsThreads = 256;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, d));
+    return v;
+}
+
+// CTA-wide sum in a fixed order (warps in order after a butterfly within each).
+__device__ __forceinline__ float cta_sum(float v, float *scratch) {
+    v = warp_sum(v);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    float total = 0.0f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) total = __fadd_rn(total, scratch[w]);
+    return total;
+}
+
+// One CTA per row.
+__global__ void __launch_bounds__(kRowsThreads) rms_rows_fwd_kernel(const float *__restrict__ x, int64_t cols,
+                                                                  const float *__restrict__ w, float eps,
+                                                                  float *__restrict__ out, float *__restrict__ inv) {
+    __shared__ float scratch[kRowsThreads / 32];
+    const float *xr = x + blockIdx.x * cols;
+    float ss = 0.0f;
+    for (int64_t k = threadIdx.x; k < cols; k += blockDim.x) ss = __fadd_rn(ss, __fmul_rn(xr[k], xr[k]));
+    const float total = cta_sum(ss, scratch);
+    const float r = rsqrtf(__fadd_rn(__fdiv_rn(total, static_cast<float>(cols)), eps));
+    if (threadIdx.x == 0) inv[blockIdx.x] = r;
+    float *o = out + blockIdx.x * cols;
+    for (int64_t k = threadIdx.x; k < cols; k += blockDim.x) o[k] = __fmul_rn(__fmul_rn(xr[k], r), w[k]);
+}
+
+// dx = r u - (r^3 / n) x sum(u x), u = dy w; dw partial (this CTA's rows) = sum dy x r.
+__global__ void __launch_bounds__(kRowsThreads) rms_rows_bwd_kernel(const float *__restrict__ x, int64_t rows,
+                                                                  int64_t cols, const float *__restrict__ w,
+                                                                  const float *__restrict__ inv,
+                                                                  const float *__restrict__ dy, float *__restrict__ dx,
+                                                                  float *__restrict__ dw_part, int rows_per_cta) {
+    __shared__ float scratch[kRowsThreads / 32];
+    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_cta;
+    float *dwp = dw_part + blockIdx.x * cols;
+    for (int64_t k = threadIdx.x; k < cols; k += blockDim.x) dwp[k] = 0.0f;
+    for (int64_t row = r0; row < r0 + rows_per_cta && row < rows; ++row) {
+        const float *xr = x + row * cols, *g = dy + row * cols;
+        const float r = inv[row];
+        float s = 0.0f;
+        for (int64_t k = threadIdx.x; k < cols; k += blockDim.x) s = __fadd_rn(s, __fmul_rn(__fmul_rn(g[k], w[k]), xr[k]));
+        const float total = cta_sum(s, scratch);
+        const float c = __fdiv_rn(__fmul_rn(__fmul_rn(r, r), r), static_cast<float>(cols)) * total;
+        float *d = dx + row * cols;
+        for (int64_t k = threadIdx.x; k < cols; k += blockDim.x) {
+            const float u = __fmul_rn(g[k], w[k]);
+            d[k] = __fsub_rn(__fmul_rn(r, u), __fmul_rn(c, xr[k]));
+            dwp[k] = __fadd_rn(dwp[k], __fmul_rn(__fmul_rn(g[k], xr[k]), r));
+        }
+    }
+}
+
+// The weight gradient: partial rows summed in order.
+__global__ void sum_partials_kernel(const float *__restrict__ part, int64_t nparts, int64_t cols,
+                                    float *__restrict__ out) {
+    const int64_t k = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (k >= cols) return;
+    float s = 0.0f;
+    for (int64_t p = 0; p < nparts; ++p) s = __fadd_rn(s, part[p * cols + k]);
+    out[k] = s;
+}
+
+struct HeadPostArgs {
+    const float *x;  // [rows][ld_x], head h at columns h * d
+    int64_t ld_x, rows;
+    int heads, d;
+    const float *w;        // [d] head rms weight, or null: no rms
+    float eps;
+    const int64_t *pos;    // [rows] positions, or null: no rotary
+    const float *freq;     // [d / 2] rotary frequencies
+    int fp16;              // round the output through fp16 (straight-through gradient)
+    float *out;            // [rows][heads][d]
+    float *inv;            // [rows][heads] rms scale (forward writes it, backward reads it)
+    const float *dy;       // backward: [rows][heads][d]
+    float *dx;             // backward: [rows][ld_x] (head columns only)
+    float *dw_part;        // backward: [grid][d]
+    int32_t *flags;
+};
+
+// One warp per (row, head); lane l holds the pairs (e, e + d/2) for e = l, l + 32, ...
+// (d <= 256).
+constexpr int kHeadPairs = 4;
+
+__global__ void __launch_bounds__(kRowsThreads) head_post_fwd_kernel(const HeadPostArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int64_t item = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (item >= a.rows * a.heads) return;
+    const int64_t row = item / a.heads;
+    const int h = static_cast<int>(item % a.heads);
+    const int half = a.d / 2;
+    const float *xr = a.x + row * a.ld_x + static_cast<int64_t>(h) * a.d;
+    float lo[kHeadPairs], hi[kHeadPairs];
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kHeadPairs; ++i) {
+        const int e = lane + 32 * i;
+        lo[i] = e < half ? xr[e] : 0.0f;
+        hi[i] = e < half ? xr[e + half] : 0.0f;
+    }
+    // the mean of squares in element order within the lane, lanes by butterfly
+#pragma unroll
+    for (int i = 0; i < kHeadPairs; ++i) ss = __fadd_rn(ss, __fadd_rn(__fmul_rn(lo[i], lo[i]), __fmul_rn(hi[i], hi[i])));
+    float r = 1.0f;
+    if (a.w) {
+        r = rsqrtf(__fadd_rn(__fdiv_rn(warp_sum(ss), static_cast<float>(a.d)), a.eps));
+        if (lane == 0) a.inv[item] = r;
+#pragma unroll
+        for (int i = 0; i < kHeadPairs; ++i) {
+            const int e = lane + 32 * i;
+            if (e < half) {
+                lo[i] = __fmul_rn(__fmul_rn(lo[i], r), a.w[e]);
+                hi[i] = __fmul_rn(__fmul_rn(hi[i], r), a.w[e + half]);
+            }
+        }
+    }
+    bool bad = false;
+    float *o = a.out + item * a.d;
+#pragma unroll
+    for (int i = 0; i < kHeadPairs; ++i) {
+        const int e = lane + 32 * i;
+        if (e >= half) continue;
+        float y0 = lo[i], y1 = hi[i];
+        if (a.pos) {
+            // value * cos + cat(-second, first) * sin, angle = position * frequency
+            const float angle = __fmul_rn(static_cast<float>(a.pos[row]), a.freq[e]);
+            const float c = cosf(angle), s = sinf(angle);
+            y0 = __fadd_rn(__fmul_rn(lo[i], c), __fmul_rn(-hi[i], s));
+            y1 = __fadd_rn(__fmul_rn(hi[i], c), __fmul_rn(lo[i], s));
+        }
+        if (a.fp16) {
+            y0 = __half2float(__float2half_rn(y0));
+            y1 = __half2float(__float2half_rn(y1));
+            bad |= !isfinite(y0) || !isfinite(y1);
+        }
+        o[e] = y0;
+        o[e + half] = y1;
+    }
+    if (__any_sync(0xffffffffu, bad) && lane == 0) set_flag(a.flags, BD_FLAG_CACHE_OVERFLOW);
+}
+
+// Gradient of the forward above (the fp16 rounding passes it straight through).
+__global__ void __launch_bounds__(kRowsThreads) head_post_bwd_kernel(const HeadPostArgs a, int items_per_warp) {
+    extern __shared__ float dws[];  // [warps][d]
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const int half = a.d / 2;
+    float dwl[kHeadPairs] = {}, dwh[kHeadPairs] = {};
+    const int64_t first = (static_cast<int64_t>(blockIdx.x) * nwarps + warp) * items_per_warp;
+    for (int64_t item = first; item < first + items_per_warp && item < a.rows * a.heads; ++item) {
+        const int64_t row = item / a.heads;
+        const int h = static_cast<int>(item % a.heads);
+        const float *xr = a.x + row * a.ld_x + static_cast<int64_t>(h) * a.d;
+        const float *g = a.dy + item * a.d;
+        float gl[kHeadPairs], gh[kHeadPairs], xl[kHeadPairs], xh[kHeadPairs];
+#pragma unroll
+        for (int i = 0; i < kHeadPairs; ++i) {
+            const int e = lane + 32 * i;
+            const bool live = e < half;
+            gl[i] = live ? g[e] : 0.0f;
+            gh[i] = live ? g[e + half] : 0.0f;
+            xl[i] = live ? xr[e] : 0.0f;
+            xh[i] = live ? xr[e + half] : 0.0f;
+            if (live && a.pos) {
+                // rotary backward: dy_e = g_e c + g_{e+h} s, dy_{e+h} = g_{e+h} c - g_e s
+                const float angle = __fmul_rn(static_cast<float>(a.pos[row]), a.freq[e]);
+                const float c = cosf(angle), s = sinf(angle);
+                const float a0 = __fadd_rn(__fmul_rn(gl[i], c), __fmul_rn(gh[i], s));
+                const float a1 = __fsub_rn(__fmul_rn(gh[i], c), __fmul_rn(gl[i], s));
+                gl[i] = a0;
+                gh[i] = a1;
+            }
+        }
+        float *d = a.dx + row * a.ld_x + static_cast<int64_t>(h) * a.d;
+        if (!a.w) {
+#pragma unroll
+            for (int i = 0; i < kHeadPairs; ++i) {
+                const int e = lane + 32 * i;
+                if (e < half) {
+                    d[e] = gl[i];
+                    d[e + half] = gh[i];
+                }
+            }
+            continue;
+        }
+        const float r = a.inv[item];
+        float s = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kHeadPairs; ++i) {
+            const int e = lane + 32 * i;
+            if (e < half)
+                s = __fadd_rn(s, __fadd_rn(__fmul_rn(__fmul_rn(gl[i], a.w[e]), xl[i]),
+                                           __fmul_rn(__fmul_rn(gh[i], a.w[e + half]), xh[i])));
+        }
+        const float c = __fdiv_rn(__fmul_rn(__fmul_rn(r, r), r), static_cast<float>(a.d)) * warp_sum(s);
+#pragma unroll
+        for (int i = 0; i < kHeadPairs; ++i) {
+            const int e = lane + 32 * i;
+            if (e >= half) continue;
+            d[e] = __fsub_rn(__fmul_rn(r, __fmul_rn(gl[i], a.w[e])), __fmul_rn(c, xl[i]));
+            d[e + half] = __fsub_rn(__fmul_rn(r, __fmul_rn(gh[i], a.w[e + half])), __fmul_rn(c, xh[i]));
+            dwl[i] = __fadd_rn(dwl[i], __fmul_rn(__fmul_rn(gl[i], xl[i]), r));
+            dwh[i] = __fadd_rn(dwh[i], __fmul_rn(__fmul_rn(gh[i], xh[i]), r));
+        }
+    }
+    if (!a.w) return;
+#pragma unroll
+    for (int i = 0; i < kHeadPairs; ++i) {
+        const int e = lane + 32 * i;
+        if (e < half) {
+            dws[warp * a.d + e] = dwl[i];
+            dws[warp * a.d + e + half] = dwh[i];
+        }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < a.d; e += blockDim.x) {
+        float t = 0.0f;
+        for (int w = 0; w < nwarps; ++w) t = __fadd_rn(t, dws[w * a.d + e]);
+        a.dw_part[static_cast<int64_t>(blockIdx.x) * a.d + e] = t;
+    }
+}
+
+static int rows_grid(int64_t items, int per) { return static_cast<int>((items + per - 1) / per); }
+
+}  // namespace bd
+
+using namespace bd;
+
+extern "C" int bd_rms_forward(const float *x, int64_t rows, int64_t cols, const float *weight, float eps, float *out,
+                           float *inv, bd_stream_t stream) {
+    if (rows < 0 || cols < 1 || rows > 0x7fffffff) return BD_ERR_INVALID;
+    if (rows == 0) return BD_OK;
+    if (!x || !weight || !out || !inv) return BD_ERR_INVALID;
+    rms_rows_fwd_kernel<<<static_cast<unsigned>(rows), kRowsThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+        x, cols, weight, eps, out, inv);
+    BD_CHECK_LAUNCH();
+    return BD_OK;
+}
+
+extern "C" int64_t bd_rms_partials(int64_t rows) { return rows < 1 ? 0 : (rows + 7) / 8; }
+
+extern "C" int bd_rms_backward(const float *x, int64_t rows, int64_t cols, const float *weight, const float *inv,
+                                    const float *dy, float *dx, float *dw_partials, float *dw, bd_stream_t stream) {
+    if (rows < 0 || cols < 1 || rows > 0x7fffffff) return BD_ERR_INVALID;
+    if (rows == 0) return BD_OK;
+    if (!x || !weight || !inv || !dy || !dx || !dw_partials || !dw) return BD_ERR_INVALID;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int64_t parts = bd_rms_partials(rows);
+    rms_rows_bwd_kernel<<<static_cast<unsigned>(parts), kRowsThreads, 0, st>>>(x, rows, cols, weight, inv, dy, dx,
+                                                                             dw_partials, 8);
+    BD_CHECK_LAUNCH();
+    sum_partials_kernel<<<rows_grid(cols, 256), 256, 0, st>>>(dw_partials, parts, cols, dw);
+    BD_CHECK_LAUNCH();
+    return BD_OK;
+}
+
+static bool head_args_ok(const HeadPostArgs &a) {
+    return a.rows >= 0 && a.heads >= 1 && a.d >= 2 && a.d % 2 == 0 && a.d <= 2 * 32 * kHeadPairs &&
+           a.ld_x >= static_cast<int64_t>(a.heads) * a.d && a.x && a.out && (!a.pos || a.freq) && (!a.w || a.inv);
+}
+
+extern "C" int bd_head_post(const float *x, int64_t ld_x, int64_t rows, int heads, int head_dim, const float *weight,
+                            float eps, const int64_t *positions, const float *frequencies, int fp16, float *out,
+                            float *inv, int32_t *flags, bd_stream_t stream) {
+    HeadPostArgs a{};
+    a.x = x;
+    a.ld_x = ld_x;
+    a.rows = rows;
+    a.heads = heads;
+    a.d = head_dim;
+    a.w = weight;
+    a.eps = eps;
+    a.pos = positions;
+    a.freq = frequencies;
+    a.fp16 = fp16;
+    a.out = out;
+    a.inv = inv;
+    a.flags = flags;
+    if (!head_args_ok(a)) return BD_ERR_INVALID;
+    if (rows == 0) return BD_OK;
+    const int64_t items = rows * heads;
+    head_post_fwd_kernel<<<rows_grid(items, kRowsThreads / 32), kRowsThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
+    BD_CHECK_LAUNCH();
+    return BD_OK;
+}
+
+// (row, head) items per warp of the backward: enough warps to fill the GPU, few
+// partial rows for the weight gradient.
+static int head_items_per_warp(int64_t items) { return items >= 148 * 64 ? 8 : 1; }
+
+extern "C" int64_t bd_head_post_partials(int64_t rows, int heads) {
+    if (rows < 1 || heads < 1) return 0;
+    const int64_t items = rows * heads;
+    return rows_grid(items, static_cast<int64_t>(kRowsThreads / 32) * head_items_per_warp(items));
+}
+
+extern "C" int bd_head_post_backward(const float *x, int64_t ld_x, int64_t rows, int heads, int head_dim,
+                                     const float *weight, const float *inv, const int64_t *positions,
+                                     const float *frequencies, const float *dy, float *dx, float *dw_partials,
+                                     float *dw, bd_stream_t stream) {
+    HeadPostArgs a{};
+    a.x = x;
+    a.ld_x = ld_x;
+    a.rows = rows;
+    a.heads = heads;
+    a.d = head_dim;
+    a.w = weight;
+    a.inv = const_cast<float *>(inv);
+    a.pos = positions;
+    a.freq = frequencies;
+    a.out = dx;  // checked as non-null below
+    a.dy = dy;
+    a.dx = dx;
+    a.dw_part = dw_partials;
+    if (!head_args_ok(a) || !dy || !dx || (weight && (!dw_partials || !dw))) return BD_ERR_INVALID;
+    if (rows == 0) return BD_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int64_t items = rows * heads;
+    const int per = head_items_per_warp(items);
+    const int64_t grid = bd_head_post_partials(rows, heads);
+    const size_t smem = static_cast<size_t>(kRowsThreads / 32) * head_dim * sizeof(float);
+    head_post_bwd_kernel<<<static_cast<unsigned>(grid), kRowsThreads, smem, st>>>(a, per);
+    BD_CHECK_LAUNCH();
+    if (weight) {
+        sum_partials_kernel<<<rows_grid(head_dim, 256), 256, 0, st>>>(dw_partials, grid, head_dim, dw);
+        BD_CHECK_LAUNCH();
+    }
+    return BD_OK;
+}

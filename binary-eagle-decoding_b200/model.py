@@ -62,8 +62,43 @@ class Geometry:
 # --------------------------------------------------------------------------- elementwise helpers
 
 
+class _RmsFn(torch.autograd.Function):
+    """``rms`` on the GPU: one kernel forward (``bd_rms_forward``), one backward
+    (``bd_rms_backward``: input and weight gradients)."""
+
+    @staticmethod
+    def forward(ctx, value, weight, epsilon):
+        cols = value.shape[-1]
+        x = value.reshape(-1, cols).float().contiguous()
+        w = weight.detach().float().contiguous()
+        rows = x.shape[0]
+        out = torch.empty_like(x)
+        inv = torch.empty(rows, dtype=torch.float32, device=x.device)
+        _lib.call("bd_rms_forward", x.data_ptr(), rows, cols, w.data_ptr(), float(epsilon), out.data_ptr(),
+                  inv.data_ptr(), _stream(x.device))
+        ctx.save_for_backward(x, w, inv)
+        ctx.shape = value.shape
+        return out.view(value.shape)
+
+    @staticmethod
+    def backward(ctx, grad):
+        x, w, inv = ctx.saved_tensors
+        rows, cols = x.shape
+        g = grad.reshape(rows, cols).float().contiguous()
+        dx = torch.empty_like(x)
+        parts = torch.empty((int(_lib.load().bd_rms_partials(rows)), cols), dtype=torch.float32, device=x.device)
+        dw = torch.empty(cols, dtype=torch.float32, device=x.device)
+        _lib.call("bd_rms_backward", x.data_ptr(), rows, cols, w.data_ptr(), inv.data_ptr(), g.data_ptr(),
+                  dx.data_ptr(), parts.data_ptr(), dw.data_ptr(), _stream(x.device), kernels=2)
+        return dx.view(ctx.shape), dw, None
+
+
 def rms(value: Tensor, weight: Tensor, epsilon: float) -> Tensor:
-    """``value / sqrt(mean(value^2) + eps) * weight`` over the last axis (``model.py:50-51``)."""
+    """``value / sqrt(mean(value^2) + eps) * weight`` over the last axis (``model.py:50-51``);
+    on CUDA tensors one kernel each way (``_RmsFn``), on CPU tensors the reference's
+    expression."""
+    if value.is_cuda and value.numel() > 0:
+        return _RmsFn.apply(value, weight, epsilon)
     return value * torch.rsqrt(value.square().mean(-1, keepdim=True) + epsilon) * weight
 
 
@@ -103,6 +138,73 @@ def cache_storage(value: Tensor) -> Tensor:
     elif not bool(torch.isfinite(rounded).all()):
         raise ValueError("F16 cache storage overflow")
     return value + (rounded - value).detach()
+
+
+class _HeadPostFn(torch.autograd.Function):
+    """Per (row, head) of ``d`` values: the head rms with ``weight`` (or none), the
+    rotary of the row's position (or none) and the fp16 storage rounding with a
+    straight-through gradient (or none), one kernel each way (``bd_head_post``)."""
+
+    @staticmethod
+    def forward(ctx, value, weight, positions, frequencies, epsilon, fp16, heads, dim):
+        rows = value.shape[0]
+        x = value.reshape(rows, heads * dim).float().contiguous()
+        device = x.device
+        w = None if weight is None else weight.detach().float().contiguous()
+        out = torch.empty((rows, heads, dim), dtype=torch.float32, device=device)
+        inv = torch.empty((rows, heads), dtype=torch.float32, device=device) if w is not None else None
+        flags, now = _flags(device)
+        _lib.call("bd_head_post", x.data_ptr(), heads * dim, rows, heads, dim, None if w is None else w.data_ptr(),
+                  float(epsilon), None if positions is None else positions.data_ptr(),
+                  None if frequencies is None else frequencies.data_ptr(), int(fp16), out.data_ptr(),
+                  None if inv is None else inv.data_ptr(), flags.ptr, _stream(device))
+        if now:
+            flags.check()
+        ctx.save_for_backward(x, w, inv, positions, frequencies)
+        ctx.sizes = (rows, heads, dim, value.shape)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad):
+        x, w, inv, positions, frequencies = ctx.saved_tensors
+        rows, heads, dim, shape = ctx.sizes
+        device = x.device
+        g = grad.reshape(rows, heads, dim).float().contiguous()
+        if w is None and positions is None:  # the fp16 rounding alone: straight through
+            return g.view(shape), None, None, None, None, None, None, None
+        dx = torch.empty_like(x)
+        parts = dw = None
+        if w is not None:
+            parts = torch.empty((int(_lib.load().bd_head_post_partials(rows, heads)), dim), dtype=torch.float32,
+                                device=device)
+            dw = torch.empty(dim, dtype=torch.float32, device=device)
+        _lib.call("bd_head_post_backward", x.data_ptr(), heads * dim, rows, heads, dim,
+                  None if w is None else w.data_ptr(), None if inv is None else inv.data_ptr(),
+                  None if positions is None else positions.data_ptr(),
+                  None if frequencies is None else frequencies.data_ptr(), g.data_ptr(), dx.data_ptr(),
+                  None if parts is None else parts.data_ptr(), None if dw is None else dw.data_ptr(),
+                  _stream(device), kernels=1 if w is None else 2)
+        return dx.view(shape), dw, None, None, None, None, None, None
+
+
+def head_post(value: Tensor, heads: int, dim: int, weight: Tensor | None, epsilon: float,
+              positions: Tensor | None, theta: float, fp16: bool) -> Tensor:
+    """``[rows, heads * dim]`` -> ``[rows, heads, dim]``: ``rms`` with ``weight`` per head, then
+    ``rope`` at ``positions``, then ``cache_storage`` when ``fp16`` (each step optional),
+    as ``Layer.forward`` applies them to queries, keys and values (``model.py:196-218``)."""
+    rows = value.shape[0]
+    if not value.is_cuda:
+        out = value.reshape(rows, heads, dim)
+        if weight is not None:
+            out = rms(out, weight, epsilon)
+        if positions is not None:
+            out = rope(out, positions, theta)
+        return cache_storage(out) if fp16 else out
+    frequencies = None
+    if positions is not None:
+        positions = positions.to(torch.int64).contiguous()
+        frequencies = _frequencies(dim, theta, value.device)
+    return _HeadPostFn.apply(value, weight, positions, frequencies, epsilon, fp16, heads, dim)
 
 
 def _to_device(values: list[int], device: torch.device) -> Tensor:
@@ -729,13 +831,14 @@ class Layer(nn.Module):
     def _keys(self, key: Tensor, positions: Tensor) -> Tensor:
         """Head rms, rotary, fp16 storage of raw keys ``[n, kvh, d]`` (``model.py:196-200, 211-213``)."""
         cfg = self.geometry
-        return cache_storage(rope(rms(key, self.k_norm, cfg.epsilon), positions, cfg.theta))
+        return head_post(key.reshape(key.shape[0], -1), cfg.kv_heads, cfg.head_dim, self.k_norm, cfg.epsilon, positions,
+                         cfg.theta, True)
 
     def context(self, encoded: Tensor, positions: Tensor) -> tuple[Tensor, Tensor]:
         """Context keys (normed, rotated) and values through fp16 storage (``model.py:195-200``)."""
         cfg = self.geometry
         key, value = _stacked_linear(encoded, self, "_kv", (self.key.operand, self.value.operand))
-        return self._keys(self._heads(key, cfg.kv_heads), positions), cache_storage(self._heads(value, cfg.kv_heads))
+        return self._keys(key, positions), head_post(value, cfg.kv_heads, cfg.head_dim, None, 0.0, None, 0.0, True)
 
     def packed_ffn(self) -> ops.PackedFFN:
         """The SwiGLU operands in the fused decode block's layout (cached per parameter versions)."""
@@ -794,9 +897,9 @@ class Layer(nn.Module):
         query, key, value = _stacked_linear(norm, self, "_qkv",
                                             (self.query.operand, self.key.operand, self.value.operand))
         flat = positions.reshape(-1)
-        query = rope(rms(self._heads(query, cfg.heads), self.q_norm, cfg.epsilon), flat, cfg.theta)
+        query = head_post(query, cfg.heads, cfg.head_dim, self.q_norm, cfg.epsilon, flat, cfg.theta, False)
         key = self._keys(self._heads(key, cfg.kv_heads), flat)
-        value = cache_storage(self._heads(value, cfg.kv_heads))
+        value = head_post(value, cfg.kv_heads, cfg.head_dim, None, 0.0, None, 0.0, True)
         attended = _window_attention(
             query.view(windows, slots, cfg.kv_heads, groups, cfg.head_dim), context[0], context[1],
             key.view(windows, slots, cfg.kv_heads, cfg.head_dim), value.view(windows, slots, cfg.kv_heads, cfg.head_dim),
@@ -858,8 +961,8 @@ class HE4(nn.Module):
         out = []
         for index, block in enumerate(self.blocks):
             key, value = parts[2 * index], parts[2 * index + 1]
-            out.append((block._keys(block._heads(key, cfg.kv_heads), positions),
-                        cache_storage(block._heads(value, cfg.kv_heads))))
+            out.append((block._keys(key, positions),
+                        head_post(value, cfg.kv_heads, cfg.head_dim, None, 0.0, None, 0.0, True)))
         return out
 
     def group_hidden(self, features: Tensor, tokens: tuple[int, ...], anchors: tuple[int, ...],

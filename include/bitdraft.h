@@ -415,6 +415,35 @@ int bd_attention_decode(const float *q, const uint16_t *k_cache, const uint16_t 
                         int64_t stable_keys, float *out, void *workspace, size_t workspace_bytes,
                         bd_stream_t stream);
 
+/* ================================================================ row-wise chains (training)
+ * bd_rms_forward: out = x * rsqrt(mean(x^2) + eps) * w over rows of cols
+ *   (w1a1_eagle/model.py:50-51, torch's rms expression in one kernel), inv[r]
+ *   the row's rsqrt factor for the backward.
+ * bd_rms_backward: dx and dw (dw through bd_rms_partials(rows) x cols
+ *   partial rows added in a fixed order).
+ * bd_head_post: per (row, head) of head_dim values of x [rows][ld_x] (heads side
+ *   by side): the head rms with weight (NULL: none), the rotate-half rotary at
+ *   positions[row] with frequencies[head_dim / 2] (NULL: none; model.py:54-63),
+ *   and with fp16 != 0 the fp16 storage rounding of cache_storage
+ *   (model.py:98-102; BD_FLAG_CACHE_OVERFLOW on overflow) -> out
+ *   [rows][heads][head_dim]; inv [rows][heads] the rms factors.  Products and
+ *   sums round as the reference's separate tensor operations do.
+ * bd_head_post_backward: dx [rows][ld_x] (the fp16 rounding passes the gradient
+ *   straight through) and dw (bd_head_post_partials(rows, heads) x head_dim
+ *   partials).  No reference C counterpart: the reference is torch autograd. */
+int bd_rms_forward(const float *x, int64_t rows, int64_t cols, const float *weight, float eps, float *out, float *inv,
+                bd_stream_t stream);
+int64_t bd_rms_partials(int64_t rows);
+int bd_rms_backward(const float *x, int64_t rows, int64_t cols, const float *weight, const float *inv,
+                         const float *dy, float *dx, float *dw_partials, float *dw, bd_stream_t stream);
+int bd_head_post(const float *x, int64_t ld_x, int64_t rows, int heads, int head_dim, const float *weight, float eps,
+                 const int64_t *positions, const float *frequencies, int fp16, float *out, float *inv,
+                 int32_t *flags, bd_stream_t stream);
+int64_t bd_head_post_partials(int64_t rows, int heads);
+int bd_head_post_backward(const float *x, int64_t ld_x, int64_t rows, int heads, int head_dim, const float *weight,
+                          const float *inv, const int64_t *positions, const float *frequencies, const float *dy,
+                          float *dx, float *dw_partials, float *dw, bd_stream_t stream);
+
 /* ================================================================ training attention
  * Layer.group's block attention at training sizes (w1a1_eagle/model.py:225-270,
  * the reference's torch einsum / masked_fill / softmax over [W, heads, k, L + k]
