@@ -132,9 +132,9 @@ SIGNATURES = {
     "bd_head_post_partials": (c_int64, [c_int64, c_int]),
     "bd_head_post_backward": (c_int, [P, c_int64, c_int64, c_int, c_int, P, P, P, P, P, P, P, P, P]),
     "bd_train_attention_forward": (c_int, [P, P, P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int,
-                                           ctypes.c_float, P, P, P]),
-    "bd_train_attention_backward": (c_int, [P, P, P, P, P, P, P, P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_int,
-                                            c_int, ctypes.c_float, P, P, P, P, P, P]),
+                                           ctypes.c_float, P, P, P, P]),
+    "bd_train_attention_backward": (c_int, [P, P, P, P, P, P, P, P, P, P, P, P, P, P, c_int, c_int, c_int, c_int,
+                                            c_int, c_int, ctypes.c_float, P, P, P, P, P, P]),
     "bd_ste_weight_grad_partials": (c_int64, [c_int64, c_int64]),
     "bd_ste_weight_grad": (c_int, [P, P, c_int64, c_int64, c_int64, P, c_int64, P, P, ctypes.c_float, P, c_int, P, P,
                                    P, P]),

@@ -42,6 +42,8 @@ struct TrainAttnArgs {
     const uint8_t *mctx, *mslot;
     const float *lse_in, *dr;  // [kv_heads][W][g][16]: saved log-sum-exp; rowsum(dO' * O)
     const float *unscale;      // 1 / dscale (device scalar)
+    uint8_t *live;             // [W][Lp / 64 + 1]: does the window see any key of the tile (the forward
+                               // writes it when not null; the dK/dV backward skips unseen tiles with it)
     float *o, *lse;            // forward outputs: [W][k][kv_heads][g][D], [kv_heads][W][g][16]
     float *dq;                 // [W][k][kv_heads][g][D]
     float *dkc, *dvc;          // [L][kv_heads][D]
@@ -239,7 +241,9 @@ __global__ void __launch_bounds__(256, 1) train_attn_fwd_kernel(const TrainAttnA
         __syncthreads();
         const int tile = 2 * it + kh;
         const uint8_t *mk = mbuf(st, kh);
-        if (head_live && tile < ntiles && tile_any(mk, lane)) {
+        const bool seen = head_live && tile < ntiles && tile_any(mk, lane);
+        if (a.live && h == 0 && hw == 0 && lane == 0 && tile < ntiles) a.live[static_cast<int64_t>(w) * ntiles + tile] = seen;
+        if (seen) {
             float s[8][4];
 #pragma unroll
             for (int n = 0; n < 8; ++n)
@@ -337,10 +341,13 @@ __global__ void __launch_bounds__(256, 1) train_attn_fwd_kernel(const TrainAttnA
 
 // ------------------------------------------------------------------ backward: dK, dV
 
+constexpr int kLiveList = 4096;  // windows listed per context tile (more: every window is staged)
+
 template <int DP>
 constexpr size_t kv_smem() {
-    // K and V tiles, then [2 stages] x (q hi, q lo, dO hi, dO lo rows, mask, lse, dr)
-    return static_cast<size_t>(2) * kTKeys * trow<DP>() + 2 * (static_cast<size_t>(4) * 16 * trow<DP>() + 1024 + 128);
+    // K and V tiles, then [2 stages] x (q hi, q lo, dO hi, dO lo rows, mask, lse, dr), then the window list
+    return static_cast<size_t>(2) * kTKeys * trow<DP>() + 2 * (static_cast<size_t>(4) * 16 * trow<DP>() + 1024 + 128) +
+           kLiveList * sizeof(uint16_t);
 }
 
 // dst (16 keys x DP, C fragments) += src^T (16 keys x 16 rows, C fragments of two n-tiles) . R (16 rows x DP),
@@ -403,11 +410,30 @@ __global__ void __launch_bounds__(128) train_attn_bwd_kv_kernel(const TrainAttnA
     const int tile = blockIdx.x, h = blockIdx.y;
     const bool slot_tile = tile >= nctx;
     const int wslot = tile - nctx;
-    const int nq = slot_tile ? a.g : a.W * a.g;
     auto sbase = [&](int st) { return sm + 2 * KV + st * STAGE; };
+    // the windows that see this context tile, in window order (the forward's table;
+    // without it, or with more windows than the list holds, every window)
+    uint16_t *wlist = reinterpret_cast<uint16_t *>(sm + 2 * KV + 2 * STAGE);
+    __shared__ int nlive_s;
+    const bool listed = !slot_tile && a.live && a.W <= kLiveList;
+    if (listed && threadIdx.x < 32) {
+        const int ntiles = nctx + 1;
+        int count = 0;
+        for (int w0 = 0; w0 < a.W; w0 += 32) {
+            const int w = w0 + static_cast<int>(threadIdx.x);
+            const bool on = w < a.W && a.live[static_cast<int64_t>(w) * ntiles + tile] != 0;
+            const unsigned mask = __ballot_sync(0xffffffffu, on);
+            if (on) wlist[count + __popc(mask & ((1u << threadIdx.x) - 1u))] = static_cast<uint16_t>(w);
+            count += __popc(mask);
+        }
+        if (threadIdx.x == 0) nlive_s = count;
+    }
+    __syncthreads();
+    const int nq = slot_tile ? a.g : (listed ? nlive_s : a.W) * a.g;
     // the query tile qt: its rows (hi, lo of q and dO), mask (16 x 64), lse and dr
     auto stage_q = [&](int st, int qt) {
-        const int w = slot_tile ? wslot : qt / a.g, j = slot_tile ? qt : qt % a.g;
+        const int w = slot_tile ? wslot : (listed ? static_cast<int>(wlist[qt / a.g]) : qt / a.g);
+        const int j = slot_tile ? qt : qt % a.g;
         char *b = sbase(st);
         constexpr int CH = DP * 2 / 16;
         const int64_t row0 = ((static_cast<int64_t>(h) * a.W + w) * a.g + j) * 16;
@@ -705,7 +731,7 @@ extern "C" int bd_train_attention_forward(const void *q_hi, const void *q_lo, co
                                           const void *slot_k, const void *slot_v, const uint8_t *ctx_mask,
                                           const uint8_t *slot_mask, int windows, int slots, int kv_heads,
                                           int groups, int head_dim, int keys, float scale, float *out, float *lse,
-                                          bd_stream_t stream) {
+                                          uint8_t *tile_live, bd_stream_t stream) {
     TrainAttnArgs a = {};
     a.qh = static_cast<const __half *>(q_hi);
     a.ql = static_cast<const __half *>(q_lo);
@@ -725,16 +751,17 @@ extern "C" int bd_train_attention_forward(const void *q_hi, const void *q_lo, co
     a.scale = scale;
     a.o = out;
     a.lse = lse;
+    a.live = tile_live;
     return train_attn(a, false, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int bd_train_attention_backward(const void *q_hi, const void *q_lo, const void *ctx_k, const void *ctx_v,
                                            const void *slot_k, const void *slot_v, const uint8_t *ctx_mask,
                                            const uint8_t *slot_mask, const void *dout_hi, const void *dout_lo,
-                                           const float *lse, const float *dr, const float *unscale, int windows,
-                                           int slots, int kv_heads, int groups, int head_dim, int keys, float scale,
-                                           float *dq, float *d_ctx_k, float *d_ctx_v, float *d_slot_k,
-                                           float *d_slot_v, bd_stream_t stream) {
+                                           const float *lse, const float *dr, const float *unscale,
+                                           const uint8_t *tile_live, int windows, int slots, int kv_heads,
+                                           int groups, int head_dim, int keys, float scale, float *dq, float *d_ctx_k,
+                                           float *d_ctx_v, float *d_slot_k, float *d_slot_v, bd_stream_t stream) {
     TrainAttnArgs a = {};
     a.qh = static_cast<const __half *>(q_hi);
     a.ql = static_cast<const __half *>(q_lo);
@@ -749,6 +776,7 @@ extern "C" int bd_train_attention_backward(const void *q_hi, const void *q_lo, c
     a.lse_in = lse;
     a.dr = dr;
     a.unscale = unscale;
+    a.live = const_cast<uint8_t *>(tile_live);
     a.W = windows;
     a.k = slots;
     a.kvh = kv_heads;

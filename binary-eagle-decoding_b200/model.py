@@ -713,17 +713,18 @@ class _TrainAttentionFn(torch.autograd.Function):
         vs[:, :, :slots, :dim] = slot_v.detach().permute(2, 0, 1, 3)
         out = torch.empty((windows, slots, kvh, groups, dim), dtype=torch.float32, device=device)
         lse = torch.full((kvh, windows, groups, 16), math.inf, dtype=torch.float32, device=device)
+        live = torch.empty((windows, padded // 64 + 1), dtype=torch.uint8, device=device)
         scale = 1.0 / math.sqrt(dim)
         _lib.call("bd_train_attention_forward", q_hi.data_ptr(), q_lo.data_ptr(), kc.data_ptr(), vc.data_ptr(),
                   ks.data_ptr(), vs.data_ptr(), ctx_mask.data_ptr(), slot_mask.data_ptr(), windows, slots, kvh, groups,
-                  dim, length, scale, out.data_ptr(), lse.data_ptr(), _stream(device))
-        ctx.save_for_backward(q_hi, q_lo, kc, vc, ks, vs, ctx_mask, slot_mask, out, lse)
+                  dim, length, scale, out.data_ptr(), lse.data_ptr(), live.data_ptr(), _stream(device))
+        ctx.save_for_backward(q_hi, q_lo, kc, vc, ks, vs, ctx_mask, slot_mask, out, lse, live)
         ctx.sizes = (windows, slots, kvh, groups, dim, length, dp, scale)
         return out
 
     @staticmethod
     def backward(ctx, grad):
-        q_hi, q_lo, kc, vc, ks, vs, ctx_mask, slot_mask, out, lse = ctx.saved_tensors
+        q_hi, q_lo, kc, vc, ks, vs, ctx_mask, slot_mask, out, lse, live = ctx.saved_tensors
         windows, slots, kvh, groups, dim, length, dp, scale = ctx.sizes
         device = out.device
         grad = grad.float().contiguous()
@@ -744,7 +745,8 @@ class _TrainAttentionFn(torch.autograd.Function):
         dvs = torch.empty_like(dks)
         _lib.call("bd_train_attention_backward", q_hi.data_ptr(), q_lo.data_ptr(), kc.data_ptr(), vc.data_ptr(),
                   ks.data_ptr(), vs.data_ptr(), ctx_mask.data_ptr(), slot_mask.data_ptr(), d_hi.data_ptr(),
-                  d_lo.data_ptr(), lse.data_ptr(), dr.data_ptr(), unscale.data_ptr(), windows, slots, kvh, groups,
+                  d_lo.data_ptr(), lse.data_ptr(), dr.data_ptr(), unscale.data_ptr(), live.data_ptr(), windows, slots,
+                  kvh, groups,
                   dim, length, scale, dq.data_ptr(), dkc.data_ptr() if length else None,
                   dvc.data_ptr() if length else None, dks.data_ptr(), dvs.data_ptr(), _stream(device))
         return dq, dkc, dvc, dks, dvs, None, None

@@ -462,19 +462,23 @@ int bd_head_post_backward(const float *x, int64_t ld_x, int64_t rows, int heads,
  * allowed key).  Backward: dout_hi/lo = the output gradient times a power of two
  * (1 / *unscale) in the q layout; dr [kv_heads][W][groups][16] = rowsum(scaled dout
  * x out); writes dq (out's layout), d_ctx_k/v fp32 [keys][kv_heads][head_dim] and
- * d_slot_k/v fp32 [W][k][kv_heads][head_dim].  fp16 tensor-core products with
+ * d_slot_k/v fp32 [W][k][kv_heads][head_dim].  tile_live [W][Lp / 64 + 1] (may be
+ * NULL): the forward records which key tiles each window sees at all, and the
+ * backward then skips the unseen (window, key tile) pairs of the context before
+ * staging them.  fp16 tensor-core products with
  * fp32 accumulation; the fp32 operands enter as hi + lo halves.  Deterministic
  * (no atomics).  No reference C counterpart: the reference is torch autograd. */
 int bd_train_attention_forward(const void *q_hi, const void *q_lo, const void *ctx_k, const void *ctx_v,
                                const void *slot_k, const void *slot_v, const uint8_t *ctx_mask,
                                const uint8_t *slot_mask, int windows, int slots, int kv_heads, int groups,
-                               int head_dim, int keys, float scale, float *out, float *lse, bd_stream_t stream);
+                               int head_dim, int keys, float scale, float *out, float *lse, uint8_t *tile_live,
+                               bd_stream_t stream);
 int bd_train_attention_backward(const void *q_hi, const void *q_lo, const void *ctx_k, const void *ctx_v,
                                 const void *slot_k, const void *slot_v, const uint8_t *ctx_mask,
                                 const uint8_t *slot_mask, const void *dout_hi, const void *dout_lo, const float *lse,
-                                const float *dr, const float *unscale, int windows, int slots, int kv_heads,
-                                int groups, int head_dim, int keys, float scale, float *dq, float *d_ctx_k,
-                                float *d_ctx_v, float *d_slot_k, float *d_slot_v, bd_stream_t stream);
+                                const float *dr, const float *unscale, const uint8_t *tile_live, int windows,
+                                int slots, int kv_heads, int groups, int head_dim, int keys, float scale, float *dq,
+                                float *d_ctx_k, float *d_ctx_v, float *d_slot_k, float *d_slot_v, bd_stream_t stream);
 
 /* ================================================================ QAT (training sizes)
  * Projection.forward at any token count (w1a1_eagle/model.py:128-150): codes and
