@@ -131,10 +131,13 @@ SIGNATURES = {
     "bd_head_post": (c_int, [P, c_int64, c_int64, c_int, c_int, P, ctypes.c_float, P, P, c_int, P, P, P, P]),
     "bd_head_post_partials": (c_int64, [c_int64, c_int]),
     "bd_head_post_backward": (c_int, [P, c_int64, c_int64, c_int, c_int, P, P, P, P, P, P, P, P, P]),
+    "bd_train_attention_pack": (c_int, [P, P, P, P, P, P, c_int64, c_int64, c_int64, P, c_int64, c_int64, c_int,
+                                        c_int, c_int, c_int, c_int, c_int, P, P, P, P, P, P, P, P, P, P]),
+    "bd_train_attention_pack_grad": (c_int, [P, P, c_int, c_int, c_int, c_int, c_int, P, P, P, P, P]),
     "bd_train_attention_forward": (c_int, [P, P, P, P, P, P, P, P, c_int, c_int, c_int, c_int, c_int, c_int,
                                            ctypes.c_float, P, P, P, P]),
     "bd_train_attention_backward": (c_int, [P, P, P, P, P, P, P, P, P, P, P, P, P, P, c_int, c_int, c_int, c_int,
-                                            c_int, c_int, ctypes.c_float, P, P, P, P, P, P]),
+                                            c_int, c_int, ctypes.c_float, P, P, P, P, P, P, P]),
     "bd_ste_weight_grad_partials": (c_int64, [c_int64, c_int64]),
     "bd_ste_weight_grad": (c_int, [P, P, c_int64, c_int64, c_int64, P, c_int64, P, P, ctypes.c_float, P, c_int, P, P,
                                    P, P]),
@@ -213,7 +216,7 @@ def load() -> ctypes.CDLL:
 # Kernel launches issued by each entry point (for launch accounting).
 KERNELS_PER_CALL = {"bd_ffn_he4": 3, "bd_ffn_he4_fused": 2, "bd_loss_head_forward": 3, "bd_ffn_w1": 4, "bd_attention_decode": 2, "bd_attention_decode_x16": 2,
                     "bd_accept_rejection": 2,
-                    "bd_ste_grad_prep": 2, "bd_ste_input_backward": 2, "bd_train_attention_backward": 2}
+                    "bd_ste_grad_prep": 2, "bd_ste_input_backward": 2, "bd_train_attention_backward": 3}
 launches = 0
 
 

@@ -22,10 +22,12 @@
 //                         softmax per half, halves merged through shared
 //                         memory.  Writes O and the row log-sum-exp.
 // train_attn_bwd_kv_kernel CTA (key tile, kv head), 4 warps of 16 keys: loops
-//                         over the query tiles that see the tile (every window
-//                         for a context tile, its own window for a slot tile),
-//                         recomputes P^T from the saved log-sum-exp and
-//                         accumulates dV = P^T dO and dK = dS^T Q in registers.
+//                         over the query tiles that see the tile (the windows
+//                         that see a context tile, split over 4 CTAs whose
+//                         partial sums are added in order afterwards; its own
+//                         window for a slot tile), recomputes P^T from the saved
+//                         log-sum-exp and accumulates dV = P^T dO and
+//                         dK = dS^T Q in registers.
 // train_attn_bwd_q_kernel CTA (window, kv head) like the forward: recomputes P
 //                         and dP = dO V^T per key tile and accumulates dQ = dS K.
 // Fully masked (query tile, key tile) pairs are skipped.  Every output element
@@ -48,6 +50,7 @@ struct TrainAttnArgs {
     float *dq;                 // [W][k][kv_heads][g][D]
     float *dkc, *dvc;          // [L][kv_heads][D]
     float *dks, *dvs;          // [W][k][kv_heads][D]
+    float *kv_part;            // [2][kKvSplit][L][kv_heads][D]: the context dK, dV of each window share
     int W, k, kvh, g, D, L, Lp;
     float scale;               // 1 / sqrt(head_dim)
 };
@@ -342,6 +345,7 @@ __global__ void __launch_bounds__(256, 1) train_attn_fwd_kernel(const TrainAttnA
 // ------------------------------------------------------------------ backward: dK, dV
 
 constexpr int kLiveList = 4096;  // windows listed per context tile (more: every window is staged)
+constexpr int kKvSplit = 4;      // CTAs per context key tile, each over a contiguous share of its windows
 
 template <int DP>
 constexpr size_t kv_smem() {
@@ -407,8 +411,11 @@ __global__ void __launch_bounds__(128) train_attn_bwd_kv_kernel(const TrainAttnA
     char *kt = sm, *vt = sm + KV;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, t = lane & 3;
     const int nctx = a.Lp / kTKeys;
-    const int tile = blockIdx.x, h = blockIdx.y;
-    const bool slot_tile = tile >= nctx;
+    const int h = blockIdx.y;
+    // blocks [0, nctx x kKvSplit): context tile, share of its windows; then one per window's slots
+    const bool slot_tile = static_cast<int>(blockIdx.x) >= nctx * kKvSplit;
+    const int tile = slot_tile ? nctx + (static_cast<int>(blockIdx.x) - nctx * kKvSplit) : blockIdx.x / kKvSplit;
+    const int part = slot_tile ? 0 : blockIdx.x % kKvSplit;
     const int wslot = tile - nctx;
     auto sbase = [&](int st) { return sm + 2 * KV + st * STAGE; };
     // the windows that see this context tile, in window order (the forward's table;
@@ -429,10 +436,13 @@ __global__ void __launch_bounds__(128) train_attn_bwd_kv_kernel(const TrainAttnA
         if (threadIdx.x == 0) nlive_s = count;
     }
     __syncthreads();
-    const int nq = slot_tile ? a.g : (listed ? nlive_s : a.W) * a.g;
+    const int nwin = listed ? nlive_s : a.W;
+    const int w_begin = part * nwin / kKvSplit, w_end = (part + 1) * nwin / kKvSplit;
+    const int nq = slot_tile ? a.g : (w_end - w_begin) * a.g;
     // the query tile qt: its rows (hi, lo of q and dO), mask (16 x 64), lse and dr
     auto stage_q = [&](int st, int qt) {
-        const int w = slot_tile ? wslot : (listed ? static_cast<int>(wlist[qt / a.g]) : qt / a.g);
+        const int wi = w_begin + qt / a.g;
+        const int w = slot_tile ? wslot : (listed ? static_cast<int>(wlist[wi]) : wi);
         const int j = slot_tile ? qt : qt % a.g;
         char *b = sbase(st);
         constexpr int CH = DP * 2 / 16;
@@ -536,10 +546,12 @@ __global__ void __launch_bounds__(128) train_attn_bwd_kv_kernel(const TrainAttnA
         const int key = warp * 16 + g + 8 * r;
         float *dkp, *dvp;
         if (!slot_tile) {
+            // this share's partial sums (the shares are added in order afterwards)
             const int64_t l = static_cast<int64_t>(tile) * kTKeys + key;
             if (l >= a.L) continue;
-            dkp = a.dkc + (l * a.kvh + h) * a.D;
-            dvp = a.dvc + (l * a.kvh + h) * a.D;
+            const int64_t stride = static_cast<int64_t>(kKvSplit) * a.L * a.kvh * a.D;
+            dkp = a.kv_part + ((static_cast<int64_t>(part) * a.L + l) * a.kvh + h) * a.D;
+            dvp = dkp + stride;
         } else {
             if (key >= a.k) continue;
             const int64_t row = (static_cast<int64_t>(wslot) * a.k + key) * a.kvh + h;
@@ -666,6 +678,151 @@ __global__ void __launch_bounds__(256, 1) train_attn_bwd_q_kernel(const TrainAtt
     }
 }
 
+// ------------------------------------------------------------------ operand preparation
+
+// fp32 rows [W][k][kvh][g][D] (times *factor when given) -> fp16 hi + lo rows
+// [kvh][W][g][16][DP], zero padded; also the forward's lse rows set to +inf.
+__global__ void pack_query_kernel(const float *__restrict__ x, int W, int k, int kvh, int g, int D, int DP,
+                                  const float *__restrict__ factor, __half *__restrict__ hi, __half *__restrict__ lo,
+                                  float *__restrict__ lse_init) {
+    const int64_t total = static_cast<int64_t>(kvh) * W * g * 16 * DP;
+    const float f = factor ? *factor : 1.0f;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int e = static_cast<int>(i % DP);
+        const int64_t row = i / DP;  // (h, w, j, s)
+        const int s = static_cast<int>(row % 16);
+        const int64_t hwj = row / 16;
+        const int j = static_cast<int>(hwj % g);
+        const int64_t hw = hwj / g;
+        const int w = static_cast<int>(hw % W), h = static_cast<int>(hw / W);
+        float v = 0.0f;
+        if (s < k && e < D) v = __fmul_rn(x[((((static_cast<int64_t>(w) * k + s) * kvh + h) * g + j) * D) + e], f);
+        const __half vh = __float2half_rn(v);
+        hi[i] = vh;
+        lo[i] = __float2half_rn(__fsub_rn(v, __half2float(vh)));
+        if (lse_init && e == 0) lse_init[row] = INFINITY;
+    }
+}
+
+// fp32 K and V rows -> fp16 rows [kvh][R][DP] (exact: the values are fp16 already).
+// Context: source [L][kvh][D], R = Lp, row r = key r.  Slots: source [W][k][kvh][D],
+// R = W x 16, row r = (window r / 16, slot r % 16).
+__global__ void pack_kv_kernel(const float *__restrict__ ksrc, const float *__restrict__ vsrc, int kvh, int D, int DP,
+                               int64_t R, int live_rows, int slots, int k, __half *__restrict__ kdst,
+                               __half *__restrict__ vdst) {
+    const int64_t total = static_cast<int64_t>(kvh) * R * DP;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int e = static_cast<int>(i % DP);
+        const int64_t r = (i / DP) % R;
+        const int h = static_cast<int>(i / (DP * R));
+        int64_t src = -1;
+        if (e < D) {
+            if (!slots) {
+                if (r < live_rows) src = (r * kvh + h) * D + e;
+            } else {
+                const int64_t w = r / 16;
+                const int s = static_cast<int>(r % 16);
+                if (s < k) src = ((w * k + s) * kvh + h) * D + e;
+            }
+        }
+        kdst[i] = __float2half_rn(src >= 0 ? ksrc[src] : 0.0f);
+        vdst[i] = __float2half_rn(src >= 0 ? vsrc[src] : 0.0f);
+    }
+}
+
+// Masks: ctx [W][16][Lp] from allowed (element strides sw, ss, sl; 0 broadcasts),
+// slots [16][16] from slot_allowed (strides s0, s1) or all allowed.
+__global__ void pack_masks_kernel(const uint8_t *__restrict__ allowed, int64_t sw, int64_t ss, int64_t sl, int W, int k,
+                                  int L, int Lp, uint8_t *__restrict__ mctx, const uint8_t *__restrict__ slot_allowed,
+                                  int64_t s0, int64_t s1, uint8_t *__restrict__ mslot) {
+    const int64_t total = static_cast<int64_t>(W) * 16 * Lp;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total + 256;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        if (i < total) {
+            const int l = static_cast<int>(i % Lp);
+            const int s = static_cast<int>((i / Lp) % 16);
+            const int64_t w = i / (static_cast<int64_t>(Lp) * 16);
+            mctx[i] = (s < k && l < L && allowed[w * sw + s * ss + l * sl]) ? 1 : 0;
+        } else {
+            const int s = static_cast<int>((i - total) / 16), t = static_cast<int>((i - total) % 16);
+            mslot[s * 16 + t] = (s < k && t < k && (!slot_allowed || slot_allowed[s * s0 + t * s1])) ? 1 : 0;
+        }
+    }
+}
+
+// Largest |g| as the bits of a non-negative float (ordered like unsigned integers).
+__global__ void abs_max_kernel(const float *__restrict__ g, int64_t n, unsigned *__restrict__ out) {
+    unsigned m = 0;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        m = max(m, __float_as_uint(fabsf(g[i])));
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, d));
+    if ((threadIdx.x & 31) == 0 && m) atomicMax(out, m);
+}
+
+// 2^-ceil(log2 m) for the largest magnitude m (1 when m is 0, subnormal or not finite).
+__device__ __forceinline__ float pow2_factor(unsigned bits) {
+    const unsigned e = (bits >> 23) & 0xffu;
+    if (e == 0u || e == 0xffu) return 1.0f;
+    int c = static_cast<int>(e) - 127 + ((bits & 0x7fffffu) ? 1 : 0);
+    int fe = 127 - c;
+    fe = fe < 1 ? 1 : (fe > 254 ? 254 : fe);
+    return __uint_as_float(static_cast<unsigned>(fe) << 23);
+}
+
+__global__ void grad_factor_kernel(const unsigned *__restrict__ maxbits, float *__restrict__ factor,
+                                   float *__restrict__ unscale) {
+    const float f = pow2_factor(*maxbits);
+    *factor = f;
+    *unscale = __frcp_rn(f);  // exact: a power of two
+}
+
+// dr[h][w][j][s] = sum_e (dO * factor)[row] * O[row] (0 for padding rows): one warp per row.
+__global__ void grad_rowdot_kernel(const float *__restrict__ dout, const float *__restrict__ out,
+                                   const float *__restrict__ factor, int W, int k, int kvh, int g, int D,
+                                   float *__restrict__ dr) {
+    const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= static_cast<int64_t>(kvh) * W * g * 16) return;
+    const int s = static_cast<int>(row % 16);
+    const int64_t hwj = row / 16;
+    const int j = static_cast<int>(hwj % g);
+    const int w = static_cast<int>((hwj / g) % W), h = static_cast<int>(hwj / g / W);
+    float acc = 0.0f;
+    if (s < k) {
+        const float f = *factor;
+        const int64_t base = (((static_cast<int64_t>(w) * k + s) * kvh + h) * g + j) * D;
+        for (int e = lane; e < D; e += 32) acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(dout[base + e], f), out[base + e]));
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, d));
+    }
+    if (lane == 0) dr[row] = acc;
+}
+
+// dK, dV of the context: the window shares' partial sums added in share order.
+__global__ void kv_share_sum_kernel(const float *__restrict__ part, int64_t n, float *__restrict__ dk,
+                                    float *__restrict__ dv) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        float sk = 0.0f, sv = 0.0f;
+#pragma unroll
+        for (int p = 0; p < kKvSplit; ++p) {
+            sk = __fadd_rn(sk, part[p * n + i]);
+            sv = __fadd_rn(sv, part[(kKvSplit + p) * n + i]);
+        }
+        dk[i] = sk;
+        dv[i] = sv;
+    }
+}
+
+static unsigned pack_grid(int64_t n) {
+    const int64_t b = (n + 255) / 256;
+    return static_cast<unsigned>(b < 148 * 32 ? (b > 0 ? b : 1) : 148 * 32);
+}
+
 template <int DP>
 static int launch_train_attn(const TrainAttnArgs &a, bool backward, cudaStream_t stream) {
     if (!backward) {
@@ -684,8 +841,13 @@ static int launch_train_attn(const TrainAttnArgs &a, bool backward, cudaStream_t
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
             cudaSuccess)
             return BD_ERR_LAUNCH;
-        kern<<<dim3(a.Lp / kTKeys + a.W, a.kvh), 128, smem, stream>>>(a);
+        kern<<<dim3(a.Lp / kTKeys * kKvSplit + a.W, a.kvh), 128, smem, stream>>>(a);
         BD_CHECK_LAUNCH();
+        if (a.L > 0) {
+            const int64_t n = static_cast<int64_t>(a.L) * a.kvh * a.D;
+            kv_share_sum_kernel<<<pack_grid(n), 256, 0, stream>>>(a.kv_part, n, a.dkc, a.dvc);
+            BD_CHECK_LAUNCH();
+        }
     }
     {
         const size_t smem = q_smem<DP>();
@@ -709,7 +871,7 @@ static int train_attn(TrainAttnArgs a, bool backward, cudaStream_t stream) {
     if (a.Lp > 0 && (!a.kc || !a.vc || !a.mctx)) return BD_ERR_INVALID;
     if (!backward && (!a.o || !a.lse)) return BD_ERR_INVALID;
     if (backward && (!a.doh || !a.dol || !a.lse_in || !a.dr || !a.unscale || !a.dq || !a.dks || !a.dvs ||
-                     (a.L > 0 && (!a.dkc || !a.dvc))))
+                     (a.L > 0 && (!a.dkc || !a.dvc || !a.kv_part))))
         return BD_ERR_INVALID;
     const void *aligned[] = {a.qh, a.ql, a.doh, a.dol, a.kc, a.vc, a.ks, a.vs, a.mctx, a.mslot, a.lse_in, a.dr};
     for (const void *p : aligned)
@@ -726,6 +888,71 @@ static int train_attn(TrainAttnArgs a, bool backward, cudaStream_t stream) {
 }  // namespace bd
 
 using namespace bd;
+
+extern "C" int bd_train_attention_pack(const float *query, const float *ctx_k, const float *ctx_v,
+                                       const float *slot_k, const float *slot_v, const uint8_t *ctx_allowed,
+                                       int64_t allowed_stride_w, int64_t allowed_stride_s, int64_t allowed_stride_l,
+                                       const uint8_t *slot_allowed, int64_t slot_stride_s, int64_t slot_stride_t,
+                                       int windows, int slots, int kv_heads, int groups, int head_dim, int keys,
+                                       void *q_hi, void *q_lo, void *kc, void *vc, void *ks, void *vs,
+                                       uint8_t *ctx_mask, uint8_t *slot_mask, float *lse, bd_stream_t stream) {
+    if (windows < 1 || slots < 1 || slots > 16 || kv_heads < 1 || groups < 1 || groups > 4 || head_dim < 1 ||
+        head_dim > 128 || keys < 0)
+        return BD_ERR_INVALID;
+    if (!query || !slot_k || !slot_v || !q_hi || !q_lo || !ks || !vs || !slot_mask || !lse ||
+        (keys > 0 && (!ctx_k || !ctx_v || !ctx_allowed || !kc || !vc || !ctx_mask)))
+        return BD_ERR_INVALID;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int dp = head_dim <= 16 ? 16 : head_dim <= 32 ? 32 : head_dim <= 64 ? 64 : 128;
+    const int lp = (keys + kTKeys - 1) / kTKeys * kTKeys;
+    const int64_t nq = static_cast<int64_t>(kv_heads) * windows * groups * 16 * dp;
+    pack_query_kernel<<<pack_grid(nq), 256, 0, st>>>(query, windows, slots, kv_heads, groups, head_dim, dp, nullptr,
+                                                     static_cast<__half *>(q_hi), static_cast<__half *>(q_lo), lse);
+    BD_CHECK_LAUNCH();
+    if (lp > 0) {
+        pack_kv_kernel<<<pack_grid(static_cast<int64_t>(kv_heads) * lp * dp), 256, 0, st>>>(
+            ctx_k, ctx_v, kv_heads, head_dim, dp, lp, keys, 0, slots, static_cast<__half *>(kc),
+            static_cast<__half *>(vc));
+        BD_CHECK_LAUNCH();
+    }
+    pack_kv_kernel<<<pack_grid(static_cast<int64_t>(kv_heads) * windows * 16 * dp), 256, 0, st>>>(
+        slot_k, slot_v, kv_heads, head_dim, dp, static_cast<int64_t>(windows) * 16, 0, 1, slots,
+        static_cast<__half *>(ks), static_cast<__half *>(vs));
+    BD_CHECK_LAUNCH();
+    pack_masks_kernel<<<pack_grid(static_cast<int64_t>(windows) * 16 * lp + 256), 256, 0, st>>>(
+        ctx_allowed ? ctx_allowed : slot_mask, allowed_stride_w, allowed_stride_s, allowed_stride_l, windows, slots,
+        keys, lp, ctx_mask ? ctx_mask : slot_mask, slot_allowed, slot_stride_s, slot_stride_t, slot_mask);
+    BD_CHECK_LAUNCH();
+    return BD_OK;
+}
+
+extern "C" int bd_train_attention_pack_grad(const float *dout, const float *out, int windows, int slots,
+                                            int kv_heads, int groups, int head_dim, void *d_hi, void *d_lo, float *dr,
+                                            float *scalars, bd_stream_t stream) {
+    if (windows < 1 || slots < 1 || slots > 16 || kv_heads < 1 || groups < 1 || groups > 4 || head_dim < 1 ||
+        head_dim > 128 || !dout || !out || !d_hi || !d_lo || !dr || !scalars)
+        return BD_ERR_INVALID;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int dp = head_dim <= 16 ? 16 : head_dim <= 32 ? 32 : head_dim <= 64 ? 64 : 128;
+    // scalars: [0] the largest |dout| (bits), [1] the power-of-two factor, [2] its inverse
+    unsigned *maxbits = reinterpret_cast<unsigned *>(scalars);
+    if (cudaMemsetAsync(maxbits, 0, sizeof(unsigned), st) != cudaSuccess) return BD_ERR_LAUNCH;
+    const int64_t n = static_cast<int64_t>(windows) * slots * kv_heads * groups * head_dim;
+    abs_max_kernel<<<pack_grid(n), 256, 0, st>>>(dout, n, maxbits);
+    BD_CHECK_LAUNCH();
+    grad_factor_kernel<<<1, 1, 0, st>>>(maxbits, scalars + 1, scalars + 2);
+    BD_CHECK_LAUNCH();
+    const int64_t nq = static_cast<int64_t>(kv_heads) * windows * groups * 16 * dp;
+    pack_query_kernel<<<pack_grid(nq), 256, 0, st>>>(dout, windows, slots, kv_heads, groups, head_dim, dp,
+                                                     scalars + 1, static_cast<__half *>(d_hi),
+                                                     static_cast<__half *>(d_lo), nullptr);
+    BD_CHECK_LAUNCH();
+    const int64_t rows = static_cast<int64_t>(kv_heads) * windows * groups * 16;
+    grad_rowdot_kernel<<<static_cast<unsigned>((rows * 32 + 255) / 256), 256, 0, st>>>(
+        dout, out, scalars + 1, windows, slots, kv_heads, groups, head_dim, dr);
+    BD_CHECK_LAUNCH();
+    return BD_OK;
+}
 
 extern "C" int bd_train_attention_forward(const void *q_hi, const void *q_lo, const void *ctx_k, const void *ctx_v,
                                           const void *slot_k, const void *slot_v, const uint8_t *ctx_mask,
@@ -761,7 +988,8 @@ extern "C" int bd_train_attention_backward(const void *q_hi, const void *q_lo, c
                                            const float *lse, const float *dr, const float *unscale,
                                            const uint8_t *tile_live, int windows, int slots, int kv_heads,
                                            int groups, int head_dim, int keys, float scale, float *dq, float *d_ctx_k,
-                                           float *d_ctx_v, float *d_slot_k, float *d_slot_v, bd_stream_t stream) {
+                                           float *d_ctx_v, float *d_slot_k, float *d_slot_v, float *kv_partials,
+                                           bd_stream_t stream) {
     TrainAttnArgs a = {};
     a.qh = static_cast<const __half *>(q_hi);
     a.ql = static_cast<const __half *>(q_lo);
@@ -790,5 +1018,6 @@ extern "C" int bd_train_attention_backward(const void *q_hi, const void *q_lo, c
     a.dvc = d_ctx_v;
     a.dks = d_slot_k;
     a.dvs = d_slot_v;
+    a.kv_part = kv_partials;
     return train_attn(a, true, static_cast<cudaStream_t>(stream));
 }

@@ -681,43 +681,50 @@ def _padded_dim(head_dim: int) -> int:
     raise ValueError("training attention supports head_dim up to 128")
 
 
-def _query_rows(x: Tensor, dp: int) -> tuple[Tensor, Tensor]:
-    """``[W, k, kvh, g, d]`` fp32 -> fp16 hi + lo rows ``[kvh, W, g, 16, dp]`` (zero padded)."""
-    windows, slots, kvh, groups, dim = x.shape
-    rows = torch.zeros((kvh, windows, groups, 16, dp), dtype=torch.float32, device=x.device)
-    rows[:, :, :, :slots, :dim] = x.permute(2, 0, 3, 1, 4)
-    hi = rows.half()
-    return hi, (rows - hi.float()).half()
-
-
 class _TrainAttentionFn(torch.autograd.Function):
     """The windows' attention on the training-attention kernels
     (``bd_train_attention_forward`` / ``_backward``): fp16 tensor-core products with
-    the fp32 operands as hi + lo halves, the row log-sum-exp saved for the backward."""
+    the fp32 operands as hi + lo halves, the row log-sum-exp saved for the backward.
+    The operand layouts are made on the device (``bd_train_attention_pack``,
+    ``bd_train_attention_pack_grad``)."""
 
     @staticmethod
-    def forward(ctx, query, ctx_k, ctx_v, slot_k, slot_v, ctx_mask, slot_mask):
+    def forward(ctx, query, ctx_k, ctx_v, slot_k, slot_v, ctx_allowed, slot_allowed):
         windows, slots, kvh, groups, dim = query.shape
         length = ctx_k.shape[0]
         dp = _padded_dim(dim)
         device = query.device
-        q_hi, q_lo = _query_rows(query.detach().float(), dp)
         padded = (length + 63) // 64 * 64
-        kc = torch.zeros((kvh, padded, dp), dtype=torch.float16, device=device)
-        vc = torch.zeros_like(kc)
-        kc[:, :length, :dim] = ctx_k.detach().permute(1, 0, 2)  # fp16 values: exact
-        vc[:, :length, :dim] = ctx_v.detach().permute(1, 0, 2)
-        ks = torch.zeros((kvh, windows, 16, dp), dtype=torch.float16, device=device)
-        vs = torch.zeros_like(ks)
-        ks[:, :, :slots, :dim] = slot_k.detach().permute(2, 0, 1, 3)
-        vs[:, :, :slots, :dim] = slot_v.detach().permute(2, 0, 1, 3)
+        f16 = dict(dtype=torch.float16, device=device)
+        q_hi = torch.empty((kvh, windows, groups, 16, dp), **f16)
+        q_lo = torch.empty_like(q_hi)
+        kc = torch.empty((kvh, padded, dp), **f16)
+        vc = torch.empty_like(kc)
+        ks = torch.empty((kvh, windows, 16, dp), **f16)
+        vs = torch.empty_like(ks)
+        ctx_mask = torch.empty((windows, 16, padded), dtype=torch.uint8, device=device)
+        slot_mask = torch.empty((16, 16), dtype=torch.uint8, device=device)
+        lse = torch.empty((kvh, windows, groups, 16), dtype=torch.float32, device=device)
+        q = query.detach().float().contiguous()
+        kk, vv = ctx_k.detach().float().contiguous(), ctx_v.detach().float().contiguous()
+        sk, sv = slot_k.detach().float().contiguous(), slot_v.detach().float().contiguous()
+        allowed = ctx_allowed.to(torch.bool).expand(windows, slots, length)
+        slot_ok = None if slot_allowed is None else slot_allowed.to(torch.bool).expand(slots, slots)
+        stream = _stream(device)
+        _lib.call("bd_train_attention_pack", q.data_ptr(), kk.data_ptr() if length else None,
+                  vv.data_ptr() if length else None, sk.data_ptr(), sv.data_ptr(),
+                  allowed.data_ptr() if length else None, *allowed.stride(),
+                  None if slot_ok is None else slot_ok.data_ptr(), *((0, 0) if slot_ok is None else slot_ok.stride()),
+                  windows, slots, kvh, groups, dim, length, q_hi.data_ptr(), q_lo.data_ptr(),
+                  kc.data_ptr() if length else None, vc.data_ptr() if length else None, ks.data_ptr(), vs.data_ptr(),
+                  ctx_mask.data_ptr() if length else None, slot_mask.data_ptr(), lse.data_ptr(), stream,
+                  kernels=4 if length else 3)
         out = torch.empty((windows, slots, kvh, groups, dim), dtype=torch.float32, device=device)
-        lse = torch.full((kvh, windows, groups, 16), math.inf, dtype=torch.float32, device=device)
         live = torch.empty((windows, padded // 64 + 1), dtype=torch.uint8, device=device)
         scale = 1.0 / math.sqrt(dim)
         _lib.call("bd_train_attention_forward", q_hi.data_ptr(), q_lo.data_ptr(), kc.data_ptr(), vc.data_ptr(),
                   ks.data_ptr(), vs.data_ptr(), ctx_mask.data_ptr(), slot_mask.data_ptr(), windows, slots, kvh, groups,
-                  dim, length, scale, out.data_ptr(), lse.data_ptr(), live.data_ptr(), _stream(device))
+                  dim, length, scale, out.data_ptr(), lse.data_ptr(), live.data_ptr(), stream)
         ctx.save_for_backward(q_hi, q_lo, kc, vc, ks, vs, ctx_mask, slot_mask, out, lse, live)
         ctx.sizes = (windows, slots, kvh, groups, dim, length, dp, scale)
         return out
@@ -727,28 +734,29 @@ class _TrainAttentionFn(torch.autograd.Function):
         q_hi, q_lo, kc, vc, ks, vs, ctx_mask, slot_mask, out, lse, live = ctx.saved_tensors
         windows, slots, kvh, groups, dim, length, dp, scale = ctx.sizes
         device = out.device
+        stream = _stream(device)
         grad = grad.float().contiguous()
         # the output gradient times a power of two with its largest magnitude in
         # (1/2, 1], so that its fp16 halves keep their precision; undone exactly
-        # on the results
-        top = grad.abs().amax()
-        factor = torch.where(top > 0, torch.exp2(-torch.ceil(torch.log2(top))), torch.ones_like(top))
-        unscale = (1.0 / factor).reshape(1).contiguous()
-        scaled = grad * factor
-        d_hi, d_lo = _query_rows(scaled, dp)
-        dr = torch.zeros((kvh, windows, groups, 16), dtype=torch.float32, device=device)
-        dr[:, :, :, :slots] = (scaled * out).sum(-1).permute(2, 0, 3, 1)
+        # on the results (scalars: the maximum, the factor, its inverse)
+        d_hi = torch.empty_like(q_hi)
+        d_lo = torch.empty_like(q_hi)
+        dr = torch.empty((kvh, windows, groups, 16), dtype=torch.float32, device=device)
+        scalars = torch.empty(4, dtype=torch.float32, device=device)
+        _lib.call("bd_train_attention_pack_grad", grad.data_ptr(), out.data_ptr(), windows, slots, kvh, groups, dim,
+                  d_hi.data_ptr(), d_lo.data_ptr(), dr.data_ptr(), scalars.data_ptr(), stream, kernels=4)
         dq = torch.empty_like(out)
         dkc = torch.empty((length, kvh, dim), dtype=torch.float32, device=device)
         dvc = torch.empty_like(dkc)
         dks = torch.empty((windows, slots, kvh, dim), dtype=torch.float32, device=device)
         dvs = torch.empty_like(dks)
+        parts = torch.empty((8, length, kvh, dim), dtype=torch.float32, device=device) if length else None
         _lib.call("bd_train_attention_backward", q_hi.data_ptr(), q_lo.data_ptr(), kc.data_ptr(), vc.data_ptr(),
                   ks.data_ptr(), vs.data_ptr(), ctx_mask.data_ptr(), slot_mask.data_ptr(), d_hi.data_ptr(),
-                  d_lo.data_ptr(), lse.data_ptr(), dr.data_ptr(), unscale.data_ptr(), live.data_ptr(), windows, slots,
-                  kvh, groups,
-                  dim, length, scale, dq.data_ptr(), dkc.data_ptr() if length else None,
-                  dvc.data_ptr() if length else None, dks.data_ptr(), dvs.data_ptr(), _stream(device))
+                  d_lo.data_ptr(), lse.data_ptr(), dr.data_ptr(), scalars[2:].data_ptr(), live.data_ptr(), windows,
+                  slots, kvh, groups, dim, length, scale, dq.data_ptr(), dkc.data_ptr() if length else None,
+                  dvc.data_ptr() if length else None, dks.data_ptr(), dvs.data_ptr(),
+                  parts.data_ptr() if length else None, stream, kernels=3 if length else 2)
         return dq, dkc, dvc, dks, dvs, None, None
 
 
@@ -758,16 +766,11 @@ def train_attention(query: Tensor, ctx_k: Tensor, ctx_v: Tensor, slot_k: Tensor,
     ``ctx_k/ctx_v [L, kvh, d]`` and ``slot_k/slot_v [W, k, kvh, d]`` holding fp16
     values (``cache_storage``), ``ctx_allowed`` broadcastable to ``[W, k, L]``,
     ``slot_allowed [k, k]`` or None.  Returns ``[W, k, kvh, g, d]``."""
-    windows, slots, kvh, groups, dim = query.shape
-    length = ctx_k.shape[0]
+    slots, groups = query.shape[1], query.shape[3]
     if slots > 16 or groups > 4:
         raise ValueError("training attention supports up to 16 slots and 4 query heads per kv head")
-    padded = (length + 63) // 64 * 64
-    ctx_mask = torch.zeros((windows, 16, padded), dtype=torch.uint8, device=query.device)
-    ctx_mask[:, :slots, :length] = ctx_allowed.expand(windows, slots, length)
-    slot_mask = torch.zeros((16, 16), dtype=torch.uint8, device=query.device)
-    slot_mask[:slots, :slots] = 1 if slot_allowed is None else slot_allowed.expand(slots, slots)
-    return _TrainAttentionFn.apply(query, ctx_k, ctx_v, slot_k, slot_v, ctx_mask, slot_mask)
+    _padded_dim(query.shape[-1])
+    return _TrainAttentionFn.apply(query, ctx_k, ctx_v, slot_k, slot_v, ctx_allowed, slot_allowed)
 
 
 def _window_attention(query: Tensor, ctx_k: Tensor, ctx_v: Tensor, slot_k: Tensor, slot_v: Tensor,

@@ -465,9 +465,29 @@ int bd_head_post_backward(const float *x, int64_t ld_x, int64_t rows, int heads,
  * d_slot_k/v fp32 [W][k][kv_heads][head_dim].  tile_live [W][Lp / 64 + 1] (may be
  * NULL): the forward records which key tiles each window sees at all, and the
  * backward then skips the unseen (window, key tile) pairs of the context before
- * staging them.  fp16 tensor-core products with
+ * staging them.  kv_partials: 8 x keys x kv_heads x head_dim floats of workspace
+ * (the context dK, dV of each of the 4 window shares of a key tile, added in
+ * order).  fp16 tensor-core products with
  * fp32 accumulation; the fp32 operands enter as hi + lo halves.  Deterministic
  * (no atomics).  No reference C counterpart: the reference is torch autograd. */
+/* The operands of the two entries above made on the device from the model's
+ * tensors: query fp32 [W][k][kv_heads][groups][head_dim], ctx_k/v fp32
+ * [keys][kv_heads][head_dim], slot_k/v fp32 [W][k][kv_heads][head_dim] (fp16
+ * values), ctx_allowed bytes addressed with element strides (w, s, l: 0
+ * broadcasts) and slot_allowed likewise (NULL: all allowed) -> q_hi/q_lo,
+ * kc/vc, ks/vs, ctx_mask, slot_mask in the layouts above (zero padded) and lse
+ * set to +inf.  bd_train_attention_pack_grad: dout (out's layout) times the
+ * power of two 2^-ceil(log2 max|dout|) as hi + lo rows, dr = rowsum(scaled
+ * dout x out); scalars[4] (fp32 workspace): [1] the factor, [2] its inverse
+ * (the backward's unscale). */
+int bd_train_attention_pack(const float *query, const float *ctx_k, const float *ctx_v, const float *slot_k,
+                            const float *slot_v, const uint8_t *ctx_allowed, int64_t allowed_stride_w,
+                            int64_t allowed_stride_s, int64_t allowed_stride_l, const uint8_t *slot_allowed,
+                            int64_t slot_stride_s, int64_t slot_stride_t, int windows, int slots, int kv_heads,
+                            int groups, int head_dim, int keys, void *q_hi, void *q_lo, void *kc, void *vc, void *ks,
+                            void *vs, uint8_t *ctx_mask, uint8_t *slot_mask, float *lse, bd_stream_t stream);
+int bd_train_attention_pack_grad(const float *dout, const float *out, int windows, int slots, int kv_heads, int groups,
+                                 int head_dim, void *d_hi, void *d_lo, float *dr, float *scalars, bd_stream_t stream);
 int bd_train_attention_forward(const void *q_hi, const void *q_lo, const void *ctx_k, const void *ctx_v,
                                const void *slot_k, const void *slot_v, const uint8_t *ctx_mask,
                                const uint8_t *slot_mask, int windows, int slots, int kv_heads, int groups,
@@ -478,7 +498,8 @@ int bd_train_attention_backward(const void *q_hi, const void *q_lo, const void *
                                 const uint8_t *slot_mask, const void *dout_hi, const void *dout_lo, const float *lse,
                                 const float *dr, const float *unscale, const uint8_t *tile_live, int windows,
                                 int slots, int kv_heads, int groups, int head_dim, int keys, float scale, float *dq,
-                                float *d_ctx_k, float *d_ctx_v, float *d_slot_k, float *d_slot_v, bd_stream_t stream);
+                                float *d_ctx_k, float *d_ctx_v, float *d_slot_k, float *d_slot_v, float *kv_partials,
+                                bd_stream_t stream);
 
 /* ================================================================ QAT (training sizes)
  * Projection.forward at any token count (w1a1_eagle/model.py:128-150): codes and
