@@ -159,7 +159,7 @@ SIGNATURES = {
     "bd_accept_greedy_noalloc": (c_int, [P, c_int, c_int, c_int64, P, P, c_int, P, P, P, P, P]),
     "bd_rejection_workspace_bytes": (c_size_t, [c_int, c_int, c_int64]),
     "bd_ingest_taps": (c_int, [P, c_int, c_int, c_int64, c_int64, P, c_int, P, P]),
-    "bd_gemm_bf16": (c_int, [P, c_int64, c_int64, c_int64, P, c_int64, c_int64, P, c_int64, P]),
+    "bd_gemm_bf16": (c_int, [P, c_int64, c_int64, c_int64, P, c_int64, c_int64, P, c_int64, P, c_size_t, P]),
     "bd_accept_rejection": (c_int, [P, P, c_int, c_int, c_int64, P, P, c_int, ctypes.c_ulonglong, ctypes.c_uint32,
                                     P, P, P, c_size_t, P, P]),
     "bd_argmax_rows_bf16": (c_int, [P, c_int64, c_int64, P, P, P]),

@@ -75,10 +75,13 @@ struct TcArgs {
     float *stats;           // [M][2 n_tiles][2]: max, sum of exp(D - max) per half tile (STATS)
     float *target;          // [M] the label's logit (STATS)
     __nv_bfloat16 *dl_hi, *dl_lo;  // [M][ld_out] (GRAD)
-    // TC_F32 split over K: work unit u = tile u / splits, K slice u % splits; every
-    // unit writes its fp32 partial tile, and per (tile, epilogue warp) the last of
-    // the splits to arrive adds them in slice order (deterministic) into out
+    // TC_F32 split over K: tiles [0, split_full) are whole units; each later tile is
+    // `splits` units of one K slice each (the tiles of a last, partial wave, or all
+    // of them when they are fewer than the SMs).  A sliced unit writes its fp32
+    // partial tile, and per (tile, epilogue warp) the last slice to arrive adds them
+    // in slice order (deterministic) into out.
     int splits;
+    int64_t split_full;
     float *split_part;      // [tiles][splits][kTcBM][BN]
     int32_t *split_count;   // [tiles][8] at the start of the workspace, zero on entry and left zero
     void *split_ws;         // caller's workspace for the above (host side only), or null: no split
@@ -110,6 +113,19 @@ static int tc_split_slices(int64_t tiles, int64_t nk, int sms) {
 }
 static size_t tc_split_bytes(int64_t tiles, int slices, int bn) {
     return kTcSplitCounts * sizeof(int32_t) + static_cast<size_t>(tiles) * slices * kTcBM * bn * sizeof(float);
+}
+
+// Which tiles are cut into how many K slices: with fewer tiles than SMs, all of
+// them (tc_split_slices).  With more, none: cutting only the tiles of a last,
+// partial wave (the kernel supports it: tiles [0, full) whole) measured 2 % faster
+// at 320 tiles, no faster at 160 and 18 % slower at 512, so it is not used.
+static void tc_split_plan(int64_t tiles, int64_t nk, int sms, int64_t &full, int &slices) {
+    full = tiles;
+    slices = 1;
+    if (tiles < sms) {
+        slices = tc_split_slices(tiles, nk, sms);
+        if (slices > 1) full = 0;
+    }
 }
 
 __device__ __forceinline__ uint32_t su32(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
@@ -193,8 +209,22 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
     constexpr int BKE = tc_bk(EPI);  // K elements per stage
     const int nk1 = static_cast<int>((a.K + BKE - 1) / BKE);
     const int nk = nk1 * (a.parts > 1 ? a.parts : 1);  // part p covers k-blocks [p nk1, (p + 1) nk1)
-    const int S = (EPI == TC_F32 && a.splits > 1) ? a.splits : 1;  // K slices per tile (at most nk)
-    const int64_t units = tiles * S;
+    const int S = (EPI == TC_F32 && a.splits > 1) ? a.splits : 1;  // K slices of a sliced tile (at most nk)
+    const int64_t whole = S > 1 ? a.split_full : tiles;              // tiles done whole
+    const int64_t units = whole + (tiles - whole) * S;
+    // unit -> (tile, K slice, slices of that tile)
+    auto unit_of = [&](int64_t u, int64_t &t, int &sp, int &us) {
+        if (u < whole) {
+            t = u;
+            sp = 0;
+            us = 1;
+        } else {
+            const int64_t v = u - whole;
+            t = whole + v / S;
+            sp = static_cast<int>(v % S);
+            us = S;
+        }
+    };
     constexpr uint32_t kCols = 2 * BN;  // two accumulator buffers
     if (threadIdx.x == 0) {
         for (int s = 0; s < kTcStages; ++s) {
@@ -222,10 +252,12 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
         if (lane == 0) {  // TMA producer
             uint32_t it = 0;
             for (int64_t u = blockIdx.x; u < units && !abort_flag; u += gridDim.x) {
-                const int64_t t = u / S;
+                int64_t t;
+                int sp, us;
+                unit_of(u, t, sp, us);
                 const int m0 = static_cast<int>((t % a.m_tiles) * kTcBM);
                 const int n0 = static_cast<int>((t / a.m_tiles) * BN);
-                const int kb = static_cast<int>((u % S) * nk / S), ke = static_cast<int>((u % S + 1) * nk / S);
+                const int kb = sp * nk / us, ke = (sp + 1) * nk / us;
                 for (int k = kb; k < ke; ++k, ++it) {
                     const int s = it % kTcStages;
                     if (it >= kTcStages && !mb_wait(&empty[s], ((it / kTcStages) - 1) & 1, &abort_flag)) break;
@@ -250,7 +282,10 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t d = tmem + b * BN;
                 bool ok = true;
-                const int kb = static_cast<int>((u % S) * nk / S), ke = static_cast<int>((u % S + 1) * nk / S);
+                int64_t t;
+                int sp, us;
+                unit_of(u, t, sp, us);
+                const int kb = sp * nk / us, ke = (sp + 1) * nk / us;
                 for (int k = kb; k < ke; ++k, ++it) {
                     const int s = it % kTcStages;
                     if (!mb_wait(&full[s], (it / kTcStages) & 1, &abort_flag)) {
@@ -305,10 +340,12 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
                                                                                                : static_cast<void *>(a.out)) & 15) == 0;
         uint32_t lt = 0;
         for (int64_t u = blockIdx.x; u < units && !abort_flag; u += gridDim.x, ++lt) {
-            const int64_t t = u / S;
-            const int sp = static_cast<int>(u % S);
+            int64_t t;
+            int sp, us;
+            unit_of(u, t, sp, us);
+            const int64_t tt = t - whole;  // index among the sliced tiles
             // this unit's partial tile (split K): rows of this thread, its half of the columns
-            float *part = S > 1 ? a.split_part + ((t * S + sp) * kTcBM + row_in_tile) * BN + half * HALF : nullptr;
+            float *part = us > 1 ? a.split_part + ((tt * S + sp) * kTcBM + row_in_tile) * BN + half * HALF : nullptr;
             const uint32_t b = lt & 1;
             if (!mb_wait(&acc_full[b], (lt >> 1) & 1, &abort_flag)) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -377,7 +414,7 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
                     }
                 }
                 const int64_t idx = row * a.ld_out + o0;
-                if (EPI == TC_F32 && S > 1) {
+                if (EPI == TC_F32 && us > 1) {
 #pragma unroll
                     for (int j = 0; j < 16; j += 4)
                         *reinterpret_cast<float4 *>(part + c + j) = make_float4(y[j], y[j + 1], y[j + 2], y[j + 3]);
@@ -493,18 +530,18 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
             if (lane == 0) mb_arrive(&acc_empty[b]);
-            if (EPI == TC_F32 && S > 1) {
+            if (EPI == TC_F32 && us > 1) {
                 // the last split of this (tile, warp region) to arrive sums the partials in slice
                 // order; no thread waits on another CTA
                 __threadfence();
                 __syncwarp();
                 int old = 0;
-                int32_t *count = a.split_count + t * 8 + (warp - 2);
+                int32_t *count = a.split_count + tt * 8 + (warp - 2);
                 if (lane == 0) old = atomicAdd(count, 1);
                 old = __shfl_sync(0xffffffffu, old, 0);
                 if (old == S - 1) {
                     __threadfence();
-                    const float *p0 = a.split_part + (t * S * kTcBM + row_in_tile) * BN + half * HALF;
+                    const float *p0 = a.split_part + (tt * S * kTcBM + row_in_tile) * BN + half * HALF;
                     for (int c = 0; c < HALF && live_row; c += 16) {
                         const int64_t o0 = o_base + c;
                         if (o0 >= a.N) break;
@@ -632,16 +669,21 @@ static int launch_tc_t(TcArgs a, const int8_t *codes, int64_t ld_codes, const in
         return BD_ERR_LAUNCH;
     const int64_t tiles = a.m_tiles * a.n_tiles;
     a.splits = 1;
+    a.split_full = tiles;
     if (EPI == TC_F32 && a.split_ws && (reinterpret_cast<uintptr_t>(a.split_ws) & 255) == 0) {
         const int64_t nk = (a.K + tc_bk(EPI) - 1) / tc_bk(EPI) * a.parts;
-        const int s = tc_split_slices(tiles, nk, sms_tc());
-        if (s > 1 && tc_split_bytes(tiles, s, BN) <= a.split_ws_bytes) {
+        int64_t full = tiles;
+        int s = 1;
+        tc_split_plan(tiles, nk, sms_tc(), full, s);
+        if (s > 1 && tc_split_bytes(tiles - full, s, BN) <= a.split_ws_bytes) {
             a.splits = s;
+            a.split_full = full;
             a.split_count = static_cast<int32_t *>(a.split_ws);
             a.split_part = reinterpret_cast<float *>(static_cast<char *>(a.split_ws) + kTcSplitCounts * sizeof(int32_t));
         }
     }
-    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(tiles * a.splits, sms_tc()));
+    const int64_t units = a.splits > 1 ? a.split_full + (tiles - a.split_full) * a.splits : tiles;
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(units, sms_tc()));
     kern<<<grid, 320, smem, stream>>>(a, ma, mb, ma2, mb2, ma3, mb3);
     BD_CHECK_LAUNCH();
     return BD_OK;
@@ -728,7 +770,8 @@ extern "C" int bd_tile_signs_i8(const float *latent, int64_t rows, int64_t cols,
 }
 
 extern "C" int bd_gemm_bf16(const uint16_t *a, int64_t m, int64_t k, int64_t lda, const uint16_t *b, int64_t n,
-                            int64_t ldb, float *c, int64_t ldc, bd_stream_t stream) {
+                            int64_t ldb, float *c, int64_t ldc, void *workspace, size_t workspace_bytes,
+                            bd_stream_t stream) {
     if (m < 1 || k < 1 || n < 1 || lda < k || ldb < k || ldc < n || !a || !b || !c) return BD_ERR_INVALID;
     TcArgs t{};
     t.M = m;
@@ -736,6 +779,8 @@ extern "C" int bd_gemm_bf16(const uint16_t *a, int64_t m, int64_t k, int64_t lda
     t.K = k;
     t.ld_out = ldc;
     t.out = c;
+    t.split_ws = workspace;
+    t.split_ws_bytes = workspace_bytes;
     // strides in bytes for the tensor maps (multiples of 16: lda, ldb multiples of 8)
     return launch_tc_gemm(TC_F32, t, reinterpret_cast<const int8_t *>(a), lda * 2,
                           reinterpret_cast<const int8_t *>(b), n, ldb * 2, static_cast<cudaStream_t>(stream));
@@ -855,8 +900,10 @@ extern "C" int bd_projection_he4_tc(const int8_t *codes, int64_t ld_codes, const
 extern "C" size_t bd_gemm_split_workspace_bytes(int64_t m, int64_t n, int64_t k, int parts) {
     if (m < 1 || n < 1 || k < 1 || parts < 1 || parts > 3) return 0;
     const int64_t tiles = tc_tiles(m, n);
-    const int s = tc_split_slices(tiles, (k + 63) / 64 * parts, sms_tc());
-    return s > 1 ? tc_split_bytes(tiles, s, 256) : 0;
+    int64_t full = tiles;
+    int s = 1;
+    tc_split_plan(tiles, (k + 63) / 64 * parts, sms_tc(), full, s);
+    return s > 1 ? tc_split_bytes(tiles - full, s, 256) : 0;
 }
 
 extern "C" int bd_gemm_bf16_split(const uint16_t *a_hi, const uint16_t *a_lo, int64_t m, int64_t k, int64_t lda,

@@ -326,7 +326,10 @@ def gemm_bf16(a: Tensor, b: Tensor, out: Tensor | None = None) -> Tensor:
         raise ValueError("gemm_bf16 operands need unit column stride and row strides that are multiples of 8")
     device = _require_cuda(a, b)
     c = torch.empty((m, n), dtype=torch.float32, device=device) if out is None else out
-    _lib.call("bd_gemm_bf16", _p(a), m, k, a.stride(0), _p(b), n, b.stride(0), _p(c), c.stride(0), _stream(device))
+    nbytes = int(_lib.load().bd_gemm_split_workspace_bytes(m, n, k, 1))
+    ws = workspace(device, "gemm_split", nbytes) if nbytes else None
+    _lib.call("bd_gemm_bf16", _p(a), m, k, a.stride(0), _p(b), n, b.stride(0), _p(c), c.stride(0),
+              None if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(), _stream(device))
     return c
 
 

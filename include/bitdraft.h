@@ -234,9 +234,11 @@ int bd_tile_signs_i8(const float *latent, int64_t rows, int64_t cols, int8_t *ou
  * TMEM): c[m][n] = sum_k a[m][k] b[n][k], a and b row-major bf16 with row strides
  * lda, ldb (elements, multiples of 8, 16-byte aligned bases), c fp32 with row
  * stride ldc.  Used for the context fusion and the context K/V projections of a
- * long prefill (model.py:349-351, 382-386). */
+ * long prefill (model.py:349-351, 382-386).  workspace: as for
+ * bd_gemm_bf16_split (bd_gemm_split_workspace_bytes(m, n, k, 1); NULL runs the
+ * product unsplit). */
 int bd_gemm_bf16(const uint16_t *a, int64_t m, int64_t k, int64_t lda, const uint16_t *b, int64_t n, int64_t ldb,
-                 float *c, int64_t ldc, bd_stream_t stream);
+                 float *c, int64_t ldc, void *workspace, size_t workspace_bytes, bd_stream_t stream);
 
 int bd_gemm_i8(const int8_t *codes, int64_t tokens, int64_t k, const int8_t *signs_i8, int64_t outs,
                int32_t *dots, bd_stream_t stream);
@@ -582,13 +584,12 @@ int bd_codes_transpose_bf16(const int8_t *codes, int64_t rows, int64_t cols, int
 int bd_gemm_bf16_split(const uint16_t *a_hi, const uint16_t *a_lo, int64_t m, int64_t k, int64_t lda,
                        const uint16_t *b, int64_t n, int64_t ldb, float *c, int64_t ldc, void *workspace,
                        size_t workspace_bytes, bd_stream_t stream);
-/* Split-K workspace of bd_gemm_bf16_split / bd_gemm_bf16_split3 (parts = 2 or 3
- * operand pairs) for an m x n x k product: when the 128 x 256 output tiles
- * leave SMs idle in their last wave, the K reduction is cut into slices on
- * more CTAs, each writing an fp32 partial tile, and the last slice of a tile to
- * finish adds them in slice order (deterministic).  The slice count minimises
- * the waves of (tile, slice) units per tile, at most 8 slices and partial tiles
- * within half of L2.  0 = no split for this shape.  The workspace (256-byte aligned) must be zero when first used; the
+/* Split-K workspace of bd_gemm_bf16 / bd_gemm_bf16_split / bd_gemm_bf16_split3
+ * (parts = 1, 2 or 3 operand pairs) for an m x n x k product: when the 128 x 256
+ * output tiles are fewer than the SMs, the K reduction is cut into slices on
+ * more CTAs (slice count from the waves of (tile, slice) units, at most 8), each
+ * slice writing an fp32 partial tile, and the last slice of a tile to finish
+ * adds them in slice order (deterministic).  0 = no split for this shape.  The workspace (256-byte aligned) must be zero when first used; the
  * calls leave its counters zero.  Calls sharing one workspace must be ordered
  * (one stream); a NULL or smaller workspace runs the product unsplit. */
 size_t bd_gemm_split_workspace_bytes(int64_t m, int64_t n, int64_t k, int parts);

@@ -64,7 +64,9 @@ def test_ffn_w1a1_large_config3(ops):
     assert np.array_equal(y_small.cpu().numpy(), y[:40].cpu().numpy())
 
 
-@pytest.mark.parametrize("m,n,k", [(512, 2560, 10240), (100, 200, 72), (1, 8, 8), (300, 2048, 5120)])
+# (2048, 2560, 10240): 160 output tiles, so the 12 of the second wave are cut into K slices
+@pytest.mark.parametrize("m,n,k", [(512, 2560, 10240), (100, 200, 72), (1, 8, 8), (300, 2048, 5120),
+                                   (2048, 2560, 10240)])
 def test_gemm_bf16(ops, m, n, k):
     g = torch.Generator().manual_seed(m + n + k)
     a = torch.randn((m, k), generator=g).to(torch.bfloat16)
