@@ -598,6 +598,210 @@ __global__ void __launch_bounds__(320, 1) tc_gemm_kernel(const TcArgs a, const _
     }
 }
 
+// ------------------------------------------------------------------ SM pairs (TC_F32)
+// A cluster of two CTAs computes a 256 x 256 output tile with tcgen05.mma.cta_group::2:
+// CTA r of the pair loads rows [128 r, 128 r + 128) of the tile's A and of its B (its
+// half of the 256 output columns) into its own shared memory; the even CTA issues the
+// MMAs, which read both CTAs' halves and leave each CTA's 128 rows x 256 columns of
+// accumulators in its own TMEM.  A stage is 32 KB per CTA instead of 48 KB, so six
+// stages fit: twice the MACs in flight of the single-CTA kernel.  Both CTAs' TMA loads
+// complete on the even CTA's full barrier (which expects both halves); the MMA
+// commits arrive on both CTAs' empty and accumulator barriers; both CTAs' epilogue
+// warps arrive on the even CTA's accumulator-empty barrier.  Every wait is bounded.
+constexpr int kPairStages = 6;
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// The even CTA's copy of a shared-memory object of this CTA (same offset).
+__device__ __forceinline__ uint32_t even_cta_addr(const void *p) {
+    uint32_t out;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(out) : "r"(su32(p)));
+    return out;
+}
+__device__ __forceinline__ void cluster_sync_pair() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tma_2d_pair(void *dst, const CUtensorMap *map, uint32_t bar_even, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+        "%4}], [%2];" ::"r"(su32(dst)),
+        "l"(map), "r"(bar_even), "r"(c0), "r"(c1)
+        : "memory");
+}
+// Instruction descriptor, kind::f16, bf16 operands, f32 accumulators, K-major, M = 256 (a pair), N.
+__host__ __device__ constexpr uint32_t idesc_bf16_pair(int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) | (256u >> 4 << 24);
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
+    tc_pair_kernel(const TcArgs a, const __grid_constant__ CUtensorMap ma, const __grid_constant__ CUtensorMap mb,
+                   const __grid_constant__ CUtensorMap ma2, const __grid_constant__ CUtensorMap mb2,
+                   const __grid_constant__ CUtensorMap ma3, const __grid_constant__ CUtensorMap mb3) {
+    constexpr int BN = 256, HALF_ROWS = 128;
+    constexpr uint32_t kStageBytes = (HALF_ROWS + HALF_ROWS) * kTcBK;  // this CTA's A and B halves
+    extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sa = smem;                                   // stages x 16 KB: A rows of this CTA
+    uint8_t *sb = smem + kPairStages * HALF_ROWS * kTcBK;  // stages x 16 KB: B rows of this CTA
+    __shared__ __align__(8) uint64_t full[kPairStages], empty[kPairStages], acc_full[2], acc_empty[2], drain;
+    __shared__ uint32_t tmem_base;
+    __shared__ volatile int abort_flag;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int64_t pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+    const int64_t pm = (a.M + 2 * HALF_ROWS - 1) / (2 * HALF_ROWS);  // 256-row tiles
+    const int64_t tiles = pm * a.n_tiles;
+    const int nk1 = static_cast<int>((a.K + 63) / 64);
+    const int nk = nk1 * (a.parts > 1 ? a.parts : 1);
+    constexpr uint32_t kCols = 2 * BN;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kPairStages; ++s) {
+            mb_init(&full[s], 1);
+            mb_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mb_init(&acc_full[b], 1);
+            mb_init(&acc_empty[b], 16);  // every epilogue warp of both CTAs (used on the even CTA)
+        }
+        mb_init(&drain, 1);
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_base)),
+                     "n"(kCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    }
+    __syncthreads();
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    cluster_sync_pair();  // both CTAs' barriers and TMEM exist before either uses the other's
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = tmem_base;
+
+    if (warp == 0) {
+        if (lane == 0) {  // TMA producer (both CTAs): this CTA's halves, completing on the even CTA's barrier
+            uint32_t it = 0;
+            for (int64_t t = pair; t < tiles && !abort_flag; t += pairs) {
+                const int m0 = static_cast<int>((t % pm) * 2 * HALF_ROWS + rank * HALF_ROWS);
+                const int n0 = static_cast<int>((t / pm) * BN + rank * HALF_ROWS);
+                for (int k = 0; k < nk; ++k, ++it) {
+                    const int s = it % kPairStages;
+                    if (it >= kPairStages && !mb_wait(&empty[s], ((it / kPairStages) - 1) & 1, &abort_flag)) break;
+                    if (rank == 0) mb_expect_tx(&full[s], 2 * kStageBytes);
+                    const int part = k / nk1, kc = k - part * nk1;
+                    const uint32_t bar = even_cta_addr(&full[s]);
+                    tma_2d_pair(sa + s * HALF_ROWS * kTcBK, part == 0 ? &ma : (part == 1 ? &ma2 : &ma3), bar, kc * 64, m0);
+                    tma_2d_pair(sb + s * HALF_ROWS * kTcBK, part == 0 ? &mb : (part == 1 ? &mb2 : &mb3), bar, kc * 64, n0);
+                }
+            }
+            if (abort_flag && rank == 0) {  // the loads of both halves of the stages issued land first
+                for (uint32_t j = it > static_cast<uint32_t>(kPairStages) ? it - kPairStages : 0; j < it; ++j)
+                    mb_drain(&full[j % kPairStages], (j / kPairStages) & 1);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {  // MMA issuer: the even CTA only
+            constexpr uint32_t idesc = idesc_bf16_pair(BN);
+            uint32_t it = 0, lt = 0;
+            for (int64_t t = pair; t < tiles && !abort_flag; t += pairs, ++lt) {
+                const uint32_t b = lt & 1;
+                if (!mb_wait(&acc_empty[b], ((lt >> 1) & 1) ^ 1, &abort_flag)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t d = tmem + b * BN;
+                bool ok = true;
+                for (int k = 0; k < nk; ++k, ++it) {
+                    const int s = it % kPairStages;
+                    if (!mb_wait(&full[s], (it / kPairStages) & 1, &abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint64_t da = sdesc(sa + s * HALF_ROWS * kTcBK), db = sdesc(sb + s * HALF_ROWS * kTcBK);
+#pragma unroll
+                    for (int kk = 0; kk < kTcBK / 32; ++kk) {
+                        const uint32_t accumulate = (k > 0 || kk > 0) ? 1u : 0u;
+                        asm volatile(
+                            "{\n .reg .pred p;\n setp.ne.u32 p, %4, 0;\n"
+                            " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+                            "l"(da + static_cast<uint64_t>(2 * kk)), "l"(db + static_cast<uint64_t>(2 * kk)),
+                            "r"(idesc), "r"(accumulate));
+                    }
+                    asm volatile(
+                        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], "
+                        "%1;" ::"r"(su32(&empty[s])),
+                        "h"(static_cast<uint16_t>(3))
+                        : "memory");
+                }
+                asm volatile(
+                    "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+                        su32(&acc_full[b])),
+                    "h"(static_cast<uint16_t>(3))
+                    : "memory");
+                if (!ok) break;
+            }
+            if (abort_flag) {  // every MMA issued completes before either CTA frees TMEM or leaves
+                asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                 su32(&drain))
+                             : "memory");
+                mb_drain(&drain, 0);
+            }
+        }
+    } else {  // epilogue warps 2..9 of both CTAs: TMEM lanes 32 (w % 4) .., column half (w - 2) / 4
+        const int quarter = warp & 3, half = (warp - 2) >> 2;
+        const int row_in_tile = quarter * 32 + lane;
+        constexpr int HALF = BN / 2;
+        const bool vec_out = (a.ld_out & 3) == 0 && (reinterpret_cast<uintptr_t>(a.out) & 15) == 0;
+        const uint32_t empty_even[2] = {even_cta_addr(&acc_empty[0]), even_cta_addr(&acc_empty[1])};
+        uint32_t lt = 0;
+        for (int64_t t = pair; t < tiles && !abort_flag; t += pairs, ++lt) {
+            const uint32_t b = lt & 1;
+            if (!mb_wait(&acc_full[b], (lt >> 1) & 1, &abort_flag)) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const int64_t row = (t % pm) * 2 * HALF_ROWS + rank * HALF_ROWS + row_in_tile;
+            const bool live_row = row < a.M;
+            const int64_t o_base = (t / pm) * BN + half * HALF;
+            for (int c = 0; c < HALF; c += 16) {
+                uint32_t v[16];
+                const uint32_t taddr = tmem + b * BN + (static_cast<uint32_t>(quarter * 32) << 16) + half * HALF + c;
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                    : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                      "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+                    : "r"(taddr));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                const int64_t o0 = o_base + c;
+                if (!live_row || o0 >= a.N) continue;
+                const int64_t idx = row * a.ld_out + o0;
+                if (o0 + 16 <= a.N && vec_out) {
+#pragma unroll
+                    for (int j = 0; j < 16; j += 4)
+                        *reinterpret_cast<float4 *>(a.out + idx + j) =
+                            make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
+                                        __uint_as_float(v[j + 3]));
+                } else {
+                    for (int j = 0; j < 16 && o0 + j < a.N; ++j) a.out[idx + j] = __uint_as_float(v[j]);
+                }
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0)
+                asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(empty_even[b])
+                             : "memory");
+        }
+    }
+    if (abort_flag && threadIdx.x == 0) set_flag(a.flags, BD_FLAG_TIMEOUT);
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    cluster_sync_pair();  // no CTA frees TMEM or leaves while the pair's MMAs or loads may touch it
+    if (warp == 1) {
+        __syncwarp();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(kCols));
+    }
+}
+
 // ------------------------------------------------------------------ host side
 
 static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
@@ -683,6 +887,25 @@ static int launch_tc_t(TcArgs a, const int8_t *codes, int64_t ld_codes, const in
         }
     }
     const int64_t units = a.splits > 1 ? a.split_full + (tiles - a.split_full) * a.splits : tiles;
+    if (EPI == TC_F32 && a.splits == 1 && BN == 256 && a.M >= 512 && tiles >= sms_tc()) {
+        // SM pairs for products that fill the GPU: 256-row tiles, A and B halves per CTA
+        // (the tensor maps' boxes are 128 rows); measured 4-8 % faster than single CTAs
+        // at 2048-4096 rows
+        CUtensorMap pb, pb2, pb3;
+        if (!make_i8_map(&pb, weights, w_rows, a.K, ld_w, kTcBM, bf16) ||
+            !make_i8_map(&pb2, more.b2 ? more.b2 : weights, w_rows, a.K, ld_w, kTcBM, bf16) ||
+            !make_i8_map(&pb3, more.b3 ? more.b3 : weights, w_rows, a.K, ld_w, kTcBM, bf16))
+            return BD_ERR_ALIGNMENT;
+        const size_t psmem = static_cast<size_t>(kPairStages) * 2 * kTcBM * kTcBK + 1024;
+        if (cudaFuncSetAttribute(tc_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(psmem)) !=
+            cudaSuccess)
+            return BD_ERR_LAUNCH;
+        const int64_t ptiles = (a.M + 255) / 256 * a.n_tiles;
+        const unsigned pgrid = static_cast<unsigned>(2 * std::min<int64_t>(ptiles, sms_tc() / 2));
+        tc_pair_kernel<<<pgrid, 320, psmem, stream>>>(a, ma, pb, ma2, pb2, ma3, pb3);
+        BD_CHECK_LAUNCH();
+        return BD_OK;
+    }
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>(units, sms_tc()));
     kern<<<grid, 320, smem, stream>>>(a, ma, mb, ma2, mb2, ma3, mb3);
     BD_CHECK_LAUNCH();

@@ -64,9 +64,10 @@ def test_ffn_w1a1_large_config3(ops):
     assert np.array_equal(y_small.cpu().numpy(), y[:40].cpu().numpy())
 
 
-# (2048, 2560, 10240): 160 output tiles, so the 12 of the second wave are cut into K slices
+# (2048, 2560, 10240) and (1000, 8192, 2560): products that fill the GPU run on SM pairs
+# (256-row tiles over two CTAs, tcgen05 cta_group::2); 1000 rows end inside a pair's second half
 @pytest.mark.parametrize("m,n,k", [(512, 2560, 10240), (100, 200, 72), (1, 8, 8), (300, 2048, 5120),
-                                   (2048, 2560, 10240)])
+                                   (2048, 2560, 10240), (1000, 8192, 2560)])
 def test_gemm_bf16(ops, m, n, k):
     g = torch.Generator().manual_seed(m + n + k)
     a = torch.randn((m, k), generator=g).to(torch.bfloat16)
