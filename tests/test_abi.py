@@ -61,6 +61,20 @@ def test_host_only_entry_points():
     addr = 256
     assert lib.bd_accept_greedy_noalloc(addr, 257, 4, 100, addr, None, 0, addr, addr, None, None, None) == 6
     assert lib.bd_accept_greedy_noalloc(addr, 1, 33, 100, addr, None, 0, addr, addr, None, None, None) == 6
+    # training entries: sizes outside what the kernels handle are refused on the host
+    assert lib.bd_train_attention_forward(*([None] * 8), 0, 16, 8, 4, 128, 2048, 0.1, None, None, None, None) == 1
+    assert lib.bd_train_attention_forward(*([None] * 8), 32, 17, 8, 4, 128, 2048, 0.1, None, None, None, None) == 1
+    assert lib.bd_train_attention_backward(*([None] * 14), 32, 16, 8, 5, 128, 2048, 0.1, *([None] * 7)) == 1
+    assert lib.bd_train_attention_pack(*([None] * 6), 0, 0, 0, None, 0, 0, 32, 16, 8, 4, 129, 2048,
+                                       *([None] * 9), None) == 1
+    assert lib.bd_train_attention_pack_grad(None, None, 32, 16, 8, 4, 0, None, None, None, None, None) == 1
+    assert lib.bd_rms_forward(None, 0, 2560, None, 1e-6, None, None, None) == 0  # nothing to do
+    assert lib.bd_rms_forward(None, -1, 2560, None, 1e-6, None, None, None) == 1
+    assert lib.bd_head_post(addr, 3, 4, 1, 3, None, 1e-6, None, None, 0, addr, None, None, None) == 1  # odd head_dim
+    assert lib.bd_rms_partials(17) == 3 and lib.bd_head_post_partials(512, 32) > 0
+    # split-K workspaces: a 480-row product over a 151936-long K is split, a 4096-row one is not
+    assert lib.bd_gemm_split_workspace_bytes(480, 2560, 151936, 3) > 0
+    assert lib.bd_gemm_split_workspace_bytes(4096, 2560, 2560, 2) == 0
 
 
 def test_missing_library_fails_loudly(monkeypatch, tmp_path):
