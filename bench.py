@@ -745,12 +745,16 @@ def workload_qat(args, pkg, device, rank: int, world: int) -> list[dict]:
     # the gradient all-reduce runs in buckets during the last sequence's backward pass
     exchange = qat.GradientExchange(params)
 
+    model_mod = importlib.import_module("binary-eagle-decoding_b200.model")
+
     def step(u):
         opt.zero_grad()
-        for i, (feats, tokens, windows) in enumerate(samples):
-            exchange.armed = i == len(samples) - 1
-            qat.group_loss_deferred(model, feats, tokens, windows, scale=1.0 / seqs)
-        exchange.finish()
+        # the device error checks of all sequences read once, before the norm and the update
+        with model_mod.deferred_checks(device):
+            for i, (feats, tokens, windows) in enumerate(samples):
+                exchange.armed = i == len(samples) - 1
+                qat.group_loss(model, feats, tokens, windows, scale=1.0 / seqs)
+            exchange.finish()
         _, coef = qat.clip_grad_norm(params, 1.0)
         opt.step(coef)
 
