@@ -427,6 +427,11 @@ __global__ void __launch_bounds__(kDnMaxWarps * 32) down_w8_kernel(const DnW8Arg
     const int t4 = lane & 3;
     const int nb = static_cast<int>(rank * ncl / a.cs), ne = static_cast<int>((rank + 1) * ncl / a.cs);
     float ep[2][2] = {};  // scale, midpoint
+    // and its residual: the block's input, written before the block's first kernel, which
+    // (like every kernel of the block) let this one launch only after its own dependency
+    // wait, so it is complete here; out may alias it (each element is read, then written,
+    // by the same thread)
+    float res[MT][4] = {};
     if (nb + warp < ne) {
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
@@ -435,6 +440,17 @@ __global__ void __launch_bounds__(kDnMaxWarps * 32) down_w8_kernel(const DnW8Arg
                 ep[0][e] = __ldg(a.scale0 + o);
                 ep[1][e] = (EPI == EPI_HE4 && a.mid0) ? __ldg(a.mid0 + o) : 0.0f;
             }
+        }
+        if (a.residual) {
+            const int g8 = lane >> 2;
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    const int tok = mt * 16 + g8 + 8 * (r >> 1);
+                    const int64_t o = (n0 + nb + warp) * 8 + 2 * t4 + (r & 1);
+                    if (tok < a.tokens && o < a.rows) res[mt][r] = a.residual[static_cast<int64_t>(tok) * a.rows + o];
+                }
         }
     }
     grid_wait();
@@ -565,7 +581,7 @@ __global__ void __launch_bounds__(kDnMaxWarps * 32) down_w8_kernel(const DnW8Arg
                     y = __fmul_rn(__fmul_rn(static_cast<float>(D), sc), __ldg(a.row_scale + tok));
                 }
                 const int64_t idx = static_cast<int64_t>(tok) * a.rows + o;
-                if (a.residual) y = __fadd_rn(a.residual[idx], y);
+                if (a.residual) y = __fadd_rn(first ? res[mt][r] : a.residual[idx], y);
                 a.out[idx] = y;
                 if (a.raw_dot) a.raw_dot[idx] = D;
             }
