@@ -746,14 +746,18 @@ def workload_qat(args, pkg, device, rank: int, world: int) -> list[dict]:
     exchange = qat.GradientExchange(params)
 
     model_mod = importlib.import_module("binary-eagle-decoding_b200.model")
+    # the latent gradients of all sequences as one product per projection, each handed
+    # to the exchange as soon as it is written
+    latent_grads = pkg.LatentGradients(model, seqs * windows_per * 16, on_ready=exchange.ready)
 
     def step(u):
         opt.zero_grad()
         # the device error checks of all sequences read once, before the norm and the update
         with model_mod.deferred_checks(device):
-            for i, (feats, tokens, windows) in enumerate(samples):
-                exchange.armed = i == len(samples) - 1
-                qat.group_loss(model, feats, tokens, windows, scale=1.0 / seqs)
+            with latent_grads:
+                for i, (feats, tokens, windows) in enumerate(samples):
+                    exchange.armed = i == len(samples) - 1
+                    qat.group_loss(model, feats, tokens, windows, scale=1.0 / seqs)
             exchange.finish()
         _, coef = qat.clip_grad_norm(params, 1.0)
         opt.step(coef)

@@ -9,5 +9,5 @@ format.  All computation on the hot path runs in ``libbitdraft.so``
 """
 
 from . import _lib, export, ops  # noqa: F401
-from .model import (HE4, FrozenLinear, Geometry, Layer, Projection, bound_latents, cache_storage,  # noqa: F401
-                    clamp_latents, hard_sign, rms, rope)
+from .model import (HE4, FrozenLinear, Geometry, LatentGradients, Layer, Projection, bound_latents,  # noqa: F401
+                    cache_storage, clamp_latents, hard_sign, rms, rope)

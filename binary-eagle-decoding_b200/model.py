@@ -29,6 +29,7 @@ from . import _lib, ops
 
 MAX_DECODE_ROWS = ops.MAX_DECODE_TOKENS
 _DEFERRED: list[ops.Flags] = []  # flags words of the active deferred_checks contexts
+_LATENT: list["LatentGradients"] = []  # active latent-gradient accumulations
 
 
 @dataclass(frozen=True)
@@ -207,6 +208,12 @@ def head_post(value: Tensor, heads: int, dim: int, weight: Tensor | None, epsilo
     return _HeadPostFn.apply(value, weight, positions, frequencies, epsilon, fp16, heads, dim)
 
 
+def _ids_valid(values: tuple, limit: int) -> bool:
+    """Every value an ``int`` (not a ``bool``) in ``[0, limit)``, in C-level passes
+    over the tuple (a per-item Python test costs milliseconds at 2048 tokens)."""
+    return not values or (set(map(type, values)) == {int} and min(values) >= 0 and max(values) < limit)
+
+
 def _to_device(values: list[int], device: torch.device) -> Tensor:
     """A small int64 tensor on ``device`` without a host synchronisation (pinned copy)."""
     host = torch.tensor(values, dtype=torch.int64)
@@ -221,8 +228,7 @@ def _need_cuda(t: Tensor) -> torch.device:
     return t.device
 
 
-def _stream(device: torch.device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+_stream = ops._stream
 
 
 class deferred_checks:
@@ -475,12 +481,20 @@ class _ProjectionFn(torch.autograd.Function):
         bits = module.bits
         need = ctx.needs_input_grad
         need_latent = need[1] or (ctx.learned and need[6])
+        # inside a LatentGradients context the latent-side operands go to its buffers
+        acc = next((a for a in reversed(_LATENT) if a.owns(module)), None) if need_latent else None
         g = grad_out.reshape(tokens, outer).float().contiguous()
         ld_o, ld_t = _round8(outer), _round8(tokens)
         hi = torch.empty((tokens, ld_o), dtype=torch.bfloat16, device=device)
         lo = torch.empty_like(hi)
-        hi_t = torch.empty((outer, ld_t), dtype=torch.bfloat16, device=device) if need_latent else None
-        lo_t = torch.empty_like(hi_t) if need_latent else None
+        hi_t = lo_t = None
+        t_hi = t_lo = t_codes = None
+        if acc is not None:
+            t_hi, t_lo, t_codes, ld_t = acc.columns(module, tokens, latent, bound, window)
+        elif need_latent:
+            hi_t = torch.empty((outer, ld_t), dtype=torch.bfloat16, device=device)
+            lo_t = torch.empty_like(hi_t)
+            t_hi, t_lo = hi_t.data_ptr(), lo_t.data_ptr()
         d_scale = torch.empty(outer, dtype=torch.float32, device=device)
         d_mid = torch.empty_like(d_scale)
         gm = torch.empty(tokens, dtype=torch.float32, device=device)
@@ -488,8 +502,7 @@ class _ProjectionFn(torch.autograd.Function):
         ws = ops.workspace(device, "ste", nbytes)
         sc, mid = scale.detach().contiguous(), midpoint.detach().contiguous()
         _lib.call("bd_ste_grad_prep", g.data_ptr(), dot.data_ptr(), tokens, outer, sc.data_ptr(), mid.data_ptr(),
-                  bound.data_ptr(), bits, sums.data_ptr(), hi.data_ptr(), lo.data_ptr(), ld_o,
-                  None if hi_t is None else hi_t.data_ptr(), None if lo_t is None else lo_t.data_ptr(), ld_t,
+                  bound.data_ptr(), bits, sums.data_ptr(), hi.data_ptr(), lo.data_ptr(), ld_o, t_hi, t_lo, ld_t,
                   d_scale.data_ptr(), d_mid.data_ptr(), gm.data_ptr(), ws.data_ptr(), ws.numel(), stream)
         dx = d_gain = d_clip = d_latent = d_window = None
         if need[0] or need[4] or need[5]:
@@ -506,7 +519,9 @@ class _ProjectionFn(torch.autograd.Function):
                       ws.data_ptr(), ws.numel(), stream)
             dx = dx.view(ctx.value_shape)
             d_clip = d_clip.reshape(())
-        if need_latent:
+        if acc is not None:
+            _lib.call("bd_codes_transpose_bf16", codes.data_ptr(), tokens, inner, ctx.ld, t_codes, ld_t, stream)
+        elif need_latent:
             codes_t = torch.empty((inner, ld_t), dtype=torch.bfloat16, device=device)
             _lib.call("bd_codes_transpose_bf16", codes.data_ptr(), tokens, inner, ctx.ld, codes_t.data_ptr(), ld_t,
                       stream)
@@ -618,6 +633,131 @@ class Projection(nn.Module):
 
 def _projections(model: nn.Module):
     return [m for m in model.modules() if isinstance(m, Projection)]
+
+
+def _add_grad(parameter: nn.Parameter, grad: Tensor) -> None:
+    if parameter.grad is None:
+        parameter.grad = grad
+    else:
+        parameter.grad.add_(grad)
+
+
+class LatentGradients:
+    """Gradient accumulation of the binary projections' latents over several
+    backward passes (one update over many sequences) as one tensor-core product
+    per projection.
+
+    Inside ``with LatentGradients(model, rows):`` a projection's backward writes
+    the transposed bf16 halves of its output gradient and its transposed codes
+    side by side into per-projection buffers of ``rows`` columns instead of
+    running its latent-gradient GEMM.  Leaving the context runs one
+    ``bd_ste_weight_grad`` per projection over all the columns, so the
+    clip-window mask, the fp32 latent read and the gradient write happen once
+    per update instead of once per sequence, and no gradient is added between
+    passes.  The product over the concatenated columns is the sum of the
+    per-sequence products (the mask, the step scale and the window do not depend
+    on the sequence), accumulated in fp32 by the tensor cores in one pass.
+
+    A buffer that would overflow, or a latent that changed since the columns were
+    written, is flushed first, so the result does not depend on ``rows``; ``rows``
+    only sizes the buffers (the sum of the rows of the backward passes).  At a
+    flush ``latent_sign.grad`` and ``log_window.grad`` are set or added to, and
+    ``on_ready(parameter)`` is called for each, in module order (every rank flushes
+    in the same order, so a data-parallel exchange issues the same collectives).
+    Buffers are kept for the next use of the same object."""
+
+    def __init__(self, model: nn.Module, rows: int, on_ready=None) -> None:
+        if rows < 1:
+            raise ValueError("rows must be positive")
+        self.modules = _projections(model)
+        self.rows = _round8(int(rows))
+        self.on_ready = on_ready
+        self._owned = {id(m) for m in self.modules}
+        self._slots: dict[int, dict] = {}
+
+    def __enter__(self) -> "LatentGradients":
+        _LATENT.append(self)
+        return self
+
+    def __exit__(self, *exc) -> None:
+        _LATENT.remove(self)
+        if exc[0] is None:
+            self.flush()
+        else:
+            for s in self._slots.values():
+                s["filled"] = 0
+
+    def owns(self, module: "Projection") -> bool:
+        return id(module) in self._owned
+
+    def columns(self, module: "Projection", tokens: int, latent: Tensor, bound: Tensor,
+                window: Tensor | None) -> tuple[int, int, int, int]:
+        """Device addresses of ``tokens`` free columns in the module's dL^T hi, dL^T lo
+        and codes^T buffers, and the buffers' row stride (elements)."""
+        width = _round8(tokens)
+        key = (latent.data_ptr(), latent._version)
+        s = self._slots.get(id(module))
+        if s is not None and s["filled"] and (s["key"] != key or s["filled"] + width > s["cap"]):
+            self._flush_one(module, s)
+        if s is None or s["cap"] < width:
+            cap = max(self.rows, width)
+            outer, inner = latent.shape
+            s = {"hi": torch.empty((outer, cap), dtype=torch.bfloat16, device=latent.device),
+                 "codes": torch.empty((inner, cap), dtype=torch.bfloat16, device=latent.device),
+                 "cap": cap, "filled": 0}
+            s["lo"] = torch.empty_like(s["hi"])
+            self._slots[id(module)] = s
+        s["key"], s["bound"], s["window"] = key, bound, window
+        off = s["filled"]
+        s["filled"] = off + width
+        if width != tokens:  # padding columns take part in the product: zero on both sides
+            for name in ("hi", "lo", "codes"):
+                s[name][:, off + tokens:off + width].zero_()
+        return (s["hi"].data_ptr() + 2 * off, s["lo"].data_ptr() + 2 * off, s["codes"].data_ptr() + 2 * off,
+                s["cap"])
+
+    def _flush_one(self, module: "Projection", s: dict) -> None:
+        filled, s["filled"] = s["filled"], 0
+        if not filled:
+            return
+        latent = module.latent_sign
+        outer, inner = latent.shape
+        device = latent.device
+        lib = _lib.load()
+        window = s["window"]
+        learned = module.log_window is not None and window is not None
+        partials = None
+        if learned:
+            partials = torch.empty(int(lib.bd_ste_weight_grad_partials(outer, inner)), dtype=torch.float32,
+                                   device=device)
+        d_latent = torch.empty((outer, inner), dtype=torch.float32, device=device)
+        flags, now = _flags(device)
+        _lib.call("bd_ste_weight_grad", s["hi"].data_ptr(), s["lo"].data_ptr(), outer, filled, s["cap"],
+                  s["codes"].data_ptr(), inner, latent.detach().data_ptr(),
+                  window.data_ptr() if learned else None, float(module.window), s["bound"].data_ptr(), module.bits,
+                  d_latent.data_ptr(), None if partials is None else partials.data_ptr(), flags.ptr,
+                  _stream(device))
+        if now:
+            flags.check()
+        ready = []
+        if latent.requires_grad:
+            _add_grad(latent, d_latent)
+            ready.append(latent)
+        if learned and module.log_window.requires_grad:
+            # d/d(log window) = window * sum over |w| > window of the unmasked gradient * sign(w)
+            d_window = (partials.view(-1, 2)[:, 1].sum() * window[0]).reshape(module.log_window.shape)
+            _add_grad(module.log_window, d_window)
+            ready.append(module.log_window)
+        if self.on_ready is not None:
+            for p in ready:
+                self.on_ready(p)
+
+    def flush(self) -> None:
+        """Run the pending latent-gradient products (module order)."""
+        for module in self.modules:
+            s = self._slots.get(id(module))
+            if s is not None:
+                self._flush_one(module, s)
 
 
 def bound_latents(model: nn.Module, multiple: float) -> None:
@@ -939,11 +1079,10 @@ class HE4(nn.Module):
 
     def check(self, features: Tensor, tokens: tuple[int, ...], anchors: tuple[int, ...]) -> None:
         cfg = self.geometry
-        if (not anchors
-                or any(type(anchor) is not int or not 0 <= anchor < len(tokens) for anchor in anchors)
+        if (not anchors or not _ids_valid(anchors, len(tokens))
                 or features.ndim != 2 or features.dtype not in (torch.float16, torch.float32)
                 or features.shape != (len(tokens), cfg.taps * cfg.hidden)
-                or any(type(token) is not int or not 0 <= token < self.vocabulary.shape[0] for token in tokens)):
+                or not _ids_valid(tokens, self.vocabulary.shape[0])):
             raise ValueError("invalid model inputs")
 
     def block(self, slots: int | None) -> int:

@@ -23,7 +23,14 @@ def _p(t: Tensor | None):
     return None if t is None else t.data_ptr()
 
 
+_RAW_STREAM = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(device: torch.device) -> int:
+    """The current CUDA stream of ``device`` as a raw handle (the torch-internal
+    getter where it exists: it skips building a Python stream object per launch)."""
+    if _RAW_STREAM is not None:
+        return _RAW_STREAM(torch.cuda.current_device() if device.index is None else device.index)
     return torch.cuda.current_stream(device).cuda_stream
 
 

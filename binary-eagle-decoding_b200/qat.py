@@ -233,9 +233,11 @@ class GradientExchange:
         self._size = 0
         self._pending: list[tuple[object, Tensor, list[Tensor]]] = []
         self.buckets = 0
-        self._hooks = [p.register_post_accumulate_grad_hook(self._ready) for p in parameters if p.requires_grad]
+        self._hooks = [p.register_post_accumulate_grad_hook(self.ready) for p in parameters if p.requires_grad]
 
-    def _ready(self, parameter: nn.Parameter) -> None:
+    def ready(self, parameter: nn.Parameter) -> None:
+        """A gradient became final (the post-accumulate hook, or a ``LatentGradients``
+        flush): add it to the bucket while the exchange is armed."""
         if not self.armed or self.world == 1 or parameter.grad is None:
             return
         self._bucket.append(parameter)

@@ -128,6 +128,46 @@ def test_projection_learned_window_against_oracle(bd):
     assert abs(gw - ww) <= 1e-3 * abs(ww), (gw, ww)
 
 
+def test_latent_gradients_accumulate_as_one_product(bd):
+    """``LatentGradients``: three backward passes (256, 100 and 300 rows; the 100-row
+    pass leaves padding columns, and ``rows`` = 400 forces a flush before the third)
+    give the latent and window gradients of the same passes accumulated by autograd,
+    within the fp32 summation-order difference, and every other gradient unchanged."""
+    g = torch.Generator().manual_seed(11)
+    inner, outer = 2560, 1536
+    latent = torch.randn((outer, inner), generator=g) * 0.02
+    log_gain = torch.randn(inner, generator=g) * 0.2
+    passes = [(torch.randn((n, inner), generator=g), torch.randn((n, outer), generator=g)) for n in (256, 100, 300)]
+
+    def run(accumulate):
+        layer = bd.Projection(latent, 4, nn.Parameter(log_gain.clone()), nn.Parameter(torch.tensor(0.1)),
+                              window=0.05, learned_window=True).to(DEV)
+        ready = []
+        acc = bd.LatentGradients(layer, 400, on_ready=ready.append) if accumulate else None
+        if acc is not None:
+            acc.__enter__()
+        for value, upstream in passes:
+            (layer(value.to(DEV)) * upstream.to(DEV)).sum().backward()
+            if acc is not None and len(ready) == 0:
+                assert layer.latent_sign.grad is None  # deferred to the flush
+        if acc is not None:
+            acc.__exit__(None, None, None)
+            assert [id(p) for p in ready] == [id(layer.latent_sign), id(layer.log_window)] * 2
+        torch.cuda.synchronize()
+        return {n: p.grad.detach().cpu().double() for n, p in layer.named_parameters()}
+
+    want, got = run(False), run(True)
+    assert set(got) == set(want)
+    for name in want:
+        if name in ("latent_sign", "log_window"):
+            err = float((got[name] - want[name]).norm() / want[name].norm())
+            assert err < 1e-5, (name, err)
+        else:
+            assert torch.equal(got[name], want[name]), name
+    outside = latent.abs() > 0.05
+    assert outside.any() and not got["latent_sign"][outside].any()
+
+
 def test_hard_sign_forward_backward(bd):
     x = torch.tensor([-2.0, -1.0, -0.0, 0.0, 0.5, 1.0, 1.5], device=DEV, requires_grad=True)
     y = bd.hard_sign(x)

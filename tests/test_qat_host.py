@@ -168,6 +168,29 @@ def test_average_gradients_without_process_group_is_a_no_op(qat):
     assert torch.equal(p.grad, torch.ones(3))
 
 
+def test_latent_gradients_context_bookkeeping():
+    """``LatentGradients`` host side: it owns the model's projections only, refuses a
+    non-positive size, and leaves the active-context stack clean on exit, also
+    when the block raises (nothing pending is flushed then)."""
+    model_mod = submodule("model")
+    gain, clip = nn.Parameter(torch.zeros(8)), nn.Parameter(torch.tensor(0.0))
+    inner = model_mod.Projection(torch.randn(4, 8), 4, gain, clip)
+    other = model_mod.Projection(torch.randn(4, 8), 4, gain, clip)
+    holder = nn.Module()
+    holder.proj = inner
+    with pytest.raises(ValueError):
+        model_mod.LatentGradients(holder, 0)
+    acc = model_mod.LatentGradients(holder, 13)
+    assert acc.rows == 16 and acc.owns(inner) and not acc.owns(other)
+    with acc:
+        assert model_mod._LATENT == [acc]
+    assert model_mod._LATENT == []
+    with pytest.raises(RuntimeError, match="boom"):
+        with acc:
+            raise RuntimeError("boom")
+    assert model_mod._LATENT == [] and inner.latent_sign.grad is None
+
+
 class _TableDrafter(nn.Module):
     """A stand-in for ``HE4`` exposing what the loss head uses: ``block``,
     ``group_hidden`` (here a trainable table of hidden states per anchor) and the
