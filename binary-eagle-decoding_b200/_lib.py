@@ -167,6 +167,7 @@ SIGNATURES = {
     "bd_tile_w16": (c_int, [P, c_int, c_int64, c_int64, P, P]),
     "bd_x16_bytes": (c_int64, [c_int, c_int64]),
     "bd_pack_x16": (c_int, [P, c_int, c_int64, c_int64, P, ctypes.c_float, P, P, c_int64, P, P]),
+    "bd_pack_x16_bf16": (c_int, [P, c_int, c_int64, c_int64, P, ctypes.c_float, P, P, c_int64, P, P]),
     "bd_gemv_workspace_bytes": (c_size_t, [c_int, c_int64, c_int64]),
     "bd_gemv_bf16": (c_int, [P, c_int64, c_int64, P, c_int, P, c_int64, P, P, P, P, c_size_t, P]),
     "bd_argmax_finish": (c_int, [P, c_int, P, P]),

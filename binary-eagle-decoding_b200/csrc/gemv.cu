@@ -225,10 +225,19 @@ __global__ void tile_w16_kernel(const T *__restrict__ w, int64_t rows, int64_t c
     }
 }
 
+__device__ __forceinline__ float load_value(const float *row, int64_t k) { return row[k]; }
+__device__ __forceinline__ float load_value(const uint16_t *row, int64_t k) {
+    return __uint_as_float(static_cast<uint32_t>(row[k]) << 16);  // bf16 bits
+}
+
 // Row scale rsqrt(mean(x^2) + eps) of rms (model.py:50-51), by one 256-thread CTA.
-__device__ __forceinline__ float rms_scale(const float *row, int64_t cols, float eps, float *part) {
+template <typename T>
+__device__ __forceinline__ float rms_scale(const T *row, int64_t cols, float eps, float *part) {
     float ss = 0.0f;
-    for (int64_t k = threadIdx.x; k < cols; k += blockDim.x) ss = fmaf(row[k], row[k], ss);
+    for (int64_t k = threadIdx.x; k < cols; k += blockDim.x) {
+        const float v = load_value(row, k);
+        ss = fmaf(v, v, ss);
+    }
 #pragma unroll
     for (int d = 16; d > 0; d >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, d);
     if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
@@ -239,8 +248,10 @@ __device__ __forceinline__ float rms_scale(const float *row, int64_t cols, float
     return rsqrtf(total / static_cast<float>(cols) + eps);
 }
 
-// Pack the 4 columns k0 .. k0 + 3 of one token row into both X16 planes.
-__device__ __forceinline__ void pack_four(const float *row, int64_t k0, int64_t cols, float scale,
+// Pack the 4 columns k0 .. k0 + 3 of one token row into both X16 planes (from bf16
+// rows without a weight the lo plane is zero: hi holds the value exactly).
+template <typename T>
+__device__ __forceinline__ void pack_four(const T *row, int64_t k0, int64_t cols, float scale,
                                           const float *weight, float *normed_row, int token, int64_t nkt,
                                           int64_t ntb, uint32_t *out, bool &bad) {
     float y[4];
@@ -249,7 +260,7 @@ __device__ __forceinline__ void pack_four(const float *row, int64_t k0, int64_t 
         const int64_t k = k0 + j;
         y[j] = 0.0f;
         if (k < cols) {
-            y[j] = row[k];
+            y[j] = load_value(row, k);
             if (weight) y[j] = y[j] * scale * weight[k];
             bad |= !isfinite(y[j]);
             if (normed_row) normed_row[k] = y[j];
@@ -277,7 +288,8 @@ __device__ __forceinline__ void pack_four(const float *row, int64_t k0, int64_t 
 // Grid (tokens, column slices of 1024): each thread packs 4 consecutive columns
 // (two bf16 pairs per plane); columns >= cols are written as zeros.  With a
 // weight every CTA recomputes its row's rms scale (the row is L2-resident).
-__global__ void __launch_bounds__(256) pack_x16_kernel(const float *__restrict__ x, int64_t cols, int64_t ldx,
+template <typename T>
+__global__ void __launch_bounds__(256) pack_x16_kernel(const T *__restrict__ x, int64_t cols, int64_t ldx,
                                                        int64_t nkt, int64_t ntb, const float *__restrict__ weight,
                                                        float eps, uint32_t *__restrict__ out, float *normed,
                                                        int64_t ld_normed, int32_t *flags) {
@@ -285,7 +297,7 @@ __global__ void __launch_bounds__(256) pack_x16_kernel(const float *__restrict__
     grid_wait();
     grid_launch_dependents();
     const int token = blockIdx.x;
-    const float *row = x + token * ldx;
+    const T *row = x + token * ldx;
     const float scale = weight ? rms_scale(row, cols, eps, part) : 1.0f;
     const int64_t k0 = static_cast<int64_t>(blockIdx.y) * 1024 + 4 * threadIdx.x;
     bool bad = false;
@@ -449,7 +461,18 @@ extern "C" int bd_pack_x16(const float *x, int tokens, int64_t cols, int64_t ldx
                            bd_stream_t stream) {
     if (tokens < 1 || tokens > 32 || cols < 1 || ldx < cols || !x || !out) return BD_ERR_INVALID;
     const unsigned slices = static_cast<unsigned>((nkt_of(cols) * 16 + 1023) / 1024);
-    return launch_pdl(pack_x16_kernel, dim3(tokens, slices), dim3(256), 0, stream, x, cols, ldx, nkt_of(cols),
+    return launch_pdl(pack_x16_kernel<float>, dim3(tokens, slices), dim3(256), 0, stream, x, cols, ldx, nkt_of(cols),
+                      static_cast<int64_t>((tokens + 7) / 8), rms_weight, epsilon, static_cast<uint32_t *>(out),
+                      normed, ld_normed, flags);
+}
+
+extern "C" int bd_pack_x16_bf16(const void *x, int tokens, int64_t cols, int64_t ldx, const float *rms_weight,
+                                float epsilon, void *out, float *normed, int64_t ld_normed, int32_t *flags,
+                                bd_stream_t stream) {
+    if (tokens < 1 || tokens > 32 || cols < 1 || ldx < cols || !x || !out) return BD_ERR_INVALID;
+    const unsigned slices = static_cast<unsigned>((nkt_of(cols) * 16 + 1023) / 1024);
+    return launch_pdl(pack_x16_kernel<uint16_t>, dim3(tokens, slices), dim3(256), 0, stream,
+                      static_cast<const uint16_t *>(x), cols, ldx, nkt_of(cols),
                       static_cast<int64_t>((tokens + 7) / 8), rms_weight, epsilon, static_cast<uint32_t *>(out),
                       normed, ld_normed, flags);
 }

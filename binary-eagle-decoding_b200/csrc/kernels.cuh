@@ -16,11 +16,19 @@ int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaS
     cfg.blockDim = block;
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    // a stream created with a priority passes it to its launches explicitly, so that
+    // a CUDA graph captured from it keeps the priority on its kernel nodes
+    int priority = 0;
+    if (cudaStreamGetPriority(stream, &priority) == cudaSuccess && priority != 0) {
+        attr[1].id = cudaLaunchAttributePriority;
+        attr[1].val.priority = priority;
+        cfg.numAttrs = 2;
+    }
     return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...) == cudaSuccess ? BD_OK : BD_ERR_LAUNCH;
 }
 

@@ -209,11 +209,15 @@ class DraftEngine:
         n = features.shape[0]
         if not 1 <= n <= 32 or pos0 + n > self.max_positions - cfg.slots:
             raise ValueError("invalid context rows")
-        feats = features if features.dtype == torch.float32 else features.float()
-        feats = feats.to(self.device).contiguous()
         width = cfg.taps * cfg.hidden
         x16 = self.x16_ctx
-        self._pack(feats, n, width, width, x16=x16)
+        if features.dtype == torch.bfloat16 and features.is_cuda and features.is_contiguous():
+            # bf16 rows pack straight into X16 (the same bits as their fp32 values)
+            _lib.call("bd_pack_x16_bf16", _p(features), n, width, width, None, float(cfg.epsilon), _p(x16), None, 0,
+                      self.flags.ptr, self._stream())
+        else:
+            feats = features if features.dtype == torch.float32 else features.float()
+            self._pack(feats.to(self.device).contiguous(), n, width, width, x16=x16)
         self._gemv(self.fc.data_ptr(), cfg.hidden, width, n, self.fused, cfg.hidden, x16=x16)
         self._pack(self.fused, n, cfg.hidden, cfg.hidden, self.enc_norm, x16=x16)
         kvd = cfg.kv_heads * cfg.head_dim
@@ -275,25 +279,36 @@ class DraftEngine:
         ops.ffn_he4(self.resid[:k], layer.ffn, self.resid[:k], flags=self.flags, out=self.state[:k],
                     norm=layer.ffn_norm, epsilon=self.cfg.epsilon)
 
-    def draft(self, anchor: int, size: int | None = None, logits: Tensor | None = None, join=None) -> Tensor:
+    def draft_start(self, anchor: int, size: int | None = None) -> None:
+        """The part of a block that reads no context row: the slot embeddings and layer
+        0's q|k|v rows (the block's own K/V cache rows)."""
+        k = self.cfg.slots if size is None else size
+        self.embed(k)
+        self.qkv_rows(0, anchor, k)
+
+    def draft(self, anchor: int, size: int | None = None, logits: Tensor | None = None, join=None,
+              started: bool = False) -> Tensor:
         """One block of the drafter over the cached context (model.py:369-396).
 
         Slot tokens come from ``self.ids`` (``set_tokens``); returns the argmax
         token of every slot (int32 [size], device) and fills ``logits`` [size, V]
-        when given.  Graph-capturable for fixed (anchor, size).  ``join`` (optional) is
-        called after layer 0's q|k|v rows and before its attention, the first kernel
-        that reads cache rows below the anchor: a round that ingests context rows on
-        another stream waits for them there.
+        when given.  Graph-capturable for fixed (anchor, size).  ``join(i)`` (optional) is
+        called after layer i's q|k|v rows and before its attention, the first kernel
+        that reads layer i's cache rows below the anchor: a round that ingests context
+        rows on other streams waits for them there.  ``started``: ``draft_start``
+        already ran (on another stream, joined before this call).
         """
         cfg = self.cfg
         k = cfg.slots if size is None else size
         H = cfg.hidden
         st = self._stream()
-        self.embed(k)
+        if not started:
+            self.draft_start(anchor, k)
         for i in range(len(self.layers)):
-            self.qkv_rows(i, anchor, k)
-            if i == 0 and join is not None:
-                join()  # the context rows the attention reads are complete from here on
+            if i > 0:
+                self.qkv_rows(i, anchor, k)
+            if join is not None:
+                join(i)  # the context rows the attention reads are complete from here on
             self.attend(i, anchor, k)
             self.ffn_half(i, k)
         self._pack(self.state, k, H, H, self.out_norm)
@@ -318,7 +333,8 @@ class DraftRound:
         self.host_first = torch.zeros(1, dtype=torch.int32).pin_memory()
         self.host_out = torch.zeros(size, dtype=torch.int32).pin_memory()
         engine.set_tokens(engine.mask, size)
-        self.stream = torch.cuda.Stream(dev)
+        # the ingest (on the capture stream) gates layer 0's attention: the higher priority
+        self.stream = torch.cuda.Stream(dev, priority=-1)
         self.side = torch.cuda.Stream(dev)
         self.stream.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(self.stream):
@@ -338,17 +354,21 @@ class DraftRound:
 
     def _body(self, host: bool = False) -> None:
         # the ingest step (fusion + context k|v of the new rows) runs beside the draft's
-        # embedding and layer-0 q|k|v rows, which do not read the context
+        # embedding and layer-0 q|k|v rows, which do not read the context; the ingest,
+        # the longer of the two, is on the capture stream, whose kernels the graph
+        # launches first
         e = self.engine
         main = torch.cuda.current_stream(e.device)
         if host:
             e.ids[:1].copy_(self.host_first, non_blocking=True)
         self.side.wait_stream(main)
         with torch.cuda.stream(self.side):
-            if host:
-                self.dev_rows.copy_(self.host_rows, non_blocking=True)
-            e.ingest(self.dev_rows, self.anchor - self.rows)
-        e.draft(self.anchor, self.size, join=lambda: main.wait_stream(self.side))
+            e.draft_start(self.anchor, self.size)
+        if host:
+            self.dev_rows.copy_(self.host_rows, non_blocking=True)
+        e.ingest(self.dev_rows, self.anchor - self.rows)
+        main.wait_stream(self.side)
+        e.draft(self.anchor, self.size, started=True)
         if host:
             self.host_out.copy_(e.drafted[: self.size], non_blocking=True)
 

@@ -329,6 +329,10 @@ int bd_tile_w16(const void *w, int dtype_bits, int64_t rows, int64_t cols, void 
 int64_t bd_x16_bytes(int tokens, int64_t cols);
 int bd_pack_x16(const float *x, int tokens, int64_t cols, int64_t ldx, const float *rms_weight, float epsilon,
                 void *out, float *normed, int64_t ld_normed, int32_t *flags, bd_stream_t stream);
+/* bd_pack_x16 of bf16 rows (the target model's feature rows as they arrive): the
+ * same X16 bits as packing their fp32 values, without a conversion pass. */
+int bd_pack_x16_bf16(const void *x, int tokens, int64_t cols, int64_t ldx, const float *rms_weight, float epsilon,
+                     void *out, float *normed, int64_t ld_normed, int32_t *flags, bd_stream_t stream);
 /* The optional workspace (bd_gemv_workspace_bytes) lets long-row matrices
  * split K over CTAs; partial sums are added in a fixed order, so results do not
  * depend on scheduling.  Zero it once: its first 16 KB hold per-row-group

@@ -66,6 +66,29 @@ def test_gemv_store_and_argmax(rows, cols, tokens, workspace):
     assert not keys.any()
 
 
+@pytest.mark.parametrize("tokens,cols,weighted", [(16, 10240, False), (5, 1000, True), (32, 2560, True)])
+def test_pack_x16_bf16_matches_fp32_pack(tokens, cols, weighted):
+    """The bf16-row pack writes the same X16 bytes as the fp32 pack of the same values."""
+    lib = package()._lib
+    g = torch.Generator().manual_seed(cols + tokens)
+    x = (torch.randn((tokens, cols), generator=g) * 3).to(torch.bfloat16).to(DEV)
+    w = torch.randn(cols, generator=g).to(DEV) if weighted else None
+    nbytes = int(lib.load().bd_x16_bytes(tokens, cols))
+    # token rows past `tokens` in the last 8-row block are left as they were: zero both
+    want = torch.zeros(nbytes, dtype=torch.uint8, device=DEV)
+    got = torch.zeros(nbytes, dtype=torch.uint8, device=DEV)
+    flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+    stream = torch.cuda.current_stream().cuda_stream
+    wp = None if w is None else w.data_ptr()
+    xf = x.float().contiguous()
+    lib.call("bd_pack_x16", xf.data_ptr(), tokens, cols, cols, wp, 1e-6, want.data_ptr(), None, 0, flags.data_ptr(),
+             stream)
+    lib.call("bd_pack_x16_bf16", x.data_ptr(), tokens, cols, cols, wp, 1e-6, got.data_ptr(), None, 0,
+             flags.data_ptr(), stream)
+    assert torch.equal(got, want)
+    assert int(flags.item()) == 0
+
+
 def test_heads_post_rope_and_cache_overflow():
     lib = package()._lib
     n, heads, d = 5, 3, 64
