@@ -191,7 +191,14 @@ __global__ void he4_epilogue_kernel(const float *__restrict__ dot, int64_t token
 // Output-side gradients: grid (column tiles of 256, row chunks of 64).
 //   dL = G * max(scale, 0) -> bf16 hi, lo;  colpart[rc][0][o] = sum_t G * (D * step);
 //   colpart[rc][1][o] = sum_t G * (sums[t] * step);  rowpart[ct][t] = sum_o G * midpoint[o].
-__global__ void __launch_bounds__(kCols) grad_prep_kernel(const float *__restrict__ grad, const float *__restrict__ dot,
+// Rows go in batches of 16: every thread requests its 16 G and D values before any
+// arithmetic (the loads of a batch are in flight together), writes the transposed
+// halves as whole 32-byte sectors (16 tokens), and the row sums of the batch are
+// reduced once through shared memory (warp w: rows 2w, 2w + 1).
+constexpr int kPrepRows = 16;
+static_assert(kRowChunk % kPrepRows == 0 && kPrepRows == 2 * (kCols / 32), "two batch rows per warp");
+
+__global__ void __launch_bounds__(kCols, 3) grad_prep_kernel(const float *__restrict__ grad, const float *__restrict__ dot,
                                                           int64_t tokens, int64_t outs, const float *__restrict__ scale,
                                                           const float *__restrict__ midpoint,
                                                           const float *__restrict__ bound, int bits,
@@ -200,9 +207,11 @@ __global__ void __launch_bounds__(kCols) grad_prep_kernel(const float *__restric
                                                           int64_t ld_dl, __nv_bfloat16 *__restrict__ hi_t,
                                                           __nv_bfloat16 *__restrict__ lo_t, int64_t ld_t,
                                                           float *__restrict__ colpart, float *__restrict__ rowpart) {
-    __shared__ float wsum[kCols / 32][kRowChunk];
+    __shared__ float gsum[kPrepRows][kCols];
+    __shared__ float rsum[kRowChunk];
     Quant q;
     q.init(__ldg(bound), bits);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t o = static_cast<int64_t>(blockIdx.x) * kCols + threadIdx.x;
     const bool live = o < outs;
     const float s = live ? __ldg(scale + o) : 0.0f;
@@ -210,46 +219,66 @@ __global__ void __launch_bounds__(kCols) grad_prep_kernel(const float *__restric
     const float mid = live ? __ldg(midpoint + o) : 0.0f;
     const int64_t t0 = static_cast<int64_t>(blockIdx.y) * kRowChunk;
     float acc_scale = 0.0f, acc_mid = 0.0f;
-    for (int r8 = 0; r8 < kRowChunk; r8 += 8) {
-        uint32_t th[4] = {0u, 0u, 0u, 0u}, tl[4] = {0u, 0u, 0u, 0u};  // eight tokens of the transposed rows
+    for (int r16 = 0; r16 < kRowChunk; r16 += kPrepRows) {
+        float g[kPrepRows], d[kPrepRows];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int r = r8 + j;
-            const int64_t t = t0 + r;
+        for (int j = 0; j < kPrepRows; ++j) {
+            const int64_t t = t0 + r16 + j;
+            const bool on = t < tokens && live;
+            g[j] = on ? grad[t * outs + o] : 0.0f;
+            d[j] = on ? dot[t * outs + o] : 0.0f;
+        }
+        uint32_t th[kPrepRows / 2], tl[kPrepRows / 2];
+#pragma unroll
+        for (int j = 0; j < kPrepRows; ++j) {
+            const int64_t t = t0 + r16 + j;
             float gm = 0.0f;
+            if ((j & 1) == 0) th[j >> 1] = tl[j >> 1] = 0u;
             if (t < tokens && live) {
-                const int64_t i = t * outs + o;
-                const float g = grad[i];
-                const float d = __fmul_rn(dot[i], q.step);
-                acc_scale = __fadd_rn(acc_scale, __fmul_rn(g, d));
-                acc_mid = __fadd_rn(acc_mid, __fmul_rn(g, __fmul_rn(static_cast<float>(__ldg(sums + t)), q.step)));
-                const float dl = __fmul_rn(g, sc);
+                acc_scale = __fadd_rn(acc_scale, __fmul_rn(g[j], __fmul_rn(d[j], q.step)));
+                acc_mid = __fadd_rn(acc_mid, __fmul_rn(g[j], __fmul_rn(static_cast<float>(__ldg(sums + t)), q.step)));
+                const float dl = __fmul_rn(g[j], sc);
                 const __nv_bfloat16 h = __float2bfloat16_rn(dl);
                 const __nv_bfloat16 l = __float2bfloat16_rn(__fsub_rn(dl, __bfloat162float(h)));
                 hi[t * ld_dl + o] = h;
                 lo[t * ld_dl + o] = l;
                 th[j >> 1] |= static_cast<uint32_t>(__bfloat16_as_ushort(h)) << (16 * (j & 1));
                 tl[j >> 1] |= static_cast<uint32_t>(__bfloat16_as_ushort(l)) << (16 * (j & 1));
-                gm = __fmul_rn(g, mid);
+                gm = __fmul_rn(g[j], mid);
             }
-            gm = warp_sum(gm);
-            if ((threadIdx.x & 31) == 0) wsum[threadIdx.x >> 5][r] = gm;
+            gsum[j][threadIdx.x] = gm;
         }
-        if (hi_t && live && t0 + r8 < tokens) {
-            *reinterpret_cast<uint4 *>(hi_t + o * ld_t + t0 + r8) = make_uint4(th[0], th[1], th[2], th[3]);
-            *reinterpret_cast<uint4 *>(lo_t + o * ld_t + t0 + r8) = make_uint4(tl[0], tl[1], tl[2], tl[3]);
+        // transposed halves: tokens [r16, r16 + 8) and [r16 + 8, r16 + 16), each written
+        // only where its first token exists (ld_t covers tokens rounded up to 8)
+        if (hi_t && live) {
+#pragma unroll
+            for (int h8 = 0; h8 < 2; ++h8) {
+                if (t0 + r16 + 8 * h8 < tokens) {
+                    *reinterpret_cast<uint4 *>(hi_t + o * ld_t + t0 + r16 + 8 * h8) =
+                        make_uint4(th[4 * h8], th[4 * h8 + 1], th[4 * h8 + 2], th[4 * h8 + 3]);
+                    *reinterpret_cast<uint4 *>(lo_t + o * ld_t + t0 + r16 + 8 * h8) =
+                        make_uint4(tl[4 * h8], tl[4 * h8 + 1], tl[4 * h8 + 2], tl[4 * h8 + 3]);
+                }
+            }
         }
+        __syncthreads();
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+            const int r = 2 * warp + rr;
+            float v = 0.0f;
+#pragma unroll
+            for (int c = 0; c < kCols / 32; ++c) v = __fadd_rn(v, gsum[r][lane + 32 * c]);
+            v = warp_sum(v);
+            if (lane == 0) rsum[r16 + r] = v;
+        }
+        __syncthreads();
     }
     if (live) {
         colpart[(static_cast<int64_t>(blockIdx.y) * 2 + 0) * outs + o] = acc_scale;
         colpart[(static_cast<int64_t>(blockIdx.y) * 2 + 1) * outs + o] = acc_mid;
     }
-    __syncthreads();
-    if (threadIdx.x < kRowChunk && t0 + threadIdx.x < tokens) {
-        float v = wsum[0][threadIdx.x];
-        for (int w = 1; w < kCols / 32; ++w) v = __fadd_rn(v, wsum[w][threadIdx.x]);
-        rowpart[static_cast<int64_t>(blockIdx.x) * tokens + t0 + threadIdx.x] = v;
-    }
+    if (threadIdx.x < kRowChunk && t0 + threadIdx.x < tokens)
+        rowpart[static_cast<int64_t>(blockIdx.x) * tokens + t0 + threadIdx.x] = rsum[threadIdx.x];
 }
 
 // d_scale[o] = sum_rc colpart[rc][0][o] * (scale[o] >= 0); d_mid[o] = sum_rc colpart[rc][1][o];

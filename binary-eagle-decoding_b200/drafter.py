@@ -203,8 +203,9 @@ class DraftEngine:
             self._heads(kv, anchor, 0, cfg.kv_heads, layer.k_norm, True, 0, self._cache_ptr(self.k_cache, i, 0), kvd)
             self._heads(kv, anchor, kvd, cfg.kv_heads, None, False, 0, self._cache_ptr(self.v_cache, i, 0), kvd)
 
-    def ingest(self, features: Tensor, pos0: int) -> None:
-        """Append up to 32 context rows at positions pos0.. through the GEMV path (one draft round)."""
+    def ingest(self, features: Tensor, pos0: int, after_fusion=None) -> None:
+        """Append up to 32 context rows at positions pos0.. through the GEMV path (one draft
+        round).  ``after_fusion`` (optional) is called once the fusion GEMV is issued."""
         cfg = self.cfg
         n = features.shape[0]
         if not 1 <= n <= 32 or pos0 + n > self.max_positions - cfg.slots:
@@ -219,6 +220,8 @@ class DraftEngine:
             feats = features if features.dtype == torch.float32 else features.float()
             self._pack(feats.to(self.device).contiguous(), n, width, width, x16=x16)
         self._gemv(self.fc.data_ptr(), cfg.hidden, width, n, self.fused, cfg.hidden, x16=x16)
+        if after_fusion is not None:
+            after_fusion()
         self._pack(self.fused, n, cfg.hidden, cfg.hidden, self.enc_norm, x16=x16)
         kvd = cfg.kv_heads * cfg.head_dim
         width_kv = cfg.layers * 2 * kvd
@@ -361,12 +364,15 @@ class DraftRound:
         main = torch.cuda.current_stream(e.device)
         if host:
             e.ids[:1].copy_(self.host_first, non_blocking=True)
-        self.side.wait_stream(main)
-        with torch.cuda.stream(self.side):
-            e.draft_start(self.anchor, self.size)
-        if host:
             self.dev_rows.copy_(self.host_rows, non_blocking=True)
-        e.ingest(self.dev_rows, self.anchor - self.rows)
+
+        def fork() -> None:
+            # the draft's first kernels start once the fusion GEMV (the widest read) is issued
+            self.side.wait_stream(main)
+            with torch.cuda.stream(self.side):
+                e.draft_start(self.anchor, self.size)
+
+        e.ingest(self.dev_rows, self.anchor - self.rows, after_fusion=fork)
         main.wait_stream(self.side)
         e.draft(self.anchor, self.size, started=True)
         if host:
