@@ -126,7 +126,7 @@ SIGNATURES = {
     "bd_loss_head_forward": (c_int, [P, P, c_int64, c_int64, c_int64, P, P, c_int64, P, P, P, P, P, P, P, P, P]),
     "bd_loss_head_grad": (c_int, [P, P, c_int64, c_int64, c_int64, P, P, c_int64, P, P, P, P, P, c_int64, P]),
     "bd_rms_forward": (c_int, [P, c_int64, c_int64, P, ctypes.c_float, P, P, P]),
-    "bd_rms_partials": (c_int64, [c_int64]),
+    "bd_rms_partials": (c_int64, [c_int64, c_int64]),
     "bd_rms_backward": (c_int, [P, c_int64, c_int64, P, P, P, P, P, P, P]),
     "bd_head_post": (c_int, [P, c_int64, c_int64, c_int, c_int, P, ctypes.c_float, P, P, c_int, P, P, P, P]),
     "bd_head_post_partials": (c_int64, [c_int64, c_int]),

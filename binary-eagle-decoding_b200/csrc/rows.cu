@@ -49,30 +49,58 @@ __global__ void __launch_bounds__(kRowsThreads) rms_rows_fwd_kernel(const float 
     for (int64_t k = threadIdx.x; k < cols; k += blockDim.x) o[k] = __fmul_rn(__fmul_rn(xr[k], r), w[k]);
 }
 
-// dx = r u - (r^3 / n) x sum(u x), u = dy w; dw partial (this CTA's rows) = sum dy x r.
-__global__ void __launch_bounds__(kRowsThreads) rms_rows_bwd_kernel(const float *__restrict__ x, int64_t rows,
-                                                                  int64_t cols, const float *__restrict__ w,
-                                                                  const float *__restrict__ inv,
-                                                                  const float *__restrict__ dy, float *__restrict__ dx,
-                                                                  float *__restrict__ dw_part, int rows_per_cta) {
-    __shared__ float scratch[kRowsThreads / 32];
-    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_cta;
-    float *dwp = dw_part + blockIdx.x * cols;
-    for (int64_t k = threadIdx.x; k < cols; k += blockDim.x) dwp[k] = 0.0f;
-    for (int64_t row = r0; row < r0 + rows_per_cta && row < rows; ++row) {
-        const float *xr = x + row * cols, *g = dy + row * cols;
-        const float r = inv[row];
-        float s = 0.0f;
-        for (int64_t k = threadIdx.x; k < cols; k += blockDim.x) s = __fadd_rn(s, __fmul_rn(__fmul_rn(g[k], w[k]), xr[k]));
-        const float total = cta_sum(s, scratch);
-        const float c = __fdiv_rn(__fmul_rn(__fmul_rn(r, r), r), static_cast<float>(cols)) * total;
-        float *d = dx + row * cols;
-        for (int64_t k = threadIdx.x; k < cols; k += blockDim.x) {
-            const float u = __fmul_rn(g[k], w[k]);
-            d[k] = __fsub_rn(__fmul_rn(r, u), __fmul_rn(c, xr[k]));
-            dwp[k] = __fadd_rn(dwp[k], __fmul_rn(__fmul_rn(g[k], xr[k]), r));
-        }
+// The backward in two passes, so that every CTA has work at a few hundred rows:
+//   rms_rows_dot_kernel   s[row] = sum_k dy w x (one warp per row);
+//   rms_rows_grad_kernel  grid (column tiles of 256, chunks of kRmsChunk rows): per
+//                         thread one column, dx = r u - (r^3 / n) x s, u = dy w, and
+//                         its column's dw partial over the chunk = sum dy x r.
+constexpr int kRmsChunk = 16;
+
+__global__ void __launch_bounds__(kRowsThreads) rms_rows_dot_kernel(const float *__restrict__ x, int64_t rows,
+                                                                   int64_t cols, const float *__restrict__ w,
+                                                                   const float *__restrict__ dy,
+                                                                   float *__restrict__ total) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * (kRowsThreads / 32) + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const float *xr = x + row * cols, *g = dy + row * cols;
+    float s = 0.0f;
+#pragma unroll 4
+    for (int64_t k = lane; k < cols; k += 32) s = __fadd_rn(s, __fmul_rn(__fmul_rn(g[k], w[k]), xr[k]));
+    s = warp_sum(s);
+    if (lane == 0) total[row] = s;
+}
+
+__global__ void __launch_bounds__(kRowsThreads) rms_rows_grad_kernel(const float *__restrict__ x, int64_t rows,
+                                                                    int64_t cols, const float *__restrict__ w,
+                                                                    const float *__restrict__ inv,
+                                                                    const float *__restrict__ dy,
+                                                                    const float *__restrict__ total,
+                                                                    float *__restrict__ dx,
+                                                                    float *__restrict__ dw_part) {
+    const int64_t k = static_cast<int64_t>(blockIdx.x) * kRowsThreads + threadIdx.x;
+    if (k >= cols) return;
+    const int64_t r0 = static_cast<int64_t>(blockIdx.y) * kRmsChunk;
+    const float wk = w[k];
+    float gv[kRmsChunk], xv[kRmsChunk];
+#pragma unroll
+    for (int j = 0; j < kRmsChunk; ++j) {  // the chunk's loads in flight together
+        const int64_t row = r0 + j;
+        gv[j] = row < rows ? dy[row * cols + k] : 0.0f;
+        xv[j] = row < rows ? x[row * cols + k] : 0.0f;
     }
+    float dw = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kRmsChunk; ++j) {
+        const int64_t row = r0 + j;
+        if (row >= rows) break;
+        const float r = inv[row];
+        const float c = __fmul_rn(__fdiv_rn(__fmul_rn(__fmul_rn(r, r), r), static_cast<float>(cols)), total[row]);
+        const float u = __fmul_rn(gv[j], wk);
+        dx[row * cols + k] = __fsub_rn(__fmul_rn(r, u), __fmul_rn(c, xv[j]));
+        dw = __fadd_rn(dw, __fmul_rn(__fmul_rn(gv[j], xv[j]), r));
+    }
+    dw_part[static_cast<int64_t>(blockIdx.y) * cols + k] = dw;
 }
 
 // The weight gradient: partial rows summed in order.
@@ -81,6 +109,7 @@ __global__ void sum_partials_kernel(const float *__restrict__ part, int64_t npar
     const int64_t k = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (k >= cols) return;
     float s = 0.0f;
+#pragma unroll 8
     for (int64_t p = 0; p < nparts; ++p) s = __fadd_rn(s, part[p * cols + k]);
     out[k] = s;
 }
@@ -260,19 +289,28 @@ extern "C" int bd_rms_forward(const float *x, int64_t rows, int64_t cols, const 
     return BD_OK;
 }
 
-extern "C" int64_t bd_rms_partials(int64_t rows) { return rows < 1 ? 0 : (rows + 7) / 8; }
+// Scratch of the backward in floats: the dw partial rows (one per chunk of rows) and
+// the per-row sums.
+extern "C" int64_t bd_rms_partials(int64_t rows, int64_t cols) {
+    return rows < 1 || cols < 1 ? 0 : (rows + kRmsChunk - 1) / kRmsChunk * cols + rows;
+}
 
 extern "C" int bd_rms_backward(const float *x, int64_t rows, int64_t cols, const float *weight, const float *inv,
                                     const float *dy, float *dx, float *dw_partials, float *dw, bd_stream_t stream) {
     if (rows < 0 || cols < 1 || rows > 0x7fffffff) return BD_ERR_INVALID;
     if (rows == 0) return BD_OK;
     if (!x || !weight || !inv || !dy || !dx || !dw_partials || !dw) return BD_ERR_INVALID;
+    const int64_t chunks = (rows + kRmsChunk - 1) / kRmsChunk;
+    if (chunks > 65535) return BD_ERR_INVALID;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const int64_t parts = bd_rms_partials(rows);
-    rms_rows_bwd_kernel<<<static_cast<unsigned>(parts), kRowsThreads, 0, st>>>(x, rows, cols, weight, inv, dy, dx,
-                                                                             dw_partials, 8);
+    float *total = dw_partials + chunks * cols;
+    rms_rows_dot_kernel<<<rows_grid(rows, kRowsThreads / 32), kRowsThreads, 0, st>>>(x, rows, cols, weight, dy,
+                                                                                     total);
     BD_CHECK_LAUNCH();
-    sum_partials_kernel<<<rows_grid(cols, 256), 256, 0, st>>>(dw_partials, parts, cols, dw);
+    rms_rows_grad_kernel<<<dim3(rows_grid(cols, kRowsThreads), static_cast<unsigned>(chunks)), kRowsThreads, 0, st>>>(
+        x, rows, cols, weight, inv, dy, total, dx, dw_partials);
+    BD_CHECK_LAUNCH();
+    sum_partials_kernel<<<rows_grid(cols, 256), 256, 0, st>>>(dw_partials, chunks, cols, dw);
     BD_CHECK_LAUNCH();
     return BD_OK;
 }

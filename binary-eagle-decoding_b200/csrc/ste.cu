@@ -323,30 +323,43 @@ __global__ void __launch_bounds__(kCols) ste_input_kernel(const float *__restric
     const float g = live ? __ldg(gain + k) : 0.0f;
     const int64_t t0 = static_cast<int64_t>(blockIdx.y) * kRowChunk;
     float acc_gain = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f, s4 = 0.0f;
-    for (int r = 0; r < kRowChunk && live; ++r) {
-        const int64_t t = t0 + r;
-        if (t >= tokens) break;
-        const int64_t i = t * cols + k;
-        float d = dv1[i];
-        if (dv2) d = __fadd_rn(d, dv2[i]);
-        d = __fadd_rn(d, __ldg(gm + t));
-        const float xv = x[i];
-        const float gained = __fmul_rn(xv, g);
-        const float mn = fminf(gained, b);
-        const float clipped = fmaxf(mn, nb);
-        const int code = q.code(gained);
-        const float d_codes = __fmul_rn(d, q.step);
-        s1 = __fadd_rn(s1, __fmul_rn(d, static_cast<float>(code)));
-        s2 = __fadd_rn(s2, __fmul_rn(d_codes, clipped));
-        const float d_clipped = __fmul_rn(d_codes, q.ratio);
-        const float to_mn = mn > nb ? 1.0f : (mn == nb ? 0.5f : 0.0f);
-        const float d_mn = __fmul_rn(d_clipped, to_mn);
-        s3 = __fadd_rn(s3, __fmul_rn(d_clipped, __fsub_rn(1.0f, to_mn)));
-        const float to_g = gained < b ? 1.0f : (gained == b ? 0.5f : 0.0f);
-        const float d_gained = __fmul_rn(d_mn, to_g);
-        s4 = __fadd_rn(s4, __fmul_rn(d_mn, __fsub_rn(1.0f, to_g)));
-        dx[i] = __fmul_rn(d_gained, g);
-        acc_gain = __fadd_rn(acc_gain, __fmul_rn(d_gained, xv));
+    // rows in batches of 16 whose loads are all requested before the arithmetic; the
+    // sums still run over the rows in order
+    for (int r16 = 0; r16 < kRowChunk && live && t0 + r16 < tokens; r16 += kPrepRows) {
+        float dva[kPrepRows], xa[kPrepRows];
+#pragma unroll
+        for (int j = 0; j < kPrepRows; ++j) {
+            const int64_t t = t0 + r16 + j;
+            const int64_t i = t * cols + k;
+            const bool on = t < tokens;
+            dva[j] = on ? dv1[i] : 0.0f;
+            if (dv2 && on) dva[j] = __fadd_rn(dva[j], dv2[i]);
+            xa[j] = on ? x[i] : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < kPrepRows; ++j) {
+            const int64_t t = t0 + r16 + j;
+            if (t >= tokens) break;
+            const int64_t i = t * cols + k;
+            const float d = __fadd_rn(dva[j], __ldg(gm + t));
+            const float xv = xa[j];
+            const float gained = __fmul_rn(xv, g);
+            const float mn = fminf(gained, b);
+            const float clipped = fmaxf(mn, nb);
+            const int code = q.code(gained);
+            const float d_codes = __fmul_rn(d, q.step);
+            s1 = __fadd_rn(s1, __fmul_rn(d, static_cast<float>(code)));
+            s2 = __fadd_rn(s2, __fmul_rn(d_codes, clipped));
+            const float d_clipped = __fmul_rn(d_codes, q.ratio);
+            const float to_mn = mn > nb ? 1.0f : (mn == nb ? 0.5f : 0.0f);
+            const float d_mn = __fmul_rn(d_clipped, to_mn);
+            s3 = __fadd_rn(s3, __fmul_rn(d_clipped, __fsub_rn(1.0f, to_mn)));
+            const float to_g = gained < b ? 1.0f : (gained == b ? 0.5f : 0.0f);
+            const float d_gained = __fmul_rn(d_mn, to_g);
+            s4 = __fadd_rn(s4, __fmul_rn(d_mn, __fsub_rn(1.0f, to_g)));
+            dx[i] = __fmul_rn(d_gained, g);
+            acc_gain = __fadd_rn(acc_gain, __fmul_rn(d_gained, xv));
+        }
     }
     if (live) colpart[static_cast<int64_t>(blockIdx.y) * cols + k] = acc_gain;
     const float v1 = block_sum_f(s1, scratch);

@@ -87,10 +87,10 @@ class _RmsFn(torch.autograd.Function):
         rows, cols = x.shape
         g = grad.reshape(rows, cols).float().contiguous()
         dx = torch.empty_like(x)
-        parts = torch.empty((int(_lib.load().bd_rms_partials(rows)), cols), dtype=torch.float32, device=x.device)
+        parts = torch.empty(int(_lib.load().bd_rms_partials(rows, cols)), dtype=torch.float32, device=x.device)
         dw = torch.empty(cols, dtype=torch.float32, device=x.device)
         _lib.call("bd_rms_backward", x.data_ptr(), rows, cols, w.data_ptr(), inv.data_ptr(), g.data_ptr(),
-                  dx.data_ptr(), parts.data_ptr(), dw.data_ptr(), _stream(x.device), kernels=2)
+                  dx.data_ptr(), parts.data_ptr(), dw.data_ptr(), _stream(x.device), kernels=3)
         return dx.view(ctx.shape), dw, None
 
 

@@ -425,8 +425,8 @@ int bd_attention_decode(const float *q, const uint16_t *k_cache, const uint16_t 
  * bd_rms_forward: out = x * rsqrt(mean(x^2) + eps) * w over rows of cols
  *   (w1a1_eagle/model.py:50-51, torch's rms expression in one kernel), inv[r]
  *   the row's rsqrt factor for the backward.
- * bd_rms_backward: dx and dw (dw through bd_rms_partials(rows) x cols
- *   partial rows added in a fixed order).
+ * bd_rms_backward: dx and dw; dw_partials is scratch of bd_rms_partials(rows,
+ *   cols) floats (per-row sums, and partial rows of dw added in a fixed order).
  * bd_head_post: per (row, head) of head_dim values of x [rows][ld_x] (heads side
  *   by side): the head rms with weight (NULL: none), the rotate-half rotary at
  *   positions[row] with frequencies[head_dim / 2] (NULL: none; model.py:54-63),
@@ -439,7 +439,7 @@ int bd_attention_decode(const float *q, const uint16_t *k_cache, const uint16_t 
  *   partials).  No reference C counterpart: the reference is torch autograd. */
 int bd_rms_forward(const float *x, int64_t rows, int64_t cols, const float *weight, float eps, float *out, float *inv,
                 bd_stream_t stream);
-int64_t bd_rms_partials(int64_t rows);
+int64_t bd_rms_partials(int64_t rows, int64_t cols);
 int bd_rms_backward(const float *x, int64_t rows, int64_t cols, const float *weight, const float *inv,
                          const float *dy, float *dx, float *dw_partials, float *dw, bd_stream_t stream);
 int bd_head_post(const float *x, int64_t ld_x, int64_t rows, int heads, int head_dim, const float *weight, float eps,

@@ -71,7 +71,7 @@ def test_host_only_entry_points():
     assert lib.bd_rms_forward(None, 0, 2560, None, 1e-6, None, None, None) == 0  # nothing to do
     assert lib.bd_rms_forward(None, -1, 2560, None, 1e-6, None, None, None) == 1
     assert lib.bd_head_post(addr, 3, 4, 1, 3, None, 1e-6, None, None, 0, addr, None, None, None) == 1  # odd head_dim
-    assert lib.bd_rms_partials(17) == 3 and lib.bd_head_post_partials(512, 32) > 0
+    assert lib.bd_rms_partials(17, 4) == 2 * 4 + 17 and lib.bd_head_post_partials(512, 32) > 0
     # split-K workspaces: a 480-row product over a 151936-long K is split, a 4096-row one is not
     assert lib.bd_gemm_split_workspace_bytes(480, 2560, 151936, 3) > 0
     assert lib.bd_gemm_split_workspace_bytes(4096, 2560, 2560, 2) == 0
