@@ -1,6 +1,7 @@
 """Data-parallel QAT over NCCL on two GPUs (skipped with fewer): the overlapped
-bucketed gradient exchange equals the mean of the ranks' own gradients, and one
-``qat.update`` leaves every rank with the same parameters."""
+bucketed gradient exchange equals the mean of the ranks' own gradients (also with
+the latent gradients deferred to ``LatentGradients``), and one ``qat.update``
+leaves every rank with the same parameters."""
 
 from __future__ import annotations
 
@@ -59,6 +60,17 @@ def _rank_main(rank: int, world: int, port: int, out) -> None:
         exchange.finish()
         exchanged = [p.grad.clone() for p in params]
         exchange.remove()
+        # the same with the latent gradients written by one product at the end of the
+        # block (LatentGradients) and handed to the exchange as they are written
+        model.zero_grad()
+        exchange = qat.GradientExchange(params, bucket_bytes=256)
+        exchange.armed = True
+        with bd.LatentGradients(model, 64, on_ready=exchange.ready):
+            qat.group_loss(model, features, tokens, windows, 6)
+        exchange.finish()
+        deferred = max(float((d.grad - e).abs().max() / e.abs().max().clamp_min(1e-30))
+                       for d, e in zip(params, exchanged))
+        exchange.remove()
         gathered = []
         for g in own:
             parts = [torch.empty_like(g) for _ in range(world)]
@@ -73,7 +85,7 @@ def _rank_main(rank: int, world: int, port: int, out) -> None:
         copies = [torch.empty_like(flat) for _ in range(world)]
         dist.all_gather(copies, flat)
         same = all(torch.equal(c, copies[0]) for c in copies)
-        out[rank] = (worst, exchange.buckets, same, loss, norm)
+        out[rank] = (worst, exchange.buckets, same, loss, norm, deferred)
         torch.cuda.synchronize()
     finally:
         dist.destroy_process_group()
@@ -87,8 +99,9 @@ def test_qat_gradient_exchange_two_nccl_ranks():
     out = manager.dict()
     mp.spawn(_rank_main, args=(2, port, out), nprocs=2, join=True)
     for rank in range(2):
-        worst, buckets, same, loss, norm = out[rank]
+        worst, buckets, same, loss, norm, deferred = out[rank]
         assert buckets >= 2, buckets
+        assert deferred <= 1e-6, (rank, deferred)
         assert worst <= 1e-6, (rank, worst)  # the kernels reduce in fixed order: same sums, same rounding
         assert same, rank
         assert torch.isfinite(torch.tensor([loss, norm])).all()
