@@ -103,15 +103,30 @@ __global__ void __launch_bounds__(kRowsThreads) rms_rows_grad_kernel(const float
     dw_part[static_cast<int64_t>(blockIdx.y) * cols + k] = dw;
 }
 
-// The weight gradient: partial rows summed in order.
-__global__ void sum_partials_kernel(const float *__restrict__ part, int64_t nparts, int64_t cols,
-                                    float *__restrict__ out) {
-    const int64_t k = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (k >= cols) return;
+// The weight gradient: partial rows summed in a fixed order.  A CTA takes 32
+// columns; its 8 warps take the partial rows p = w, w + 8, ... (increasing p),
+// and the 8 sums of a column are then added in warp order, so narrow matrices
+// with many partial rows (a head's 128 columns) still spread over many threads.
+constexpr int kSumCols = 32, kSumGroups = kRowsThreads / kSumCols;
+
+__global__ void __launch_bounds__(kRowsThreads) sum_partials_kernel(const float *__restrict__ part, int64_t nparts,
+                                                                    int64_t cols, float *__restrict__ out) {
+    __shared__ float sums[kSumGroups][kSumCols];
+    const int c = threadIdx.x & (kSumCols - 1), grp = threadIdx.x / kSumCols;
+    const int64_t k = static_cast<int64_t>(blockIdx.x) * kSumCols + c;
     float s = 0.0f;
+    if (k < cols) {
 #pragma unroll 8
-    for (int64_t p = 0; p < nparts; ++p) s = __fadd_rn(s, part[p * cols + k]);
-    out[k] = s;
+        for (int64_t p = grp; p < nparts; p += kSumGroups) s = __fadd_rn(s, part[p * cols + k]);
+    }
+    sums[grp][c] = s;
+    __syncthreads();
+    if (grp == 0 && k < cols) {
+        float t = sums[0][c];
+#pragma unroll
+        for (int i = 1; i < kSumGroups; ++i) t = __fadd_rn(t, sums[i][c]);
+        out[k] = t;
+    }
 }
 
 struct HeadPostArgs {
@@ -193,67 +208,97 @@ __global__ void __launch_bounds__(kRowsThreads) head_post_fwd_kernel(const HeadP
 }
 
 // Gradient of the forward above (the fp16 rounding passes it straight through).
+// The loads of one (row, head) item: its gradient and input halves, the gradient
+// rotated back through the rotary (dy_e = g_e c + g_{e+h} s, dy_{e+h} = g_{e+h} c - g_e s).
+struct HeadItem {
+    float gl[kHeadPairs], gh[kHeadPairs], xl[kHeadPairs], xh[kHeadPairs];
+};
+
+__device__ __forceinline__ void head_item_load(const HeadPostArgs &a, int64_t item, int lane, HeadItem &it) {
+    const int half = a.d / 2;
+    const int64_t row = item / a.heads;
+    const int h = static_cast<int>(item % a.heads);
+    const float *xr = a.x + row * a.ld_x + static_cast<int64_t>(h) * a.d;
+    const float *g = a.dy + item * a.d;
+#pragma unroll
+    for (int i = 0; i < kHeadPairs; ++i) {
+        const int e = lane + 32 * i;
+        const bool live = e < half;
+        it.gl[i] = live ? g[e] : 0.0f;
+        it.gh[i] = live ? g[e + half] : 0.0f;
+        it.xl[i] = live ? xr[e] : 0.0f;
+        it.xh[i] = live ? xr[e + half] : 0.0f;
+    }
+}
+
+__device__ __forceinline__ void head_item_finish(const HeadPostArgs &a, int64_t item, int lane, HeadItem &it,
+                                                 float (&dwl)[kHeadPairs], float (&dwh)[kHeadPairs]) {
+    const int half = a.d / 2;
+    const int64_t row = item / a.heads;
+    const int h = static_cast<int>(item % a.heads);
+    if (a.pos) {
+#pragma unroll
+        for (int i = 0; i < kHeadPairs; ++i) {
+            const int e = lane + 32 * i;
+            if (e >= half) continue;
+            const float angle = __fmul_rn(static_cast<float>(a.pos[row]), a.freq[e]);
+            const float c = cosf(angle), s = sinf(angle);
+            const float a0 = __fadd_rn(__fmul_rn(it.gl[i], c), __fmul_rn(it.gh[i], s));
+            const float a1 = __fsub_rn(__fmul_rn(it.gh[i], c), __fmul_rn(it.gl[i], s));
+            it.gl[i] = a0;
+            it.gh[i] = a1;
+        }
+    }
+    float *d = a.dx + row * a.ld_x + static_cast<int64_t>(h) * a.d;
+    if (!a.w) {
+#pragma unroll
+        for (int i = 0; i < kHeadPairs; ++i) {
+            const int e = lane + 32 * i;
+            if (e < half) {
+                d[e] = it.gl[i];
+                d[e + half] = it.gh[i];
+            }
+        }
+        return;
+    }
+    const float r = a.inv[item];
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kHeadPairs; ++i) {
+        const int e = lane + 32 * i;
+        if (e < half)
+            s = __fadd_rn(s, __fadd_rn(__fmul_rn(__fmul_rn(it.gl[i], a.w[e]), it.xl[i]),
+                                       __fmul_rn(__fmul_rn(it.gh[i], a.w[e + half]), it.xh[i])));
+    }
+    const float c = __fdiv_rn(__fmul_rn(__fmul_rn(r, r), r), static_cast<float>(a.d)) * warp_sum(s);
+#pragma unroll
+    for (int i = 0; i < kHeadPairs; ++i) {
+        const int e = lane + 32 * i;
+        if (e >= half) continue;
+        d[e] = __fsub_rn(__fmul_rn(r, __fmul_rn(it.gl[i], a.w[e])), __fmul_rn(c, it.xl[i]));
+        d[e + half] = __fsub_rn(__fmul_rn(r, __fmul_rn(it.gh[i], a.w[e + half])), __fmul_rn(c, it.xh[i]));
+        dwl[i] = __fadd_rn(dwl[i], __fmul_rn(__fmul_rn(it.gl[i], it.xl[i]), r));
+        dwh[i] = __fadd_rn(dwh[i], __fmul_rn(__fmul_rn(it.gh[i], it.xh[i]), r));
+    }
+}
+
+// Items in pairs: both items' loads are issued before either item's stores (the
+// gradient and output buffers may not be assumed apart by the compiler).
 __global__ void __launch_bounds__(kRowsThreads) head_post_bwd_kernel(const HeadPostArgs a, int items_per_warp) {
     extern __shared__ float dws[];  // [warps][d]
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     const int half = a.d / 2;
     float dwl[kHeadPairs] = {}, dwh[kHeadPairs] = {};
     const int64_t first = (static_cast<int64_t>(blockIdx.x) * nwarps + warp) * items_per_warp;
-    for (int64_t item = first; item < first + items_per_warp && item < a.rows * a.heads; ++item) {
-        const int64_t row = item / a.heads;
-        const int h = static_cast<int>(item % a.heads);
-        const float *xr = a.x + row * a.ld_x + static_cast<int64_t>(h) * a.d;
-        const float *g = a.dy + item * a.d;
-        float gl[kHeadPairs], gh[kHeadPairs], xl[kHeadPairs], xh[kHeadPairs];
-#pragma unroll
-        for (int i = 0; i < kHeadPairs; ++i) {
-            const int e = lane + 32 * i;
-            const bool live = e < half;
-            gl[i] = live ? g[e] : 0.0f;
-            gh[i] = live ? g[e + half] : 0.0f;
-            xl[i] = live ? xr[e] : 0.0f;
-            xh[i] = live ? xr[e + half] : 0.0f;
-            if (live && a.pos) {
-                // rotary backward: dy_e = g_e c + g_{e+h} s, dy_{e+h} = g_{e+h} c - g_e s
-                const float angle = __fmul_rn(static_cast<float>(a.pos[row]), a.freq[e]);
-                const float c = cosf(angle), s = sinf(angle);
-                const float a0 = __fadd_rn(__fmul_rn(gl[i], c), __fmul_rn(gh[i], s));
-                const float a1 = __fsub_rn(__fmul_rn(gh[i], c), __fmul_rn(gl[i], s));
-                gl[i] = a0;
-                gh[i] = a1;
-            }
-        }
-        float *d = a.dx + row * a.ld_x + static_cast<int64_t>(h) * a.d;
-        if (!a.w) {
-#pragma unroll
-            for (int i = 0; i < kHeadPairs; ++i) {
-                const int e = lane + 32 * i;
-                if (e < half) {
-                    d[e] = gl[i];
-                    d[e + half] = gh[i];
-                }
-            }
-            continue;
-        }
-        const float r = a.inv[item];
-        float s = 0.0f;
-#pragma unroll
-        for (int i = 0; i < kHeadPairs; ++i) {
-            const int e = lane + 32 * i;
-            if (e < half)
-                s = __fadd_rn(s, __fadd_rn(__fmul_rn(__fmul_rn(gl[i], a.w[e]), xl[i]),
-                                           __fmul_rn(__fmul_rn(gh[i], a.w[e + half]), xh[i])));
-        }
-        const float c = __fdiv_rn(__fmul_rn(__fmul_rn(r, r), r), static_cast<float>(a.d)) * warp_sum(s);
-#pragma unroll
-        for (int i = 0; i < kHeadPairs; ++i) {
-            const int e = lane + 32 * i;
-            if (e >= half) continue;
-            d[e] = __fsub_rn(__fmul_rn(r, __fmul_rn(gl[i], a.w[e])), __fmul_rn(c, xl[i]));
-            d[e + half] = __fsub_rn(__fmul_rn(r, __fmul_rn(gh[i], a.w[e + half])), __fmul_rn(c, xh[i]));
-            dwl[i] = __fadd_rn(dwl[i], __fmul_rn(__fmul_rn(gl[i], xl[i]), r));
-            dwh[i] = __fadd_rn(dwh[i], __fmul_rn(__fmul_rn(gh[i], xh[i]), r));
-        }
+    const int64_t items = a.rows * a.heads;
+    const int64_t end = first + items_per_warp < items ? first + items_per_warp : items;
+    for (int64_t item = first; item < end; item += 2) {
+        HeadItem it0, it1;
+        head_item_load(a, item, lane, it0);
+        const bool two = item + 1 < end;
+        if (two) head_item_load(a, item + 1, lane, it1);
+        head_item_finish(a, item, lane, it0, dwl, dwh);
+        if (two) head_item_finish(a, item + 1, lane, it1, dwl, dwh);
     }
     if (!a.w) return;
 #pragma unroll
@@ -310,7 +355,7 @@ extern "C" int bd_rms_backward(const float *x, int64_t rows, int64_t cols, const
     rms_rows_grad_kernel<<<dim3(rows_grid(cols, kRowsThreads), static_cast<unsigned>(chunks)), kRowsThreads, 0, st>>>(
         x, rows, cols, weight, inv, dy, total, dx, dw_partials);
     BD_CHECK_LAUNCH();
-    sum_partials_kernel<<<rows_grid(cols, 256), 256, 0, st>>>(dw_partials, chunks, cols, dw);
+    sum_partials_kernel<<<rows_grid(cols, kSumCols), kRowsThreads, 0, st>>>(dw_partials, chunks, cols, dw);
     BD_CHECK_LAUNCH();
     return BD_OK;
 }
@@ -383,7 +428,8 @@ extern "C" int bd_head_post_backward(const float *x, int64_t ld_x, int64_t rows,
     head_post_bwd_kernel<<<static_cast<unsigned>(grid), kRowsThreads, smem, st>>>(a, per);
     BD_CHECK_LAUNCH();
     if (weight) {
-        sum_partials_kernel<<<rows_grid(head_dim, 256), 256, 0, st>>>(dw_partials, grid, head_dim, dw);
+        sum_partials_kernel<<<rows_grid(head_dim, kSumCols), kRowsThreads, 0, st>>>(dw_partials, grid, head_dim,
+                                                                                       dw);
         BD_CHECK_LAUNCH();
     }
     return BD_OK;

@@ -106,15 +106,21 @@ __global__ void sign_rows_kernel(const float *__restrict__ latent, int64_t n, __
 // Tiled transpose into bf16: dst[c][r] = f(src[r][c]) for r < rows, c < cols (32 x 32 tiles).
 // SIGNS = true: f = +-1 of an fp32 latent (x >= 0 -> +1, -0.0 -> +1), with the finiteness check;
 // SIGNS = false: f = the int8 code itself (exact in bf16).
+// 64 x 64 tiles through shared memory: rows of the tile are read along the source
+// rows, and each destination row of the tile (64 source rows) is written as one
+// 128-byte run of bf16 pairs (single values where ldd is odd or at the last row).
+constexpr int kTr = 64;
+
 template <bool SIGNS, typename In>
 __global__ void __launch_bounds__(256) transpose_bf16_kernel(const In *__restrict__ src, int64_t rows, int64_t cols,
                                                              int64_t lds, __nv_bfloat16 *__restrict__ dst,
                                                              int64_t ldd, int32_t *flags) {
-    __shared__ float tile[32][33];
-    const int64_t r0 = static_cast<int64_t>(blockIdx.y) * 32, c0 = static_cast<int64_t>(blockIdx.x) * 32;
-    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    __shared__ float tile[kTr][kTr + 1];
+    const int64_t r0 = static_cast<int64_t>(blockIdx.y) * kTr, c0 = static_cast<int64_t>(blockIdx.x) * kTr;
+    const int tx = threadIdx.x & (kTr - 1), ty = threadIdx.x / kTr;  // 64 x 4
     bool bad = false;
-    for (int i = ty; i < 32; i += 8) {
+#pragma unroll 4
+    for (int i = ty; i < kTr; i += 256 / kTr) {
         const int64_t r = r0 + i, c = c0 + tx;
         float v = 0.0f;
         if (r < rows && c < cols) {
@@ -128,11 +134,24 @@ __global__ void __launch_bounds__(256) transpose_bf16_kernel(const In *__restric
         }
         tile[i][tx] = v;
     }
-    if (SIGNS && __any_sync(0xffffffffu, bad) && tx == 0) set_flag(flags, BD_FLAG_NONFINITE_LATENT);
+    if (SIGNS && __any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) set_flag(flags, BD_FLAG_NONFINITE_LATENT);
     __syncthreads();
-    for (int i = ty; i < 32; i += 8) {
-        const int64_t c = c0 + i, r = r0 + tx;
-        if (c < cols && r < rows) dst[c * ldd + r] = __float2bfloat16_rn(tile[tx][i]);
+    const int lane = threadIdx.x & 31, wc = threadIdx.x >> 5;  // 32 lanes x 8 column rows at a time
+    const bool pairs = (ldd & 1) == 0 && (reinterpret_cast<uintptr_t>(dst) & 3) == 0;
+#pragma unroll 2
+    for (int i = wc; i < kTr; i += 8) {
+        const int64_t c = c0 + i, r = r0 + 2 * lane;
+        if (c >= cols || r >= rows) continue;
+        const __nv_bfloat16 e0 = __float2bfloat16_rn(tile[2 * lane][i]);
+        if (r + 1 < rows && pairs) {
+            __nv_bfloat162 two;
+            two.x = e0;
+            two.y = __float2bfloat16_rn(tile[2 * lane + 1][i]);
+            *reinterpret_cast<__nv_bfloat162 *>(dst + c * ldd + r) = two;
+        } else {
+            dst[c * ldd + r] = e0;
+            if (r + 1 < rows) dst[c * ldd + r + 1] = __float2bfloat16_rn(tile[2 * lane + 1][i]);
+        }
     }
 }
 
@@ -486,9 +505,9 @@ extern "C" int bd_quantize_rows_i8(const float *x, int64_t rows, int64_t cols, c
 // codes int8 [rows][ld] -> bf16 [cols][ld_t] (the weight-gradient GEMM's K-major operand)
 extern "C" int bd_codes_transpose_bf16(const int8_t *codes, int64_t rows, int64_t cols, int64_t ld, uint16_t *out,
                                        int64_t ld_t, bd_stream_t stream) {
-    if (rows < 1 || cols < 1 || ld < cols || ld_t < rows || (rows + 31) / 32 > 65535 || !codes || !out)
+    if (rows < 1 || cols < 1 || ld < cols || ld_t < rows || (rows + kTr - 1) / kTr > 65535 || !codes || !out)
         return BD_ERR_INVALID;
-    dim3 grid(static_cast<unsigned>((cols + 31) / 32), static_cast<unsigned>((rows + 31) / 32));
+    dim3 grid(static_cast<unsigned>((cols + kTr - 1) / kTr), static_cast<unsigned>((rows + kTr - 1) / kTr));
     transpose_bf16_kernel<false, int8_t><<<grid, 256, 0, stream>>>(codes, rows, cols, ld,
                                                                    reinterpret_cast<__nv_bfloat16 *>(out), ld_t,
                                                                    nullptr);
@@ -516,8 +535,9 @@ extern "C" int bd_split_bf16(const float *x, int64_t rows, int64_t cols, int64_t
 // latent fp32 [rows][cols] -> +-1 bf16 [cols][ld_t] (the input-gradient GEMM's K-major operand)
 extern "C" int bd_sign_cols_bf16(const float *latent, int64_t rows, int64_t cols, uint16_t *out, int64_t ld_t,
                                  int32_t *flags, bd_stream_t stream) {
-    if (rows < 1 || cols < 1 || ld_t < rows || (rows + 31) / 32 > 65535 || !latent || !out) return BD_ERR_INVALID;
-    dim3 grid(static_cast<unsigned>((cols + 31) / 32), static_cast<unsigned>((rows + 31) / 32));
+    if (rows < 1 || cols < 1 || ld_t < rows || (rows + kTr - 1) / kTr > 65535 || !latent || !out)
+        return BD_ERR_INVALID;
+    dim3 grid(static_cast<unsigned>((cols + kTr - 1) / kTr), static_cast<unsigned>((rows + kTr - 1) / kTr));
     transpose_bf16_kernel<true, float><<<grid, 256, 0, stream>>>(latent, rows, cols, cols,
                                                                  reinterpret_cast<__nv_bfloat16 *>(out), ld_t, flags);
     BD_CHECK_LAUNCH();

@@ -943,22 +943,45 @@ int launch_tc_gemm(int epi, const TcArgs &a, const int8_t *codes, int64_t ld_cod
 
 // ------------------------------------------------------------------ I8 sign copies
 
+// One thread per 16 consecutive columns of one (padded) row: 16 latents in (four
+// 16-byte loads when the row stride allows), one 16-byte store of +-1 / 0 out.
 __global__ void tile_i8_kernel(const float *__restrict__ latent, int64_t rows, int64_t cols, int64_t ld,
                                int8_t *__restrict__ out, int stride, int offset, int32_t *flags) {
     const int64_t rows_pad = (rows + kTcBM - 1) / kTcBM * kTcBM;
-    const int64_t total = rows_pad * ld;
+    const int64_t groups = ld / 16;
+    const int64_t total = rows_pad * groups;
+    const bool vec = (cols & 3) == 0 && (reinterpret_cast<uintptr_t>(latent) & 15) == 0;
     bool bad = false;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t r = i / ld, k = i - r * ld;
-        int8_t v = 0;
-        if (r < rows && k < cols) {
-            const float x = latent[r * cols + k];
-            bad |= !isfinite(x);
-            v = x >= 0.0f ? 1 : -1;
+        const int64_t r = i / groups, k0 = (i - r * groups) * 16;
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+        if (r < rows) {
+            const float *src = latent + r * cols + k0;
+            float x[16];
+            if (vec && k0 + 16 <= cols) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float4 f = __ldg(reinterpret_cast<const float4 *>(src) + q);
+                    x[4 * q] = f.x;
+                    x[4 * q + 1] = f.y;
+                    x[4 * q + 2] = f.z;
+                    x[4 * q + 3] = f.w;
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) x[e] = k0 + e < cols ? src[e] : 0.0f;
+            }
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                if (k0 + e < cols) {
+                    bad |= !isfinite(x[e]);
+                    w[e >> 2] |= static_cast<uint32_t>(x[e] >= 0.0f ? 0x01u : 0xFFu) << (8 * (e & 3));
+                }
+            }
         }
         const int64_t orow = ((r / kTcBM) * stride + offset) * kTcBM + (r % kTcBM);
-        out[orow * ld + k] = v;
+        *reinterpret_cast<uint4 *>(out + orow * ld + k0) = make_uint4(w[0], w[1], w[2], w[3]);
     }
     if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) set_flag(flags, BD_FLAG_NONFINITE_LATENT);
 }
@@ -983,9 +1006,9 @@ extern "C" int bd_tile_signs_i8(const float *latent, int64_t rows, int64_t cols,
     if (rows == 0) return BD_OK;
     if (!latent || !out) return BD_ERR_INVALID;
     const int64_t ld = i8_ld(cols);
-    const int64_t total = (rows + kTcBM - 1) / kTcBM * kTcBM * ld;
+    const int64_t total = (rows + kTcBM - 1) / kTcBM * kTcBM * (ld / 16);
     int64_t grid = (total + 255) / 256;
-    if (grid > 148 * 64) grid = 148 * 64;
+    if (grid > 148 * 16) grid = 148 * 16;
     tile_i8_kernel<<<static_cast<unsigned>(grid), 256, 0, stream>>>(latent, rows, cols, ld, out, block_stride,
                                                                     block_offset, flags);
     BD_CHECK_LAUNCH();

@@ -11,9 +11,15 @@ the reference.  The binary projections run in ``libbitdraft.so``:
   (``bd_ffn_he4``) when no gradient is needed and at most 32 rows come in;
 * ``hard_sign``, ``bound_latents`` and ``clamp_latents`` are kernels too.
 
-Attention, norms and rotary embedding stay torch expressions of the same
-mathematics (the serving path has kernels for them in ``drafter.py``).  A CUDA
-device is required: there is no CPU fallback.
+* the training attention (``train_attention``), the norms, the per-head rms,
+  rotary and fp16 storage (``rms``, ``head_post``) and the frozen products
+  (``frozen_linear``) are kernels of this library, forward and backward;
+* ``LatentGradients`` turns the latent gradients of many backward passes into
+  one tensor-core product per projection.
+
+A CUDA device is required for these paths: there is no CPU fallback (``rms`` and
+the loss bookkeeping keep the reference's torch expressions for CPU tensors, for
+host-side checks only).
 """
 
 from __future__ import annotations

@@ -298,3 +298,40 @@ def test_argmax_rows(ops):
     x = (torch.randn((16, 151936), generator=torch.Generator().manual_seed(9)) * 3).to(torch.bfloat16)
     got = ops.argmax_rows(x.to(DEV)).cpu().numpy()
     assert np.array_equal(got, acceptance.argmax_rows(x.float().numpy()))
+
+
+@pytest.mark.parametrize("rows,cols", [(300, 1000), (128, 2560), (5, 17), (9728, 2560)])
+def test_sign_operands_and_code_transpose(ops, rows, cols):
+    """The tensor-core sign operands against torch expressions: the +-1 int8 rows
+    (padded to 128 rows and bd_i8_ld columns, block-interleaved with stride 2 at
+    offset 1), the +-1 bf16 transposed signs, and the transposed int8 codes as bf16;
+    -0.0 counts as +1, padding stays zero."""
+    lib = package()._lib
+    g = torch.Generator().manual_seed(rows + cols)
+    latent = torch.randn((rows, cols), generator=g)
+    latent[0, 0] = -0.0
+    ld = int(lib.load().bd_i8_ld(cols))
+    rows_pad = (rows + 127) // 128 * 128
+    signs = torch.where(latent >= 0, 1, -1).to(torch.int8)
+    tiled = ops.tile_i8(latent.to(DEV), block_stride=2, block_offset=1).cpu().view(-1, 2, 128, ld)
+    want = torch.zeros((rows_pad, ld), dtype=torch.int8)
+    want[:rows, :cols] = signs
+    assert torch.equal(tiled[:, 1].reshape(rows_pad, ld), want.view(-1, 128, ld).reshape(rows_pad, ld))
+    assert not tiled[:, 0].any()  # the other interleave slot is untouched
+    ld_t = (rows + 7) // 8 * 8
+    flags = torch.zeros(1, dtype=torch.int32, device=DEV)
+    stream = torch.cuda.current_stream().cuda_stream
+    cols_t = torch.zeros((cols, ld_t), dtype=torch.bfloat16, device=DEV)
+    latent_d = latent.to(DEV)
+    lib.call("bd_sign_cols_bf16", latent_d.data_ptr(), rows, cols, cols_t.data_ptr(), ld_t, flags.data_ptr(), stream)
+    assert torch.equal(cols_t.cpu()[:, :rows], signs.t().to(torch.bfloat16))
+    assert not cols_t.cpu()[:, rows:].any()
+    codes = torch.randint(-127, 128, (rows, cols), generator=g, dtype=torch.int8)
+    ldc = cols + 3
+    codes_pad = torch.zeros((rows, ldc), dtype=torch.int8)
+    codes_pad[:, :cols] = codes
+    codes_d = codes_pad.to(DEV)
+    codes_t = torch.zeros((cols, ld_t), dtype=torch.bfloat16, device=DEV)
+    lib.call("bd_codes_transpose_bf16", codes_d.data_ptr(), rows, cols, ldc, codes_t.data_ptr(), ld_t, stream)
+    assert torch.equal(codes_t.cpu()[:, :rows], codes.t().to(torch.bfloat16))
+    assert int(flags.item()) == 0
