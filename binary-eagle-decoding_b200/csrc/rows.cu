@@ -65,8 +65,22 @@ __global__ void __launch_bounds__(kRowsThreads) rms_rows_dot_kernel(const float 
     if (row >= rows) return;
     const float *xr = x + row * cols, *g = dy + row * cols;
     float s = 0.0f;
+    const bool vec = (cols & 3) == 0 && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dy) |
+                                          reinterpret_cast<uintptr_t>(w)) & 15) == 0;
+    if (vec) {  // 16-byte loads: lane l takes columns 4 (l + 32 i) .. 4 (l + 32 i) + 3
 #pragma unroll 4
-    for (int64_t k = lane; k < cols; k += 32) s = __fadd_rn(s, __fmul_rn(__fmul_rn(g[k], w[k]), xr[k]));
+        for (int64_t k = 4 * lane; k < cols; k += 128) {
+            const float4 gv = *reinterpret_cast<const float4 *>(g + k), wv = *reinterpret_cast<const float4 *>(w + k);
+            const float4 xv = *reinterpret_cast<const float4 *>(xr + k);
+            s = __fadd_rn(s, __fmul_rn(__fmul_rn(gv.x, wv.x), xv.x));
+            s = __fadd_rn(s, __fmul_rn(__fmul_rn(gv.y, wv.y), xv.y));
+            s = __fadd_rn(s, __fmul_rn(__fmul_rn(gv.z, wv.z), xv.z));
+            s = __fadd_rn(s, __fmul_rn(__fmul_rn(gv.w, wv.w), xv.w));
+        }
+    } else {
+#pragma unroll 4
+        for (int64_t k = lane; k < cols; k += 32) s = __fadd_rn(s, __fmul_rn(__fmul_rn(g[k], w[k]), xr[k]));
+    }
     s = warp_sum(s);
     if (lane == 0) total[row] = s;
 }
