@@ -221,6 +221,19 @@ KERNELS_PER_CALL = {"bd_ffn_he4": 3, "bd_ffn_he4_fused": 2, "bd_loss_head_forwar
 launches = 0
 
 
+_SIZES: dict[tuple, int] = {}
+
+
+def size(name: str, *args) -> int:
+    """A size query of the library (``bd_*_bytes``, ``*_partials``, ``*_ld``, ...), memoised:
+    each is a pure function of its integer arguments within a process."""
+    key = (name,) + args
+    hit = _SIZES.get(key)
+    if hit is None:
+        hit = _SIZES[key] = int(getattr(load(), name)(*args))
+    return hit
+
+
 def call(name: str, *args, kernels: int | None = None) -> None:
     """Call an int-status entry point; raise on a non-zero status.  ``kernels``
     overrides the launch count of entry points whose count depends on sizes."""

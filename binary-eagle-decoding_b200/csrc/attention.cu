@@ -117,9 +117,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 1) attn_chunk_kernel(const At
     for (int n = 0; n < kDim / 8; ++n)
 #pragma unroll
         for (int i = 0; i < 4; ++i) o_acc[n][i] = 0.0f;
-    if (head_live) {
+    // a key part with no live key (the short last chunk) keeps m = -inf, l = 0, O = 0:
+    // exactly what its masked products would give, without the MMAs
+    const int kbase = kh * kPartKeys;
+    if (head_live && kbase < nkeys) {
         // S = Q K^T over this warp's 64 keys: 8 n-tiles of 8 keys
-        const int kbase = kh * kPartKeys;
         float s_acc[kPartKeys / 8][4];
 #pragma unroll
         for (int n = 0; n < kPartKeys / 8; ++n)

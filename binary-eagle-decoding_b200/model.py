@@ -9,8 +9,7 @@ the reference.  The binary projections run in ``libbitdraft.so``:
   straight-through kernels and tcgen05 GEMMs (``bd_ste_*``);
 * ``Layer`` runs its SwiGLU tail through the fused decode block
   (``bd_ffn_he4``) when no gradient is needed and at most 32 rows come in;
-* ``hard_sign``, ``bound_latents`` and ``clamp_latents`` are kernels too.
-
+* ``hard_sign``, ``bound_latents`` and ``clamp_latents`` are kernels too;
 * the training attention (``train_attention``), the norms, the per-head rms,
   rotary and fp16 storage (``rms``, ``head_post``) and the frozen products
   (``frozen_linear``) are kernels of this library, forward and backward;
@@ -93,7 +92,7 @@ class _RmsFn(torch.autograd.Function):
         rows, cols = x.shape
         g = grad.reshape(rows, cols).float().contiguous()
         dx = torch.empty_like(x)
-        parts = torch.empty(int(_lib.load().bd_rms_partials(rows, cols)), dtype=torch.float32, device=x.device)
+        parts = torch.empty(_lib.size("bd_rms_partials", rows, cols), dtype=torch.float32, device=x.device)
         dw = torch.empty(cols, dtype=torch.float32, device=x.device)
         _lib.call("bd_rms_backward", x.data_ptr(), rows, cols, w.data_ptr(), inv.data_ptr(), g.data_ptr(),
                   dx.data_ptr(), parts.data_ptr(), dw.data_ptr(), _stream(x.device), kernels=3)
@@ -182,7 +181,7 @@ class _HeadPostFn(torch.autograd.Function):
         dx = torch.empty_like(x)
         parts = dw = None
         if w is not None:
-            parts = torch.empty((int(_lib.load().bd_head_post_partials(rows, heads)), dim), dtype=torch.float32,
+            parts = torch.empty((_lib.size("bd_head_post_partials", rows, heads), dim), dtype=torch.float32,
                                 device=device)
             dw = torch.empty(dim, dtype=torch.float32, device=device)
         _lib.call("bd_head_post_backward", x.data_ptr(), heads * dim, rows, heads, dim,
@@ -350,7 +349,7 @@ def _frozen_halves(owner, operand: Tensor) -> _FrozenOperand:
 def _split_workspace(device: torch.device, m: int, n: int, k: int, parts: int) -> tuple[int | None, int]:
     """The split-K workspace of a bf16 split product (one per device, used in stream
     order), or (None, 0) when the shape runs unsplit."""
-    nbytes = int(_lib.load().bd_gemm_split_workspace_bytes(m, n, k, parts))
+    nbytes = _lib.size("bd_gemm_split_workspace_bytes", m, n, k, parts)
     if nbytes == 0:
         return None, 0
     buf = ops.workspace(device, "gemm_split", nbytes)
@@ -447,12 +446,11 @@ class _ProjectionFn(torch.autograd.Function):
         tokens, inner = x.shape
         outer = latent.shape[0]
         bits = module.bits
-        lib = _lib.load()
         gain = log_gain.detach().exp().contiguous()
         bound = log_clip.detach().exp().reshape(1).contiguous()
         stream = _stream(device)
         flags, now = _flags(device)
-        ld = int(lib.bd_i8_ld(inner))
+        ld = _lib.size("bd_i8_ld", inner)
         codes = torch.empty((tokens, ld), dtype=torch.int8, device=device)
         sums = torch.empty(tokens, dtype=torch.int32, device=device)
         _lib.call("bd_quantize_rows_i8", x.data_ptr(), tokens, inner, gain.data_ptr(), bound.data_ptr(), bits,
@@ -481,7 +479,6 @@ class _ProjectionFn(torch.autograd.Function):
         module = ctx.module
         device = x.device
         stream = _stream(device)
-        lib = _lib.load()
         tokens, inner = x.shape
         outer = latent.shape[0]
         bits = module.bits
@@ -504,7 +501,7 @@ class _ProjectionFn(torch.autograd.Function):
         d_scale = torch.empty(outer, dtype=torch.float32, device=device)
         d_mid = torch.empty_like(d_scale)
         gm = torch.empty(tokens, dtype=torch.float32, device=device)
-        nbytes = int(lib.bd_ste_workspace_bytes(tokens, outer, inner))
+        nbytes = _lib.size("bd_ste_workspace_bytes", tokens, outer, inner)
         ws = ops.workspace(device, "ste", nbytes)
         sc, mid = scale.detach().contiguous(), midpoint.detach().contiguous()
         _lib.call("bd_ste_grad_prep", g.data_ptr(), dot.data_ptr(), tokens, outer, sc.data_ptr(), mid.data_ptr(),
@@ -534,7 +531,7 @@ class _ProjectionFn(torch.autograd.Function):
             d_latent = torch.empty((outer, inner), dtype=torch.float32, device=device)
             partials = None
             if ctx.learned:
-                partials = torch.empty(int(lib.bd_ste_weight_grad_partials(outer, inner)), dtype=torch.float32,
+                partials = torch.empty(_lib.size("bd_ste_weight_grad_partials", outer, inner), dtype=torch.float32,
                                        device=device)
             flags, now = _flags(device)
             _lib.call("bd_ste_weight_grad", hi_t.data_ptr(), lo_t.data_ptr(), outer, tokens, ld_t, codes_t.data_ptr(),
@@ -729,12 +726,11 @@ class LatentGradients:
         latent = module.latent_sign
         outer, inner = latent.shape
         device = latent.device
-        lib = _lib.load()
         window = s["window"]
         learned = module.log_window is not None and window is not None
         partials = None
         if learned:
-            partials = torch.empty(int(lib.bd_ste_weight_grad_partials(outer, inner)), dtype=torch.float32,
+            partials = torch.empty(_lib.size("bd_ste_weight_grad_partials", outer, inner), dtype=torch.float32,
                                    device=device)
         d_latent = torch.empty((outer, inner), dtype=torch.float32, device=device)
         flags, now = _flags(device)
